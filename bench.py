@@ -1,0 +1,344 @@
+"""Benchmark of the int4 linear hot path on B200 (one JSON line on rank 0).
+
+Default workload: a FLUX-style DiT block stack --
+8 blocks of qkv 3072->9216, proj 3072->3072, fc1 3072->9216, fc2 9216->3072,
+AutoGPTQ v1 int4, groupsize 32, bf16 activations N(0,1), M = 4608 tokens
+(4096 image + 512 text). Random-init packed weights (seeded), synthetic
+activations. Glue between linears (q slice of qkv as the attention stand-in,
+residual adds, RMS norm, tanh-GELU) runs in torch and is timed with the step.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                    [--workload cfg1|cfg0|cfg2]
+
+* ``value``: whole-job tokens/s (N ranks each run their own 4608-token batch:
+  weak scaling, no data-path collective), device-timed with CUDA events,
+  max over ranks. Inputs and weights are resident in HBM; the stack's weights
+  (437 MB packed) exceed the 126 MB L2, so every step streams them from HBM.
+* ``e2e``: the same step through the public module API with the input copied
+  from pinned host memory and the output read back every step.
+* ``roofline``: the tcgen05 GEMM launches, timed individually with CUDA events
+  inside the timed steps: achieved = 2*M*K*N summed / their summed duration,
+  against the measured sustained bf16 peak (MEASURED_PEAKS.json).
+* ``cpu_baseline`` (rank 0, N=1): the reference CPU eager path (dequantize once,
+  torch CPU bf16 ``F.linear``) restated in ``oracle/``, on a bounded sample
+  (one block, extrapolated to the stack).
+* ``--impl reference``: the same CPU eager path as the reference arm.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+PKG = ROOT / "onecompression-runtime_b200"
+for _p in (str(ROOT), str(PKG)):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "DiT-stack tokens/s (int4 GPTQ linear stack)"
+
+
+def load_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d.get("hbm_gbs"), "bf16": d.get("bf16_tflops"),
+                "bf16_sustained": d.get("bf16_tflops_sustained"), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16": 1590.0, "bf16_sustained": 1400.0, "source": "fallback"}
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.file = None
+
+    def start(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=self.file, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.file.flush()
+        rows = []
+        with open(self.file.name) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.file.name)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if "Active" in r[5 + i] and "Not" not in r[5 + i]})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ----------------------------------------------------------------------------- model
+def rms_norm(h: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    hf = h.float()
+    return (hf * torch.rsqrt(hf.pow(2).mean(-1, keepdim=True) + eps)).to(h.dtype)
+
+
+class DiTStack:
+    """8 FLUX-style blocks of FusedInt4Linear layers (random packed weights)."""
+
+    def __init__(self, device, blocks: int, layers, gs: int, seed: int = 1000):
+        from onecomp_runtime.layers import FusedInt4Linear
+        from onecomp_runtime.testing import gptq_layer
+        self.blocks = []
+        for b in range(blocks):
+            blk = {}
+            for li, (name, K, N) in enumerate(layers):
+                t = gptq_layer(K, N, gs, seed=seed * (b + 1) + li, device=device)
+                blk[name] = FusedInt4Linear(K, N, t["qweight"], t["scales"], t["qzeros"], t["bias"], gs)
+            self.blocks.append(blk)
+        self.hidden = layers[0][1]
+        self.gemm_events: list | None = None
+
+    def _lin(self, layer, x):
+        if self.gemm_events is None:
+            return layer(x)
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record()
+        y = layer(x)
+        e.record()
+        self.gemm_events.append((s, e, 2 * x.shape[0] * layer.in_features * layer.out_features))
+        return y
+
+    def forward(self, h: torch.Tensor) -> torch.Tensor:
+        H = self.hidden
+        for blk in self.blocks:
+            qkv = self._lin(blk["qkv"], h)
+            q = qkv[:, :H]                       # attention stand-in: the q slice
+            h = rms_norm(h + self._lin(blk["proj"], q))
+            f = torch.nn.functional.gelu(self._lin(blk["fc1"], h), approximate="tanh")
+            h = rms_norm(h + self._lin(blk["fc2"], f))
+        return h
+
+    def gemm_count_per_step(self) -> int:
+        return 4 * len(self.blocks)
+
+
+# ----------------------------------------------------------------------------- CPU eager
+def cpu_eager_block(layers, gs: int, M: int, seed: int = 1000):
+    """The reference CPU eager path (oracle restatement) for one block.
+
+    Weights are dequantized once by the oracle (as ``backend.build_eager``
+    does at load time, not timed); each call runs the block's four
+    ``F.linear`` in bf16 on the host cores plus the glue. Returns
+    ``(run, threads)``.
+    """
+    from oracle import gptq
+    from oracle.eager import EagerCPU
+    from onecomp_runtime.testing import gptq_layer
+    torch.set_num_threads(os.cpu_count() or 1)
+    mods = {}
+    for li, (name, K, N) in enumerate(layers):
+        t = gptq_layer(K, N, gs, seed=seed + li)
+        s_bits = t["scales"].view(torch.int16).numpy().view(np.uint16)
+        w = gptq.dequant_gptq(t["qweight"].numpy(), s_bits, "f16", t["qzeros"].numpy(), t["g_idx"].numpy(), K, N,
+                              "bf16")
+        b_bits = t["bias"].view(torch.int16).numpy().view(np.uint16)
+        mods[name] = EagerCPU(w, "bf16", b_bits, "f16")
+    H = layers[0][1]
+    x = torch.randn(M, H, dtype=torch.float32).to(torch.bfloat16)
+
+    def run():
+        qkv = mods["qkv"](x)
+        h = rms_norm(x + mods["proj"](qkv[:, :H].contiguous()))
+        f = torch.nn.functional.gelu(mods["fc1"](h), approximate="tanh")
+        return rms_norm(h + mods["fc2"](f))
+
+    return run, torch.get_num_threads()
+
+
+def time_cpu(run, warmup: int, steps: int) -> float:
+    for _ in range(warmup):
+        run()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        run()
+    return (time.perf_counter() - t0) / steps
+
+
+# ----------------------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--workload", default="cfg1", choices=["cfg1"])
+    ap.add_argument("--cpu-sample-m", type=int, default=1152,
+                    help="tokens of the bounded CPU-baseline sample (one block)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    from onecomp_runtime.testing import CFG1, CFG1_LAYERS
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    M, blocks, gs = CFG1["M"], CFG1["blocks"], CFG1["gs"]
+    config = {"workload": "cfg1: FLUX-style DiT int4 stack, 8 blocks x (qkv 3072->9216, proj 3072->3072, "
+                          "fc1 3072->9216, fc2 9216->3072), GPTQ v1 gs32, M=4608 tokens per GPU",
+              "global_batch_tokens": M * world, "tokens_per_gpu": M, "blocks": blocks,
+              "parallelism": f"replicas x{world} (weak scaling, no collective)",
+              "l2": "weights 437 MB packed per stack > 126 MB L2 (streamed every step)"}
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        sample_m = args.cpu_sample_m
+        run, cores = cpu_eager_block(CFG1_LAYERS, gs, sample_m)
+        per_block = time_cpu(run, args.warmup, args.steps)
+        tps = sample_m / (per_block * blocks)
+        sample = (f"one block (4 linears + glue) at M={sample_m} tokens per step, torch CPU bf16 F.linear on "
+                  "weights dequantized once by the oracle, extrapolated x8 blocks")
+        line = {"metric": METRIC, "impl": "reference", "value": round(tps, 1), "unit": "tokens/s",
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": round(1e3 * M / tps, 3), "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": config,
+                "cpu_baseline": {"value": round(tps, 1), "unit": "tokens/s", "cores": cores, "kind": "port",
+                                 "sample": sample},
+                "e2e": {"value": round(tps, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=dev)
+    from onecomp_runtime import _lib
+    _lib.require_b200(dev)
+    torch.manual_seed(1234 + rank)
+    stack = DiTStack(dev, blocks, CFG1_LAYERS, gs, seed=1000 + 17 * rank)
+    x = torch.randn(M, CFG1["hidden"], device=dev).to(torch.bfloat16)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(dev)
+
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            y = stack.forward(x)
+        torch.cuda.synchronize(dev)
+        if not torch.isfinite(y).all():
+            raise RuntimeError("non-finite stack output")
+
+        # ---- device-timed steps (inputs resident in HBM)
+        clocks = ClockSampler(local)
+        barrier()
+        clocks.start()
+        stack.gemm_events = []
+        t_start = torch.cuda.Event(enable_timing=True)
+        t_end = torch.cuda.Event(enable_timing=True)
+        t_start.record()
+        for _ in range(args.steps):
+            y = stack.forward(x)
+        t_end.record()
+        barrier()
+        clk = clocks.stop()
+        ms_total = t_start.elapsed_time(t_end)
+        gemm = [(s.elapsed_time(e), fl) for s, e, fl in stack.gemm_events]
+        stack.gemm_events = None
+
+        # ---- end-to-end through the module API with host buffers
+        x_host = torch.empty((M, CFG1["hidden"]), dtype=torch.bfloat16, pin_memory=True)
+        x_host.copy_(x.cpu())
+        y_host = torch.empty((M, CFG1["hidden"]), dtype=torch.bfloat16, pin_memory=True)
+        for _ in range(2):
+            y_host.copy_(stack.forward(x_host.to(dev, non_blocking=True)), non_blocking=True)
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            xd = x_host.to(dev, non_blocking=True)
+            y_host.copy_(stack.forward(xd), non_blocking=True)
+        e1.record()
+        barrier()
+        ms_e2e = e0.elapsed_time(e1)
+
+    t = torch.tensor([ms_total, ms_e2e], device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms_total, ms_e2e = float(t[0]), float(t[1])
+    ms_step = ms_total / args.steps
+    value = world * M * args.steps / (ms_total / 1e3)
+    e2e_value = world * M * args.steps / (ms_e2e / 1e3)
+
+    peaks = load_peaks()
+    gemm_ms = sum(g[0] for g in gemm)
+    gemm_flops = sum(g[1] for g in gemm)
+    achieved = gemm_flops / (gemm_ms / 1e3) / 1e12
+    peak = peaks["bf16_sustained"]
+    roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+                "frac": round(achieved / peak, 4), "traffic": None,
+                "kernel": "gptq_gemm_tc_kernel (tcgen05, BT=192)",
+                "peak_source": f"{peaks['source']} bf16_tflops_sustained",
+                "gemm_share_of_step": round(gemm_ms / ms_total, 4),
+                "gemm_ms_per_step": round(gemm_ms / args.steps, 3)}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        run, cores = cpu_eager_block(CFG1_LAYERS, gs, args.cpu_sample_m)
+        per_block = time_cpu(run, 1, 3)
+        cpu = {"value": round(args.cpu_sample_m / (per_block * blocks), 1), "unit": "tokens/s", "cores": cores,
+               "kind": "port",
+               "sample": f"one block (4 linears + glue) at M={args.cpu_sample_m} tokens, torch CPU bf16 "
+                         "F.linear on oracle-dequantized weights, extrapolated x8 blocks"}
+
+    if world > 1:
+        torch.distributed.destroy_process_group()
+    if rank != 0:
+        return
+    line = {"metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded random packed weights, N(0,1) activations)", "config": config,
+            "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": M * CFG1["hidden"] * 2,
+                    "d2h_bytes_per_step": M * CFG1["hidden"] * 2},
+            "gpu_launches": stack.gemm_count_per_step() * args.steps,
+            "roofline": roofline, "cpu_baseline": cpu, "clocks": clk}
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,131 @@
+/*
+ * oc_b200.h -- C ABI of the B200 (sm_100a) int4/int2 linear hot path of
+ * onecomp_runtime (kizuna-intelligence/onecompression-runtime).
+ *
+ * Plain C: raw device pointers, sizes, dtype tags and a cudaStream_t. No torch
+ * types. Every call is stream-ordered, allocates no device memory and returns an
+ * int status (OC_OK == 0); oc_b200_last_error() holds the message of the last
+ * failing call on the calling thread.
+ *
+ * The reference has no native FFI; each entry point below replaces a Python
+ * function or a Triton launch of the reference, cited as file:line relative to
+ * the reference package root (onecomp_runtime/).
+ */
+#ifndef OC_B200_H_
+#define OC_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* oc_stream_t; /* identical to cudaStream_t */
+typedef struct oc_b200_layer oc_b200_layer; /* opaque: host-side metadata of one packed layer */
+
+enum {
+  OC_OK = 0,
+  OC_ERR_INVALID = 1,     /* bad argument (shape, dtype, alignment, null pointer) */
+  OC_ERR_UNSUPPORTED = 2, /* valid request this build does not implement, or not an sm_100 device */
+  OC_ERR_CUDA = 3,        /* a CUDA runtime/driver call failed */
+  OC_ERR_DEVICE = 4,      /* a kernel reported a bounded wait that gave up (see oc_b200_read_device_error) */
+  OC_ERR_WORKSPACE = 5    /* workspace missing or too small */
+};
+
+enum { OC_DT_F16 = 0, OC_DT_BF16 = 1, OC_DT_F32 = 2 };
+
+enum {
+  OC_OPT_GEMM_PATH = 1,    /* 0 auto (M<=16 -> split-K GEMV, else tcgen05), 1 force GEMV, 2 force tcgen05 */
+  OC_OPT_TC_TILE = 2,      /* tokens per tcgen05 tile: 0 auto, 128, 192, 256 */
+  OC_OPT_GEMV_CTAS = 3     /* GEMV target CTAs per SM for split-K sizing (default 3) */
+};
+
+/* ---- library / device ------------------------------------------------------ */
+int oc_b200_abi_version(void);
+const char* oc_b200_last_error(void);
+/* OC_OK when `device` is an sm_100 (B200-class) GPU. Mirrors the build-time
+ * capability gate of backend.resolve_backend (backend.py:103-144). */
+int oc_b200_device_check(int device);
+int oc_b200_set_option(int key, int value);
+/* Copies the kernels' device error word into *code (0 = none) and clears it.
+ * Synchronises `stream`. */
+int oc_b200_read_device_error(int* code, oc_stream_t stream);
+
+/* ---- unpack / pack / dequant ---------------------------------------------- */
+/* Replaces quant_utils.unpack_int_weights (quant_utils.py:36-42): qweight
+ * int32 [K/(32/wbits), N] -> w_int int32 [N, K]. */
+int oc_b200_gptq_unpack(const int32_t* qweight, int K, int N, int wbits, int32_t* w_int, oc_stream_t stream);
+/* Replaces quant_utils.unpack_zeros (quant_utils.py:45-47): qzeros int32
+ * [G, N/(32/wbits)] -> zeros int32 [G, N] (stored values, no v1 restore). */
+int oc_b200_gptq_unpack_zeros(const int32_t* qzeros, int G, int N, int wbits, int32_t* zeros, oc_stream_t stream);
+/* Replaces _pack_int4_weights (layers/fused_int4_linear.py:76-91), any wbits
+ * dividing 32: w_int int32 [N, K] -> qweight int32 [ceil(K/pf), N]. */
+int oc_b200_gptq_pack(const int32_t* w_int, int N, int K, int wbits, int32_t* qweight, oc_stream_t stream);
+/* Replaces quant_utils.dequant_gptq_to_fp (quant_utils.py:50-69), bit-exact:
+ * out[n, k] = RNE_out( f32(s[g,n]) * (q[n,k] - z[g,n]) ), g = g_idx[k] (g_idx may be
+ * NULL: g = k / groupsize). v1 != 0 applies the AutoGPTQ-v1 zero restore
+ * (z + 1) & mask (quant_utils.py:64-65). out is [N, K] (nn.Linear layout). */
+int oc_b200_gptq_dequant(const int32_t* qweight, const int32_t* qzeros, const void* scales, int scales_dtype,
+                         const int64_t* g_idx, int K, int N, int G, int groupsize, int wbits, int v1, void* out,
+                         int out_dtype, oc_stream_t stream);
+/* Replaces quant_utils.dequant_extra_u8_to_weight (quant_utils.py:72-103),
+ * bit-exact including its two roundings in the output dtype. qweight_u8 is
+ * [N, ld_bytes] (low nibble = even k); scales/zeros [N, G] of any float dtype. */
+int oc_b200_rtn_dequant(const uint8_t* qweight_u8, int64_t ld_bytes, const void* scales, int scales_dtype,
+                        const void* zeros, int zeros_dtype, int K, int N, int G, void* out, int out_dtype,
+                        oc_stream_t stream);
+/* Replaces layers/dsv4_packed_linear.dequant_dsv4_packed (dsv4_packed_linear.py:22-56),
+ * bit-exact. packed is [N, ld_bytes], 8/wbits codes per byte (code j at bits
+ * j*wbits). scales/zeros element (n, g) sits at n*stride_n + g*stride_g
+ * (covers both the [N, G] and [G, N] layouts); groupsize <= 0: one group per row. */
+int oc_b200_dsv4_dequant(const uint8_t* packed, int64_t ld_bytes, int wbits, const void* scales, int scales_dtype,
+                         const void* zeros, int zeros_dtype, int64_t stride_n, int64_t stride_g, int groupsize,
+                         int K, int N, void* out, int out_dtype, oc_stream_t stream);
+
+/* ---- K re-layout (load time) ----------------------------------------------- */
+/* Builds the kernel-side K order used for act-order g_idx and for groupsizes
+ * that are not a multiple of 8 (the role of _repack_groups_to_32,
+ * fused_int4_linear.py:94-124): qweight_out[w', n] packs, for i < 8, the code of
+ * source row k_perm[8w'+i] (or 0 when it is -1). */
+int oc_b200_gptq_repack_k(const int32_t* qweight, const int32_t* k_perm, int k_packed, int N, int32_t* qweight_out,
+                          oc_stream_t stream);
+/* x_out[m, k'] = x[m, k_perm[k']] (0 when -1); 16-bit elements. */
+int oc_b200_permute_cols(const void* x, int64_t ldx, int64_t M, int K, const int32_t* k_perm, int k_packed,
+                         void* x_out, oc_stream_t stream);
+
+/* ---- packed GPTQ int4 linear ----------------------------------------------- */
+/* Describes one AutoGPTQ int4 layer for the GEMM kernels. Replaces the module
+ * state of FusedInt4Linear (fused_int4_linear.py:966-1014),
+ * FusedInt4LinearAnyGroup (:646-670), FusedInt4LinearPaddedGroups (:770-811) and
+ * PackedGPTQLinear (packed_gptq_linear.py:34-64).
+ *   qweight    int32 [k_packed/8, N] in kernel K order
+ *   qzeros     int32 [G, N/8], scales [G, N] (f16 or bf16)
+ *   k_perm     int32 [k_packed] or NULL: kernel row k' reads activation column
+ *              k_perm[k'] (-1 = zero padding); NULL means k_packed == in_features
+ *   word_group int32 [k_packed/8] or NULL: group of each 8-row word; NULL means
+ *              group = 8*w / groupsize
+ * Pointers must stay valid for the handle's lifetime; the handle owns no device memory. */
+int oc_b200_gptq_layer_create(const int32_t* qweight, const int32_t* qzeros, const void* scales, int scales_dtype,
+                              const int32_t* k_perm, const int32_t* word_group, int in_features, int k_packed,
+                              int N, int G, int groupsize, int v1, oc_b200_layer** out);
+int oc_b200_layer_destroy(oc_b200_layer* layer);
+/* Bytes of workspace oc_b200_gptq_gemm needs for M rows. The first
+ * 1024 bytes hold split-K tickets that must be zero before the first call on a
+ * workspace (every call leaves them zero again). */
+size_t oc_b200_gptq_gemm_workspace(const oc_b200_layer* layer, int64_t M);
+/* C[M, N] = A[M, in_features] @ dequant(W)^T + bias, fp32 accumulation, bias
+ * added in fp32, one rounding to a_dtype (f16/bf16). Replaces fused_int4_gemm /
+ * _fused_int4_gemm_kernel (fused_int4_linear.py:388-537, :127-272) and
+ * PackedGPTQLinear.forward (packed_gptq_linear.py:66-74). M <= 16 runs the
+ * split-K GEMV, larger M the tcgen05 kernel. A rows are lda elements apart
+ * (16-byte aligned), C rows ldc apart. */
+int oc_b200_gptq_gemm(const oc_b200_layer* layer, const void* a, int a_dtype, int64_t M, int64_t lda,
+                      const void* bias, int bias_dtype, void* c, int64_t ldc, void* workspace,
+                      size_t workspace_bytes, oc_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* OC_B200_H_ */

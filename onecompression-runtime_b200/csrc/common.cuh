@@ -1,0 +1,306 @@
+// Shared device helpers for the onecomp B200 kernels (sm_100a only).
+//
+// * dtype tags and scalar load/convert helpers;
+// * packed bf16x2 / f16x2 arithmetic written as explicit PTX so every
+//   rounding is the IEEE round-to-nearest-even of the exact result;
+// * mbarrier / TMA / tcgen05 wrappers;
+// * bounded waits: every spin has an iteration limit after which the kernel
+//   records an error code in `g_oc_dev_error` and the caller unwinds.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#ifndef OC_WAIT_LIMIT
+// ~ a few seconds of polling with try_wait's internal suspend; far above any
+// legitimate wait, far below a hang.
+#define OC_WAIT_LIMIT (1u << 25)
+#endif
+
+namespace oc {
+
+enum DType : int { kF16 = 0, kBF16 = 1, kF32 = 2 };
+
+// Device-side error word. 0 = ok; otherwise a code identifying the wait that
+// gave up (see OC_DEVERR_*). Read and cleared by oc_b200_read_device_error().
+__device__ unsigned int g_oc_dev_error;
+
+enum : unsigned {
+  kDevErrTmaFull = 0x101,
+  kDevErrTmaEmpty = 0x102,
+  kDevErrAFull = 0x103,
+  kDevErrAEmpty = 0x104,
+  kDevErrAccFull = 0x105,
+  kDevErrAccEmpty = 0x106,
+  kDevErrWFull = 0x107,
+  kDevErrWEmpty = 0x108,
+  kDevErrDrain = 0x109,
+  kDevErrSplitK = 0x201,
+};
+
+__device__ __forceinline__ void record_error(unsigned code) { atomicCAS(&g_oc_dev_error, 0u, code); }
+
+// ----------------------------------------------------------------------------
+// scalar conversions
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ float load_as_f32(const void* p, int dtype, long long i) {
+  if (dtype == kF16) return __half2float(reinterpret_cast<const __half*>(p)[i]);
+  if (dtype == kBF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+  return reinterpret_cast<const float*>(p)[i];
+}
+
+__device__ __forceinline__ uint16_t f32_to_bits(float v, int dtype) {
+  if (dtype == kF16) return __half_as_ushort(__float2half_rn(v));
+  return __bfloat16_as_ushort(__float2bfloat16_rn(v));
+}
+
+__device__ __forceinline__ float bits_to_f32(uint16_t b, int dtype) {
+  if (dtype == kF16) return __half2float(__ushort_as_half(b));
+  return __bfloat162float(__ushort_as_bfloat16(b));
+}
+
+// ----------------------------------------------------------------------------
+// packed 16-bit pair arithmetic (each op rounds the exact result once, RNE)
+// ----------------------------------------------------------------------------
+template <bool BF16> struct Pair;
+
+template <> struct Pair<true> {
+  // 128.0 in bf16: OR-ing a 4-bit code into the low mantissa bits gives 128 + q exactly.
+  static constexpr uint32_t kMagic = 0x43004300u;
+  static constexpr float kMagicF = 128.0f;
+  __device__ __forceinline__ static uint32_t sub(uint32_t a, uint32_t b) {
+    uint32_t d; asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b)); return d;
+  }
+  __device__ __forceinline__ static uint32_t mul(uint32_t a, uint32_t b) {
+    uint32_t d; asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b)); return d;
+  }
+  __device__ __forceinline__ static uint32_t fma(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d; asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d;
+  }
+  __device__ __forceinline__ static uint16_t from_f32(float v) { return __bfloat16_as_ushort(__float2bfloat16_rn(v)); }
+  __device__ __forceinline__ static float to_f32(uint16_t b) { return __bfloat162float(__ushort_as_bfloat16(b)); }
+};
+
+template <> struct Pair<false> {
+  // 1024.0 in fp16: 1024 + q exactly for a 4-bit code.
+  static constexpr uint32_t kMagic = 0x64006400u;
+  static constexpr float kMagicF = 1024.0f;
+  __device__ __forceinline__ static uint32_t sub(uint32_t a, uint32_t b) {
+    uint32_t d; asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b)); return d;
+  }
+  __device__ __forceinline__ static uint32_t mul(uint32_t a, uint32_t b) {
+    uint32_t d; asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b)); return d;
+  }
+  __device__ __forceinline__ static uint32_t fma(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d; asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d;
+  }
+  __device__ __forceinline__ static uint16_t from_f32(float v) { return __half_as_ushort(__float2half_rn(v)); }
+  __device__ __forceinline__ static float to_f32(uint16_t b) { return __half2float(__ushort_as_half(b)); }
+};
+
+__device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t mask, uint32_t magic) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(mask), "r"(magic));  // (a & b) | c
+  return d;
+}
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d; asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel)); return d;
+}
+
+__device__ __forceinline__ uint32_t pack2(uint16_t lo, uint16_t hi) { return (uint32_t)lo | ((uint32_t)hi << 16); }
+
+// Per-(group, row) dequant constants for the exact packed path.
+//   w = RNE( s * (q - z) ) computed as  d = (M+q) - (M+z)            (exact)
+//                                       w = fma(d, s_hi, d * s_lo)   (one rounding)
+// with s_hi = RNE(s) in the pair type and s_lo = s - s_hi (exact, <= 3 bits),
+// so d * s_lo is exact and the fma rounds d*s exactly once.
+template <bool BF16> struct DqConst {
+  uint32_t zm;   // (M+z, M+z)
+  uint32_t shi;  // (s_hi, s_hi)
+  uint32_t slo;  // (s_lo, s_lo)
+};
+
+template <bool BF16>
+__device__ __forceinline__ DqConst<BF16> make_dq_const(float s, int z) {
+  using P = Pair<BF16>;
+  DqConst<BF16> c;
+  const uint16_t zm = P::from_f32(P::kMagicF + (float)z);
+  const uint16_t hi = P::from_f32(s);
+  const uint16_t lo = P::from_f32(s - P::to_f32(hi));
+  c.zm = pack2(zm, zm);
+  c.shi = pack2(hi, hi);
+  c.slo = pack2(lo, lo);
+  return c;
+}
+
+template <bool BF16, bool HAS_LO>
+__device__ __forceinline__ uint32_t dq_pair(uint32_t magic_q, const DqConst<BF16>& c) {
+  using P = Pair<BF16>;
+  const uint32_t d = P::sub(magic_q, c.zm);
+  if (HAS_LO) return P::fma(d, c.shi, P::mul(d, c.slo));
+  return P::mul(d, c.shi);
+}
+
+// ----------------------------------------------------------------------------
+// mbarrier
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: returns false (and records `code`) if the phase never completes
+// or another role of this CTA has already aborted.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          unsigned code) {
+  for (uint32_t it = 0; it < OC_WAIT_LIMIT; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 63u) == 63u && *abort_flag) return false;
+  }
+  record_error(code);
+  *abort_flag = 1;
+  return false;
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_shared() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ----------------------------------------------------------------------------
+// TMA (no multicast anywhere in this code base)
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// ----------------------------------------------------------------------------
+// tcgen05 (cta_group::1 only)
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// D[tmem] (+)= A[tmem] x B[smem desc]
+__device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// 32 lanes x 32 columns of 32-bit: thread i of the warp owns lane (base lane + i).
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+
+// K-major operand in shared memory with the 128-byte swizzle: rows of 64 16-bit
+// elements (128 B), 8-row atoms 1024 B apart. `addr` must sit in a 1024-B aligned tile.
+__device__ __forceinline__ uint64_t smem_desc_kmajor_sw128(uint32_t addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr & 0x3FFFFu) >> 4);        // start address
+  d |= (uint64_t)1 << 16;                          // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024u >> 4) << 32;               // stride byte offset between 8-row atoms
+  d |= (uint64_t)1 << 46;                          // descriptor version (tcgen05)
+  d |= (uint64_t)2 << 61;                          // layout: 128-byte swizzle
+  return d;
+}
+
+// Instruction descriptor for kind::f16: D=f32, A/B = bf16 or f16, both K-major.
+__host__ __device__ constexpr uint32_t make_idesc_f16(bool bf16, int m, int n) {
+  return (1u << 4)                                    // D format: f32
+         | ((bf16 ? 1u : 0u) << 7)                    // A format
+         | ((bf16 ? 1u : 0u) << 10)                   // B format
+         | ((uint32_t)(n >> 3) << 17)                 // N / 8
+         | ((uint32_t)(m >> 4) << 24);                // M / 16
+}
+
+__device__ __forceinline__ int warp_id() { return threadIdx.x >> 5; }
+__device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
+
+__device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+}  // namespace oc

@@ -1,0 +1,285 @@
+// Prefill / large-M int4 GEMM on the 5th-generation tensor cores (tcgen05, sm_100a).
+//
+// Replaces the Triton kernel _fused_int4_gemm_kernel (fused_int4_linear.py:127-272) and
+// its odd-group / any-group variants (:275-385, :540-636).
+//
+// Orientation: C^T tile = W_tile (128 output features) x X_tile^T (BT tokens).
+//   * A operand = dequantized weights, written by a dequant warpgroup straight
+//     into TMEM (tcgen05.st) -- 128 lanes = 128 output features, 2 bf16/fp16
+//     per 32-bit column. The dequantized weights never touch shared memory.
+//   * B operand = activation tile X[BT tokens, 64 k] loaded by TMA with the
+//     128-byte swizzle (K-major canonical layout).
+//   * D = fp32 accumulator in TMEM: 128 lanes x BT columns (tokens), double
+//     buffered when TMEM allows so the epilogue overlaps the next tile.
+//   * Packed qweight tiles [8 word rows x 128 columns] arrive by TMA into a
+//     shared-memory ring; scales/zeros are read per group with cached loads.
+//   * Exact dequant: w = RNE(s*(q-z)) as in quant_utils.dequant_gptq_to_fp.
+// Warp roles (384 threads, one persistent CTA per SM):
+//   warp 0 lane 0: TMA producer     warp 1: TMEM alloc + MMA issuer (lane 0)
+//   warps 4-7: dequant warpgroup    warps 8-11: epilogue warpgroup
+// Every mbarrier wait is bounded; on timeout the kernel records an error
+// code, drains its own TMA loads / MMAs, frees TMEM and returns.
+#pragma once
+
+#include "common.cuh"
+
+namespace oc {
+
+struct TcParams {
+  int M, N, Kp;
+  const uint32_t* qz;      // [G, N/8]
+  const void* s;           // [G, N]
+  int s_dtype;
+  const int32_t* wgrp;     // [Kp/8] or null
+  int G, gs, v1;
+  const void* bias;
+  int bias_dtype;
+  uint16_t* out;
+  long long ldc;
+  int n_tiles_n, n_tiles_m, num_tiles;
+};
+
+constexpr int kTcThreads = 384;
+constexpr int kTcBK = 64;            // k per pipeline stage (one 128-byte swizzle atom of 16-bit)
+constexpr int kTcBN = 128;           // output features per tile (= TMEM lanes = UMMA M)
+constexpr int kTcWStageBytes = 8 * kTcBN * 4;
+
+template <int BT, int ACC_STAGES, int X_STAGES, int W_STAGES, int A_STAGES>
+struct TcCfg {
+  static constexpr int kAccCols = ACC_STAGES * BT;
+  static constexpr int kACols = A_STAGES * (kTcBK / 2);
+  static_assert(kAccCols + kACols <= 512, "TMEM budget");
+  static constexpr int kXStageBytes = BT * 128;
+  static constexpr int kSmemBytes = X_STAGES * kXStageBytes + W_STAGES * kTcWStageBytes + 1024 /*align*/ +
+                                    (2 * (X_STAGES + W_STAGES + A_STAGES + ACC_STAGES) + 2) * 8 + 64;
+};
+
+template <bool BF16, bool HAS_LO, int BT, int ACC_STAGES, int X_STAGES, int W_STAGES, int A_STAGES>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    gptq_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
+                        const TcParams p) {
+  using Cfg = TcCfg<BT, ACC_STAGES, X_STAGES, W_STAGES, A_STAGES>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* x_smem = smem;
+  uint8_t* w_smem = x_smem + X_STAGES * Cfg::kXStageBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(w_smem + W_STAGES * kTcWStageBytes);
+  uint64_t* full_x = bars;
+  uint64_t* empty_x = full_x + X_STAGES;
+  uint64_t* full_w = empty_x + X_STAGES;
+  uint64_t* empty_w = full_w + W_STAGES;
+  uint64_t* full_a = empty_w + W_STAGES;
+  uint64_t* empty_a = full_a + A_STAGES;
+  uint64_t* full_acc = empty_a + A_STAGES;
+  uint64_t* empty_acc = full_acc + ACC_STAGES;
+  uint64_t* drain = empty_acc + ACC_STAGES;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = warp_id(), lane = lane_id();
+  const int KB = (p.Kp + kTcBK - 1) / kTcBK;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < X_STAGES; ++i) { mbar_init(&full_x[i], 1); mbar_init(&empty_x[i], 1); }
+    for (int i = 0; i < W_STAGES; ++i) { mbar_init(&full_w[i], 1); mbar_init(&empty_w[i], 128); }
+    for (int i = 0; i < A_STAGES; ++i) { mbar_init(&full_a[i], 128); mbar_init(&empty_a[i], 1); }
+    for (int i = 0; i < ACC_STAGES; ++i) { mbar_init(&full_acc[i], 1); mbar_init(&empty_acc[i], 128); }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmap_x);
+    tma_prefetch_desc(&tmap_w);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int sx = 0, px = 0, sw = 0, pw = 0;
+      int x_armed[X_STAGES], w_armed[W_STAGES];
+      for (int i = 0; i < X_STAGES; ++i) x_armed[i] = -1;
+      for (int i = 0; i < W_STAGES; ++i) w_armed[i] = -1;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+        const int nb = tile % p.n_tiles_n, mb = tile / p.n_tiles_n;
+        for (int kb = 0; kb < KB; ++kb) {
+          if (!mbar_wait(&empty_x[sx], px ^ 1, abort_flag, kDevErrTmaEmpty)) { ok = false; break; }
+          mbar_arrive_expect_tx(&full_x[sx], Cfg::kXStageBytes);
+          tma_load_2d(x_smem + sx * Cfg::kXStageBytes, &tmap_x, &full_x[sx], kb * kTcBK, mb * BT);
+          x_armed[sx] = px;
+          if (++sx == X_STAGES) { sx = 0; px ^= 1; }
+          if (!mbar_wait(&empty_w[sw], pw ^ 1, abort_flag, kDevErrWEmpty)) { ok = false; break; }
+          mbar_arrive_expect_tx(&full_w[sw], kTcWStageBytes);
+          tma_load_2d(w_smem + sw * kTcWStageBytes, &tmap_w, &full_w[sw], nb * kTcBN, kb * 8);
+          w_armed[sw] = pw;
+          if (++sw == W_STAGES) { sw = 0; pw ^= 1; }
+        }
+      }
+      if (!ok) {
+        // drain our own loads in flight before the CTA (and its smem) goes away
+        for (int i = 0; i < X_STAGES; ++i)
+          if (x_armed[i] >= 0) {
+            for (uint32_t it = 0; it < OC_WAIT_LIMIT && !mbar_try_wait(&full_x[i], x_armed[i]); ++it) {}
+          }
+        for (int i = 0; i < W_STAGES; ++i)
+          if (w_armed[i] >= 0) {
+            for (uint32_t it = 0; it < OC_WAIT_LIMIT && !mbar_try_wait(&full_w[i], w_armed[i]); ++it) {}
+          }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_f16(BF16, kTcBN, BT);
+      int sx = 0, px = 0, sa = 0, pa = 0, sc = 0, pc = 0;
+      bool ok = true, issued = false;
+      for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+        if (!mbar_wait(&empty_acc[sc], pc ^ 1, abort_flag, kDevErrAccEmpty)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(sc * BT);
+        for (int kb = 0; kb < KB; ++kb) {
+          if (!mbar_wait(&full_x[sx], px, abort_flag, kDevErrTmaFull)) { ok = false; break; }
+          if (!mbar_wait(&full_a[sa], pa, abort_flag, kDevErrAFull)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t xaddr = smem_u32(x_smem + sx * Cfg::kXStageBytes);
+          const uint32_t a_tmem = tmem_base + (uint32_t)(Cfg::kAccCols + sa * (kTcBK / 2));
+#pragma unroll
+          for (int j = 0; j < kTcBK / 16; ++j) {
+            const uint64_t bdesc = smem_desc_kmajor_sw128(xaddr + j * 32);
+            tc_mma_ts(d_tmem, a_tmem + j * 8, bdesc, idesc, (kb | j) != 0 ? 1u : 0u);
+          }
+          issued = true;
+          tc_commit(&empty_x[sx]);
+          tc_commit(&empty_a[sa]);
+          if (++sx == X_STAGES) { sx = 0; px ^= 1; }
+          if (++sa == A_STAGES) { sa = 0; pa ^= 1; }
+        }
+        if (!ok) break;
+        tc_commit(&full_acc[sc]);
+        if (++sc == ACC_STAGES) { sc = 0; pc ^= 1; }
+      }
+      if (!ok && issued) {
+        tc_commit(drain);
+        for (uint32_t it = 0; it < OC_WAIT_LIMIT && !mbar_try_wait(drain, 0); ++it) {}
+      }
+    }
+  } else if (warp >= 4 && warp < 8) {
+    // ------------------------------------------------------------ dequant warpgroup
+    using Pp = Pair<BF16>;
+    const int q4 = warp & 3;
+    const int row = q4 * 32 + lane;  // TMEM lane == output feature within the tile
+    const int kw_rows = p.Kp >> 3;
+    int sw = 0, pw = 0, sa = 0, pa = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+      const int nb = tile % p.n_tiles_n;
+      const int n = nb * kTcBN + row;
+      const bool nvalid = n < p.N;
+      const int nn = nvalid ? n : 0;
+      for (int kb = 0; kb < KB; ++kb) {
+        // group constants for the 8 words of this k-block (loads issued before the smem wait)
+        float sv[8];
+        uint32_t zv[8];
+        int last = -1;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+          const int kw = kb * 8 + w;
+          const int grp = (kw < kw_rows) ? (p.wgrp ? __ldg(p.wgrp + kw) : (8 * kw) / p.gs) : 0;
+          if (grp != last) {
+            sv[w] = load_as_f32(p.s, p.s_dtype, (long long)grp * p.N + nn);
+            zv[w] = __ldg(p.qz + (long long)grp * (p.N >> 3) + (nn >> 3));
+            last = grp;
+          } else {
+            sv[w] = sv[w > 0 ? w - 1 : 0];
+            zv[w] = zv[w > 0 ? w - 1 : 0];
+          }
+        }
+        if (!mbar_wait(&full_w[sw], pw, abort_flag, kDevErrWFull)) { ok = false; break; }
+        const uint32_t* wt = reinterpret_cast<const uint32_t*>(w_smem + sw * kTcWStageBytes);
+        uint32_t q[8];
+#pragma unroll
+        for (int w = 0; w < 8; ++w) q[w] = wt[w * kTcBN + row];
+        mbar_arrive(&empty_w[sw]);
+        if (++sw == W_STAGES) { sw = 0; pw ^= 1; }
+
+        uint32_t r[32];
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+          uint32_t z = (zv[w] >> (4 * (nn & 7))) & 0xFu;
+          if (p.v1) z = (z + 1u) & 0xFu;
+          const DqConst<BF16> c = make_dq_const<BF16>(sv[w], (int)z);
+          const uint32_t qq = q[w];
+          const uint32_t p0 = dq_pair<BF16, HAS_LO>(lop3_and_or(qq, 0x000F000Fu, Pp::kMagic), c);        // k0,k4
+          const uint32_t p1 = dq_pair<BF16, HAS_LO>(lop3_and_or(qq >> 4, 0x000F000Fu, Pp::kMagic), c);   // k1,k5
+          const uint32_t p2 = dq_pair<BF16, HAS_LO>(lop3_and_or(qq >> 8, 0x000F000Fu, Pp::kMagic), c);   // k2,k6
+          const uint32_t p3 = dq_pair<BF16, HAS_LO>(lop3_and_or(qq >> 12, 0x000F000Fu, Pp::kMagic), c);  // k3,k7
+          r[4 * w + 0] = prmt(p0, p1, 0x5410u);  // k0,k1
+          r[4 * w + 1] = prmt(p2, p3, 0x5410u);  // k2,k3
+          r[4 * w + 2] = prmt(p0, p1, 0x7632u);  // k4,k5
+          r[4 * w + 3] = prmt(p2, p3, 0x7632u);  // k6,k7
+        }
+        if (!mbar_wait(&empty_a[sa], pa ^ 1, abort_flag, kDevErrAEmpty)) { ok = false; break; }
+        tc_fence_after();
+        __syncwarp();
+        const uint32_t taddr = tmem_base + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(Cfg::kAccCols + sa * (kTcBK / 2));
+        tmem_st_32x32b_x32(taddr, r);
+        tc_wait_st();
+        tc_fence_before();
+        mbar_arrive(&full_a[sa]);
+        if (++sa == A_STAGES) { sa = 0; pa ^= 1; }
+      }
+    }
+  } else if (warp >= 8) {
+    // ------------------------------------------------------------ epilogue warpgroup
+    const int q4 = warp & 3;
+    const int row = q4 * 32 + lane;
+    const int odt = BF16 ? kBF16 : kF16;
+    int sc = 0, pc = 0;
+    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+      const int nb = tile % p.n_tiles_n, mb = tile / p.n_tiles_n;
+      const int n = nb * kTcBN + row;
+      const bool nvalid = n < p.N;
+      const float bv = (p.bias && nvalid) ? load_as_f32(p.bias, p.bias_dtype, n) : 0.f;
+      if (!mbar_wait(&full_acc[sc], pc, abort_flag, kDevErrAccFull)) break;
+      tc_fence_after();
+      __syncwarp();
+      const uint32_t tbase = tmem_base + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(sc * BT);
+#pragma unroll 1
+      for (int c = 0; c < BT / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tbase + (uint32_t)(c * 32), v);
+        tc_wait_ld();
+        const int m0 = mb * BT + c * 32;
+        if (nvalid) {
+          uint16_t* dst = p.out + (long long)m0 * p.ldc + n;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            if (m0 + i < p.M) dst[(long long)i * p.ldc] = f32_to_bits(__uint_as_float(v[i]) + bv, odt);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&empty_acc[sc]);
+      if (++sc == ACC_STAGES) { sc = 0; pc ^= 1; }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
+}  // namespace oc

@@ -1,0 +1,526 @@
+// C ABI of the onecomp B200 hot path: argument checks, launch configuration,
+// TMA descriptors and kernel dispatch. One translation unit (no -rdc).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/oc_b200.h"
+#include "common.cuh"
+#include "dequant.cuh"
+#include "gemm_tc.cuh"
+#include "gemv.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_check(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return OC_OK;
+  return fail(OC_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+int launch_check(const char* what) { return cuda_check(cudaGetLastError(), what); }
+
+bool dt16(int dt) { return dt == OC_DT_F16 || dt == OC_DT_BF16; }
+bool dtf(int dt) { return dt == OC_DT_F16 || dt == OC_DT_BF16 || dt == OC_DT_F32; }
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+std::atomic<int> g_opt_path{0}, g_opt_tile{0}, g_opt_gemv_ctas{3};
+
+constexpr int kMaxDevices = 64;
+int g_sm_count[kMaxDevices];
+std::mutex g_mu;
+
+int current_device(int* dev) { return cuda_check(cudaGetDevice(dev), "cudaGetDevice"); }
+
+int sm_count(int dev) {
+  if (dev < 0 || dev >= kMaxDevices) return 148;
+  if (g_sm_count[dev] == 0) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    g_sm_count[dev] = v > 0 ? v : 148;
+  }
+  return g_sm_count[dev];
+}
+
+int grid_1d(long long total, int threads, int dev) {
+  long long blocks = (total + threads - 1) / threads;
+  long long cap = (long long)sm_count(dev) * 16;
+  if (blocks > cap) blocks = cap;
+  return (int)(blocks < 1 ? 1 : blocks);
+}
+
+// ---- cuTensorMapEncodeTiled through the runtime's driver entry point -------
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+int make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dt, int esize, const void* base, uint64_t inner,
+                 uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+                 CUtensorMapSwizzle swz) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(OC_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  if (!aligned(base, 16) || row_stride_bytes % 16 != 0 || (box_inner * esize) % 16 != 0)
+    return fail(OC_ERR_INVALID, "TMA operand alignment: base %p stride %llu", base,
+                (unsigned long long)row_stride_bytes);
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(OC_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return OC_OK;
+}
+
+}  // namespace
+
+struct oc_b200_layer {
+  int device;
+  const uint32_t* qw;
+  const uint32_t* qz;
+  const void* s;
+  int s_dtype;
+  const int32_t* kperm;
+  const int32_t* wgrp;
+  int K_in, Kp, N, G, gs, v1;
+  CUtensorMap tmap_w;
+};
+
+extern "C" {
+
+int oc_b200_abi_version(void) { return 1; }
+
+const char* oc_b200_last_error(void) { return g_last_error.c_str(); }
+
+int oc_b200_device_check(int device) {
+  int major = 0, minor = 0;
+  int rc = cuda_check(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device), "capability");
+  if (rc) return rc;
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device);
+  if (major != 10 || minor != 0)
+    return fail(OC_ERR_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a (B200) only", device,
+                major, minor);
+  return OC_OK;
+}
+
+int oc_b200_set_option(int key, int value) {
+  switch (key) {
+    case OC_OPT_GEMM_PATH:
+      if (value < 0 || value > 2) return fail(OC_ERR_INVALID, "OC_OPT_GEMM_PATH: %d", value);
+      g_opt_path = value;
+      return OC_OK;
+    case OC_OPT_TC_TILE:
+      if (value != 0 && value != 128 && value != 192 && value != 256)
+        return fail(OC_ERR_INVALID, "OC_OPT_TC_TILE: %d", value);
+      g_opt_tile = value;
+      return OC_OK;
+    case OC_OPT_GEMV_CTAS:
+      if (value < 1 || value > 32) return fail(OC_ERR_INVALID, "OC_OPT_GEMV_CTAS: %d", value);
+      g_opt_gemv_ctas = value;
+      return OC_OK;
+  }
+  return fail(OC_ERR_INVALID, "unknown option %d", key);
+}
+
+int oc_b200_read_device_error(int* code, oc_stream_t stream) {
+  if (!code) return fail(OC_ERR_INVALID, "code is NULL");
+  unsigned v = 0, zero = 0;
+  int rc = cuda_check(cudaMemcpyFromSymbolAsync(&v, oc::g_oc_dev_error, sizeof(v), 0, cudaMemcpyDeviceToHost, stream),
+                      "read device error");
+  if (rc) return rc;
+  rc = cuda_check(cudaMemcpyToSymbolAsync(oc::g_oc_dev_error, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice, stream),
+                  "clear device error");
+  if (rc) return rc;
+  rc = cuda_check(cudaStreamSynchronize(stream), "sync");
+  if (rc) return rc;
+  *code = (int)v;
+  return OC_OK;
+}
+
+// ---------------------------------------------------------------- unpack / pack / dequant
+int oc_b200_gptq_unpack(const int32_t* qweight, int K, int N, int wbits, int32_t* w_int, oc_stream_t stream) {
+  if (!qweight || !w_int || K <= 0 || N <= 0) return fail(OC_ERR_INVALID, "gptq_unpack: bad arguments");
+  if (32 % wbits != 0) return fail(OC_ERR_INVALID, "wbits must divide 32, got %d", wbits);
+  int dev = 0;
+  if (int rc = current_device(&dev)) return rc;
+  oc::gptq_unpack_kernel<<<grid_1d((long long)K * N, 256, dev), 256, 0, stream>>>(
+      reinterpret_cast<const uint32_t*>(qweight), K, N, wbits, w_int);
+  return launch_check("gptq_unpack");
+}
+
+int oc_b200_gptq_unpack_zeros(const int32_t* qzeros, int G, int N, int wbits, int32_t* zeros, oc_stream_t stream) {
+  if (!qzeros || !zeros || G <= 0 || N <= 0) return fail(OC_ERR_INVALID, "gptq_unpack_zeros: bad arguments");
+  if (32 % wbits != 0 || N % (32 / wbits) != 0) return fail(OC_ERR_INVALID, "unpack_zeros: wbits %d N %d", wbits, N);
+  int dev = 0;
+  if (int rc = current_device(&dev)) return rc;
+  oc::gptq_unpack_zeros_kernel<<<grid_1d((long long)G * N, 256, dev), 256, 0, stream>>>(
+      reinterpret_cast<const uint32_t*>(qzeros), G, N, wbits, zeros);
+  return launch_check("gptq_unpack_zeros");
+}
+
+int oc_b200_gptq_pack(const int32_t* w_int, int N, int K, int wbits, int32_t* qweight, oc_stream_t stream) {
+  if (!w_int || !qweight || K <= 0 || N <= 0) return fail(OC_ERR_INVALID, "gptq_pack: bad arguments");
+  if (32 % wbits != 0) return fail(OC_ERR_INVALID, "wbits must divide 32, got %d", wbits);
+  int dev = 0;
+  if (int rc = current_device(&dev)) return rc;
+  const int rows = (K + 32 / wbits - 1) / (32 / wbits);
+  oc::gptq_pack_kernel<<<grid_1d((long long)rows * N, 256, dev), 256, 0, stream>>>(
+      w_int, N, K, wbits, reinterpret_cast<uint32_t*>(qweight));
+  return launch_check("gptq_pack");
+}
+
+int oc_b200_gptq_dequant(const int32_t* qweight, const int32_t* qzeros, const void* scales, int scales_dtype,
+                         const int64_t* g_idx, int K, int N, int G, int groupsize, int wbits, int v1, void* out,
+                         int out_dtype, oc_stream_t stream) {
+  if (!qweight || !qzeros || !scales || !out) return fail(OC_ERR_INVALID, "gptq_dequant: NULL pointer");
+  if (K <= 0 || N <= 0 || G <= 0) return fail(OC_ERR_INVALID, "gptq_dequant: K=%d N=%d G=%d", K, N, G);
+  if (wbits != 4 && wbits != 8 && wbits != 2) return fail(OC_ERR_UNSUPPORTED, "gptq_dequant: wbits=%d", wbits);
+  if (N % (32 / wbits) != 0) return fail(OC_ERR_INVALID, "N=%d must be a multiple of %d", N, 32 / wbits);
+  if (!g_idx && groupsize <= 0) return fail(OC_ERR_INVALID, "groupsize must be > 0 without g_idx");
+  if (!dtf(scales_dtype) || !dtf(out_dtype)) return fail(OC_ERR_INVALID, "gptq_dequant: dtype");
+  const int pf = 32 / wbits;
+  if (out_dtype == OC_DT_F32) {
+    int dev = 0;
+    if (int rc = current_device(&dev)) return rc;
+    oc::gptq_dequant_f32_kernel<<<grid_1d((long long)N * K, 256, dev), 256, 0, stream>>>(
+        reinterpret_cast<const uint32_t*>(qweight), reinterpret_cast<const uint32_t*>(qzeros), scales, scales_dtype,
+        reinterpret_cast<const long long*>(g_idx), K, N, groupsize, wbits, v1, reinterpret_cast<float*>(out));
+    return launch_check("gptq_dequant_f32");
+  }
+  dim3 grid((N + 31) / 32, ((K + pf - 1) / pf + 7) / 8);
+  const auto* qw = reinterpret_cast<const uint32_t*>(qweight);
+  const auto* qz = reinterpret_cast<const uint32_t*>(qzeros);
+  auto* o = reinterpret_cast<uint16_t*>(out);
+  const auto* gi = reinterpret_cast<const long long*>(g_idx);
+  if (wbits == 4)
+    oc::gptq_dequant_kernel<4><<<grid, 256, 0, stream>>>(qw, qz, scales, scales_dtype, gi, K, N, G, groupsize, v1, o,
+                                                         out_dtype);
+  else if (wbits == 8)
+    oc::gptq_dequant_kernel<8><<<grid, 256, 0, stream>>>(qw, qz, scales, scales_dtype, gi, K, N, G, groupsize, v1, o,
+                                                         out_dtype);
+  else
+    oc::gptq_dequant_kernel<2><<<grid, 256, 0, stream>>>(qw, qz, scales, scales_dtype, gi, K, N, G, groupsize, v1, o,
+                                                         out_dtype);
+  return launch_check("gptq_dequant");
+}
+
+int oc_b200_rtn_dequant(const uint8_t* qweight_u8, int64_t ld_bytes, const void* scales, int scales_dtype,
+                        const void* zeros, int zeros_dtype, int K, int N, int G, void* out, int out_dtype,
+                        oc_stream_t stream) {
+  if (!qweight_u8 || !scales || !zeros || !out) return fail(OC_ERR_INVALID, "rtn_dequant: NULL pointer");
+  if (K <= 0 || N <= 0 || G <= 0 || ld_bytes * 2 < K) return fail(OC_ERR_INVALID, "rtn_dequant: shape");
+  if (G != 1 && K % G != 0)
+    return fail(OC_ERR_INVALID, "in_features=%d not divisible by num_groups=%d", K, G);
+  if (!dtf(scales_dtype) || !dtf(zeros_dtype) || !dt16(out_dtype)) return fail(OC_ERR_INVALID, "rtn_dequant: dtype");
+  int dev = 0;
+  if (int rc = current_device(&dev)) return rc;
+  oc::rtn_dequant_kernel<<<grid_1d((long long)N * K, 256, dev), 256, 0, stream>>>(
+      qweight_u8, ld_bytes, scales, scales_dtype, zeros, zeros_dtype, K, N, G, reinterpret_cast<uint16_t*>(out),
+      out_dtype);
+  return launch_check("rtn_dequant");
+}
+
+int oc_b200_dsv4_dequant(const uint8_t* packed, int64_t ld_bytes, int wbits, const void* scales, int scales_dtype,
+                         const void* zeros, int zeros_dtype, int64_t stride_n, int64_t stride_g, int groupsize,
+                         int K, int N, void* out, int out_dtype, oc_stream_t stream) {
+  if (!packed || !scales || !zeros || !out) return fail(OC_ERR_INVALID, "dsv4_dequant: NULL pointer");
+  if (wbits != 2 && wbits != 4 && wbits != 8) return fail(OC_ERR_UNSUPPORTED, "dsv4_dequant: wbits=%d", wbits);
+  if (K <= 0 || N <= 0 || ld_bytes * (8 / wbits) < K) return fail(OC_ERR_INVALID, "dsv4_dequant: shape");
+  if (!dtf(scales_dtype) || !dtf(zeros_dtype) || !dt16(out_dtype)) return fail(OC_ERR_INVALID, "dsv4_dequant: dtype");
+  int dev = 0;
+  if (int rc = current_device(&dev)) return rc;
+  oc::dsv4_dequant_kernel<<<grid_1d((long long)N * K, 256, dev), 256, 0, stream>>>(
+      packed, ld_bytes, wbits, scales, scales_dtype, zeros, zeros_dtype, stride_n, stride_g, groupsize, K, N,
+      reinterpret_cast<uint16_t*>(out), out_dtype);
+  return launch_check("dsv4_dequant");
+}
+
+int oc_b200_gptq_repack_k(const int32_t* qweight, const int32_t* k_perm, int k_packed, int N, int32_t* qweight_out,
+                          oc_stream_t stream) {
+  if (!qweight || !k_perm || !qweight_out) return fail(OC_ERR_INVALID, "repack_k: NULL pointer");
+  if (k_packed <= 0 || k_packed % 8 != 0 || N <= 0) return fail(OC_ERR_INVALID, "repack_k: k_packed=%d", k_packed);
+  int dev = 0;
+  if (int rc = current_device(&dev)) return rc;
+  oc::gptq_repack_k_kernel<<<grid_1d((long long)(k_packed / 8) * N, 256, dev), 256, 0, stream>>>(
+      reinterpret_cast<const uint32_t*>(qweight), k_perm, k_packed, N, reinterpret_cast<uint32_t*>(qweight_out));
+  return launch_check("repack_k");
+}
+
+int oc_b200_permute_cols(const void* x, int64_t ldx, int64_t M, int K, const int32_t* k_perm, int k_packed,
+                         void* x_out, oc_stream_t stream) {
+  if (!x || !k_perm || !x_out || M < 0 || K <= 0 || k_packed <= 0) return fail(OC_ERR_INVALID, "permute_cols");
+  if (M == 0) return OC_OK;
+  int dev = 0;
+  if (int rc = current_device(&dev)) return rc;
+  oc::permute_cols_kernel<<<grid_1d(M * k_packed, 256, dev), 256, 0, stream>>>(
+      reinterpret_cast<const uint16_t*>(x), ldx, (int)M, K, k_perm, k_packed, reinterpret_cast<uint16_t*>(x_out));
+  return launch_check("permute_cols");
+}
+
+// ---------------------------------------------------------------- GPTQ layer
+int oc_b200_gptq_layer_create(const int32_t* qweight, const int32_t* qzeros, const void* scales, int scales_dtype,
+                              const int32_t* k_perm, const int32_t* word_group, int in_features, int k_packed, int N,
+                              int G, int groupsize, int v1, oc_b200_layer** out) {
+  if (!out) return fail(OC_ERR_INVALID, "layer_create: out is NULL");
+  *out = nullptr;
+  if (!qweight || !qzeros || !scales) return fail(OC_ERR_INVALID, "layer_create: NULL tensor");
+  if (!dt16(scales_dtype)) return fail(OC_ERR_UNSUPPORTED, "layer_create: scales must be f16 or bf16");
+  if (in_features <= 0 || k_packed <= 0 || k_packed % 8 != 0)
+    return fail(OC_ERR_INVALID, "layer_create: in_features=%d k_packed=%d (k_packed must be a multiple of 8)",
+                in_features, k_packed);
+  if (!k_perm && k_packed != in_features)
+    return fail(OC_ERR_INVALID, "layer_create: k_packed != in_features needs k_perm");
+  if (N <= 0 || N % 8 != 0) return fail(OC_ERR_INVALID, "layer_create: N=%d must be a multiple of 8", N);
+  if (G <= 0 || (!word_group && (groupsize <= 0 || groupsize % 8 != 0)))
+    return fail(OC_ERR_INVALID, "layer_create: groupsize=%d must be a positive multiple of 8 without word_group",
+                groupsize);
+  if (!aligned(qweight, 16) || !aligned(scales, 8) || !aligned(qzeros, 4))
+    return fail(OC_ERR_INVALID, "layer_create: misaligned weight tensors");
+  int dev = 0;
+  if (int rc = current_device(&dev)) return rc;
+  if (int rc = oc_b200_device_check(dev)) return rc;
+  auto* L = new oc_b200_layer();
+  L->device = dev;
+  L->qw = reinterpret_cast<const uint32_t*>(qweight);
+  L->qz = reinterpret_cast<const uint32_t*>(qzeros);
+  L->s = scales;
+  L->s_dtype = scales_dtype;
+  L->kperm = k_perm;
+  L->wgrp = word_group;
+  L->K_in = in_features;
+  L->Kp = k_packed;
+  L->N = N;
+  L->G = G;
+  L->gs = groupsize;
+  L->v1 = v1 ? 1 : 0;
+  int rc = make_tmap_2d(&L->tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, qweight, (uint64_t)N, (uint64_t)(k_packed / 8),
+                        (uint64_t)N * 4, oc::kTcBN, 8, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc) {
+    delete L;
+    return rc;
+  }
+  *out = L;
+  return OC_OK;
+}
+
+int oc_b200_layer_destroy(oc_b200_layer* layer) {
+  delete layer;
+  return OC_OK;
+}
+
+}  // extern "C"
+
+namespace {
+
+constexpr size_t kTicketBytes = 1024;  // 256 tickets: enough for N <= 32768 (128 columns each)
+
+struct GemvPlan {
+  int splits, kstep;
+};
+
+GemvPlan gemv_plan(const oc_b200_layer* L, int dev) {
+  const int n_tiles = (L->N + oc::kGemvCols - 1) / oc::kGemvCols;
+  const int steps = (L->Kp + 31) / 32;
+  const int target = sm_count(dev) * g_opt_gemv_ctas.load();
+  int splits = (target + n_tiles - 1) / n_tiles;
+  const int max_splits = steps / 8 > 0 ? steps / 8 : 1;
+  if (splits > max_splits) splits = max_splits;
+  if (splits < 1) splits = 1;
+  if (n_tiles > (int)(kTicketBytes / 4)) splits = 1;
+  int kstep = (steps + splits - 1) / splits;
+  splits = (steps + kstep - 1) / kstep;
+  return {splits, kstep};
+}
+
+bool use_gemv(int64_t M) {
+  const int path = g_opt_path.load();
+  if (path == 1) return M <= 16;
+  if (path == 2) return false;
+  return M <= 16;
+}
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+}  // namespace
+
+extern "C" size_t oc_b200_gptq_gemm_workspace(const oc_b200_layer* L, int64_t M) {
+  if (!L || M <= 0) return kTicketBytes;
+  size_t bytes = kTicketBytes;
+  if (L->kperm) bytes += align_up((size_t)M * L->Kp * 2, 256);  // gathered activations
+  if (use_gemv(M)) {
+    const GemvPlan gp = gemv_plan(L, L->device);
+    if (gp.splits > 1) bytes += align_up((size_t)gp.splits * M * L->N * 4, 256);
+  }
+  return bytes;
+}
+
+namespace {
+
+template <bool BF16, bool HAS_LO>
+int launch_gemv(const oc::GemvParams& p, int n_tiles, int splits, cudaStream_t stream) {
+  dim3 grid(n_tiles, splits);
+  if (p.M <= 8)
+    oc::gptq_gemv_kernel<BF16, HAS_LO, 1, 4><<<grid, oc::kGemvThreads, 0, stream>>>(p);
+  else
+    oc::gptq_gemv_kernel<BF16, HAS_LO, 2, 4><<<grid, oc::kGemvThreads, 0, stream>>>(p);
+  return launch_check("gptq_gemv");
+}
+
+template <bool BF16, bool HAS_LO, int BT, int ACC, int XS, int WS, int AS>
+int launch_tc_t(const CUtensorMap& tx, const CUtensorMap& tw, const oc::TcParams& p, int dev, cudaStream_t stream) {
+  using Cfg = oc::TcCfg<BT, ACC, XS, WS, AS>;
+  auto kern = oc::gptq_gemm_tc_kernel<BF16, HAS_LO, BT, ACC, XS, WS, AS>;
+  static bool attr_set[kMaxDevices] = {};
+  if (dev >= 0 && dev < kMaxDevices && !attr_set[dev]) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (int rc = cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes),
+                            "cudaFuncSetAttribute(smem)"))
+      return rc;
+    attr_set[dev] = true;
+  }
+  int grid = p.num_tiles < sm_count(dev) ? p.num_tiles : sm_count(dev);
+  kern<<<grid, oc::kTcThreads, Cfg::kSmemBytes, stream>>>(tx, tw, p);
+  return launch_check("gptq_gemm_tc");
+}
+
+template <bool BF16, bool HAS_LO>
+int launch_tc(int bt, const CUtensorMap& tx, const CUtensorMap& tw, const oc::TcParams& p, int dev,
+              cudaStream_t stream) {
+  if (bt == 128) return launch_tc_t<BF16, HAS_LO, 128, 2, 6, 8, 8>(tx, tw, p, dev, stream);
+  if (bt == 256) return launch_tc_t<BF16, HAS_LO, 256, 1, 4, 8, 4>(tx, tw, p, dev, stream);
+  return launch_tc_t<BF16, HAS_LO, 192, 2, 5, 8, 4>(tx, tw, p, dev, stream);
+}
+
+}  // namespace
+
+extern "C" int oc_b200_gptq_gemm(const oc_b200_layer* L, const void* a, int a_dtype, int64_t M, int64_t lda, const void* bias,
+                      int bias_dtype, void* c, int64_t ldc, void* workspace, size_t workspace_bytes,
+                      oc_stream_t stream_) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  if (!L) return fail(OC_ERR_INVALID, "gptq_gemm: layer is NULL");
+  if (M < 0) return fail(OC_ERR_INVALID, "gptq_gemm: M=%lld", (long long)M);
+  if (M == 0) return OC_OK;
+  if (!a || !c) return fail(OC_ERR_INVALID, "gptq_gemm: NULL activation/output");
+  if (!dt16(a_dtype)) return fail(OC_ERR_INVALID, "gptq_gemm: activations must be f16 or bf16");
+  if (bias && !dtf(bias_dtype)) return fail(OC_ERR_INVALID, "gptq_gemm: bias dtype");
+  if (lda < L->K_in || lda % 8 != 0 || !aligned(a, 16))
+    return fail(OC_ERR_INVALID, "gptq_gemm: A must be 16-byte aligned with lda %% 8 == 0 (lda=%lld)", (long long)lda);
+  if (ldc < L->N || ldc % 4 != 0 || !aligned(c, 8))
+    return fail(OC_ERR_INVALID, "gptq_gemm: C must be 8-byte aligned with ldc %% 4 == 0 (ldc=%lld)", (long long)ldc);
+  if (M > 0x7fffffffLL) return fail(OC_ERR_INVALID, "gptq_gemm: M too large");
+  int dev = 0;
+  if (int rc = current_device(&dev)) return rc;
+  if (dev != L->device) return fail(OC_ERR_INVALID, "gptq_gemm: layer lives on device %d, current is %d", L->device, dev);
+  const size_t need = oc_b200_gptq_gemm_workspace(L, M);
+  if (!workspace || workspace_bytes < need || !aligned(workspace, 256))
+    return fail(OC_ERR_WORKSPACE, "gptq_gemm: workspace needs %zu bytes (got %zu)", need, workspace_bytes);
+  uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
+  unsigned* tickets = reinterpret_cast<unsigned*>(ws);
+  size_t off = kTicketBytes;
+
+  // activations in kernel K order
+  const uint16_t* xk = reinterpret_cast<const uint16_t*>(a);
+  int64_t ldx = lda;
+  if (L->kperm) {
+    uint16_t* xg = reinterpret_cast<uint16_t*>(ws + off);
+    off += align_up((size_t)M * L->Kp * 2, 256);
+    if (int rc = oc_b200_permute_cols(a, lda, M, L->K_in, L->kperm, L->Kp, xg, stream_)) return rc;
+    xk = xg;
+    ldx = L->Kp;
+  }
+  const bool bf16 = a_dtype == OC_DT_BF16;
+  const bool has_lo = L->s_dtype != a_dtype;
+
+  if (use_gemv(M)) {
+    const GemvPlan gp = gemv_plan(L, dev);
+    oc::GemvParams p{};
+    p.x = xk;
+    p.ldx = ldx;
+    p.M = (int)M;
+    p.qw = L->qw;
+    p.qz = L->qz;
+    p.s = L->s;
+    p.s_dtype = L->s_dtype;
+    p.wgrp = L->wgrp;
+    p.Kp = L->Kp;
+    p.N = L->N;
+    p.G = L->G;
+    p.gs = L->gs;
+    p.v1 = L->v1;
+    p.bias = bias;
+    p.bias_dtype = bias_dtype;
+    p.out = reinterpret_cast<uint16_t*>(c);
+    p.ldc = ldc;
+    p.ws = gp.splits > 1 ? reinterpret_cast<float*>(ws + off) : nullptr;
+    p.tickets = tickets;
+    p.splits = gp.splits;
+    p.kstep_per_split = gp.kstep;
+    const int n_tiles = (L->N + oc::kGemvCols - 1) / oc::kGemvCols;
+    if (bf16) return has_lo ? launch_gemv<true, true>(p, n_tiles, gp.splits, stream)
+                            : launch_gemv<true, false>(p, n_tiles, gp.splits, stream);
+    return has_lo ? launch_gemv<false, true>(p, n_tiles, gp.splits, stream)
+                  : launch_gemv<false, false>(p, n_tiles, gp.splits, stream);
+  }
+
+  int bt = g_opt_tile.load();
+  if (bt == 0) bt = 192;
+  CUtensorMap tx;
+  if (int rc = make_tmap_2d(&tx, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xk,
+                            (uint64_t)L->Kp, (uint64_t)M, (uint64_t)ldx * 2, oc::kTcBK, (uint32_t)bt,
+                            CU_TENSOR_MAP_SWIZZLE_128B))
+    return rc;
+  oc::TcParams p{};
+  p.M = (int)M;
+  p.N = L->N;
+  p.Kp = L->Kp;
+  p.qz = L->qz;
+  p.s = L->s;
+  p.s_dtype = L->s_dtype;
+  p.wgrp = L->wgrp;
+  p.G = L->G;
+  p.gs = L->gs;
+  p.v1 = L->v1;
+  p.bias = bias;
+  p.bias_dtype = bias_dtype;
+  p.out = reinterpret_cast<uint16_t*>(c);
+  p.ldc = ldc;
+  p.n_tiles_n = (L->N + oc::kTcBN - 1) / oc::kTcBN;
+  p.n_tiles_m = (int)((M + bt - 1) / bt);
+  p.num_tiles = p.n_tiles_n * p.n_tiles_m;
+  if (bf16) return has_lo ? launch_tc<true, true>(bt, tx, L->tmap_w, p, dev, stream)
+                          : launch_tc<true, false>(bt, tx, L->tmap_w, p, dev, stream);
+  return has_lo ? launch_tc<false, true>(bt, tx, L->tmap_w, p, dev, stream)
+                : launch_tc<false, false>(bt, tx, L->tmap_w, p, dev, stream);
+}
+
+

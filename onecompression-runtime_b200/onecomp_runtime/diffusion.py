@@ -1,0 +1,143 @@
+"""Generic int4 loader for OneCompression GPTQ-packed diffusion checkpoints (B200 build).
+
+Same contract as the reference ``onecomp_runtime/diffusion.py:57-239``: a single
+``safetensors`` file with metadata ``config_json``, ``quant_layers_json``
+(entries ``name, wbits, groupsize, actorder, in_features, out_features``) and
+``checkpoint_format`` (``gptq`` / ``gptq_v2``). The model is built on the meta
+device by ``build_meta_model``, every quantized Linear is swapped for the module
+``backend.build_quant_layer`` returns, the remaining tensors are materialised on
+the device, key checks run, and the unique layer signatures are warmed up.
+``backend`` accepts ``"b200"`` (the default ``"auto"`` resolves to it).
+"""
+from __future__ import annotations
+
+import json
+import time
+from pathlib import Path
+from typing import Any, Callable
+
+import torch
+from safetensors import safe_open
+
+from .backend import build_quant_layer, resolve_backend, resolve_dtype
+from .layers._gptq_base import B200GPTQLinear
+
+
+def load_int4_model(
+    checkpoint_path: str,
+    build_meta_model: Callable[[dict], torch.nn.Module],
+    *,
+    device: str = "cuda:0",
+    dtype: str | torch.dtype = "bfloat16",
+    backend: str | None = "auto",
+    use_fused: bool = True,
+    post_load: Callable[[torch.nn.Module], None] | None = None,
+    prepare_meta_model: Callable[[torch.nn.Module], None] | None = None,
+    quant_layer_filter: Callable[[str], bool] | None = None,
+    tensor_filter: Callable[[str], bool] | None = None,
+    warmup: bool = True,
+    warmup_m_values: tuple[int, ...] = (64, 128, 256, 1024, 4096),
+    label: str = "onecomp_runtime",
+) -> torch.nn.Module:
+    """Rebuild a packed-int4 diffusion transformer for inference on B200."""
+    backend = resolve_backend(backend, use_fused)
+    resolved = resolve_dtype(dtype)
+    dev = torch.device(device)
+    path = Path(checkpoint_path)
+
+    with safe_open(str(path), framework="pt", device="cpu") as f:
+        md = f.metadata() or {}
+        cfg_json = md.get("config_json")
+        quant_layers_json = md.get("quant_layers_json")
+        if cfg_json is None or quant_layers_json is None:
+            raise ValueError(
+                f"{path} is missing 'config_json' / 'quant_layers_json' "
+                "metadata; not a packed OneCompression diffusion checkpoint")
+        cfg = {k: v for k, v in json.loads(cfg_json).items() if not k.startswith("_")}
+        quant_layers = json.loads(quant_layers_json)
+        ckpt_fmt = md.get("checkpoint_format", "gptq")
+        tensor_keys = set(f.keys())
+
+        with torch.device("meta"):
+            model = build_meta_model(cfg)
+        if prepare_meta_model is not None:
+            prepare_meta_model(model)
+
+        modules = dict(model.named_modules())
+        counts = {"gemlite": 0, "a8w4": 0, "a8w4_ffn_up": 0, "mxfp4_ffn": 0, "mxfp4_ffn_up": 0,
+                  "nvfp4_ffn": 0, "fused": 0, "packed": 0, "eager": 0}
+        quant_keys: set[str] = set()
+        quant_names: list[str] = []
+        for entry in quant_layers:
+            name = entry["name"]
+            quant_keys.add(f"{name}.weight")
+            for suffix in ("qweight", "scales", "qzeros", "g_idx", "bias"):
+                key = f"{name}.{suffix}"
+                if key in tensor_keys:
+                    quant_keys.add(key)
+        for entry in quant_layers:
+            entry["checkpoint_format"] = ckpt_fmt
+            name = entry["name"]
+            if quant_layer_filter is not None and not quant_layer_filter(name):
+                continue
+            quant_names.append(name)
+            parent_name, _, child = name.rpartition(".")
+            parent = modules.get(parent_name) if parent_name else model
+            if parent is None:
+                raise KeyError(f"quant layer parent not found: {parent_name!r}")
+            st: dict[str, Any] = {}
+            for s in ("qweight", "scales", "qzeros", "g_idx", "bias"):
+                k = f"{name}.{s}"
+                if k in tensor_keys:
+                    st[s] = f.get_tensor(k)
+            layer, kind = build_quant_layer(entry, st, backend, resolved, dev)
+            counts[kind] += 1
+            setattr(parent, child, layer)
+            del st
+
+        non_quant = {}
+        for k in tensor_keys:
+            if k in quant_keys:
+                continue
+            if tensor_filter is not None and not tensor_filter(k):
+                continue
+            tensor = f.get_tensor(k)
+            non_quant[k] = tensor.to(device=dev, dtype=resolved if tensor.dtype.is_floating_point else tensor.dtype)
+            del tensor
+    missing, unexpected = model.load_state_dict(non_quant, strict=False, assign=True)
+    quant_prefixes = tuple(f"{n}." for n in quant_names)
+    real_missing = [m for m in missing if m not in quant_keys and not m.startswith(quant_prefixes)]
+    if real_missing:
+        raise RuntimeError(f"missing keys: {real_missing[:8]} ...")
+    if unexpected:
+        raise RuntimeError(f"unexpected keys: {unexpected[:8]} ...")
+
+    if post_load is not None:
+        post_load(model)
+
+    leftover = [n for n, p in model.named_parameters() if p.is_meta]
+    if leftover:
+        raise RuntimeError(f"parameter left on meta device: {leftover[:8]} ...")
+
+    model.eval()
+    print(f"[{label}] loaded {len(quant_names)} int4 layers "
+          f"(gemlite={counts['gemlite']}, a8w4={counts['a8w4']}, "
+          f"a8w4_ffn_up={counts['a8w4_ffn_up']}, "
+          f"mxfp4_ffn={counts['mxfp4_ffn']}, "
+          f"mxfp4_ffn_up={counts['mxfp4_ffn_up']}, "
+          f"nvfp4_ffn={counts['nvfp4_ffn']}, fused={counts['fused']}, "
+          f"packed={counts['packed']}, eager={counts['eager']}) on {dev}")
+
+    if warmup and dev.type == "cuda":
+        t0 = time.perf_counter()
+        seen: dict[tuple, Any] = {}
+        for m in model.modules():
+            if isinstance(m, B200GPTQLinear):
+                seen.setdefault((m.in_features, m.out_features, m.bias is not None), m)
+        if seen:
+            for layer in seen.values():
+                layer.warmup(m_values=warmup_m_values)
+            torch.cuda.synchronize(dev)
+            print(f"[{label}] warmup {(time.perf_counter()-t0)*1000:.0f} ms "
+                  f"({len(seen)} unique signatures)")
+    return model

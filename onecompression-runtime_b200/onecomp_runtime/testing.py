@@ -1,0 +1,88 @@
+"""Seeded synthetic packed layers for tests and benchmarks (like ``torch.testing``).
+
+Generates AutoGPTQ / RTN / DSV4 tensors with the shapes and value
+distributions of the benchmark configurations (there are no real checkpoints
+to download): uniform 4-bit codes, zero points stored v1-shifted (``zero - 1``)
+or unshifted (v2), uniform fp16 scales, N(0, 0.02^2) fp16 bias.
+"""
+from __future__ import annotations
+
+import torch
+
+
+def _to_int32(words: torch.Tensor) -> torch.Tensor:
+    """int64 words in [0, 2^32) -> int32 with the same bit pattern."""
+    return ((words + 2**31) % 2**32 - 2**31).to(torch.int32)
+
+
+def pack_along_n(zeros_gn: torch.Tensor, wbits: int = 4) -> torch.Tensor:
+    """int [G, N] -> qzeros int32 [G, N / (32/wbits)] (value j of a word = column pf*c + j)."""
+    pf = 32 // wbits
+    z = zeros_gn.to(torch.int64) & ((1 << wbits) - 1)
+    acc = torch.zeros((z.shape[0], z.shape[1] // pf), dtype=torch.int64, device=z.device)
+    for j in range(pf):
+        acc |= z[:, j::pf] << (wbits * j)
+    return _to_int32(acc)
+
+
+def pack_along_k(codes_nk: torch.Tensor, wbits: int = 4) -> torch.Tensor:
+    """int [N, K] -> qweight int32 [K / (32/wbits), N] (value i of a word = row pf*r + i)."""
+    pf = 32 // wbits
+    rows = codes_nk.t().to(torch.int64) & ((1 << wbits) - 1)
+    acc = torch.zeros((rows.shape[0] // pf, rows.shape[1]), dtype=torch.int64, device=rows.device)
+    for i in range(pf):
+        acc |= rows[i::pf] << (wbits * i)
+    return _to_int32(acc)
+
+
+def gptq_layer(K: int, N: int, groupsize: int, *, seed: int = 0, v1: bool = True, actorder: bool = False,
+               scales_range=(0.002, 0.02), bias: bool = True, device="cpu",
+               scales_dtype=torch.float16) -> dict:
+    """Random AutoGPTQ int4 layer: ``qweight, qzeros, scales, g_idx, bias`` (+ ``codes`` on request)."""
+    gen_dev = torch.device(device)
+    g = torch.Generator(device=gen_dev).manual_seed(int(seed))
+    G = (K + groupsize - 1) // groupsize
+    qweight = torch.randint(-2**31, 2**31, (K // 8, N), generator=g, device=gen_dev, dtype=torch.int64)
+    qweight = qweight.to(torch.int32)
+    zero = torch.randint(1, 16, (G, N), generator=g, device=gen_dev)
+    stored = (zero - 1) & 15 if v1 else zero
+    qzeros = pack_along_n(stored)
+    lo, hi = scales_range
+    scales = (torch.rand((G, N), generator=g, device=gen_dev) * (hi - lo) + lo).to(scales_dtype)
+    if actorder:
+        perm = torch.randperm(K, generator=g, device=gen_dev)
+        g_idx = (torch.arange(K, device=gen_dev) // groupsize)[perm].to(torch.long)
+    else:
+        g_idx = (torch.arange(K, device=gen_dev) // groupsize).to(torch.long)
+    out = {"qweight": qweight, "qzeros": qzeros, "scales": scales, "g_idx": g_idx}
+    if bias:
+        out["bias"] = (torch.randn(N, generator=g, device=gen_dev) * 0.02).to(torch.float16)
+    return out
+
+
+def activations(M: int, K: int, *, seed: int = 0, dtype=torch.bfloat16, device="cpu") -> torch.Tensor:
+    g = torch.Generator(device=torch.device(device)).manual_seed(int(seed))
+    return torch.randn((M, K), generator=g, device=device).to(dtype)
+
+
+# --------------------------------------------------------------------- benchmark configs
+CFG0 = dict(K=3072, N=3072, gs=32, M=256)
+
+# FLUX-style DiT block: hidden 3072; qkv 3072->9216, proj, MLP 3072->9216->3072; M = 4096 + 512 tokens
+CFG1_LAYERS = (("qkv", 3072, 9216), ("proj", 3072, 3072), ("fc1", 3072, 9216), ("fc2", 9216, 3072))
+CFG1 = dict(hidden=3072, blocks=8, M=4608, gs=32)
+
+# dense LLM decode set, gptq_v2, gs=128, act-order
+CFG2_LAYERS = (("qkv", 5120, 8192), ("o", 6144, 5120), ("gate", 5120, 17408), ("up", 5120, 17408),
+               ("down", 17408, 5120))
+CFG2 = dict(gs=128, M=(1, 4, 16), scales_range=(0.001, 0.01))
+
+# video-DiT tensor-parallel stack: hidden 4096; qkv 4096->12288, out 4096->4096, FFN 4096->16384->4096
+CFG4_LAYERS = (("qkv", 4096, 12288), ("out", 4096, 4096), ("fc1", 4096, 16384), ("fc2", 16384, 4096))
+CFG4 = dict(hidden=4096, blocks=12, M=32768, gs=32)
+
+
+def entry(name: str, K: int, N: int, groupsize: int, actorder: bool = False, wbits: int = 4) -> dict:
+    """A ``quant_layers_json`` manifest entry (diffusion.py contract)."""
+    return {"name": name, "wbits": wbits, "groupsize": groupsize, "actorder": actorder,
+            "in_features": K, "out_features": N}

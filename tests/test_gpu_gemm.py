@@ -1,0 +1,188 @@
+"""GEMM parity on the GPU: split-K GEMV (M <= 16) and the tcgen05 kernel against the oracle.
+
+Reference: fp64-accumulated ``x @ W.T + b`` where ``W`` is the oracle's exact
+dequantized weight (bit-identical to quant_utils.dequant_gptq_to_fp); the bar is
+max-abs-relative error <= 2e-2 (north star), and the tests also bound it to
+1e-2 to catch layout bugs that stay inside the loose bound.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GPTQ_CASES, load_golden
+from gpu_util import GEMM_TOL, NAME, TDT, max_abs_rel, oracle_weight, reference_output, to_torch
+from oracle import eager, gptq
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture
+def path_option():
+    from onecomp_runtime import _lib
+    yield lambda v: _lib.set_option(_lib.OPT_GEMM_PATH, v)
+    _lib.set_option(_lib.OPT_GEMM_PATH, 0)
+    _lib.set_option(_lib.OPT_TC_TILE, 0)
+
+
+def _module(t, K, N, gs, v1, kind, device):
+    from onecomp_runtime.layers import FusedInt4Linear, FusedInt4LinearAnyGroup, PackedGPTQLinear
+    tc = {k: v.to(device) for k, v in t.items()}
+    if kind == "fused":
+        return FusedInt4Linear(K, N, tc["qweight"], tc["scales"], tc["qzeros"], tc.get("bias"), 32, v1=v1)
+    if kind == "any":
+        return FusedInt4LinearAnyGroup(K, N, tc["qweight"], tc["scales"], tc["qzeros"], tc.get("bias"), gs, v1=v1)
+    return PackedGPTQLinear(K, N, tc["qweight"], tc["scales"], tc["qzeros"], tc["g_idx"], tc.get("bias"), gs,
+                            4, v1)
+
+
+@pytest.mark.parametrize("case", [c for c in GPTQ_CASES if load_golden(c)["meta"]["M"]])
+@pytest.mark.parametrize("path", [1, 2])
+def test_golden_cases(cuda_device, case, path, path_option):
+    d = load_golden(case)
+    m = d["meta"]
+    if path == 1 and m["M"] > 16:
+        pytest.skip("GEMV path takes M <= 16")
+    path_option(path)
+    from onecomp_runtime.layers import PackedGPTQLinear
+    qw = torch.from_numpy(d["qweight"]).to(cuda_device)
+    qz = torch.from_numpy(d["qzeros"]).to(cuda_device)
+    s = to_torch(d["scales"], m["scales_dtype"])
+    gi = torch.from_numpy(d["g_idx"]).to(cuda_device)
+    bias = to_torch(d["bias_f16"], "f16") if "bias_f16" in d else None
+    layer = PackedGPTQLinear(m["K"], m["N"], qw, s, qz, gi, bias, m["gs"], 4, m["v1"])
+    for od in m["out_dtypes"]:
+        x = to_torch(d[f"x_{od}"], od)
+        y = layer(x)
+        assert y.dtype == TDT[od] and y.shape == (m["M"], m["N"])
+        ref = reference_output(x, d[f"w_{od}"], od, bias)
+        err = max_abs_rel(y, ref)
+        assert err < 1e-2, (case, od, err)
+        # and against the reference's own eager (CPU bf16 nn.Linear) output
+        from oracle.fp import to_f32
+        assert eager.max_abs_rel(y.float().cpu().numpy(), to_f32(d[f"y_{od}"], od)) < GEMM_TOL
+
+
+SHAPES = [
+    # M, K, N, gs, v1, actorder, act dtype, scales dtype, bias
+    (1, 256, 128, 32, True, False, torch.bfloat16, torch.float16, True),
+    (5, 512, 200, 32, True, False, torch.bfloat16, torch.float16, True),
+    (8, 384, 136, 128, False, True, torch.bfloat16, torch.bfloat16, False),
+    (9, 1024, 256, 32, True, False, torch.float16, torch.float16, True),
+    (16, 2048, 384, 128, False, True, torch.bfloat16, torch.float16, True),
+    (17, 512, 256, 32, True, False, torch.bfloat16, torch.float16, True),
+    (100, 768, 392, 64, True, False, torch.float16, torch.bfloat16, True),
+    (193, 1024, 256, 32, True, False, torch.bfloat16, torch.float16, False),
+    (300, 520, 128, 26, True, False, torch.bfloat16, torch.float16, True),
+    (512, 1536, 640, 128, False, True, torch.bfloat16, torch.bfloat16, True),
+]
+
+
+@pytest.mark.parametrize("shape", SHAPES, ids=lambda s: f"M{s[0]}K{s[1]}N{s[2]}g{s[3]}")
+@pytest.mark.parametrize("path", [0, 2])
+def test_shapes(cuda_device, shape, path, path_option):
+    M, K, N, gs, v1, act, adt, sdt, has_bias = shape
+    from onecomp_runtime.testing import gptq_layer, activations
+    path_option(path)
+    t = gptq_layer(K, N, gs, seed=M * 7 + K, v1=v1, actorder=act, bias=has_bias, scales_dtype=sdt)
+    kind = "packed" if (act or gs % 8) else ("fused" if gs == 32 else "any")
+    if gs % 8:
+        from onecomp_runtime.layers import FusedInt4LinearPaddedGroups
+        tc = {k: v.to(cuda_device) for k, v in t.items()}
+        layer = FusedInt4LinearPaddedGroups(K, N, tc["qweight"], tc["scales"], tc["qzeros"], tc.get("bias"), gs, v1=v1)
+    else:
+        layer = _module(t, K, N, gs, v1, kind, cuda_device)
+    x = activations(M, K, seed=M, dtype=adt).to(cuda_device)
+    y = layer(x)
+    w = oracle_weight(t, K, N, NAME[adt], v1=v1)
+    ref = reference_output(x, w, NAME[adt], layer.bias)
+    err = max_abs_rel(y, ref)
+    assert err < 1e-2, err
+
+
+@pytest.mark.parametrize("tile", [128, 192, 256])
+def test_tc_tiles(cuda_device, tile, path_option):
+    from onecomp_runtime import _lib
+    from onecomp_runtime.testing import gptq_layer, activations
+    path_option(2)
+    _lib.set_option(_lib.OPT_TC_TILE, tile)
+    M, K, N = 700, 1024, 384
+    t = gptq_layer(K, N, 32, seed=tile)
+    layer = _module(t, K, N, 32, True, "fused", cuda_device)
+    x = activations(M, K, seed=5).to(cuda_device)
+    y = layer(x)
+    ref = reference_output(x, oracle_weight(t, K, N, "bf16"), "bf16", layer.bias)
+    assert max_abs_rel(y, ref) < 1e-2
+
+
+def test_cfg0_fused_linear(cuda_device):
+    """Config 0: K=N=3072, gs=32, v1, M=256 bf16 through FusedInt4Linear."""
+    from onecomp_runtime.testing import gptq_layer, activations
+    t = gptq_layer(3072, 3072, 32, seed=0)
+    layer = _module(t, 3072, 3072, 32, True, "fused", cuda_device)
+    x = activations(256, 3072, seed=1).to(cuda_device)
+    y = layer(x)
+    ref = reference_output(x, oracle_weight(t, 3072, 3072, "bf16"), "bf16", layer.bias)
+    assert max_abs_rel(y, ref) < 1e-2
+
+
+@pytest.mark.parametrize("M", [1, 4, 16])
+def test_cfg2_decode_layers(cuda_device, M):
+    """Config 2: gptq_v2, gs=128, act-order, scales in bf16 (as backend.build_packed stores them)."""
+    from onecomp_runtime.testing import CFG2_LAYERS, gptq_layer, activations
+    for i, (name, K, N) in enumerate(CFG2_LAYERS):
+        t = gptq_layer(K, N, 128, seed=2000 + i, v1=False, actorder=True, scales_range=(0.001, 0.01),
+                       scales_dtype=torch.bfloat16, bias=False)
+        layer = _module(t, K, N, 128, False, "packed", cuda_device)
+        x = activations(M, K, seed=M + i).to(cuda_device)
+        y = layer(x)
+        ref = reference_output(x, oracle_weight(t, K, N, "bf16", v1=False), "bf16", None)
+        assert max_abs_rel(y, ref) < 1e-2, name
+
+
+def test_full_size_vs_torch_fp32(cuda_device):
+    """Config-1 qkv layer at full M: the tcgen05 kernel vs a torch fp32 GEMM of the exact weight."""
+    from onecomp_runtime import quant_utils
+    from onecomp_runtime.testing import gptq_layer, activations
+    K, N, M = 3072, 9216, 4608
+    t = {k: v.to(cuda_device) for k, v in gptq_layer(K, N, 32, seed=77, device="cpu").items()}
+    layer = _module(t, K, N, 32, True, "fused", cuda_device)
+    x = activations(M, K, seed=3).to(cuda_device)
+    y = layer(x)
+    w = quant_utils.dequant_gptq_to_fp(t["qweight"], t["scales"], t["qzeros"], t["g_idx"], K, N, torch.bfloat16)
+    ref = x.float() @ w.float().t() + t["bias"].float()
+    err = float((y.float() - ref).abs().max() / ref.abs().max())
+    assert err < 1e-2, err
+
+
+def test_module_api(cuda_device):
+    from onecomp_runtime.testing import gptq_layer
+    t = gptq_layer(256, 128, 32, seed=9)
+    layer = _module(t, 256, 128, 32, True, "fused", cuda_device)
+    x3 = torch.randn(2, 3, 256, device=cuda_device, dtype=torch.bfloat16)
+    y3 = layer(x3)
+    assert y3.shape == (2, 3, 128)
+    torch.testing.assert_close(y3.reshape(6, 128), layer(x3.reshape(6, 256)), rtol=0, atol=0)
+    y32 = layer(x3.float())
+    assert y32.dtype == torch.float32
+    y0 = layer(torch.empty(0, 256, device=cuda_device, dtype=torch.bfloat16))
+    assert y0.shape == (0, 128)
+    xs = torch.randn(4, 512, device=cuda_device, dtype=torch.bfloat16)[:, ::2]
+    torch.testing.assert_close(layer(xs), layer(xs.contiguous()), rtol=0, atol=0)
+
+
+def test_fused_int4_gemm_functional(cuda_device):
+    from onecomp_runtime.layers import fused_int4_gemm
+    from onecomp_runtime.testing import gptq_layer, activations
+    t = {k: v.to(cuda_device) for k, v in gptq_layer(512, 256, 32, seed=4).items()}
+    x = activations(40, 512, seed=2, dtype=torch.float16).to(cuda_device)
+    y = fused_int4_gemm(x, t["qweight"], t["scales"], t["qzeros"], t["bias"], 32)
+    ref = reference_output(x, oracle_weight({k: v.cpu() for k, v in t.items()}, 512, 256, "f16"), "f16",
+                           t["bias"])
+    assert y.dtype == torch.float16 and max_abs_rel(y, ref) < 1e-2
+
+
+def test_no_device_errors_recorded(cuda_device):
+    from onecomp_runtime import _lib
+    assert _lib.read_device_error(cuda_device) == 0
