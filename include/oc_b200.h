@@ -124,6 +124,29 @@ int oc_b200_gptq_gemm(const oc_b200_layer* layer, const void* a, int a_dtype, in
                       const void* bias, int bias_dtype, void* c, int64_t ldc, void* workspace,
                       size_t workspace_bytes, oc_stream_t stream);
 
+/* ---- packed-expert MoE -------------------------------- */
+/* The reference routes in an unvendored model file (models/dsv4/loader.py:50-53);
+ * the convention implemented: fp32 softmax over E logits, top-k with ties to the
+ * lower expert id, weights renormalised to sum 1 when renorm != 0.
+ * logits [T, E] (f32/bf16/f16) -> ids int32 [T, k], weights f32 [T, k]. E <= 1024, k <= 16. */
+int oc_b200_moe_route(const void* logits, int logits_dtype, int T, int E, int k, int renorm, int32_t* ids,
+                      float* weights, oc_stream_t stream);
+/* Stable expert-major order of the T*k assignments: counts int32 [E],
+ * offsets int32 [E+1], sorted_token int32 [T*k], slot_pos int32 [T*k]
+ * (sorted position of assignment t*k+j). Replaces the per-expert loop over
+ * Dsv4PackedLinear (dsv4_packed_linear.py:95-98). */
+int oc_b200_moe_permute(const int32_t* ids, int T, int k, int E, int32_t* counts, int32_t* offsets,
+                        int32_t* sorted_token, int32_t* slot_pos, oc_stream_t stream);
+/* dst[p, :] = src[idx[p], :] for 16-bit rows of H elements (H % 8 == 0, 16-byte aligned rows). */
+int oc_b200_gather_rows(const void* src, int64_t lds, const int32_t* idx, int P, int H, void* dst, int64_t ldd,
+                        oc_stream_t stream);
+/* h = silu(g) * u elementwise ([P, F], 16-bit, fp32 math, one rounding). */
+int oc_b200_silu_mul(const void* g, const void* u, int64_t ld_in, int P, int F, void* h, int64_t ld_out, int dtype,
+                     oc_stream_t stream);
+/* out[t, :] = sum_j w[t,j] * y[slot_pos[t*k+j], :] (+ shared[t, :]); fp32 sum, one rounding. */
+int oc_b200_moe_combine(const void* y, int64_t ldy, const int32_t* slot_pos, const float* w, int T, int k, int H,
+                        const void* shared, int64_t lds, void* out, int64_t ldo, int dtype, oc_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

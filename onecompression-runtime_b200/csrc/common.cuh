@@ -14,10 +14,10 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-#ifndef OC_WAIT_LIMIT
-// ~ a few seconds of polling with try_wait's internal suspend; far above any
-// legitimate wait, far below a hang.
-#define OC_WAIT_LIMIT (1u << 25)
+#ifndef OC_WAIT_NS
+// Wall-clock bound of every spin-wait (device %globaltimer, ns): far above any
+// legitimate wait (a whole tile takes well under a millisecond), far below a hang.
+#define OC_WAIT_NS 2000000000ull
 #endif
 
 namespace oc {
@@ -176,17 +176,39 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait: returns false (and records `code`) if the phase never completes
-// or another role of this CTA has already aborted.
+__device__ __forceinline__ uint64_t global_timer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait: returns false (and records `code`) if the phase does not complete
+// within OC_WAIT_NS, or as soon as another role of this CTA has aborted.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                           unsigned code) {
-  for (uint32_t it = 0; it < OC_WAIT_LIMIT; ++it) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 63u) == 63u && *abort_flag) return false;
+    if ((it & 15u) == 0u) {
+      if (*abort_flag) return false;
+      if (global_timer_ns() - t0 > OC_WAIT_NS) break;
+    }
   }
   record_error(code);
   *abort_flag = 1;
   return false;
+}
+
+// Bounded wait used while unwinding after an abort (no abort-flag check).
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
+  const uint64_t t0 = global_timer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (global_timer_ns() - t0 > OC_WAIT_NS) {
+      record_error(kDevErrDrain);
+      return;
+    }
+  }
 }
 
 __device__ __forceinline__ void fence_barrier_init() {

@@ -4,20 +4,23 @@
 // its odd-group / any-group variants (:275-385, :540-636).
 //
 // Orientation: C^T tile = W_tile (128 output features) x X_tile^T (BT tokens).
-//   * A operand = dequantized weights, written by a dequant warpgroup straight
+//   * A operand = dequantized weights, written by the dequant warpgroups straight
 //     into TMEM (tcgen05.st) -- 128 lanes = 128 output features, 2 bf16/fp16
 //     per 32-bit column. The dequantized weights never touch shared memory.
 //   * B operand = activation tile X[BT tokens, 64 k] loaded by TMA with the
 //     128-byte swizzle (K-major canonical layout).
 //   * D = fp32 accumulator in TMEM: 128 lanes x BT columns (tokens), double
 //     buffered when TMEM allows so the epilogue overlaps the next tile.
-//   * Packed qweight tiles [8 word rows x 128 columns] arrive by TMA into a
-//     shared-memory ring; scales/zeros are read per group with cached loads.
+//   * Per 64-k block a TMA stage carries the packed qweight tile [8 x 128] int32
+//     and, for uniform aligned groups, the scale rows [R x 128] and zero rows
+//     [R x 16 words] (R = 2 for groupsize 32, 1 for multiples of 64); other group
+//     structures read scales/zeros with cached global loads.
 //   * Exact dequant: w = RNE(s*(q-z)) as in quant_utils.dequant_gptq_to_fp.
-// Warp roles (384 threads, one persistent CTA per SM):
-//   warp 0 lane 0: TMA producer     warp 1: TMEM alloc + MMA issuer (lane 0)
-//   warps 4-7: dequant warpgroup    warps 8-11: epilogue warpgroup
-// Every mbarrier wait is bounded; on timeout the kernel records an error
+// Warp roles (512 threads, one persistent CTA per SM):
+//   warp 0 lane 0: TMA producer      warp 1: TMEM alloc + MMA issuer (lane 0)
+//   warps 4-7 / 8-11: dequant warpgroups for even / odd k-blocks
+//   warps 12-15: epilogue warpgroup (tcgen05.ld, bias, round, store)
+// Every mbarrier wait is bounded in time; on timeout the kernel records an error
 // code, drains its own TMA loads / MMAs, frees TMEM and returns.
 #pragma once
 
@@ -32,6 +35,8 @@ struct TcParams {
   int s_dtype;
   const int32_t* wgrp;     // [Kp/8] or null
   int G, gs, v1;
+  int sz_tma;              // scales/zeros staged by TMA (uniform, aligned groups)
+  int sz_rows;             // scale rows per 64-k block when sz_tma (1 or 2)
   const void* bias;
   int bias_dtype;
   uint16_t* out;
@@ -39,16 +44,20 @@ struct TcParams {
   int n_tiles_n, n_tiles_m, num_tiles;
 };
 
-constexpr int kTcThreads = 384;
+constexpr int kTcThreads = 512;
 constexpr int kTcBK = 64;            // k per pipeline stage (one 128-byte swizzle atom of 16-bit)
 constexpr int kTcBN = 128;           // output features per tile (= TMEM lanes = UMMA M)
-constexpr int kTcWStageBytes = 8 * kTcBN * 4;
+constexpr int kTcWBytes = 8 * kTcBN * 4;           // packed words of one stage
+constexpr int kTcSOff = kTcWBytes;                  // scale rows [2][128] 16-bit
+constexpr int kTcZOff = kTcSOff + 2 * kTcBN * 2;    // zero rows [2][16] int32
+constexpr int kTcWStageBytes = kTcZOff + 2 * 16 * 4 + 128;  // 4864, multiple of 128
 
 template <int BT, int ACC_STAGES, int X_STAGES, int W_STAGES, int A_STAGES>
 struct TcCfg {
   static constexpr int kAccCols = ACC_STAGES * BT;
   static constexpr int kACols = A_STAGES * (kTcBK / 2);
   static_assert(kAccCols + kACols <= 512, "TMEM budget");
+  static_assert(W_STAGES % 2 == 0 && A_STAGES % 2 == 0, "two dequant warpgroups alternate stages");
   static constexpr int kXStageBytes = BT * 128;
   static constexpr int kSmemBytes = X_STAGES * kXStageBytes + W_STAGES * kTcWStageBytes + 1024 /*align*/ +
                                     (2 * (X_STAGES + W_STAGES + A_STAGES + ACC_STAGES) + 2) * 8 + 64;
@@ -57,6 +66,7 @@ struct TcCfg {
 template <bool BF16, bool HAS_LO, int BT, int ACC_STAGES, int X_STAGES, int W_STAGES, int A_STAGES>
 __global__ void __launch_bounds__(kTcThreads, 1)
     gptq_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
+                        const __grid_constant__ CUtensorMap tmap_s, const __grid_constant__ CUtensorMap tmap_z,
                         const TcParams p) {
   using Cfg = TcCfg<BT, ACC_STAGES, X_STAGES, W_STAGES, A_STAGES>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -78,6 +88,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   const int warp = warp_id(), lane = lane_id();
   const int KB = (p.Kp + kTcBK - 1) / kTcBK;
+  const uint32_t w_tx = kTcWBytes + (p.sz_tma ? p.sz_rows * (kTcBN * 2 + 16 * 4) : 0);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < X_STAGES; ++i) { mbar_init(&full_x[i], 1); mbar_init(&empty_x[i], 1); }
@@ -91,6 +102,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmap_x);
     tma_prefetch_desc(&tmap_w);
+    if (p.sz_tma) {
+      tma_prefetch_desc(&tmap_s);
+      tma_prefetch_desc(&tmap_z);
+    }
   }
   if (warp == 1) {
     tmem_alloc(tmem_holder, 512);
@@ -104,49 +119,54 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      int sx = 0, px = 0, sw = 0, pw = 0;
+      int it = 0;
       int x_armed[X_STAGES], w_armed[W_STAGES];
       for (int i = 0; i < X_STAGES; ++i) x_armed[i] = -1;
       for (int i = 0; i < W_STAGES; ++i) w_armed[i] = -1;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
         const int nb = tile % p.n_tiles_n, mb = tile / p.n_tiles_n;
-        for (int kb = 0; kb < KB; ++kb) {
+        for (int kb = 0; kb < KB; ++kb, ++it) {
+          const int sx = it % X_STAGES, px = (it / X_STAGES) & 1;
+          const int sw = it % W_STAGES, pw = (it / W_STAGES) & 1;
           if (!mbar_wait(&empty_x[sx], px ^ 1, abort_flag, kDevErrTmaEmpty)) { ok = false; break; }
           mbar_arrive_expect_tx(&full_x[sx], Cfg::kXStageBytes);
           tma_load_2d(x_smem + sx * Cfg::kXStageBytes, &tmap_x, &full_x[sx], kb * kTcBK, mb * BT);
           x_armed[sx] = px;
-          if (++sx == X_STAGES) { sx = 0; px ^= 1; }
           if (!mbar_wait(&empty_w[sw], pw ^ 1, abort_flag, kDevErrWEmpty)) { ok = false; break; }
-          mbar_arrive_expect_tx(&full_w[sw], kTcWStageBytes);
-          tma_load_2d(w_smem + sw * kTcWStageBytes, &tmap_w, &full_w[sw], nb * kTcBN, kb * 8);
+          uint8_t* ws = w_smem + sw * kTcWStageBytes;
+          mbar_arrive_expect_tx(&full_w[sw], w_tx);
+          tma_load_2d(ws, &tmap_w, &full_w[sw], nb * kTcBN, kb * 8);
+          if (p.sz_tma) {
+            const int row0 = (p.sz_rows == 2) ? kb * 2 : (kb * kTcBK) / p.gs;
+            tma_load_2d(ws + kTcSOff, &tmap_s, &full_w[sw], nb * kTcBN, row0);
+            tma_load_2d(ws + kTcZOff, &tmap_z, &full_w[sw], nb * (kTcBN / 8), row0);
+          }
           w_armed[sw] = pw;
-          if (++sw == W_STAGES) { sw = 0; pw ^= 1; }
         }
       }
       if (!ok) {
         // drain our own loads in flight before the CTA (and its smem) goes away
         for (int i = 0; i < X_STAGES; ++i)
-          if (x_armed[i] >= 0) {
-            for (uint32_t it = 0; it < OC_WAIT_LIMIT && !mbar_try_wait(&full_x[i], x_armed[i]); ++it) {}
-          }
+          if (x_armed[i] >= 0) mbar_drain(&full_x[i], x_armed[i]);
         for (int i = 0; i < W_STAGES; ++i)
-          if (w_armed[i] >= 0) {
-            for (uint32_t it = 0; it < OC_WAIT_LIMIT && !mbar_try_wait(&full_w[i], w_armed[i]); ++it) {}
-          }
+          if (w_armed[i] >= 0) mbar_drain(&full_w[i], w_armed[i]);
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = make_idesc_f16(BF16, kTcBN, BT);
-      int sx = 0, px = 0, sa = 0, pa = 0, sc = 0, pc = 0;
+      int it = 0, tcount = 0;
       bool ok = true, issued = false;
-      for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+      for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x, ++tcount) {
+        const int sc = tcount % ACC_STAGES, pc = (tcount / ACC_STAGES) & 1;
         if (!mbar_wait(&empty_acc[sc], pc ^ 1, abort_flag, kDevErrAccEmpty)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(sc * BT);
-        for (int kb = 0; kb < KB; ++kb) {
+        for (int kb = 0; kb < KB; ++kb, ++it) {
+          const int sx = it % X_STAGES, px = (it / X_STAGES) & 1;
+          const int sa = it % A_STAGES, pa = (it / A_STAGES) & 1;
           if (!mbar_wait(&full_x[sx], px, abort_flag, kDevErrTmaFull)) { ok = false; break; }
           if (!mbar_wait(&full_a[sa], pa, abort_flag, kDevErrAFull)) { ok = false; break; }
           tc_fence_after();
@@ -160,91 +180,113 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           issued = true;
           tc_commit(&empty_x[sx]);
           tc_commit(&empty_a[sa]);
-          if (++sx == X_STAGES) { sx = 0; px ^= 1; }
-          if (++sa == A_STAGES) { sa = 0; pa ^= 1; }
         }
         if (!ok) break;
         tc_commit(&full_acc[sc]);
-        if (++sc == ACC_STAGES) { sc = 0; pc ^= 1; }
       }
       if (!ok && issued) {
         tc_commit(drain);
-        for (uint32_t it = 0; it < OC_WAIT_LIMIT && !mbar_try_wait(drain, 0); ++it) {}
+        mbar_drain(drain, 0);
       }
     }
-  } else if (warp >= 4 && warp < 8) {
-    // ------------------------------------------------------------ dequant warpgroup
+  } else if (warp >= 4 && warp < 12) {
+    // ------------------------------------------------------------ dequant warpgroups
     using Pp = Pair<BF16>;
+    const int wg = (warp - 4) >> 2;   // 0: even k-blocks, 1: odd k-blocks
     const int q4 = warp & 3;
-    const int row = q4 * 32 + lane;  // TMEM lane == output feature within the tile
+    const int row = q4 * 32 + lane;   // TMEM lane == output feature within the tile
     const int kw_rows = p.Kp >> 3;
-    int sw = 0, pw = 0, sa = 0, pa = 0;
+    int it = 0;
     bool ok = true;
     for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
       const int nb = tile % p.n_tiles_n;
       const int n = nb * kTcBN + row;
-      const bool nvalid = n < p.N;
-      const int nn = nvalid ? n : 0;
-      for (int kb = 0; kb < KB; ++kb) {
-        // group constants for the 8 words of this k-block (loads issued before the smem wait)
-        float sv[8];
-        uint32_t zv[8];
-        int last = -1;
+      const int nn = n < p.N ? n : 0;
+      const int zsh = 4 * (nn & 7);
+      for (int kb = 0; kb < KB; ++kb, ++it) {
+        if ((it & 1) != wg) continue;
+        const int sw = it % W_STAGES, pw = (it / W_STAGES) & 1;
+        const int sa = it % A_STAGES, pa = (it / A_STAGES) & 1;
+        // per-word group constants
+        DqConst<BF16> cst[8];
+        if (!p.sz_tma) {
+          int last = -1;
+          float sv = 0.f;
+          uint32_t zw = 0;
 #pragma unroll
-        for (int w = 0; w < 8; ++w) {
-          const int kw = kb * 8 + w;
-          const int grp = (kw < kw_rows) ? (p.wgrp ? __ldg(p.wgrp + kw) : (8 * kw) / p.gs) : 0;
-          if (grp != last) {
-            sv[w] = load_as_f32(p.s, p.s_dtype, (long long)grp * p.N + nn);
-            zv[w] = __ldg(p.qz + (long long)grp * (p.N >> 3) + (nn >> 3));
-            last = grp;
-          } else {
-            sv[w] = sv[w > 0 ? w - 1 : 0];
-            zv[w] = zv[w > 0 ? w - 1 : 0];
+          for (int w = 0; w < 8; ++w) {
+            const int kw = kb * 8 + w;
+            const int grp = (kw < kw_rows) ? (p.wgrp ? __ldg(p.wgrp + kw) : (8 * kw) / p.gs) : 0;
+            if (grp != last) {
+              sv = load_as_f32(p.s, p.s_dtype, (long long)grp * p.N + nn);
+              zw = __ldg(p.qz + (long long)grp * (p.N >> 3) + (nn >> 3));
+              uint32_t z = (zw >> zsh) & 0xFu;
+              if (p.v1) z = (z + 1u) & 0xFu;
+              cst[w] = make_dq_const<BF16>(sv, (int)z);
+              last = grp;
+            } else {
+              cst[w] = cst[w > 0 ? w - 1 : 0];
+            }
           }
         }
         if (!mbar_wait(&full_w[sw], pw, abort_flag, kDevErrWFull)) { ok = false; break; }
-        const uint32_t* wt = reinterpret_cast<const uint32_t*>(w_smem + sw * kTcWStageBytes);
+        const uint8_t* ws = w_smem + sw * kTcWStageBytes;
+        const uint32_t* wt = reinterpret_cast<const uint32_t*>(ws);
         uint32_t q[8];
 #pragma unroll
         for (int w = 0; w < 8; ++w) q[w] = wt[w * kTcBN + row];
+        if (p.sz_tma) {
+          const uint16_t* st = reinterpret_cast<const uint16_t*>(ws + kTcSOff);
+          const uint32_t* zt = reinterpret_cast<const uint32_t*>(ws + kTcZOff);
+          const int nr = p.sz_rows;
+#pragma unroll
+          for (int r = 0; r < 2; ++r) {
+            if (r < nr) {
+              const float sv = (p.s_dtype == kF16) ? __half2float(__ushort_as_half(st[r * kTcBN + row]))
+                                                   : __bfloat162float(__ushort_as_bfloat16(st[r * kTcBN + row]));
+              uint32_t z = (zt[r * 16 + (row >> 3)] >> zsh) & 0xFu;
+              if (p.v1) z = (z + 1u) & 0xFu;
+              const DqConst<BF16> c = make_dq_const<BF16>(sv, (int)z);
+              // words 4r..4r+3 (nr == 2) or all 8 words (nr == 1)
+#pragma unroll
+              for (int w = 0; w < 8; ++w)
+                if ((nr == 1) || (w >> 2) == r) cst[w] = c;
+            }
+          }
+        }
         mbar_arrive(&empty_w[sw]);
-        if (++sw == W_STAGES) { sw = 0; pw ^= 1; }
 
-        uint32_t r[32];
+        uint32_t r32[32];
 #pragma unroll
         for (int w = 0; w < 8; ++w) {
-          uint32_t z = (zv[w] >> (4 * (nn & 7))) & 0xFu;
-          if (p.v1) z = (z + 1u) & 0xFu;
-          const DqConst<BF16> c = make_dq_const<BF16>(sv[w], (int)z);
           const uint32_t qq = q[w];
-          const uint32_t p0 = dq_pair<BF16, HAS_LO>(lop3_and_or(qq, 0x000F000Fu, Pp::kMagic), c);        // k0,k4
-          const uint32_t p1 = dq_pair<BF16, HAS_LO>(lop3_and_or(qq >> 4, 0x000F000Fu, Pp::kMagic), c);   // k1,k5
-          const uint32_t p2 = dq_pair<BF16, HAS_LO>(lop3_and_or(qq >> 8, 0x000F000Fu, Pp::kMagic), c);   // k2,k6
-          const uint32_t p3 = dq_pair<BF16, HAS_LO>(lop3_and_or(qq >> 12, 0x000F000Fu, Pp::kMagic), c);  // k3,k7
-          r[4 * w + 0] = prmt(p0, p1, 0x5410u);  // k0,k1
-          r[4 * w + 1] = prmt(p2, p3, 0x5410u);  // k2,k3
-          r[4 * w + 2] = prmt(p0, p1, 0x7632u);  // k4,k5
-          r[4 * w + 3] = prmt(p2, p3, 0x7632u);  // k6,k7
+          const uint32_t p0 = dq_pair<BF16, HAS_LO>(lop3_and_or(qq, 0x000F000Fu, Pp::kMagic), cst[w]);        // k0,k4
+          const uint32_t p1 = dq_pair<BF16, HAS_LO>(lop3_and_or(qq >> 4, 0x000F000Fu, Pp::kMagic), cst[w]);   // k1,k5
+          const uint32_t p2 = dq_pair<BF16, HAS_LO>(lop3_and_or(qq >> 8, 0x000F000Fu, Pp::kMagic), cst[w]);   // k2,k6
+          const uint32_t p3 = dq_pair<BF16, HAS_LO>(lop3_and_or(qq >> 12, 0x000F000Fu, Pp::kMagic), cst[w]);  // k3,k7
+          r32[4 * w + 0] = prmt(p0, p1, 0x5410u);  // k0,k1
+          r32[4 * w + 1] = prmt(p2, p3, 0x5410u);  // k2,k3
+          r32[4 * w + 2] = prmt(p0, p1, 0x7632u);  // k4,k5
+          r32[4 * w + 3] = prmt(p2, p3, 0x7632u);  // k6,k7
         }
         if (!mbar_wait(&empty_a[sa], pa ^ 1, abort_flag, kDevErrAEmpty)) { ok = false; break; }
         tc_fence_after();
         __syncwarp();
         const uint32_t taddr = tmem_base + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(Cfg::kAccCols + sa * (kTcBK / 2));
-        tmem_st_32x32b_x32(taddr, r);
+        tmem_st_32x32b_x32(taddr, r32);
         tc_wait_st();
         tc_fence_before();
         mbar_arrive(&full_a[sa]);
-        if (++sa == A_STAGES) { sa = 0; pa ^= 1; }
       }
     }
-  } else if (warp >= 8) {
+  } else if (warp >= 12) {
     // ------------------------------------------------------------ epilogue warpgroup
     const int q4 = warp & 3;
     const int row = q4 * 32 + lane;
     const int odt = BF16 ? kBF16 : kF16;
-    int sc = 0, pc = 0;
-    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+    int tcount = 0;
+    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++tcount) {
+      const int sc = tcount % ACC_STAGES, pc = (tcount / ACC_STAGES) & 1;
       const int nb = tile % p.n_tiles_n, mb = tile / p.n_tiles_n;
       const int n = nb * kTcBN + row;
       const bool nvalid = n < p.N;
@@ -269,7 +311,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       tc_fence_before();
       mbar_arrive(&empty_acc[sc]);
-      if (++sc == ACC_STAGES) { sc = 0; pc ^= 1; }
     }
   }
 

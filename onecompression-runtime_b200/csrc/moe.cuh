@@ -1,0 +1,194 @@
+// MoE routing and token permutation for the packed-expert path.
+//
+// The reference delegates routing to an unvendored model file (models/dsv4/loader.py:50-53),
+// so the convention here is stated, not pinned: softmax over the expert logits in fp32,
+// top-k (ties -> lower expert id), weights renormalised to sum 1 (optional),
+// expert(x) = down(silu(gate(x)) * up(x)), y = sum_k w_k expert_k(x) (+ shared(x)).
+#pragma once
+
+#include "common.cuh"
+
+namespace oc {
+
+constexpr int kMoeMaxE = 1024;
+constexpr int kMoeMaxK = 16;
+
+// One warp per token: softmax over E logits, then K rounds of warp arg-max.
+__global__ void moe_route_kernel(const void* __restrict__ logits, int logit_dtype, int T, int E, int K, int renorm,
+                                 int32_t* __restrict__ ids, float* __restrict__ weights) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= T) return;
+  constexpr int kPer = kMoeMaxE / 32;
+  float v[kPer];
+  const long long base = (long long)warp * E;
+  float mx = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int e = lane + 32 * i;
+    v[i] = (e < E) ? load_as_f32(logits, logit_dtype, base + e) : -INFINITY;
+    mx = fmaxf(mx, v[i]);
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int e = lane + 32 * i;
+    v[i] = (e < E) ? expf(v[i] - mx) : 0.f;
+    sum += v[i];
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  const float inv = 1.f / sum;
+  float picked[kMoeMaxK];
+  int pid[kMoeMaxK];
+  float tot = 0.f;
+  for (int r = 0; r < K; ++r) {
+    float best = -1.f;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int e = lane + 32 * i;
+      if (e < E && (v[i] > best || (v[i] == best && e < bi))) { best = v[i]; bi = e; }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
+    }
+    picked[r] = best * inv;
+    pid[r] = bi;
+    tot += picked[r];
+    if ((bi & 31) == lane) v[bi >> 5] = -2.f;  // remove from further rounds
+  }
+  if (lane == 0) {
+    const float scale = renorm ? 1.f / tot : 1.f;
+    for (int r = 0; r < K; ++r) {
+      ids[(long long)warp * K + r] = pid[r];
+      weights[(long long)warp * K + r] = picked[r] * scale;
+    }
+  }
+}
+
+// Block e ranks, in (token, slot) order, every assignment to expert e: stable and
+// deterministic. counts[e] = number of assignments; offsets = exclusive scan (computed
+// by the caller kernel below).
+__global__ void moe_count_kernel(const int32_t* __restrict__ ids, int TK, int E, int32_t* __restrict__ counts) {
+  __shared__ int part[32];
+  const int e = blockIdx.x;
+  int c = 0;
+  for (int i = threadIdx.x; i < TK; i += blockDim.x) c += (ids[i] == e);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = c;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int s = 0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) s += part[w];
+    counts[e] = s;
+  }
+}
+
+__global__ void moe_scan_kernel(const int32_t* __restrict__ counts, int E, int32_t* __restrict__ offsets) {
+  // single block, E <= kMoeMaxE
+  __shared__ int buf[kMoeMaxE + 1];
+  for (int i = threadIdx.x; i < E; i += blockDim.x) buf[i] = counts[i];
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int s = 0;
+    for (int i = 0; i < E; ++i) {
+      const int c = buf[i];
+      buf[i] = s;
+      s += c;
+    }
+    buf[E] = s;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i <= E; i += blockDim.x) offsets[i] = buf[i];
+}
+
+__global__ void moe_scatter_kernel(const int32_t* __restrict__ ids, int TK, int K,
+                                   const int32_t* __restrict__ offsets, int32_t* __restrict__ sorted_token,
+                                   int32_t* __restrict__ slot_pos) {
+  __shared__ int part[33];
+  const int e = blockIdx.x;
+  int running = offsets[e];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (int base = 0; base < TK; base += blockDim.x) {
+    const int i = base + threadIdx.x;
+    const bool hit = i < TK && ids[i] == e;
+    const unsigned m = __ballot_sync(0xffffffffu, hit);
+    if (lane == 0) part[warp] = __popc(m);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int s = 0;
+      for (int w = 0; w < nw; ++w) {
+        const int c = part[w];
+        part[w] = s;
+        s += c;
+      }
+      part[32] = s;
+    }
+    __syncthreads();
+    if (hit) {
+      const int pos = running + part[warp] + __popc(m & ((1u << lane) - 1u));
+      sorted_token[pos] = i / K;
+      slot_pos[i] = pos;
+    }
+    running += part[32];
+    __syncthreads();
+  }
+}
+
+// rows: dst[p, :] = src[idx[p], :] (16-bit elements, H % 8 == 0)
+__global__ void gather_rows_kernel(const uint16_t* __restrict__ src, long long lds, const int32_t* __restrict__ idx,
+                                   int P, int H, uint16_t* __restrict__ dst, long long ldd) {
+  const int vec = H / 8;
+  const long long total = (long long)P * vec;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int p = (int)(i / vec), c = (int)(i % vec);
+    const uint4 v = *reinterpret_cast<const uint4*>(src + (long long)idx[p] * lds + 8 * c);
+    *reinterpret_cast<uint4*>(dst + (long long)p * ldd + 8 * c) = v;
+  }
+}
+
+// h = silu(g) * u, with g/u the two halves of a [P, 2F] row (or separate tensors).
+template <bool BF16>
+__global__ void silu_mul_kernel(const uint16_t* __restrict__ g, const uint16_t* __restrict__ u, long long ld_in,
+                                int P, int F, uint16_t* __restrict__ h, long long ld_out) {
+  const long long total = (long long)P * F;
+  const int dt = BF16 ? kBF16 : kF16;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int p = (int)(i / F), f = (int)(i % F);
+    const float gv = bits_to_f32(g[(long long)p * ld_in + f], dt);
+    const float uv = bits_to_f32(u[(long long)p * ld_in + f], dt);
+    const float s = gv / (1.f + expf(-gv));
+    h[(long long)p * ld_out + f] = f32_to_bits(s * uv, dt);
+  }
+}
+
+// out[t, :] = sum_j w[t, j] * y[slot_pos[t*K + j], :] (+ shared[t, :]); fp32 sum, one rounding.
+template <bool BF16>
+__global__ void moe_combine_kernel(const uint16_t* __restrict__ y, long long ldy, const int32_t* __restrict__ slot_pos,
+                                   const float* __restrict__ w, int T, int K, int H,
+                                   const uint16_t* __restrict__ shared, long long lds, uint16_t* __restrict__ out,
+                                   long long ldo) {
+  const int dt = BF16 ? kBF16 : kF16;
+  const long long total = (long long)T * H;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int t = (int)(i / H), c = (int)(i % H);
+    float acc = shared ? bits_to_f32(shared[(long long)t * lds + c], dt) : 0.f;
+    for (int j = 0; j < K; ++j) {
+      const int p = slot_pos[(long long)t * K + j];
+      acc += w[(long long)t * K + j] * bits_to_f32(y[(long long)p * ldy + c], dt);
+    }
+    out[(long long)t * ldo + c] = f32_to_bits(acc, dt);
+  }
+}
+
+}  // namespace oc

@@ -15,6 +15,7 @@
 #include "dequant.cuh"
 #include "gemm_tc.cuh"
 #include "gemv.cuh"
+#include "moe.cuh"
 
 namespace {
 
@@ -113,7 +114,8 @@ struct oc_b200_layer {
   const int32_t* kperm;
   const int32_t* wgrp;
   int K_in, Kp, N, G, gs, v1;
-  CUtensorMap tmap_w;
+  int sz_tma, sz_rows;     // scales/zeros staged by TMA in the tcgen05 kernel
+  CUtensorMap tmap_w, tmap_s, tmap_z;
 };
 
 extern "C" {
@@ -329,6 +331,25 @@ int oc_b200_gptq_layer_create(const int32_t* qweight, const int32_t* qzeros, con
     delete L;
     return rc;
   }
+  // Uniform groups aligned to the 64-k block: stage scales/zeros with the packed tile.
+  L->sz_tma = 0;
+  L->sz_rows = 0;
+  L->tmap_s = L->tmap_w;
+  L->tmap_z = L->tmap_w;
+  if (!word_group && N % 32 == 0 && (groupsize == 32 || groupsize % 64 == 0) && aligned(scales, 16) &&
+      aligned(qzeros, 16)) {
+    const int rows = groupsize == 32 ? 2 : 1;
+    if (make_tmap_2d(&L->tmap_s, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, scales, (uint64_t)N, (uint64_t)G, (uint64_t)N * 2,
+                     oc::kTcBN, rows, CU_TENSOR_MAP_SWIZZLE_NONE) == OC_OK &&
+        make_tmap_2d(&L->tmap_z, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, qzeros, (uint64_t)(N / 8), (uint64_t)G,
+                     (uint64_t)(N / 8) * 4, oc::kTcBN / 8, rows, CU_TENSOR_MAP_SWIZZLE_NONE) == OC_OK) {
+      L->sz_tma = 1;
+      L->sz_rows = rows;
+    } else {
+      L->tmap_s = L->tmap_w;
+      L->tmap_z = L->tmap_w;
+    }
+  }
   *out = L;
   return OC_OK;
 }
@@ -397,7 +418,7 @@ int launch_gemv(const oc::GemvParams& p, int n_tiles, int splits, cudaStream_t s
 }
 
 template <bool BF16, bool HAS_LO, int BT, int ACC, int XS, int WS, int AS>
-int launch_tc_t(const CUtensorMap& tx, const CUtensorMap& tw, const oc::TcParams& p, int dev, cudaStream_t stream) {
+int launch_tc_t(const CUtensorMap& tx, const oc_b200_layer* L, const oc::TcParams& p, int dev, cudaStream_t stream) {
   using Cfg = oc::TcCfg<BT, ACC, XS, WS, AS>;
   auto kern = oc::gptq_gemm_tc_kernel<BF16, HAS_LO, BT, ACC, XS, WS, AS>;
   static bool attr_set[kMaxDevices] = {};
@@ -409,16 +430,16 @@ int launch_tc_t(const CUtensorMap& tx, const CUtensorMap& tw, const oc::TcParams
     attr_set[dev] = true;
   }
   int grid = p.num_tiles < sm_count(dev) ? p.num_tiles : sm_count(dev);
-  kern<<<grid, oc::kTcThreads, Cfg::kSmemBytes, stream>>>(tx, tw, p);
+  kern<<<grid, oc::kTcThreads, Cfg::kSmemBytes, stream>>>(tx, L->tmap_w, L->tmap_s, L->tmap_z, p);
   return launch_check("gptq_gemm_tc");
 }
 
 template <bool BF16, bool HAS_LO>
-int launch_tc(int bt, const CUtensorMap& tx, const CUtensorMap& tw, const oc::TcParams& p, int dev,
+int launch_tc(int bt, const CUtensorMap& tx, const oc_b200_layer* L, const oc::TcParams& p, int dev,
               cudaStream_t stream) {
-  if (bt == 128) return launch_tc_t<BF16, HAS_LO, 128, 2, 6, 8, 8>(tx, tw, p, dev, stream);
-  if (bt == 256) return launch_tc_t<BF16, HAS_LO, 256, 1, 4, 8, 4>(tx, tw, p, dev, stream);
-  return launch_tc_t<BF16, HAS_LO, 192, 2, 5, 8, 4>(tx, tw, p, dev, stream);
+  if (bt == 128) return launch_tc_t<BF16, HAS_LO, 128, 2, 6, 8, 8>(tx, L, p, dev, stream);
+  if (bt == 256) return launch_tc_t<BF16, HAS_LO, 256, 1, 4, 8, 4>(tx, L, p, dev, stream);
+  return launch_tc_t<BF16, HAS_LO, 192, 2, 5, 8, 4>(tx, L, p, dev, stream);
 }
 
 }  // namespace
@@ -510,6 +531,8 @@ extern "C" int oc_b200_gptq_gemm(const oc_b200_layer* L, const void* a, int a_dt
   p.G = L->G;
   p.gs = L->gs;
   p.v1 = L->v1;
+  p.sz_tma = L->sz_tma;
+  p.sz_rows = L->sz_rows;
   p.bias = bias;
   p.bias_dtype = bias_dtype;
   p.out = reinterpret_cast<uint16_t*>(c);
@@ -517,10 +540,83 @@ extern "C" int oc_b200_gptq_gemm(const oc_b200_layer* L, const void* a, int a_dt
   p.n_tiles_n = (L->N + oc::kTcBN - 1) / oc::kTcBN;
   p.n_tiles_m = (int)((M + bt - 1) / bt);
   p.num_tiles = p.n_tiles_n * p.n_tiles_m;
-  if (bf16) return has_lo ? launch_tc<true, true>(bt, tx, L->tmap_w, p, dev, stream)
-                          : launch_tc<true, false>(bt, tx, L->tmap_w, p, dev, stream);
-  return has_lo ? launch_tc<false, true>(bt, tx, L->tmap_w, p, dev, stream)
-                : launch_tc<false, false>(bt, tx, L->tmap_w, p, dev, stream);
+  if (bf16) return has_lo ? launch_tc<true, true>(bt, tx, L, p, dev, stream)
+                          : launch_tc<true, false>(bt, tx, L, p, dev, stream);
+  return has_lo ? launch_tc<false, true>(bt, tx, L, p, dev, stream)
+                : launch_tc<false, false>(bt, tx, L, p, dev, stream);
 }
 
 
+
+// ---------------------------------------------------------------- MoE routing / permutation
+extern "C" int oc_b200_moe_route(const void* logits, int logits_dtype, int T, int E, int k, int renorm, int32_t* ids,
+                                 float* weights, oc_stream_t stream) {
+  if (!logits || !ids || !weights) return fail(OC_ERR_INVALID, "moe_route: NULL pointer");
+  if (T < 0 || E <= 0 || E > oc::kMoeMaxE || k <= 0 || k > oc::kMoeMaxK || k > E)
+    return fail(OC_ERR_INVALID, "moe_route: T=%d E=%d k=%d", T, E, k);
+  if (!dtf(logits_dtype)) return fail(OC_ERR_INVALID, "moe_route: logits dtype");
+  if (T == 0) return OC_OK;
+  const int threads = 256;
+  const int blocks = (T * 32 + threads - 1) / threads;
+  oc::moe_route_kernel<<<blocks, threads, 0, stream>>>(logits, logits_dtype, T, E, k, renorm, ids, weights);
+  return launch_check("moe_route");
+}
+
+extern "C" int oc_b200_moe_permute(const int32_t* ids, int T, int k, int E, int32_t* counts, int32_t* offsets,
+                                   int32_t* sorted_token, int32_t* slot_pos, oc_stream_t stream) {
+  if (!ids || !counts || !offsets || !sorted_token || !slot_pos) return fail(OC_ERR_INVALID, "moe_permute: NULL");
+  if (T < 0 || k <= 0 || E <= 0 || E > oc::kMoeMaxE) return fail(OC_ERR_INVALID, "moe_permute: T=%d k=%d E=%d", T, k, E);
+  const int TK = T * k;
+  oc::moe_count_kernel<<<E, 256, 0, stream>>>(ids, TK, E, counts);
+  oc::moe_scan_kernel<<<1, 256, 0, stream>>>(counts, E, offsets);
+  if (TK > 0) oc::moe_scatter_kernel<<<E, 1024, 0, stream>>>(ids, TK, k, offsets, sorted_token, slot_pos);
+  return launch_check("moe_permute");
+}
+
+extern "C" int oc_b200_gather_rows(const void* src, int64_t lds, const int32_t* idx, int P, int H, void* dst,
+                                   int64_t ldd, oc_stream_t stream) {
+  if (!src || !idx || !dst) return fail(OC_ERR_INVALID, "gather_rows: NULL pointer");
+  if (P < 0 || H <= 0 || H % 8 || lds % 8 || ldd % 8 || !aligned(src, 16) || !aligned(dst, 16))
+    return fail(OC_ERR_INVALID, "gather_rows: H=%d must be a multiple of 8 with 16-byte aligned rows", H);
+  if (P == 0) return OC_OK;
+  int dev = 0;
+  if (int rc = current_device(&dev)) return rc;
+  oc::gather_rows_kernel<<<grid_1d((long long)P * (H / 8), 256, dev), 256, 0, stream>>>(
+      reinterpret_cast<const uint16_t*>(src), lds, idx, P, H, reinterpret_cast<uint16_t*>(dst), ldd);
+  return launch_check("gather_rows");
+}
+
+extern "C" int oc_b200_silu_mul(const void* g, const void* u, int64_t ld_in, int P, int F, void* h, int64_t ld_out,
+                                int dtype, oc_stream_t stream) {
+  if (!g || !u || !h || P < 0 || F <= 0 || !dt16(dtype)) return fail(OC_ERR_INVALID, "silu_mul: bad arguments");
+  if (P == 0) return OC_OK;
+  int dev = 0;
+  if (int rc = current_device(&dev)) return rc;
+  const int blocks = grid_1d((long long)P * F, 256, dev);
+  if (dtype == OC_DT_BF16)
+    oc::silu_mul_kernel<true><<<blocks, 256, 0, stream>>>(reinterpret_cast<const uint16_t*>(g),
+        reinterpret_cast<const uint16_t*>(u), ld_in, P, F, reinterpret_cast<uint16_t*>(h), ld_out);
+  else
+    oc::silu_mul_kernel<false><<<blocks, 256, 0, stream>>>(reinterpret_cast<const uint16_t*>(g),
+        reinterpret_cast<const uint16_t*>(u), ld_in, P, F, reinterpret_cast<uint16_t*>(h), ld_out);
+  return launch_check("silu_mul");
+}
+
+extern "C" int oc_b200_moe_combine(const void* y, int64_t ldy, const int32_t* slot_pos, const float* w, int T, int k,
+                                   int H, const void* shared, int64_t lds, void* out, int64_t ldo, int dtype,
+                                   oc_stream_t stream) {
+  if (!y || !slot_pos || !w || !out || T < 0 || k <= 0 || H <= 0 || !dt16(dtype))
+    return fail(OC_ERR_INVALID, "moe_combine: bad arguments");
+  if (T == 0) return OC_OK;
+  int dev = 0;
+  if (int rc = current_device(&dev)) return rc;
+  const int blocks = grid_1d((long long)T * H, 256, dev);
+  const auto* yy = reinterpret_cast<const uint16_t*>(y);
+  const auto* sh = reinterpret_cast<const uint16_t*>(shared);
+  auto* o = reinterpret_cast<uint16_t*>(out);
+  if (dtype == OC_DT_BF16)
+    oc::moe_combine_kernel<true><<<blocks, 256, 0, stream>>>(yy, ldy, slot_pos, w, T, k, H, sh, lds, o, ldo);
+  else
+    oc::moe_combine_kernel<false><<<blocks, 256, 0, stream>>>(yy, ldy, slot_pos, w, T, k, H, sh, lds, o, ldo);
+  return launch_check("moe_combine");
+}

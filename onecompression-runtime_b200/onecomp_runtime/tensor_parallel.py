@@ -1,0 +1,127 @@
+"""Tensor-parallel sharding of packed GPTQ int4 linears (one process per GPU, NCCL).
+
+The reference has no distributed code; this is the multi-GPU layer the north
+star asks for on the video-DiT stack:
+
+* column-parallel (``shard_gptq_columns``): split N. qweight/scales columns,
+  qzeros word-columns (N/world must stay a multiple of 8), bias columns;
+* row-parallel (``shard_gptq_rows``): split K. qweight rows (K/world must be a
+  multiple of the groupsize and of 8), scales/qzeros rows; the bias is added by
+  rank 0 only so the all-reduce sums it once;
+* ``RowParallelInt4Linear.forward`` runs the local GEMM in M-chunks and issues
+  an asynchronous all-reduce (sum, bf16) per chunk, so the reduction of chunk i
+  overlaps the GEMM of chunk i+1; the current stream waits on every chunk's
+  reduction before returning.
+
+Sharding helpers are plain tensor slicing and run on any device; the linears
+themselves are the B200 modules (``FusedInt4Linear`` / ``FusedInt4LinearAnyGroup``).
+"""
+from __future__ import annotations
+
+from typing import Callable
+
+import torch
+import torch.distributed as dist
+
+
+def shard_gptq_columns(t: dict, rank: int, world: int, parts: int = 1) -> dict:
+    """Column shard of a packed GPTQ layer (split output features).
+
+    ``parts > 1`` treats the output as ``parts`` equal blocks (e.g. q | k | v) and
+    gives each rank its slice of every block, concatenated in block order, so a
+    fused qkv shard holds the rank's q, k and v columns.
+    """
+    N = t["scales"].shape[1]
+    if N % (world * parts) or (N // (world * parts)) % 8:
+        raise ValueError(f"N={N} does not split into {world}x{parts} shards of a multiple of 8")
+    blk = N // parts
+    n = blk // world
+    spans = [(p * blk + rank * n, p * blk + (rank + 1) * n) for p in range(parts)]
+
+    def cols(x, div=1):
+        return torch.cat([x[:, lo // div:hi // div] for lo, hi in spans], dim=1).contiguous()
+
+    out = {"qweight": cols(t["qweight"]), "scales": cols(t["scales"]), "qzeros": cols(t["qzeros"], 8)}
+    if t.get("g_idx") is not None:
+        out["g_idx"] = t["g_idx"]
+    if t.get("bias") is not None:
+        out["bias"] = torch.cat([t["bias"][lo:hi] for lo, hi in spans]).contiguous()
+    return out
+
+
+def shard_gptq_rows(t: dict, rank: int, world: int, groupsize: int) -> dict:
+    """Row shard of a packed GPTQ layer (split input features); bias kept on rank 0."""
+    K = t["qweight"].shape[0] * 8
+    if K % world or (K // world) % groupsize or (K // world) % 8:
+        raise ValueError(f"K={K} does not split into {world} shards aligned to groupsize {groupsize}")
+    k = K // world
+    g = k // groupsize
+    out = {
+        "qweight": t["qweight"][rank * k // 8:(rank + 1) * k // 8].contiguous(),
+        "scales": t["scales"][rank * g:(rank + 1) * g].contiguous(),
+        "qzeros": t["qzeros"][rank * g:(rank + 1) * g].contiguous(),
+    }
+    if t.get("g_idx") is not None:
+        out["g_idx"] = (t["g_idx"][rank * k:(rank + 1) * k] - rank * g).contiguous()
+    if t.get("bias") is not None and rank == 0:
+        out["bias"] = t["bias"]
+    return out
+
+
+class ColumnParallelInt4Linear(torch.nn.Module):
+    """Local column shard; output stays sharded ([M, N/world])."""
+
+    def __init__(self, local: torch.nn.Module):
+        super().__init__()
+        self.local = local
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return self.local(x)
+
+
+class RowParallelInt4Linear(torch.nn.Module):
+    """Local row shard followed by an all-reduce (sum) of the partial outputs.
+
+    ``chunks`` splits M so each chunk's all-reduce overlaps the next chunk's GEMM.
+    """
+
+    def __init__(self, local: torch.nn.Module, group=None, chunks: int = 4):
+        super().__init__()
+        self.local = local
+        self.group = group
+        self.chunks = max(1, int(chunks))
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        M = x.shape[0]
+        world = dist.get_world_size(self.group) if dist.is_initialized() else 1
+        if world == 1:
+            return self.local(x)
+        out = torch.empty((M, self.local.out_features), dtype=x.dtype, device=x.device)
+        step = (M + self.chunks - 1) // self.chunks
+        works = []
+        for c0 in range(0, M, step):
+            c1 = min(M, c0 + step)
+            out[c0:c1] = self.local(x[c0:c1])
+            works.append(dist.all_reduce(out[c0:c1], op=dist.ReduceOp.SUM, group=self.group, async_op=True))
+        for w in works:
+            w.wait()
+        return out
+
+
+def build_tp_block(tensors: dict, layers, rank: int, world: int, groupsize: int,
+                   make_linear: Callable[[dict, int, int], torch.nn.Module], group=None, chunks: int = 4) -> dict:
+    """Shard one DiT block: qkv/fc1 column-parallel, out/fc2 row-parallel.
+
+    ``layers`` = ((name, K, N), ...) in the order qkv, out, fc1, fc2; ``make_linear``
+    builds the local module from a shard dict and its (K, N).
+    """
+    (qn, qk, qN), (on, ok, oN), (fn, fk, fN), (gn, gk, gN) = layers
+    blk = {}
+    blk[qn] = ColumnParallelInt4Linear(make_linear(shard_gptq_columns(tensors[qn], rank, world, parts=3), qk,
+                                                   qN // world))
+    blk[on] = RowParallelInt4Linear(make_linear(shard_gptq_rows(tensors[on], rank, world, groupsize), ok // world, oN),
+                                    group, chunks)
+    blk[fn] = ColumnParallelInt4Linear(make_linear(shard_gptq_columns(tensors[fn], rank, world), fk, fN // world))
+    blk[gn] = RowParallelInt4Linear(make_linear(shard_gptq_rows(tensors[gn], rank, world, groupsize), gk // world, gN),
+                                    group, chunks)
+    return blk
