@@ -124,6 +124,32 @@ int oc_b200_gptq_gemm(const oc_b200_layer* layer, const void* a, int a_dtype, in
                       const void* bias, int bias_dtype, void* c, int64_t ldc, void* workspace,
                       size_t workspace_bytes, oc_stream_t stream);
 
+/* ---- row-packed int4/int2 linears: RTN nibble layers, DSV4 layers, expert groups ---- */
+/* Device bytes the caller provides (256-byte aligned) to describe E row-packed matrices. */
+size_t oc_b200_rows_table_bytes(int E);
+/* Describes E row-packed weight matrices of one shape [N, K] (E = 1: a dense layer). Replaces
+ * the module state of PackedRTNLinear (packed_linear.py:22-45) and Dsv4PackedLinear
+ * (dsv4_packed_linear.py:59-83) and, for E > 1, the routed-expert set of the DSV4 adapter
+ * (models/dsv4/loader.py:109-119).
+ *   packed[e]      host array of device pointers: uint8 [N, ld_bytes], 8/wbits codes per byte,
+ *                  code j of a byte at bits j*wbits (RTN: low nibble = even k)
+ *   scales[e], zeros[e]  host arrays of device pointers; element (n, g) at n*stride_n + g*stride_g
+ *   groupsize      k per scale group (>= K: one group per row)
+ *   mode           0: (q - z) * s in fp32, one rounding (DSV4, dsv4_packed_linear.py:52-56)
+ *                  1: RTN, two roundings in the activation dtype (quant_utils.py:91-103)
+ *   table          caller-allocated device memory of oc_b200_rows_table_bytes(E) bytes; the call
+ *                  fills it (TMA descriptors + pointer arrays) and synchronises `stream`. */
+int oc_b200_rows_layer_create(int E, const uint8_t* const* packed, int64_t ld_bytes, int wbits,
+                              const void* const* scales, int scales_dtype, const void* const* zeros, int zeros_dtype,
+                              int64_t stride_n, int64_t stride_g, int groupsize, int K, int N, int mode, void* table,
+                              oc_stream_t stream, oc_b200_layer** out);
+/* Dense (offsets == NULL): C[M, N] = A[M, K] @ W^T + bias. Grouped (offsets: device int32 [E+1]):
+ * the rows of A are sorted by expert and C row r = A row r @ W_e^T for offsets[e] <= r < offsets[e+1]
+ * (no bias). fp32 accumulation, one rounding to a_dtype. No workspace. */
+int oc_b200_rows_gemm(const oc_b200_layer* layer, const void* a, int a_dtype, int64_t M, int64_t lda,
+                      const int32_t* offsets, const void* bias, int bias_dtype, void* c, int64_t ldc,
+                      oc_stream_t stream);
+
 /* ---- packed-expert MoE -------------------------------- */
 /* The reference routes in an unvendored model file (models/dsv4/loader.py:50-53);
  * the convention implemented: fp32 softmax over E logits, top-k with ties to the

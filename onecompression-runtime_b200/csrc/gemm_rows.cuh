@@ -1,0 +1,367 @@
+// Row-packed int4/int2 GEMM on tcgen05 (sm_100a): RTN uint8-nibble layers, DSV4 int4/int2
+// layers, and the grouped packed-expert GEMM of the MoE path.
+//
+// Replaces PackedRTNLinear.forward (packed_linear.py:53-56 -> quant_utils.py:72-103 + F.linear),
+// Dsv4PackedLinear.forward (dsv4_packed_linear.py:95-98) and the per-expert loop over routed
+// experts that the reference's DSV4 adapter runs (models/dsv4/loader.py:92-119).
+//
+// Weights: uint8 [N, ldq] per expert, 8/WBITS codes per byte along K (code j of a byte at
+// bits j*WBITS; for WBITS = 4 the RTN layout "low nibble = even k" is the same thing).
+// Scales/zeros: element (n, g) at n*stride_n + g*stride_g, any float dtype.
+// Pipeline identical to gptq_gemm_tc_kernel (gemm_tc.cuh): dequantized weights are the
+// MMA A operand in TMEM, activation tiles the B operand via TMA, fp32 accumulators in TMEM.
+// Grouped mode: rows of X are sorted by expert, offsets[E+1] delimit the segments, and a
+// tile never straddles two experts (the MMA may read rows of the next segment; those
+// outputs are not stored).
+//
+// Dequant numerics (MODE):
+//   kRowsExact   (DSV4): w = RNE((q - z) * s) computed in pair arithmetic as
+//                 d = q - z, w = fma(d, s_hi, d * s_lo) -- exact whenever q - z is exact in
+//                 the pair type (always for half-integer zeros such as 1.5).
+//   kRowsRtn     (RTN, quant_utils.py:91-103): z_o = RNE(z), s_o = RNE(s),
+//                 d = RNE(q - z_o), w = RNE(d * s_o) -- the reference's two roundings.
+#pragma once
+
+#include "common.cuh"
+
+namespace oc {
+
+enum RowsMode : int { kRowsExact = 0, kRowsRtn = 1 };
+
+constexpr int kRowsMaxE = 1024;
+
+struct RowsParams {
+  int M;                      // dense: rows of X; grouped: total sorted rows
+  int N, K;
+  int E;                      // experts (1 = dense layer)
+  const int32_t* offsets;     // [E+1] segment starts (grouped) or null (dense)
+  const CUtensorMap* wmaps;   // [E] TMA maps over the packed weights (device memory)
+  const void* const* sptr;    // [E] scales
+  const void* const* zptr;    // [E] zeros
+  int s_dtype, z_dtype;
+  long long s_stride_n, s_stride_g;
+  int gs;                     // k per scale group (a multiple of the k held by one 32-bit word)
+  const void* bias;
+  int bias_dtype;
+  uint16_t* out;
+  long long ldc;
+  int n_tiles_n;
+};
+
+constexpr int kRowsThreads = 512;
+
+template <int WBITS, int BT, int ACC_STAGES, int X_STAGES, int W_STAGES, int A_STAGES>
+struct RowsCfg {
+  static constexpr int kKbBytes = 64 * WBITS / 8;               // packed bytes of one row per 64-k block
+  static constexpr int kWStageBytes = 128 * kKbBytes;            // 2 KB (int2) / 4 KB (int4)
+  static constexpr int kAccCols = ACC_STAGES * BT;
+  static constexpr int kACols = A_STAGES * 32;
+  static_assert(kAccCols + kACols <= 512, "TMEM budget");
+  static_assert(W_STAGES % 2 == 0 && A_STAGES % 2 == 0, "two dequant warpgroups alternate stages");
+  static constexpr int kXStageBytes = BT * 128;
+  static constexpr int kSmemBytes = X_STAGES * kXStageBytes + W_STAGES * kWStageBytes + 1024 +
+                                    (2 * (X_STAGES + W_STAGES + A_STAGES + ACC_STAGES) + 2) * 8 + 64 +
+                                    (kRowsMaxE + 1) * 4;
+};
+
+template <bool BF16, int MODE>
+struct RowsConst {
+  uint32_t zm;   // (z, z) in the pair type (RNE of z)
+  uint32_t shi;  // RNE(s)
+  uint32_t slo;  // exact mode: s - s_hi
+};
+
+template <bool BF16, int MODE>
+__device__ __forceinline__ RowsConst<BF16, MODE> rows_const(float s, float z) {
+  using P = Pair<BF16>;
+  RowsConst<BF16, MODE> c;
+  const uint16_t zz = P::from_f32(z);
+  const uint16_t hi = P::from_f32(s);
+  const uint16_t lo = P::from_f32(s - P::to_f32(hi));
+  c.zm = pack2(zz, zz);
+  c.shi = pack2(hi, hi);
+  c.slo = pack2(lo, lo);
+  return c;
+}
+
+// magic-biased code pair (M+c_a, M+c_b) -> dequantized pair
+template <bool BF16, int MODE, bool HAS_LO>
+__device__ __forceinline__ uint32_t rows_dq(uint32_t mq, const RowsConst<BF16, MODE>& c) {
+  using P = Pair<BF16>;
+  const uint32_t q = P::sub(mq, P::kMagic);   // exact integer codes
+  const uint32_t d = P::sub(q, c.zm);         // RNE(q - z)
+  if (MODE == kRowsRtn) return P::mul(d, c.shi);
+  if (HAS_LO) return P::fma(d, c.shi, P::mul(d, c.slo));
+  return P::mul(d, c.shi);
+}
+
+template <bool BF16, int WBITS, int MODE, bool HAS_LO, int BT, int ACC_STAGES, int X_STAGES, int W_STAGES,
+          int A_STAGES>
+__global__ void __launch_bounds__(kRowsThreads, 1)
+    rows_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const RowsParams p) {
+  using Cfg = RowsCfg<WBITS, BT, ACC_STAGES, X_STAGES, W_STAGES, A_STAGES>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* x_smem = smem;
+  uint8_t* w_smem = x_smem + X_STAGES * Cfg::kXStageBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(w_smem + W_STAGES * Cfg::kWStageBytes);
+  uint64_t* full_x = bars;
+  uint64_t* empty_x = full_x + X_STAGES;
+  uint64_t* full_w = empty_x + X_STAGES;
+  uint64_t* empty_w = full_w + W_STAGES;
+  uint64_t* full_a = empty_w + W_STAGES;
+  uint64_t* empty_a = full_a + A_STAGES;
+  uint64_t* full_acc = empty_a + A_STAGES;
+  uint64_t* empty_acc = full_acc + ACC_STAGES;
+  uint64_t* drain = empty_acc + ACC_STAGES;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  int* prefix = reinterpret_cast<int*>(tmem_holder + 16);  // [E+1] m-tile prefix over experts
+
+  const int warp = warp_id(), lane = lane_id();
+  const int KB = (p.K + 63) / 64;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < X_STAGES; ++i) { mbar_init(&full_x[i], 1); mbar_init(&empty_x[i], 1); }
+    for (int i = 0; i < W_STAGES; ++i) { mbar_init(&full_w[i], 1); mbar_init(&empty_w[i], 128); }
+    for (int i = 0; i < A_STAGES; ++i) { mbar_init(&full_a[i], 128); mbar_init(&empty_a[i], 1); }
+    for (int i = 0; i < ACC_STAGES; ++i) { mbar_init(&full_acc[i], 1); mbar_init(&empty_acc[i], 128); }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 2) {
+    // m-tile prefix over the expert segments (dense: one segment of M rows), 32 experts per step
+    int running = 0;
+    for (int base = 0; base < p.E; base += 32) {
+      const int e = base + lane;
+      int v = 0;
+      if (e < p.E) {
+        const int cnt = p.offsets ? (p.offsets[e + 1] - p.offsets[e]) : p.M;
+        v = (cnt + BT - 1) / BT;
+      }
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += y;
+      }
+      if (e < p.E) prefix[e + 1] = running + v;
+      running += __shfl_sync(0xffffffffu, v, 31);
+    }
+    if (lane == 0) prefix[0] = 0;
+  }
+  if (warp == 0 && lane == 0) tma_prefetch_desc(&tmap_x);
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  const int num_tiles = prefix[p.E] * p.n_tiles_n;
+
+  // tile -> (expert, first row, row end, n block)
+  auto tile_info = [&](int tile, int& e, int& m0, int& mend, int& nb) {
+    nb = tile % p.n_tiles_n;
+    const int mt = tile / p.n_tiles_n;
+    int lo = 0, hi = p.E;  // largest e with prefix[e] <= mt (skips empty experts)
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (prefix[mid] <= mt) lo = mid; else hi = mid;
+    }
+    e = lo;
+    const int base = p.offsets ? p.offsets[e] : 0;
+    m0 = base + (mt - prefix[e]) * BT;
+    mend = p.offsets ? p.offsets[e + 1] : p.M;
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int it = 0;
+      int x_armed[X_STAGES], w_armed[W_STAGES];
+      for (int i = 0; i < X_STAGES; ++i) x_armed[i] = -1;
+      for (int i = 0; i < W_STAGES; ++i) w_armed[i] = -1;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+        int e, m0, mend, nb;
+        tile_info(tile, e, m0, mend, nb);
+        const CUtensorMap* wm = p.wmaps + e;
+        for (int kb = 0; kb < KB; ++kb, ++it) {
+          const int sx = it % X_STAGES, px = (it / X_STAGES) & 1;
+          const int sw = it % W_STAGES, pw = (it / W_STAGES) & 1;
+          if (!mbar_wait(&empty_x[sx], px ^ 1, abort_flag, kDevErrTmaEmpty)) { ok = false; break; }
+          mbar_arrive_expect_tx(&full_x[sx], Cfg::kXStageBytes);
+          tma_load_2d(x_smem + sx * Cfg::kXStageBytes, &tmap_x, &full_x[sx], kb * 64, m0);
+          x_armed[sx] = px;
+          if (!mbar_wait(&empty_w[sw], pw ^ 1, abort_flag, kDevErrWEmpty)) { ok = false; break; }
+          mbar_arrive_expect_tx(&full_w[sw], Cfg::kWStageBytes);
+          tma_load_2d(w_smem + sw * Cfg::kWStageBytes, wm, &full_w[sw], kb * Cfg::kKbBytes, nb * 128);
+          w_armed[sw] = pw;
+        }
+      }
+      if (!ok) {
+        for (int i = 0; i < X_STAGES; ++i)
+          if (x_armed[i] >= 0) mbar_drain(&full_x[i], x_armed[i]);
+        for (int i = 0; i < W_STAGES; ++i)
+          if (w_armed[i] >= 0) mbar_drain(&full_w[i], w_armed[i]);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_f16(BF16, 128, BT);
+      int it = 0, tcount = 0;
+      bool ok = true, issued = false;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x, ++tcount) {
+        const int sc = tcount % ACC_STAGES, pc = (tcount / ACC_STAGES) & 1;
+        if (!mbar_wait(&empty_acc[sc], pc ^ 1, abort_flag, kDevErrAccEmpty)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(sc * BT);
+        for (int kb = 0; kb < KB; ++kb, ++it) {
+          const int sx = it % X_STAGES, px = (it / X_STAGES) & 1;
+          const int sa = it % A_STAGES, pa = (it / A_STAGES) & 1;
+          if (!mbar_wait(&full_x[sx], px, abort_flag, kDevErrTmaFull)) { ok = false; break; }
+          if (!mbar_wait(&full_a[sa], pa, abort_flag, kDevErrAFull)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t xaddr = smem_u32(x_smem + sx * Cfg::kXStageBytes);
+          const uint32_t a_tmem = tmem_base + (uint32_t)(Cfg::kAccCols + sa * 32);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            tc_mma_ts(d_tmem, a_tmem + j * 8, smem_desc_kmajor_sw128(xaddr + j * 32), idesc, (kb | j) != 0 ? 1u : 0u);
+          issued = true;
+          tc_commit(&empty_x[sx]);
+          tc_commit(&empty_a[sa]);
+        }
+        if (!ok) break;
+        tc_commit(&full_acc[sc]);
+      }
+      if (!ok && issued) {
+        tc_commit(drain);
+        mbar_drain(drain, 0);
+      }
+    }
+  } else if (warp >= 4 && warp < 12) {
+    // ------------------------------------------------------------ dequant warpgroups
+    using Pp = Pair<BF16>;
+    constexpr int kWords = Cfg::kKbBytes / 4;     // 32-bit words per row per k-block (8 or 4)
+    constexpr int kSpan = 32 / WBITS;              // k per word (8 or 16)
+    constexpr uint32_t kMask = WBITS == 4 ? 0x000F000Fu : 0x00030003u;
+    const int wg = (warp - 4) >> 2;
+    const int q4 = warp & 3;
+    const int row = q4 * 32 + lane;
+    int it = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+      int e, m0, mend, nb;
+      tile_info(tile, e, m0, mend, nb);
+      const int n = nb * 128 + row;
+      const int nn = n < p.N ? n : 0;
+      const void* sb = p.sptr[e];
+      const void* zb = p.zptr[e];
+      for (int kb = 0; kb < KB; ++kb, ++it) {
+        if ((it & 1) != wg) continue;
+        const int sw = it % W_STAGES, pw = (it / W_STAGES) & 1;
+        const int sa = it % A_STAGES, pa = (it / A_STAGES) & 1;
+        RowsConst<BF16, MODE> cst[kWords];
+        int last = -1;
+#pragma unroll
+        for (int w = 0; w < kWords; ++w) {
+          const int k0 = kb * 64 + w * kSpan;
+          const int grp = (k0 < p.K) ? k0 / p.gs : 0;
+          if (grp != last) {
+            const long long si = (long long)nn * p.s_stride_n + (long long)grp * p.s_stride_g;
+            cst[w] = rows_const<BF16, MODE>(load_as_f32(sb, p.s_dtype, si), load_as_f32(zb, p.z_dtype, si));
+            last = grp;
+          } else {
+            cst[w] = cst[w > 0 ? w - 1 : 0];
+          }
+        }
+        if (!mbar_wait(&full_w[sw], pw, abort_flag, kDevErrWFull)) { ok = false; break; }
+        uint32_t q[kWords];
+        const uint32_t* wt = reinterpret_cast<const uint32_t*>(w_smem + sw * Cfg::kWStageBytes + row * Cfg::kKbBytes);
+#pragma unroll
+        for (int w = 0; w < kWords; w += 4) {
+          const uint4 v = *reinterpret_cast<const uint4*>(wt + w);
+          q[w] = v.x; q[w + 1] = v.y; q[w + 2] = v.z; q[w + 3] = v.w;
+        }
+        mbar_arrive(&empty_w[sw]);
+
+        uint32_t r32[32];
+#pragma unroll
+        for (int w = 0; w < kWords; ++w) {
+          const uint32_t qq = q[w];
+          if (WBITS == 4) {
+            const uint32_t p0 = rows_dq<BF16, MODE, HAS_LO>(lop3_and_or(qq, kMask, Pp::kMagic), cst[w]);
+            const uint32_t p1 = rows_dq<BF16, MODE, HAS_LO>(lop3_and_or(qq >> 4, kMask, Pp::kMagic), cst[w]);
+            const uint32_t p2 = rows_dq<BF16, MODE, HAS_LO>(lop3_and_or(qq >> 8, kMask, Pp::kMagic), cst[w]);
+            const uint32_t p3 = rows_dq<BF16, MODE, HAS_LO>(lop3_and_or(qq >> 12, kMask, Pp::kMagic), cst[w]);
+            r32[4 * w + 0] = prmt(p0, p1, 0x5410u);
+            r32[4 * w + 1] = prmt(p2, p3, 0x5410u);
+            r32[4 * w + 2] = prmt(p0, p1, 0x7632u);
+            r32[4 * w + 3] = prmt(p2, p3, 0x7632u);
+          } else {
+            uint32_t pp[8];  // pp[i] = (code i, code i+8)
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              pp[i] = rows_dq<BF16, MODE, HAS_LO>(lop3_and_or(qq >> (2 * i), kMask, Pp::kMagic), cst[w]);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              r32[8 * w + j] = prmt(pp[2 * j], pp[2 * j + 1], 0x5410u);       // codes 2j, 2j+1
+              r32[8 * w + 4 + j] = prmt(pp[2 * j], pp[2 * j + 1], 0x7632u);   // codes 2j+8, 2j+9
+            }
+          }
+        }
+        if (!mbar_wait(&empty_a[sa], pa ^ 1, abort_flag, kDevErrAEmpty)) { ok = false; break; }
+        tc_fence_after();
+        __syncwarp();
+        const uint32_t taddr = tmem_base + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(Cfg::kAccCols + sa * 32);
+        tmem_st_32x32b_x32(taddr, r32);
+        tc_wait_st();
+        tc_fence_before();
+        mbar_arrive(&full_a[sa]);
+      }
+    }
+  } else if (warp >= 12) {
+    const int q4 = warp & 3;
+    const int row = q4 * 32 + lane;
+    const int odt = BF16 ? kBF16 : kF16;
+    int tcount = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++tcount) {
+      const int sc = tcount % ACC_STAGES, pc = (tcount / ACC_STAGES) & 1;
+      int e, m0, mend, nb;
+      tile_info(tile, e, m0, mend, nb);
+      const int n = nb * 128 + row;
+      const bool nvalid = n < p.N;
+      const float bv = (p.bias && nvalid) ? load_as_f32(p.bias, p.bias_dtype, n) : 0.f;
+      if (!mbar_wait(&full_acc[sc], pc, abort_flag, kDevErrAccFull)) break;
+      tc_fence_after();
+      __syncwarp();
+      const uint32_t tbase = tmem_base + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(sc * BT);
+#pragma unroll 1
+      for (int c = 0; c < BT / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tbase + (uint32_t)(c * 32), v);
+        tc_wait_ld();
+        const int r0 = m0 + c * 32;
+        if (nvalid) {
+          uint16_t* dst = p.out + (long long)r0 * p.ldc + n;
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (r0 + i < mend) dst[(long long)i * p.ldc] = f32_to_bits(__uint_as_float(v[i]) + bv, odt);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&empty_acc[sc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
+}  // namespace oc

@@ -13,6 +13,7 @@
 #include "../../include/oc_b200.h"
 #include "common.cuh"
 #include "dequant.cuh"
+#include "gemm_rows.cuh"
 #include "gemm_tc.cuh"
 #include "gemv.cuh"
 #include "moe.cuh"
@@ -106,6 +107,7 @@ int make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dt, int esize, const void
 }  // namespace
 
 struct oc_b200_layer {
+  int kind;                // 0: AutoGPTQ layer, 1: row-packed (RTN / DSV4) layer or expert group
   int device;
   const uint32_t* qw;
   const uint32_t* qz;
@@ -116,6 +118,12 @@ struct oc_b200_layer {
   int K_in, Kp, N, G, gs, v1;
   int sz_tma, sz_rows;     // scales/zeros staged by TMA in the tcgen05 kernel
   CUtensorMap tmap_w, tmap_s, tmap_z;
+  // row-packed layers
+  int E, wbits, mode, s_dtype_r, z_dtype_r;
+  long long stride_n, stride_g;
+  const CUtensorMap* d_wmaps;
+  const void* const* d_sptr;
+  const void* const* d_zptr;
 };
 
 extern "C" {
@@ -312,6 +320,7 @@ int oc_b200_gptq_layer_create(const int32_t* qweight, const int32_t* qzeros, con
   if (int rc = current_device(&dev)) return rc;
   if (int rc = oc_b200_device_check(dev)) return rc;
   auto* L = new oc_b200_layer();
+  L->kind = 0;
   L->device = dev;
   L->qw = reinterpret_cast<const uint32_t*>(qweight);
   L->qz = reinterpret_cast<const uint32_t*>(qzeros);
@@ -449,6 +458,7 @@ extern "C" int oc_b200_gptq_gemm(const oc_b200_layer* L, const void* a, int a_dt
                       oc_stream_t stream_) {
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   if (!L) return fail(OC_ERR_INVALID, "gptq_gemm: layer is NULL");
+  if (L->kind != 0) return fail(OC_ERR_INVALID, "gptq_gemm: not an AutoGPTQ layer");
   if (M < 0) return fail(OC_ERR_INVALID, "gptq_gemm: M=%lld", (long long)M);
   if (M == 0) return OC_OK;
   if (!a || !c) return fail(OC_ERR_INVALID, "gptq_gemm: NULL activation/output");
@@ -619,4 +629,166 @@ extern "C" int oc_b200_moe_combine(const void* y, int64_t ldy, const int32_t* sl
   else
     oc::moe_combine_kernel<false><<<blocks, 256, 0, stream>>>(yy, ldy, slot_pos, w, T, k, H, sh, lds, o, ldo);
   return launch_check("moe_combine");
+}
+
+// ---------------------------------------------------------------- row-packed (RTN / DSV4) layers
+namespace {
+size_t rows_table_bytes(int E) { return align_up((size_t)E * sizeof(CUtensorMap), 256) + align_up((size_t)E * 16, 256); }
+}
+
+extern "C" size_t oc_b200_rows_table_bytes(int E) { return E > 0 ? rows_table_bytes(E) : 0; }
+
+extern "C" int oc_b200_rows_layer_create(int E, const uint8_t* const* packed, int64_t ld_bytes, int wbits,
+                                         const void* const* scales, int scales_dtype, const void* const* zeros,
+                                         int zeros_dtype, int64_t stride_n, int64_t stride_g, int groupsize, int K,
+                                         int N, int mode, void* table, oc_stream_t stream_, oc_b200_layer** out) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  if (!out) return fail(OC_ERR_INVALID, "rows_layer_create: out is NULL");
+  *out = nullptr;
+  if (E <= 0 || E > oc::kRowsMaxE) return fail(OC_ERR_INVALID, "rows_layer_create: E=%d (1..%d)", E, oc::kRowsMaxE);
+  if (!packed || !scales || !zeros || !table) return fail(OC_ERR_INVALID, "rows_layer_create: NULL pointer");
+  if (wbits != 2 && wbits != 4) return fail(OC_ERR_UNSUPPORTED, "rows_layer_create: wbits=%d", wbits);
+  if (mode != 0 && mode != 1) return fail(OC_ERR_INVALID, "rows_layer_create: mode=%d", mode);
+  if (mode == 1 && wbits != 4) return fail(OC_ERR_UNSUPPORTED, "rows_layer_create: RTN layers are 4-bit");
+  const int span = 32 / wbits;
+  if (K <= 0 || N <= 0 || K % 8 != 0) return fail(OC_ERR_INVALID, "rows_layer_create: K=%d N=%d", K, N);
+  if (ld_bytes * (8 / wbits) < K || ld_bytes % 16 != 0)
+    return fail(OC_ERR_UNSUPPORTED, "rows_layer_create: row stride %lld bytes must cover K and be a multiple of 16",
+                (long long)ld_bytes);
+  if (groupsize <= 0 || (groupsize % span != 0 && groupsize < K))
+    return fail(OC_ERR_UNSUPPORTED, "rows_layer_create: groupsize %d must be a multiple of %d", groupsize, span);
+  if (!dtf(scales_dtype) || !dtf(zeros_dtype)) return fail(OC_ERR_INVALID, "rows_layer_create: dtype");
+  if (!aligned(table, 256)) return fail(OC_ERR_INVALID, "rows_layer_create: table must be 256-byte aligned");
+  int dev = 0;
+  if (int rc = current_device(&dev)) return rc;
+  if (int rc = oc_b200_device_check(dev)) return rc;
+  const size_t maps_bytes = align_up((size_t)E * sizeof(CUtensorMap), 256);
+  uint8_t* host = new uint8_t[rows_table_bytes(E)]();
+  CUtensorMap* maps = reinterpret_cast<CUtensorMap*>(host);
+  const void** sp = reinterpret_cast<const void**>(host + maps_bytes);
+  const void** zp = sp + E;
+  for (int e = 0; e < E; ++e) {
+    if (!packed[e] || !scales[e] || !zeros[e]) {
+      delete[] host;
+      return fail(OC_ERR_INVALID, "rows_layer_create: NULL tensor for expert %d", e);
+    }
+    if (int rc = make_tmap_2d(&maps[e], CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, packed[e], (uint64_t)ld_bytes, (uint64_t)N,
+                              (uint64_t)ld_bytes, (uint32_t)(64 * wbits / 8), 128, CU_TENSOR_MAP_SWIZZLE_NONE)) {
+      delete[] host;
+      return rc;
+    }
+    sp[e] = scales[e];
+    zp[e] = zeros[e];
+  }
+  int rc = cuda_check(cudaMemcpyAsync(table, host, rows_table_bytes(E), cudaMemcpyHostToDevice, stream), "table copy");
+  if (!rc) rc = cuda_check(cudaStreamSynchronize(stream), "table copy sync");
+  delete[] host;
+  if (rc) return rc;
+  auto* L = new oc_b200_layer();
+  L->kind = 1;
+  L->device = dev;
+  L->E = E;
+  L->wbits = wbits;
+  L->mode = mode;
+  L->s_dtype_r = scales_dtype;
+  L->z_dtype_r = zeros_dtype;
+  L->stride_n = stride_n;
+  L->stride_g = stride_g;
+  // one group per row when groupsize covers K (any K % span is then harmless)
+  L->gs = groupsize >= K ? (K + span - 1) / span * span : groupsize;
+  L->K_in = K;
+  L->Kp = K;
+  L->N = N;
+  L->d_wmaps = reinterpret_cast<const CUtensorMap*>(table);
+  L->d_sptr = reinterpret_cast<const void* const*>(reinterpret_cast<uint8_t*>(table) + maps_bytes);
+  L->d_zptr = L->d_sptr + E;
+  *out = L;
+  return OC_OK;
+}
+
+namespace {
+
+template <bool BF16, int WB, int MODE, bool HL, int BT, int ACC, int XS, int WS, int AS>
+int launch_rows_t(const CUtensorMap& tx, const oc::RowsParams& p, int dev, cudaStream_t stream) {
+  using Cfg = oc::RowsCfg<WB, BT, ACC, XS, WS, AS>;
+  auto kern = oc::rows_gemm_tc_kernel<BF16, WB, MODE, HL, BT, ACC, XS, WS, AS>;
+  static bool attr_set[kMaxDevices] = {};
+  if (dev >= 0 && dev < kMaxDevices && !attr_set[dev]) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (int rc = cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes),
+                            "cudaFuncSetAttribute(smem)"))
+      return rc;
+    attr_set[dev] = true;
+  }
+  kern<<<sm_count(dev), oc::kRowsThreads, Cfg::kSmemBytes, stream>>>(tx, p);
+  return launch_check("rows_gemm_tc");
+}
+
+template <bool BF16, int WB, int MODE, bool HL>
+int launch_rows_bt(int bt, const CUtensorMap& tx, const oc::RowsParams& p, int dev, cudaStream_t stream) {
+  if (bt == 128) return launch_rows_t<BF16, WB, MODE, HL, 128, 2, 6, 8, 8>(tx, p, dev, stream);
+  return launch_rows_t<BF16, WB, MODE, HL, 192, 2, 5, 8, 4>(tx, p, dev, stream);
+}
+
+template <bool BF16>
+int launch_rows(int bt, int wbits, int mode, bool has_lo, const CUtensorMap& tx, const oc::RowsParams& p, int dev,
+                cudaStream_t stream) {
+  if (mode == oc::kRowsRtn) return launch_rows_bt<BF16, 4, oc::kRowsRtn, false>(bt, tx, p, dev, stream);
+  if (wbits == 4)
+    return has_lo ? launch_rows_bt<BF16, 4, oc::kRowsExact, true>(bt, tx, p, dev, stream)
+                  : launch_rows_bt<BF16, 4, oc::kRowsExact, false>(bt, tx, p, dev, stream);
+  return has_lo ? launch_rows_bt<BF16, 2, oc::kRowsExact, true>(bt, tx, p, dev, stream)
+                : launch_rows_bt<BF16, 2, oc::kRowsExact, false>(bt, tx, p, dev, stream);
+}
+
+}  // namespace
+
+extern "C" int oc_b200_rows_gemm(const oc_b200_layer* L, const void* a, int a_dtype, int64_t M, int64_t lda,
+                                 const int32_t* offsets, const void* bias, int bias_dtype, void* c, int64_t ldc,
+                                 oc_stream_t stream_) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  if (!L || L->kind != 1) return fail(OC_ERR_INVALID, "rows_gemm: not a row-packed layer");
+  if (M < 0) return fail(OC_ERR_INVALID, "rows_gemm: M=%lld", (long long)M);
+  if (M == 0) return OC_OK;
+  if (!a || !c) return fail(OC_ERR_INVALID, "rows_gemm: NULL activation/output");
+  if (!dt16(a_dtype)) return fail(OC_ERR_INVALID, "rows_gemm: activations must be f16 or bf16");
+  if (L->E > 1 && !offsets) return fail(OC_ERR_INVALID, "rows_gemm: expert groups need offsets");
+  if (bias && (offsets || !dtf(bias_dtype))) return fail(OC_ERR_INVALID, "rows_gemm: bias (dense layers only)");
+  if (lda < L->K_in || lda % 8 != 0 || !aligned(a, 16))
+    return fail(OC_ERR_INVALID, "rows_gemm: A must be 16-byte aligned with lda %% 8 == 0");
+  if (ldc < L->N || !aligned(c, 2)) return fail(OC_ERR_INVALID, "rows_gemm: ldc");
+  if (M > 0x7fffffffLL) return fail(OC_ERR_INVALID, "rows_gemm: M too large");
+  int dev = 0;
+  if (int rc = current_device(&dev)) return rc;
+  if (dev != L->device) return fail(OC_ERR_INVALID, "rows_gemm: layer lives on device %d", L->device);
+  const bool bf16 = a_dtype == OC_DT_BF16;
+  int bt = g_opt_tile.load();
+  if (bt != 128 && bt != 192) bt = offsets ? 128 : 192;
+  CUtensorMap tx;
+  if (int rc = make_tmap_2d(&tx, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a,
+                            (uint64_t)L->K_in, (uint64_t)M, (uint64_t)lda * 2, 64, (uint32_t)bt,
+                            CU_TENSOR_MAP_SWIZZLE_128B))
+    return rc;
+  oc::RowsParams p{};
+  p.M = (int)M;
+  p.N = L->N;
+  p.K = L->K_in;
+  p.E = L->E;
+  p.offsets = offsets;
+  p.wmaps = L->d_wmaps;
+  p.sptr = L->d_sptr;
+  p.zptr = L->d_zptr;
+  p.s_dtype = L->s_dtype_r;
+  p.z_dtype = L->z_dtype_r;
+  p.s_stride_n = L->stride_n;
+  p.s_stride_g = L->stride_g;
+  p.gs = L->gs;
+  p.bias = bias;
+  p.bias_dtype = bias_dtype;
+  p.out = reinterpret_cast<uint16_t*>(c);
+  p.ldc = ldc;
+  p.n_tiles_n = (L->N + 127) / 128;
+  const bool has_lo = L->s_dtype_r != a_dtype;
+  if (bf16) return launch_rows<true>(bt, L->wbits, L->mode, has_lo, tx, p, dev, stream);
+  return launch_rows<false>(bt, L->wbits, L->mode, has_lo, tx, p, dev, stream);
 }

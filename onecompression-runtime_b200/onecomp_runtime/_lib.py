@@ -49,6 +49,10 @@ _SIGNATURES = {
     "oc_b200_layer_destroy": ([_p], _i),
     "oc_b200_gptq_gemm_workspace": ([_p, _i64], _sz),
     "oc_b200_gptq_gemm": ([_p, _p, _i, _i64, _i64, _p, _i, _p, _i64, _p, _sz, _p], _i),
+    "oc_b200_rows_table_bytes": ([_i], _sz),
+    "oc_b200_rows_layer_create": ([_i, _p, _i64, _i, _p, _i, _p, _i, _i64, _i64, _i, _i, _i, _i, _p, _p,
+                                   ctypes.POINTER(_p)], _i),
+    "oc_b200_rows_gemm": ([_p, _p, _i, _i64, _i64, _p, _p, _i, _p, _i64, _p], _i),
     "oc_b200_moe_route": ([_p, _i, _i, _i, _i, _i, _p, _p, _p], _i),
     "oc_b200_moe_permute": ([_p, _i, _i, _i, _p, _p, _p, _p, _p], _i),
     "oc_b200_gather_rows": ([_p, _i64, _p, _i, _i, _p, _i64, _p], _i),

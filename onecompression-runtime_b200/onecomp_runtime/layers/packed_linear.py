@@ -8,8 +8,11 @@ Same API as the reference ``layers/packed_linear.py``:
   activation dtype with a rounding after each op (quant_utils.py:72-103).
 * ``PackedEmbedding`` (reference :65-110): gathers token rows, then dequantizes.
 
-The weight is dequantized by the bit-exact sm_100a RTN kernel
-(``oc_b200_rtn_dequant``); the matmul is ``F.linear`` on that weight.
+On the GPU, ``PackedRTNLinear.forward`` runs the fused row-packed tcgen05 GEMM
+(``oc_b200_rows_gemm``, RTN mode: the kernel multiplies exactly the weights
+``dequant_extra_u8_to_weight`` produces) whenever the byte stride of a packed
+row is a multiple of 16 and the group size a multiple of 8; other shapes
+dequantize with the bit-exact ``oc_b200_rtn_dequant`` kernel and call ``F.linear``.
 """
 from __future__ import annotations
 
@@ -18,6 +21,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from ..quant_utils import dequant_extra_u8_to_weight
+from ._rows_base import MODE_RTN, RowsHandle, float_param, prep_activation, rows_fusable
 
 
 class PackedRTNLinear(nn.Module):
@@ -40,10 +44,39 @@ class PackedRTNLinear(nn.Module):
         return dequant_extra_u8_to_weight(self.qweight_u8, self.scales, self.zeros, self.in_features,
                                           self.out_features, dtype)
 
+    def _rows_handle(self):
+        key = (self.qweight_u8.data_ptr(), self.scales.data_ptr(), self.zeros.data_ptr(), self.scales.dtype,
+               self.zeros.dtype)
+        h = self.__dict__.get("_handle")
+        if h is not None and self.__dict__.get("_handle_key") == key:
+            return h
+        G = int(self.scales.shape[1])
+        gs = self.in_features if G == 1 else self.in_features // G
+        if not rows_fusable(int(self.qweight_u8.shape[1]), self.in_features, self.out_features, gs, 4):
+            return None
+        h = RowsHandle([self.qweight_u8], [float_param(self.scales)], [float_param(self.zeros)], 4, gs,
+                       self.in_features, self.out_features, MODE_RTN, G, 1)
+        self.__dict__["_handle"] = h
+        self.__dict__["_handle_key"] = key
+        return h
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if x.is_cuda and x.dtype in (torch.float16, torch.bfloat16):
+            h = self._rows_handle()
+            if h is not None:
+                a = prep_activation(x, self.in_features)
+                out = torch.empty((a.shape[0], self.out_features), dtype=x.dtype, device=x.device)
+                if a.shape[0]:
+                    bias = self.bias.to(x.dtype) if self.bias is not None else None
+                    h.gemm(a, out, bias=bias)
+                return out.reshape(*x.shape[:-1], self.out_features)
         w = self._materialize(x.dtype)
         bias = self.bias.to(x.dtype) if self.bias is not None else None
         return F.linear(x, w, bias)
+
+    def _apply(self, fn, recurse=True):
+        self.__dict__["_handle"] = None
+        return super()._apply(fn, recurse=recurse)
 
     def extra_repr(self) -> str:
         return (f"in_features={self.in_features}, out_features={self.out_features}, "
