@@ -121,3 +121,97 @@ class ExpertParallelMoE(torch.nn.Module):
         if self.shared is not None:
             out = out + self.shared(x).float()
         return out.to(x.dtype)
+
+
+# ----------------------------------------------------------------------------- B200 module
+class PackedMoE(torch.nn.Module):
+    """Routed packed experts (+ optional shared expert) on the sm_100a kernels.
+
+    ``experts[e]`` and ``shared`` are dicts ``{"gate", "up", "down"}`` of DSV4
+    packed dicts (``qweight_packed``, ``scales``, ``qzeros``, ``wbits``,
+    ``groupsize``, ``in_features``), the format ``Dsv4PackedLinear`` takes.
+    All routed experts share one shape. ``forward(x [T, H], logits [T, E])``.
+    """
+
+    def __init__(self, experts: list[dict], shared: dict | None = None, k: int = 8, renorm: bool = True,
+                 device="cuda"):
+        super().__init__()
+        from . import _lib
+        from .layers._rows_base import MODE_EXACT, RowsHandle, float_param
+        from .layers.dsv4_packed_linear import _stride_of
+        dev = torch.device(device)
+        _lib.require_b200(dev)
+        self.E = len(experts)
+        self.k = int(k)
+        self.renorm = bool(renorm)
+        self.device = dev
+
+        def build(mats: list[dict]):
+            p0 = mats[0]
+            wbits, gs, K = int(p0["wbits"]), int(p0["groupsize"]), int(p0["in_features"])
+            N = int(p0["qweight_packed"].shape[0])
+            q = [m["qweight_packed"].to(dev).contiguous() for m in mats]
+            s = [float_param(m["scales"].to(dev)) for m in mats]
+            z = [float_param(m["qzeros"].to(dev)) for m in mats]
+            sn, sg = _stride_of(s[0], N, K, gs)
+            return RowsHandle(q, s, z, wbits, gs if gs > 0 else K, K, N, MODE_EXACT, sn, sg)
+
+        self._h = {name: build([ex[name] for ex in experts]) for name in ("gate", "up", "down")}
+        self._shared = {name: build([shared[name]]) for name in ("gate", "up", "down")} if shared else None
+        self.hidden = self._h["gate"].K
+        self.ffn = self._h["gate"].N
+
+    def _ffn(self, handles, xs: torch.Tensor, offsets: torch.Tensor | None) -> torch.Tensor:
+        from . import _lib
+        P = xs.shape[0]
+        F_ = handles["gate"].N
+        g = torch.empty((P, 2 * F_), dtype=xs.dtype, device=xs.device)
+        handles["gate"].gemm(xs, g[:, :F_], offsets)
+        handles["up"].gemm(xs, g[:, F_:], offsets)
+        h = torch.empty((P, F_), dtype=xs.dtype, device=xs.device)
+        _lib.call("oc_b200_silu_mul", g.data_ptr(), g[:, F_:].data_ptr(), g.stride(0), P, F_, h.data_ptr(),
+                  h.stride(0), _lib.DT[xs.dtype], _lib.stream_of(xs.device))
+        y = torch.empty((P, handles["down"].N), dtype=xs.dtype, device=xs.device)
+        handles["down"].gemm(h, y, offsets)
+        return y
+
+    def expert_ffn(self, xs: torch.Tensor, offsets: torch.Tensor) -> torch.Tensor:
+        """Grouped SwiGLU FFN over rows sorted by expert (``offsets`` int32 [E+1] on the device)."""
+        if xs.shape[0] == 0:
+            return xs.new_empty((0, self._h["down"].N))
+        return self._ffn(self._h, xs.contiguous(), offsets.to(device=xs.device, dtype=torch.int32))
+
+    def route(self, logits: torch.Tensor, k: int):
+        from . import _lib
+        T, E = logits.shape
+        ids = torch.empty((T, k), dtype=torch.int32, device=logits.device)
+        w = torch.empty((T, k), dtype=torch.float32, device=logits.device)
+        lg = logits.contiguous()
+        _lib.call("oc_b200_moe_route", lg.data_ptr(), _lib.DT[lg.dtype], T, E, k, int(self.renorm), ids.data_ptr(),
+                  w.data_ptr(), _lib.stream_of(lg.device))
+        return ids, w
+
+    def forward(self, x: torch.Tensor, logits: torch.Tensor) -> torch.Tensor:
+        from . import _lib
+        T, H = x.shape
+        dev = x.device
+        st = _lib.stream_of(dev)
+        x = x.contiguous()
+        ids, w = self.route(logits, self.k)
+        TK = T * self.k
+        counts = torch.empty(self.E, dtype=torch.int32, device=dev)
+        offsets = torch.empty(self.E + 1, dtype=torch.int32, device=dev)
+        sorted_token = torch.empty(TK, dtype=torch.int32, device=dev)
+        slot_pos = torch.empty(TK, dtype=torch.int32, device=dev)
+        _lib.call("oc_b200_moe_permute", ids.data_ptr(), T, self.k, self.E, counts.data_ptr(), offsets.data_ptr(),
+                  sorted_token.data_ptr(), slot_pos.data_ptr(), st)
+        xs = torch.empty((TK, H), dtype=x.dtype, device=dev)
+        _lib.call("oc_b200_gather_rows", x.data_ptr(), x.stride(0), sorted_token.data_ptr(), TK, H, xs.data_ptr(),
+                  xs.stride(0), st)
+        y = self._ffn(self._h, xs, offsets) if TK else xs.new_empty((0, H))
+        shared = self._ffn(self._shared, x, None) if self._shared is not None else None
+        out = torch.empty((T, H), dtype=x.dtype, device=dev)
+        _lib.call("oc_b200_moe_combine", y.data_ptr(), y.stride(0), slot_pos.data_ptr(), w.data_ptr(), T, self.k, H,
+                  None if shared is None else shared.data_ptr(), 0 if shared is None else shared.stride(0),
+                  out.data_ptr(), out.stride(0), _lib.DT[x.dtype], st)
+        return out
