@@ -253,6 +253,143 @@ def bench_decode(args):
     print(json.dumps(line), flush=True)
 
 
+# ----------------------------------------------------------------------------- MoE (cfg3)
+def _dist_init(dev):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world > 1 and not torch.distributed.is_initialized():
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    return world, int(os.environ.get("RANK", "0"))
+
+
+def _timed(fn, steps, warmup, dev, world):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        torch.distributed.barrier()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record()
+    for _ in range(steps):
+        fn()
+    s1.record()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        torch.distributed.barrier()
+    ms = torch.tensor([s0.elapsed_time(s1) / steps], device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(ms, op=torch.distributed.ReduceOp.MAX)
+    return float(ms[0])
+
+
+def bench_moe(args):
+    """256 int2 experts (top-8) + int4 shared expert, T=2048 tokens per rank.
+
+    N ranks: experts split contiguously, each rank routes its own 2048 tokens and exchanges
+    rows with NCCL all_to_all (weak scaling). value = tokens/s over all ranks.
+    """
+    from onecomp_runtime import _lib
+    from onecomp_runtime.moe import ExpertParallelMoE, PackedMoE
+    from onecomp_runtime.testing import CFG3, dsv4_packed
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    world, rank = _dist_init(dev)
+    _lib.require_b200(dev)
+    E, k, H, F, T = CFG3["E"], CFG3["k"], CFG3["H"], CFG3["F"], CFG3["T"]
+    el = E // world
+    wb, gs = CFG3["expert_wbits"], CFG3["expert_gs"]
+    experts = [{"gate": dsv4_packed(F, H, wb, gs, seed=3 * e, device=dev),
+                "up": dsv4_packed(F, H, wb, gs, seed=3 * e + 1, device=dev),
+                "down": dsv4_packed(H, F, wb, gs, seed=3 * e + 2, device=dev)} for e in range(rank * el, (rank + 1) * el)]
+    sw, sgs = CFG3["shared_wbits"], CFG3["shared_gs"]
+    shared = {"gate": dsv4_packed(F, H, sw, sgs, seed=9000, zero=None, scales_range=(0.002, 0.02), device=dev),
+              "up": dsv4_packed(F, H, sw, sgs, seed=9001, zero=None, scales_range=(0.002, 0.02), device=dev),
+              "down": dsv4_packed(H, F, sw, sgs, seed=9002, zero=None, scales_range=(0.002, 0.02), device=dev)}
+    g = torch.Generator(device=dev).manual_seed(77 + rank)
+    x = torch.randn((T, H), generator=g, device=dev).to(torch.bfloat16)
+    logits = torch.randn((T, E), generator=g, device=dev)
+    if world == 1:
+        moe = PackedMoE(experts, shared, k=k, device=dev)
+        fn = lambda: moe(x, logits)  # noqa: E731
+    else:
+        loc = PackedMoE(experts, shared, k=k, device=dev)
+        ep = ExpertParallelMoE(E, k, loc.expert_ffn, route=loc.route,
+                               shared=lambda xx: loc._ffn(loc._shared, xx.contiguous(), None))
+        fn = lambda: ep(x, logits)  # noqa: E731
+    with torch.no_grad():
+        ms = _timed(fn, args.steps, args.warmup, dev, world)
+    flops = 2 * T * k * 3 * H * F + 2 * T * 3 * H * F
+    line = {"metric": "packed-MoE layer tokens/s (256 int2 experts top-8 + int4 shared)",
+            "value": round(world * T / (ms / 1e3), 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "cfg3", "tokens_per_gpu": T, "experts_per_gpu": el,
+                       "parallelism": f"expert parallel x{world} (NCCL all_to_all)" if world > 1 else "1 GPU"},
+            "tflops_per_gpu": round(flops / (ms / 1e3) / 1e12, 1)}
+    if world > 1:
+        torch.distributed.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- TP stack (cfg4)
+def bench_tp(args):
+    """12 video-DiT blocks (hidden 4096), M=32768 tokens, column/row tensor parallel.
+
+    Strong scaling: the same 32768 tokens on every N; row-parallel outputs are summed with a
+    chunked NCCL all-reduce that overlaps the next chunk's GEMM.
+    """
+    from onecomp_runtime import _lib
+    from onecomp_runtime.layers import FusedInt4Linear
+    from onecomp_runtime.tensor_parallel import build_tp_block
+    from onecomp_runtime.testing import CFG4, CFG4_LAYERS, gptq_layer
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    world, rank = _dist_init(dev)
+    _lib.require_b200(dev)
+    blocks = args.blocks or CFG4["blocks"]
+    M, gs, H = CFG4["M"], CFG4["gs"], CFG4["hidden"]
+
+    def make(t, K, N):
+        return FusedInt4Linear(K, N, t["qweight"], t["scales"], t["qzeros"], t.get("bias"), gs)
+
+    stack = []
+    for b in range(blocks):
+        tens = {name: gptq_layer(K, N, gs, seed=4000 + 10 * b + i, device=dev)
+                for i, (name, K, N) in enumerate(CFG4_LAYERS)}
+        stack.append(build_tp_block(tens, CFG4_LAYERS, rank, world, gs, make))
+        del tens
+    g = torch.Generator(device=dev).manual_seed(5)
+    x = torch.randn((M, H), generator=g, device=dev).to(torch.bfloat16)
+    hq = H // world
+
+    def step():
+        h = x
+        for blk in stack:
+            qkv = blk["qkv"](h)
+            h = rms_norm(h + blk["out"](qkv[:, :hq]))
+            f = torch.nn.functional.gelu(blk["fc1"](h), approximate="tanh")
+            h = rms_norm(h + blk["fc2"](f))
+        return h
+
+    with torch.no_grad():
+        ms = _timed(step, args.steps, args.warmup, dev, world)
+    flops = blocks * sum(2 * M * K * N for _, K, N in CFG4_LAYERS)
+    line = {"metric": "TP video-DiT stack tokens/s (12 blocks, hidden 4096, int4 GPTQ gs32)",
+            "value": round(M / (ms / 1e3), 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "cfg4", "tokens": M, "blocks": blocks,
+                       "parallelism": f"tensor parallel x{world} (column/row, NCCL all-reduce)"},
+            "tflops_total": round(flops / (ms / 1e3) / 1e12, 1)}
+    if world > 1:
+        torch.distributed.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 # ----------------------------------------------------------------------------- main
 def main():
     ap = argparse.ArgumentParser()
@@ -260,8 +397,9 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--workload", default="cfg1", choices=["cfg1", "cfg2"],
-                    help="cfg1: DiT stack (default, headline); cfg2: decode GEMV layer set")
+    ap.add_argument("--workload", default="cfg1", choices=["cfg1", "cfg2", "cfg3", "cfg4"],
+                    help="cfg1: DiT stack (default, headline); cfg2: decode GEMV layer set; "
+                         "cfg3: packed MoE layer (expert parallel); cfg4: tensor-parallel video-DiT stack")
     ap.add_argument("--tc-tile", type=int, default=0, help="tokens per tcgen05 tile (0 = library default)")
     ap.add_argument("--gemv-ctas", type=int, default=0, help="GEMV split-K target CTAs per SM (0 = default)")
     ap.add_argument("--blocks", type=int, default=0, help="override the number of DiT blocks (profiling only)")
@@ -273,6 +411,10 @@ def main():
 
     if args.workload == "cfg2":
         return bench_decode(args)
+    if args.workload == "cfg3":
+        return bench_moe(args)
+    if args.workload == "cfg4":
+        return bench_tp(args)
     from onecomp_runtime.testing import CFG1, CFG1_LAYERS
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

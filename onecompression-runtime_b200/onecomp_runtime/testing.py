@@ -86,3 +86,26 @@ def entry(name: str, K: int, N: int, groupsize: int, actorder: bool = False, wbi
     """A ``quant_layers_json`` manifest entry (diffusion.py contract)."""
     return {"name": name, "wbits": wbits, "groupsize": groupsize, "actorder": actorder,
             "in_features": K, "out_features": N}
+
+
+# packed MoE layer: 256 experts, top-8, hidden 4096, FFN 2048; int2 DSV4 experts gs64, zeros 1.5;
+# shared expert int4 gs128; T = 2048 tokens
+CFG3 = dict(E=256, k=8, H=4096, F=2048, T=2048, expert_wbits=2, expert_gs=64, shared_wbits=4, shared_gs=128)
+
+
+def dsv4_packed(out_f: int, in_f: int, wbits: int, groupsize: int, *, seed: int = 0, zero: float | None = 1.5,
+                scales_range=(0.005, 0.05), device="cpu") -> dict:
+    """Random DSV4 byte-packed layer dict (``qweight_packed``, ``scales``, ``qzeros`` [out, G] fp16)."""
+    g = torch.Generator(device=torch.device(device)).manual_seed(int(seed))
+    per = 8 // wbits
+    ncol = (in_f + per - 1) // per
+    packed = torch.randint(0, 256, (out_f, ncol), generator=g, device=device, dtype=torch.int32).to(torch.uint8)
+    G = (in_f + groupsize - 1) // groupsize if groupsize > 0 else 1
+    lo, hi = scales_range
+    scales = (torch.rand((out_f, G), generator=g, device=device) * (hi - lo) + lo).to(torch.float16)
+    if zero is None:
+        zeros = (torch.rand((out_f, G), generator=g, device=device) * ((1 << wbits) - 1)).to(torch.float16)
+    else:
+        zeros = torch.full((out_f, G), zero, dtype=torch.float16, device=device)
+    return {"qweight_packed": packed, "scales": scales, "qzeros": zeros, "wbits": wbits, "groupsize": groupsize,
+            "in_features": in_f}
