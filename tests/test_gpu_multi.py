@@ -1,0 +1,109 @@
+"""Tensor- and expert-parallel paths on 2 GPUs over NCCL (skipped with fewer GPUs).
+
+Each test spawns one process per GPU; rank 0 compares the parallel result with the
+same layer computed on one GPU with the unsharded weights.
+"""
+from __future__ import annotations
+
+import datetime
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _need_gpus(n):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < n:
+        pytest.skip(f"needs {n} GPUs")
+    if torch.cuda.get_device_capability(0) != (10, 0):
+        pytest.skip("needs sm_100")
+
+
+def _init(rank, world, port):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    torch.distributed.init_process_group("nccl", rank=rank, world_size=world,
+                                         timeout=datetime.timedelta(seconds=60), device_id=dev)
+    return dev
+
+
+LAYERS = (("qkv", 512, 1536), ("out", 512, 512), ("fc1", 512, 2048), ("fc2", 2048, 512))
+
+
+def _tp_worker(rank, world, port, out_path):
+    dev = _init(rank, world, port)
+    from onecomp_runtime.layers import FusedInt4Linear
+    from onecomp_runtime.tensor_parallel import build_tp_block
+    from onecomp_runtime.testing import gptq_layer
+
+    def make(t, K, N):
+        return FusedInt4Linear(K, N, t["qweight"], t["scales"], t["qzeros"], t.get("bias"), 32)
+
+    tens = {n: gptq_layer(K, N, 32, seed=70 + i, device=dev) for i, (n, K, N) in enumerate(LAYERS)}
+    x = torch.randn(300, 512, generator=torch.Generator(device=dev).manual_seed(1), device=dev).to(torch.bfloat16)
+
+    def fwd(blk, q):
+        qkv = blk["qkv"](x)
+        h = x + blk["out"](qkv[:, :q])
+        return h + blk["fc2"](torch.nn.functional.gelu(blk["fc1"](h), approximate="tanh"))
+
+    y = fwd(build_tp_block(tens, LAYERS, rank, world, 32, make, chunks=2), 512 // world)
+    if rank == 0:
+        full = {n: make(tens[n], K, N) for n, K, N in LAYERS}
+        ref = fwd(full, 512)
+        err = float((y.float() - ref.float()).abs().max() / ref.float().abs().max())
+        torch.save(torch.tensor([err]), out_path)
+    torch.distributed.barrier()
+    torch.distributed.destroy_process_group()
+
+
+def test_tp_two_gpus(tmp_path):
+    _need_gpus(2)
+    out = tmp_path / "err.pt"
+    mp.spawn(_tp_worker, args=(2, _free_port(), str(out)), nprocs=2, join=True)
+    assert float(torch.load(out)[0]) < 2e-2
+
+
+def _ep_worker(rank, world, port, out_path):
+    dev = _init(rank, world, port)
+    from onecomp_runtime.moe import ExpertParallelMoE, PackedMoE
+    from onecomp_runtime.testing import dsv4_packed
+    E, k, H, F, T = 8, 2, 256, 128, 24
+    experts = [{"gate": dsv4_packed(F, H, 2, 64, seed=3 * e, device=dev),
+                "up": dsv4_packed(F, H, 2, 64, seed=3 * e + 1, device=dev),
+                "down": dsv4_packed(H, F, 2, 64, seed=3 * e + 2, device=dev)} for e in range(E)]
+    g = torch.Generator(device=dev).manual_seed(9)
+    x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+    logits = torch.randn(T, E, generator=g, device=dev)
+    el = E // world
+    local = PackedMoE(experts[rank * el:(rank + 1) * el], None, k=k, device=dev)
+    ep = ExpertParallelMoE(E, k, local.expert_ffn, route=local.route)
+    sh = T // world
+    y = ep(x[rank * sh:(rank + 1) * sh], logits[rank * sh:(rank + 1) * sh])
+    ys = [torch.empty_like(y) for _ in range(world)]
+    torch.distributed.all_gather(ys, y)
+    if rank == 0:
+        ref = PackedMoE(experts, None, k=k, device=dev)(x, logits)
+        y = torch.cat(ys)
+        err = float((y.float() - ref.float()).abs().max() / ref.float().abs().max())
+        torch.save(torch.tensor([err]), out_path)
+    torch.distributed.barrier()
+    torch.distributed.destroy_process_group()
+
+
+def test_ep_two_gpus(tmp_path):
+    _need_gpus(2)
+    out = tmp_path / "err.pt"
+    mp.spawn(_ep_worker, args=(2, _free_port(), str(out)), nprocs=2, join=True)
+    assert float(torch.load(out)[0]) < 1e-2
