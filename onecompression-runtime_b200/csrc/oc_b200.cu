@@ -720,7 +720,11 @@ int launch_rows_t(const CUtensorMap& tx, const oc::RowsParams& p, int dev, cudaS
       return rc;
     attr_set[dev] = true;
   }
-  kern<<<sm_count(dev), oc::kRowsThreads, Cfg::kSmemBytes, stream>>>(tx, p);
+  // upper bound on tiles: every expert segment adds at most one partial m-tile
+  const long long m_tiles = ((long long)p.M + BT - 1) / BT + (p.offsets ? p.E : 0);
+  const long long tiles = m_tiles * p.n_tiles_n;
+  const int grid = tiles < sm_count(dev) ? (int)tiles : sm_count(dev);
+  kern<<<grid, oc::kRowsThreads, Cfg::kSmemBytes, stream>>>(tx, p);
   return launch_check("rows_gemm_tc");
 }
 
