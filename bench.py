@@ -106,8 +106,8 @@ class ClockSampler:
 
 # ----------------------------------------------------------------------------- model
 def rms_norm(h: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
-    hf = h.float()
-    return (hf * torch.rsqrt(hf.pow(2).mean(-1, keepdim=True) + eps)).to(h.dtype)
+    """RMS norm without weight, fp32 statistics (torch's fused rms_norm)."""
+    return torch.nn.functional.rms_norm(h, (h.shape[-1],), eps=eps)
 
 
 class DiTStack:
@@ -126,25 +126,28 @@ class DiTStack:
         self.hidden = layers[0][1]
         self.gemm_events: list | None = None
 
-    def _lin(self, layer, x):
+    def _lin(self, layer, x, residual=None, activation=None):
         if self.gemm_events is None:
-            return layer(x)
+            return layer.forward_fused(x, residual=residual, activation=activation)
         s = torch.cuda.Event(enable_timing=True)
         e = torch.cuda.Event(enable_timing=True)
         s.record()
-        y = layer(x)
+        y = layer.forward_fused(x, residual=residual, activation=activation)
         e.record()
         self.gemm_events.append((s, e, 2 * x.shape[0] * layer.in_features * layer.out_features))
         return y
 
     def forward(self, h: torch.Tensor) -> torch.Tensor:
+        """Per block: q = qkv(h)[:, :H]; h = rms(h + proj(q)); h = rms(h + fc2(gelu(fc1(h)))).
+
+        The residual adds and the tanh-GELU run in the GEMM epilogues (forward_fused)."""
         H = self.hidden
         for blk in self.blocks:
             qkv = self._lin(blk["qkv"], h)
             q = qkv[:, :H]                       # attention stand-in: the q slice
-            h = rms_norm(h + self._lin(blk["proj"], q))
-            f = torch.nn.functional.gelu(self._lin(blk["fc1"], h), approximate="tanh")
-            h = rms_norm(h + self._lin(blk["fc2"], f))
+            h = rms_norm(self._lin(blk["proj"], q, residual=h))
+            f = self._lin(blk["fc1"], h, activation="gelu_tanh")
+            h = rms_norm(self._lin(blk["fc2"], f, residual=h))
         return h
 
     def gemm_count_per_step(self) -> int:

@@ -123,6 +123,14 @@ size_t oc_b200_gptq_gemm_workspace(const oc_b200_layer* layer, int64_t M);
 int oc_b200_gptq_gemm(const oc_b200_layer* layer, const void* a, int a_dtype, int64_t M, int64_t lda,
                       const void* bias, int bias_dtype, void* c, int64_t ldc, void* workspace,
                       size_t workspace_bytes, oc_stream_t stream);
+enum { OC_ACT_NONE = 0, OC_ACT_GELU_TANH = 1 };
+/* oc_b200_gptq_gemm with a fused epilogue: C = act(A @ W^T + bias) + residual, evaluated in
+ * fp32 and rounded once (act: OC_ACT_NONE or OC_ACT_GELU_TANH, torch's approximate="tanh";
+ * residual: optional [M, ldr] in a_dtype, may alias C). Folds the activation and residual
+ * add that follow the reference's linears in DiT blocks into the GEMM's store. */
+int oc_b200_gptq_gemm_ex(const oc_b200_layer* layer, const void* a, int a_dtype, int64_t M, int64_t lda,
+                         const void* bias, int bias_dtype, const void* residual, int64_t ldr, int act, void* c,
+                         int64_t ldc, void* workspace, size_t workspace_bytes, oc_stream_t stream);
 
 /* ---- row-packed int4/int2 linears: RTN nibble layers, DSV4 layers, expert groups ---- */
 /* Device bytes the caller provides (256-byte aligned) to describe E row-packed matrices. */

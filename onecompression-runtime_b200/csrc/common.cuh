@@ -62,6 +62,23 @@ __device__ __forceinline__ float bits_to_f32(uint16_t b, int dtype) {
   return __bfloat162float(__ushort_as_bfloat16(b));
 }
 
+// GEMM epilogue activations
+enum Act : int { kActNone = 0, kActGeluTanh = 1 };
+
+// 0.5 v (1 + tanh(sqrt(2/pi) (v + 0.044715 v^3))) -- torch's approximate="tanh" GELU
+__device__ __forceinline__ float gelu_tanh(float v) {
+  const float u = 0.7978845608028654f * (v + 0.044715f * v * v * v);
+  return 0.5f * v * (1.f + tanhf(u));
+}
+
+__device__ __forceinline__ float epilogue_value(float acc, float bias, int act, const uint16_t* residual,
+                                                int dtype) {
+  float v = acc + bias;
+  if (act == kActGeluTanh) v = gelu_tanh(v);
+  if (residual) v += bits_to_f32(*residual, dtype);
+  return v;
+}
+
 // ----------------------------------------------------------------------------
 // packed 16-bit pair arithmetic (each op rounds the exact result once, RNE)
 // ----------------------------------------------------------------------------

@@ -177,10 +177,33 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
   };
 
   if (warp == 0) {
+    // activation tiles
     if (lane == 0) {
       int it = 0;
-      int x_armed[X_STAGES], w_armed[W_STAGES];
+      int x_armed[X_STAGES];
       for (int i = 0; i < X_STAGES; ++i) x_armed[i] = -1;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+        int e, m0, mend, nb;
+        tile_info(tile, e, m0, mend, nb);
+        for (int kb = 0; kb < KB; ++kb, ++it) {
+          const int sx = it % X_STAGES, px = (it / X_STAGES) & 1;
+          if (!mbar_wait(&empty_x[sx], px ^ 1, abort_flag, kDevErrTmaEmpty)) { ok = false; break; }
+          mbar_arrive_expect_tx(&full_x[sx], Cfg::kXStageBytes);
+          tma_load_2d(x_smem + sx * Cfg::kXStageBytes, &tmap_x, &full_x[sx], kb * 64, m0);
+          x_armed[sx] = px;
+        }
+      }
+      if (!ok) {
+        for (int i = 0; i < X_STAGES; ++i)
+          if (x_armed[i] >= 0) mbar_drain(&full_x[i], x_armed[i]);
+      }
+    }
+  } else if (warp == 2) {
+    // packed weight tiles, decoupled from the activation stream
+    if (lane == 0) {
+      int it = 0;
+      int w_armed[W_STAGES];
       for (int i = 0; i < W_STAGES; ++i) w_armed[i] = -1;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
@@ -188,12 +211,7 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
         tile_info(tile, e, m0, mend, nb);
         const CUtensorMap* wm = p.wmaps + e;
         for (int kb = 0; kb < KB; ++kb, ++it) {
-          const int sx = it % X_STAGES, px = (it / X_STAGES) & 1;
           const int sw = it % W_STAGES, pw = (it / W_STAGES) & 1;
-          if (!mbar_wait(&empty_x[sx], px ^ 1, abort_flag, kDevErrTmaEmpty)) { ok = false; break; }
-          mbar_arrive_expect_tx(&full_x[sx], Cfg::kXStageBytes);
-          tma_load_2d(x_smem + sx * Cfg::kXStageBytes, &tmap_x, &full_x[sx], kb * 64, m0);
-          x_armed[sx] = px;
           if (!mbar_wait(&empty_w[sw], pw ^ 1, abort_flag, kDevErrWEmpty)) { ok = false; break; }
           mbar_arrive_expect_tx(&full_w[sw], Cfg::kWStageBytes);
           tma_load_2d(w_smem + sw * Cfg::kWStageBytes, wm, &full_w[sw], kb * Cfg::kKbBytes, nb * 128);
@@ -201,8 +219,6 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
         }
       }
       if (!ok) {
-        for (int i = 0; i < X_STAGES; ++i)
-          if (x_armed[i] >= 0) mbar_drain(&full_x[i], x_armed[i]);
         for (int i = 0; i < W_STAGES; ++i)
           if (w_armed[i] >= 0) mbar_drain(&full_w[i], w_armed[i]);
       }

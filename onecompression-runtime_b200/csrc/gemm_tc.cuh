@@ -17,7 +17,9 @@
 //     structures read scales/zeros with cached global loads.
 //   * Exact dequant: w = RNE(s*(q-z)) as in quant_utils.dequant_gptq_to_fp.
 // Warp roles (512 threads, one persistent CTA per SM):
-//   warp 0 lane 0: TMA producer      warp 1: TMEM alloc + MMA issuer (lane 0)
+//   warp 0 lane 0: TMA producer of activation tiles
+//   warp 2 lane 0: TMA producer of packed weights/scales/zeros (runs ahead, decoupled)
+//   warp 1: TMEM alloc + MMA issuer (lane 0)
 //   warps 4-7 / 8-11: dequant warpgroups for even / odd k-blocks
 //   warps 12-15: epilogue warpgroup (tcgen05.ld, bias, round, store)
 // Every mbarrier wait is bounded in time; on timeout the kernel records an error
@@ -39,6 +41,9 @@ struct TcParams {
   int sz_rows;             // scale rows per 64-k block when sz_tma (1 or 2)
   const void* bias;
   int bias_dtype;
+  const uint16_t* residual;  // optional [M, ldr] added after the activation
+  long long ldr;
+  int act;                   // Act
   uint16_t* out;
   long long ldc;
   int n_tiles_n, n_tiles_m, num_tiles;
@@ -117,22 +122,40 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const uint32_t tmem_base = *tmem_holder;
 
   if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer
+    // ------------------------------------------------------------ TMA producer: activation tiles
     if (lane == 0) {
       int it = 0;
-      int x_armed[X_STAGES], w_armed[W_STAGES];
+      int x_armed[X_STAGES];
       for (int i = 0; i < X_STAGES; ++i) x_armed[i] = -1;
-      for (int i = 0; i < W_STAGES; ++i) w_armed[i] = -1;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
-        const int nb = tile % p.n_tiles_n, mb = tile / p.n_tiles_n;
+        const int mb = tile / p.n_tiles_n;
         for (int kb = 0; kb < KB; ++kb, ++it) {
           const int sx = it % X_STAGES, px = (it / X_STAGES) & 1;
-          const int sw = it % W_STAGES, pw = (it / W_STAGES) & 1;
           if (!mbar_wait(&empty_x[sx], px ^ 1, abort_flag, kDevErrTmaEmpty)) { ok = false; break; }
           mbar_arrive_expect_tx(&full_x[sx], Cfg::kXStageBytes);
           tma_load_2d(x_smem + sx * Cfg::kXStageBytes, &tmap_x, &full_x[sx], kb * kTcBK, mb * BT);
           x_armed[sx] = px;
+        }
+      }
+      if (!ok) {
+        // drain our own loads in flight before the CTA (and its smem) goes away
+        for (int i = 0; i < X_STAGES; ++i)
+          if (x_armed[i] >= 0) mbar_drain(&full_x[i], x_armed[i]);
+      }
+    }
+  } else if (warp == 2) {
+    // ------------------------------------------------------------ TMA producer: packed weights (+ scales/zeros)
+    // Runs ahead of the activation stream by up to W_STAGES blocks so dequant overlaps the MMAs.
+    if (lane == 0) {
+      int it = 0;
+      int w_armed[W_STAGES];
+      for (int i = 0; i < W_STAGES; ++i) w_armed[i] = -1;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+        const int nb = tile % p.n_tiles_n;
+        for (int kb = 0; kb < KB; ++kb, ++it) {
+          const int sw = it % W_STAGES, pw = (it / W_STAGES) & 1;
           if (!mbar_wait(&empty_w[sw], pw ^ 1, abort_flag, kDevErrWEmpty)) { ok = false; break; }
           uint8_t* ws = w_smem + sw * kTcWStageBytes;
           mbar_arrive_expect_tx(&full_w[sw], w_tx);
@@ -146,9 +169,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
       }
       if (!ok) {
-        // drain our own loads in flight before the CTA (and its smem) goes away
-        for (int i = 0; i < X_STAGES; ++i)
-          if (x_armed[i] >= 0) mbar_drain(&full_x[i], x_armed[i]);
         for (int i = 0; i < W_STAGES; ++i)
           if (w_armed[i] >= 0) mbar_drain(&full_w[i], w_armed[i]);
       }
@@ -303,9 +323,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int m0 = mb * BT + c * 32;
         if (nvalid) {
           uint16_t* dst = p.out + (long long)m0 * p.ldc + n;
+          if (!p.residual && p.act == kActNone) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            if (m0 + i < p.M) dst[(long long)i * p.ldc] = f32_to_bits(__uint_as_float(v[i]) + bv, odt);
+            for (int i = 0; i < 32; ++i)
+              if (m0 + i < p.M) dst[(long long)i * p.ldc] = f32_to_bits(__uint_as_float(v[i]) + bv, odt);
+          } else {
+            const uint16_t* res = p.residual ? p.residual + (long long)m0 * p.ldr + n : nullptr;
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (m0 + i < p.M)
+                dst[(long long)i * p.ldc] = f32_to_bits(
+                    epilogue_value(__uint_as_float(v[i]), bv, p.act, res ? res + (long long)i * p.ldr : nullptr, odt),
+                    odt);
           }
         }
       }

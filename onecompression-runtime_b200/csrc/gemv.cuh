@@ -38,6 +38,9 @@ struct GemvParams {
   int Kp, N, G, gs, v1;
   const void* bias;         // [N] or null
   int bias_dtype;
+  const uint16_t* residual; // optional [M, ldr] added after the activation
+  long long ldr;
+  int act;                  // Act
   uint16_t* out;            // [M, ldc]
   long long ldc;
   float* ws;                // [splits, M, N] fp32 partials (splits > 1)
@@ -75,19 +78,25 @@ struct GemvStage {
   int valid;
 };
 
+// Every lane of a warp must execute the same mma.sync, so out-of-range lanes are not
+// skipped: a k-word past K loads zero activations (its B rows contribute nothing), a
+// column past N loads zero weights/scales (its A rows feed only discarded outputs) but
+// still loads the activations, because a lane's B fragment feeds every row of the tile.
 template <int MT>
 __device__ __forceinline__ void gemv_load(GemvStage& st, const GemvParams& p, int kw, int col, int g) {
   const int kw_rows = p.Kp >> 3;
-  st.valid = (kw < kw_rows) && (col < p.N);
+  const bool kvalid = kw < kw_rows;
+  st.valid = kvalid && (col < p.N);
   st.w = make_uint4(0, 0, 0, 0);
   st.xa = make_uint4(0, 0, 0, 0);
   st.xb = make_uint4(0, 0, 0, 0);
   st.s = make_uint2(0, 0);
   st.z = 0;
-  if (!st.valid) return;
-  st.w = __ldg(reinterpret_cast<const uint4*>(p.qw + (long long)kw * p.N + col));
+  if (!kvalid) return;
   if (g < p.M) st.xa = __ldg(reinterpret_cast<const uint4*>(p.x + (long long)g * p.ldx + 8 * kw));
   if (MT == 2 && g + 8 < p.M) st.xb = __ldg(reinterpret_cast<const uint4*>(p.x + (long long)(g + 8) * p.ldx + 8 * kw));
+  if (!st.valid) return;
+  st.w = __ldg(reinterpret_cast<const uint4*>(p.qw + (long long)kw * p.N + col));
   const int grp = p.wgrp ? __ldg(p.wgrp + kw) : (8 * kw) / p.gs;
   st.s = __ldg(reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(p.s) + (long long)grp * p.N + col));
   st.z = __ldg(p.qz + (long long)grp * (p.N >> 3) + (col >> 3));
@@ -97,7 +106,6 @@ template <bool BF16, bool HAS_LO, int MT>
 __device__ __forceinline__ void gemv_compute(const GemvStage& st, const GemvParams& p, int col,
                                              float (&acc)[MT][2][4]) {
   using P = Pair<BF16>;
-  if (!st.valid) return;
   const int zsh = 4 * (col & 7);
   uint32_t pr[4][4];  // [column j][pair: (k0,k4) (k1,k5) (k2,k6) (k3,k7)]
   const uint32_t sw[4] = {st.s.x & 0xFFFFu, st.s.x >> 16, st.s.y & 0xFFFFu, st.s.y >> 16};
@@ -131,6 +139,76 @@ __device__ __forceinline__ void gemv_compute(const GemvStage& st, const GemvPara
       mma_16816<BF16>(acc[mt][beta], a1, b10, b11);
     }
   }
+}
+
+// Split-K partials (deterministic last-CTA reduction), bias, rounding, store.
+// fragment -> (token, 4 columns): token 8*a + 2t + h has columns col..col+3 =
+// {acc[a][0][h], acc[a][0][2+h], acc[a][1][h], acc[a][1][2+h]}
+template <bool BF16, int MT>
+__device__ __forceinline__ void gemv_finish(const GemvParams& p, float (&acc)[MT][2][4], int wk, int col, int t,
+                                            int tile, int split, int* is_last) {
+  if (p.splits > 1) {
+    if (wk == 0 && col < p.N) {
+#pragma unroll
+      for (int a = 0; a < MT; ++a)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int tok = 8 * a + 2 * t + h;
+          if (tok < p.M) {
+            const float4 v = make_float4(acc[a][0][h], acc[a][0][2 + h], acc[a][1][h], acc[a][1][2 + h]);
+            *reinterpret_cast<float4*>(p.ws + ((long long)split * p.M + tok) * p.N + col) = v;
+          }
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const unsigned prev = atomicAdd(p.tickets + tile, 1u);
+      *is_last = (prev == (unsigned)(p.splits - 1));
+    }
+    __syncthreads();
+    if (!*is_last) return;
+    __threadfence();
+    if (wk == 0 && col < p.N) {
+#pragma unroll
+      for (int a = 0; a < MT; ++a)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int tok = 8 * a + 2 * t + h;
+          if (tok < p.M) {
+            float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int sp = 0; sp < p.splits; ++sp) {
+              const float4 v = __ldcg(reinterpret_cast<const float4*>(p.ws + ((long long)sp * p.M + tok) * p.N + col));
+              sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
+            }
+            acc[a][0][h] = sum.x; acc[a][0][2 + h] = sum.y; acc[a][1][h] = sum.z; acc[a][1][2 + h] = sum.w;
+          }
+        }
+    }
+    if (threadIdx.x == 0) p.tickets[tile] = 0u;  // re-arm for the next launch (stream order)
+  }
+  if (wk != 0 || col >= p.N) return;
+  float bv[4] = {0.f, 0.f, 0.f, 0.f};
+  if (p.bias) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) bv[j] = load_as_f32(p.bias, p.bias_dtype, col + j);
+  }
+  const int odt = BF16 ? kBF16 : kF16;
+#pragma unroll
+  for (int a = 0; a < MT; ++a)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int tok = 8 * a + 2 * t + h;
+      if (tok < p.M) {
+        const uint16_t* res = p.residual ? p.residual + (long long)tok * p.ldr + col : nullptr;
+        const uint16_t o0 = f32_to_bits(epilogue_value(acc[a][0][h], bv[0], p.act, res, odt), odt);
+        const uint16_t o1 = f32_to_bits(epilogue_value(acc[a][0][2 + h], bv[1], p.act, res ? res + 1 : res, odt), odt);
+        const uint16_t o2 = f32_to_bits(epilogue_value(acc[a][1][h], bv[2], p.act, res ? res + 2 : res, odt), odt);
+        const uint16_t o3 = f32_to_bits(epilogue_value(acc[a][1][2 + h], bv[3], p.act, res ? res + 3 : res, odt), odt);
+        uint16_t* dst = p.out + (long long)tok * p.ldc + col;
+        *reinterpret_cast<uint2*>(dst) = make_uint2(pack2(o0, o1), pack2(o2, o3));
+      }
+    }
 }
 
 template <bool BF16, bool HAS_LO, int MT, int DEPTH>
@@ -190,69 +268,147 @@ __global__ void __launch_bounds__(kGemvThreads) gptq_gemv_kernel(const GemvParam
         for (int c = 0; c < 4; ++c) acc[a][b][c] += red[wn][lane][a * 8 + b * 4 + c];
   }
 
-  // fragment -> (token, 4 columns): token 8*a + 2t + h has columns col..col+3 =
-  // {acc[a][0][h], acc[a][0][2+h], acc[a][1][h], acc[a][1][2+h]}
-  if (p.splits > 1) {
-    if (wk == 0 && col < p.N) {
+  gemv_finish<BF16, MT>(p, acc, wk, col, t, tile, split, &is_last);
+}
+
+// ------------------------------------------------------------------------------------------
+// Factored GEMV for uniform groups spanning whole 32-k steps (gs % 32 == 0, no word table):
+// the tensor cores multiply the raw magic-biased codes (M + q) -- exact in bf16/fp16 -- and
+// the scale/zero are applied once per group to fp32 sums:
+//     sum_k x_k s (q_k - z) = s * sum_k x_k (M + q_k)  -  s (M + z) * sum_k x_k
+// sum_k x_k comes from a second MMA against an all-ones A fragment, already in the layout
+// of the accumulators. Per weight this leaves only the nibble extraction (lop3 + shift) on
+// the CUDA cores; the result is the exact-weight product evaluated in fp32 (it does not
+// round the weights to 16 bits first). Warps take contiguous K ranges so a group's steps
+// are accumulated together before its correction.
+template <bool BF16, int MT, int DEPTH>
+__global__ void __launch_bounds__(kGemvThreads) gptq_gemv_fact_kernel(const GemvParams p) {
+  using P = Pair<BF16>;
+  __shared__ float red[kGemvWarpsN][32][MT * 8];
+  __shared__ int is_last;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int wn = warp % kGemvWarpsN, wk = warp / kGemvWarpsN;
+  const int g = lane >> 2, t = lane & 3;
+  const int tile = blockIdx.x, split = blockIdx.y;
+  const int col = tile * kGemvCols + wn * 32 + 4 * g;
+  const int total_steps = (p.Kp + 31) / 32;
+  const int step0 = split * p.kstep_per_split;
+  const int step1 = min(total_steps, step0 + p.kstep_per_split);
+  const int half = (step1 - step0 + kGemvWarpsK - 1) / kGemvWarpsK;
+  const int ws0 = step0 + wk * half;
+  const int ws1 = min(step1, ws0 + half);
+  const int steps_per_group = p.gs / 32;
+  const uint32_t ones = BF16 ? 0x3F803F80u : 0x3C003C00u;
+  const uint32_t ones4[4] = {ones, ones, ones, ones};
+
+  float acc[MT][2][4], cg[MT][2][4], xo[MT][4];
 #pragma unroll
-      for (int a = 0; a < MT; ++a)
+  for (int a = 0; a < MT; ++a) {
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int tok = 8 * a + 2 * t + h;
-          if (tok < p.M) {
-            const float4 v = make_float4(acc[a][0][h], acc[a][0][2 + h], acc[a][1][h], acc[a][1][2 + h]);
-            *reinterpret_cast<float4*>(p.ws + ((long long)split * p.M + tok) * p.N + col) = v;
-          }
-        }
-    }
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      const unsigned prev = atomicAdd(p.tickets + tile, 1u);
-      is_last = (prev == (unsigned)(p.splits - 1));
-    }
-    __syncthreads();
-    if (!is_last) return;
-    __threadfence();
-    if (wk == 0 && col < p.N) {
+    for (int b = 0; b < 2; ++b)
 #pragma unroll
-      for (int a = 0; a < MT; ++a)
+      for (int c = 0; c < 4; ++c) acc[a][b][c] = cg[a][b][c] = 0.f;
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int tok = 8 * a + 2 * t + h;
-          if (tok < p.M) {
-            float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int sp = 0; sp < p.splits; ++sp) {
-              const float4 v = __ldcg(reinterpret_cast<const float4*>(p.ws + ((long long)sp * p.M + tok) * p.N + col));
-              sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
-            }
-            acc[a][0][h] = sum.x; acc[a][0][2 + h] = sum.y; acc[a][1][h] = sum.z; acc[a][1][2 + h] = sum.w;
-          }
-        }
-    }
-    if (threadIdx.x == 0) p.tickets[tile] = 0u;  // re-arm for the next launch (stream order)
+    for (int c = 0; c < 4; ++c) xo[a][c] = 0.f;
   }
-  if (wk != 0 || col >= p.N) return;
-  float bv[4] = {0.f, 0.f, 0.f, 0.f};
-  if (p.bias) {
+  float sj[4] = {0.f, 0.f, 0.f, 0.f}, czj[4] = {0.f, 0.f, 0.f, 0.f};
+  int cur_grp = -1;
+
+  auto flush = [&]() {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) bv[j] = load_as_f32(p.bias, p.bias_dtype, col + j);
+    for (int a = 0; a < MT; ++a) {
+#pragma unroll
+      for (int b = 0; b < 2; ++b)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int j = 2 * b + (c >> 1);
+          acc[a][b][c] += sj[j] * cg[a][b][c] - czj[j] * xo[a][c & 1];
+          cg[a][b][c] = 0.f;
+        }
+#pragma unroll
+      for (int c = 0; c < 4; ++c) xo[a][c] = 0.f;
+    }
+  };
+
+  GemvStage buf[DEPTH];
+#pragma unroll
+  for (int d = 0; d < DEPTH; ++d) {
+    const int s = ws0 + d;
+    gemv_load<MT>(buf[d], p, s < ws1 ? 4 * s + t : 0x7fffffff, col, g);
   }
-  const int odt = BF16 ? kBF16 : kF16;
+  for (int base = ws0; base < ws1; base += DEPTH) {
 #pragma unroll
-  for (int a = 0; a < MT; ++a)
+    for (int d = 0; d < DEPTH; ++d) {
+      const int s = base + d;
+      if (s < ws1) {  // warp-uniform
+        const int grp = s / steps_per_group;
+        if (grp != cur_grp) {  // warp-uniform: a 32-k step lies inside one group
+          if (cur_grp >= 0) flush();
+          const uint32_t sw4[4] = {buf[d].s.x & 0xFFFFu, buf[d].s.x >> 16, buf[d].s.y & 0xFFFFu, buf[d].s.y >> 16};
+          const int zsh = 4 * (col & 7);
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int tok = 8 * a + 2 * t + h;
-      if (tok < p.M) {
-        const uint16_t o0 = f32_to_bits(acc[a][0][h] + bv[0], odt);
-        const uint16_t o1 = f32_to_bits(acc[a][0][2 + h] + bv[1], odt);
-        const uint16_t o2 = f32_to_bits(acc[a][1][h] + bv[2], odt);
-        const uint16_t o3 = f32_to_bits(acc[a][1][2 + h] + bv[3], odt);
-        uint16_t* dst = p.out + (long long)tok * p.ldc + col;
-        *reinterpret_cast<uint2*>(dst) = make_uint2(pack2(o0, o1), pack2(o2, o3));
+          for (int j = 0; j < 4; ++j) {
+            uint32_t z = (buf[d].z >> (zsh + 4 * j)) & 0xFu;
+            if (p.v1) z = (z + 1u) & 0xFu;
+            const float sv = (p.s_dtype == kF16) ? __half2float(__ushort_as_half((uint16_t)sw4[j]))
+                                                 : __bfloat162float(__ushort_as_bfloat16((uint16_t)sw4[j]));
+            sj[j] = sv;
+            czj[j] = sv * (P::kMagicF + (float)z);   // exact: <= 19 significant bits
+          }
+          cur_grp = grp;
+        }
+        const uint32_t wv[4] = {buf[d].w.x, buf[d].w.y, buf[d].w.z, buf[d].w.w};
+        uint32_t pr[4][4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          pr[j][0] = lop3_and_or(wv[j], 0x000F000Fu, P::kMagic);
+          pr[j][1] = lop3_and_or(wv[j] >> 4, 0x000F000Fu, P::kMagic);
+          pr[j][2] = lop3_and_or(wv[j] >> 8, 0x000F000Fu, P::kMagic);
+          pr[j][3] = lop3_and_or(wv[j] >> 12, 0x000F000Fu, P::kMagic);
+        }
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+          const uint4 xv = (mt == 0) ? buf[d].xa : buf[d].xb;
+          const uint32_t b00 = prmt(xv.x, xv.z, 0x5410u);
+          const uint32_t b01 = prmt(xv.x, xv.z, 0x7632u);
+          const uint32_t b10 = prmt(xv.y, xv.w, 0x5410u);
+          const uint32_t b11 = prmt(xv.y, xv.w, 0x7632u);
+#pragma unroll
+          for (int beta = 0; beta < 2; ++beta) {
+            const uint32_t a0[4] = {pr[2 * beta][0], pr[2 * beta + 1][0], pr[2 * beta][1], pr[2 * beta + 1][1]};
+            const uint32_t a1[4] = {pr[2 * beta][2], pr[2 * beta + 1][2], pr[2 * beta][3], pr[2 * beta + 1][3]};
+            mma_16816<BF16>(cg[mt][beta], a0, b00, b01);
+            mma_16816<BF16>(cg[mt][beta], a1, b10, b11);
+          }
+          mma_16816<BF16>(xo[mt], ones4, b00, b01);
+          mma_16816<BF16>(xo[mt], ones4, b10, b11);
+        }
       }
+      const int sn = s + DEPTH;
+      gemv_load<MT>(buf[d], p, sn < ws1 ? 4 * sn + t : 0x7fffffff, col, g);
     }
+  }
+  if (cur_grp >= 0) flush();
+
+  // ---- reduction across the K warps, split-K, epilogue (same as gptq_gemv_kernel)
+  if (wk == 1) {
+#pragma unroll
+    for (int a = 0; a < MT; ++a)
+#pragma unroll
+      for (int b = 0; b < 2; ++b)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) red[wn][lane][a * 8 + b * 4 + c] = acc[a][b][c];
+  }
+  __syncthreads();
+  if (wk == 0) {
+#pragma unroll
+    for (int a = 0; a < MT; ++a)
+#pragma unroll
+      for (int b = 0; b < 2; ++b)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[a][b][c] += red[wn][lane][a * 8 + b * 4 + c];
+  }
+  gemv_finish<BF16, MT>(p, acc, wk, col, t, tile, split, &is_last);
 }
 
 }  // namespace oc

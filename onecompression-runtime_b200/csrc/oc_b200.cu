@@ -419,6 +419,13 @@ namespace {
 template <bool BF16, bool HAS_LO>
 int launch_gemv(const oc::GemvParams& p, int n_tiles, int splits, cudaStream_t stream) {
   dim3 grid(n_tiles, splits);
+  if (!p.wgrp && p.gs % 32 == 0) {  // whole groups per 32-k step: factored scaling
+    if (p.M <= 8)
+      oc::gptq_gemv_fact_kernel<BF16, 1, 6><<<grid, oc::kGemvThreads, 0, stream>>>(p);
+    else
+      oc::gptq_gemv_fact_kernel<BF16, 2, 3><<<grid, oc::kGemvThreads, 0, stream>>>(p);
+    return launch_check("gptq_gemv_fact");
+  }
   if (p.M <= 8)
     oc::gptq_gemv_kernel<BF16, HAS_LO, 1, 4><<<grid, oc::kGemvThreads, 0, stream>>>(p);
   else
@@ -446,16 +453,17 @@ int launch_tc_t(const CUtensorMap& tx, const oc_b200_layer* L, const oc::TcParam
 template <bool BF16, bool HAS_LO>
 int launch_tc(int bt, const CUtensorMap& tx, const oc_b200_layer* L, const oc::TcParams& p, int dev,
               cudaStream_t stream) {
-  if (bt == 128) return launch_tc_t<BF16, HAS_LO, 128, 2, 6, 8, 8>(tx, L, p, dev, stream);
-  if (bt == 256) return launch_tc_t<BF16, HAS_LO, 256, 1, 4, 8, 4>(tx, L, p, dev, stream);
-  return launch_tc_t<BF16, HAS_LO, 192, 2, 5, 8, 4>(tx, L, p, dev, stream);
+  if (bt == 128) return launch_tc_t<BF16, HAS_LO, 128, 2, 10, 8, 8>(tx, L, p, dev, stream);
+  if (bt == 256) return launch_tc_t<BF16, HAS_LO, 256, 1, 5, 8, 4>(tx, L, p, dev, stream);
+  return launch_tc_t<BF16, HAS_LO, 192, 2, 7, 8, 4>(tx, L, p, dev, stream);
 }
 
 }  // namespace
 
-extern "C" int oc_b200_gptq_gemm(const oc_b200_layer* L, const void* a, int a_dtype, int64_t M, int64_t lda, const void* bias,
-                      int bias_dtype, void* c, int64_t ldc, void* workspace, size_t workspace_bytes,
-                      oc_stream_t stream_) {
+extern "C" int oc_b200_gptq_gemm_ex(const oc_b200_layer* L, const void* a, int a_dtype, int64_t M, int64_t lda,
+                                    const void* bias, int bias_dtype, const void* residual, int64_t ldr, int act,
+                                    void* c, int64_t ldc, void* workspace, size_t workspace_bytes,
+                                    oc_stream_t stream_) {
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   if (!L) return fail(OC_ERR_INVALID, "gptq_gemm: layer is NULL");
   if (L->kind != 0) return fail(OC_ERR_INVALID, "gptq_gemm: not an AutoGPTQ layer");
@@ -469,6 +477,8 @@ extern "C" int oc_b200_gptq_gemm(const oc_b200_layer* L, const void* a, int a_dt
   if (ldc < L->N || ldc % 4 != 0 || !aligned(c, 8))
     return fail(OC_ERR_INVALID, "gptq_gemm: C must be 8-byte aligned with ldc %% 4 == 0 (ldc=%lld)", (long long)ldc);
   if (M > 0x7fffffffLL) return fail(OC_ERR_INVALID, "gptq_gemm: M too large");
+  if (act != oc::kActNone && act != oc::kActGeluTanh) return fail(OC_ERR_INVALID, "gptq_gemm: act=%d", act);
+  if (residual && ldr < L->N) return fail(OC_ERR_INVALID, "gptq_gemm: residual ldr=%lld", (long long)ldr);
   int dev = 0;
   if (int rc = current_device(&dev)) return rc;
   if (dev != L->device) return fail(OC_ERR_INVALID, "gptq_gemm: layer lives on device %d, current is %d", L->device, dev);
@@ -510,6 +520,9 @@ extern "C" int oc_b200_gptq_gemm(const oc_b200_layer* L, const void* a, int a_dt
     p.v1 = L->v1;
     p.bias = bias;
     p.bias_dtype = bias_dtype;
+    p.residual = reinterpret_cast<const uint16_t*>(residual);
+    p.ldr = ldr;
+    p.act = act;
     p.out = reinterpret_cast<uint16_t*>(c);
     p.ldc = ldc;
     p.ws = gp.splits > 1 ? reinterpret_cast<float*>(ws + off) : nullptr;
@@ -545,6 +558,9 @@ extern "C" int oc_b200_gptq_gemm(const oc_b200_layer* L, const void* a, int a_dt
   p.sz_rows = L->sz_rows;
   p.bias = bias;
   p.bias_dtype = bias_dtype;
+  p.residual = reinterpret_cast<const uint16_t*>(residual);
+  p.ldr = ldr;
+  p.act = act;
   p.out = reinterpret_cast<uint16_t*>(c);
   p.ldc = ldc;
   p.n_tiles_n = (L->N + oc::kTcBN - 1) / oc::kTcBN;
@@ -730,8 +746,8 @@ int launch_rows_t(const CUtensorMap& tx, const oc::RowsParams& p, int dev, cudaS
 
 template <bool BF16, int WB, int MODE, bool HL>
 int launch_rows_bt(int bt, const CUtensorMap& tx, const oc::RowsParams& p, int dev, cudaStream_t stream) {
-  if (bt == 128) return launch_rows_t<BF16, WB, MODE, HL, 128, 2, 6, 8, 8>(tx, p, dev, stream);
-  return launch_rows_t<BF16, WB, MODE, HL, 192, 2, 5, 8, 4>(tx, p, dev, stream);
+  if (bt == 128) return launch_rows_t<BF16, WB, MODE, HL, 128, 2, 10, 8, 8>(tx, p, dev, stream);
+  return launch_rows_t<BF16, WB, MODE, HL, 192, 2, 7, 8, 4>(tx, p, dev, stream);
 }
 
 template <bool BF16>
@@ -795,4 +811,11 @@ extern "C" int oc_b200_rows_gemm(const oc_b200_layer* L, const void* a, int a_dt
   const bool has_lo = L->s_dtype_r != a_dtype;
   if (bf16) return launch_rows<true>(bt, L->wbits, L->mode, has_lo, tx, p, dev, stream);
   return launch_rows<false>(bt, L->wbits, L->mode, has_lo, tx, p, dev, stream);
+}
+
+extern "C" int oc_b200_gptq_gemm(const oc_b200_layer* L, const void* a, int a_dtype, int64_t M, int64_t lda,
+                                 const void* bias, int bias_dtype, void* c, int64_t ldc, void* workspace,
+                                 size_t workspace_bytes, oc_stream_t stream) {
+  return oc_b200_gptq_gemm_ex(L, a, a_dtype, M, lda, bias, bias_dtype, nullptr, 0, oc::kActNone, c, ldc, workspace,
+                              workspace_bytes, stream);
 }

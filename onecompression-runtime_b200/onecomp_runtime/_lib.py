@@ -21,6 +21,8 @@ DT = {torch.float16: 0, torch.bfloat16: 1, torch.float32: 2}
 OPT_GEMM_PATH = 1
 OPT_TC_TILE = 2
 OPT_GEMV_CTAS = 3
+ACT_NONE = 0
+ACT_GELU_TANH = 1
 
 _lock = threading.Lock()
 _lib = None
@@ -49,6 +51,7 @@ _SIGNATURES = {
     "oc_b200_layer_destroy": ([_p], _i),
     "oc_b200_gptq_gemm_workspace": ([_p, _i64], _sz),
     "oc_b200_gptq_gemm": ([_p, _p, _i, _i64, _i64, _p, _i, _p, _i64, _p, _sz, _p], _i),
+    "oc_b200_gptq_gemm_ex": ([_p, _p, _i, _i64, _i64, _p, _i, _p, _i64, _i, _p, _i64, _p, _sz, _p], _i),
     "oc_b200_rows_table_bytes": ([_i], _sz),
     "oc_b200_rows_layer_create": ([_i, _p, _i64, _i, _p, _i, _p, _i, _i64, _i64, _i, _i, _i, _i, _p, _p,
                                    ctypes.POINTER(_p)], _i),

@@ -194,7 +194,8 @@ class B200GPTQLinear(torch.nn.Module):
     def __del__(self):
         self._release_handle()
 
-    def _gemm_2d(self, a_2d: torch.Tensor, out: torch.Tensor) -> None:
+    def _gemm_2d(self, a_2d: torch.Tensor, out: torch.Tensor, residual: torch.Tensor | None = None,
+                 act: int = 0) -> None:
         h = self._get_handle()
         M = a_2d.shape[0]
         dev = a_2d.device
@@ -202,11 +203,39 @@ class B200GPTQLinear(torch.nn.Module):
         need = lib.oc_b200_gptq_gemm_workspace(h, M)
         ws = _lib.workspace(dev, need)
         bias = self.bias
-        rc = lib.oc_b200_gptq_gemm(h, a_2d.data_ptr(), _lib.DT[a_2d.dtype], M, a_2d.stride(0),
-                                   None if bias is None else bias.data_ptr(),
-                                   _lib.DT[bias.dtype] if bias is not None else 0,
-                                   out.data_ptr(), out.stride(0), ws.data_ptr(), ws.numel(), _lib.stream_of(dev))
-        _lib.check(rc, "oc_b200_gptq_gemm")
+        rc = lib.oc_b200_gptq_gemm_ex(h, a_2d.data_ptr(), _lib.DT[a_2d.dtype], M, a_2d.stride(0),
+                                      None if bias is None else bias.data_ptr(),
+                                      _lib.DT[bias.dtype] if bias is not None else 0,
+                                      None if residual is None else residual.data_ptr(),
+                                      0 if residual is None else residual.stride(0), act,
+                                      out.data_ptr(), out.stride(0), ws.data_ptr(), ws.numel(), _lib.stream_of(dev))
+        _lib.check(rc, "oc_b200_gptq_gemm_ex")
+
+    _ACTS = {None: 0, "none": 0, "gelu_tanh": 1}
+
+    def forward_fused(self, x: torch.Tensor, residual: torch.Tensor | None = None,
+                      activation: str | None = None) -> torch.Tensor:
+        """``act(x @ W.T + bias) + residual`` with the activation and residual add in the
+        GEMM epilogue (one rounding). ``activation``: None or ``"gelu_tanh"``; ``residual``:
+        same shape and dtype as the output."""
+        if x.dtype not in (torch.float16, torch.bfloat16):
+            raise TypeError(f"forward_fused takes fp16/bf16 inputs, got {x.dtype}")
+        act = self._ACTS[activation]
+        lead = x.shape[:-1]
+        a_2d = x.reshape(-1, self.in_features)
+        if (a_2d.stride(1) != 1 or a_2d.data_ptr() % 16 != 0 or a_2d.stride(0) % 8 != 0
+                or a_2d.stride(0) < self.in_features):
+            a_2d = a_2d.contiguous()
+        M = a_2d.shape[0]
+        r2 = None
+        if residual is not None:
+            r2 = residual.reshape(M, self.out_features)
+            if r2.dtype != x.dtype or r2.stride(1) != 1:
+                raise ValueError("residual must match the output's dtype with unit column stride")
+        out = torch.empty((M, self.out_features), dtype=x.dtype, device=x.device)
+        if M:
+            self._gemm_2d(a_2d, out, r2, act)
+        return out.reshape(*lead, self.out_features)
 
     def _forward_impl(self, x: torch.Tensor, kind: str) -> torch.Tensor:
         if x.dtype == torch.float32:

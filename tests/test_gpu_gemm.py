@@ -198,3 +198,28 @@ def test_fused_int4_gemm_functional(cuda_device):
 def test_no_device_errors_recorded(cuda_device):
     from onecomp_runtime import _lib
     assert _lib.read_device_error(cuda_device) == 0
+
+
+@pytest.mark.parametrize("M", [3, 16, 300])
+@pytest.mark.parametrize("act", [None, "gelu_tanh"])
+@pytest.mark.parametrize("residual", [False, True])
+def test_fused_epilogue(cuda_device, M, act, residual):
+    """oc_b200_gptq_gemm_ex: act(x @ W.T + b) + residual computed in the GEMM epilogue
+    (GEMV for M <= 16, tcgen05 above) against the fp64 GEMM of the exact weight."""
+    from onecomp_runtime.testing import gptq_layer, activations
+    K, N = 1024, 384
+    t = {k: v.to(cuda_device) for k, v in gptq_layer(K, N, 32, seed=11 + M).items()}
+    layer = _module(t, K, N, 32, True, "fused", cuda_device)
+    x = activations(M, K, seed=M).to(cuda_device)
+    r = activations(M, N, seed=M + 1).to(cuda_device) if residual else None
+    y = layer.forward_fused(x, residual=r, activation=act)
+    ref = _gpu_reference(t, K, N, x, True, t["bias"])
+    if act == "gelu_tanh":
+        ref = torch.nn.functional.gelu(ref, approximate="tanh")
+    if r is not None:
+        ref = ref + r.double()
+    err = float((y.double() - ref).abs().max() / ref.abs().max())
+    assert y.dtype == x.dtype and y.shape == (M, N)
+    assert err < 1e-2, err
+    if act is None and r is None:
+        torch.testing.assert_close(y, layer(x), rtol=0, atol=0)
