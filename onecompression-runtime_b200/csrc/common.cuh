@@ -38,6 +38,7 @@ enum : unsigned {
   kDevErrWFull = 0x107,
   kDevErrWEmpty = 0x108,
   kDevErrDrain = 0x109,
+  kDevErrResFull = 0x10a,
   kDevErrSplitK = 0x201,
 };
 
@@ -65,10 +66,18 @@ __device__ __forceinline__ float bits_to_f32(uint16_t b, int dtype) {
 // GEMM epilogue activations
 enum Act : int { kActNone = 0, kActGeluTanh = 1 };
 
-// 0.5 v (1 + tanh(sqrt(2/pi) (v + 0.044715 v^3))) -- torch's approximate="tanh" GELU
+// tanh-approximated GELU, 0.5 v (1 + tanh(sqrt(2/pi) (v + 0.044715 v^3))), the formula of
+// torch.nn.functional.gelu(approximate="tanh"); tanh from the hardware approximation
+// (tanh.approx.f32, relative error ~2^-11, below the 2^-8 spacing of the 16-bit output).
+__device__ __forceinline__ float tanh_approx(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 __device__ __forceinline__ float gelu_tanh(float v) {
-  const float u = 0.7978845608028654f * (v + 0.044715f * v * v * v);
-  return 0.5f * v * (1.f + tanhf(u));
+  const float u = 0.7978845608028654f * fmaf(0.044715f * v, v * v, v);
+  const float h = 0.5f * v;
+  return fmaf(h, tanh_approx(u), h);
 }
 
 __device__ __forceinline__ float epilogue_value(float acc, float bias, int act, const uint16_t* residual,
@@ -245,6 +254,40 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
           smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
       : "memory");
+}
+
+// Tiled TMA store smem -> global (bulk-group completion). Coordinates are non-negative;
+// parts of the box outside the tensor are not written.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until every committed bulk store has finished reading its shared-memory source.
+__device__ __forceinline__ void bulk_wait_group_read0() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// Wait until every committed bulk store has completed.
+__device__ __forceinline__ void bulk_wait_group0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// Named barrier over `count` threads (a multiple of 32) of the CTA.
+__device__ __forceinline__ void named_bar_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+// Named barrier that also ORs a predicate over the participating threads.
+__device__ __forceinline__ bool named_bar_or(int id, int count, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id), "r"(count)
+      : "memory");
+  return r != 0;
 }
 
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {

@@ -46,10 +46,13 @@ struct TcParams {
   int act;                   // Act
   uint16_t* out;
   long long ldc;
+  int tma_epi;               // 1: output (and residual) tiles move by TMA through shared memory
   int n_tiles_n, n_tiles_m, num_tiles;
 };
 
-constexpr int kTcThreads = 512;
+constexpr int kTcDqGroups = 2;   // dequant warpgroups (k-block `it` goes to group it % kTcDqGroups)
+constexpr int kTcThreads = 128 * (2 + kTcDqGroups);
+constexpr int kTcEpiWarp0 = 4 + 4 * kTcDqGroups;
 constexpr int kTcBK = 64;            // k per pipeline stage (one 128-byte swizzle atom of 16-bit)
 constexpr int kTcBN = 128;           // output features per tile (= TMEM lanes = UMMA M)
 constexpr int kTcWBytes = 8 * kTcBN * 4;           // packed words of one stage
@@ -62,23 +65,26 @@ struct TcCfg {
   static constexpr int kAccCols = ACC_STAGES * BT;
   static constexpr int kACols = A_STAGES * (kTcBK / 2);
   static_assert(kAccCols + kACols <= 512, "TMEM budget");
-  static_assert(W_STAGES % 2 == 0 && A_STAGES % 2 == 0, "two dequant warpgroups alternate stages");
   static constexpr int kXStageBytes = BT * 128;
-  static constexpr int kSmemBytes = X_STAGES * kXStageBytes + W_STAGES * kTcWStageBytes + 1024 /*align*/ +
-                                    (2 * (X_STAGES + W_STAGES + A_STAGES + ACC_STAGES) + 2) * 8 + 64;
+  static constexpr int kEpiBytes = BT * kTcBN * 2;   // output / residual staging tile [BT tokens][128 features]
+  static constexpr int kSmemBytes = X_STAGES * kXStageBytes + W_STAGES * kTcWStageBytes + kEpiBytes +
+                                    1024 /*align*/ + (2 * (X_STAGES + W_STAGES + A_STAGES + ACC_STAGES) + 3) * 8 + 64;
+  static_assert(kSmemBytes <= 232448, "shared memory per CTA");
 };
 
 template <bool BF16, bool HAS_LO, int BT, int ACC_STAGES, int X_STAGES, int W_STAGES, int A_STAGES>
 __global__ void __launch_bounds__(kTcThreads, 1)
     gptq_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
                         const __grid_constant__ CUtensorMap tmap_s, const __grid_constant__ CUtensorMap tmap_z,
+                        const __grid_constant__ CUtensorMap tmap_c, const __grid_constant__ CUtensorMap tmap_r,
                         const TcParams p) {
   using Cfg = TcCfg<BT, ACC_STAGES, X_STAGES, W_STAGES, A_STAGES>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* x_smem = smem;
   uint8_t* w_smem = x_smem + X_STAGES * Cfg::kXStageBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(w_smem + W_STAGES * kTcWStageBytes);
+  uint8_t* epi_smem = w_smem + W_STAGES * kTcWStageBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(epi_smem + Cfg::kEpiBytes);
   uint64_t* full_x = bars;
   uint64_t* empty_x = full_x + X_STAGES;
   uint64_t* full_w = empty_x + X_STAGES;
@@ -88,7 +94,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint64_t* full_acc = empty_a + A_STAGES;
   uint64_t* empty_acc = full_acc + ACC_STAGES;
   uint64_t* drain = empty_acc + ACC_STAGES;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* res_full = drain + 1;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(res_full + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = warp_id(), lane = lane_id();
@@ -101,6 +108,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     for (int i = 0; i < A_STAGES; ++i) { mbar_init(&full_a[i], 128); mbar_init(&empty_a[i], 1); }
     for (int i = 0; i < ACC_STAGES; ++i) { mbar_init(&full_acc[i], 1); mbar_init(&empty_acc[i], 128); }
     mbar_init(drain, 1);
+    mbar_init(res_full, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -111,6 +119,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tma_prefetch_desc(&tmap_s);
       tma_prefetch_desc(&tmap_z);
     }
+    if (p.tma_epi) tma_prefetch_desc(&tmap_c);
+    if (p.tma_epi && p.residual) tma_prefetch_desc(&tmap_r);
   }
   if (warp == 1) {
     tmem_alloc(tmem_holder, 512);
@@ -209,10 +219,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         mbar_drain(drain, 0);
       }
     }
-  } else if (warp >= 4 && warp < 12) {
+  } else if (warp >= 4 && warp < kTcEpiWarp0) {
     // ------------------------------------------------------------ dequant warpgroups
     using Pp = Pair<BF16>;
-    const int wg = (warp - 4) >> 2;   // 0: even k-blocks, 1: odd k-blocks
+    const int wg = (warp - 4) >> 2;   // takes k-blocks it with it % kTcDqGroups == wg
     const int q4 = warp & 3;
     const int row = q4 * 32 + lane;   // TMEM lane == output feature within the tile
     const int kw_rows = p.Kp >> 3;
@@ -224,7 +234,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int nn = n < p.N ? n : 0;
       const int zsh = 4 * (nn & 7);
       for (int kb = 0; kb < KB; ++kb, ++it) {
-        if ((it & 1) != wg) continue;
+        if ((it % kTcDqGroups) != wg) continue;
         const int sw = it % W_STAGES, pw = (it / W_STAGES) & 1;
         const int sa = it % A_STAGES, pa = (it / A_STAGES) & 1;
         // per-word group constants
@@ -299,8 +309,73 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         mbar_arrive(&full_a[sa]);
       }
     }
-  } else if (warp >= 12) {
-    // ------------------------------------------------------------ epilogue warpgroup
+  } else if (warp >= kTcEpiWarp0 && p.tma_epi) {
+    // ------------------------------------------------------------ epilogue warpgroup, TMA path
+    // Per tile: the residual tile (if any) is TMA-loaded into the staging tile while the
+    // mainloop runs; each thread turns its feature's accumulators into
+    // act(acc + bias) + residual in place; one TMA store writes the tile (rows past M and
+    // features past N are clipped by the tensor map).
+    const int q4 = warp & 3;
+    const int row = q4 * 32 + lane;
+    const int et = threadIdx.x - kTcEpiWarp0 * 32;
+    const int odt = BF16 ? kBF16 : kF16;
+    uint16_t* epi = reinterpret_cast<uint16_t*>(epi_smem);
+    int tcount = 0;
+    uint32_t rphase = 0;
+    bool res_armed = false;
+    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++tcount) {
+      const int sc = tcount % ACC_STAGES, pc = (tcount / ACC_STAGES) & 1;
+      const int nb = tile % p.n_tiles_n, mb = tile / p.n_tiles_n;
+      const int n = nb * kTcBN + row;
+      const float bv = (p.bias && n < p.N) ? load_as_f32(p.bias, p.bias_dtype, n) : 0.f;
+      if (et == 0) {
+        bulk_wait_group_read0();  // the previous tile's store has read the staging tile
+        if (p.residual) {
+          mbar_arrive_expect_tx(res_full, Cfg::kEpiBytes);
+          tma_load_2d(epi, &tmap_r, res_full, nb * kTcBN, mb * BT);
+          res_armed = true;
+        }
+      }
+      named_bar_sync(1, 128);
+      bool ok = mbar_wait(&full_acc[sc], pc, abort_flag, kDevErrAccFull);
+      if (ok && p.residual) ok = mbar_wait(res_full, rphase, abort_flag, kDevErrResFull);
+      if (named_bar_or(1, 128, !ok)) break;  // all four warps leave together
+      if (p.residual) {
+        rphase ^= 1u;
+        res_armed = false;
+      }
+      tc_fence_after();
+      const uint32_t tbase = tmem_base + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(sc * BT);
+#pragma unroll 1
+      for (int c = 0; c < BT / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tbase + (uint32_t)(c * 32), v);
+        tc_wait_ld();
+        uint16_t* e = epi + (c * 32) * kTcBN + row;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          float o = __uint_as_float(v[i]) + bv;
+          if (p.act == kActGeluTanh) o = gelu_tanh(o);
+          if (p.residual) o += bits_to_f32(e[i * kTcBN], odt);
+          e[i * kTcBN] = f32_to_bits(o, odt);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&empty_acc[sc]);  // the accumulator is in registers/smem: the next tile may start
+      fence_proxy_async_shared();   // generic-proxy smem writes -> visible to the TMA store
+      named_bar_sync(1, 128);
+      if (et == 0) {
+        tma_store_2d(&tmap_c, epi, nb * kTcBN, mb * BT);
+        bulk_commit_group();
+      }
+    }
+    if (et == 0) {
+      bulk_wait_group0();
+      if (res_armed) mbar_drain(res_full, rphase);
+    }
+  } else if (warp >= kTcEpiWarp0) {
+    // ------------------------------------------------------------ epilogue warpgroup, direct stores
+    // (outputs or residuals whose layout a tensor map cannot describe)
     const int q4 = warp & 3;
     const int row = q4 * 32 + lane;
     const int odt = BF16 ? kBF16 : kF16;
@@ -328,13 +403,23 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             for (int i = 0; i < 32; ++i)
               if (m0 + i < p.M) dst[(long long)i * p.ldc] = f32_to_bits(__uint_as_float(v[i]) + bv, odt);
           } else {
-            const uint16_t* res = p.residual ? p.residual + (long long)m0 * p.ldr + n : nullptr;
+            // residual rows first: 32 independent loads in flight, then the math and stores
+            float rv[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) rv[i] = 0.f;
+            if (p.residual) {
+              const uint16_t* res = p.residual + (long long)m0 * p.ldr + n;
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                if (m0 + i < p.M) rv[i] = bits_to_f32(__ldg(res + (long long)i * p.ldr), odt);
+            }
 #pragma unroll
             for (int i = 0; i < 32; ++i)
-              if (m0 + i < p.M)
-                dst[(long long)i * p.ldc] = f32_to_bits(
-                    epilogue_value(__uint_as_float(v[i]), bv, p.act, res ? res + (long long)i * p.ldr : nullptr, odt),
-                    odt);
+              if (m0 + i < p.M) {
+                float o = __uint_as_float(v[i]) + bv;
+                if (p.act == kActGeluTanh) o = gelu_tanh(o);
+                dst[(long long)i * p.ldc] = f32_to_bits(o + rv[i], odt);
+              }
           }
         }
       }

@@ -392,6 +392,24 @@ GemvPlan gemv_plan(const oc_b200_layer* L, int dev) {
   return {splits, kstep};
 }
 
+// Tokens per tcgen05 tile when the caller leaves it to the library: the preset with the
+// least (waves of persistent CTAs) x (measured time of one tile at K = 3072 on B200, us).
+int choose_tile(int64_t M, int n_tiles_n, int sms) {
+  static const int kBt[3] = {256, 192, 128};
+  static const double kTileUs[3] = {29.0, 24.8, 23.4};
+  int best = 256;
+  double best_cost = 1e300;
+  for (int i = 0; i < 3; ++i) {
+    const int64_t tiles = (int64_t)n_tiles_n * ((M + kBt[i] - 1) / kBt[i]);
+    const double cost = (double)((tiles + sms - 1) / sms) * kTileUs[i];
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = kBt[i];
+    }
+  }
+  return best;
+}
+
 bool use_gemv(int64_t M) {
   const int path = g_opt_path.load();
   if (path == 1) return M <= 16;
@@ -433,8 +451,12 @@ int launch_gemv(const oc::GemvParams& p, int n_tiles, int splits, cudaStream_t s
   return launch_check("gptq_gemv");
 }
 
+struct TcMaps {
+  CUtensorMap x, c, r;
+};
+
 template <bool BF16, bool HAS_LO, int BT, int ACC, int XS, int WS, int AS>
-int launch_tc_t(const CUtensorMap& tx, const oc_b200_layer* L, const oc::TcParams& p, int dev, cudaStream_t stream) {
+int launch_tc_t(const TcMaps& tm, const oc_b200_layer* L, const oc::TcParams& p, int dev, cudaStream_t stream) {
   using Cfg = oc::TcCfg<BT, ACC, XS, WS, AS>;
   auto kern = oc::gptq_gemm_tc_kernel<BF16, HAS_LO, BT, ACC, XS, WS, AS>;
   static bool attr_set[kMaxDevices] = {};
@@ -446,16 +468,17 @@ int launch_tc_t(const CUtensorMap& tx, const oc_b200_layer* L, const oc::TcParam
     attr_set[dev] = true;
   }
   int grid = p.num_tiles < sm_count(dev) ? p.num_tiles : sm_count(dev);
-  kern<<<grid, oc::kTcThreads, Cfg::kSmemBytes, stream>>>(tx, L->tmap_w, L->tmap_s, L->tmap_z, p);
+  kern<<<grid, oc::kTcThreads, Cfg::kSmemBytes, stream>>>(tm.x, L->tmap_w, L->tmap_s, L->tmap_z, tm.c, tm.r, p);
   return launch_check("gptq_gemm_tc");
 }
 
+// Tile presets (tokens per tile, accumulators, activation / weight / TMEM-A stages), sized to
+// 512 TMEM columns and the 227 KB of shared memory with the epilogue staging tile.
 template <bool BF16, bool HAS_LO>
-int launch_tc(int bt, const CUtensorMap& tx, const oc_b200_layer* L, const oc::TcParams& p, int dev,
-              cudaStream_t stream) {
-  if (bt == 128) return launch_tc_t<BF16, HAS_LO, 128, 2, 10, 8, 8>(tx, L, p, dev, stream);
-  if (bt == 256) return launch_tc_t<BF16, HAS_LO, 256, 1, 5, 8, 4>(tx, L, p, dev, stream);
-  return launch_tc_t<BF16, HAS_LO, 192, 2, 7, 8, 4>(tx, L, p, dev, stream);
+int launch_tc(int bt, const TcMaps& tm, const oc_b200_layer* L, const oc::TcParams& p, int dev, cudaStream_t stream) {
+  if (bt == 128) return launch_tc_t<BF16, HAS_LO, 128, 2, 8, 8, 8>(tm, L, p, dev, stream);
+  if (bt == 256) return launch_tc_t<BF16, HAS_LO, 256, 1, 4, 6, 4>(tm, L, p, dev, stream);
+  return launch_tc_t<BF16, HAS_LO, 192, 2, 5, 8, 4>(tm, L, p, dev, stream);
 }
 
 }  // namespace
@@ -537,12 +560,28 @@ extern "C" int oc_b200_gptq_gemm_ex(const oc_b200_layer* L, const void* a, int a
   }
 
   int bt = g_opt_tile.load();
-  if (bt == 0) bt = 192;
-  CUtensorMap tx;
-  if (int rc = make_tmap_2d(&tx, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xk,
-                            (uint64_t)L->Kp, (uint64_t)M, (uint64_t)ldx * 2, oc::kTcBK, (uint32_t)bt,
-                            CU_TENSOR_MAP_SWIZZLE_128B))
+  if (bt == 0) bt = choose_tile(M, (L->N + oc::kTcBN - 1) / oc::kTcBN, sm_count(dev));
+  const CUtensorMapDataType tdt = bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  TcMaps tm;
+  std::memset(&tm, 0, sizeof(tm));
+  if (int rc = make_tmap_2d(&tm.x, tdt, 2, xk, (uint64_t)L->Kp, (uint64_t)M, (uint64_t)ldx * 2, oc::kTcBK,
+                            (uint32_t)bt, CU_TENSOR_MAP_SWIZZLE_128B))
     return rc;
+  // Output (and residual) tiles go through shared memory by TMA when a tensor map can
+  // describe them (16-byte aligned base, row pitch a multiple of 16 bytes); otherwise the
+  // epilogue stores directly.
+  const bool c_tma = aligned(c, 16) && ldc % 8 == 0;
+  const bool r_tma = !residual || (aligned(residual, 16) && ldr % 8 == 0);
+  const bool tma_epi = c_tma && r_tma;
+  if (tma_epi) {
+    if (int rc = make_tmap_2d(&tm.c, tdt, 2, c, (uint64_t)L->N, (uint64_t)M, (uint64_t)ldc * 2, oc::kTcBN,
+                              (uint32_t)bt, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return rc;
+    if (residual)
+      if (int rc = make_tmap_2d(&tm.r, tdt, 2, residual, (uint64_t)L->N, (uint64_t)M, (uint64_t)ldr * 2, oc::kTcBN,
+                                (uint32_t)bt, CU_TENSOR_MAP_SWIZZLE_NONE))
+        return rc;
+  }
   oc::TcParams p{};
   p.M = (int)M;
   p.N = L->N;
@@ -563,13 +602,14 @@ extern "C" int oc_b200_gptq_gemm_ex(const oc_b200_layer* L, const void* a, int a
   p.act = act;
   p.out = reinterpret_cast<uint16_t*>(c);
   p.ldc = ldc;
+  p.tma_epi = tma_epi ? 1 : 0;
   p.n_tiles_n = (L->N + oc::kTcBN - 1) / oc::kTcBN;
   p.n_tiles_m = (int)((M + bt - 1) / bt);
   p.num_tiles = p.n_tiles_n * p.n_tiles_m;
-  if (bf16) return has_lo ? launch_tc<true, true>(bt, tx, L, p, dev, stream)
-                          : launch_tc<true, false>(bt, tx, L, p, dev, stream);
-  return has_lo ? launch_tc<false, true>(bt, tx, L, p, dev, stream)
-                : launch_tc<false, false>(bt, tx, L, p, dev, stream);
+  if (bf16) return has_lo ? launch_tc<true, true>(bt, tm, L, p, dev, stream)
+                          : launch_tc<true, false>(bt, tm, L, p, dev, stream);
+  return has_lo ? launch_tc<false, true>(bt, tm, L, p, dev, stream)
+                : launch_tc<false, false>(bt, tm, L, p, dev, stream);
 }
 
 

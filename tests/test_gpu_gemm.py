@@ -202,16 +202,21 @@ def test_no_device_errors_recorded(cuda_device):
 
 @pytest.mark.parametrize("M", [3, 16, 300])
 @pytest.mark.parametrize("act", [None, "gelu_tanh"])
-@pytest.mark.parametrize("residual", [False, True])
+@pytest.mark.parametrize("residual", ["none", "dense", "strided"])
 def test_fused_epilogue(cuda_device, M, act, residual):
     """oc_b200_gptq_gemm_ex: act(x @ W.T + b) + residual computed in the GEMM epilogue
-    (GEMV for M <= 16, tcgen05 above) against the fp64 GEMM of the exact weight."""
+    (GEMV for M <= 16, tcgen05 above) against the fp64 GEMM of the exact weight. A residual
+    whose row pitch is not a multiple of 8 elements takes the direct-store epilogue."""
     from onecomp_runtime.testing import gptq_layer, activations
     K, N = 1024, 384
     t = {k: v.to(cuda_device) for k, v in gptq_layer(K, N, 32, seed=11 + M).items()}
     layer = _module(t, K, N, 32, True, "fused", cuda_device)
     x = activations(M, K, seed=M).to(cuda_device)
-    r = activations(M, N, seed=M + 1).to(cuda_device) if residual else None
+    r = None
+    if residual == "dense":
+        r = activations(M, N, seed=M + 1).to(cuda_device)
+    elif residual == "strided":
+        r = activations(M, N + 4, seed=M + 1).to(cuda_device)[:, :N]
     y = layer.forward_fused(x, residual=r, activation=act)
     ref = _gpu_reference(t, K, N, x, True, t["bias"])
     if act == "gelu_tanh":
