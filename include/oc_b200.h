@@ -131,6 +131,22 @@ enum { OC_ACT_NONE = 0, OC_ACT_GELU_TANH = 1 };
 int oc_b200_gptq_gemm_ex(const oc_b200_layer* layer, const void* a, int a_dtype, int64_t M, int64_t lda,
                          const void* bias, int bias_dtype, const void* residual, int64_t ldr, int act, void* c,
                          int64_t ldc, void* workspace, size_t workspace_bytes, oc_stream_t stream);
+/* No counterpart in the reference. The decode GEMV of oc_b200_gptq_gemm (1 <= M <= 16, same
+ * kernels, same result) for callers that cannot allocate device memory at call time (a host
+ * whose allocator is out of reach of the FFI, or a runtime that forbids allocation after
+ * start-up): instead of a caller workspace it uses a fixed scratch array of
+ * OC_B200_NOALLOC_SCRATCH_BYTES built into this library, one per device, for the gathered
+ * activations of act-order layers, the split-K partial sums and the per-column tickets.
+ *   - The first call on a device sets the scratch up (looks up its address, zeroes the
+ *     tickets, waits for the device); make that first call before any stream capture.
+ *   - Calls needing more scratch than that (large M * N with many splits, or a large act-order
+ *     gather) fail with OC_ERR_INVALID and a message giving the bytes needed; M > 16 fails too.
+ *   - Calls on one device share the scratch: two calls that overlap in time (different
+ *     streams, or host threads without ordering) race and give wrong results. Order them on
+ *     one stream. */
+#define OC_B200_NOALLOC_SCRATCH_BYTES (8u << 20)
+int oc_b200_gptq_gemv_noalloc(const oc_b200_layer* layer, const void* a, int a_dtype, int64_t M, int64_t lda,
+                              const void* bias, int bias_dtype, void* c, int64_t ldc, oc_stream_t stream);
 
 /* ---- row-packed int4/int2 linears: RTN nibble layers, DSV4 layers, expert groups ---- */
 /* Device bytes the caller provides (256-byte aligned) to describe E row-packed matrices. */

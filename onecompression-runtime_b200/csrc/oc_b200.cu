@@ -853,6 +853,115 @@ extern "C" int oc_b200_rows_gemm(const oc_b200_layer* L, const void* a, int a_dt
   return launch_rows<false>(bt, L->wbits, L->mode, has_lo, tx, p, dev, stream);
 }
 
+// ---------------------------------------------------------------- decode GEMV without a workspace
+// For callers that cannot allocate device memory when they call (see oc_b200_gptq_gemv_noalloc
+// in the header): the split-K partials, the act-order gather and the column tickets live in
+// this fixed array instead of a caller workspace. The tickets (first kTicketBytes) must be
+// zero before the first launch; the one-time setup zeroes them and every launch leaves them
+// zero again. One array per device (a __device__ variable exists once per device context),
+// so concurrent calls on one device race on it.
+namespace {
+constexpr size_t kNoAllocScratchBytes = OC_B200_NOALLOC_SCRATCH_BYTES;
+__device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+std::atomic<void*> g_noalloc_ptr[kMaxDevices];
+
+// Address of this device's scratch (the device must be current); the first call per device
+// looks it up, zeroes the tickets and waits for the device, so it belongs before any capture.
+int noalloc_scratch(int dev, uint8_t** out) {
+  if (dev < 0 || dev >= kMaxDevices) return fail(OC_ERR_INVALID, "gemv_noalloc: device %d out of range", dev);
+  void* ptr = g_noalloc_ptr[dev].load(std::memory_order_acquire);
+  if (!ptr) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    ptr = g_noalloc_ptr[dev].load(std::memory_order_relaxed);
+    if (!ptr) {
+      if (int rc = cuda_check(cudaGetSymbolAddress(&ptr, g_noalloc_scratch), "cudaGetSymbolAddress(noalloc scratch)"))
+        return rc;
+      if (int rc = cuda_check(cudaMemset(ptr, 0, kTicketBytes), "cudaMemset(noalloc tickets)")) return rc;
+      if (int rc = cuda_check(cudaDeviceSynchronize(), "cudaDeviceSynchronize(noalloc setup)")) return rc;
+      g_noalloc_ptr[dev].store(ptr, std::memory_order_release);
+    }
+  }
+  *out = reinterpret_cast<uint8_t*>(ptr);
+  return OC_OK;
+}
+}  // namespace
+
+extern "C" int oc_b200_gptq_gemv_noalloc(const oc_b200_layer* L, const void* a, int a_dtype, int64_t M, int64_t lda,
+                                         const void* bias, int bias_dtype, void* c, int64_t ldc,
+                                         oc_stream_t stream_) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  if (!L) return fail(OC_ERR_INVALID, "gemv_noalloc: layer is NULL");
+  if (L->kind != 0) return fail(OC_ERR_INVALID, "gemv_noalloc: not an AutoGPTQ layer");
+  if (M < 0 || M > 16) return fail(OC_ERR_INVALID, "gemv_noalloc: M=%lld (takes 0 <= M <= 16)", (long long)M);
+  if (M == 0) return OC_OK;
+  if (!a || !c) return fail(OC_ERR_INVALID, "gemv_noalloc: NULL activation/output");
+  if (!dt16(a_dtype)) return fail(OC_ERR_INVALID, "gemv_noalloc: activations must be f16 or bf16");
+  if (bias && !dtf(bias_dtype)) return fail(OC_ERR_INVALID, "gemv_noalloc: bias dtype");
+  if (lda < L->K_in || lda % 8 != 0 || !aligned(a, 16))
+    return fail(OC_ERR_INVALID, "gemv_noalloc: A must be 16-byte aligned with lda %% 8 == 0 (lda=%lld)",
+                (long long)lda);
+  if (ldc < L->N || ldc % 4 != 0 || !aligned(c, 8))
+    return fail(OC_ERR_INVALID, "gemv_noalloc: C must be 8-byte aligned with ldc %% 4 == 0 (ldc=%lld)",
+                (long long)ldc);
+  int dev = 0;
+  if (int rc = current_device(&dev)) return rc;
+  if (dev != L->device)
+    return fail(OC_ERR_INVALID, "gemv_noalloc: layer lives on device %d, current is %d", L->device, dev);
+  const GemvPlan gp = gemv_plan(L, dev);
+  size_t need = kTicketBytes;
+  const size_t gather_bytes = L->kperm ? align_up((size_t)M * L->Kp * 2, 256) : 0;
+  need += gather_bytes;
+  if (gp.splits > 1) need += align_up((size_t)gp.splits * M * L->N * 4, 256);
+  if (need > kNoAllocScratchBytes)
+    return fail(OC_ERR_INVALID, "gemv_noalloc: needs %zu bytes of scratch, the fixed scratch holds %zu (M=%lld N=%d)",
+                need, kNoAllocScratchBytes, (long long)M, L->N);
+  uint8_t* ws = nullptr;
+  if (int rc = noalloc_scratch(dev, &ws)) return rc;
+  unsigned* tickets = reinterpret_cast<unsigned*>(ws);
+  size_t off = kTicketBytes;
+  const uint16_t* xk = reinterpret_cast<const uint16_t*>(a);
+  int64_t ldx = lda;
+  if (L->kperm) {
+    uint16_t* xg = reinterpret_cast<uint16_t*>(ws + off);
+    off += gather_bytes;
+    if (int rc = oc_b200_permute_cols(a, lda, M, L->K_in, L->kperm, L->Kp, xg, stream_)) return rc;
+    xk = xg;
+    ldx = L->Kp;
+  }
+  oc::GemvParams p{};
+  p.x = xk;
+  p.ldx = ldx;
+  p.M = (int)M;
+  p.qw = L->qw;
+  p.qz = L->qz;
+  p.s = L->s;
+  p.s_dtype = L->s_dtype;
+  p.wgrp = L->wgrp;
+  p.Kp = L->Kp;
+  p.N = L->N;
+  p.G = L->G;
+  p.gs = L->gs;
+  p.v1 = L->v1;
+  p.bias = bias;
+  p.bias_dtype = bias_dtype;
+  p.residual = nullptr;
+  p.ldr = 0;
+  p.act = oc::kActNone;
+  p.out = reinterpret_cast<uint16_t*>(c);
+  p.ldc = ldc;
+  p.ws = gp.splits > 1 ? reinterpret_cast<float*>(ws + off) : nullptr;
+  p.tickets = tickets;
+  p.splits = gp.splits;
+  p.kstep_per_split = gp.kstep;
+  const int n_tiles = (L->N + oc::kGemvCols - 1) / oc::kGemvCols;
+  const bool bf16 = a_dtype == OC_DT_BF16;
+  const bool has_lo = L->s_dtype != a_dtype;
+  if (bf16) return has_lo ? launch_gemv<true, true>(p, n_tiles, gp.splits, stream)
+                          : launch_gemv<true, false>(p, n_tiles, gp.splits, stream);
+  return has_lo ? launch_gemv<false, true>(p, n_tiles, gp.splits, stream)
+                : launch_gemv<false, false>(p, n_tiles, gp.splits, stream);
+}
+
 extern "C" int oc_b200_gptq_gemm(const oc_b200_layer* L, const void* a, int a_dtype, int64_t M, int64_t lda,
                                  const void* bias, int bias_dtype, void* c, int64_t ldc, void* workspace,
                                  size_t workspace_bytes, oc_stream_t stream) {

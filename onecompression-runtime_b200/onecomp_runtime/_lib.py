@@ -52,6 +52,7 @@ _SIGNATURES = {
     "oc_b200_gptq_gemm_workspace": ([_p, _i64], _sz),
     "oc_b200_gptq_gemm": ([_p, _p, _i, _i64, _i64, _p, _i, _p, _i64, _p, _sz, _p], _i),
     "oc_b200_gptq_gemm_ex": ([_p, _p, _i, _i64, _i64, _p, _i, _p, _i64, _i, _p, _i64, _p, _sz, _p], _i),
+    "oc_b200_gptq_gemv_noalloc": ([_p, _p, _i, _i64, _i64, _p, _i, _p, _i64, _p], _i),
     "oc_b200_rows_table_bytes": ([_i], _sz),
     "oc_b200_rows_layer_create": ([_i, _p, _i64, _i, _p, _i, _p, _i, _i64, _i64, _i, _i, _i, _i, _p, _p,
                                    ctypes.POINTER(_p)], _i),
