@@ -155,6 +155,10 @@ __global__ void gptq_repack_k_kernel(const uint32_t* __restrict__ qw, const int3
 // --- activation gather: x'[m, k'] = x[m, kperm[k']] (0 for -1) --------------------------
 __global__ void permute_cols_kernel(const uint16_t* __restrict__ x, long long ldx, int M, int K,
                                     const int32_t* __restrict__ kperm, int Kp, uint16_t* __restrict__ out) {
+  // Launched with programmatic stream serialization: let the next kernel (the GEMV, which
+  // prefetches its weights meanwhile) launch, and wait for the kernel that produced x.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const long long total = (long long)M * Kp;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {

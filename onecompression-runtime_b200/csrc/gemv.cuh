@@ -69,84 +69,95 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4],
   }
 }
 
-struct GemvStage {
-  uint4 w;        // 4 words: columns 4g..4g+3 at word row kw
-  uint4 xa;       // x[token g][8kw .. 8kw+7]
-  uint4 xb;       // x[token g+8][...] (MT == 2)
-  uint2 s;        // 4 scales (16-bit each)
-  uint32_t z;     // packed zero word
-  int valid;
+// ---- per-warp cp.async ring --------------------------------------------------------------
+// Each warp streams its K range through a ring of kGemvDepth<MT> shared-memory slots filled
+// with cp.async (16-byte weight vectors straight to shared memory, no register staging), so a
+// warp keeps up to depth x 512 bytes of packed weights in flight. Every lane reads back only
+// the bytes it loaded itself, so a lane's own cp.async.wait_group is the only synchronisation.
+// Slot layout (structure of arrays, conflict-free 16/8/4-byte lane accesses):
+//   w[32] uint4 | x[MT][32] uint4 | s[32] uint2 | z[32] uint32
+template <int MT> struct GemvRing {
+  static constexpr int kDepth = MT == 1 ? 8 : 6;
+  static constexpr int kSlotBytes = 32 * 16 + MT * 32 * 16 + 32 * 8 + 32 * 4;
+  static constexpr int kWarpBytes = kDepth * kSlotBytes;
+  static constexpr int kSmemBytes = kGemvThreads / 32 * kWarpBytes;
 };
 
-// Every lane of a warp must execute the same mma.sync, so out-of-range lanes are not
-// skipped: a k-word past K loads zero activations (its B rows contribute nothing), a
-// column past N loads zero weights/scales (its A rows feed only discarded outputs) but
-// still loads the activations, because a lane's B fragment feeds every row of the tile.
-template <int MT>
-__device__ __forceinline__ void gemv_load(GemvStage& st, const GemvParams& p, int kw, int col, int g) {
-  const int kw_rows = p.Kp >> 3;
-  const bool kvalid = kw < kw_rows;
-  st.valid = kvalid && (col < p.N);
-  st.w = make_uint4(0, 0, 0, 0);
-  st.xa = make_uint4(0, 0, 0, 0);
-  st.xb = make_uint4(0, 0, 0, 0);
-  st.s = make_uint2(0, 0);
-  st.z = 0;
-  if (!kvalid) return;
-  if (g < p.M) st.xa = __ldg(reinterpret_cast<const uint4*>(p.x + (long long)g * p.ldx + 8 * kw));
-  if (MT == 2 && g + 8 < p.M) st.xb = __ldg(reinterpret_cast<const uint4*>(p.x + (long long)(g + 8) * p.ldx + 8 * kw));
-  if (!st.valid) return;
-  st.w = __ldg(reinterpret_cast<const uint4*>(p.qw + (long long)kw * p.N + col));
-  const int grp = p.wgrp ? __ldg(p.wgrp + kw) : (8 * kw) / p.gs;
-  st.s = __ldg(reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(p.s) + (long long)grp * p.N + col));
-  st.z = __ldg(p.qz + (long long)grp * (p.N >> 3) + (col >> 3));
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async8(void* dst, const void* src, bool valid) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(valid ? 8 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* dst, const void* src, bool valid) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(valid ? 4 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N> __device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-template <bool BF16, bool HAS_LO, int MT>
-__device__ __forceinline__ void gemv_compute(const GemvStage& st, const GemvParams& p, int col,
-                                             float (&acc)[MT][2][4]) {
-  using P = Pair<BF16>;
-  const int zsh = 4 * (col & 7);
-  uint32_t pr[4][4];  // [column j][pair: (k0,k4) (k1,k5) (k2,k6) (k3,k7)]
-  const uint32_t sw[4] = {st.s.x & 0xFFFFu, st.s.x >> 16, st.s.y & 0xFFFFu, st.s.y >> 16};
-  const uint32_t wv[4] = {st.w.x, st.w.y, st.w.z, st.w.w};
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    uint32_t z = (st.z >> (zsh + 4 * j)) & 0xFu;
-    if (p.v1) z = (z + 1u) & 0xFu;
-    const float s = (p.s_dtype == kF16) ? __half2float(__ushort_as_half((uint16_t)sw[j]))
-                                        : __bfloat162float(__ushort_as_bfloat16((uint16_t)sw[j]));
-    const DqConst<BF16> c = make_dq_const<BF16>(s, (int)z);
-    const uint32_t w = wv[j];
-    pr[j][0] = dq_pair<BF16, HAS_LO>(lop3_and_or(w, 0x000F000Fu, P::kMagic), c);
-    pr[j][1] = dq_pair<BF16, HAS_LO>(lop3_and_or(w >> 4, 0x000F000Fu, P::kMagic), c);
-    pr[j][2] = dq_pair<BF16, HAS_LO>(lop3_and_or(w >> 8, 0x000F000Fu, P::kMagic), c);
-    pr[j][3] = dq_pair<BF16, HAS_LO>(lop3_and_or(w >> 12, 0x000F000Fu, P::kMagic), c);
-  }
-  // B fragments: natural x (x0x1, x2x3, x4x5, x6x7) -> (x0x4, x1x5) and (x2x6, x3x7)
+// Issue the loads of 32-k step `s` (word kw = 4s + t of this lane) into ring slot `slot`.
+// Out-of-range words/columns are zero-filled; a column past N still loads the activations,
+// because every lane's B fragment feeds every row of the tile. Scales/zeros are loaded only
+// when `need_sz` (a group starts at this step, or per-word groups).
+template <int MT>
+__device__ __forceinline__ void gemv_issue(uint8_t* slot, const GemvParams& p, int s, int step1, int col, int g, int t,
+                                           int lane, bool need_sz) {
+  const int kw = 4 * s + t;
+  const bool kvalid = s < step1 && kw < (p.Kp >> 3);
+  const bool valid = kvalid && col < p.N;
+  const int kwc = kvalid ? kw : 0;
+  const int colc = col < p.N ? col : 0;
+  cp_async16(slot + lane * 16, p.qw + (long long)kwc * p.N + colc, valid);
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt) {
-    const uint4 xv = (mt == 0) ? st.xa : st.xb;
-    const uint32_t b00 = prmt(xv.x, xv.z, 0x5410u);  // (x0, x4)
-    const uint32_t b01 = prmt(xv.x, xv.z, 0x7632u);  // (x1, x5)
-    const uint32_t b10 = prmt(xv.y, xv.w, 0x5410u);  // (x2, x6)
-    const uint32_t b11 = prmt(xv.y, xv.w, 0x7632u);  // (x3, x7)
-#pragma unroll
-    for (int beta = 0; beta < 2; ++beta) {
-      const uint32_t a0[4] = {pr[2 * beta][0], pr[2 * beta + 1][0], pr[2 * beta][1], pr[2 * beta + 1][1]};
-      const uint32_t a1[4] = {pr[2 * beta][2], pr[2 * beta + 1][2], pr[2 * beta][3], pr[2 * beta + 1][3]};
-      mma_16816<BF16>(acc[mt][beta], a0, b00, b01);
-      mma_16816<BF16>(acc[mt][beta], a1, b10, b11);
-    }
+    const int tok = g + 8 * mt;
+    if (tok < p.M) cp_async16(slot + 512 + mt * 512 + lane * 16, p.x + (long long)tok * p.ldx + 8 * kwc, kvalid);
   }
+  if (need_sz) {
+    const int grp = valid ? (p.wgrp ? __ldg(p.wgrp + kw) : (8 * kw) / p.gs) : 0;
+    cp_async8(slot + 512 + MT * 512 + lane * 8,
+              reinterpret_cast<const uint16_t*>(p.s) + (long long)grp * p.N + colc, valid);
+    cp_async4(slot + 512 + MT * 512 + 256 + lane * 4, p.qz + (long long)grp * (p.N >> 3) + (colc >> 3), valid);
+  }
+}
+
+template <int MT>
+__device__ __forceinline__ void gemv_read_x(const uint8_t* slot, const GemvParams& p, int g, int lane,
+                                            uint4 (&xv)[MT]) {
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt)
+    xv[mt] = (g + 8 * mt < p.M) ? *reinterpret_cast<const uint4*>(slot + 512 + mt * 512 + lane * 16)
+                                : make_uint4(0, 0, 0, 0);
+}
+
+// B fragments: natural x (x0x1, x2x3, x4x5, x6x7) -> (x0x4, x1x5) and (x2x6, x3x7)
+__device__ __forceinline__ void x_frags(const uint4& xv, uint32_t& b00, uint32_t& b01, uint32_t& b10, uint32_t& b11) {
+  b00 = prmt(xv.x, xv.z, 0x5410u);
+  b01 = prmt(xv.x, xv.z, 0x7632u);
+  b10 = prmt(xv.y, xv.w, 0x5410u);
+  b11 = prmt(xv.y, xv.w, 0x7632u);
 }
 
 // Split-K partials (deterministic last-CTA reduction), bias, rounding, store.
 // fragment -> (token, 4 columns): token 8*a + 2t + h has columns col..col+3 =
 // {acc[a][0][h], acc[a][0][2+h], acc[a][1][h], acc[a][1][2+h]}
+// bar_threads = 0: the whole CTA takes part (__syncthreads); otherwise the first bar_threads
+// threads do, synchronised on named barrier 2 (kernels whose producer warp has left).
+__device__ __forceinline__ void gemv_bar(int bar_threads) {
+  if (bar_threads == 0)
+    __syncthreads();
+  else
+    named_bar_sync(2, bar_threads);
+}
+
 template <bool BF16, int MT>
-__device__ __forceinline__ void gemv_finish(const GemvParams& p, float (&acc)[MT][2][4], int wk, int col, int t,
-                                            int tile, int split, int* is_last) {
+__device__ __forceinline__ void gemv_finish_n(const GemvParams& p, float (&acc)[MT][2][4], int wk, int col, int t,
+                                              int tile, int split, int* is_last, int bar_threads) {
   if (p.splits > 1) {
     if (wk == 0 && col < p.N) {
 #pragma unroll
@@ -161,12 +172,12 @@ __device__ __forceinline__ void gemv_finish(const GemvParams& p, float (&acc)[MT
         }
     }
     __threadfence();
-    __syncthreads();
+    gemv_bar(bar_threads);
     if (threadIdx.x == 0) {
       const unsigned prev = atomicAdd(p.tickets + tile, 1u);
       *is_last = (prev == (unsigned)(p.splits - 1));
     }
-    __syncthreads();
+    gemv_bar(bar_threads);
     if (!*is_last) return;
     __threadfence();
     if (wk == 0 && col < p.N) {
@@ -211,8 +222,19 @@ __device__ __forceinline__ void gemv_finish(const GemvParams& p, float (&acc)[MT
     }
 }
 
-template <bool BF16, bool HAS_LO, int MT, int DEPTH>
+// Exact-weight GEMV (any group structure, incl. per-word group tables): every weight is
+// dequantized to RNE(s (q - z)) in the activation type before the MMA.
+template <bool BF16, int MT>
+__device__ __forceinline__ void gemv_finish(const GemvParams& p, float (&acc)[MT][2][4], int wk, int col, int t,
+                                            int tile, int split, int* is_last) {
+  gemv_finish_n<BF16, MT>(p, acc, wk, col, t, tile, split, is_last, 0);
+}
+
+template <bool BF16, bool HAS_LO, int MT>
 __global__ void __launch_bounds__(kGemvThreads) gptq_gemv_kernel(const GemvParams p) {
+  using P = Pair<BF16>;
+  using Ring = GemvRing<MT>;
+  extern __shared__ __align__(128) uint8_t gemv_smem[];
   __shared__ float red[kGemvWarpsN][32][MT * 8];
   __shared__ int is_last;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -223,6 +245,10 @@ __global__ void __launch_bounds__(kGemvThreads) gptq_gemv_kernel(const GemvParam
   const int total_steps = (p.Kp + 31) / 32;
   const int step0 = split * p.kstep_per_split;
   const int step1 = min(total_steps, step0 + p.kstep_per_split);
+  const int half = (step1 - step0 + kGemvWarpsK - 1) / kGemvWarpsK;
+  const int ws0 = step0 + wk * half;
+  const int ws1 = min(step1, ws0 + half);
+  uint8_t* ring = gemv_smem + warp * Ring::kWarpBytes;
 
   float acc[MT][2][4];
 #pragma unroll
@@ -232,22 +258,54 @@ __global__ void __launch_bounds__(kGemvThreads) gptq_gemv_kernel(const GemvParam
 #pragma unroll
       for (int c = 0; c < 4; ++c) acc[a][b][c] = 0.f;
 
-  // this warp's steps: step0 + wk, step0 + wk + kGemvWarpsK, ...
-  GemvStage buf[DEPTH];
 #pragma unroll
-  for (int d = 0; d < DEPTH; ++d) {
-    const int s = step0 + wk + d * kGemvWarpsK;
-    gemv_load<MT>(buf[d], p, s < step1 ? 4 * s + t : 0x7fffffff, col, g);
+  for (int d = 0; d < Ring::kDepth; ++d) {
+    gemv_issue<MT>(ring + d * Ring::kSlotBytes, p, ws0 + d, ws1, col, g, t, lane, true);
+    cp_async_commit();
   }
-  for (int base = step0 + wk; base < step1; base += DEPTH * kGemvWarpsK) {
+  const int zsh = 4 * (col & 7);
+  int slot_i = 0;
+  for (int s = ws0; s < ws1; ++s) {
+    cp_async_wait<Ring::kDepth - 1>();
+    uint8_t* slot = ring + slot_i * Ring::kSlotBytes;
+    const uint4 w = *reinterpret_cast<const uint4*>(slot + lane * 16);
+    const uint2 sv = *reinterpret_cast<const uint2*>(slot + 512 + MT * 512 + lane * 8);
+    const uint32_t zw = *reinterpret_cast<const uint32_t*>(slot + 512 + MT * 512 + 256 + lane * 4);
+    uint4 xv[MT];
+    gemv_read_x<MT>(slot, p, g, lane, xv);
+    gemv_issue<MT>(slot, p, s + Ring::kDepth, ws1, col, g, t, lane, true);
+    cp_async_commit();
+    if (++slot_i == Ring::kDepth) slot_i = 0;
+
+    uint32_t pr[4][4];  // [column j][pair: (k0,k4) (k1,k5) (k2,k6) (k3,k7)]
+    const uint32_t sw[4] = {sv.x & 0xFFFFu, sv.x >> 16, sv.y & 0xFFFFu, sv.y >> 16};
+    const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-    for (int d = 0; d < DEPTH; ++d) {
-      const int s = base + d * kGemvWarpsK;
-      if (s < step1) gemv_compute<BF16, HAS_LO, MT>(buf[d], p, col, acc);
-      const int sn = s + DEPTH * kGemvWarpsK;
-      gemv_load<MT>(buf[d], p, sn < step1 ? 4 * sn + t : 0x7fffffff, col, g);
+    for (int j = 0; j < 4; ++j) {
+      uint32_t z = (zw >> (zsh + 4 * j)) & 0xFu;
+      if (p.v1) z = (z + 1u) & 0xFu;
+      const float sc = (p.s_dtype == kF16) ? __half2float(__ushort_as_half((uint16_t)sw[j]))
+                                           : __bfloat162float(__ushort_as_bfloat16((uint16_t)sw[j]));
+      const DqConst<BF16> c = make_dq_const<BF16>(sc, (int)z);
+      pr[j][0] = dq_pair<BF16, HAS_LO>(lop3_and_or(wv[j], 0x000F000Fu, P::kMagic), c);
+      pr[j][1] = dq_pair<BF16, HAS_LO>(lop3_and_or(wv[j] >> 4, 0x000F000Fu, P::kMagic), c);
+      pr[j][2] = dq_pair<BF16, HAS_LO>(lop3_and_or(wv[j] >> 8, 0x000F000Fu, P::kMagic), c);
+      pr[j][3] = dq_pair<BF16, HAS_LO>(lop3_and_or(wv[j] >> 12, 0x000F000Fu, P::kMagic), c);
+    }
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+      uint32_t b00, b01, b10, b11;
+      x_frags(xv[mt], b00, b01, b10, b11);
+#pragma unroll
+      for (int beta = 0; beta < 2; ++beta) {
+        const uint32_t a0[4] = {pr[2 * beta][0], pr[2 * beta + 1][0], pr[2 * beta][1], pr[2 * beta + 1][1]};
+        const uint32_t a1[4] = {pr[2 * beta][2], pr[2 * beta + 1][2], pr[2 * beta][3], pr[2 * beta + 1][3]};
+        mma_16816<BF16>(acc[mt][beta], a0, b00, b01);
+        mma_16816<BF16>(acc[mt][beta], a1, b10, b11);
+      }
     }
   }
+  cp_async_wait<0>();
 
   // reduce the K-warps of this CTA
   if (wk == 1) {
@@ -267,7 +325,6 @@ __global__ void __launch_bounds__(kGemvThreads) gptq_gemv_kernel(const GemvParam
 #pragma unroll
         for (int c = 0; c < 4; ++c) acc[a][b][c] += red[wn][lane][a * 8 + b * 4 + c];
   }
-
   gemv_finish<BF16, MT>(p, acc, wk, col, t, tile, split, &is_last);
 }
 
@@ -280,10 +337,12 @@ __global__ void __launch_bounds__(kGemvThreads) gptq_gemv_kernel(const GemvParam
 // of the accumulators. Per weight this leaves only the nibble extraction (lop3 + shift) on
 // the CUDA cores; the result is the exact-weight product evaluated in fp32 (it does not
 // round the weights to 16 bits first). Warps take contiguous K ranges so a group's steps
-// are accumulated together before its correction.
-template <bool BF16, int MT, int DEPTH>
+// are accumulated together before its correction; scales/zeros are fetched once per group.
+template <bool BF16, int MT>
 __global__ void __launch_bounds__(kGemvThreads) gptq_gemv_fact_kernel(const GemvParams p) {
   using P = Pair<BF16>;
+  using Ring = GemvRing<MT>;
+  extern __shared__ __align__(128) uint8_t gemv_smem[];
   __shared__ float red[kGemvWarpsN][32][MT * 8];
   __shared__ int is_last;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -297,9 +356,48 @@ __global__ void __launch_bounds__(kGemvThreads) gptq_gemv_fact_kernel(const Gemv
   const int half = (step1 - step0 + kGemvWarpsK - 1) / kGemvWarpsK;
   const int ws0 = step0 + wk * half;
   const int ws1 = min(step1, ws0 + half);
-  const int steps_per_group = p.gs / 32;
+  const int spg = p.gs / 32;  // steps per group
+  uint8_t* ring = gemv_smem + warp * Ring::kWarpBytes;
   const uint32_t ones = BF16 ? 0x3F803F80u : 0x3C003C00u;
   const uint32_t ones4[4] = {ones, ones, ones, ones};
+
+  // Load-side cursors (step `si`, D steps ahead of the math): running pointers instead of
+  // per-step index arithmetic; a group countdown instead of divisions.
+  const bool cvalid = col < p.N;
+  const int colc = cvalid ? col : 0;
+  const int kw_rows = p.Kp >> 3;
+  const long long wstride = 4LL * p.N;  // one 32-k step of qweight rows
+  const uint32_t* wp = p.qw + (long long)(4 * ws0 + t) * p.N + colc;
+  const uint16_t* xp[MT];
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt) xp[mt] = p.x + (long long)min(g + 8 * mt, p.M - 1) * p.ldx + 8 * (4 * ws0 + t);
+  int grp_i = ws0 / spg;
+  int left_i = spg - (ws0 - grp_i * spg);  // steps of the current group left, counting si
+  const uint16_t* sp = reinterpret_cast<const uint16_t*>(p.s) + (long long)grp_i * p.N + colc;
+  const uint32_t* zp = p.qz + (long long)grp_i * (p.N >> 3) + (colc >> 3);
+  int si = ws0;
+  auto issue = [&](uint8_t* slot, bool need_sz) {
+    const bool kvalid = si < ws1 && 4 * si + t < kw_rows;
+    cp_async16(slot + lane * 16, kvalid ? (const void*)wp : (const void*)p.qw, kvalid && cvalid);
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+      if (g + 8 * mt < p.M) cp_async16(slot + 512 + mt * 512 + lane * 16, kvalid ? (const void*)xp[mt] : (const void*)p.x, kvalid);
+    if (need_sz) {
+      const bool v = kvalid && cvalid;
+      cp_async8(slot + 512 + MT * 512 + lane * 8, v ? (const void*)sp : p.s, v);
+      cp_async4(slot + 512 + MT * 512 + 256 + lane * 4, v ? (const void*)zp : (const void*)p.qz, v);
+    }
+    cp_async_commit();
+    ++si;
+    wp += wstride;
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) xp[mt] += 32;
+    if (--left_i == 0) {
+      left_i = spg;
+      sp += p.N;
+      zp += p.N >> 3;
+    }
+  };
 
   float acc[MT][2][4], cg[MT][2][4], xo[MT][4];
 #pragma unroll
@@ -312,7 +410,6 @@ __global__ void __launch_bounds__(kGemvThreads) gptq_gemv_fact_kernel(const Gemv
     for (int c = 0; c < 4; ++c) xo[a][c] = 0.f;
   }
   float sj[4] = {0.f, 0.f, 0.f, 0.f}, czj[4] = {0.f, 0.f, 0.f, 0.f};
-  int cur_grp = -1;
 
   auto flush = [&]() {
 #pragma unroll
@@ -330,65 +427,64 @@ __global__ void __launch_bounds__(kGemvThreads) gptq_gemv_fact_kernel(const Gemv
     }
   };
 
-  GemvStage buf[DEPTH];
 #pragma unroll
-  for (int d = 0; d < DEPTH; ++d) {
-    const int s = ws0 + d;
-    gemv_load<MT>(buf[d], p, s < ws1 ? 4 * s + t : 0x7fffffff, col, g);
-  }
-  for (int base = ws0; base < ws1; base += DEPTH) {
+  for (int d = 0; d < Ring::kDepth; ++d) issue(ring + d * Ring::kSlotBytes, d == 0 || left_i == spg);
+  const int zsh = 4 * (col & 7);
+  int slot_i = 0;
+  int left_c = spg - (ws0 - (ws0 / spg) * spg);  // math side: steps left in the current group
+  bool first = true;
+  for (int s = ws0; s < ws1; ++s) {
+    cp_async_wait<Ring::kDepth - 1>();
+    uint8_t* slot = ring + slot_i * Ring::kSlotBytes;
+    const uint4 w = *reinterpret_cast<const uint4*>(slot + lane * 16);
+    uint4 xv[MT];
+    gemv_read_x<MT>(slot, p, g, lane, xv);
+    if (first || left_c == spg) {  // warp-uniform: a group starts (or the range does)
+      if (!first) flush();
+      first = false;
+      const uint2 sv = *reinterpret_cast<const uint2*>(slot + 512 + MT * 512 + lane * 8);
+      const uint32_t zw = *reinterpret_cast<const uint32_t*>(slot + 512 + MT * 512 + 256 + lane * 4);
+      const uint32_t sw4[4] = {sv.x & 0xFFFFu, sv.x >> 16, sv.y & 0xFFFFu, sv.y >> 16};
 #pragma unroll
-    for (int d = 0; d < DEPTH; ++d) {
-      const int s = base + d;
-      if (s < ws1) {  // warp-uniform
-        const int grp = s / steps_per_group;
-        if (grp != cur_grp) {  // warp-uniform: a 32-k step lies inside one group
-          if (cur_grp >= 0) flush();
-          const uint32_t sw4[4] = {buf[d].s.x & 0xFFFFu, buf[d].s.x >> 16, buf[d].s.y & 0xFFFFu, buf[d].s.y >> 16};
-          const int zsh = 4 * (col & 7);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            uint32_t z = (buf[d].z >> (zsh + 4 * j)) & 0xFu;
-            if (p.v1) z = (z + 1u) & 0xFu;
-            const float sv = (p.s_dtype == kF16) ? __half2float(__ushort_as_half((uint16_t)sw4[j]))
-                                                 : __bfloat162float(__ushort_as_bfloat16((uint16_t)sw4[j]));
-            sj[j] = sv;
-            czj[j] = sv * (P::kMagicF + (float)z);   // exact: <= 19 significant bits
-          }
-          cur_grp = grp;
-        }
-        const uint32_t wv[4] = {buf[d].w.x, buf[d].w.y, buf[d].w.z, buf[d].w.w};
-        uint32_t pr[4][4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          pr[j][0] = lop3_and_or(wv[j], 0x000F000Fu, P::kMagic);
-          pr[j][1] = lop3_and_or(wv[j] >> 4, 0x000F000Fu, P::kMagic);
-          pr[j][2] = lop3_and_or(wv[j] >> 8, 0x000F000Fu, P::kMagic);
-          pr[j][3] = lop3_and_or(wv[j] >> 12, 0x000F000Fu, P::kMagic);
-        }
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt) {
-          const uint4 xv = (mt == 0) ? buf[d].xa : buf[d].xb;
-          const uint32_t b00 = prmt(xv.x, xv.z, 0x5410u);
-          const uint32_t b01 = prmt(xv.x, xv.z, 0x7632u);
-          const uint32_t b10 = prmt(xv.y, xv.w, 0x5410u);
-          const uint32_t b11 = prmt(xv.y, xv.w, 0x7632u);
-#pragma unroll
-          for (int beta = 0; beta < 2; ++beta) {
-            const uint32_t a0[4] = {pr[2 * beta][0], pr[2 * beta + 1][0], pr[2 * beta][1], pr[2 * beta + 1][1]};
-            const uint32_t a1[4] = {pr[2 * beta][2], pr[2 * beta + 1][2], pr[2 * beta][3], pr[2 * beta + 1][3]};
-            mma_16816<BF16>(cg[mt][beta], a0, b00, b01);
-            mma_16816<BF16>(cg[mt][beta], a1, b10, b11);
-          }
-          mma_16816<BF16>(xo[mt], ones4, b00, b01);
-          mma_16816<BF16>(xo[mt], ones4, b10, b11);
-        }
+      for (int j = 0; j < 4; ++j) {
+        uint32_t z = (zw >> (zsh + 4 * j)) & 0xFu;
+        if (p.v1) z = (z + 1u) & 0xFu;
+        const float sc = (p.s_dtype == kF16) ? __half2float(__ushort_as_half((uint16_t)sw4[j]))
+                                             : __bfloat162float(__ushort_as_bfloat16((uint16_t)sw4[j]));
+        sj[j] = sc;
+        czj[j] = sc * (P::kMagicF + (float)z);  // exact: <= 19 significant bits
       }
-      const int sn = s + DEPTH;
-      gemv_load<MT>(buf[d], p, sn < ws1 ? 4 * sn + t : 0x7fffffff, col, g);
+    }
+    if (--left_c == 0) left_c = spg;
+    issue(slot, left_i == spg);
+    if (++slot_i == Ring::kDepth) slot_i = 0;
+
+    const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+    uint32_t pr[4][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      pr[j][0] = lop3_and_or(wv[j], 0x000F000Fu, P::kMagic);
+      pr[j][1] = lop3_and_or(wv[j] >> 4, 0x000F000Fu, P::kMagic);
+      pr[j][2] = lop3_and_or(wv[j] >> 8, 0x000F000Fu, P::kMagic);
+      pr[j][3] = lop3_and_or(wv[j] >> 12, 0x000F000Fu, P::kMagic);
+    }
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+      uint32_t b00, b01, b10, b11;
+      x_frags(xv[mt], b00, b01, b10, b11);
+#pragma unroll
+      for (int beta = 0; beta < 2; ++beta) {
+        const uint32_t a0[4] = {pr[2 * beta][0], pr[2 * beta + 1][0], pr[2 * beta][1], pr[2 * beta + 1][1]};
+        const uint32_t a1[4] = {pr[2 * beta][2], pr[2 * beta + 1][2], pr[2 * beta][3], pr[2 * beta + 1][3]};
+        mma_16816<BF16>(cg[mt][beta], a0, b00, b01);
+        mma_16816<BF16>(cg[mt][beta], a1, b10, b11);
+      }
+      mma_16816<BF16>(xo[mt], ones4, b00, b01);
+      mma_16816<BF16>(xo[mt], ones4, b10, b11);
     }
   }
-  if (cur_grp >= 0) flush();
+  if (!first) flush();
+  cp_async_wait<0>();
 
   // ---- reduction across the K warps, split-K, epilogue (same as gptq_gemv_kernel)
   if (wk == 1) {

@@ -1,0 +1,284 @@
+// Decode-sized (M <= 16) factored GEMV fed by TMA, for uniform groups of 32, 64 or a multiple
+// of 128 rows (every GPTQ layout of configs 0-2). Same arithmetic as gptq_gemv_fact_kernel
+// (gemv.cuh): the tensor cores multiply raw magic-biased codes (M + q) by the activations and
+// each group's scale / zero is applied once to the fp32 sums.
+//
+// Why a separate kernel: with per-lane cp.async the decode GEMV is issue-bound (address and
+// ring bookkeeping per 16-byte vector). Here one producer lane moves a whole 128-k block of a
+// 128-column tile per stage with five TMA copies (four 32-column weight slabs with the 128-byte
+// swizzle, the block's scale and zero rows, the activation rows), and the eight consumer warps
+// only read shared memory, extract nibbles and issue MMAs.
+//
+// Launch overlap: the kernel is launched with programmatic stream serialization. Every CTA lets
+// the next kernel in the stream launch at once (griddepcontrol.launch_dependents), and the
+// producer streams the first stages of weights, which no earlier kernel writes, before it waits
+// for the previous kernel (griddepcontrol.wait); activations and every global write (split-K
+// partials, tickets, output) come after that wait.
+//
+// CTA: 8 consumer warps (4 column warps x 2 k halves; warp (wn, kh) takes steps 2kh, 2kh+1 of
+// each 4-step stage) + 1 producer warp. Split-K over CTAs as in gemv.cuh (deterministic
+// last-CTA reduction). Every mbarrier wait is bounded; on timeout the kernel records an error
+// code, drains its own copies and skips its writes.
+#pragma once
+
+#include "common.cuh"
+#include "gemv.cuh"
+
+namespace oc {
+
+constexpr int kGtConsumerWarps = 8;
+constexpr int kGtThreads = 32 * (kGtConsumerWarps + 1);
+constexpr int kGtBK = 128;  // k per stage: 16 word rows, 4 MMA steps of 32 k
+
+template <int MT>
+struct GtCfg {
+  static constexpr int kDepth = MT == 1 ? 8 : 6;
+  static constexpr int kWBytes = 4 * 16 * 128;          // four [16 rows][32 words] slabs, 128B-swizzled
+  static constexpr int kSBytes = 4 * kGemvCols * 2;     // up to 4 scale rows (groups of 32)
+  static constexpr int kZBytes = 4 * (kGemvCols / 8) * 4;
+  static constexpr int kXBytes = 8 * MT * kGtBK * 2;    // [8 MT tokens][128 k]
+  static constexpr int kWOff = 0;
+  static constexpr int kSOff = kDepth * kWBytes;
+  static constexpr int kZOff = kSOff + kDepth * kSBytes;
+  static constexpr int kXOff = kZOff + kDepth * kZBytes;
+  static constexpr int kBarOff = kXOff + kDepth * kXBytes;
+  static constexpr int kSmemBytes = kBarOff + 2 * kDepth * 8 + 16 + 1024 /*align*/;
+};
+
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+struct GtParams {
+  GemvParams g;
+  int rows_sz;        // scale/zero rows per stage: 4 (gs 32), 2 (gs 64), 1 (gs multiple of 128)
+  int stages_per_grp; // stages per group when gs >= 128 (else 1)
+  int kb_per_split;   // stages per split
+};
+
+template <bool BF16, int MT>
+__global__ void __launch_bounds__(kGtThreads, 2)
+    gptq_gemv_tma_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_s,
+                         const __grid_constant__ CUtensorMap tmap_z, const __grid_constant__ CUtensorMap tmap_x,
+                         const GtParams gp) {
+  using P = Pair<BF16>;
+  using Cfg = GtCfg<MT>;
+  const GemvParams& p = gp.g;
+  extern __shared__ __align__(1024) uint8_t gt_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gt_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::kBarOff);
+  uint64_t* empty = full + Cfg::kDepth;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + Cfg::kDepth);
+  __shared__ float red[kGemvWarpsN][32][MT * 8];
+  __shared__ int is_last;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = blockIdx.x, split = blockIdx.y;
+  const int KB = (p.Kp + kGtBK - 1) / kGtBK;
+  const int kb0 = split * gp.kb_per_split;
+  const int kb1 = min(KB, kb0 + gp.kb_per_split);
+  const int nst = kb1 - kb0;
+  const int col0 = tile * kGemvCols;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < Cfg::kDepth; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kGtConsumerWarps);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  griddep_launch_dependents();
+
+  if (warp == kGtConsumerWarps) {
+    // ------------------------------------------------------------------ producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmap_w);
+      tma_prefetch_desc(&tmap_s);
+      tma_prefetch_desc(&tmap_z);
+      tma_prefetch_desc(&tmap_x);
+      const uint32_t bytes = Cfg::kWBytes + gp.rows_sz * (kGemvCols * 2 + (kGemvCols / 8) * 4) + Cfg::kXBytes;
+      int armed[Cfg::kDepth];
+      for (int i = 0; i < Cfg::kDepth; ++i) armed[i] = -1;
+      auto load_wsz = [&](int i) {
+        const int s = i % Cfg::kDepth;
+        const int kb = kb0 + i;
+        mbar_arrive_expect_tx(&full[s], bytes);
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          tma_load_2d(smem + Cfg::kWOff + s * Cfg::kWBytes + c * 2048, &tmap_w, &full[s], col0 + 32 * c, kb * 16);
+        const int g0 = (kb * kGtBK) / p.gs;
+        tma_load_2d(smem + Cfg::kSOff + s * Cfg::kSBytes, &tmap_s, &full[s], col0, g0);
+        tma_load_2d(smem + Cfg::kZOff + s * Cfg::kZBytes, &tmap_z, &full[s], col0 / 8, g0);
+        armed[s] = (i / Cfg::kDepth) & 1;
+      };
+      auto load_x = [&](int i) {
+        const int s = i % Cfg::kDepth;
+        tma_load_2d(smem + Cfg::kXOff + s * Cfg::kXBytes, &tmap_x, &full[s], (kb0 + i) * kGtBK, 0);
+      };
+      // weights of the first stages before the previous kernel has finished
+      const int pre = nst < Cfg::kDepth ? nst : Cfg::kDepth;
+      for (int i = 0; i < pre; ++i) load_wsz(i);
+      griddep_wait();
+      for (int i = 0; i < pre; ++i) load_x(i);
+      bool ok = true;
+      for (int i = pre; i < nst; ++i) {
+        const int s = i % Cfg::kDepth;
+        if (!mbar_wait(&empty[s], ((i / Cfg::kDepth) & 1) ^ 1, abort_flag, kDevErrWEmpty)) {
+          ok = false;
+          break;
+        }
+        load_wsz(i);
+        load_x(i);
+      }
+      if (!ok)
+        for (int s = 0; s < Cfg::kDepth; ++s)
+          if (armed[s] >= 0) mbar_drain(&full[s], armed[s]);
+    }
+    return;  // the producer warp takes no part in the reduction below (no further __syncthreads)
+  }
+
+  // -------------------------------------------------------------------- consumers
+  const int wn = warp & 3, kh = warp >> 2;
+  const int g = lane >> 2, t = lane & 3;
+  const int cw = wn * 32 + 4 * g;  // column within the tile
+  const int col = col0 + cw;
+  const int zsh = 4 * (col & 7);
+  const int spg_step = p.gs / 32;  // steps per group when gs < 128 (1 or 2)
+  const uint32_t ones = BF16 ? 0x3F803F80u : 0x3C003C00u;
+  const uint32_t ones4[4] = {ones, ones, ones, ones};
+
+  float acc[MT][2][4], cg[MT][2][4], xo[MT][4];
+#pragma unroll
+  for (int a = 0; a < MT; ++a) {
+#pragma unroll
+    for (int b = 0; b < 2; ++b)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) acc[a][b][c] = cg[a][b][c] = 0.f;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) xo[a][c] = 0.f;
+  }
+  float sj[4] = {0.f, 0.f, 0.f, 0.f}, czj[4] = {0.f, 0.f, 0.f, 0.f};
+  auto flush = [&]() {
+#pragma unroll
+    for (int a = 0; a < MT; ++a) {
+#pragma unroll
+      for (int b = 0; b < 2; ++b)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int j = 2 * b + (c >> 1);
+          acc[a][b][c] += sj[j] * cg[a][b][c] - czj[j] * xo[a][c & 1];
+          cg[a][b][c] = 0.f;
+        }
+#pragma unroll
+      for (int c = 0; c < 4; ++c) xo[a][c] = 0.f;
+    }
+  };
+  auto load_sz = [&](const uint8_t* srow, const uint8_t* zrow) {
+    const uint2 sv = *reinterpret_cast<const uint2*>(srow + cw * 2);
+    const uint32_t zw = *reinterpret_cast<const uint32_t*>(zrow + (cw >> 3) * 4);
+    const uint32_t sw4[4] = {sv.x & 0xFFFFu, sv.x >> 16, sv.y & 0xFFFFu, sv.y >> 16};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint32_t z = (zw >> (zsh + 4 * j)) & 0xFu;
+      if (p.v1) z = (z + 1u) & 0xFu;
+      const float sc = (p.s_dtype == kF16) ? __half2float(__ushort_as_half((uint16_t)sw4[j]))
+                                           : __bfloat162float(__ushort_as_bfloat16((uint16_t)sw4[j]));
+      sj[j] = sc;
+      czj[j] = sc * (P::kMagicF + (float)z);  // exact: <= 19 significant bits
+    }
+  };
+
+  bool first = true, ok = true;
+  // stages left in the current group (gs >= 128); the first stage's position in its group
+  int stg_left = gp.stages_per_grp - (kb0 % gp.stages_per_grp);
+  for (int i = 0; i < nst; ++i) {
+    const int s = i % Cfg::kDepth;
+    if (!mbar_wait(&full[s], (i / Cfg::kDepth) & 1, abort_flag, kDevErrWFull)) {
+      ok = false;
+      break;
+    }
+    const uint8_t* wst = smem + Cfg::kWOff + s * Cfg::kWBytes + wn * 2048;
+    const uint8_t* sst = smem + Cfg::kSOff + s * Cfg::kSBytes;
+    const uint8_t* zst = smem + Cfg::kZOff + s * Cfg::kZBytes;
+    const uint8_t* xst = smem + Cfg::kXOff + s * Cfg::kXBytes;
+#pragma unroll
+    for (int jj = 0; jj < 2; ++jj) {
+      const int j = 2 * kh + jj;  // step within the stage
+      // group boundaries (warp-uniform)
+      bool new_grp;
+      int srow;
+      if (gp.rows_sz == 1) {
+        new_grp = first || (jj == 0 && stg_left == gp.stages_per_grp);
+        srow = 0;
+      } else {
+        new_grp = first || (j % spg_step == 0);
+        srow = j / spg_step;
+      }
+      if (new_grp) {
+        if (!first) flush();
+        first = false;
+        load_sz(sst + srow * (kGemvCols * 2), zst + srow * (kGemvCols / 8) * 4);
+      }
+      const int r = 4 * j + t;  // word row within the slab
+      const uint4 w = *reinterpret_cast<const uint4*>(wst + r * 128 + ((g ^ (r & 7)) << 4));
+      uint4 xv[MT];
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt)
+        xv[mt] = *reinterpret_cast<const uint4*>(xst + (g + 8 * mt) * (kGtBK * 2) + (32 * j + 8 * t) * 2);
+      const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+      uint32_t pr[4][4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        pr[q][0] = lop3_and_or(wv[q], 0x000F000Fu, P::kMagic);
+        pr[q][1] = lop3_and_or(wv[q] >> 4, 0x000F000Fu, P::kMagic);
+        pr[q][2] = lop3_and_or(wv[q] >> 8, 0x000F000Fu, P::kMagic);
+        pr[q][3] = lop3_and_or(wv[q] >> 12, 0x000F000Fu, P::kMagic);
+      }
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+        uint32_t b00, b01, b10, b11;
+        x_frags(xv[mt], b00, b01, b10, b11);
+#pragma unroll
+        for (int beta = 0; beta < 2; ++beta) {
+          const uint32_t a0[4] = {pr[2 * beta][0], pr[2 * beta + 1][0], pr[2 * beta][1], pr[2 * beta + 1][1]};
+          const uint32_t a1[4] = {pr[2 * beta][2], pr[2 * beta + 1][2], pr[2 * beta][3], pr[2 * beta + 1][3]};
+          mma_16816<BF16>(cg[mt][beta], a0, b00, b01);
+          mma_16816<BF16>(cg[mt][beta], a1, b10, b11);
+        }
+        mma_16816<BF16>(xo[mt], ones4, b00, b01);
+        mma_16816<BF16>(xo[mt], ones4, b10, b11);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+    if (--stg_left == 0) stg_left = gp.stages_per_grp;
+  }
+  if (!first) flush();
+
+  // reduce the two k halves of the CTA (named barrier over the 256 consumer threads)
+  if (kh == 1) {
+#pragma unroll
+    for (int a = 0; a < MT; ++a)
+#pragma unroll
+      for (int b = 0; b < 2; ++b)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) red[wn][lane][a * 8 + b * 4 + c] = acc[a][b][c];
+  }
+  const bool any_fail = named_bar_or(1, kGtConsumerWarps * 32, !ok);
+  if (kh == 0) {
+#pragma unroll
+    for (int a = 0; a < MT; ++a)
+#pragma unroll
+      for (int b = 0; b < 2; ++b)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[a][b][c] += red[wn][lane][a * 8 + b * 4 + c];
+  }
+  if (any_fail) return;  // error recorded; leave the tickets and the output alone
+  griddep_wait();         // the previous kernel is done with the workspace and the output
+  gemv_finish_n<BF16, MT>(p, acc, kh, col, t, tile, split, &is_last, kGtConsumerWarps * 32);
+}
+
+}  // namespace oc

@@ -9,6 +9,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <utility>
 
 #include "../../include/oc_b200.h"
 #include "common.cuh"
@@ -16,6 +17,7 @@
 #include "gemm_rows.cuh"
 #include "gemm_tc.cuh"
 #include "gemv.cuh"
+#include "gemv_tma.cuh"
 #include "moe.cuh"
 
 namespace {
@@ -43,7 +45,7 @@ bool dt16(int dt) { return dt == OC_DT_F16 || dt == OC_DT_BF16; }
 bool dtf(int dt) { return dt == OC_DT_F16 || dt == OC_DT_BF16 || dt == OC_DT_F32; }
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
-std::atomic<int> g_opt_path{0}, g_opt_tile{0}, g_opt_gemv_ctas{3};
+std::atomic<int> g_opt_path{0}, g_opt_tile{0}, g_opt_gemv_ctas{2};
 
 constexpr int kMaxDevices = 64;
 int g_sm_count[kMaxDevices];
@@ -59,6 +61,25 @@ int sm_count(int dev) {
     g_sm_count[dev] = v > 0 ? v : 148;
   }
   return g_sm_count[dev];
+}
+
+// Launch with programmatic stream serialization (PDL): the kernel may start while the previous
+// kernel in the stream finishes, and orders itself with griddepcontrol.wait.
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, const char* what,
+               Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (int rc = cuda_check(cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...), what)) return rc;
+  return launch_check(what);
 }
 
 int grid_1d(long long total, int threads, int dev) {
@@ -118,6 +139,8 @@ struct oc_b200_layer {
   int K_in, Kp, N, G, gs, v1;
   int sz_tma, sz_rows;     // scales/zeros staged by TMA in the tcgen05 kernel
   CUtensorMap tmap_w, tmap_s, tmap_z;
+  int gt_ok, gt_rows;      // decode GEMV fed by TMA (uniform groups of 32, 64 or 128*n rows)
+  CUtensorMap tmap_gw, tmap_gs, tmap_gz;
   // row-packed layers
   int E, wbits, mode, s_dtype_r, z_dtype_r;
   long long stride_n, stride_g;
@@ -292,9 +315,9 @@ int oc_b200_permute_cols(const void* x, int64_t ldx, int64_t M, int K, const int
   if (M == 0) return OC_OK;
   int dev = 0;
   if (int rc = current_device(&dev)) return rc;
-  oc::permute_cols_kernel<<<grid_1d(M * k_packed, 256, dev), 256, 0, stream>>>(
-      reinterpret_cast<const uint16_t*>(x), ldx, (int)M, K, k_perm, k_packed, reinterpret_cast<uint16_t*>(x_out));
-  return launch_check("permute_cols");
+  return launch_pdl(oc::permute_cols_kernel, dim3(grid_1d(M * k_packed, 256, dev)), dim3(256), 0, stream,
+                    "permute_cols", reinterpret_cast<const uint16_t*>(x), (long long)ldx, (int)M, K, k_perm, k_packed,
+                    reinterpret_cast<uint16_t*>(x_out));
 }
 
 // ---------------------------------------------------------------- GPTQ layer
@@ -359,6 +382,24 @@ int oc_b200_gptq_layer_create(const int32_t* qweight, const int32_t* qzeros, con
       L->tmap_z = L->tmap_w;
     }
   }
+  // Decode GEMV by TMA: uniform groups of 32, 64 or a multiple of 128 rows, at least one full
+  // 128-column tile and one 128-k stage; other layouts take the cp.async GEMV kernels.
+  L->gt_ok = 0;
+  L->gt_rows = 0;
+  if (!word_group && N % 32 == 0 && N >= 128 && k_packed >= 128 &&
+      (groupsize == 32 || groupsize == 64 || groupsize % 128 == 0) && aligned(qweight, 16) && aligned(scales, 16) &&
+      aligned(qzeros, 16)) {
+    const int rows = groupsize >= 128 ? 1 : 128 / groupsize;
+    if (make_tmap_2d(&L->tmap_gw, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, qweight, (uint64_t)N, (uint64_t)(k_packed / 8),
+                     (uint64_t)N * 4, 32, 16, CU_TENSOR_MAP_SWIZZLE_128B) == OC_OK &&
+        make_tmap_2d(&L->tmap_gs, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, scales, (uint64_t)N, (uint64_t)G, (uint64_t)N * 2,
+                     oc::kGemvCols, rows, CU_TENSOR_MAP_SWIZZLE_NONE) == OC_OK &&
+        make_tmap_2d(&L->tmap_gz, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, qzeros, (uint64_t)(N / 8), (uint64_t)G,
+                     (uint64_t)(N / 8) * 4, oc::kGemvCols / 8, rows, CU_TENSOR_MAP_SWIZZLE_NONE) == OC_OK) {
+      L->gt_ok = 1;
+      L->gt_rows = rows;
+    }
+  }
   *out = L;
   return OC_OK;
 }
@@ -378,11 +419,25 @@ struct GemvPlan {
   int splits, kstep;
 };
 
+// Split-K plan: as many K splits as fit one wave of CTAs (sm_count x OC_OPT_GEMV_CTAS, two
+// 100 KB cp.async-ring CTAs per SM by default) over the layer's 128-column tiles, each K-warp
+// keeping at least 4 steps of 32 k.
 GemvPlan gemv_plan(const oc_b200_layer* L, int dev) {
   const int n_tiles = (L->N + oc::kGemvCols - 1) / oc::kGemvCols;
   const int steps = (L->Kp + 31) / 32;
   const int target = sm_count(dev) * g_opt_gemv_ctas.load();
-  int splits = (target + n_tiles - 1) / n_tiles;
+  if (L->gt_ok) {  // TMA GEMV: splits in whole 128-k stages, at least two per CTA
+    const int KB = (L->Kp + oc::kGtBK - 1) / oc::kGtBK;
+    int splits = target / n_tiles;
+    const int max_splits = KB / 2 > 0 ? KB / 2 : 1;
+    if (splits > max_splits) splits = max_splits;
+    if (splits < 1) splits = 1;
+    if (n_tiles > (int)(kTicketBytes / 4)) splits = 1;
+    const int kbs = (KB + splits - 1) / splits;
+    splits = (KB + kbs - 1) / kbs;
+    return {splits, kbs * (oc::kGtBK / 32)};
+  }
+  int splits = target / n_tiles;
   const int max_splits = steps / 8 > 0 ? steps / 8 : 1;
   if (splits > max_splits) splits = max_splits;
   if (splits < 1) splits = 1;
@@ -434,21 +489,77 @@ extern "C" size_t oc_b200_gptq_gemm_workspace(const oc_b200_layer* L, int64_t M)
 
 namespace {
 
+// Launch one GEMV kernel with its cp.async ring as dynamic shared memory (the attribute is
+// set once per device for each kernel: one template instance per kernel).
+template <auto Kern>
+int launch_gemv_k(int smem, const oc::GemvParams& p, dim3 grid, cudaStream_t stream, const char* what) {
+  static bool attr_set[kMaxDevices] = {};
+  int dev = 0;
+  if (int rc = current_device(&dev)) return rc;
+  if (dev >= 0 && dev < kMaxDevices && !attr_set[dev]) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (int rc = cuda_check(cudaFuncSetAttribute(Kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+                            "cudaFuncSetAttribute(gemv smem)"))
+      return rc;
+    attr_set[dev] = true;
+  }
+  Kern<<<grid, oc::kGemvThreads, smem, stream>>>(p);
+  return launch_check(what);
+}
+
+template <auto Kern>
+int launch_gt_k(int smem, dim3 grid, cudaStream_t stream, const oc_b200_layer* L, const CUtensorMap& tx,
+                const oc::GtParams& g) {
+  static bool attr_set[kMaxDevices] = {};
+  int dev = 0;
+  if (int rc = current_device(&dev)) return rc;
+  if (dev >= 0 && dev < kMaxDevices && !attr_set[dev]) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (int rc = cuda_check(cudaFuncSetAttribute(Kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+                            "cudaFuncSetAttribute(gemv tma smem)"))
+      return rc;
+    attr_set[dev] = true;
+  }
+  return launch_pdl(Kern, grid, dim3(oc::kGtThreads), (size_t)smem, stream, "gptq_gemv_tma", L->tmap_gw, L->tmap_gs,
+                    L->tmap_gz, tx, g);
+}
+
+// The TMA-fed factored GEMV (layers with gt_ok); the activation tensor map is made per call.
+template <bool BF16>
+int launch_gemv_tma(const oc_b200_layer* L, const oc::GemvParams& p, const GemvPlan& gp, int n_tiles,
+                    cudaStream_t stream) {
+  oc::GtParams g{};
+  g.g = p;
+  g.rows_sz = L->gt_rows;
+  g.stages_per_grp = L->gs >= oc::kGtBK ? L->gs / oc::kGtBK : 1;
+  g.kb_per_split = gp.kstep / (oc::kGtBK / 32);
+  const int mt = p.M <= 8 ? 1 : 2;
+  CUtensorMap tx;
+  if (int rc = make_tmap_2d(&tx, BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.x,
+                            (uint64_t)p.Kp, (uint64_t)p.M, (uint64_t)p.ldx * 2, oc::kGtBK, (uint32_t)(8 * mt),
+                            CU_TENSOR_MAP_SWIZZLE_NONE))
+    return rc;
+  const dim3 grid(n_tiles, gp.splits);
+  if (mt == 1)
+    return launch_gt_k<oc::gptq_gemv_tma_kernel<BF16, 1>>(oc::GtCfg<1>::kSmemBytes, grid, stream, L, tx, g);
+  return launch_gt_k<oc::gptq_gemv_tma_kernel<BF16, 2>>(oc::GtCfg<2>::kSmemBytes, grid, stream, L, tx, g);
+}
+
 template <bool BF16, bool HAS_LO>
 int launch_gemv(const oc::GemvParams& p, int n_tiles, int splits, cudaStream_t stream) {
   dim3 grid(n_tiles, splits);
   if (!p.wgrp && p.gs % 32 == 0) {  // whole groups per 32-k step: factored scaling
     if (p.M <= 8)
-      oc::gptq_gemv_fact_kernel<BF16, 1, 6><<<grid, oc::kGemvThreads, 0, stream>>>(p);
-    else
-      oc::gptq_gemv_fact_kernel<BF16, 2, 3><<<grid, oc::kGemvThreads, 0, stream>>>(p);
-    return launch_check("gptq_gemv_fact");
+      return launch_gemv_k<oc::gptq_gemv_fact_kernel<BF16, 1>>(oc::GemvRing<1>::kSmemBytes, p, grid, stream,
+                           "gptq_gemv_fact");
+    return launch_gemv_k<oc::gptq_gemv_fact_kernel<BF16, 2>>(oc::GemvRing<2>::kSmemBytes, p, grid, stream,
+                         "gptq_gemv_fact");
   }
   if (p.M <= 8)
-    oc::gptq_gemv_kernel<BF16, HAS_LO, 1, 4><<<grid, oc::kGemvThreads, 0, stream>>>(p);
-  else
-    oc::gptq_gemv_kernel<BF16, HAS_LO, 2, 4><<<grid, oc::kGemvThreads, 0, stream>>>(p);
-  return launch_check("gptq_gemv");
+    return launch_gemv_k<oc::gptq_gemv_kernel<BF16, HAS_LO, 1>>(oc::GemvRing<1>::kSmemBytes, p, grid, stream,
+                         "gptq_gemv");
+  return launch_gemv_k<oc::gptq_gemv_kernel<BF16, HAS_LO, 2>>(oc::GemvRing<2>::kSmemBytes, p, grid, stream,
+                       "gptq_gemv");
 }
 
 struct TcMaps {
@@ -553,6 +664,8 @@ extern "C" int oc_b200_gptq_gemm_ex(const oc_b200_layer* L, const void* a, int a
     p.splits = gp.splits;
     p.kstep_per_split = gp.kstep;
     const int n_tiles = (L->N + oc::kGemvCols - 1) / oc::kGemvCols;
+    if (L->gt_ok)
+      return bf16 ? launch_gemv_tma<true>(L, p, gp, n_tiles, stream) : launch_gemv_tma<false>(L, p, gp, n_tiles, stream);
     if (bf16) return has_lo ? launch_gemv<true, true>(p, n_tiles, gp.splits, stream)
                             : launch_gemv<true, false>(p, n_tiles, gp.splits, stream);
     return has_lo ? launch_gemv<false, true>(p, n_tiles, gp.splits, stream)
@@ -956,6 +1069,8 @@ extern "C" int oc_b200_gptq_gemv_noalloc(const oc_b200_layer* L, const void* a, 
   const int n_tiles = (L->N + oc::kGemvCols - 1) / oc::kGemvCols;
   const bool bf16 = a_dtype == OC_DT_BF16;
   const bool has_lo = L->s_dtype != a_dtype;
+  if (L->gt_ok)
+    return bf16 ? launch_gemv_tma<true>(L, p, gp, n_tiles, stream) : launch_gemv_tma<false>(L, p, gp, n_tiles, stream);
   if (bf16) return has_lo ? launch_gemv<true, true>(p, n_tiles, gp.splits, stream)
                           : launch_gemv<true, false>(p, n_tiles, gp.splits, stream);
   return has_lo ? launch_gemv<false, true>(p, n_tiles, gp.splits, stream)
