@@ -526,7 +526,7 @@ def main():
     peak = peaks["bf16_sustained"]
     roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
                 "frac": round(achieved / peak, 4), "traffic": None,
-                "kernel": "gptq_gemm_tc_kernel (tcgen05, BT=256 chosen by the library at M=4608)",
+                "kernel": "gptq_gemm_tc_kernel (tcgen05, 384-token tiles = 2 x 192 chosen by the library at M=4608)",
                 "peak_source": f"{peaks['source']} bf16_tflops_sustained",
                 "gemm_share_of_step": round(gemm_ms / ms_total, 4),
                 "gemm_ms_per_step": round(gemm_ms / args.steps, 3)}

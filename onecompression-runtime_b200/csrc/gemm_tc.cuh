@@ -60,25 +60,36 @@ constexpr int kTcSOff = kTcWBytes;                  // scale rows [2][128] 16-bi
 constexpr int kTcZOff = kTcSOff + 2 * kTcBN * 2;    // zero rows [2][16] int32
 constexpr int kTcWStageBytes = kTcZOff + 2 * 16 * 4 + 128;  // 4864, multiple of 128
 
-template <int BT, int ACC_STAGES, int X_STAGES, int W_STAGES, int A_STAGES>
+constexpr int kTcEpiBufs = 4;                        // staging buffers per epilogue warp
+constexpr int kTcWarpChunkBytes = 32 * 32 * 2;         // one warp's chunk: [32 tokens][32 features] 16-bit
+constexpr int kTcChunkBytes = 4 * kTcWarpChunkBytes;   // the four warps' buffers of one chunk slot
+
+// BT tokens per MMA (UMMA N) and NSUB sub-tiles per tile: the NSUB sub-tiles of a tile share
+// every dequantized weight stage, so the dequant work per MMA flop falls as 1 / (NSUB * BT).
+template <int BT, int NSUB, int ACC_STAGES, int X_STAGES, int W_STAGES, int A_STAGES>
 struct TcCfg {
-  static constexpr int kAccCols = ACC_STAGES * BT;
+  static constexpr int kTileTok = NSUB * BT;
+  static constexpr int kAccCols = ACC_STAGES * kTileTok;
   static constexpr int kACols = A_STAGES * (kTcBK / 2);
   static_assert(kAccCols + kACols <= 512, "TMEM budget");
-  static constexpr int kXStageBytes = BT * 128;
-  static constexpr int kEpiBytes = BT * kTcBN * 2;   // output / residual staging tile [BT tokens][128 features]
+  static_assert(BT % 32 == 0 && BT <= 256, "UMMA N");
+  static constexpr int kXSubBytes = BT * 128;
+  static constexpr int kXStageBytes = NSUB * kXSubBytes;
+  static constexpr int kEpiBytes = kTcEpiBufs * kTcChunkBytes;
   static constexpr int kSmemBytes = X_STAGES * kXStageBytes + W_STAGES * kTcWStageBytes + kEpiBytes +
-                                    1024 /*align*/ + (2 * (X_STAGES + W_STAGES + A_STAGES + ACC_STAGES) + 3) * 8 + 64;
+                                    1024 /*align*/ +
+                                    (2 * (X_STAGES + W_STAGES + A_STAGES + ACC_STAGES) + 2 + 4 * kTcEpiBufs) * 8 + 64;
   static_assert(kSmemBytes <= 232448, "shared memory per CTA");
 };
 
-template <bool BF16, bool HAS_LO, int BT, int ACC_STAGES, int X_STAGES, int W_STAGES, int A_STAGES>
+template <bool BF16, bool HAS_LO, int BT, int NSUB, int ACC_STAGES, int X_STAGES, int W_STAGES, int A_STAGES>
 __global__ void __launch_bounds__(kTcThreads, 1)
     gptq_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
                         const __grid_constant__ CUtensorMap tmap_s, const __grid_constant__ CUtensorMap tmap_z,
                         const __grid_constant__ CUtensorMap tmap_c, const __grid_constant__ CUtensorMap tmap_r,
                         const TcParams p) {
-  using Cfg = TcCfg<BT, ACC_STAGES, X_STAGES, W_STAGES, A_STAGES>;
+  using Cfg = TcCfg<BT, NSUB, ACC_STAGES, X_STAGES, W_STAGES, A_STAGES>;
+  constexpr int kTileTok = Cfg::kTileTok;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* x_smem = smem;
@@ -94,8 +105,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint64_t* full_acc = empty_a + A_STAGES;
   uint64_t* empty_acc = full_acc + ACC_STAGES;
   uint64_t* drain = empty_acc + ACC_STAGES;
-  uint64_t* res_full = drain + 1;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(res_full + 1);
+  uint64_t* res_full = drain + 1;  // [4 epilogue warps][kTcEpiBufs]
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(res_full + 4 * kTcEpiBufs);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = warp_id(), lane = lane_id();
@@ -108,7 +119,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     for (int i = 0; i < A_STAGES; ++i) { mbar_init(&full_a[i], 128); mbar_init(&empty_a[i], 1); }
     for (int i = 0; i < ACC_STAGES; ++i) { mbar_init(&full_acc[i], 1); mbar_init(&empty_acc[i], 128); }
     mbar_init(drain, 1);
-    mbar_init(res_full, 1);
+    for (int i = 0; i < 4 * kTcEpiBufs; ++i) mbar_init(&res_full[i], 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -144,7 +155,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           const int sx = it % X_STAGES, px = (it / X_STAGES) & 1;
           if (!mbar_wait(&empty_x[sx], px ^ 1, abort_flag, kDevErrTmaEmpty)) { ok = false; break; }
           mbar_arrive_expect_tx(&full_x[sx], Cfg::kXStageBytes);
-          tma_load_2d(x_smem + sx * Cfg::kXStageBytes, &tmap_x, &full_x[sx], kb * kTcBK, mb * BT);
+#pragma unroll
+          for (int sb = 0; sb < NSUB; ++sb)
+            tma_load_2d(x_smem + sx * Cfg::kXStageBytes + sb * Cfg::kXSubBytes, &tmap_x, &full_x[sx], kb * kTcBK,
+                        mb * kTileTok + sb * BT);
           x_armed[sx] = px;
         }
       }
@@ -193,7 +207,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int sc = tcount % ACC_STAGES, pc = (tcount / ACC_STAGES) & 1;
         if (!mbar_wait(&empty_acc[sc], pc ^ 1, abort_flag, kDevErrAccEmpty)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + (uint32_t)(sc * BT);
+        const uint32_t d_tmem = tmem_base + (uint32_t)(sc * kTileTok);
         for (int kb = 0; kb < KB; ++kb, ++it) {
           const int sx = it % X_STAGES, px = (it / X_STAGES) & 1;
           const int sa = it % A_STAGES, pa = (it / A_STAGES) & 1;
@@ -203,10 +217,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           const uint32_t xaddr = smem_u32(x_smem + sx * Cfg::kXStageBytes);
           const uint32_t a_tmem = tmem_base + (uint32_t)(Cfg::kAccCols + sa * (kTcBK / 2));
 #pragma unroll
-          for (int j = 0; j < kTcBK / 16; ++j) {
-            const uint64_t bdesc = smem_desc_kmajor_sw128(xaddr + j * 32);
-            tc_mma_ts(d_tmem, a_tmem + j * 8, bdesc, idesc, (kb | j) != 0 ? 1u : 0u);
-          }
+          for (int j = 0; j < kTcBK / 16; ++j)
+#pragma unroll
+            for (int sb = 0; sb < NSUB; ++sb) {
+              const uint64_t bdesc = smem_desc_kmajor_sw128(xaddr + sb * Cfg::kXSubBytes + j * 32);
+              tc_mma_ts(d_tmem + sb * BT, a_tmem + j * 8, bdesc, idesc, (kb | j) != 0 ? 1u : 0u);
+            }
           issued = true;
           tc_commit(&empty_x[sx]);
           tc_commit(&empty_a[sa]);
@@ -310,68 +326,88 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
     }
   } else if (warp >= kTcEpiWarp0 && p.tma_epi) {
-    // ------------------------------------------------------------ epilogue warpgroup, TMA path
-    // Per tile: the residual tile (if any) is TMA-loaded into the staging tile while the
-    // mainloop runs; each thread turns its feature's accumulators into
-    // act(acc + bias) + residual in place; one TMA store writes the tile (rows past M and
-    // features past N are clipped by the tensor map).
+    // ------------------------------------------------------------ epilogue warps, TMA path
+    // Each of the four warps drains its 32 features (TMEM lanes) of the accumulator tile in
+    // 32-token chunks through its own four staging buffers (running chunk counter q, buffer
+    // q & 3), with no synchronisation across warps: lane 0 TMA-loads the residual chunk two
+    // chunks ahead and TMA-stores each finished [32 x 32] chunk (rows past M and features past
+    // N are clipped); bulk groups and residual barriers are per warp.
     const int q4 = warp & 3;
     const int row = q4 * 32 + lane;
-    const int et = threadIdx.x - kTcEpiWarp0 * 32;
     const int odt = BF16 ? kBF16 : kF16;
-    uint16_t* epi = reinterpret_cast<uint16_t*>(epi_smem);
+    constexpr int kChunks = kTileTok / 32;
+    uint16_t* wepi = reinterpret_cast<uint16_t*>(epi_smem) + q4 * (kTcEpiBufs * kTcWarpChunkBytes / 2);
+    uint64_t* wres = res_full + q4 * kTcEpiBufs;
+    uint32_t q = 0;
+    uint32_t res_pend = 0, res_par = 0;  // lane 0: buffers with a residual load in flight, its phase
     int tcount = 0;
-    uint32_t rphase = 0;
-    bool res_armed = false;
+    auto issue_res = [&](uint32_t qq, int f0, int m0) {  // lane 0
+      const int b = qq & (kTcEpiBufs - 1);
+      mbar_arrive_expect_tx(&wres[b], kTcWarpChunkBytes);
+      tma_load_2d(wepi + b * (kTcWarpChunkBytes / 2), &tmap_r, &wres[b], f0, m0);
+      res_pend |= 1u << b;
+      res_par = (res_par & ~(1u << b)) | (((qq >> 2) & 1u) << b);
+    };
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++tcount) {
       const int sc = tcount % ACC_STAGES, pc = (tcount / ACC_STAGES) & 1;
       const int nb = tile % p.n_tiles_n, mb = tile / p.n_tiles_n;
-      const int n = nb * kTcBN + row;
+      const int f0 = nb * kTcBN + q4 * 32;  // this warp's first feature
+      const int n = f0 + lane;
+      const int m_base = mb * kTileTok;
+      const int nchunks = min(kChunks, (p.M - m_base + 31) / 32);  // chunks holding rows < M
       const float bv = (p.bias && n < p.N) ? load_as_f32(p.bias, p.bias_dtype, n) : 0.f;
-      if (et == 0) {
-        bulk_wait_group_read0();  // the previous tile's store has read the staging tile
-        if (p.residual) {
-          mbar_arrive_expect_tx(res_full, Cfg::kEpiBytes);
-          tma_load_2d(epi, &tmap_r, res_full, nb * kTcBN, mb * BT);
-          res_armed = true;
-        }
+      if (lane == 0) {
+        bulk_wait_group_read<2>();  // stores q-3, q-4 have read buffers q, q+1
+        if (p.residual)
+          for (int c = 0; c < 2 && c < nchunks; ++c) issue_res(q + c, f0, m_base + c * 32);
       }
-      named_bar_sync(1, 128);
-      bool ok = mbar_wait(&full_acc[sc], pc, abort_flag, kDevErrAccFull);
-      if (ok && p.residual) ok = mbar_wait(res_full, rphase, abort_flag, kDevErrResFull);
-      if (named_bar_or(1, 128, !ok)) break;  // all four warps leave together
-      if (p.residual) {
-        rphase ^= 1u;
-        res_armed = false;
-      }
+      __syncwarp();
+      if (!mbar_wait(&full_acc[sc], pc, abort_flag, kDevErrAccFull)) break;
       tc_fence_after();
-      const uint32_t tbase = tmem_base + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(sc * BT);
+      const uint32_t tbase = tmem_base + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(sc * kTileTok);
+      bool failed = false;
 #pragma unroll 1
-      for (int c = 0; c < BT / 32; ++c) {
+      for (int c = 0; c < nchunks; ++c, ++q) {
+        const int b = q & (kTcEpiBufs - 1);
+        if (lane == 0 && c + 2 < nchunks) {
+          bulk_wait_group_read<1>();  // store q-2 has read buffer q+2
+          if (p.residual) issue_res(q + 2, f0, m_base + (c + 2) * 32);
+        }
         uint32_t v[32];
         tmem_ld_32x32b_x32(tbase + (uint32_t)(c * 32), v);
         tc_wait_ld();
-        uint16_t* e = epi + (c * 32) * kTcBN + row;
+        if (p.residual) {
+          if (!mbar_wait(&wres[b], (q >> 2) & 1, abort_flag, kDevErrResFull)) failed = true;
+          if (__any_sync(0xffffffffu, failed)) {
+            failed = true;
+            break;
+          }
+          if (lane == 0) res_pend &= ~(1u << b);
+        }
+        __syncwarp();  // buffer b is free (lane 0 waited for its last store) / holds the residual
+        uint16_t* e = wepi + b * (kTcWarpChunkBytes / 2) + lane;
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           float o = __uint_as_float(v[i]) + bv;
           if (p.act == kActGeluTanh) o = gelu_tanh(o);
-          if (p.residual) o += bits_to_f32(e[i * kTcBN], odt);
-          e[i * kTcBN] = f32_to_bits(o, odt);
+          if (p.residual) o += bits_to_f32(e[i * 32], odt);
+          e[i * 32] = f32_to_bits(o, odt);
+        }
+        fence_proxy_async_shared();  // generic-proxy smem writes -> visible to the TMA store
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmap_c, wepi + b * (kTcWarpChunkBytes / 2), f0, m_base + c * 32);
+          bulk_commit_group();
         }
       }
+      if (failed) break;
       tc_fence_before();
-      mbar_arrive(&empty_acc[sc]);  // the accumulator is in registers/smem: the next tile may start
-      fence_proxy_async_shared();   // generic-proxy smem writes -> visible to the TMA store
-      named_bar_sync(1, 128);
-      if (et == 0) {
-        tma_store_2d(&tmap_c, epi, nb * kTcBN, mb * BT);
-        bulk_commit_group();
-      }
+      mbar_arrive(&empty_acc[sc]);  // this warp has read its accumulator lanes
     }
-    if (et == 0) {
+    if (lane == 0) {
       bulk_wait_group0();
-      if (res_armed) mbar_drain(res_full, rphase);
+      for (int b = 0; b < kTcEpiBufs; ++b)  // residual loads issued ahead and never consumed
+        if (res_pend & (1u << b)) mbar_drain(&wres[b], (res_par >> b) & 1u);
     }
   } else if (warp >= kTcEpiWarp0) {
     // ------------------------------------------------------------ epilogue warpgroup, direct stores
@@ -389,13 +425,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       if (!mbar_wait(&full_acc[sc], pc, abort_flag, kDevErrAccFull)) break;
       tc_fence_after();
       __syncwarp();
-      const uint32_t tbase = tmem_base + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(sc * BT);
+      const uint32_t tbase = tmem_base + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(sc * kTileTok);
 #pragma unroll 1
-      for (int c = 0; c < BT / 32; ++c) {
+      for (int c = 0; c < kTileTok / 32; ++c) {
         uint32_t v[32];
         tmem_ld_32x32b_x32(tbase + (uint32_t)(c * 32), v);
         tc_wait_ld();
-        const int m0 = mb * BT + c * 32;
+        const int m0 = mb * kTileTok + c * 32;
         if (nvalid) {
           uint16_t* dst = p.out + (long long)m0 * p.ldc + n;
           if (!p.residual && p.act == kActNone) {

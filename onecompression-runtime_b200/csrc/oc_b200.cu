@@ -173,7 +173,7 @@ int oc_b200_set_option(int key, int value) {
       g_opt_path = value;
       return OC_OK;
     case OC_OPT_TC_TILE:
-      if (value != 0 && value != 128 && value != 192 && value != 256)
+      if (value != 0 && value != 128 && value != 192 && value != 256 && value != 384 && value != 448)
         return fail(OC_ERR_INVALID, "OC_OPT_TC_TILE: %d", value);
       g_opt_tile = value;
       return OC_OK;
@@ -449,12 +449,13 @@ GemvPlan gemv_plan(const oc_b200_layer* L, int dev) {
 
 // Tokens per tcgen05 tile when the caller leaves it to the library: the preset with the
 // least (waves of persistent CTAs) x (measured time of one tile at K = 3072 on B200, us).
+// 384 and 448 are two sub-tiles of 192 / 224 tokens sharing each dequantized weight stage.
 int choose_tile(int64_t M, int n_tiles_n, int sms) {
-  static const int kBt[3] = {256, 192, 128};
-  static const double kTileUs[3] = {29.0, 24.8, 23.4};
-  int best = 256;
+  static const int kBt[5] = {384, 448, 256, 192, 128};
+  static const double kTileUs[5] = {41.7, 42.5, 31.7, 25.0, 22.7};
+  int best = 384;
   double best_cost = 1e300;
-  for (int i = 0; i < 3; ++i) {
+  for (int i = 0; i < 5; ++i) {
     const int64_t tiles = (int64_t)n_tiles_n * ((M + kBt[i] - 1) / kBt[i]);
     const double cost = (double)((tiles + sms - 1) / sms) * kTileUs[i];
     if (cost < best_cost) {
@@ -566,10 +567,10 @@ struct TcMaps {
   CUtensorMap x, c, r;
 };
 
-template <bool BF16, bool HAS_LO, int BT, int ACC, int XS, int WS, int AS>
+template <bool BF16, bool HAS_LO, int BT, int NSUB, int ACC, int XS, int WS, int AS>
 int launch_tc_t(const TcMaps& tm, const oc_b200_layer* L, const oc::TcParams& p, int dev, cudaStream_t stream) {
-  using Cfg = oc::TcCfg<BT, ACC, XS, WS, AS>;
-  auto kern = oc::gptq_gemm_tc_kernel<BF16, HAS_LO, BT, ACC, XS, WS, AS>;
+  using Cfg = oc::TcCfg<BT, NSUB, ACC, XS, WS, AS>;
+  auto kern = oc::gptq_gemm_tc_kernel<BF16, HAS_LO, BT, NSUB, ACC, XS, WS, AS>;
   static bool attr_set[kMaxDevices] = {};
   if (dev >= 0 && dev < kMaxDevices && !attr_set[dev]) {
     std::lock_guard<std::mutex> lk(g_mu);
@@ -587,9 +588,11 @@ int launch_tc_t(const TcMaps& tm, const oc_b200_layer* L, const oc::TcParams& p,
 // 512 TMEM columns and the 227 KB of shared memory with the epilogue staging tile.
 template <bool BF16, bool HAS_LO>
 int launch_tc(int bt, const TcMaps& tm, const oc_b200_layer* L, const oc::TcParams& p, int dev, cudaStream_t stream) {
-  if (bt == 128) return launch_tc_t<BF16, HAS_LO, 128, 2, 8, 8, 8>(tm, L, p, dev, stream);
-  if (bt == 256) return launch_tc_t<BF16, HAS_LO, 256, 1, 4, 6, 4>(tm, L, p, dev, stream);
-  return launch_tc_t<BF16, HAS_LO, 192, 2, 5, 8, 4>(tm, L, p, dev, stream);
+  if (bt == 128) return launch_tc_t<BF16, HAS_LO, 128, 1, 2, 8, 8, 8>(tm, L, p, dev, stream);
+  if (bt == 256) return launch_tc_t<BF16, HAS_LO, 256, 1, 1, 5, 6, 4>(tm, L, p, dev, stream);
+  if (bt == 384) return launch_tc_t<BF16, HAS_LO, 192, 2, 1, 3, 8, 4>(tm, L, p, dev, stream);
+  if (bt == 448) return launch_tc_t<BF16, HAS_LO, 224, 2, 1, 3, 4, 2>(tm, L, p, dev, stream);
+  return launch_tc_t<BF16, HAS_LO, 192, 1, 2, 6, 8, 4>(tm, L, p, dev, stream);
 }
 
 }  // namespace
@@ -677,8 +680,9 @@ extern "C" int oc_b200_gptq_gemm_ex(const oc_b200_layer* L, const void* a, int a
   const CUtensorMapDataType tdt = bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   TcMaps tm;
   std::memset(&tm, 0, sizeof(tm));
+  const int sub_rows = bt > 256 ? bt / 2 : bt;  // tokens per MMA (tiles of 384 / 448 are two sub-tiles)
   if (int rc = make_tmap_2d(&tm.x, tdt, 2, xk, (uint64_t)L->Kp, (uint64_t)M, (uint64_t)ldx * 2, oc::kTcBK,
-                            (uint32_t)bt, CU_TENSOR_MAP_SWIZZLE_128B))
+                            (uint32_t)sub_rows, CU_TENSOR_MAP_SWIZZLE_128B))
     return rc;
   // Output (and residual) tiles go through shared memory by TMA when a tensor map can
   // describe them (16-byte aligned base, row pitch a multiple of 16 bytes); otherwise the
@@ -687,12 +691,12 @@ extern "C" int oc_b200_gptq_gemm_ex(const oc_b200_layer* L, const void* a, int a
   const bool r_tma = !residual || (aligned(residual, 16) && ldr % 8 == 0);
   const bool tma_epi = c_tma && r_tma;
   if (tma_epi) {
-    if (int rc = make_tmap_2d(&tm.c, tdt, 2, c, (uint64_t)L->N, (uint64_t)M, (uint64_t)ldc * 2, oc::kTcBN,
-                              (uint32_t)bt, CU_TENSOR_MAP_SWIZZLE_NONE))
+    if (int rc = make_tmap_2d(&tm.c, tdt, 2, c, (uint64_t)L->N, (uint64_t)M, (uint64_t)ldc * 2, 32, 32,
+                              CU_TENSOR_MAP_SWIZZLE_NONE))
       return rc;
     if (residual)
-      if (int rc = make_tmap_2d(&tm.r, tdt, 2, residual, (uint64_t)L->N, (uint64_t)M, (uint64_t)ldr * 2, oc::kTcBN,
-                                (uint32_t)bt, CU_TENSOR_MAP_SWIZZLE_NONE))
+      if (int rc = make_tmap_2d(&tm.r, tdt, 2, residual, (uint64_t)L->N, (uint64_t)M, (uint64_t)ldr * 2, 32, 32,
+                                CU_TENSOR_MAP_SWIZZLE_NONE))
         return rc;
   }
   oc::TcParams p{};

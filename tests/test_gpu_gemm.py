@@ -101,7 +101,7 @@ def test_shapes(cuda_device, shape, path, path_option):
     assert err < 1e-2, err
 
 
-@pytest.mark.parametrize("tile", [128, 192, 256])
+@pytest.mark.parametrize("tile", [128, 192, 256, 384, 448])
 def test_tc_tiles(cuda_device, tile, path_option):
     from onecomp_runtime import _lib
     from onecomp_runtime.testing import gptq_layer, activations
@@ -228,3 +228,22 @@ def test_fused_epilogue(cuda_device, M, act, residual):
     assert err < 1e-2, err
     if act is None and r is None:
         torch.testing.assert_close(y, layer(x), rtol=0, atol=0)
+
+
+@pytest.mark.parametrize("tile", [192, 384, 448])
+@pytest.mark.parametrize("M", [200, 1000])
+def test_tc_tiles_fused_epilogue(cuda_device, tile, M, path_option):
+    """Every tile preset (one and two sub-tiles) with a residual + GELU epilogue, partial last tile."""
+    from onecomp_runtime import _lib
+    from onecomp_runtime.testing import gptq_layer, activations
+    path_option(2)
+    _lib.set_option(_lib.OPT_TC_TILE, tile)
+    K, N = 768, 384
+    t = {k: v.to(cuda_device) for k, v in gptq_layer(K, N, 32, seed=tile + M).items()}
+    layer = _module(t, K, N, 32, True, "fused", cuda_device)
+    x = activations(M, K, seed=M).to(cuda_device)
+    r = activations(M, N, seed=M + 7).to(cuda_device)
+    y = layer.forward_fused(x, residual=r, activation="gelu_tanh")
+    ref = torch.nn.functional.gelu(_gpu_reference(t, K, N, x, True, t["bias"]), approximate="tanh") + r.double()
+    err = float((y.double() - ref).abs().max() / ref.abs().max())
+    assert err < 1e-2, err
