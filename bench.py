@@ -47,6 +47,12 @@ import torch  # noqa: E402
 METRIC = "DiT-stack tokens/s (int4 GPTQ linear stack)"
 
 
+
+# DRAM traffic measured by ncu (dram__bytes_read.sum + dram__bytes_write.sum) for the dominant
+# kernel of each workload; the commands and per-launch figures are in profiles/.
+TC_TRAFFIC_BYTES_PER_LAUNCH = 103_400_000    # cfg1: mean of qkv, proj, fc1, fc2 launches
+GEMV_TRAFFIC_BYTES_PER_LAUNCH = 21_849_088   # cfg2: q/k/v layer, M = 1 (algorithmic 21.8 MB)
+
 def load_peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -252,7 +258,9 @@ def bench_decode(args):
                        "packed_bytes_per_set": nbytes, "graph": "CUDA graph of the 5 layers, replayed"},
             "per_m": per_m,
             "roofline": {"bound": "hbm", "achieved": top["GB_s"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                         "frac": top["frac_hbm"], "traffic": None, "peak_source": f"{peaks['source']} hbm_gbs"}}
+                         "frac": top["frac_hbm"], "traffic": GEMV_TRAFFIC_BYTES_PER_LAUNCH,
+                         "traffic_unit": "bytes per launch (q/k/v layer)",
+                         "peak_source": f"{peaks['source']} hbm_gbs"}}
     print(json.dumps(line), flush=True)
 
 
@@ -525,7 +533,11 @@ def main():
     achieved = gemm_flops / (gemm_ms / 1e3) / 1e12
     peak = peaks["bf16_sustained"]
     roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
-                "frac": round(achieved / peak, 4), "traffic": None,
+                "frac": round(achieved / peak, 4),
+                # DRAM read + write bytes per launch, mean over one block's four GEMM launches, from
+                # one ncu capture of this workload (profiles/gptq_gemm_tc_cfg1.txt)
+                "traffic": TC_TRAFFIC_BYTES_PER_LAUNCH if args.blocks == 0 else None,
+                "traffic_unit": "bytes per launch",
                 "kernel": "gptq_gemm_tc_kernel (tcgen05, 384-token tiles = 2 x 192 chosen by the library at M=4608)",
                 "peak_source": f"{peaks['source']} bf16_tflops_sustained",
                 "gemm_share_of_step": round(gemm_ms / ms_total, 4),
