@@ -333,7 +333,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // chunks ahead and TMA-stores each finished [32 x 32] chunk (rows past M and features past
     // N are clipped); bulk groups and residual barriers are per warp.
     const int q4 = warp & 3;
-    const int row = q4 * 32 + lane;
     const int odt = BF16 ? kBF16 : kF16;
     constexpr int kChunks = kTileTok / 32;
     uint16_t* wepi = reinterpret_cast<uint16_t*>(epi_smem) + q4 * (kTcEpiBufs * kTcWarpChunkBytes / 2);

@@ -18,6 +18,7 @@
 #include "gemm_tc.cuh"
 #include "gemv.cuh"
 #include "gemv_tma.cuh"
+#include "gemv_tc.cuh"
 #include "moe.cuh"
 
 namespace {
@@ -45,7 +46,7 @@ bool dt16(int dt) { return dt == OC_DT_F16 || dt == OC_DT_BF16; }
 bool dtf(int dt) { return dt == OC_DT_F16 || dt == OC_DT_BF16 || dt == OC_DT_F32; }
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
-std::atomic<int> g_opt_path{0}, g_opt_tile{0}, g_opt_gemv_ctas{2};
+std::atomic<int> g_opt_path{0}, g_opt_tile{0}, g_opt_gemv_ctas{2}, g_opt_gemv_impl{1};
 
 constexpr int kMaxDevices = 64;
 int g_sm_count[kMaxDevices];
@@ -141,6 +142,7 @@ struct oc_b200_layer {
   CUtensorMap tmap_w, tmap_s, tmap_z;
   int gt_ok, gt_rows;      // decode GEMV fed by TMA (uniform groups of 32, 64 or 128*n rows)
   CUtensorMap tmap_gw, tmap_gs, tmap_gz;
+  CUtensorMap tmap_s1, tmap_z1;  // one scale / zero row per box (tcgen05 decode GEMV)
   // row-packed layers
   int E, wbits, mode, s_dtype_r, z_dtype_r;
   long long stride_n, stride_g;
@@ -180,6 +182,10 @@ int oc_b200_set_option(int key, int value) {
     case OC_OPT_GEMV_CTAS:
       if (value < 1 || value > 32) return fail(OC_ERR_INVALID, "OC_OPT_GEMV_CTAS: %d", value);
       g_opt_gemv_ctas = value;
+      return OC_OK;
+    case OC_OPT_GEMV_IMPL:
+      if (value < 0 || value > 2) return fail(OC_ERR_INVALID, "OC_OPT_GEMV_IMPL: %d", value);
+      g_opt_gemv_impl = value;
       return OC_OK;
   }
   return fail(OC_ERR_INVALID, "unknown option %d", key);
@@ -395,7 +401,11 @@ int oc_b200_gptq_layer_create(const int32_t* qweight, const int32_t* qzeros, con
         make_tmap_2d(&L->tmap_gs, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, scales, (uint64_t)N, (uint64_t)G, (uint64_t)N * 2,
                      oc::kGemvCols, rows, CU_TENSOR_MAP_SWIZZLE_NONE) == OC_OK &&
         make_tmap_2d(&L->tmap_gz, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, qzeros, (uint64_t)(N / 8), (uint64_t)G,
-                     (uint64_t)(N / 8) * 4, oc::kGemvCols / 8, rows, CU_TENSOR_MAP_SWIZZLE_NONE) == OC_OK) {
+                     (uint64_t)(N / 8) * 4, oc::kGemvCols / 8, rows, CU_TENSOR_MAP_SWIZZLE_NONE) == OC_OK &&
+        make_tmap_2d(&L->tmap_s1, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, scales, (uint64_t)N, (uint64_t)G, (uint64_t)N * 2,
+                     oc::kGemvCols, 1, CU_TENSOR_MAP_SWIZZLE_NONE) == OC_OK &&
+        make_tmap_2d(&L->tmap_z1, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, qzeros, (uint64_t)(N / 8), (uint64_t)G,
+                     (uint64_t)(N / 8) * 4, oc::kGemvCols / 8, 1, CU_TENSOR_MAP_SWIZZLE_NONE) == OC_OK) {
       L->gt_ok = 1;
       L->gt_rows = rows;
     }
@@ -422,11 +432,30 @@ struct GemvPlan {
 // Split-K plan: as many K splits as fit one wave of CTAs (sm_count x OC_OPT_GEMV_CTAS, two
 // 100 KB cp.async-ring CTAs per SM by default) over the layer's 128-column tiles, each K-warp
 // keeping at least 4 steps of 32 k.
+// Which decode kernel runs for a layer: 0 tcgen05 GEMV, 1 TMA + mma.sync GEMV (both for
+// uniform groups of 32, 64 or 128*n rows; 1 is the default, measured faster), 2 cp.async +
+// mma.sync GEMV (any layout).
+int gemv_impl(const oc_b200_layer* L) {
+  if (!L->gt_ok) return 2;
+  return g_opt_gemv_impl.load();
+}
+
 GemvPlan gemv_plan(const oc_b200_layer* L, int dev) {
   const int n_tiles = (L->N + oc::kGemvCols - 1) / oc::kGemvCols;
   const int steps = (L->Kp + 31) / 32;
   const int target = sm_count(dev) * g_opt_gemv_ctas.load();
-  if (L->gt_ok) {  // TMA GEMV: splits in whole 128-k stages, at least two per CTA
+  if (gemv_impl(L) == 0) {  // tcgen05 GEMV: one CTA per SM, splits in 64-k blocks, at least 4 each
+    const int KB = (L->Kp + oc::kVtBK - 1) / oc::kVtBK;
+    int splits = sm_count(dev) / n_tiles;
+    const int max_splits = KB / 4 > 0 ? KB / 4 : 1;
+    if (splits > max_splits) splits = max_splits;
+    if (splits < 1) splits = 1;
+    if (n_tiles > (int)(kTicketBytes / 4)) splits = 1;
+    const int kbs = (KB + splits - 1) / splits;
+    splits = (KB + kbs - 1) / kbs;
+    return {splits, kbs * (oc::kVtBK / 32)};
+  }
+  if (gemv_impl(L) == 1) {  // TMA GEMV: splits in whole 128-k stages, at least two per CTA
     const int KB = (L->Kp + oc::kGtBK - 1) / oc::kGtBK;
     int splits = target / n_tiles;
     const int max_splits = KB / 2 > 0 ? KB / 2 : 1;
@@ -523,6 +552,33 @@ int launch_gt_k(int smem, dim3 grid, cudaStream_t stream, const oc_b200_layer* L
   }
   return launch_pdl(Kern, grid, dim3(oc::kGtThreads), (size_t)smem, stream, "gptq_gemv_tma", L->tmap_gw, L->tmap_gs,
                     L->tmap_gz, tx, g);
+}
+
+// The tcgen05 decode GEMV (layers with gt_ok); the activation tensor map is made per call.
+template <bool BF16>
+int launch_gemv_tcv(const oc_b200_layer* L, const oc::GemvParams& p, const GemvPlan& gp, int n_tiles,
+                    cudaStream_t stream) {
+  oc::VtParams v{};
+  v.g = p;
+  v.kb_per_split = gp.kstep / (oc::kVtBK / 32);
+  CUtensorMap tx;
+  if (int rc = make_tmap_2d(&tx, BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.x,
+                            (uint64_t)p.Kp, (uint64_t)p.M, (uint64_t)p.ldx * 2, oc::kVtBK, (uint32_t)oc::kVtN,
+                            CU_TENSOR_MAP_SWIZZLE_128B))
+    return rc;
+  auto kern = oc::gptq_gemv_tc_kernel<BF16>;
+  static bool attr_set[kMaxDevices] = {};
+  int dev = 0;
+  if (int rc = current_device(&dev)) return rc;
+  if (dev >= 0 && dev < kMaxDevices && !attr_set[dev]) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (int rc = cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, oc::kVtSmemBytes),
+                            "cudaFuncSetAttribute(gemv tc smem)"))
+      return rc;
+    attr_set[dev] = true;
+  }
+  return launch_pdl(kern, dim3(n_tiles, gp.splits), dim3(oc::kVtThreads), (size_t)oc::kVtSmemBytes, stream,
+                    "gptq_gemv_tc", L->tmap_w, L->tmap_s1, L->tmap_z1, tx, v);
 }
 
 // The TMA-fed factored GEMV (layers with gt_ok); the activation tensor map is made per call.
@@ -667,7 +723,9 @@ extern "C" int oc_b200_gptq_gemm_ex(const oc_b200_layer* L, const void* a, int a
     p.splits = gp.splits;
     p.kstep_per_split = gp.kstep;
     const int n_tiles = (L->N + oc::kGemvCols - 1) / oc::kGemvCols;
-    if (L->gt_ok)
+    if (gemv_impl(L) == 0)
+      return bf16 ? launch_gemv_tcv<true>(L, p, gp, n_tiles, stream) : launch_gemv_tcv<false>(L, p, gp, n_tiles, stream);
+    if (gemv_impl(L) == 1)
       return bf16 ? launch_gemv_tma<true>(L, p, gp, n_tiles, stream) : launch_gemv_tma<false>(L, p, gp, n_tiles, stream);
     if (bf16) return has_lo ? launch_gemv<true, true>(p, n_tiles, gp.splits, stream)
                             : launch_gemv<true, false>(p, n_tiles, gp.splits, stream);
@@ -1073,7 +1131,9 @@ extern "C" int oc_b200_gptq_gemv_noalloc(const oc_b200_layer* L, const void* a, 
   const int n_tiles = (L->N + oc::kGemvCols - 1) / oc::kGemvCols;
   const bool bf16 = a_dtype == OC_DT_BF16;
   const bool has_lo = L->s_dtype != a_dtype;
-  if (L->gt_ok)
+  if (gemv_impl(L) == 0)
+    return bf16 ? launch_gemv_tcv<true>(L, p, gp, n_tiles, stream) : launch_gemv_tcv<false>(L, p, gp, n_tiles, stream);
+  if (gemv_impl(L) == 1)
     return bf16 ? launch_gemv_tma<true>(L, p, gp, n_tiles, stream) : launch_gemv_tma<false>(L, p, gp, n_tiles, stream);
   if (bf16) return has_lo ? launch_gemv<true, true>(p, n_tiles, gp.splits, stream)
                           : launch_gemv<true, false>(p, n_tiles, gp.splits, stream);

@@ -21,6 +21,7 @@ DT = {torch.float16: 0, torch.bfloat16: 1, torch.float32: 2}
 OPT_GEMM_PATH = 1
 OPT_TC_TILE = 2
 OPT_GEMV_CTAS = 3
+OPT_GEMV_IMPL = 4
 ACT_NONE = 0
 ACT_GELU_TANH = 1
 

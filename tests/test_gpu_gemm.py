@@ -247,3 +247,41 @@ def test_tc_tiles_fused_epilogue(cuda_device, tile, M, path_option):
     ref = torch.nn.functional.gelu(_gpu_reference(t, K, N, x, True, t["bias"]), approximate="tanh") + r.double()
     err = float((y.double() - ref).abs().max() / ref.abs().max())
     assert err < 1e-2, err
+
+
+GEMV_IMPL_SHAPES = [
+    # M, K, N, gs, v1, act-order, scales dtype
+    (1, 3072, 3072, 32, True, False, torch.float16),
+    (3, 1024, 384, 64, True, False, torch.float16),
+    (8, 5120, 1024, 128, False, True, torch.bfloat16),
+    (11, 4096, 640, 256, False, False, torch.bfloat16),
+    (16, 2176, 512, 128, False, True, torch.float16),
+]
+
+
+@pytest.mark.parametrize("impl", [0, 1, 2])
+@pytest.mark.parametrize("shape", GEMV_IMPL_SHAPES, ids=lambda s: f"M{s[0]}K{s[1]}N{s[2]}g{s[3]}")
+def test_gemv_impls(cuda_device, impl, shape):
+    """The three decode kernels for uniform-group layers (tcgen05, TMA + mma.sync, cp.async +
+    mma.sync) against the fp64 GEMM of the exact weight, with a residual + GELU epilogue."""
+    from onecomp_runtime import _lib
+    from onecomp_runtime.testing import gptq_layer, activations
+    M, K, N, gs, v1, act, sdt = shape
+    t = {k: v.to(cuda_device) for k, v in gptq_layer(K, N, gs, seed=K + N + M, v1=v1, actorder=act,
+                                                     scales_dtype=sdt).items()}
+    layer = _module(t, K, N, gs, v1, "packed" if act else ("fused" if gs == 32 else "any"), cuda_device)
+    x = activations(M, K, seed=M).to(cuda_device)
+    r = activations(M, N, seed=M + 3).to(cuda_device)
+    _lib.set_option(_lib.OPT_GEMV_IMPL, impl)
+    try:
+        y = layer(x)
+        yf = layer.forward_fused(x, residual=r, activation="gelu_tanh")
+    finally:
+        _lib.set_option(_lib.OPT_GEMV_IMPL, 1)
+    ref = _gpu_reference(t, K, N, x, v1, t["bias"])
+    err = float((y.double() - ref).abs().max() / ref.abs().max())
+    assert err < 1e-2, err
+    reff = torch.nn.functional.gelu(ref, approximate="tanh") + r.double()
+    errf = float((yf.double() - reff).abs().max() / reff.abs().max())
+    assert errf < 1e-2, errf
+    assert _lib.read_device_error(cuda_device) == 0

@@ -78,10 +78,13 @@ def test_noalloc_rejects_oversize(cuda_device):
     assert _noalloc(layer, x, out) != 0
     assert "M=32" in _lib.last_error()
     try:
-        _lib.set_option(_lib.OPT_GEMV_CTAS, 16)   # more splits: 16 rows x 16384 x splits fp32 partials
+        # the cp.async GEMV with many splits: 16 rows x 16384 x splits fp32 partials
+        _lib.set_option(_lib.OPT_GEMV_IMPL, 2)
+        _lib.set_option(_lib.OPT_GEMV_CTAS, 16)
         assert _noalloc(layer, x[:16], out[:16]) != 0
         assert "bytes of scratch" in _lib.last_error()
     finally:
-        _lib.set_option(_lib.OPT_GEMV_CTAS, 2)   # the library default
+        _lib.set_option(_lib.OPT_GEMV_CTAS, 2)   # the library defaults
+        _lib.set_option(_lib.OPT_GEMV_IMPL, 1)
     _lib.check(_noalloc(layer, x[:16], out[:16]), "oc_b200_gptq_gemv_noalloc")
     torch.testing.assert_close(out[:16], layer(x[:16]), rtol=0, atol=0)
