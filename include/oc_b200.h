@@ -39,8 +39,9 @@ enum {
   OC_OPT_GEMM_PATH = 1,    /* 0 auto (M<=16 -> split-K GEMV, else tcgen05), 1 force GEMV, 2 force tcgen05 */
   OC_OPT_TC_TILE = 2,      /* tokens per tcgen05 tile: 0 auto, 128, 192, 256, 384, 448 */
   OC_OPT_GEMV_CTAS = 3,    /* GEMV CTAs per SM that split-K sizing fills in one wave (default 2) */
-  OC_OPT_GEMV_IMPL = 4     /* decode kernel for uniform-group layers: 0 tcgen05, 1 TMA + mma.sync (default),
+  OC_OPT_GEMV_IMPL = 4,    /* decode kernel for uniform-group layers: 0 tcgen05, 1 TMA + mma.sync (default),
                               2 cp.async + mma.sync */
+  OC_OPT_TC_PAIR = 5       /* tcgen05 GEMM on CTA pairs (cta_group::2): 0 auto, 1 single CTAs (default), 2 pairs */
 };
 
 /* ---- library / device ------------------------------------------------------ */

@@ -66,14 +66,18 @@ constexpr int kTcChunkBytes = 4 * kTcWarpChunkBytes;   // the four warps' buffer
 
 // BT tokens per MMA (UMMA N) and NSUB sub-tiles per tile: the NSUB sub-tiles of a tile share
 // every dequantized weight stage, so the dequant work per MMA flop falls as 1 / (NSUB * BT).
-template <int BT, int NSUB, int ACC_STAGES, int X_STAGES, int W_STAGES, int A_STAGES>
+// CG = 2: a cluster of two CTAs (one per SM) computes 256 features x the tile's tokens with
+// cta_group::2 MMAs; each CTA dequantizes its own 128 features and holds half of every
+// activation sub-tile (BT / 2 tokens), so the activation traffic per SM halves.
+template <int BT, int NSUB, int ACC_STAGES, int X_STAGES, int W_STAGES, int A_STAGES, int CG = 1>
 struct TcCfg {
   static constexpr int kTileTok = NSUB * BT;
   static constexpr int kAccCols = ACC_STAGES * kTileTok;
   static constexpr int kACols = A_STAGES * (kTcBK / 2);
   static_assert(kAccCols + kACols <= 512, "TMEM budget");
   static_assert(BT % 32 == 0 && BT <= 256, "UMMA N");
-  static constexpr int kXSubBytes = BT * 128;
+  static_assert(CG == 1 || CG == 2, "CTA group");
+  static constexpr int kXSubBytes = BT / CG * 128;  // this CTA's rows of one activation sub-tile
   static constexpr int kXStageBytes = NSUB * kXSubBytes;
   static constexpr int kEpiBytes = kTcEpiBufs * kTcChunkBytes;
   static constexpr int kSmemBytes = X_STAGES * kXStageBytes + W_STAGES * kTcWStageBytes + kEpiBytes +
@@ -82,14 +86,21 @@ struct TcCfg {
   static_assert(kSmemBytes <= 232448, "shared memory per CTA");
 };
 
-template <bool BF16, bool HAS_LO, int BT, int NSUB, int ACC_STAGES, int X_STAGES, int W_STAGES, int A_STAGES>
+template <bool BF16, bool HAS_LO, int BT, int NSUB, int ACC_STAGES, int X_STAGES, int W_STAGES, int A_STAGES,
+          int CG>
 __global__ void __launch_bounds__(kTcThreads, 1)
     gptq_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
                         const __grid_constant__ CUtensorMap tmap_s, const __grid_constant__ CUtensorMap tmap_z,
                         const __grid_constant__ CUtensorMap tmap_c, const __grid_constant__ CUtensorMap tmap_r,
                         const TcParams p) {
-  using Cfg = TcCfg<BT, NSUB, ACC_STAGES, X_STAGES, W_STAGES, A_STAGES>;
+  using Cfg = TcCfg<BT, NSUB, ACC_STAGES, X_STAGES, W_STAGES, A_STAGES, CG>;
   constexpr int kTileTok = Cfg::kTileTok;
+  // CTA pairs: rank 0 (leader) issues the MMAs and owns the full_x / full_a / empty_acc
+  // barriers the pair waits on; both CTAs own their empty_x / empty_a / full_acc barriers,
+  // which the leader's commits reach by multicast.
+  const uint32_t rank = CG == 2 ? cluster_ctarank() : 0u;
+  const bool leader = rank == 0;
+  const int tile0 = blockIdx.x / CG, tile_step = gridDim.x / CG;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* x_smem = smem;
@@ -116,8 +127,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < X_STAGES; ++i) { mbar_init(&full_x[i], 1); mbar_init(&empty_x[i], 1); }
     for (int i = 0; i < W_STAGES; ++i) { mbar_init(&full_w[i], 1); mbar_init(&empty_w[i], 128); }
-    for (int i = 0; i < A_STAGES; ++i) { mbar_init(&full_a[i], 128); mbar_init(&empty_a[i], 1); }
-    for (int i = 0; i < ACC_STAGES; ++i) { mbar_init(&full_acc[i], 1); mbar_init(&empty_acc[i], 128); }
+    // pairs arrive once per warp from each CTA (4 warps x 2), single CTAs once per thread
+    for (int i = 0; i < A_STAGES; ++i) { mbar_init(&full_a[i], CG == 2 ? 8 : 128); mbar_init(&empty_a[i], 1); }
+    for (int i = 0; i < ACC_STAGES; ++i) { mbar_init(&full_acc[i], 1); mbar_init(&empty_acc[i], CG == 2 ? 8 : 128); }
     mbar_init(drain, 1);
     for (int i = 0; i < 4 * kTcEpiBufs; ++i) mbar_init(&res_full[i], 1);
     *abort_flag = 0;
@@ -134,11 +146,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (p.tma_epi && p.residual) tma_prefetch_desc(&tmap_r);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_holder, 512);
-    tmem_relinquish();
+    if (CG == 2) {
+      tmem_alloc_cg2(tmem_holder, 512);
+      tmem_relinquish_cg2();
+    } else {
+      tmem_alloc(tmem_holder, 512);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if (CG == 2)
+    cluster_sync_all();  // both CTAs' barriers are initialised before any cross-CTA arrive / copy
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
 
@@ -149,20 +169,35 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       int x_armed[X_STAGES];
       for (int i = 0; i < X_STAGES; ++i) x_armed[i] = -1;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+      for (int tile = tile0; ok && tile < p.num_tiles; tile += tile_step) {
         const int mb = tile / p.n_tiles_n;
         for (int kb = 0; kb < KB; ++kb, ++it) {
           const int sx = it % X_STAGES, px = (it / X_STAGES) & 1;
           if (!mbar_wait(&empty_x[sx], px ^ 1, abort_flag, kDevErrTmaEmpty)) { ok = false; break; }
-          mbar_arrive_expect_tx(&full_x[sx], Cfg::kXStageBytes);
+          if (CG == 2) {
+            // both CTAs load their half of each sub-tile; the leader's barrier counts both
+            if (leader) mbar_arrive_expect_tx(&full_x[sx], 2 * Cfg::kXStageBytes);
+            const uint32_t bar = mapa_shared(&full_x[sx], 0);
 #pragma unroll
-          for (int sb = 0; sb < NSUB; ++sb)
-            tma_load_2d(x_smem + sx * Cfg::kXStageBytes + sb * Cfg::kXSubBytes, &tmap_x, &full_x[sx], kb * kTcBK,
-                        mb * kTileTok + sb * BT);
+            for (int sb = 0; sb < NSUB; ++sb)
+              tma_load_2d_pair(x_smem + sx * Cfg::kXStageBytes + sb * Cfg::kXSubBytes, &tmap_x, bar, kb * kTcBK,
+                               mb * kTileTok + sb * BT + (int)rank * (BT / 2));
+          } else {
+            mbar_arrive_expect_tx(&full_x[sx], Cfg::kXStageBytes);
+#pragma unroll
+            for (int sb = 0; sb < NSUB; ++sb)
+              tma_load_2d(x_smem + sx * Cfg::kXStageBytes + sb * Cfg::kXSubBytes, &tmap_x, &full_x[sx], kb * kTcBK,
+                          mb * kTileTok + sb * BT);
+          }
           x_armed[sx] = px;
         }
       }
-      if (!ok) {
+      if (CG == 2) {
+        // Our loads signal the leader's barrier, so wait (bounded) until the pair's MMAs have
+        // released every stage we filled: then each of our copies has landed.
+        for (int i = 0; i < X_STAGES; ++i)
+          if (x_armed[i] >= 0) mbar_drain(&empty_x[i], x_armed[i]);
+      } else if (!ok) {
         // drain our own loads in flight before the CTA (and its smem) goes away
         for (int i = 0; i < X_STAGES; ++i)
           if (x_armed[i] >= 0) mbar_drain(&full_x[i], x_armed[i]);
@@ -176,18 +211,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       int w_armed[W_STAGES];
       for (int i = 0; i < W_STAGES; ++i) w_armed[i] = -1;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+      for (int tile = tile0; ok && tile < p.num_tiles; tile += tile_step) {
         const int nb = tile % p.n_tiles_n;
         for (int kb = 0; kb < KB; ++kb, ++it) {
           const int sw = it % W_STAGES, pw = (it / W_STAGES) & 1;
           if (!mbar_wait(&empty_w[sw], pw ^ 1, abort_flag, kDevErrWEmpty)) { ok = false; break; }
           uint8_t* ws = w_smem + sw * kTcWStageBytes;
           mbar_arrive_expect_tx(&full_w[sw], w_tx);
-          tma_load_2d(ws, &tmap_w, &full_w[sw], nb * kTcBN, kb * 8);
+          const int fb = nb * CG + (int)rank;  // this CTA's 128-feature block
+          tma_load_2d(ws, &tmap_w, &full_w[sw], fb * kTcBN, kb * 8);
           if (p.sz_tma) {
             const int row0 = (p.sz_rows == 2) ? kb * 2 : (kb * kTcBK) / p.gs;
-            tma_load_2d(ws + kTcSOff, &tmap_s, &full_w[sw], nb * kTcBN, row0);
-            tma_load_2d(ws + kTcZOff, &tmap_z, &full_w[sw], nb * (kTcBN / 8), row0);
+            tma_load_2d(ws + kTcSOff, &tmap_s, &full_w[sw], fb * kTcBN, row0);
+            tma_load_2d(ws + kTcZOff, &tmap_z, &full_w[sw], fb * (kTcBN / 8), row0);
           }
           w_armed[sw] = pw;
         }
@@ -199,11 +235,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc_f16(BF16, kTcBN, BT);
+    if (lane == 0 && leader) {
+      constexpr uint32_t idesc = make_idesc_f16(BF16, kTcBN * CG, BT);
       int it = 0, tcount = 0;
       bool ok = true, issued = false;
-      for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x, ++tcount) {
+      for (int tile = tile0; ok && tile < p.num_tiles; tile += tile_step, ++tcount) {
         const int sc = tcount % ACC_STAGES, pc = (tcount / ACC_STAGES) & 1;
         if (!mbar_wait(&empty_acc[sc], pc ^ 1, abort_flag, kDevErrAccEmpty)) { ok = false; break; }
         tc_fence_after();
@@ -221,17 +257,31 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
             for (int sb = 0; sb < NSUB; ++sb) {
               const uint64_t bdesc = smem_desc_kmajor_sw128(xaddr + sb * Cfg::kXSubBytes + j * 32);
-              tc_mma_ts(d_tmem + sb * BT, a_tmem + j * 8, bdesc, idesc, (kb | j) != 0 ? 1u : 0u);
+              if (CG == 2)
+                tc_mma_ts_pair(d_tmem + sb * BT, a_tmem + j * 8, bdesc, idesc, (kb | j) != 0 ? 1u : 0u);
+              else
+                tc_mma_ts(d_tmem + sb * BT, a_tmem + j * 8, bdesc, idesc, (kb | j) != 0 ? 1u : 0u);
             }
           issued = true;
-          tc_commit(&empty_x[sx]);
-          tc_commit(&empty_a[sa]);
+          if (CG == 2) {
+            tc_commit_pair(&empty_x[sx], 0x3);
+            tc_commit_pair(&empty_a[sa], 0x3);
+          } else {
+            tc_commit(&empty_x[sx]);
+            tc_commit(&empty_a[sa]);
+          }
         }
         if (!ok) break;
-        tc_commit(&full_acc[sc]);
+        if (CG == 2)
+          tc_commit_pair(&full_acc[sc], 0x3);
+        else
+          tc_commit(&full_acc[sc]);
       }
       if (!ok && issued) {
-        tc_commit(drain);
+        if (CG == 2)
+          tc_commit_pair(drain, 0x1);
+        else
+          tc_commit(drain);
         mbar_drain(drain, 0);
       }
     }
@@ -244,9 +294,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int kw_rows = p.Kp >> 3;
     int it = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+    for (int tile = tile0; ok && tile < p.num_tiles; tile += tile_step) {
       const int nb = tile % p.n_tiles_n;
-      const int n = nb * kTcBN + row;
+      const int n = (nb * CG + (int)rank) * kTcBN + row;
       const int nn = n < p.N ? n : 0;
       const int zsh = 4 * (nn & 7);
       for (int kb = 0; kb < KB; ++kb, ++it) {
@@ -322,7 +372,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         tmem_st_32x32b_x32(taddr, r32);
         tc_wait_st();
         tc_fence_before();
-        mbar_arrive(&full_a[sa]);
+        if (CG == 2) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(mapa_shared(&full_a[sa], 0));
+        } else {
+          mbar_arrive(&full_a[sa]);
+        }
       }
     }
   } else if (warp >= kTcEpiWarp0 && p.tma_epi) {
@@ -347,10 +402,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       res_pend |= 1u << b;
       res_par = (res_par & ~(1u << b)) | (((qq >> 2) & 1u) << b);
     };
-    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++tcount) {
+    for (int tile = tile0; tile < p.num_tiles; tile += tile_step, ++tcount) {
       const int sc = tcount % ACC_STAGES, pc = (tcount / ACC_STAGES) & 1;
       const int nb = tile % p.n_tiles_n, mb = tile / p.n_tiles_n;
-      const int f0 = nb * kTcBN + q4 * 32;  // this warp's first feature
+      const int f0 = (nb * CG + (int)rank) * kTcBN + q4 * 32;  // this warp's first feature
       const int n = f0 + lane;
       const int m_base = mb * kTileTok;
       const int nchunks = min(kChunks, (p.M - m_base + 31) / 32);  // chunks holding rows < M
@@ -401,7 +456,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       if (failed) break;
       tc_fence_before();
-      mbar_arrive(&empty_acc[sc]);  // this warp has read its accumulator lanes
+      if (CG == 2) {  // this warp has read its accumulator lanes
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(mapa_shared(&empty_acc[sc], 0));
+      } else {
+        mbar_arrive(&empty_acc[sc]);
+      }
     }
     if (lane == 0) {
       bulk_wait_group0();
@@ -415,10 +475,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int row = q4 * 32 + lane;
     const int odt = BF16 ? kBF16 : kF16;
     int tcount = 0;
-    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++tcount) {
+    for (int tile = tile0; tile < p.num_tiles; tile += tile_step, ++tcount) {
       const int sc = tcount % ACC_STAGES, pc = (tcount / ACC_STAGES) & 1;
       const int nb = tile % p.n_tiles_n, mb = tile / p.n_tiles_n;
-      const int n = nb * kTcBN + row;
+      const int n = (nb * CG + (int)rank) * kTcBN + row;
       const bool nvalid = n < p.N;
       const float bv = (p.bias && nvalid) ? load_as_f32(p.bias, p.bias_dtype, n) : 0.f;
       if (!mbar_wait(&full_acc[sc], pc, abort_flag, kDevErrAccFull)) break;
@@ -459,16 +519,27 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
       }
       tc_fence_before();
-      mbar_arrive(&empty_acc[sc]);
+      if (CG == 2) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(mapa_shared(&empty_acc[sc], 0));
+      } else {
+        mbar_arrive(&empty_acc[sc]);
+      }
     }
   }
 
   tc_fence_before();
-  __syncthreads();
+  if (CG == 2)
+    cluster_sync_all();  // neither CTA leaves (or frees TMEM) while the pair's MMAs / arrivals may touch it
+  else
+    __syncthreads();
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem_base, 512);
+    if (CG == 2)
+      tmem_dealloc_cg2(tmem_base, 512);
+    else
+      tmem_dealloc(tmem_base, 512);
   }
 }
 

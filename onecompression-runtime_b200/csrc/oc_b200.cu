@@ -46,7 +46,7 @@ bool dt16(int dt) { return dt == OC_DT_F16 || dt == OC_DT_BF16; }
 bool dtf(int dt) { return dt == OC_DT_F16 || dt == OC_DT_BF16 || dt == OC_DT_F32; }
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
-std::atomic<int> g_opt_path{0}, g_opt_tile{0}, g_opt_gemv_ctas{2}, g_opt_gemv_impl{1};
+std::atomic<int> g_opt_path{0}, g_opt_tile{0}, g_opt_gemv_ctas{2}, g_opt_gemv_impl{1}, g_opt_tc_pair{1};
 
 constexpr int kMaxDevices = 64;
 int g_sm_count[kMaxDevices];
@@ -182,6 +182,10 @@ int oc_b200_set_option(int key, int value) {
     case OC_OPT_GEMV_CTAS:
       if (value < 1 || value > 32) return fail(OC_ERR_INVALID, "OC_OPT_GEMV_CTAS: %d", value);
       g_opt_gemv_ctas = value;
+      return OC_OK;
+    case OC_OPT_TC_PAIR:
+      if (value < 0 || value > 2) return fail(OC_ERR_INVALID, "OC_OPT_TC_PAIR: %d", value);
+      g_opt_tc_pair = value;
       return OC_OK;
     case OC_OPT_GEMV_IMPL:
       if (value < 0 || value > 2) return fail(OC_ERR_INVALID, "OC_OPT_GEMV_IMPL: %d", value);
@@ -495,6 +499,15 @@ int choose_tile(int64_t M, int n_tiles_n, int sms) {
   return best;
 }
 
+// CTA pairs for the tcgen05 GEMM: 1 single CTAs (default, measured faster), 2 pairs, 0 auto
+// (pairs for tiles of 256 tokens and more).
+bool use_pairs(int64_t M, int bt) {
+  const int v = g_opt_tc_pair.load();
+  if (v == 2) return true;
+  if (v == 1) return false;
+  return M >= 256 && bt >= 256;
+}
+
 bool use_gemv(int64_t M) {
   const int path = g_opt_path.load();
   if (path == 1) return M <= 16;
@@ -623,10 +636,10 @@ struct TcMaps {
   CUtensorMap x, c, r;
 };
 
-template <bool BF16, bool HAS_LO, int BT, int NSUB, int ACC, int XS, int WS, int AS>
+template <bool BF16, bool HAS_LO, int BT, int NSUB, int ACC, int XS, int WS, int AS, int CG = 1>
 int launch_tc_t(const TcMaps& tm, const oc_b200_layer* L, const oc::TcParams& p, int dev, cudaStream_t stream) {
-  using Cfg = oc::TcCfg<BT, NSUB, ACC, XS, WS, AS>;
-  auto kern = oc::gptq_gemm_tc_kernel<BF16, HAS_LO, BT, NSUB, ACC, XS, WS, AS>;
+  using Cfg = oc::TcCfg<BT, NSUB, ACC, XS, WS, AS, CG>;
+  auto kern = oc::gptq_gemm_tc_kernel<BF16, HAS_LO, BT, NSUB, ACC, XS, WS, AS, CG>;
   static bool attr_set[kMaxDevices] = {};
   if (dev >= 0 && dev < kMaxDevices && !attr_set[dev]) {
     std::lock_guard<std::mutex> lk(g_mu);
@@ -635,15 +648,42 @@ int launch_tc_t(const TcMaps& tm, const oc_b200_layer* L, const oc::TcParams& p,
       return rc;
     attr_set[dev] = true;
   }
-  int grid = p.num_tiles < sm_count(dev) ? p.num_tiles : sm_count(dev);
-  kern<<<grid, oc::kTcThreads, Cfg::kSmemBytes, stream>>>(tm.x, L->tmap_w, L->tmap_s, L->tmap_z, tm.c, tm.r, p);
-  return launch_check("gptq_gemm_tc");
+  if (CG == 1) {
+    int grid = p.num_tiles < sm_count(dev) ? p.num_tiles : sm_count(dev);
+    kern<<<grid, oc::kTcThreads, Cfg::kSmemBytes, stream>>>(tm.x, L->tmap_w, L->tmap_s, L->tmap_z, tm.c, tm.r, p);
+    return launch_check("gptq_gemm_tc");
+  }
+  // CTA pairs: clusters of two, one pair tile (256 features) at a time
+  const int pairs = sm_count(dev) / 2;
+  const int grid = 2 * (p.num_tiles < pairs ? p.num_tiles : pairs);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(oc::kTcThreads);
+  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (int rc = cuda_check(cudaLaunchKernelEx(&cfg, kern, tm.x, L->tmap_w, L->tmap_s, L->tmap_z, tm.c, tm.r, p),
+                          "gptq_gemm_tc (pairs)"))
+    return rc;
+  return launch_check("gptq_gemm_tc (pairs)");
 }
 
 // Tile presets (tokens per tile, accumulators, activation / weight / TMEM-A stages), sized to
 // 512 TMEM columns and the 227 KB of shared memory with the epilogue staging tile.
 template <bool BF16, bool HAS_LO>
-int launch_tc(int bt, const TcMaps& tm, const oc_b200_layer* L, const oc::TcParams& p, int dev, cudaStream_t stream) {
+int launch_tc(int bt, bool pair, const TcMaps& tm, const oc_b200_layer* L, const oc::TcParams& p, int dev,
+              cudaStream_t stream) {
+  if (pair) {  // per CTA: half of each sub-tile's tokens, so the activation stages are half as large
+    if (bt == 256) return launch_tc_t<BF16, HAS_LO, 256, 1, 1, 8, 8, 4, 2>(tm, L, p, dev, stream);
+    if (bt == 448) return launch_tc_t<BF16, HAS_LO, 224, 2, 1, 5, 4, 2, 2>(tm, L, p, dev, stream);
+    return launch_tc_t<BF16, HAS_LO, 192, 2, 1, 6, 8, 4, 2>(tm, L, p, dev, stream);
+  }
   if (bt == 128) return launch_tc_t<BF16, HAS_LO, 128, 1, 2, 8, 8, 8>(tm, L, p, dev, stream);
   if (bt == 256) return launch_tc_t<BF16, HAS_LO, 256, 1, 1, 5, 6, 4>(tm, L, p, dev, stream);
   if (bt == 384) return launch_tc_t<BF16, HAS_LO, 192, 2, 1, 3, 8, 4>(tm, L, p, dev, stream);
@@ -738,7 +778,10 @@ extern "C" int oc_b200_gptq_gemm_ex(const oc_b200_layer* L, const void* a, int a
   const CUtensorMapDataType tdt = bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   TcMaps tm;
   std::memset(&tm, 0, sizeof(tm));
-  const int sub_rows = bt > 256 ? bt / 2 : bt;  // tokens per MMA (tiles of 384 / 448 are two sub-tiles)
+  const bool pair = use_pairs(M, bt);
+  if (pair && bt != 256 && bt != 384 && bt != 448) bt = 384;
+  // rows per activation box: tokens per MMA (tiles of 384 / 448 are two sub-tiles), halved for pairs
+  const int sub_rows = (bt > 256 ? bt / 2 : bt) / (pair ? 2 : 1);
   if (int rc = make_tmap_2d(&tm.x, tdt, 2, xk, (uint64_t)L->Kp, (uint64_t)M, (uint64_t)ldx * 2, oc::kTcBK,
                             (uint32_t)sub_rows, CU_TENSOR_MAP_SWIZZLE_128B))
     return rc;
@@ -778,13 +821,13 @@ extern "C" int oc_b200_gptq_gemm_ex(const oc_b200_layer* L, const void* a, int a
   p.out = reinterpret_cast<uint16_t*>(c);
   p.ldc = ldc;
   p.tma_epi = tma_epi ? 1 : 0;
-  p.n_tiles_n = (L->N + oc::kTcBN - 1) / oc::kTcBN;
+  p.n_tiles_n = (L->N + oc::kTcBN * (pair ? 2 : 1) - 1) / (oc::kTcBN * (pair ? 2 : 1));
   p.n_tiles_m = (int)((M + bt - 1) / bt);
   p.num_tiles = p.n_tiles_n * p.n_tiles_m;
-  if (bf16) return has_lo ? launch_tc<true, true>(bt, tm, L, p, dev, stream)
-                          : launch_tc<true, false>(bt, tm, L, p, dev, stream);
-  return has_lo ? launch_tc<false, true>(bt, tm, L, p, dev, stream)
-                : launch_tc<false, false>(bt, tm, L, p, dev, stream);
+  if (bf16) return has_lo ? launch_tc<true, true>(bt, pair, tm, L, p, dev, stream)
+                          : launch_tc<true, false>(bt, pair, tm, L, p, dev, stream);
+  return has_lo ? launch_tc<false, true>(bt, pair, tm, L, p, dev, stream)
+                : launch_tc<false, false>(bt, pair, tm, L, p, dev, stream);
 }
 
 

@@ -22,6 +22,7 @@ OPT_GEMM_PATH = 1
 OPT_TC_TILE = 2
 OPT_GEMV_CTAS = 3
 OPT_GEMV_IMPL = 4
+OPT_TC_PAIR = 5
 ACT_NONE = 0
 ACT_GELU_TANH = 1
 

@@ -285,3 +285,54 @@ def test_gemv_impls(cuda_device, impl, shape):
     errf = float((yf.double() - reff).abs().max() / reff.abs().max())
     assert errf < 1e-2, errf
     assert _lib.read_device_error(cuda_device) == 0
+
+
+@pytest.fixture
+def pair_option():
+    from onecomp_runtime import _lib
+    yield lambda v: _lib.set_option(_lib.OPT_TC_PAIR, v)
+    _lib.set_option(_lib.OPT_TC_PAIR, 1)
+
+
+@pytest.mark.parametrize("tile", [256, 384, 448])
+@pytest.mark.parametrize("M", [200, 1000])
+def test_tc_pairs(cuda_device, tile, M, path_option, pair_option):
+    """The tcgen05 GEMM on CTA pairs (cta_group::2, 256 features per pair tile, half of each
+    activation sub-tile per CTA): plain and residual + GELU epilogues, partial last tiles, a
+    pair tile whose second half lies past N."""
+    from onecomp_runtime import _lib
+    from onecomp_runtime.testing import gptq_layer, activations
+    path_option(2)
+    pair_option(2)
+    _lib.set_option(_lib.OPT_TC_TILE, tile)
+    K, N = 768, 384
+    t = {k: v.to(cuda_device) for k, v in gptq_layer(K, N, 32, seed=3 * tile + M).items()}
+    layer = _module(t, K, N, 32, True, "fused", cuda_device)
+    x = activations(M, K, seed=M + 1).to(cuda_device)
+    r = activations(M, N, seed=M + 9).to(cuda_device)
+    ref = _gpu_reference(t, K, N, x, True, t["bias"])
+    y = layer(x)
+    err = float((y.double() - ref).abs().max() / ref.abs().max())
+    assert err < 1e-2, err
+    yf = layer.forward_fused(x, residual=r, activation="gelu_tanh")
+    reff = torch.nn.functional.gelu(ref, approximate="tanh") + r.double()
+    errf = float((yf.double() - reff).abs().max() / reff.abs().max())
+    assert errf < 1e-2, errf
+    assert _lib.read_device_error(cuda_device) == 0
+
+
+def test_tc_pairs_full_size(cuda_device, pair_option):
+    """Config-1 qkv layer at M = 4608 on CTA pairs vs a torch fp32 GEMM of the exact weight."""
+    from onecomp_runtime import _lib, quant_utils
+    from onecomp_runtime.testing import gptq_layer, activations
+    pair_option(2)
+    K, N, M = 3072, 9216, 4608
+    t = {k: v.to(cuda_device) for k, v in gptq_layer(K, N, 32, seed=78, device="cpu").items()}
+    layer = _module(t, K, N, 32, True, "fused", cuda_device)
+    x = activations(M, K, seed=4).to(cuda_device)
+    y = layer(x)
+    w = quant_utils.dequant_gptq_to_fp(t["qweight"], t["scales"], t["qzeros"], t["g_idx"], K, N, torch.bfloat16)
+    ref = x.float() @ w.float().t() + t["bias"].float()
+    err = float((y.float() - ref).abs().max() / ref.abs().max())
+    assert err < 1e-2, err
+    assert _lib.read_device_error(cuda_device) == 0
