@@ -32,6 +32,7 @@ import os
 import subprocess
 import sys
 import tempfile
+import threading
 import time
 from pathlib import Path
 
@@ -64,7 +65,8 @@ def load_peaks() -> dict:
 
 # ----------------------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi clocks/throttle sampling during the timed region."""
+    """SM clock / throttle-reason sampling during the timed region: NVML polled every 5 ms from a
+    thread (reads only; no GPU setting is changed), nvidia-smi at 100 ms if NVML is missing."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -74,8 +76,32 @@ class ClockSampler:
         self.index = index
         self.proc = None
         self.file = None
+        self.thread = None
+        self.rows = []
+        self.stop_evt = threading.Event()
+
+    def _nvml_loop(self, nv, h):
+        names = (("hw_slowdown", nv.nvmlClocksEventReasonHwSlowdown),
+                 ("hw_thermal_slowdown", nv.nvmlClocksEventReasonHwThermalSlowdown),
+                 ("sw_thermal_slowdown", nv.nvmlClocksEventReasonSwThermalSlowdown),
+                 ("sw_power_cap", nv.nvmlClocksEventReasonSwPowerCap))
+        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        while not self.stop_evt.is_set():
+            sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+            bits = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+            self.rows.append((sm, mx, [n for n, b in names if bits & b]))
+            self.stop_evt.wait(0.005)
 
     def start(self):
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            h = nv.nvmlDeviceGetHandleByIndex(self.index)
+            self.thread = threading.Thread(target=self._nvml_loop, args=(nv, h), daemon=True)
+            self.thread.start()
+            return
+        except Exception:
+            self.thread = None
         try:
             self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
             self.proc = subprocess.Popen(
@@ -85,6 +111,15 @@ class ClockSampler:
             self.proc = None
 
     def stop(self) -> dict | None:
+        if self.thread is not None:
+            self.stop_evt.set()
+            self.thread.join(timeout=5)
+            if not self.rows:
+                return None
+            sm = [r[0] for r in self.rows]
+            reasons = sorted({n for r in self.rows for n in r[2]})
+            return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": float(max(r[1] for r in self.rows)),
+                    "reasons": reasons, "samples": len(self.rows), "source": "nvml 5 ms"}
         if self.proc is None:
             return None
         self.proc.terminate()
@@ -107,7 +142,7 @@ class ClockSampler:
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in rows for i in range(4) if "Active" in r[5 + i] and "Not" not in r[5 + i]})
         return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows)}
+                "reasons": reasons, "samples": len(rows), "source": "nvidia-smi 100 ms"}
 
 
 # ----------------------------------------------------------------------------- model
@@ -405,7 +440,7 @@ def bench_tp(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--workload", default="cfg1", choices=["cfg1", "cfg2", "cfg3", "cfg4"],
@@ -502,22 +537,51 @@ def main():
         gemm = [(s.elapsed_time(e), fl) for s, e, fl in stack.gemm_events]
         stack.gemm_events = None
 
-        # ---- end-to-end through the module API with host buffers
-        x_host = torch.empty((M, CFG1["hidden"]), dtype=torch.bfloat16, pin_memory=True)
-        x_host.copy_(x.cpu())
-        y_host = torch.empty((M, CFG1["hidden"]), dtype=torch.bfloat16, pin_memory=True)
-        for _ in range(2):
-            y_host.copy_(stack.forward(x_host.to(dev, non_blocking=True)), non_blocking=True)
+        # ---- end-to-end through the module API with host buffers: every step copies its input
+        # from pinned host memory and reads its result back; the copies of step i+1 / i-1 run on
+        # their own streams while step i computes (double-buffered device and host tensors)
+        shape = (M, CFG1["hidden"])
+        x_host = [torch.empty(shape, dtype=torch.bfloat16, pin_memory=True) for _ in range(2)]
+        y_host = [torch.empty(shape, dtype=torch.bfloat16, pin_memory=True) for _ in range(2)]
+        for b in range(2):
+            x_host[b].copy_(x.cpu())
+        x_dev = [torch.empty(shape, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+        main = torch.cuda.current_stream(dev)
+        s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        in_ready = [torch.cuda.Event() for _ in range(2)]
+        in_free = [torch.cuda.Event() for _ in range(2)]
+        out_ready = [torch.cuda.Event() for _ in range(2)]
+
+        def e2e_steps(n):
+            for i in range(n):
+                b = i & 1
+                with torch.cuda.stream(s_in):
+                    if i >= 2:
+                        s_in.wait_event(in_free[b])
+                    x_dev[b].copy_(x_host[b], non_blocking=True)
+                    in_ready[b].record(s_in)
+                main.wait_event(in_ready[b])
+                y = stack.forward(x_dev[b])
+                in_free[b].record(main)
+                out_ready[b].record(main)
+                with torch.cuda.stream(s_out):
+                    s_out.wait_event(out_ready[b])
+                    y_host[b].copy_(y, non_blocking=True)
+                    y.record_stream(s_out)
+            main.wait_stream(s_in)
+            main.wait_stream(s_out)
+
+        e2e_steps(2)
         barrier()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(args.steps):
-            xd = x_host.to(dev, non_blocking=True)
-            y_host.copy_(stack.forward(xd), non_blocking=True)
-        e1.record()
+        e0.record(main)
+        e2e_steps(args.steps)
+        e1.record(main)
         barrier()
         ms_e2e = e0.elapsed_time(e1)
+        if not torch.equal(y_host[(args.steps - 1) & 1], y.cpu()):
+            raise RuntimeError("end-to-end output differs from the device-timed output")
 
     t = torch.tensor([ms_total, ms_e2e], device=dev)
     if world > 1:
