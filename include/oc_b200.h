@@ -73,11 +73,20 @@ int oc_b200_gptq_dequant(const int32_t* qweight, const int32_t* qzeros, const vo
                          const int64_t* g_idx, int K, int N, int G, int groupsize, int wbits, int v1, void* out,
                          int out_dtype, oc_stream_t stream);
 /* Replaces quant_utils.dequant_extra_u8_to_weight (quant_utils.py:72-103),
- * bit-exact including its two roundings in the output dtype. qweight_u8 is
- * [N, ld_bytes] (low nibble = even k); scales/zeros [N, G] of any float dtype. */
+ * bit-exact including its roundings in the output dtype (f16, bf16 or f32).
+ * qweight_u8 is [N, ld_bytes] (low nibble = even k); scales/zeros [N, G] f16/bf16/f32. */
 int oc_b200_rtn_dequant(const uint8_t* qweight_u8, int64_t ld_bytes, const void* scales, int scales_dtype,
                         const void* zeros, int zeros_dtype, int K, int N, int G, void* out, int out_dtype,
                         oc_stream_t stream);
+/* Replaces PackedEmbedding.forward (packed_linear.py:92-104: three row gathers, then
+ * dequant_extra_u8_to_weight): out[i, :] = the RTN-dequantized row ids[i] of a packed table
+ * qweight_u8 [vocab, ld_bytes] with scales/zeros [vocab, G], bit-exact with the reference.
+ * Negative ids count from the end of the table; ids outside [-vocab, vocab) give a zero row
+ * and set the device error word (read with oc_b200_read_device_error). out_dtype f16, bf16
+ * or f32 (the reference returns the scales' dtype). */
+int oc_b200_rtn_embedding(const int64_t* ids, int64_t n_ids, int64_t vocab, const uint8_t* qweight_u8,
+                          int64_t ld_bytes, const void* scales, int scales_dtype, const void* zeros, int zeros_dtype,
+                          int dim, int G, void* out, int out_dtype, oc_stream_t stream);
 /* Replaces layers/dsv4_packed_linear.dequant_dsv4_packed (dsv4_packed_linear.py:22-56),
  * bit-exact. packed is [N, ld_bytes], 8/wbits codes per byte (code j at bits
  * j*wbits). scales/zeros element (n, g) sits at n*stride_n + g*stride_g

@@ -39,6 +39,7 @@ enum : unsigned {
   kDevErrWEmpty = 0x108,
   kDevErrDrain = 0x109,
   kDevErrResFull = 0x10a,
+  kDevErrIndex = 0x301,   // embedding id outside the table
   kDevErrSplitK = 0x201,
 };
 

@@ -3,6 +3,7 @@
 // All dequant kernels reproduce the reference's rounding exactly:
 //  * GPTQ  (quant_utils.py:50-69)          w = RNE_out( f32(s) * (f32(q) - f32(z)) )  -- one rounding
 //  * RTN   (quant_utils.py:72-103)         d = RNE_out(q - RNE_out(z)); w = RNE_out(d * RNE_out(s))
+//                                          (fp32 output: w = f32(f32(q - z) * s))
 //  * DSV4  (dsv4_packed_linear.py:22-56)   w = RNE_out( f32(f32(q) - z) * s )      -- fp32 ops, one cast
 #pragma once
 
@@ -169,11 +170,24 @@ __global__ void permute_cols_kernel(const uint16_t* __restrict__ x, long long ld
 }
 
 // --- RTN uint8-nibble dequant (a11) ----------------------------------------------------
-// qweight_u8 [N, ldq] bytes: low nibble = even k. scales/zeros [N, G] (any float dtype).
-// Arithmetic in the output dtype with a rounding after each op, like torch bf16/fp16 ops.
+// One element of torch's (q.to(dt) - z.to(dt)) * s.to(dt): for 16-bit dt a rounding after
+// each cast and op; for fp32 the casts are exact and each op rounds once.
+__device__ __forceinline__ void rtn_store(void* out, long long i, float qv, float zv, float sv, int out_dtype) {
+  if (out_dtype == kF32) {
+    static_cast<float*>(out)[i] = __fmul_rn(__fsub_rn(qv, zv), sv);
+    return;
+  }
+  const float zo = bits_to_f32(f32_to_bits(zv, out_dtype), out_dtype);
+  const float so = bits_to_f32(f32_to_bits(sv, out_dtype), out_dtype);
+  const float d = bits_to_f32(f32_to_bits(__fsub_rn(qv, zo), out_dtype), out_dtype);
+  static_cast<uint16_t*>(out)[i] = f32_to_bits(__fmul_rn(d, so), out_dtype);
+}
+
+// qweight_u8 [N, ldq] bytes: low nibble = even k. scales/zeros [N, G] (f16/bf16/f32);
+// output f16, bf16 or f32.
 __global__ void rtn_dequant_kernel(const uint8_t* __restrict__ q, long long ldq, const void* __restrict__ s,
                                    int s_dtype, const void* __restrict__ z, int z_dtype, int K, int N, int G,
-                                   uint16_t* __restrict__ out, int out_dtype) {
+                                   void* __restrict__ out, int out_dtype) {
   const long long total = (long long)N * K;
   const int gs = K / G;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
@@ -182,10 +196,37 @@ __global__ void rtn_dequant_kernel(const uint8_t* __restrict__ q, long long ldq,
     const uint8_t b = q[(long long)n * ldq + (k >> 1)];
     const float qv = (float)((k & 1) ? (b >> 4) : (b & 0xF));
     const int g = (G == 1) ? 0 : (k / gs);
-    const float zo = bits_to_f32(f32_to_bits(load_as_f32(z, z_dtype, (long long)n * G + g), out_dtype), out_dtype);
-    const float so = bits_to_f32(f32_to_bits(load_as_f32(s, s_dtype, (long long)n * G + g), out_dtype), out_dtype);
-    const float d = bits_to_f32(f32_to_bits(__fsub_rn(qv, zo), out_dtype), out_dtype);
-    out[i] = f32_to_bits(__fmul_rn(d, so), out_dtype);
+    const long long si = (long long)n * G + g;
+    rtn_store(out, i, qv, load_as_f32(z, z_dtype, si), load_as_f32(s, s_dtype, si), out_dtype);
+  }
+}
+
+// --- RTN packed embedding: gather + dequant ------------------------------------------
+// out[i, k] = dequant of row ids[i] of the table (same arithmetic as rtn_dequant_kernel).
+// Negative ids count from the end of the table, as torch indexing does; an id outside
+// [-vocab, vocab) records kDevErrIndex and yields a zero row (no out-of-bounds read).
+__global__ void rtn_embedding_kernel(const int64_t* __restrict__ ids, long long n_ids, long long vocab,
+                                     const uint8_t* __restrict__ q, long long ldq, const void* __restrict__ s,
+                                     int s_dtype, const void* __restrict__ z, int z_dtype, int K, int G,
+                                     void* __restrict__ out, int out_dtype) {
+  const long long total = n_ids * K;
+  const int gs = K / G;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / K;
+    const int k = (int)(i % K);
+    long long n = ids[r];
+    if (n < 0) n += vocab;
+    if (n < 0 || n >= vocab) {
+      if (k == 0) record_error(kDevErrIndex);
+      if (out_dtype == kF32) static_cast<float*>(out)[i] = 0.f;
+      else static_cast<uint16_t*>(out)[i] = 0;
+      continue;
+    }
+    const uint8_t b = q[n * ldq + (k >> 1)];
+    const float qv = (float)((k & 1) ? (b >> 4) : (b & 0xF));
+    const int g = (G == 1) ? 0 : (k / gs);
+    rtn_store(out, i, qv, load_as_f32(z, z_dtype, n * G + g), load_as_f32(s, s_dtype, n * G + g), out_dtype);
   }
 }
 

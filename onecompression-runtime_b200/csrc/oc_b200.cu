@@ -284,13 +284,29 @@ int oc_b200_rtn_dequant(const uint8_t* qweight_u8, int64_t ld_bytes, const void*
   if (K <= 0 || N <= 0 || G <= 0 || ld_bytes * 2 < K) return fail(OC_ERR_INVALID, "rtn_dequant: shape");
   if (G != 1 && K % G != 0)
     return fail(OC_ERR_INVALID, "in_features=%d not divisible by num_groups=%d", K, G);
-  if (!dtf(scales_dtype) || !dtf(zeros_dtype) || !dt16(out_dtype)) return fail(OC_ERR_INVALID, "rtn_dequant: dtype");
+  if (!dtf(scales_dtype) || !dtf(zeros_dtype) || !dtf(out_dtype)) return fail(OC_ERR_INVALID, "rtn_dequant: dtype");
   int dev = 0;
   if (int rc = current_device(&dev)) return rc;
   oc::rtn_dequant_kernel<<<grid_1d((long long)N * K, 256, dev), 256, 0, stream>>>(
-      qweight_u8, ld_bytes, scales, scales_dtype, zeros, zeros_dtype, K, N, G, reinterpret_cast<uint16_t*>(out),
-      out_dtype);
+      qweight_u8, ld_bytes, scales, scales_dtype, zeros, zeros_dtype, K, N, G, out, out_dtype);
   return launch_check("rtn_dequant");
+}
+
+int oc_b200_rtn_embedding(const int64_t* ids, int64_t n_ids, int64_t vocab, const uint8_t* qweight_u8,
+                          int64_t ld_bytes, const void* scales, int scales_dtype, const void* zeros, int zeros_dtype,
+                          int dim, int G, void* out, int out_dtype, oc_stream_t stream) {
+  if (n_ids < 0 || vocab <= 0 || dim <= 0 || G <= 0 || ld_bytes * 2 < dim)
+    return fail(OC_ERR_INVALID, "rtn_embedding: shape");
+  if (n_ids == 0) return OC_OK;
+  if (!ids || !qweight_u8 || !scales || !zeros || !out) return fail(OC_ERR_INVALID, "rtn_embedding: NULL pointer");
+  if (G != 1 && dim % G != 0)
+    return fail(OC_ERR_INVALID, "in_features=%d not divisible by num_groups=%d", dim, G);
+  if (!dtf(scales_dtype) || !dtf(zeros_dtype) || !dtf(out_dtype)) return fail(OC_ERR_INVALID, "rtn_embedding: dtype");
+  int dev = 0;
+  if (int rc = current_device(&dev)) return rc;
+  oc::rtn_embedding_kernel<<<grid_1d((long long)n_ids * dim, 256, dev), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      ids, n_ids, vocab, qweight_u8, ld_bytes, scales, scales_dtype, zeros, zeros_dtype, dim, G, out, out_dtype);
+  return launch_check("rtn_embedding");
 }
 
 int oc_b200_dsv4_dequant(const uint8_t* packed, int64_t ld_bytes, int wbits, const void* scales, int scales_dtype,

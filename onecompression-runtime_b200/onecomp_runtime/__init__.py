@@ -18,12 +18,16 @@ from .layers import (
     FusedInt4Linear,
     FusedInt4LinearAnyGroup,
     FusedInt4LinearPaddedGroups,
+    GemLiteInt4Linear,
     PackedEmbedding,
     PackedGPTQLinear,
+    PackedInt4Conv1d,
+    PackedInt4ConvTranspose1d,
     PackedRTNLinear,
     dequant_dsv4_packed,
     fused_int4_gemm,
     gemlite_available,
+    replace_conv_with_packed,
 )
 
 __version__ = "0.1.0+b200"
@@ -35,7 +39,11 @@ __all__ = [
     "FusedInt4LinearPaddedGroups",
     "fused_int4_gemm",
     "gemlite_available",
+    "GemLiteInt4Linear",
     "PackedGPTQLinear",
+    "PackedInt4Conv1d",
+    "PackedInt4ConvTranspose1d",
+    "replace_conv_with_packed",
     "PackedRTNLinear",
     "PackedEmbedding",
     "Dsv4PackedLinear",

@@ -46,6 +46,7 @@ _SIGNATURES = {
     "oc_b200_gptq_pack": ([_p, _i, _i, _i, _p, _p], _i),
     "oc_b200_gptq_dequant": ([_p, _p, _p, _i, _p, _i, _i, _i, _i, _i, _i, _p, _i, _p], _i),
     "oc_b200_rtn_dequant": ([_p, _i64, _p, _i, _p, _i, _i, _i, _i, _p, _i, _p], _i),
+    "oc_b200_rtn_embedding": ([_p, _i64, _i64, _p, _i64, _p, _i, _p, _i, _i, _i, _p, _i, _p], _i),
     "oc_b200_dsv4_dequant": ([_p, _i64, _i, _p, _i, _p, _i, _i64, _i64, _i, _i, _i, _p, _i, _p], _i),
     "oc_b200_gptq_repack_k": ([_p, _p, _i, _i, _p, _p], _i),
     "oc_b200_permute_cols": ([_p, _i64, _i64, _i, _p, _i, _p, _p], _i),

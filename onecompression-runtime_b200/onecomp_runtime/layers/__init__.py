@@ -5,10 +5,11 @@
 - :class:`FusedInt4LinearAnyGroup` / :class:`FusedInt4LinearPaddedGroups` -- other groupsizes;
 - :class:`PackedGPTQLinear` -- 4/8-bit, any groupsize, act-order, v1/v2;
 - :class:`PackedRTNLinear` / :class:`PackedEmbedding` -- RTN uint8-nibble layers;
-- :class:`Dsv4PackedLinear` / :func:`dequant_dsv4_packed` -- int4/int2 byte-packed layers.
+- :class:`Dsv4PackedLinear` / :func:`dequant_dsv4_packed` -- int4/int2 byte-packed layers;
+- :class:`PackedInt4Conv1d` / :class:`PackedInt4ConvTranspose1d` and the conv codec helpers.
 
-The GemLite wrappers and the int4 conv codecs of the reference are not part of
-this build (``gemlite_available()`` reports whether GemLite is importable).
+GemLite is not part of this build: ``GemLiteInt4Linear`` imports but raises on construction
+and ``gemlite_available()`` reports whether GemLite is importable.
 """
 from __future__ import annotations
 
@@ -19,16 +20,16 @@ from .fused_int4_linear import (
     FusedInt4LinearPaddedGroups,
     fused_int4_gemm,
 )
+from .gemlite_int4_linear import GemLiteInt4Linear, gemlite_available
+from .packed_conv import (
+    PackedInt4Conv1d,
+    PackedInt4ConvTranspose1d,
+    quantize_conv_module,
+    quantize_conv_weight,
+    replace_conv_with_packed,
+)
 from .packed_gptq_linear import PackedGPTQLinear
 from .packed_linear import PackedEmbedding, PackedRTNLinear
-
-
-def gemlite_available() -> bool:
-    try:
-        import gemlite  # noqa: F401
-    except Exception:
-        return False
-    return True
 
 
 __all__ = [
@@ -37,6 +38,12 @@ __all__ = [
     "FusedInt4LinearPaddedGroups",
     "fused_int4_gemm",
     "gemlite_available",
+    "GemLiteInt4Linear",
+    "PackedInt4Conv1d",
+    "PackedInt4ConvTranspose1d",
+    "quantize_conv_module",
+    "quantize_conv_weight",
+    "replace_conv_with_packed",
     "PackedGPTQLinear",
     "PackedRTNLinear",
     "PackedEmbedding",

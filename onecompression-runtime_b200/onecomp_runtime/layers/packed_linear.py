@@ -20,6 +20,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
+from .. import _lib
 from ..quant_utils import dequant_extra_u8_to_weight
 from ._rows_base import MODE_RTN, RowsHandle, float_param, prep_activation, rows_fusable
 
@@ -97,13 +98,28 @@ class PackedEmbedding(nn.Module):
         self.register_buffer("zeros", zeros.contiguous())
 
     def forward(self, input_ids: torch.Tensor) -> torch.Tensor:
-        flat = input_ids.reshape(-1).long()
-        rows_q = self.qweight_u8[flat]
-        rows_s = self.scales[flat]
-        rows_z = self.zeros[flat]
-        dtype = self.scales.dtype if self.scales.dtype in (torch.float16, torch.bfloat16) else torch.float16
-        rows = dequant_extra_u8_to_weight(rows_q, rows_s, rows_z, self.embedding_dim, flat.shape[0], dtype)
-        return rows.reshape(*input_ids.shape, self.embedding_dim)
+        """Gather + dequantize the requested rows in one kernel (``oc_b200_rtn_embedding``);
+        same output as the reference's gathers + ``dequant_extra_u8_to_weight``
+        (packed_linear.py:92-104), in the scales' dtype (fp16 for integer scales; fp16,
+        bf16 and fp32 tables are supported).
+        Negative ids count from the end of the table; ids outside the table give zero rows
+        and set the device error word (``_lib.read_device_error``)."""
+        dev = self.qweight_u8.device
+        _lib.require_b200(dev)
+        flat = input_ids.reshape(-1).to(device=dev, dtype=torch.int64).contiguous()
+        dtype = self.scales.dtype if self.scales.dtype.is_floating_point else torch.float16
+        if dtype not in _lib.DT:
+            raise TypeError(f"unsupported scales dtype {dtype} (fp16/bf16/fp32 or integer)")
+        out = torch.empty((flat.shape[0], self.embedding_dim), dtype=dtype, device=dev)
+        s = self.scales if self.scales.dtype in _lib.DT else self.scales.float()
+        z = self.zeros if self.zeros.dtype in _lib.DT else self.zeros.float()
+        s, z = s.contiguous(), z.contiguous()
+        if flat.shape[0]:
+            _lib.call("oc_b200_rtn_embedding", flat.data_ptr(), flat.shape[0], self.num_embeddings,
+                      self.qweight_u8.data_ptr(), self.qweight_u8.shape[1], s.data_ptr(), _lib.DT[s.dtype],
+                      z.data_ptr(), _lib.DT[z.dtype], self.embedding_dim, int(s.shape[1]), out.data_ptr(),
+                      _lib.DT[dtype], _lib.stream_of(dev))
+        return out.reshape(*input_ids.shape, self.embedding_dim)
 
     def extra_repr(self) -> str:
         return f"num_embeddings={self.num_embeddings}, embedding_dim={self.embedding_dim}, packed=int4"

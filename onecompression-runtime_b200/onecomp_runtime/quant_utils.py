@@ -112,8 +112,8 @@ def dequant_extra_u8_to_weight(
     num_groups = scales.shape[1]
     if num_groups != 1 and in_features % num_groups != 0:
         raise RuntimeError(f"in_features={in_features} not divisible by num_groups={num_groups}")
-    if dtype not in (torch.float16, torch.bfloat16):
-        raise TypeError(f"unsupported dtype {dtype} (the B200 RTN path computes in fp16/bf16)")
+    if dtype not in _lib.DT:
+        raise TypeError(f"unsupported dtype {dtype} (the B200 RTN path computes in fp16/bf16/fp32)")
     q = qweight_u8.contiguous()
     s = scales.to(dev)
     z = zeros.to(dev)

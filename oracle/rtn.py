@@ -48,3 +48,39 @@ def pack_u8_nibbles(w_int: np.ndarray) -> np.ndarray:
     if in_f % 2:
         w = np.concatenate([w, np.zeros((out_f, 1), dtype=np.int64)], axis=1)
     return (w[:, 0::2] | (w[:, 1::2] << 4)).astype(np.uint8)
+
+
+def embedding_rtn(ids, qweight_u8, scales, scales_dtype, zeros, zeros_dtype, dim, dtype):
+    """PackedEmbedding.forward (reference packed_linear.py:92-104): gather the rows of ``ids``
+    (negative ids count from the end, as torch indexing does) and dequantize them like
+    ``dequant_rtn`` -> bit patterns [*ids.shape, dim]."""
+    ids = np.asarray(ids, dtype=np.int64)
+    vocab = qweight_u8.shape[0]
+    flat = ids.reshape(-1)
+    if ((flat < -vocab) | (flat >= vocab)).any():
+        raise IndexError("embedding id out of range")
+    flat = np.where(flat < 0, flat + vocab, flat)
+    w = dequant_rtn(qweight_u8[flat], np.asarray(scales)[flat], scales_dtype, np.asarray(zeros)[flat], zeros_dtype,
+                    dim, flat.shape[0], dtype)
+    return w.reshape(*ids.shape, dim)
+
+
+def quantize_conv_weight_f32(weight: np.ndarray, groupsize: int):
+    """RTN encoder of the conv codecs (reference packed_conv.py:63-90) in numpy fp32:
+    returns (qweight_u8, scales_f16_bits, zeros_f16_bits, cols). The division and rounding
+    steps are the same IEEE fp32 operations torch performs, round-half-to-even."""
+    w2 = np.asarray(weight, dtype=np.float32)
+    rows, cols = w2.shape
+    groups = cols // groupsize if groupsize > 0 and cols % groupsize == 0 else 1
+    w = w2.reshape(rows, groups, cols // groups)
+    hi = w.max(axis=-1, keepdims=True)
+    lo = w.min(axis=-1, keepdims=True)
+    empty = (hi == 0) & (lo == 0)
+    hi = np.where(empty, np.float32(1), hi)
+    lo = np.where(empty, np.float32(-1), lo)
+    scale = np.maximum((hi - lo) / np.float32(15), np.float32(1e-8)).astype(np.float32)
+    zero = np.round(-lo / scale).astype(np.float32)
+    q = np.clip(np.round(w / scale) + zero, 0, 15).astype(np.int64).reshape(rows, cols)
+    s16 = scale.reshape(rows, groups).astype(np.float16).view(np.uint16)
+    z16 = zero.reshape(rows, groups).astype(np.float16).view(np.uint16)
+    return pack_u8_nibbles(q), s16, z16, cols

@@ -39,6 +39,8 @@ GPTQ_CASES = [
 ]
 RTN_CASES = ["rtn_grouped", "rtn_perrow", "rtn_gs32_bf16"]
 DSV4_CASES = ["dsv4_int2_gs64", "dsv4_int4_gs128_go", "dsv4_int2_perrow", "dsv4_int4_ragged"]
+EMB_CASES = ["rtn_embedding_f16", "rtn_embedding_bf16_perrow", "rtn_embedding_f32"]
+CONV_CASES = ["conv1d_int4", "conv1d_int4_causal_grouped", "convtr1d_int4"]
 
 
 @pytest.fixture(scope="session")

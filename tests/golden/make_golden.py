@@ -7,7 +7,7 @@ Run in a container that has the reference checked out (read-only is fine)::
 Every case draws seeded inputs with numpy, feeds them to the reference's own
 functions (``quant_utils.dequant_gptq_to_fp``, ``quant_utils.dequant_extra_u8_to_weight``,
 ``layers.dsv4_packed_linear.dequant_dsv4_packed``, ``backend.build_eager`` +
-``nn.Linear``) and stores inputs and outputs (bf16/fp16 as uint16 bit patterns)
+``nn.Linear``, ``layers.packed_linear.PackedEmbedding``, ``layers.packed_conv``) and stores inputs and outputs (bf16/fp16 as uint16 bit patterns)
 in ``tests/golden/<case>.npz``. The tests load these fixtures; nothing at test
 time imports the reference.
 """
@@ -174,6 +174,54 @@ def dsv4_case(name, *, out_f, in_f, wbits, gs, layout, seed, zeros="const"):
     print("wrote", name)
 
 
+def embedding_case(name, *, vocab, dim, groups, scales_dtype, zeros_dtype, ids_shape, seed):
+    import torch
+    from onecomp_runtime.layers.packed_linear import PackedEmbedding
+
+    rng = np.random.default_rng(seed)
+    q = rng.integers(0, 256, size=(vocab, (dim + 1) // 2), dtype=np.uint8)
+    s32 = rng.uniform(0.002, 0.05, size=(vocab, groups)).astype(np.float32)
+    z32 = (rng.integers(0, 16, size=(vocab, groups)) + 0.5 * rng.integers(0, 2, size=(vocab, groups))).astype(np.float32)
+    ids = rng.integers(-vocab, vocab, size=ids_shape).astype(np.int64)
+    s_t = torch.from_numpy(s32).to(_tdt(scales_dtype))
+    z_t = torch.from_numpy(z32).to(_tdt(zeros_dtype))
+    emb = PackedEmbedding(vocab, dim, torch.from_numpy(q), s_t, z_t)
+    with torch.no_grad():
+        y = emb(torch.from_numpy(ids))
+    np.savez_compressed(HERE / f"{name}.npz", qweight_u8=q, scales=_bits(s_t), zeros=_bits(z_t), ids=ids,
+                        y=_bits(y), meta=json.dumps(dict(vocab=vocab, dim=dim, groups=groups,
+                                                         scales_dtype=scales_dtype, zeros_dtype=zeros_dtype,
+                                                         out_dtype={torch.float16: "f16", torch.bfloat16: "bf16",
+                                                                    torch.float32: "f32"}[y.dtype])))
+    print("wrote", name)
+
+
+def conv_case(name, *, transpose, cin, cout, k, stride, dilation, groups, groupsize, causal, pad_mode, L, seed):
+    import torch
+    from onecomp_runtime.layers import packed_conv as pc
+
+    rng = np.random.default_rng(seed)
+    wshape = (cin, cout // groups, k) if transpose else (cout, cin // groups, k)
+    w32 = (rng.standard_normal(wshape) * 0.1).astype(np.float32)
+    w32.reshape(w32.shape[0], -1)[0, :] = 0.0          # an all-zero quantization group
+    b32 = (rng.standard_normal(cout) * 0.05).astype(np.float32)
+    q, s, z, cols = pc.quantize_conv_weight(torch.from_numpy(w32).reshape(w32.shape[0], -1), groupsize=groupsize)
+    common = dict(kernel_size=k, stride=stride, dilation=dilation, groups=groups, qweight=q, scales=s, zeros=z,
+                  cols=cols, bias=torch.from_numpy(b32), causal=causal, pad_mode=pad_mode)
+    mod = (pc.PackedInt4ConvTranspose1d(cin, cout, **common) if transpose else pc.PackedInt4Conv1d(cin, cout, **common))
+    x32 = rng.standard_normal((2, cin, L)).astype(np.float32)
+    data = dict(weight_f32=w32, bias_f32=b32, qweight=q.numpy(), scales=_bits(s), zeros=_bits(z), x_f32=x32,
+                meta=json.dumps(dict(transpose=transpose, cin=cin, cout=cout, k=k, stride=stride, dilation=dilation,
+                                     groups=groups, groupsize=groupsize, causal=causal, pad_mode=pad_mode, cols=cols)))
+    for od in ("bf16", "f16"):
+        data[f"w_{od}"] = _bits(pc._dequant_weight(q, s, z, cols, _tdt(od)))
+    x = torch.from_numpy(x32).to(torch.bfloat16)
+    with torch.no_grad():
+        data["y_bf16"] = _bits(mod(x))
+    np.savez_compressed(HERE / f"{name}.npz", **data)
+    print("wrote", name)
+
+
 def main():
     ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("ONECOMP_REFERENCE", "")
     if not ref:
@@ -202,6 +250,18 @@ def main():
               zeros="rand")
     dsv4_case("dsv4_int4_ragged", out_f=40, in_f=200, wbits=4, gs=64, layout="og", seed=23,
               zeros="rand")
+    embedding_case("rtn_embedding_f16", vocab=300, dim=192, groups=6, scales_dtype="f16", zeros_dtype="f16",
+                   ids_shape=(3, 5), seed=30)
+    embedding_case("rtn_embedding_bf16_perrow", vocab=50, dim=70, groups=1, scales_dtype="bf16",
+                   zeros_dtype="f32", ids_shape=(9,), seed=31)
+    embedding_case("rtn_embedding_f32", vocab=64, dim=96, groups=4, scales_dtype="f32", zeros_dtype="f16",
+                   ids_shape=(2, 7), seed=32)
+    conv_case("conv1d_int4", transpose=False, cin=12, cout=16, k=5, stride=2, dilation=1, groups=1, groupsize=20,
+              causal=False, pad_mode="auto", L=33, seed=40)
+    conv_case("conv1d_int4_causal_grouped", transpose=False, cin=8, cout=12, k=7, stride=1, dilation=2, groups=2,
+              groupsize=4, causal=True, pad_mode="auto", L=40, seed=41)
+    conv_case("convtr1d_int4", transpose=True, cin=16, cout=8, k=8, stride=4, dilation=1, groups=1, groupsize=32,
+              causal=False, pad_mode="auto", L=11, seed=42)
 
 
 if __name__ == "__main__":

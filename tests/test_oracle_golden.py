@@ -4,7 +4,7 @@ from __future__ import annotations
 import numpy as np
 import pytest
 
-from conftest import DSV4_CASES, GPTQ_CASES, RTN_CASES, load_golden
+from conftest import EMB_CASES, CONV_CASES, DSV4_CASES, GPTQ_CASES, RTN_CASES, load_golden
 from oracle import dsv4, eager, gptq, rtn
 
 
@@ -95,3 +95,51 @@ def test_bf16_rounding_ties_and_nan():
     np.testing.assert_array_equal(bf16_bits_to_f32(b)[:4], np.array([1.0, 1.0, 1.0 + 2**-6, -2.5], np.float32))
     assert np.isinf(bf16_bits_to_f32(b)[4])
     assert np.isnan(bf16_bits_to_f32(f32_to_bf16_bits(np.array([np.nan], np.float32))))[0]
+
+
+@pytest.mark.parametrize("case", EMB_CASES)
+def test_embedding_oracle_bit_exact(case):
+    d = load_golden(case)
+    m = d["meta"]
+    y = rtn.embedding_rtn(d["ids"], d["qweight_u8"], d["scales"], m["scales_dtype"], d["zeros"], m["zeros_dtype"],
+                          m["dim"], m["out_dtype"])
+    np.testing.assert_array_equal(y, d["y"])
+
+
+@pytest.mark.parametrize("case", CONV_CASES)
+def test_conv_codec_oracle_bit_exact(case):
+    """The conv codec's encoder and its weight dequant (the RTN arithmetic) against the
+    reference's own outputs."""
+    d = load_golden(case)
+    m = d["meta"]
+    w2 = d["weight_f32"].reshape(d["weight_f32"].shape[0], -1)
+    q, s16, z16, cols = rtn.quantize_conv_weight_f32(w2, m["groupsize"])
+    assert cols == m["cols"]
+    np.testing.assert_array_equal(q, d["qweight"])
+    np.testing.assert_array_equal(s16, d["scales"])
+    np.testing.assert_array_equal(z16, d["zeros"])
+    for od in ("bf16", "f16"):
+        w = rtn.dequant_rtn(d["qweight"], d["scales"], "f16", d["zeros"], "f16", cols, q.shape[0], od)
+        np.testing.assert_array_equal(w, d[f"w_{od}"])
+
+
+@pytest.mark.parametrize("case", CONV_CASES)
+def test_conv_quantizer_matches_reference(case):
+    """The package's host-side quantize_conv_weight (torch, CPU) reproduces the reference's."""
+    import torch
+    from onecomp_runtime.layers import quantize_conv_weight
+    d = load_golden(case)
+    w2 = torch.from_numpy(d["weight_f32"].reshape(d["weight_f32"].shape[0], -1))
+    q, s, z, cols = quantize_conv_weight(w2, groupsize=d["meta"]["groupsize"])
+    np.testing.assert_array_equal(q.numpy(), d["qweight"])
+    np.testing.assert_array_equal(s.view(torch.int16).numpy().view(np.uint16), d["scales"])
+    np.testing.assert_array_equal(z.view(torch.int16).numpy().view(np.uint16), d["zeros"])
+
+
+def test_conv_nibble_pack_roundtrip():
+    import torch
+    from onecomp_runtime.layers.packed_conv import pack_int4_nibbles, unpack_int4_nibbles
+    codes = torch.randint(0, 16, (5, 37), generator=torch.Generator().manual_seed(3))
+    packed = pack_int4_nibbles(codes)
+    assert packed.shape == (5, 19) and packed.dtype == torch.uint8
+    assert torch.equal(unpack_int4_nibbles(packed, 37).to(torch.int64), codes)
