@@ -253,12 +253,21 @@ def bench_decode(args):
     if args.gemv_ctas:
         _lib.set_option(_lib.OPT_GEMV_CTAS, args.gemv_ctas)
     layers, nbytes = [], 0
+    w8 = args.wbits == 8
     for i, (name, K, N) in enumerate(CFG2_LAYERS):
-        t = gptq_layer(K, N, 128, seed=2000 + i, v1=False, actorder=True, scales_range=(0.001, 0.01),
-                       scales_dtype=torch.bfloat16, bias=False, device=dev)
-        layers.append(PackedGPTQLinear(K, N, t["qweight"], t["scales"], t["qzeros"], t["g_idx"], None, 128, 4, False))
         G = (K + 127) // 128
-        nbytes += K * N // 2 + 2 * G * N + G * N // 2 + 4 * K
+        if w8:  # the 8-bit layers of a {4,8}-bit GPTQ checkpoint: v1 zeros, gs128, no act-order
+            t = gptq_layer(K, N, 128, seed=2000 + i, v1=True, scales_range=(0.001, 0.01),
+                           scales_dtype=torch.bfloat16, bias=False, device=dev, wbits=8)
+            layers.append(PackedGPTQLinear(K, N, t["qweight"], t["scales"], t["qzeros"], t["g_idx"], None, 128, 8,
+                                           True))
+            nbytes += K * N + 2 * G * N + G * N
+        else:
+            t = gptq_layer(K, N, 128, seed=2000 + i, v1=False, actorder=True, scales_range=(0.001, 0.01),
+                           scales_dtype=torch.bfloat16, bias=False, device=dev)
+            layers.append(PackedGPTQLinear(K, N, t["qweight"], t["scales"], t["qzeros"], t["g_idx"], None, 128, 4,
+                                           False))
+            nbytes += K * N // 2 + 2 * G * N + G * N // 2 + 4 * K
     peaks = load_peaks()
     per_m = {}
     for M in (1, 4, 16):
@@ -286,14 +295,16 @@ def bench_decode(args):
                     "frac_hbm": round((nbytes + act) / (us * 1e-6) / 1e9 / peaks["hbm_gbs"], 4)}
         del g, outs
     top = per_m[16]
-    line = {"metric": "decode GB/s (gptq_v2 gs128 act-order layer set, M=16)", "value": top["GB_s"], "unit": "GB/s",
+    kind = "gptq v1 gs128 8-bit" if w8 else "gptq_v2 gs128 act-order"
+    line = {"metric": f"decode GB/s ({kind} layer set, M=16)", "value": top["GB_s"], "unit": "GB/s",
             "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "cfg2: q/k/v 5120->8192, o 6144->5120, gate/up 5120->17408, down 17408->5120",
+            "config": {"workload": "cfg2: q/k/v 5120->8192, o 6144->5120, gate/up 5120->17408, down 17408->5120"
+                                   + (", 8-bit codes" if w8 else ""),
                        "packed_bytes_per_set": nbytes, "graph": "CUDA graph of the 5 layers, replayed"},
             "per_m": per_m,
             "roofline": {"bound": "hbm", "achieved": top["GB_s"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                         "frac": top["frac_hbm"], "traffic": GEMV_TRAFFIC_BYTES_PER_LAUNCH,
+                         "frac": top["frac_hbm"], "traffic": None if w8 else GEMV_TRAFFIC_BYTES_PER_LAUNCH,
                          "traffic_unit": "bytes per launch (q/k/v layer)",
                          "peak_source": f"{peaks['source']} hbm_gbs"}}
     print(json.dumps(line), flush=True)
@@ -448,6 +459,7 @@ def main():
                          "cfg3: packed MoE layer (expert parallel); cfg4: tensor-parallel video-DiT stack")
     ap.add_argument("--tc-tile", type=int, default=0, help="tokens per tcgen05 tile (0 = library default)")
     ap.add_argument("--gemv-ctas", type=int, default=0, help="GEMV split-K target CTAs per SM (0 = default)")
+    ap.add_argument("--wbits", type=int, default=4, choices=[4, 8], help="cfg2 only: code width of the layer set")
     ap.add_argument("--blocks", type=int, default=0, help="override the number of DiT blocks (profiling only)")
     ap.add_argument("--cpu-sample-m", type=int, default=1152,
                     help="tokens of the bounded CPU-baseline sample (one block)")

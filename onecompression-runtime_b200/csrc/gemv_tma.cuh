@@ -15,6 +15,12 @@
 // for the previous kernel (griddepcontrol.wait); activations and every global write (split-K
 // partials, tickets, output) come after that wait.
 //
+// 8-bit layers (WB = 8): a 32-bit word holds 4 k of one column, so a stage of 16 word rows
+// covers 64 k. bf16 cannot hold M + q exactly for q >= 128, so each byte is split into its two
+// nibbles, both multiplied as magic-biased 4-bit codes into separate fp32 accumulators, and the
+// group flush combines them: s * (C_lo + 16 C_hi) - s * (17 M + z) * sum(x) = s * sum(x (q - z)).
+// The MMA count per weight byte is the 4-bit kernel's.
+//
 // CTA: 8 consumer warps (4 column warps x 2 k halves; warp (wn, kh) takes steps 2kh, 2kh+1 of
 // each 4-step stage) + 1 producer warp. Split-K over CTAs as in gemv.cuh (deterministic
 // last-CTA reduction). Every mbarrier wait is bounded; on timeout the kernel records an error
@@ -28,14 +34,18 @@ namespace oc {
 
 constexpr int kGtConsumerWarps = 8;
 constexpr int kGtThreads = 32 * (kGtConsumerWarps + 1);
-constexpr int kGtBK = 128;  // k per stage: 16 word rows, 4 MMA steps of 32 k
+constexpr int kGtBK = 128;  // 4-bit k per stage: 16 word rows, 4 MMA steps of 32 k (8-bit: 64 k)
+
+// k covered by one stage of 16 word rows
+template <int WB>
+constexpr int gt_stage_k() { return WB == 8 ? 64 : kGtBK; }
 
 template <int MT>
 struct GtCfg {
   static constexpr int kDepth = MT == 1 ? 8 : 6;
   static constexpr int kWBytes = 4 * 16 * 128;          // four [16 rows][32 words] slabs, 128B-swizzled
   static constexpr int kSBytes = 4 * kGemvCols * 2;     // up to 4 scale rows (groups of 32)
-  static constexpr int kZBytes = 4 * (kGemvCols / 8) * 4;
+  static constexpr int kZBytes = 4 * (kGemvCols / 8) * 4;  // 4 rows of 4-bit zeros = 2 rows of 8-bit
   static constexpr int kXBytes = 8 * MT * kGtBK * 2;    // [8 MT tokens][128 k]
   static constexpr int kWOff = 0;
   static constexpr int kSOff = kDepth * kWBytes;
@@ -52,12 +62,12 @@ __device__ __forceinline__ void griddep_launch_dependents() {
 
 struct GtParams {
   GemvParams g;
-  int rows_sz;        // scale/zero rows per stage: 4 (gs 32), 2 (gs 64), 1 (gs multiple of 128)
+  int rows_sz;        // scale/zero rows per stage: stage k / gs when gs divides it, else 1
   int stages_per_grp; // stages per group when gs >= 128 (else 1)
   int kb_per_split;   // stages per split
 };
 
-template <bool BF16, int MT>
+template <bool BF16, int MT, int WB = 4>
 __global__ void __launch_bounds__(kGtThreads, 2)
     gptq_gemv_tma_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_s,
                          const __grid_constant__ CUtensorMap tmap_z, const __grid_constant__ CUtensorMap tmap_x,
@@ -73,9 +83,13 @@ __global__ void __launch_bounds__(kGtThreads, 2)
   __shared__ float red[kGemvWarpsN][32][MT * 8];
   __shared__ int is_last;
 
+  static_assert(WB == 4 || WB == 8, "4- or 8-bit codes");
+  constexpr int KS = gt_stage_k<WB>();   // k per stage
+  constexpr int KSTEP = KS / 4;          // k per MMA step (4 word rows)
+  constexpr int kZRowBytes = kGemvCols * WB / 8;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x, split = blockIdx.y;
-  const int KB = (p.Kp + kGtBK - 1) / kGtBK;
+  const int KB = (p.Kp + KS - 1) / KS;
   const int kb0 = split * gp.kb_per_split;
   const int kb1 = min(KB, kb0 + gp.kb_per_split);
   const int nst = kb1 - kb0;
@@ -99,7 +113,7 @@ __global__ void __launch_bounds__(kGtThreads, 2)
       tma_prefetch_desc(&tmap_s);
       tma_prefetch_desc(&tmap_z);
       tma_prefetch_desc(&tmap_x);
-      const uint32_t bytes = Cfg::kWBytes + gp.rows_sz * (kGemvCols * 2 + (kGemvCols / 8) * 4) + Cfg::kXBytes;
+      const uint32_t bytes = Cfg::kWBytes + gp.rows_sz * (kGemvCols * 2 + kZRowBytes) + 8 * MT * KS * 2;
       int armed[Cfg::kDepth];
       for (int i = 0; i < Cfg::kDepth; ++i) armed[i] = -1;
       auto load_wsz = [&](int i) {
@@ -109,14 +123,14 @@ __global__ void __launch_bounds__(kGtThreads, 2)
 #pragma unroll
         for (int c = 0; c < 4; ++c)
           tma_load_2d(smem + Cfg::kWOff + s * Cfg::kWBytes + c * 2048, &tmap_w, &full[s], col0 + 32 * c, kb * 16);
-        const int g0 = (kb * kGtBK) / p.gs;
+        const int g0 = (kb * KS) / p.gs;
         tma_load_2d(smem + Cfg::kSOff + s * Cfg::kSBytes, &tmap_s, &full[s], col0, g0);
-        tma_load_2d(smem + Cfg::kZOff + s * Cfg::kZBytes, &tmap_z, &full[s], col0 / 8, g0);
+        tma_load_2d(smem + Cfg::kZOff + s * Cfg::kZBytes, &tmap_z, &full[s], col0 * WB / 32, g0);
         armed[s] = (i / Cfg::kDepth) & 1;
       };
       auto load_x = [&](int i) {
         const int s = i % Cfg::kDepth;
-        tma_load_2d(smem + Cfg::kXOff + s * Cfg::kXBytes, &tmap_x, &full[s], (kb0 + i) * kGtBK, 0);
+        tma_load_2d(smem + Cfg::kXOff + s * Cfg::kXBytes, &tmap_x, &full[s], (kb0 + i) * KS, 0);
       };
       // weights of the first stages before the previous kernel has finished
       const int pre = nst < Cfg::kDepth ? nst : Cfg::kDepth;
@@ -145,12 +159,14 @@ __global__ void __launch_bounds__(kGtThreads, 2)
   const int g = lane >> 2, t = lane & 3;
   const int cw = wn * 32 + 4 * g;  // column within the tile
   const int col = col0 + cw;
-  const int zsh = 4 * (col & 7);
-  const int spg_step = p.gs / 32;  // steps per group when gs < 128 (1 or 2)
+  const int zsh = WB == 8 ? 0 : 4 * (col & 7);
+  const int spg_step = p.gs / KSTEP;  // steps per group when a stage holds several groups
   const uint32_t ones = BF16 ? 0x3F803F80u : 0x3C003C00u;
   const uint32_t ones4[4] = {ones, ones, ones, ones};
 
-  float acc[MT][2][4], cg[MT][2][4], xo[MT][4];
+  // cg: codes (low nibbles for 8-bit) x activations; ch: high nibbles (8-bit only)
+  constexpr int NH = WB == 8 ? MT : 1;
+  float acc[MT][2][4], cg[MT][2][4], ch[NH][2][4], xo[MT][4];
 #pragma unroll
   for (int a = 0; a < MT; ++a) {
 #pragma unroll
@@ -160,6 +176,12 @@ __global__ void __launch_bounds__(kGtThreads, 2)
 #pragma unroll
     for (int c = 0; c < 4; ++c) xo[a][c] = 0.f;
   }
+#pragma unroll
+  for (int a = 0; a < NH; ++a)
+#pragma unroll
+    for (int b = 0; b < 2; ++b)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) ch[a][b][c] = 0.f;
   float sj[4] = {0.f, 0.f, 0.f, 0.f}, czj[4] = {0.f, 0.f, 0.f, 0.f};
   auto flush = [&]() {
 #pragma unroll
@@ -169,7 +191,12 @@ __global__ void __launch_bounds__(kGtThreads, 2)
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           const int j = 2 * b + (c >> 1);
-          acc[a][b][c] += sj[j] * cg[a][b][c] - czj[j] * xo[a][c & 1];
+          float cv = cg[a][b][c];
+          if constexpr (WB == 8) {
+            cv = fmaf(16.f, ch[a % NH][b][c], cv);
+            ch[a % NH][b][c] = 0.f;
+          }
+          acc[a][b][c] += sj[j] * cv - czj[j] * xo[a][c & 1];
           cg[a][b][c] = 0.f;
         }
 #pragma unroll
@@ -178,16 +205,21 @@ __global__ void __launch_bounds__(kGtThreads, 2)
   };
   auto load_sz = [&](const uint8_t* srow, const uint8_t* zrow) {
     const uint2 sv = *reinterpret_cast<const uint2*>(srow + cw * 2);
-    const uint32_t zw = *reinterpret_cast<const uint32_t*>(zrow + (cw >> 3) * 4);
+    const uint32_t zw = *reinterpret_cast<const uint32_t*>(zrow + (cw * WB / 32) * 4);
     const uint32_t sw4[4] = {sv.x & 0xFFFFu, sv.x >> 16, sv.y & 0xFFFFu, sv.y >> 16};
+    constexpr uint32_t kZMask = (1u << WB) - 1u;
+    // bias of the codes in the MMA sums: M (4-bit), M + 16 M (the two nibbles of 8-bit)
+    constexpr float kBias = WB == 8 ? 17.f * P::kMagicF : P::kMagicF;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      uint32_t z = (zw >> (zsh + 4 * j)) & 0xFu;
-      if (p.v1) z = (z + 1u) & 0xFu;
+      uint32_t z = (zw >> (zsh + WB * j)) & kZMask;
+      if (p.v1) z = (z + 1u) & kZMask;
       const float sc = (p.s_dtype == kF16) ? __half2float(__ushort_as_half((uint16_t)sw4[j]))
                                            : __bfloat162float(__ushort_as_bfloat16((uint16_t)sw4[j]));
       sj[j] = sc;
-      czj[j] = sc * (P::kMagicF + (float)z);  // exact: <= 19 significant bits
+      // exact for 4-bit codes (<= 19 significant bits); 8-bit: exact for bf16 scales, one
+      // fp32 rounding for fp16 scales
+      czj[j] = sc * (kBias + (float)z);
     }
   };
 
@@ -220,15 +252,42 @@ __global__ void __launch_bounds__(kGtThreads, 2)
       if (new_grp) {
         if (!first) flush();
         first = false;
-        load_sz(sst + srow * (kGemvCols * 2), zst + srow * (kGemvCols / 8) * 4);
+        load_sz(sst + srow * (kGemvCols * 2), zst + srow * kZRowBytes);
       }
       const int r = 4 * j + t;  // word row within the slab
       const uint4 w = *reinterpret_cast<const uint4*>(wst + r * 128 + ((g ^ (r & 7)) << 4));
+      const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+      if constexpr (WB == 8) {
+        // lane k = KSTEP j + 4t + {0..3}; nibble pairs (lo k0, lo k2), (hi k0, hi k2),
+        // (lo k1, lo k3), (hi k1, hi k3) of each column
+        uint32_t pr[4][4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          pr[q][0] = lop3_and_or(wv[q], 0x000F000Fu, P::kMagic);
+          pr[q][1] = lop3_and_or(wv[q] >> 4, 0x000F000Fu, P::kMagic);
+          pr[q][2] = lop3_and_or(wv[q] >> 8, 0x000F000Fu, P::kMagic);
+          pr[q][3] = lop3_and_or(wv[q] >> 12, 0x000F000Fu, P::kMagic);
+        }
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+          const uint2 xv = *reinterpret_cast<const uint2*>(xst + (g + 8 * mt) * (KS * 2) + (KSTEP * j + 4 * t) * 2);
+          const uint32_t b0 = prmt(xv.x, xv.y, 0x5410u);  // (x0, x2)
+          const uint32_t b1 = prmt(xv.x, xv.y, 0x7632u);  // (x1, x3)
+#pragma unroll
+          for (int beta = 0; beta < 2; ++beta) {
+            const uint32_t alo[4] = {pr[2 * beta][0], pr[2 * beta + 1][0], pr[2 * beta][2], pr[2 * beta + 1][2]};
+            const uint32_t ahi[4] = {pr[2 * beta][1], pr[2 * beta + 1][1], pr[2 * beta][3], pr[2 * beta + 1][3]};
+            mma_16816<BF16>(cg[mt][beta], alo, b0, b1);
+            mma_16816<BF16>(ch[mt % NH][beta], ahi, b0, b1);
+          }
+          mma_16816<BF16>(xo[mt], ones4, b0, b1);
+        }
+        continue;
+      }
       uint4 xv[MT];
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt)
-        xv[mt] = *reinterpret_cast<const uint4*>(xst + (g + 8 * mt) * (kGtBK * 2) + (32 * j + 8 * t) * 2);
-      const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+        xv[mt] = *reinterpret_cast<const uint4*>(xst + (g + 8 * mt) * (KS * 2) + (KSTEP * j + 8 * t) * 2);
       uint32_t pr[4][4];
 #pragma unroll
       for (int q = 0; q < 4; ++q) {

@@ -347,12 +347,77 @@ int oc_b200_permute_cols(const void* x, int64_t ldx, int64_t M, int K, const int
 }
 
 // ---------------------------------------------------------------- GPTQ layer
+// 8-bit layers: the TMA decode GEMV only (uniform groups, no K permutation).
+static int gptq_layer_create8(const int32_t* qweight, const int32_t* qzeros, const void* scales, int scales_dtype,
+                              int in_features, int N, int G, int groupsize, int v1, oc_b200_layer** out) {
+  const int ks = oc::gt_stage_k<8>();
+  if (in_features < ks || in_features % 8 != 0)
+    return fail(OC_ERR_UNSUPPORTED, "layer_create: 8-bit in_features=%d (needs a multiple of 8, >= %d)", in_features,
+                ks);
+  if (N < oc::kGemvCols || N % 32 != 0)
+    return fail(OC_ERR_UNSUPPORTED, "layer_create: 8-bit N=%d (needs a multiple of 32, >= %d)", N, oc::kGemvCols);
+  if (groupsize != 32 && (groupsize <= 0 || groupsize % ks != 0))
+    return fail(OC_ERR_UNSUPPORTED, "layer_create: 8-bit groupsize=%d (needs 32 or a multiple of %d)", groupsize, ks);
+  if (G != (in_features + groupsize - 1) / groupsize)
+    return fail(OC_ERR_INVALID, "layer_create: G=%d for in_features=%d groupsize=%d", G, in_features, groupsize);
+  if (!aligned(qweight, 16) || !aligned(scales, 16) || !aligned(qzeros, 16))
+    return fail(OC_ERR_UNSUPPORTED, "layer_create: 8-bit tensors must be 16-byte aligned");
+  int dev = 0;
+  if (int rc = current_device(&dev)) return rc;
+  if (int rc = oc_b200_device_check(dev)) return rc;
+  auto* L = new oc_b200_layer();
+  L->kind = 0;
+  L->wbits = 8;
+  L->device = dev;
+  L->qw = reinterpret_cast<const uint32_t*>(qweight);
+  L->qz = reinterpret_cast<const uint32_t*>(qzeros);
+  L->s = scales;
+  L->s_dtype = scales_dtype;
+  L->K_in = in_features;
+  L->Kp = in_features;
+  L->N = N;
+  L->G = G;
+  L->gs = groupsize;
+  L->v1 = v1 ? 1 : 0;
+  const int rows = groupsize >= ks ? 1 : ks / groupsize;
+  int rc = make_tmap_2d(&L->tmap_gw, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, qweight, (uint64_t)N,
+                        (uint64_t)(in_features / 4), (uint64_t)N * 4, 32, 16, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!rc)
+    rc = make_tmap_2d(&L->tmap_gs, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, scales, (uint64_t)N, (uint64_t)G,
+                      (uint64_t)N * 2, oc::kGemvCols, rows, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (!rc)
+    rc = make_tmap_2d(&L->tmap_gz, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, qzeros, (uint64_t)(N / 4), (uint64_t)G,
+                      (uint64_t)(N / 4) * 4, oc::kGemvCols / 4, rows, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc) {
+    delete L;
+    return rc;
+  }
+  L->gt_ok = 1;
+  L->gt_rows = rows;
+  *out = L;
+  return OC_OK;
+}
+
 int oc_b200_gptq_layer_create(const int32_t* qweight, const int32_t* qzeros, const void* scales, int scales_dtype,
                               const int32_t* k_perm, const int32_t* word_group, int in_features, int k_packed, int N,
                               int G, int groupsize, int v1, oc_b200_layer** out) {
+  return oc_b200_gptq_layer_create_ex(qweight, qzeros, scales, scales_dtype, k_perm, word_group, in_features,
+                                      k_packed, N, G, groupsize, 4, v1, out);
+}
+
+int oc_b200_gptq_layer_create_ex(const int32_t* qweight, const int32_t* qzeros, const void* scales, int scales_dtype,
+                                 const int32_t* k_perm, const int32_t* word_group, int in_features, int k_packed,
+                                 int N, int G, int groupsize, int wbits, int v1, oc_b200_layer** out) {
   if (!out) return fail(OC_ERR_INVALID, "layer_create: out is NULL");
   *out = nullptr;
   if (!qweight || !qzeros || !scales) return fail(OC_ERR_INVALID, "layer_create: NULL tensor");
+  if (wbits != 4 && wbits != 8) return fail(OC_ERR_UNSUPPORTED, "layer_create: wbits=%d (4 or 8)", wbits);
+  if (wbits == 8) {
+    if (!dt16(scales_dtype)) return fail(OC_ERR_UNSUPPORTED, "layer_create: scales must be f16 or bf16");
+    if (k_perm || word_group || k_packed != in_features)
+      return fail(OC_ERR_UNSUPPORTED, "layer_create: 8-bit layers take no K permutation or word groups");
+    return gptq_layer_create8(qweight, qzeros, scales, scales_dtype, in_features, N, G, groupsize, v1, out);
+  }
   if (!dt16(scales_dtype)) return fail(OC_ERR_UNSUPPORTED, "layer_create: scales must be f16 or bf16");
   if (in_features <= 0 || k_packed <= 0 || k_packed % 8 != 0)
     return fail(OC_ERR_INVALID, "layer_create: in_features=%d k_packed=%d (k_packed must be a multiple of 8)",
@@ -370,6 +435,7 @@ int oc_b200_gptq_layer_create(const int32_t* qweight, const int32_t* qzeros, con
   if (int rc = oc_b200_device_check(dev)) return rc;
   auto* L = new oc_b200_layer();
   L->kind = 0;
+  L->wbits = 4;
   L->device = dev;
   L->qw = reinterpret_cast<const uint32_t*>(qweight);
   L->qz = reinterpret_cast<const uint32_t*>(qzeros);
@@ -456,6 +522,7 @@ struct GemvPlan {
 // uniform groups of 32, 64 or 128*n rows; 1 is the default, measured faster), 2 cp.async +
 // mma.sync GEMV (any layout).
 int gemv_impl(const oc_b200_layer* L) {
+  if (L->wbits == 8) return 1;  // 8-bit layers have only the TMA GEMV
   if (!L->gt_ok) return 2;
   return g_opt_gemv_impl.load();
 }
@@ -475,8 +542,9 @@ GemvPlan gemv_plan(const oc_b200_layer* L, int dev) {
     splits = (KB + kbs - 1) / kbs;
     return {splits, kbs * (oc::kVtBK / 32)};
   }
-  if (gemv_impl(L) == 1) {  // TMA GEMV: splits in whole 128-k stages, at least two per CTA
-    const int KB = (L->Kp + oc::kGtBK - 1) / oc::kGtBK;
+  if (gemv_impl(L) == 1) {  // TMA GEMV: splits in whole stages (128 k, 64 k for 8-bit), at least two per CTA
+    const int ks = L->wbits == 8 ? oc::gt_stage_k<8>() : oc::kGtBK;
+    const int KB = (L->Kp + ks - 1) / ks;
     int splits = target / n_tiles;
     const int max_splits = KB / 2 > 0 ? KB / 2 : 1;
     if (splits > max_splits) splits = max_splits;
@@ -533,13 +601,16 @@ bool use_gemv(int64_t M) {
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
+// 8-bit layers have the decode GEMV only: M <= 16 whatever OC_OPT_GEMM_PATH says.
+bool layer_gemv(const oc_b200_layer* L, int64_t M) { return L->wbits == 8 ? M <= 16 : use_gemv(M); }
+
 }  // namespace
 
 extern "C" size_t oc_b200_gptq_gemm_workspace(const oc_b200_layer* L, int64_t M) {
   if (!L || M <= 0) return kTicketBytes;
   size_t bytes = kTicketBytes;
   if (L->kperm) bytes += align_up((size_t)M * L->Kp * 2, 256);  // gathered activations
-  if (use_gemv(M)) {
+  if (layer_gemv(L, M)) {
     const GemvPlan gp = gemv_plan(L, L->device);
     if (gp.splits > 1) bytes += align_up((size_t)gp.splits * M * L->N * 4, 256);
   }
@@ -616,16 +687,22 @@ int launch_gemv_tma(const oc_b200_layer* L, const oc::GemvParams& p, const GemvP
                     cudaStream_t stream) {
   oc::GtParams g{};
   g.g = p;
+  const int ks = L->wbits == 8 ? oc::gt_stage_k<8>() : oc::kGtBK;  // k per stage
   g.rows_sz = L->gt_rows;
-  g.stages_per_grp = L->gs >= oc::kGtBK ? L->gs / oc::kGtBK : 1;
+  g.stages_per_grp = L->gs >= ks ? L->gs / ks : 1;
   g.kb_per_split = gp.kstep / (oc::kGtBK / 32);
   const int mt = p.M <= 8 ? 1 : 2;
   CUtensorMap tx;
   if (int rc = make_tmap_2d(&tx, BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.x,
-                            (uint64_t)p.Kp, (uint64_t)p.M, (uint64_t)p.ldx * 2, oc::kGtBK, (uint32_t)(8 * mt),
+                            (uint64_t)p.Kp, (uint64_t)p.M, (uint64_t)p.ldx * 2, (uint32_t)ks, (uint32_t)(8 * mt),
                             CU_TENSOR_MAP_SWIZZLE_NONE))
     return rc;
   const dim3 grid(n_tiles, gp.splits);
+  if (L->wbits == 8) {
+    if (mt == 1)
+      return launch_gt_k<oc::gptq_gemv_tma_kernel<BF16, 1, 8>>(oc::GtCfg<1>::kSmemBytes, grid, stream, L, tx, g);
+    return launch_gt_k<oc::gptq_gemv_tma_kernel<BF16, 2, 8>>(oc::GtCfg<2>::kSmemBytes, grid, stream, L, tx, g);
+  }
   if (mt == 1)
     return launch_gt_k<oc::gptq_gemv_tma_kernel<BF16, 1>>(oc::GtCfg<1>::kSmemBytes, grid, stream, L, tx, g);
   return launch_gt_k<oc::gptq_gemv_tma_kernel<BF16, 2>>(oc::GtCfg<2>::kSmemBytes, grid, stream, L, tx, g);
@@ -750,8 +827,11 @@ extern "C" int oc_b200_gptq_gemm_ex(const oc_b200_layer* L, const void* a, int a
   }
   const bool bf16 = a_dtype == OC_DT_BF16;
   const bool has_lo = L->s_dtype != a_dtype;
+  if (L->wbits == 8 && M > 16)
+    return fail(OC_ERR_UNSUPPORTED, "gptq_gemm: 8-bit layers run the decode GEMV only (M <= 16), M=%lld",
+                (long long)M);
 
-  if (use_gemv(M)) {
+  if (layer_gemv(L, M)) {
     const GemvPlan gp = gemv_plan(L, dev);
     oc::GemvParams p{};
     p.x = xk;

@@ -51,6 +51,7 @@ _SIGNATURES = {
     "oc_b200_gptq_repack_k": ([_p, _p, _i, _i, _p, _p], _i),
     "oc_b200_permute_cols": ([_p, _i64, _i64, _i, _p, _i, _p, _p], _i),
     "oc_b200_gptq_layer_create": ([_p, _p, _p, _i, _p, _p, _i, _i, _i, _i, _i, _i, ctypes.POINTER(_p)], _i),
+    "oc_b200_gptq_layer_create_ex": ([_p, _p, _p, _i, _p, _p, _i, _i, _i, _i, _i, _i, _i, ctypes.POINTER(_p)], _i),
     "oc_b200_layer_destroy": ([_p], _i),
     "oc_b200_gptq_gemm_workspace": ([_p, _i64], _sz),
     "oc_b200_gptq_gemm": ([_p, _p, _i, _i64, _i64, _p, _i, _p, _i64, _p, _sz, _p], _i),

@@ -169,6 +169,7 @@ def build_eager(entry: dict, st: dict, dtype: torch.dtype, device: torch.device)
     weight = dequant_gptq_to_fp(
         qweight=st["qweight"].to(device), scales=st["scales"].to(device), qzeros=st["qzeros"].to(device),
         g_idx=g_idx.to(device), in_features=in_f, out_features=out_f, dtype=dtype, v1=_v1(entry),
+        wbits=int(entry.get("wbits", 4)),
     )
     has_bias = "bias" in st
     lin = torch.nn.Linear(in_f, out_f, bias=has_bias, device=device, dtype=dtype)

@@ -12,15 +12,23 @@ layers here run the fused sm_100a kernels directly on the packed buffers:
   stores them in the model dtype, backend.py:275) and the kernels multiply
   exactly the weights ``dequant_gptq_to_fp`` would produce.
 
-8-bit layers dequantize with the B200 dequant kernel and call ``F.linear``.
+8-bit layers with uniform groups (``g_idx == k // groupsize``, groupsize 32 or a multiple
+of 64) run the 8-bit decode GEMV for M <= 16 tokens; larger M, act-order 8-bit layers and
+fp32 inputs dequantize with the B200 dequant kernel and call ``F.linear``, as the
+reference does for every call.
 """
 from __future__ import annotations
+
+import ctypes
 
 import torch
 import torch.nn.functional as F
 
+from .. import _lib
 from ..quant_utils import dequant_gptq_to_fp
 from ._gptq_base import B200GPTQLinear
+
+_GEMV_MAX_M = 16
 
 
 class PackedGPTQLinear(B200GPTQLinear):
@@ -53,10 +61,64 @@ class PackedGPTQLinear(B200GPTQLinear):
             self._relayout = False
             self._handle = None
             self._handle_key = None
+            K, N, gs = self.in_features, self.out_features, self.groupsize
+            trivial = torch.arange(K, device=self.g_idx.device, dtype=torch.long) // gs
+            self._gemv8 = (self.wbits == 8 and K >= 64 and K % 8 == 0 and N >= 128 and N % 32 == 0
+                           and (gs == 32 or (gs > 0 and gs % 64 == 0))
+                           and tuple(self.qweight.shape) == (K // 4, N)
+                           and int(self.scales.shape[0]) == (K + gs - 1) // gs
+                           and bool(torch.equal(self.g_idx, trivial)))
+
+    # ------------------------------------------------------------------ 8-bit decode GEMV
+    def _get_handle8(self):
+        key = (self.qweight.data_ptr(), self.qzeros.data_ptr(), self.scales.data_ptr(), self.scales.dtype,
+               self.qweight.device)
+        if self._handle is not None and self._handle_key == key:
+            return self._handle
+        self._release_handle()
+        _lib.require_b200(self.qweight.device)
+        h = ctypes.c_void_p()
+        with torch.cuda.device(self.qweight.device):
+            _lib.call("oc_b200_gptq_layer_create_ex", self.qweight.data_ptr(), self.qzeros.data_ptr(),
+                      self.scales.data_ptr(), _lib.DT[self.scales.dtype], None, None, self.in_features,
+                      self.in_features, self.out_features, int(self.scales.shape[0]), self.groupsize, 8,
+                      int(self.v1), ctypes.byref(h))
+        self._handle = h
+        self._handle_key = key
+        return h
+
+    def _use_gemv8(self, x: torch.Tensor, M: int) -> bool:
+        return (self._gemv8 and 0 < M <= _GEMV_MAX_M and x.is_cuda and x.dtype in (torch.float16, torch.bfloat16)
+                and self.scales.dtype in (torch.float16, torch.bfloat16) and self.qweight.device == x.device
+                and all(t.data_ptr() % 16 == 0 for t in (self.qweight, self.qzeros, self.scales)))
+
+    def _forward_gemv8(self, x: torch.Tensor, M: int) -> torch.Tensor:
+        lead = x.shape[:-1]
+        a_2d = x.reshape(M, self.in_features)
+        if a_2d.stride(1) != 1 or a_2d.stride(0) % 8 != 0 or a_2d.data_ptr() % 16 != 0:
+            a_2d = a_2d.contiguous()
+            if a_2d.data_ptr() % 16 != 0:
+                a_2d = a_2d.clone()
+        out = torch.empty((M, self.out_features), dtype=x.dtype, device=x.device)
+        h = self._get_handle8()
+        lib = _lib.lib()
+        ws = _lib.workspace(x.device, lib.oc_b200_gptq_gemm_workspace(h, M))
+        bias = self.bias
+        _lib.check(lib.oc_b200_gptq_gemm(h, a_2d.data_ptr(), _lib.DT[x.dtype], M, a_2d.stride(0),
+                                         None if bias is None else bias.data_ptr(),
+                                         _lib.DT[bias.dtype] if bias is not None else 0, out.data_ptr(),
+                                         out.stride(0), ws.data_ptr(), ws.numel(), _lib.stream_of(x.device)),
+                   "oc_b200_gptq_gemm (8-bit)")
+        return out.reshape(*lead, self.out_features)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if self.wbits == 4:
             return self._forward_impl(x, "packed")
+        if x.shape[-1] != self.in_features:
+            raise ValueError(f"expected last dim {self.in_features}, got {tuple(x.shape)}")
+        M = x.numel() // self.in_features
+        if self._use_gemv8(x, M):
+            return self._forward_gemv8(x, M)
         weight = dequant_gptq_to_fp(qweight=self.qweight, scales=self.scales, qzeros=self.qzeros,
                                     g_idx=self.g_idx, in_features=self.in_features,
                                     out_features=self.out_features, dtype=x.dtype, v1=self.v1, wbits=self.wbits)
@@ -66,6 +128,7 @@ class PackedGPTQLinear(B200GPTQLinear):
     def _apply(self, fn, recurse=True):
         if self.wbits == 4:
             return super()._apply(fn, recurse=recurse)
+        self._release_handle()
         qw, qz, gi = self.qweight, self.qzeros, self.g_idx
         result = torch.nn.Module._apply(self, fn, recurse=recurse)
         if self.qweight.dtype != torch.int32:

@@ -37,16 +37,17 @@ def pack_along_k(codes_nk: torch.Tensor, wbits: int = 4) -> torch.Tensor:
 
 def gptq_layer(K: int, N: int, groupsize: int, *, seed: int = 0, v1: bool = True, actorder: bool = False,
                scales_range=(0.002, 0.02), bias: bool = True, device="cpu",
-               scales_dtype=torch.float16) -> dict:
-    """Random AutoGPTQ int4 layer: ``qweight, qzeros, scales, g_idx, bias`` (+ ``codes`` on request)."""
+               scales_dtype=torch.float16, wbits: int = 4) -> dict:
+    """Random AutoGPTQ layer (4- or 8-bit codes): ``qweight, qzeros, scales, g_idx, bias``."""
     gen_dev = torch.device(device)
     g = torch.Generator(device=gen_dev).manual_seed(int(seed))
     G = (K + groupsize - 1) // groupsize
-    qweight = torch.randint(-2**31, 2**31, (K // 8, N), generator=g, device=gen_dev, dtype=torch.int64)
+    qmax = (1 << wbits) - 1
+    qweight = torch.randint(-2**31, 2**31, (K * wbits // 32, N), generator=g, device=gen_dev, dtype=torch.int64)
     qweight = qweight.to(torch.int32)
-    zero = torch.randint(1, 16, (G, N), generator=g, device=gen_dev)
-    stored = (zero - 1) & 15 if v1 else zero
-    qzeros = pack_along_n(stored)
+    zero = torch.randint(1, qmax + 1, (G, N), generator=g, device=gen_dev)
+    stored = (zero - 1) & qmax if v1 else zero
+    qzeros = pack_along_n(stored, wbits)
     lo, hi = scales_range
     scales = (torch.rand((G, N), generator=g, device=gen_dev) * (hi - lo) + lo).to(scales_dtype)
     if actorder:

@@ -36,6 +36,8 @@ GPTQ_CASES = [
     "gptq_v1_gs64_8bit",
     "gptq_v2_irregular_gidx",
     "gptq_v1_gs32_m17",
+    "gptq_v1_gs32_8bit_m5",
+    "gptq_v2_gs128_8bit_bf16",
 ]
 RTN_CASES = ["rtn_grouped", "rtn_perrow", "rtn_gs32_bf16"]
 DSV4_CASES = ["dsv4_int2_gs64", "dsv4_int4_gs128_go", "dsv4_int2_perrow", "dsv4_int4_ragged"]

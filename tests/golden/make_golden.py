@@ -85,7 +85,7 @@ def gptq_case(name, *, K, N, gs, wbits=4, v1=True, actorder=False, scales_dtype=
             torch.from_numpy(qweight), scales_t, torch.from_numpy(qzeros),
             torch.from_numpy(g_idx), K, N, _tdt(od), v1=v1, wbits=wbits)
         data[f"w_{od}"] = _bits(w)
-    if M and wbits == 4:
+    if M:
         x32 = rng.standard_normal((M, K)).astype(np.float32)
         b32 = (rng.standard_normal(N) * 0.02).astype(np.float32)
         for od in out_dtypes:
@@ -97,7 +97,14 @@ def gptq_case(name, *, K, N, gs, wbits=4, v1=True, actorder=False, scales_dtype=
             entry = dict(name="l", wbits=wbits, groupsize=gs, actorder=actorder,
                          in_features=K, out_features=N,
                          checkpoint_format="gptq" if v1 else "gptq_v2")
-            lin = backend.build_eager(entry, st, dt, torch.device("cpu"))
+            if wbits == 4:
+                lin = backend.build_eager(entry, st, dt, torch.device("cpu"))
+            else:
+                # the reference's build_eager dequantizes with the default wbits=4
+                # (backend.py:253-257); its PackedGPTQLinear passes wbits through
+                from onecomp_runtime.layers.packed_gptq_linear import PackedGPTQLinear
+                lin = PackedGPTQLinear(K, N, st["qweight"], st["scales"], st["qzeros"], st["g_idx"],
+                                       st.get("bias"), gs, wbits, v1)
             x = torch.from_numpy(x32).to(dt)
             with torch.no_grad():
                 y = lin(x)
@@ -237,6 +244,9 @@ def main():
     gptq_case("gptq_v1_gs64_8bit", K=128, N=64, gs=64, wbits=8, seed=5)
     gptq_case("gptq_v2_irregular_gidx", K=256, N=32, gs=32, v1=False, g_idx_mode="irregular", M=2, seed=6)
     gptq_case("gptq_v1_gs32_m17", K=192, N=72, gs=32, M=17, bias=False, seed=7)
+    gptq_case("gptq_v1_gs32_8bit_m5", K=512, N=128, gs=32, wbits=8, M=5, seed=8)
+    gptq_case("gptq_v2_gs128_8bit_bf16", K=640, N=256, gs=128, wbits=8, v1=False, scales_dtype="bf16", M=2,
+              seed=9)
     rtn_case("rtn_grouped", out_f=48, in_f=202, ncols=104, groups=2, zeros_dtype="f32",
              scales_dtype="f16", seed=10, M=3)
     rtn_case("rtn_perrow", out_f=40, in_f=96, ncols=48, groups=1, zeros_dtype="f16",

@@ -38,11 +38,12 @@ def tensors_to_np(d: dict) -> dict:
     return out
 
 
-def oracle_weight(t: dict, K: int, N: int, out_name: str, v1: bool = True) -> np.ndarray:
+def oracle_weight(t: dict, K: int, N: int, out_name: str, v1: bool = True, wbits: int = 4) -> np.ndarray:
     """Exact dequantized weight [N, K] (bit patterns) from torch layer tensors."""
     n = tensors_to_np(t)
     s_name = NAME[t["scales"].dtype]
-    return gptq.dequant_gptq(n["qweight"], n["scales"], s_name, n["qzeros"], n["g_idx"], K, N, out_name, v1=v1)
+    return gptq.dequant_gptq(n["qweight"], n["scales"], s_name, n["qzeros"], n["g_idx"], K, N, out_name, v1=v1,
+                             wbits=wbits)
 
 
 def reference_output(x: torch.Tensor, w_bits: np.ndarray, w_name: str, bias: torch.Tensor | None):

@@ -51,7 +51,7 @@ def test_golden_cases(cuda_device, case, path, path_option):
     s = to_torch(d["scales"], m["scales_dtype"])
     gi = torch.from_numpy(d["g_idx"]).to(cuda_device)
     bias = to_torch(d["bias_f16"], "f16") if "bias_f16" in d else None
-    layer = PackedGPTQLinear(m["K"], m["N"], qw, s, qz, gi, bias, m["gs"], 4, m["v1"])
+    layer = PackedGPTQLinear(m["K"], m["N"], qw, s, qz, gi, bias, m["gs"], m["wbits"], m["v1"])
     for od in m["out_dtypes"]:
         x = to_torch(d[f"x_{od}"], od)
         y = layer(x)
@@ -99,6 +99,67 @@ def test_shapes(cuda_device, shape, path, path_option):
     ref = reference_output(x, w, NAME[adt], layer.bias)
     err = max_abs_rel(y, ref)
     assert err < 1e-2, err
+
+
+SHAPES8 = [
+    # M, K, N, gs, v1, act dtype, scales dtype, bias
+    (1, 4096, 4096, 128, True, torch.bfloat16, torch.bfloat16, False),
+    (3, 1000, 256, 32, True, torch.bfloat16, torch.float16, True),     # K not a multiple of the 64-k stage
+    (8, 2048, 384, 64, False, torch.float16, torch.float16, True),
+    (9, 1536, 640, 192, True, torch.bfloat16, torch.bfloat16, True),   # 3 stages per group
+    (16, 4096, 1024, 32, False, torch.float16, torch.bfloat16, False),
+    (17, 512, 256, 32, True, torch.bfloat16, torch.float16, True),     # M > 16: dequant + GEMM
+]
+
+
+@pytest.mark.parametrize("shape", SHAPES8, ids=lambda s: f"M{s[0]}K{s[1]}N{s[2]}g{s[3]}")
+def test_gemv_8bit(cuda_device, shape):
+    """8-bit PackedGPTQLinear: the 8-bit decode GEMV for M <= 16 against the oracle weights."""
+    M, K, N, gs, v1, adt, sdt, has_bias = shape
+    from onecomp_runtime import _lib
+    from onecomp_runtime.layers import PackedGPTQLinear
+    from onecomp_runtime.testing import activations, gptq_layer
+    t = gptq_layer(K, N, gs, seed=M * 13 + K, v1=v1, bias=has_bias, scales_dtype=sdt, wbits=8)
+    tc = {k: v.to(cuda_device) for k, v in t.items()}
+    layer = PackedGPTQLinear(K, N, tc["qweight"], tc["scales"], tc["qzeros"], tc["g_idx"], tc.get("bias"), gs, 8, v1)
+    x = activations(M, K, seed=M, dtype=adt).to(cuda_device)
+    assert layer._use_gemv8(x, M) == (M <= 16)
+    y = layer(x)
+    assert y.dtype == adt and y.shape == (M, N)
+    w = oracle_weight(t, K, N, NAME[adt], v1=v1, wbits=8)
+    ref = reference_output(x, w, NAME[adt], layer.bias)
+    err = max_abs_rel(y, ref)
+    assert err < 1e-2, err
+    assert _lib.read_device_error(cuda_device) == 0
+    # a second call on the same workspace (split-K tickets re-armed) gives the same result
+    assert torch.equal(layer(x), y)
+
+
+def test_gemv_8bit_layer_errors(cuda_device):
+    """8-bit handles refuse what the 8-bit GEMV does not cover, with an error (no launch)."""
+    import ctypes
+    from onecomp_runtime import _lib
+    from onecomp_runtime.testing import gptq_layer
+    t = {k: v.to(cuda_device) for k, v in gptq_layer(256, 128, 32, wbits=8, scales_dtype=torch.float16).items()}
+    lib = _lib.lib()
+    h = ctypes.c_void_p()
+    kperm = torch.arange(256, dtype=torch.int32, device=cuda_device)
+    args = (t["qweight"].data_ptr(), t["qzeros"].data_ptr(), t["scales"].data_ptr(), _lib.DT[torch.float16])
+    assert lib.oc_b200_gptq_layer_create_ex(*args, kperm.data_ptr(), None, 256, 256, 128, 8, 32, 8, 1,
+                                            ctypes.byref(h)) != 0
+    assert b"K permutation" in lib.oc_b200_last_error()
+    assert lib.oc_b200_gptq_layer_create_ex(*args, None, None, 256, 256, 128, 8, 48, 8, 1, ctypes.byref(h)) != 0
+    assert lib.oc_b200_gptq_layer_create_ex(*args, None, None, 256, 256, 128, 8, 32, 6, 1, ctypes.byref(h)) != 0
+    assert lib.oc_b200_gptq_layer_create_ex(*args, None, None, 256, 256, 128, 8, 32, 8, 1, ctypes.byref(h)) == 0
+    try:
+        x = torch.zeros((17, 256), dtype=torch.bfloat16, device=cuda_device)
+        y = torch.empty((17, 128), dtype=torch.bfloat16, device=cuda_device)
+        ws = _lib.workspace(cuda_device, lib.oc_b200_gptq_gemm_workspace(h, 17))
+        rc = lib.oc_b200_gptq_gemm(h, x.data_ptr(), _lib.DT[torch.bfloat16], 17, 256, None, 0, y.data_ptr(), 128,
+                                   ws.data_ptr(), ws.numel(), _lib.stream_of(cuda_device))
+        assert rc != 0 and b"8-bit" in lib.oc_b200_last_error()
+    finally:
+        lib.oc_b200_layer_destroy(h)
 
 
 @pytest.mark.parametrize("tile", [128, 192, 256, 384, 448])
