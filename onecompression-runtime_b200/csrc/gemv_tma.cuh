@@ -21,8 +21,9 @@
 // group flush combines them: s * (C_lo + 16 C_hi) - s * (17 M + z) * sum(x) = s * sum(x (q - z)).
 // The MMA count per weight byte is the 4-bit kernel's.
 //
-// CTA: 8 consumer warps (4 column warps x 2 k halves; warp (wn, kh) takes steps 2kh, 2kh+1 of
-// each 4-step stage) + 1 producer warp. Split-K over CTAs as in gemv.cuh (deterministic
+// CTA: 8 consumer warps (4 column warps x 2 stage halves; warp (wn, kh) takes every other
+// stage, kh, kh + 2, ..., all 4 steps of it, so a group of 128 rows is flushed once per 4
+// steps) + 1 producer warp. Split-K over CTAs as in gemv.cuh (deterministic
 // last-CTA reduction). Every mbarrier wait is bounded; on timeout the kernel records an error
 // code, drains its own copies and skips its writes.
 #pragma once
@@ -98,7 +99,7 @@ __global__ void __launch_bounds__(kGtThreads, 2)
   if (threadIdx.x == 0) {
     for (int i = 0; i < Cfg::kDepth; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], kGtConsumerWarps);
+      mbar_init(&empty[i], kGtConsumerWarps / 2);  // the 4 column warps of one stage half
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -203,30 +204,44 @@ __global__ void __launch_bounds__(kGtThreads, 2)
       for (int c = 0; c < 4; ++c) xo[a][c] = 0.f;
     }
   };
+  // fp32 bit pattern of (bias + z) built as z * 2^e + bits(bias): the bias of the codes in the MMA
+  // sums is M (4-bit) or M + 16 M (the two nibbles of 8-bit); z * 2^e lands on the units bit of
+  // the bias's mantissa (bias 128: 2^16, 1024: 2^13, 2176: 2^12, 17408: 2^9).
+  constexpr uint32_t kBiasBits = WB == 8 ? (BF16 ? 0x45080000u : 0x46880000u) : (BF16 ? 0x43000000u : 0x44800000u);
+  constexpr uint32_t kZUnit = WB == 8 ? (BF16 ? 4096u : 512u) : (BF16 ? 65536u : 8192u);
   auto load_sz = [&](const uint8_t* srow, const uint8_t* zrow) {
     const uint2 sv = *reinterpret_cast<const uint2*>(srow + cw * 2);
-    const uint32_t zw = *reinterpret_cast<const uint32_t*>(zrow + (cw * WB / 32) * 4);
-    const uint32_t sw4[4] = {sv.x & 0xFFFFu, sv.x >> 16, sv.y & 0xFFFFu, sv.y >> 16};
+    uint32_t zw = *reinterpret_cast<const uint32_t*>(zrow + (cw * WB / 32) * 4);
     constexpr uint32_t kZMask = (1u << WB) - 1u;
-    // bias of the codes in the MMA sums: M (4-bit), M + 16 M (the two nibbles of 8-bit)
-    constexpr float kBias = WB == 8 ? 17.f * P::kMagicF : P::kMagicF;
+    if (p.v1) {  // (z + 1) mod 2^WB in every field of the word at once
+      constexpr uint32_t kLow = WB == 8 ? 0x7F7F7F7Fu : 0x77777777u;
+      constexpr uint32_t kOne = WB == 8 ? 0x01010101u : 0x11111111u;
+      zw = ((zw & kLow) + kOne) ^ (zw & ~kLow);
+    }
+    float sc[4];
+    if (p.s_dtype == kF16) {
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&sv.x));
+      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&sv.y));
+      sc[0] = a.x; sc[1] = a.y; sc[2] = b.x; sc[3] = b.y;
+    } else {
+      sc[0] = __uint_as_float(sv.x << 16);
+      sc[1] = __uint_as_float(sv.x & 0xFFFF0000u);
+      sc[2] = __uint_as_float(sv.y << 16);
+      sc[3] = __uint_as_float(sv.y & 0xFFFF0000u);
+    }
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      uint32_t z = (zw >> (zsh + WB * j)) & kZMask;
-      if (p.v1) z = (z + 1u) & kZMask;
-      const float sc = (p.s_dtype == kF16) ? __half2float(__ushort_as_half((uint16_t)sw4[j]))
-                                           : __bfloat162float(__ushort_as_bfloat16((uint16_t)sw4[j]));
-      sj[j] = sc;
+      const uint32_t z = (zw >> (zsh + WB * j)) & kZMask;
+      sj[j] = sc[j];
       // exact for 4-bit codes (<= 19 significant bits); 8-bit: exact for bf16 scales, one
       // fp32 rounding for fp16 scales
-      czj[j] = sc * (kBias + (float)z);
+      czj[j] = sc[j] * __uint_as_float(z * kZUnit + kBiasBits);
     }
   };
 
   bool first = true, ok = true;
-  // stages left in the current group (gs >= 128); the first stage's position in its group
-  int stg_left = gp.stages_per_grp - (kb0 % gp.stages_per_grp);
-  for (int i = 0; i < nst; ++i) {
+  int cur_grp = -1;  // group of the warp's last stage when a group spans whole stages
+  for (int i = kh; i < nst; i += 2) {
     const int s = i % Cfg::kDepth;
     if (!mbar_wait(&full[s], (i / Cfg::kDepth) & 1, abort_flag, kDevErrWFull)) {
       ok = false;
@@ -237,16 +252,20 @@ __global__ void __launch_bounds__(kGtThreads, 2)
     const uint8_t* zst = smem + Cfg::kZOff + s * Cfg::kZBytes;
     const uint8_t* xst = smem + Cfg::kXOff + s * Cfg::kXBytes;
 #pragma unroll
-    for (int jj = 0; jj < 2; ++jj) {
-      const int j = 2 * kh + jj;  // step within the stage
+    for (int j = 0; j < 4; ++j) {  // step within the stage
       // group boundaries (warp-uniform)
       bool new_grp;
       int srow;
       if (gp.rows_sz == 1) {
-        new_grp = first || (jj == 0 && stg_left == gp.stages_per_grp);
+        new_grp = false;
+        if (j == 0) {
+          const int grp = ((kb0 + i) * KS) / p.gs;
+          new_grp = grp != cur_grp;
+          cur_grp = grp;
+        }
         srow = 0;
       } else {
-        new_grp = first || (j % spg_step == 0);
+        new_grp = j % spg_step == 0;
         srow = j / spg_step;
       }
       if (new_grp) {
@@ -313,7 +332,6 @@ __global__ void __launch_bounds__(kGtThreads, 2)
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
-    if (--stg_left == 0) stg_left = gp.stages_per_grp;
   }
   if (!first) flush();
 
