@@ -109,6 +109,7 @@ SHAPES8 = [
     (9, 1536, 640, 192, True, torch.bfloat16, torch.bfloat16, True),   # 3 stages per group
     (16, 4096, 1024, 32, False, torch.float16, torch.bfloat16, False),
     (17, 512, 256, 32, True, torch.bfloat16, torch.float16, True),     # M > 16: dequant + GEMM
+    (4, 2048, 256, 256, False, torch.bfloat16, torch.bfloat16, True),  # a group spans 4 stages
 ]
 
 
@@ -317,6 +318,8 @@ GEMV_IMPL_SHAPES = [
     (8, 5120, 1024, 128, False, True, torch.bfloat16),
     (11, 4096, 640, 256, False, False, torch.bfloat16),
     (16, 2176, 512, 128, False, True, torch.float16),
+    (2, 6144, 256, 512, True, False, torch.float16),     # a group spans 4 stages
+    (5, 4160, 384, 64, True, False, torch.bfloat16),     # K not a multiple of the 128-k stage
 ]
 
 
