@@ -8,6 +8,11 @@ device by ``build_meta_model``, every quantized Linear is swapped for the module
 ``backend.build_quant_layer`` returns, the remaining tensors are materialised on
 the device, key checks run, and the unique layer signatures are warmed up.
 ``backend`` accepts ``"b200"`` (the default ``"auto"`` resolves to it).
+
+``io="stream"`` (the default) reads the checkpoint with ``_io.DeviceStreamer``: tensor bytes
+go from the file into pinned staging buffers and on to the device in large asynchronous copies,
+overlapped with the reads, before the layers are built from the device tensors. ``io="simple"``
+reads tensor by tensor as the reference does.
 """
 from __future__ import annotations
 
@@ -19,6 +24,7 @@ from typing import Any, Callable
 import torch
 from safetensors import safe_open
 
+from ._io import DeviceStreamer
 from .backend import build_quant_layer, resolve_backend, resolve_dtype
 from .layers._gptq_base import B200GPTQLinear
 
@@ -38,14 +44,18 @@ def load_int4_model(
     warmup: bool = True,
     warmup_m_values: tuple[int, ...] = (64, 128, 256, 1024, 4096),
     label: str = "onecomp_runtime",
+    io: str = "stream",
 ) -> torch.nn.Module:
     """Rebuild a packed-int4 diffusion transformer for inference on B200."""
     backend = resolve_backend(backend, use_fused)
     resolved = resolve_dtype(dtype)
     dev = torch.device(device)
     path = Path(checkpoint_path)
+    if io not in ("stream", "simple"):
+        raise ValueError(f"io must be 'stream' or 'simple', got {io!r}")
 
     with safe_open(str(path), framework="pt", device="cpu") as f:
+        streamer = DeviceStreamer(str(path), dev) if io == "stream" else None
         md = f.metadata() or {}
         cfg_json = md.get("config_json")
         quant_layers_json = md.get("quant_layers_json")
@@ -75,33 +85,43 @@ def load_int4_model(
                 key = f"{name}.{suffix}"
                 if key in tensor_keys:
                     quant_keys.add(key)
+        selected = []
         for entry in quant_layers:
             entry["checkpoint_format"] = ckpt_fmt
             name = entry["name"]
             if quant_layer_filter is not None and not quant_layer_filter(name):
                 continue
-            quant_names.append(name)
             parent_name, _, child = name.rpartition(".")
             parent = modules.get(parent_name) if parent_name else model
             if parent is None:
                 raise KeyError(f"quant layer parent not found: {parent_name!r}")
+            selected.append((entry, parent, child))
+        non_quant_keys = [k for k in sorted(tensor_keys) if k not in quant_keys
+                          and (tensor_filter is None or tensor_filter(k))]
+
+        if streamer is not None:  # every needed tensor to the device in a few large copies
+            wanted = [f"{e['name']}.{s}" for e, _, _ in selected
+                      for s in ("qweight", "scales", "qzeros", "g_idx", "bias") if f"{e['name']}.{s}" in tensor_keys]
+            dev_tensors = streamer.load(wanted + non_quant_keys)
+            get = dev_tensors.pop
+        else:
+            get = f.get_tensor
+        for entry, parent, child in selected:
+            name = entry["name"]
+            quant_names.append(name)
             st: dict[str, Any] = {}
             for s in ("qweight", "scales", "qzeros", "g_idx", "bias"):
                 k = f"{name}.{s}"
                 if k in tensor_keys:
-                    st[s] = f.get_tensor(k)
+                    st[s] = get(k)
             layer, kind = build_quant_layer(entry, st, backend, resolved, dev)
             counts[kind] += 1
             setattr(parent, child, layer)
             del st
 
         non_quant = {}
-        for k in tensor_keys:
-            if k in quant_keys:
-                continue
-            if tensor_filter is not None and not tensor_filter(k):
-                continue
-            tensor = f.get_tensor(k)
+        for k in non_quant_keys:
+            tensor = get(k)
             non_quant[k] = tensor.to(device=dev, dtype=resolved if tensor.dtype.is_floating_point else tensor.dtype)
             del tensor
     missing, unexpected = model.load_state_dict(non_quant, strict=False, assign=True)

@@ -110,3 +110,71 @@ def dsv4_packed(out_f: int, in_f: int, wbits: int, groupsize: int, *, seed: int 
         zeros = torch.full((out_f, G), zero, dtype=torch.float16, device=device)
     return {"qweight_packed": packed, "scales": scales, "qzeros": zeros, "wbits": wbits, "groupsize": groupsize,
             "in_features": in_f}
+
+
+# --------------------------------------------------------------------- packed checkpoints
+class TinyBlock(torch.nn.Module):
+    """A DiT-style block (pre-norm attention-shaped and MLP linears) for loader tests."""
+
+    def __init__(self, hidden: int, mlp: int) -> None:
+        super().__init__()
+        self.norm1 = torch.nn.LayerNorm(hidden)
+        self.qkv = torch.nn.Linear(hidden, 3 * hidden)
+        self.proj = torch.nn.Linear(hidden, hidden)
+        self.norm2 = torch.nn.LayerNorm(hidden)
+        self.fc1 = torch.nn.Linear(hidden, mlp)
+        self.fc2 = torch.nn.Linear(mlp, hidden)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        h = self.qkv(self.norm1(x))
+        x = x + self.proj(h[..., : x.shape[-1]])
+        return x + self.fc2(torch.nn.functional.gelu(self.fc1(self.norm2(x)), approximate="tanh"))
+
+
+class TinyDiT(torch.nn.Module):
+    def __init__(self, cfg: dict) -> None:
+        super().__init__()
+        self.embed = torch.nn.Linear(cfg["in_channels"], cfg["hidden"])
+        self.blocks = torch.nn.ModuleList(TinyBlock(cfg["hidden"], cfg["mlp"]) for _ in range(cfg["blocks"]))
+        self.out = torch.nn.Linear(cfg["hidden"], cfg["in_channels"])
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        h = self.embed(x)
+        for b in self.blocks:
+            h = b(h)
+        return self.out(h)
+
+
+def write_int4_checkpoint(path, cfg: dict, *, groupsize: int = 32, seed: int = 0, v1: bool = True,
+                          actorder: bool = False, extra: dict | None = None) -> list[dict]:
+    """Write a OneCompression packed checkpoint of ``TinyDiT(cfg)``: every block Linear as a
+    random AutoGPTQ int4 layer (``qweight, scales, qzeros, g_idx, bias``), the rest as bf16
+    tensors, with the ``config_json`` / ``quant_layers_json`` / ``checkpoint_format`` metadata
+    the loader reads. ``extra`` adds tensors. Returns the quant-layer entries."""
+    import json
+
+    from safetensors.torch import save_file
+
+    torch.manual_seed(seed)
+    model = TinyDiT(cfg)
+    tensors, entries = {}, []
+    for i, blk in enumerate(model.blocks):
+        for lname in ("qkv", "proj", "fc1", "fc2"):
+            lin = getattr(blk, lname)
+            name = f"blocks.{i}.{lname}"
+            K, N = lin.in_features, lin.out_features
+            t = gptq_layer(K, N, groupsize, seed=seed * 1000 + len(entries), v1=v1, actorder=actorder)
+            for k, v in t.items():
+                tensors[f"{name}.{k}"] = v.contiguous()
+            entries.append(dict(name=name, wbits=4, groupsize=groupsize, actorder=actorder, in_features=K,
+                                out_features=N))
+    quant = {e["name"] for e in entries}
+    for k, v in model.state_dict().items():
+        if k.rsplit(".", 1)[0] not in quant:
+            tensors[k] = v.to(torch.bfloat16).contiguous()
+    if extra:
+        tensors.update(extra)
+    meta = {"config_json": json.dumps(cfg), "quant_layers_json": json.dumps(entries),
+            "checkpoint_format": "gptq" if v1 else "gptq_v2"}
+    save_file(tensors, str(path), metadata=meta)
+    return entries
