@@ -274,20 +274,28 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
       const int nn = n < p.N ? n : 0;
       const void* sb = p.sptr[e];
       const void* zb = p.zptr[e];
+      const long long s_row = (long long)nn * p.s_stride_n;
       for (int kb = 0; kb < KB; ++kb, ++it) {
         if ((it & 1) != wg) continue;
         const int sw = it % W_STAGES, pw = (it / W_STAGES) & 1;
         const int sa = it % A_STAGES, pa = (it / A_STAGES) & 1;
+        // group constants of the block's words: one division per k-block, then the group
+        // advances where a word starts on a group boundary (gs is a multiple of kSpan)
         RowsConst<BF16, MODE> cst[kWords];
-        int last = -1;
+        const int kbase = kb * 64;
+        int grp = kbase / p.gs;
+        int next_k = (grp + 1) * p.gs;
 #pragma unroll
         for (int w = 0; w < kWords; ++w) {
-          const int k0 = kb * 64 + w * kSpan;
-          const int grp = (k0 < p.K) ? k0 / p.gs : 0;
-          if (grp != last) {
-            const long long si = (long long)nn * p.s_stride_n + (long long)grp * p.s_stride_g;
+          const int k0 = kbase + w * kSpan;
+          const bool fresh = (w == 0) || (k0 >= next_k && k0 < p.K);
+          if (w > 0 && fresh) {
+            ++grp;
+            next_k += p.gs;
+          }
+          if (fresh) {
+            const long long si = s_row + (long long)(k0 < p.K ? grp : 0) * p.s_stride_g;
             cst[w] = rows_const<BF16, MODE>(load_as_f32(sb, p.s_dtype, si), load_as_f32(zb, p.z_dtype, si));
-            last = grp;
           } else {
             cst[w] = cst[w > 0 ? w - 1 : 0];
           }
