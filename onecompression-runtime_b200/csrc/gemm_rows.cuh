@@ -48,7 +48,12 @@ struct RowsParams {
   int n_tiles_n;
 };
 
-constexpr int kRowsThreads = 512;
+// warps: 0 activation TMA, 1 MMA issuer, 2 weight TMA (and the m-tile prefix), 3 idle,
+// 4 .. 4 + 4 kRowsDqGroups - 1 dequant warpgroups (k-block it goes to group it % kRowsDqGroups),
+// the last 4 the epilogue
+constexpr int kRowsDqGroups = 4;
+constexpr int kRowsEpiWarp0 = 4 + 4 * kRowsDqGroups;
+constexpr int kRowsThreads = 32 * (kRowsEpiWarp0 + 4);
 
 template <int WBITS, int BT, int ACC_STAGES, int X_STAGES, int W_STAGES, int A_STAGES>
 struct RowsCfg {
@@ -57,7 +62,8 @@ struct RowsCfg {
   static constexpr int kAccCols = ACC_STAGES * BT;
   static constexpr int kACols = A_STAGES * 32;
   static_assert(kAccCols + kACols <= 512, "TMEM budget");
-  static_assert(W_STAGES % 2 == 0 && A_STAGES % 2 == 0, "two dequant warpgroups alternate stages");
+  static_assert(W_STAGES % kRowsDqGroups == 0 && A_STAGES % kRowsDqGroups == 0,
+                "the dequant warpgroups take stages in turn");
   static constexpr int kXStageBytes = BT * 128;
   static constexpr int kSmemBytes = X_STAGES * kXStageBytes + W_STAGES * kWStageBytes + 1024 +
                                     (2 * (X_STAGES + W_STAGES + A_STAGES + ACC_STAGES) + 2) * 8 + 64 +
@@ -256,7 +262,7 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
         mbar_drain(drain, 0);
       }
     }
-  } else if (warp >= 4 && warp < 12) {
+  } else if (warp >= 4 && warp < kRowsEpiWarp0) {
     // ------------------------------------------------------------ dequant warpgroups
     using Pp = Pair<BF16>;
     constexpr int kWords = Cfg::kKbBytes / 4;     // 32-bit words per row per k-block (8 or 4)
@@ -276,7 +282,7 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
       const void* zb = p.zptr[e];
       const long long s_row = (long long)nn * p.s_stride_n;
       for (int kb = 0; kb < KB; ++kb, ++it) {
-        if ((it & 1) != wg) continue;
+        if ((it % kRowsDqGroups) != wg) continue;
         const int sw = it % W_STAGES, pw = (it / W_STAGES) & 1;
         const int sa = it % A_STAGES, pa = (it / A_STAGES) & 1;
         // group constants of the block's words: one division per k-block, then the group
@@ -345,7 +351,7 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
         mbar_arrive(&full_a[sa]);
       }
     }
-  } else if (warp >= 12) {
+  } else if (warp >= kRowsEpiWarp0) {
     const int q4 = warp & 3;
     const int row = q4 * 32 + lane;
     const int odt = BF16 ? kBF16 : kF16;
