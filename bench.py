@@ -239,7 +239,9 @@ def time_cpu(run, warmup: int, steps: int) -> float:
 
 # ----------------------------------------------------------------------------- decode (cfg2)
 def bench_decode(args):
-    """gptq_v2 gs128 act-order layer set, M in {1, 4, 16}, CUDA-graph replayed.
+    """gptq_v2 gs128 act-order layer set (fp16 scales, bf16 activations),
+    M in {1, 4, 16}, CUDA-graph replayed. ``--wbits 8``: the same shapes as 8-bit gs128 layers
+    without act-order and with bf16 scales (the model dtype), as the Qwen3.6 adapter builds them.
 
     Reported value: packed bytes streamed per second (qweight + scales + qzeros
     + g_idx of the 5 layers, + activations) at the largest M; every M in ``per_m``.
@@ -264,7 +266,7 @@ def bench_decode(args):
             nbytes += K * N + 2 * G * N + G * N
         else:
             t = gptq_layer(K, N, 128, seed=2000 + i, v1=False, actorder=True, scales_range=(0.001, 0.01),
-                           scales_dtype=torch.bfloat16, bias=False, device=dev)
+                           scales_dtype=torch.float16, bias=False, device=dev)  # config 2: fp16 scales
             layers.append(PackedGPTQLinear(K, N, t["qweight"], t["scales"], t["qzeros"], t["g_idx"], None, 128, 4,
                                            False))
             nbytes += K * N // 2 + 2 * G * N + G * N // 2 + 4 * K
@@ -354,6 +356,8 @@ def bench_moe(args):
     world, rank = _dist_init(dev)
     _lib.require_b200(dev)
     E, k, H, F, T = CFG3["E"], CFG3["k"], CFG3["H"], CFG3["F"], CFG3["T"]
+    E = args.moe_experts or E  # profiling only: a smaller case with the same rows per expert
+    T = args.moe_tokens or T
     el = E // world
     wb, gs = CFG3["expert_wbits"], CFG3["expert_gs"]
     experts = [{"gate": dsv4_packed(F, H, wb, gs, seed=3 * e, device=dev),
@@ -461,6 +465,8 @@ def main():
     ap.add_argument("--gemv-ctas", type=int, default=0, help="GEMV split-K target CTAs per SM (0 = default)")
     ap.add_argument("--wbits", type=int, default=4, choices=[4, 8], help="cfg2 only: code width of the layer set")
     ap.add_argument("--blocks", type=int, default=0, help="override the number of DiT blocks (profiling only)")
+    ap.add_argument("--moe-experts", type=int, default=0, help="cfg3: override the expert count (profiling only)")
+    ap.add_argument("--moe-tokens", type=int, default=0, help="cfg3: override tokens per GPU (profiling only)")
     ap.add_argument("--cpu-sample-m", type=int, default=1152,
                     help="tokens of the bounded CPU-baseline sample (one block)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
