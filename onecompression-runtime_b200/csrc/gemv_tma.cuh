@@ -64,7 +64,6 @@ __device__ __forceinline__ void griddep_launch_dependents() {
 struct GtParams {
   GemvParams g;
   int rows_sz;        // scale/zero rows per stage: stage k / gs when gs divides it, else 1
-  int stages_per_grp; // stages per group when gs >= 128 (else 1)
   int kb_per_split;   // stages per split
 };
 

@@ -689,7 +689,6 @@ int launch_gemv_tma(const oc_b200_layer* L, const oc::GemvParams& p, const GemvP
   g.g = p;
   const int ks = L->wbits == 8 ? oc::gt_stage_k<8>() : oc::kGtBK;  // k per stage
   g.rows_sz = L->gt_rows;
-  g.stages_per_grp = L->gs >= ks ? L->gs / ks : 1;
   g.kb_per_split = gp.kstep / (oc::kGtBK / 32);
   const int mt = p.M <= 8 ? 1 : 2;
   CUtensorMap tx;
