@@ -123,11 +123,11 @@ int oc_b200_gptq_layer_create(const int32_t* qweight, const int32_t* qzeros, con
                               int N, int G, int groupsize, int v1, oc_b200_layer** out);
 /* oc_b200_gptq_layer_create with the code width: wbits 4 (as above) or 8. 8-bit layers
  * (quant_utils.py:12-28 with wbits=8; PackedGPTQLinear(wbits=8), packed_gptq_linear.py:66-74)
- * have qweight int32 [in_features/4, N] and qzeros int32 [G, N/4]; they run the decode GEMV
- * only (oc_b200_gptq_gemm with M <= 16; larger M returns OC_ERR_UNSUPPORTED) and need
- * uniform groups (groupsize 32 or a multiple of 64, no k_perm / word_group), N a multiple of
- * 32 and >= 128, in_features >= 64, and 16-byte aligned tensors; other layouts return
- * OC_ERR_UNSUPPORTED. */
+ * have qweight int32 [in_features/4, N] and qzeros int32 [G, N/4]; oc_b200_gptq_gemm runs
+ * them on the decode GEMV (M <= 16) or the tcgen05 GEMM (8-bit stages, exact dequant). They
+ * need uniform groups (groupsize 32 or a multiple of 64, no k_perm / word_group), N a
+ * multiple of 32 and >= 128, in_features >= 64, and 16-byte aligned tensors; other layouts
+ * return OC_ERR_UNSUPPORTED. */
 int oc_b200_gptq_layer_create_ex(const int32_t* qweight, const int32_t* qzeros, const void* scales, int scales_dtype,
                                  const int32_t* k_perm, const int32_t* word_group, int in_features, int k_packed,
                                  int N, int G, int groupsize, int wbits, int v1, oc_b200_layer** out);

@@ -128,6 +128,18 @@ template <> struct Pair<false> {
   __device__ __forceinline__ static float to_f32(uint16_t b) { return __half2float(__ushort_as_half(b)); }
 };
 
+// Two fp32 values rounded (to nearest even) to a bf16x2 / f16x2 pair: lo in the low half.
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack2_rn(float lo, float hi) {
+  if constexpr (BF16) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  } else {
+    const __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
+}
+
 __device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t mask, uint32_t magic) {
   uint32_t d;
   asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(mask), "r"(magic));  // (a & b) | c

@@ -16,6 +16,10 @@
 //     [R x 16 words] (R = 2 for groupsize 32, 1 for multiples of 64); other group
 //     structures read scales/zeros with cached global loads.
 //   * Exact dequant: w = RNE(s*(q-z)) as in quant_utils.dequant_gptq_to_fp.
+//   * 8-bit layers (WB = 8, quant_utils.py:12-28 with wbits=8): a stage carries 16 word rows
+//     (4 k per word); each code becomes the fp32 2^23 + q with one byte permute, q - z and
+//     (q - z) * s are exact in fp32 (8 x 11 significant bits), and one conversion rounds a
+//     pair to the activation dtype -- the reference's single rounding, for every scale dtype.
 // Warp roles (512 threads, one persistent CTA per SM):
 //   warp 0 lane 0: TMA producer of activation tiles
 //   warp 2 lane 0: TMA producer of packed weights/scales/zeros (runs ahead, decoupled)
@@ -55,10 +59,22 @@ constexpr int kTcThreads = 128 * (2 + kTcDqGroups);
 constexpr int kTcEpiWarp0 = 4 + 4 * kTcDqGroups;
 constexpr int kTcBK = 64;            // k per pipeline stage (one 128-byte swizzle atom of 16-bit)
 constexpr int kTcBN = 128;           // output features per tile (= TMEM lanes = UMMA M)
-constexpr int kTcWBytes = 8 * kTcBN * 4;           // packed words of one stage
-constexpr int kTcSOff = kTcWBytes;                  // scale rows [2][128] 16-bit
-constexpr int kTcZOff = kTcSOff + 2 * kTcBN * 2;    // zero rows [2][16] int32
-constexpr int kTcWStageBytes = kTcZOff + 2 * 16 * 4 + 128;  // 4864, multiple of 128
+// One weight stage (64 k): packed words [64 * WB / 32 rows][128], scale rows [2][128] 16-bit,
+// zero rows [2][128 * WB / 32] int32.
+template <int WB>
+struct TcW {
+  static constexpr int kRows = kTcBK * WB / 32;                 // word rows: 8 (4-bit) or 16 (8-bit)
+  static constexpr int kWBytes = kRows * kTcBN * 4;
+  static constexpr int kSOff = kWBytes;
+  static constexpr int kZWords = kTcBN * WB / 32;               // zero words per row: 16 or 32
+  static constexpr int kZOff = kSOff + 2 * kTcBN * 2;
+  static constexpr int kStageBytes = kZOff + 2 * kZWords * 4 + 128;  // 4864 / 9088, multiples of 128
+  static_assert(kStageBytes % 128 == 0, "stage alignment");
+};
+constexpr int kTcWBytes = TcW<4>::kWBytes;
+constexpr int kTcSOff = TcW<4>::kSOff;
+constexpr int kTcZOff = TcW<4>::kZOff;
+constexpr int kTcWStageBytes = TcW<4>::kStageBytes;
 
 constexpr int kTcEpiBufs = 4;                        // staging buffers per epilogue warp
 constexpr int kTcWarpChunkBytes = 32 * 32 * 2;         // one warp's chunk: [32 tokens][32 features] 16-bit
@@ -69,7 +85,7 @@ constexpr int kTcChunkBytes = 4 * kTcWarpChunkBytes;   // the four warps' buffer
 // CG = 2: a cluster of two CTAs (one per SM) computes 256 features x the tile's tokens with
 // cta_group::2 MMAs; each CTA dequantizes its own 128 features and holds half of every
 // activation sub-tile (BT / 2 tokens), so the activation traffic per SM halves.
-template <int BT, int NSUB, int ACC_STAGES, int X_STAGES, int W_STAGES, int A_STAGES, int CG = 1>
+template <int BT, int NSUB, int ACC_STAGES, int X_STAGES, int W_STAGES, int A_STAGES, int CG = 1, int WB = 4>
 struct TcCfg {
   static constexpr int kTileTok = NSUB * BT;
   static constexpr int kAccCols = ACC_STAGES * kTileTok;
@@ -80,20 +96,22 @@ struct TcCfg {
   static constexpr int kXSubBytes = BT / CG * 128;  // this CTA's rows of one activation sub-tile
   static constexpr int kXStageBytes = NSUB * kXSubBytes;
   static constexpr int kEpiBytes = kTcEpiBufs * kTcChunkBytes;
-  static constexpr int kSmemBytes = X_STAGES * kXStageBytes + W_STAGES * kTcWStageBytes + kEpiBytes +
+  static constexpr int kSmemBytes = X_STAGES * kXStageBytes + W_STAGES * TcW<WB>::kStageBytes + kEpiBytes +
                                     1024 /*align*/ +
                                     (2 * (X_STAGES + W_STAGES + A_STAGES + ACC_STAGES) + 2 + 4 * kTcEpiBufs) * 8 + 64;
   static_assert(kSmemBytes <= 232448, "shared memory per CTA");
 };
 
 template <bool BF16, bool HAS_LO, int BT, int NSUB, int ACC_STAGES, int X_STAGES, int W_STAGES, int A_STAGES,
-          int CG>
+          int CG, int WB = 4>
 __global__ void __launch_bounds__(kTcThreads, 1)
     gptq_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
                         const __grid_constant__ CUtensorMap tmap_s, const __grid_constant__ CUtensorMap tmap_z,
                         const __grid_constant__ CUtensorMap tmap_c, const __grid_constant__ CUtensorMap tmap_r,
                         const TcParams p) {
-  using Cfg = TcCfg<BT, NSUB, ACC_STAGES, X_STAGES, W_STAGES, A_STAGES, CG>;
+  using Cfg = TcCfg<BT, NSUB, ACC_STAGES, X_STAGES, W_STAGES, A_STAGES, CG, WB>;
+  using WL = TcW<WB>;
+  static_assert(WB == 4 || (WB == 8 && CG == 1), "8-bit codes: single CTAs");
   constexpr int kTileTok = Cfg::kTileTok;
   // CTA pairs: rank 0 (leader) issues the MMAs and owns the full_x / full_a / empty_acc
   // barriers the pair waits on; both CTAs own their empty_x / empty_a / full_acc barriers,
@@ -105,7 +123,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* x_smem = smem;
   uint8_t* w_smem = x_smem + X_STAGES * Cfg::kXStageBytes;
-  uint8_t* epi_smem = w_smem + W_STAGES * kTcWStageBytes;
+  uint8_t* epi_smem = w_smem + W_STAGES * WL::kStageBytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(epi_smem + Cfg::kEpiBytes);
   uint64_t* full_x = bars;
   uint64_t* empty_x = full_x + X_STAGES;
@@ -122,7 +140,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   const int warp = warp_id(), lane = lane_id();
   const int KB = (p.Kp + kTcBK - 1) / kTcBK;
-  const uint32_t w_tx = kTcWBytes + (p.sz_tma ? p.sz_rows * (kTcBN * 2 + 16 * 4) : 0);
+  const uint32_t w_tx = WL::kWBytes + (p.sz_tma ? p.sz_rows * (kTcBN * 2 + WL::kZWords * 4) : 0);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < X_STAGES; ++i) { mbar_init(&full_x[i], 1); mbar_init(&empty_x[i], 1); }
@@ -216,14 +234,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         for (int kb = 0; kb < KB; ++kb, ++it) {
           const int sw = it % W_STAGES, pw = (it / W_STAGES) & 1;
           if (!mbar_wait(&empty_w[sw], pw ^ 1, abort_flag, kDevErrWEmpty)) { ok = false; break; }
-          uint8_t* ws = w_smem + sw * kTcWStageBytes;
+          uint8_t* ws = w_smem + sw * WL::kStageBytes;
           mbar_arrive_expect_tx(&full_w[sw], w_tx);
           const int fb = nb * CG + (int)rank;  // this CTA's 128-feature block
-          tma_load_2d(ws, &tmap_w, &full_w[sw], fb * kTcBN, kb * 8);
+          tma_load_2d(ws, &tmap_w, &full_w[sw], fb * kTcBN, kb * WL::kRows);
           if (p.sz_tma) {
             const int row0 = (p.sz_rows == 2) ? kb * 2 : (kb * kTcBK) / p.gs;
-            tma_load_2d(ws + kTcSOff, &tmap_s, &full_w[sw], fb * kTcBN, row0);
-            tma_load_2d(ws + kTcZOff, &tmap_z, &full_w[sw], fb * (kTcBN / 8), row0);
+            tma_load_2d(ws + WL::kSOff, &tmap_s, &full_w[sw], fb * kTcBN, row0);
+            tma_load_2d(ws + WL::kZOff, &tmap_z, &full_w[sw], fb * WL::kZWords, row0);
           }
           w_armed[sw] = pw;
         }
@@ -303,67 +321,104 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if ((it % kTcDqGroups) != wg) continue;
         const int sw = it % W_STAGES, pw = (it / W_STAGES) & 1;
         const int sa = it % A_STAGES, pa = (it / A_STAGES) & 1;
-        // per-word group constants
-        DqConst<BF16> cst[8];
-        if (!p.sz_tma) {
-          int last = -1;
-          float sv = 0.f;
-          uint32_t zw = 0;
+        uint32_t r32[32];
+        if constexpr (WB == 8) {
+          // 16 words of 4 codes; uniform groups with scale / zero rows staged by TMA (the host
+          // only builds 8-bit layers that way): row r covers words 8r .. 8r+7 when there are two
+          if (!mbar_wait(&full_w[sw], pw, abort_flag, kDevErrWFull)) { ok = false; break; }
+          const uint8_t* ws = w_smem + sw * WL::kStageBytes;
+          const uint32_t* wt = reinterpret_cast<const uint32_t*>(ws);
+          uint32_t q[16];
 #pragma unroll
-          for (int w = 0; w < 8; ++w) {
-            const int kw = kb * 8 + w;
-            const int grp = (kw < kw_rows) ? (p.wgrp ? __ldg(p.wgrp + kw) : (8 * kw) / p.gs) : 0;
-            if (grp != last) {
-              sv = load_as_f32(p.s, p.s_dtype, (long long)grp * p.N + nn);
-              zw = __ldg(p.qz + (long long)grp * (p.N >> 3) + (nn >> 3));
-              uint32_t z = (zw >> zsh) & 0xFu;
-              if (p.v1) z = (z + 1u) & 0xFu;
-              cst[w] = make_dq_const<BF16>(sv, (int)z);
-              last = grp;
-            } else {
-              cst[w] = cst[w > 0 ? w - 1 : 0];
-            }
-          }
-        }
-        if (!mbar_wait(&full_w[sw], pw, abort_flag, kDevErrWFull)) { ok = false; break; }
-        const uint8_t* ws = w_smem + sw * kTcWStageBytes;
-        const uint32_t* wt = reinterpret_cast<const uint32_t*>(ws);
-        uint32_t q[8];
-#pragma unroll
-        for (int w = 0; w < 8; ++w) q[w] = wt[w * kTcBN + row];
-        if (p.sz_tma) {
-          const uint16_t* st = reinterpret_cast<const uint16_t*>(ws + kTcSOff);
-          const uint32_t* zt = reinterpret_cast<const uint32_t*>(ws + kTcZOff);
-          const int nr = p.sz_rows;
+          for (int w = 0; w < 16; ++w) q[w] = wt[w * kTcBN + row];
+          const uint16_t* st = reinterpret_cast<const uint16_t*>(ws + WL::kSOff);
+          const uint32_t* zt = reinterpret_cast<const uint32_t*>(ws + WL::kZOff);
+          float sr[2], zr[2];  // scale, 2^23 + z of the stage's (up to two) groups
 #pragma unroll
           for (int r = 0; r < 2; ++r) {
-            if (r < nr) {
-              const float sv = (p.s_dtype == kF16) ? __half2float(__ushort_as_half(st[r * kTcBN + row]))
-                                                   : __bfloat162float(__ushort_as_bfloat16(st[r * kTcBN + row]));
-              uint32_t z = (zt[r * 16 + (row >> 3)] >> zsh) & 0xFu;
-              if (p.v1) z = (z + 1u) & 0xFu;
-              const DqConst<BF16> c = make_dq_const<BF16>(sv, (int)z);
-              // words 4r..4r+3 (nr == 2) or all 8 words (nr == 1)
+            const int rr = r < p.sz_rows ? r : 0;
+            const uint16_t sb = st[rr * kTcBN + row];
+            sr[r] = (p.s_dtype == kF16) ? __half2float(__ushort_as_half(sb)) : __bfloat162float(__ushort_as_bfloat16(sb));
+            uint32_t z = (zt[rr * WL::kZWords + (row >> 2)] >> (8 * (row & 3))) & 0xFFu;
+            if (p.v1) z = (z + 1u) & 0xFFu;
+            zr[r] = 8388608.f + (float)z;
+          }
+          mbar_arrive(&empty_w[sw]);
 #pragma unroll
-              for (int w = 0; w < 8; ++w)
-                if ((nr == 1) || (w >> 2) == r) cst[w] = c;
+          for (int w = 0; w < 16; ++w) {
+            const float sv = (w >= 8) ? sr[1] : sr[0];
+            const float zv = (w >= 8) ? zr[1] : zr[0];
+            float v[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float qf = __uint_as_float(prmt(q[w], 0x4B000000u, 0x7540u | (uint32_t)j));  // 2^23 + q_j
+              v[j] = __fmul_rn(__fsub_rn(qf, zv), sv);  // exact: (q - z) * s has <= 19 significant bits
+            }
+            r32[2 * w] = pack2_rn<BF16>(v[0], v[1]);      // k 4w, 4w+1
+            r32[2 * w + 1] = pack2_rn<BF16>(v[2], v[3]);  // k 4w+2, 4w+3
+          }
+        } else {
+          // per-word group constants
+          DqConst<BF16> cst[8];
+          if (!p.sz_tma) {
+            int last = -1;
+            float sv = 0.f;
+            uint32_t zw = 0;
+  #pragma unroll
+            for (int w = 0; w < 8; ++w) {
+              const int kw = kb * 8 + w;
+              const int grp = (kw < kw_rows) ? (p.wgrp ? __ldg(p.wgrp + kw) : (8 * kw) / p.gs) : 0;
+              if (grp != last) {
+                sv = load_as_f32(p.s, p.s_dtype, (long long)grp * p.N + nn);
+                zw = __ldg(p.qz + (long long)grp * (p.N >> 3) + (nn >> 3));
+                uint32_t z = (zw >> zsh) & 0xFu;
+                if (p.v1) z = (z + 1u) & 0xFu;
+                cst[w] = make_dq_const<BF16>(sv, (int)z);
+                last = grp;
+              } else {
+                cst[w] = cst[w > 0 ? w - 1 : 0];
+              }
             }
           }
-        }
-        mbar_arrive(&empty_w[sw]);
+          if (!mbar_wait(&full_w[sw], pw, abort_flag, kDevErrWFull)) { ok = false; break; }
+          const uint8_t* ws = w_smem + sw * WL::kStageBytes;
+          const uint32_t* wt = reinterpret_cast<const uint32_t*>(ws);
+          uint32_t q[8];
+  #pragma unroll
+          for (int w = 0; w < 8; ++w) q[w] = wt[w * kTcBN + row];
+          if (p.sz_tma) {
+            const uint16_t* st = reinterpret_cast<const uint16_t*>(ws + kTcSOff);
+            const uint32_t* zt = reinterpret_cast<const uint32_t*>(ws + kTcZOff);
+            const int nr = p.sz_rows;
+  #pragma unroll
+            for (int r = 0; r < 2; ++r) {
+              if (r < nr) {
+                const float sv = (p.s_dtype == kF16) ? __half2float(__ushort_as_half(st[r * kTcBN + row]))
+                                                     : __bfloat162float(__ushort_as_bfloat16(st[r * kTcBN + row]));
+                uint32_t z = (zt[r * 16 + (row >> 3)] >> zsh) & 0xFu;
+                if (p.v1) z = (z + 1u) & 0xFu;
+                const DqConst<BF16> c = make_dq_const<BF16>(sv, (int)z);
+                // words 4r..4r+3 (nr == 2) or all 8 words (nr == 1)
+  #pragma unroll
+                for (int w = 0; w < 8; ++w)
+                  if ((nr == 1) || (w >> 2) == r) cst[w] = c;
+              }
+            }
+          }
+          mbar_arrive(&empty_w[sw]);
 
-        uint32_t r32[32];
-#pragma unroll
-        for (int w = 0; w < 8; ++w) {
-          const uint32_t qq = q[w];
-          const uint32_t p0 = dq_pair<BF16, HAS_LO>(lop3_and_or(qq, 0x000F000Fu, Pp::kMagic), cst[w]);        // k0,k4
-          const uint32_t p1 = dq_pair<BF16, HAS_LO>(lop3_and_or(qq >> 4, 0x000F000Fu, Pp::kMagic), cst[w]);   // k1,k5
-          const uint32_t p2 = dq_pair<BF16, HAS_LO>(lop3_and_or(qq >> 8, 0x000F000Fu, Pp::kMagic), cst[w]);   // k2,k6
-          const uint32_t p3 = dq_pair<BF16, HAS_LO>(lop3_and_or(qq >> 12, 0x000F000Fu, Pp::kMagic), cst[w]);  // k3,k7
-          r32[4 * w + 0] = prmt(p0, p1, 0x5410u);  // k0,k1
-          r32[4 * w + 1] = prmt(p2, p3, 0x5410u);  // k2,k3
-          r32[4 * w + 2] = prmt(p0, p1, 0x7632u);  // k4,k5
-          r32[4 * w + 3] = prmt(p2, p3, 0x7632u);  // k6,k7
+  #pragma unroll
+          for (int w = 0; w < 8; ++w) {
+            const uint32_t qq = q[w];
+            const uint32_t p0 = dq_pair<BF16, HAS_LO>(lop3_and_or(qq, 0x000F000Fu, Pp::kMagic), cst[w]);        // k0,k4
+            const uint32_t p1 = dq_pair<BF16, HAS_LO>(lop3_and_or(qq >> 4, 0x000F000Fu, Pp::kMagic), cst[w]);   // k1,k5
+            const uint32_t p2 = dq_pair<BF16, HAS_LO>(lop3_and_or(qq >> 8, 0x000F000Fu, Pp::kMagic), cst[w]);   // k2,k6
+            const uint32_t p3 = dq_pair<BF16, HAS_LO>(lop3_and_or(qq >> 12, 0x000F000Fu, Pp::kMagic), cst[w]);  // k3,k7
+            r32[4 * w + 0] = prmt(p0, p1, 0x5410u);  // k0,k1
+            r32[4 * w + 1] = prmt(p2, p3, 0x5410u);  // k2,k3
+            r32[4 * w + 2] = prmt(p0, p1, 0x7632u);  // k4,k5
+            r32[4 * w + 3] = prmt(p2, p3, 0x7632u);  // k6,k7
+          }
         }
         if (!mbar_wait(&empty_a[sa], pa ^ 1, abort_flag, kDevErrAEmpty)) { ok = false; break; }
         tc_fence_after();

@@ -380,8 +380,20 @@ static int gptq_layer_create8(const int32_t* qweight, const int32_t* qzeros, con
   L->gs = groupsize;
   L->v1 = v1 ? 1 : 0;
   const int rows = groupsize >= ks ? 1 : ks / groupsize;
-  int rc = make_tmap_2d(&L->tmap_gw, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, qweight, (uint64_t)N,
-                        (uint64_t)(in_features / 4), (uint64_t)N * 4, 32, 16, CU_TENSOR_MAP_SWIZZLE_128B);
+  // tcgen05 GEMM (M > 16): 16 word rows (64 k) per stage, scale / zero rows of the 64-k block
+  L->sz_tma = 1;
+  L->sz_rows = groupsize == 32 ? 2 : 1;
+  int rc = make_tmap_2d(&L->tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, qweight, (uint64_t)N,
+                        (uint64_t)(in_features / 4), (uint64_t)N * 4, oc::kTcBN, 16, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (!rc)
+    rc = make_tmap_2d(&L->tmap_s, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, scales, (uint64_t)N, (uint64_t)G, (uint64_t)N * 2,
+                      oc::kTcBN, L->sz_rows, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (!rc)
+    rc = make_tmap_2d(&L->tmap_z, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, qzeros, (uint64_t)(N / 4), (uint64_t)G,
+                      (uint64_t)(N / 4) * 4, oc::kTcBN / 4, L->sz_rows, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (!rc)
+    rc = make_tmap_2d(&L->tmap_gw, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, qweight, (uint64_t)N,
+                      (uint64_t)(in_features / 4), (uint64_t)N * 4, 32, 16, CU_TENSOR_MAP_SWIZZLE_128B);
   if (!rc)
     rc = make_tmap_2d(&L->tmap_gs, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, scales, (uint64_t)N, (uint64_t)G,
                       (uint64_t)N * 2, oc::kGemvCols, rows, CU_TENSOR_MAP_SWIZZLE_NONE);
@@ -601,8 +613,7 @@ bool use_gemv(int64_t M) {
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-// 8-bit layers have the decode GEMV only: M <= 16 whatever OC_OPT_GEMM_PATH says.
-bool layer_gemv(const oc_b200_layer* L, int64_t M) { return L->wbits == 8 ? M <= 16 : use_gemv(M); }
+bool layer_gemv(const oc_b200_layer* L, int64_t M) { return use_gemv(M); }
 
 }  // namespace
 
@@ -728,10 +739,10 @@ struct TcMaps {
   CUtensorMap x, c, r;
 };
 
-template <bool BF16, bool HAS_LO, int BT, int NSUB, int ACC, int XS, int WS, int AS, int CG = 1>
+template <bool BF16, bool HAS_LO, int BT, int NSUB, int ACC, int XS, int WS, int AS, int CG = 1, int WB = 4>
 int launch_tc_t(const TcMaps& tm, const oc_b200_layer* L, const oc::TcParams& p, int dev, cudaStream_t stream) {
-  using Cfg = oc::TcCfg<BT, NSUB, ACC, XS, WS, AS, CG>;
-  auto kern = oc::gptq_gemm_tc_kernel<BF16, HAS_LO, BT, NSUB, ACC, XS, WS, AS, CG>;
+  using Cfg = oc::TcCfg<BT, NSUB, ACC, XS, WS, AS, CG, WB>;
+  auto kern = oc::gptq_gemm_tc_kernel<BF16, HAS_LO, BT, NSUB, ACC, XS, WS, AS, CG, WB>;
   static bool attr_set[kMaxDevices] = {};
   if (dev >= 0 && dev < kMaxDevices && !attr_set[dev]) {
     std::lock_guard<std::mutex> lk(g_mu);
@@ -771,6 +782,10 @@ int launch_tc_t(const TcMaps& tm, const oc_b200_layer* L, const oc::TcParams& p,
 template <bool BF16, bool HAS_LO>
 int launch_tc(int bt, bool pair, const TcMaps& tm, const oc_b200_layer* L, const oc::TcParams& p, int dev,
               cudaStream_t stream) {
+  if (L->wbits == 8) {  // 8-bit stages are twice as large: four weight stages
+    if (bt <= 128) return launch_tc_t<BF16, HAS_LO, 128, 1, 2, 8, 4, 8, 1, 8>(tm, L, p, dev, stream);
+    return launch_tc_t<BF16, HAS_LO, 192, 2, 1, 3, 4, 4, 1, 8>(tm, L, p, dev, stream);
+  }
   if (pair) {  // per CTA: half of each sub-tile's tokens, so the activation stages are half as large
     if (bt == 256) return launch_tc_t<BF16, HAS_LO, 256, 1, 1, 8, 8, 4, 2>(tm, L, p, dev, stream);
     if (bt == 448) return launch_tc_t<BF16, HAS_LO, 224, 2, 1, 5, 4, 2, 2>(tm, L, p, dev, stream);
@@ -826,9 +841,6 @@ extern "C" int oc_b200_gptq_gemm_ex(const oc_b200_layer* L, const void* a, int a
   }
   const bool bf16 = a_dtype == OC_DT_BF16;
   const bool has_lo = L->s_dtype != a_dtype;
-  if (L->wbits == 8 && M > 16)
-    return fail(OC_ERR_UNSUPPORTED, "gptq_gemm: 8-bit layers run the decode GEMV only (M <= 16), M=%lld",
-                (long long)M);
 
   if (layer_gemv(L, M)) {
     const GemvPlan gp = gemv_plan(L, dev);
@@ -870,10 +882,11 @@ extern "C" int oc_b200_gptq_gemm_ex(const oc_b200_layer* L, const void* a, int a
 
   int bt = g_opt_tile.load();
   if (bt == 0) bt = choose_tile(M, (L->N + oc::kTcBN - 1) / oc::kTcBN, sm_count(dev));
+  if (L->wbits == 8) bt = (bt <= 128) ? 128 : 384;  // the two 8-bit presets
   const CUtensorMapDataType tdt = bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   TcMaps tm;
   std::memset(&tm, 0, sizeof(tm));
-  const bool pair = use_pairs(M, bt);
+  const bool pair = L->wbits == 4 && use_pairs(M, bt);
   if (pair && bt != 256 && bt != 384 && bt != 448) bt = 384;
   // rows per activation box: tokens per MMA (tiles of 384 / 448 are two sub-tiles), halved for pairs
   const int sub_rows = (bt > 256 ? bt / 2 : bt) / (pair ? 2 : 1);

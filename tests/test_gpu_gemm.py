@@ -108,14 +108,18 @@ SHAPES8 = [
     (8, 2048, 384, 64, False, torch.float16, torch.float16, True),
     (9, 1536, 640, 192, True, torch.bfloat16, torch.bfloat16, True),   # 3 stages per group
     (16, 4096, 1024, 32, False, torch.float16, torch.bfloat16, False),
-    (17, 512, 256, 32, True, torch.bfloat16, torch.float16, True),     # M > 16: dequant + GEMM
     (4, 2048, 256, 256, False, torch.bfloat16, torch.bfloat16, True),  # a group spans 4 stages
+    # M > 16: the tcgen05 GEMM with 8-bit stages (128- and 384-token presets)
+    (17, 512, 256, 32, True, torch.bfloat16, torch.float16, True),
+    (96, 640, 256, 64, False, torch.bfloat16, torch.bfloat16, False),
+    (200, 1024, 384, 32, True, torch.float16, torch.float16, True),
+    (700, 2048, 512, 128, False, torch.bfloat16, torch.float16, True),
 ]
 
 
 @pytest.mark.parametrize("shape", SHAPES8, ids=lambda s: f"M{s[0]}K{s[1]}N{s[2]}g{s[3]}")
 def test_gemv_8bit(cuda_device, shape):
-    """8-bit PackedGPTQLinear: the 8-bit decode GEMV for M <= 16 against the oracle weights."""
+    """8-bit PackedGPTQLinear (decode GEMV for M <= 16, tcgen05 GEMM above) against the oracle weights."""
     M, K, N, gs, v1, adt, sdt, has_bias = shape
     from onecomp_runtime import _lib
     from onecomp_runtime.layers import PackedGPTQLinear
@@ -124,7 +128,7 @@ def test_gemv_8bit(cuda_device, shape):
     tc = {k: v.to(cuda_device) for k, v in t.items()}
     layer = PackedGPTQLinear(K, N, tc["qweight"], tc["scales"], tc["qzeros"], tc["g_idx"], tc.get("bias"), gs, 8, v1)
     x = activations(M, K, seed=M, dtype=adt).to(cuda_device)
-    assert layer._use_gemv8(x, M) == (M <= 16)
+    assert layer._use_kernel8(x, M)  # every SHAPES8 M is within the kernels' range
     y = layer(x)
     assert y.dtype == adt and y.shape == (M, N)
     w = oracle_weight(t, K, N, NAME[adt], v1=v1, wbits=8)
@@ -137,7 +141,7 @@ def test_gemv_8bit(cuda_device, shape):
 
 
 def test_gemv_8bit_layer_errors(cuda_device):
-    """8-bit handles refuse what the 8-bit GEMV does not cover, with an error (no launch)."""
+    """8-bit handles refuse the layouts their kernels do not cover, with an error (no launch)."""
     import ctypes
     from onecomp_runtime import _lib
     from onecomp_runtime.testing import gptq_layer
@@ -153,12 +157,7 @@ def test_gemv_8bit_layer_errors(cuda_device):
     assert lib.oc_b200_gptq_layer_create_ex(*args, None, None, 256, 256, 128, 8, 32, 6, 1, ctypes.byref(h)) != 0
     assert lib.oc_b200_gptq_layer_create_ex(*args, None, None, 256, 256, 128, 8, 32, 8, 1, ctypes.byref(h)) == 0
     try:
-        x = torch.zeros((17, 256), dtype=torch.bfloat16, device=cuda_device)
-        y = torch.empty((17, 128), dtype=torch.bfloat16, device=cuda_device)
-        ws = _lib.workspace(cuda_device, lib.oc_b200_gptq_gemm_workspace(h, 17))
-        rc = lib.oc_b200_gptq_gemm(h, x.data_ptr(), _lib.DT[torch.bfloat16], 17, 256, None, 0, y.data_ptr(), 128,
-                                   ws.data_ptr(), ws.numel(), _lib.stream_of(cuda_device))
-        assert rc != 0 and b"8-bit" in lib.oc_b200_last_error()
+        assert lib.oc_b200_gptq_gemm_workspace(h, 17) >= 1024
     finally:
         lib.oc_b200_layer_destroy(h)
 
