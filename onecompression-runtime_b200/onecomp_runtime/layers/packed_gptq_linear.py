@@ -66,7 +66,7 @@ class PackedGPTQLinear(B200GPTQLinear):
             self._handle_key = None
             K, N, gs = self.in_features, self.out_features, self.groupsize
             trivial = torch.arange(K, device=self.g_idx.device, dtype=torch.long) // gs
-            self._gemv8 = (self.wbits == 8 and K >= 64 and K % 8 == 0 and N >= 128 and N % 32 == 0
+            self._kernel8_ok = (self.wbits == 8 and K >= 64 and K % 8 == 0 and N >= 128 and N % 32 == 0
                            and (gs == 32 or (gs > 0 and gs % 64 == 0))
                            and tuple(self.qweight.shape) == (K // 4, N)
                            and int(self.scales.shape[0]) == (K + gs - 1) // gs
@@ -91,7 +91,7 @@ class PackedGPTQLinear(B200GPTQLinear):
         return h
 
     def _use_kernel8(self, x: torch.Tensor, M: int) -> bool:
-        return (self._gemv8 and 0 < M <= _KERNEL8_MAX_M and x.is_cuda and x.dtype in (torch.float16, torch.bfloat16)
+        return (self._kernel8_ok and 0 < M <= _KERNEL8_MAX_M and x.is_cuda and x.dtype in (torch.float16, torch.bfloat16)
                 and self.scales.dtype in (torch.float16, torch.bfloat16) and self.qweight.device == x.device
                 and all(t.data_ptr() % 16 == 0 for t in (self.qweight, self.qzeros, self.scales)))
 
