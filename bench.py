@@ -51,7 +51,7 @@ METRIC = "DiT-stack tokens/s (int4 GPTQ linear stack)"
 
 # DRAM traffic measured by ncu (dram__bytes_read.sum + dram__bytes_write.sum) for the dominant
 # kernel of each workload; the commands and per-launch figures are in profiles/.
-TC_TRAFFIC_BYTES_PER_LAUNCH = 102_500_000    # cfg1: mean of qkv, proj, fc1, fc2 launches
+TC_TRAFFIC_BYTES_PER_LAUNCH = 103_200_000    # cfg1: mean of qkv, proj, fc1, fc2 launches
 GEMV_TRAFFIC_BYTES_PER_LAUNCH = 21_852_160   # cfg2: q/k/v layer, M = 1 (algorithmic 21.8 MB)
 
 def load_peaks() -> dict:

@@ -102,6 +102,20 @@ struct TcCfg {
   static_assert(kSmemBytes <= 232448, "shared memory per CTA");
 };
 
+// One 32-token chunk of a warp's epilogue, specialised on the activation and the residual so
+// the per-value loop carries no runtime tests: e[i * 32] (token i, this lane's feature) holds the
+// residual on entry when RES and the rounded output on exit.
+template <bool GELU, bool RES, int ODT>
+__device__ __forceinline__ void epi_chunk(const uint32_t (&v)[32], float bv, uint16_t* e) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    float o = __uint_as_float(v[i]) + bv;
+    if constexpr (GELU) o = gelu_tanh(o);
+    if constexpr (RES) o += bits_to_f32(e[i * 32], ODT);
+    e[i * 32] = f32_to_bits(o, ODT);
+  }
+}
+
 template <bool BF16, bool HAS_LO, int BT, int NSUB, int ACC_STAGES, int X_STAGES, int W_STAGES, int A_STAGES,
           int CG, int WB = 4>
 __global__ void __launch_bounds__(kTcThreads, 1)
@@ -443,7 +457,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // chunks ahead and TMA-stores each finished [32 x 32] chunk (rows past M and features past
     // N are clipped); bulk groups and residual barriers are per warp.
     const int q4 = warp & 3;
-    const int odt = BF16 ? kBF16 : kF16;
     constexpr int kChunks = kTileTok / 32;
     uint16_t* wepi = reinterpret_cast<uint16_t*>(epi_smem) + q4 * (kTcEpiBufs * kTcWarpChunkBytes / 2);
     uint64_t* wres = res_full + q4 * kTcEpiBufs;
@@ -495,12 +508,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         __syncwarp();  // buffer b is free (lane 0 waited for its last store) / holds the residual
         uint16_t* e = wepi + b * (kTcWarpChunkBytes / 2) + lane;
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          float o = __uint_as_float(v[i]) + bv;
-          if (p.act == kActGeluTanh) o = gelu_tanh(o);
-          if (p.residual) o += bits_to_f32(e[i * 32], odt);
-          e[i * 32] = f32_to_bits(o, odt);
+        constexpr int kOdt = BF16 ? kBF16 : kF16;
+        if (p.residual) {
+          if (p.act == kActGeluTanh) epi_chunk<true, true, kOdt>(v, bv, e);
+          else epi_chunk<false, true, kOdt>(v, bv, e);
+        } else {
+          if (p.act == kActGeluTanh) epi_chunk<true, false, kOdt>(v, bv, e);
+          else epi_chunk<false, false, kOdt>(v, bv, e);
         }
         fence_proxy_async_shared();  // generic-proxy smem writes -> visible to the TMA store
         __syncwarp();
