@@ -160,7 +160,10 @@ __global__ void __launch_bounds__(kGtThreads, 2)
   const int cw = wn * 32 + 4 * g;  // column within the tile
   const int col = col0 + cw;
   const int zsh = WB == 8 ? 0 : 4 * (col & 7);
-  const int spg_step = p.gs / KSTEP;  // steps per group when a stage holds several groups
+  // steps per group when a stage holds several groups: 1 or 2 (groups of 32 or 64 rows), so the
+  // per-step tests below are a mask and a shift
+  const int spg_step = p.gs / KSTEP;
+  const int spg_shift = spg_step >= 2 ? 1 : 0;
   const uint32_t ones = BF16 ? 0x3F803F80u : 0x3C003C00u;
   const uint32_t ones4[4] = {ones, ones, ones, ones};
 
@@ -264,8 +267,8 @@ __global__ void __launch_bounds__(kGtThreads, 2)
         }
         srow = 0;
       } else {
-        new_grp = j % spg_step == 0;
-        srow = j / spg_step;
+        new_grp = (j & (spg_step - 1)) == 0;
+        srow = j >> spg_shift;
       }
       if (new_grp) {
         if (!first) flush();
