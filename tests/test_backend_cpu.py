@@ -126,3 +126,20 @@ def test_synthetic_packers_match_oracle():
     np.testing.assert_array_equal(pack_along_k(codes).numpy(), gptq.pack_int_weights(codes.numpy(), 4))
     z = torch.randint(0, 16, (3, 32), generator=g)
     np.testing.assert_array_equal(pack_along_n(z).numpy(), gptq.pack_zeros(z.numpy(), 4))
+
+
+@pytest.mark.parametrize("K,N,gs,actorder,ok", [
+    (512, 256, 128, False, True),    # Qwen3.6-style 8-bit layer: uniform groups of 128
+    (1000, 256, 32, False, True),    # K not a multiple of the 64-k stage
+    (512, 256, 48, False, False),    # groups of 48: neither 32 nor a multiple of 64
+    (512, 64, 128, False, False),    # N below one 128-column tile
+    (512, 256, 128, True, False),    # act-order: dequant + F.linear
+])
+def test_packed_gptq_8bit_kernel_eligibility(K, N, gs, actorder, ok):
+    """Which 8-bit PackedGPTQLinear layers take the 8-bit kernels (decided at construction, no GPU)."""
+    from onecomp_runtime.layers import PackedGPTQLinear
+    from onecomp_runtime.testing import gptq_layer
+    t = gptq_layer(K, N, gs, seed=1, actorder=actorder, wbits=8, bias=False)
+    layer = PackedGPTQLinear(K, N, t["qweight"], t["scales"], t["qzeros"], t["g_idx"], None, gs, 8, True)
+    assert layer._kernel8_ok is ok
+    assert layer.qweight.shape == (K // 4, N) and layer.qzeros.shape == (t["scales"].shape[0], N // 4)
