@@ -6,7 +6,9 @@ kernels must reproduce:
 
 * ``oracle.gptq``  -- AutoGPTQ v1/v2 unpack + dequant (``quant_utils.py:12-69``)
   and the qweight packer (``layers/fused_int4_linear.py:76-91``);
-* ``oracle.rtn``   -- RTN uint8-nibble dequant (``quant_utils.py:72-103``);
+* ``oracle.rtn``   -- RTN uint8-nibble dequant (``quant_utils.py:72-103``), the packed
+  embedding lookup (``layers/packed_linear.py:93-104``) and the conv codecs' RTN encoder
+  (``layers/packed_conv.py:63-90``);
 * ``oracle.dsv4``  -- DSV4 int4/int2 byte-packed dequant
   (``layers/dsv4_packed_linear.py:22-56``);
 * ``oracle.eager`` -- the eager linear (``backend.py:246-264`` + ``F.linear``)
