@@ -60,3 +60,50 @@ def test_null_arguments_rejected_before_any_launch(lib):
     assert rc == 1
     assert lib.oc_b200_gptq_gemm(None, None, 1, 1, 64, None, 0, None, 64, None, 0, None) == 1
     assert lib.oc_b200_gptq_gemm_workspace(None, 4) == 1024
+
+
+def test_layer_create_ex_validation(lib):
+    """wbits and 8-bit layout checks happen on the host, before any device work (the pointers
+    below are never dereferenced)."""
+    from onecomp_runtime import _lib
+    out = ctypes.c_void_p()
+    qw, qz, sc = ctypes.c_void_p(0x10000), ctypes.c_void_p(0x20000), ctypes.c_void_p(0x30000)
+    assert lib.oc_b200_gptq_layer_create_ex(qw, qz, sc, 0, None, None, 256, 256, 128, 8, 32, 3, 1,
+                                            ctypes.byref(out)) != 0
+    assert "wbits" in _lib.last_error()
+    kp = ctypes.c_void_p(0x40000)
+    assert lib.oc_b200_gptq_layer_create_ex(qw, qz, sc, 0, kp, None, 256, 256, 128, 8, 32, 8, 1,
+                                            ctypes.byref(out)) != 0
+    assert "K permutation" in _lib.last_error()
+    assert lib.oc_b200_gptq_layer_create_ex(qw, qz, sc, 0, None, None, 256, 256, 128, 6, 48, 8, 1,
+                                            ctypes.byref(out)) != 0
+    assert "groupsize" in _lib.last_error()
+    assert lib.oc_b200_gptq_layer_create_ex(qw, qz, sc, 0, None, None, 256, 256, 64, 8, 32, 8, 1,
+                                            ctypes.byref(out)) != 0
+    assert "N=64" in _lib.last_error()
+    assert lib.oc_b200_gptq_layer_create_ex(qw, qz, sc, 0, None, None, 256, 256, 128, 7, 32, 8, 1,
+                                            ctypes.byref(out)) != 0
+    assert "G=7" in _lib.last_error()
+    assert not out.value
+
+
+def test_embedding_and_rtn_validation(lib):
+    from onecomp_runtime import _lib
+    p = ctypes.c_void_p(0x10000)
+    # no ids: nothing to do, no device work
+    assert lib.oc_b200_rtn_embedding(None, 0, 10, p, 32, p, 0, p, 0, 64, 1, p, 0, None) == 0
+    assert lib.oc_b200_rtn_embedding(None, -1, 10, p, 32, p, 0, p, 0, 64, 1, p, 0, None) != 0
+    assert lib.oc_b200_rtn_embedding(None, 4, 10, p, 32, p, 0, p, 0, 64, 1, p, 0, None) != 0
+    assert "NULL" in _lib.last_error()
+    assert lib.oc_b200_rtn_embedding(p, 4, 10, p, 32, p, 0, p, 0, 64, 3, p, 0, None) != 0
+    assert "num_groups" in _lib.last_error()
+    assert lib.oc_b200_rtn_embedding(p, 4, 10, p, 32, p, 0, p, 0, 64, 1, p, 9, None) != 0
+    assert "dtype" in _lib.last_error()
+    assert lib.oc_b200_rtn_dequant(p, 32, p, 0, p, 0, 64, 8, 1, p, 9, None) != 0
+    assert "dtype" in _lib.last_error()
+
+
+def test_gemv_noalloc_validation(lib):
+    from onecomp_runtime import _lib
+    assert lib.oc_b200_gptq_gemv_noalloc(None, None, 1, 1, 64, None, 0, None, 64, None) != 0
+    assert "NULL" in _lib.last_error()
