@@ -66,11 +66,14 @@ class ExpertParallelMoE(torch.nn.Module):
 
     ``expert_ffn(x_sorted, offsets_local) -> y_sorted`` runs the local experts on
     rows sorted by local expert id. ``route`` / ``shared`` are callables on the
-    local token shard.
+    local token shard. ``combine(y_sorted, slot_pos, w, shared_out) -> out``, when
+    given, replaces the torch weighted sum (``PackedMoE.combine`` is the fused
+    kernel). On CUDA the shared expert runs on a side stream, issued before the
+    routed rows are exchanged, so it overlaps the all-to-alls and the routed FFN.
     """
 
     def __init__(self, num_experts: int, k: int, expert_ffn: Callable, route: Callable = route_reference,
-                 shared: Callable | None = None, group=None):
+                 shared: Callable | None = None, group=None, combine: Callable | None = None):
         super().__init__()
         self.E = int(num_experts)
         self.k = int(k)
@@ -78,6 +81,23 @@ class ExpertParallelMoE(torch.nn.Module):
         self.route = route
         self.shared = shared
         self.group = group
+        self.combine = combine
+        self._side: dict[int, torch.cuda.Stream] = {}
+
+    def _launch_shared(self, x: torch.Tensor):
+        """(shared_out, side stream or None): the shared expert, on a side stream on CUDA."""
+        if self.shared is None:
+            return None, None
+        if x.device.type != "cuda":
+            return self.shared(x), None
+        idx = x.device.index if x.device.index is not None else torch.cuda.current_device()
+        side = self._side.get(idx)
+        if side is None:
+            side = self._side[idx] = torch.cuda.Stream(device=x.device)
+        side.wait_stream(torch.cuda.current_stream(x.device))
+        with torch.cuda.stream(side):
+            out = self.shared(x)
+        return out, side
 
     def forward(self, x: torch.Tensor, logits: torch.Tensor) -> torch.Tensor:
         world = dist.get_world_size(self.group) if dist.is_initialized() else 1
@@ -87,6 +107,7 @@ class ExpertParallelMoE(torch.nn.Module):
             raise ValueError(f"{E} experts do not split over {world} ranks")
         el = E // world
         T, H = x.shape
+        shared_out, side = self._launch_shared(x)
         ids, w = self.route(logits, K)
         offsets, sorted_token, slot_pos = permute_reference(ids, E)
         x_send = x.index_select(0, sorted_token.long())
@@ -116,10 +137,16 @@ class ExpertParallelMoE(torch.nn.Module):
             y_recv[order] = y_loc
             y_sorted = x.new_empty((T * K, y_recv.shape[1]))
             dist.all_to_all_single(y_sorted, y_recv, ss, rs, group=self.group)
+        if side is not None:
+            cur = torch.cuda.current_stream(x.device)
+            cur.wait_stream(side)
+            shared_out.record_stream(cur)
+        if self.combine is not None:
+            return self.combine(y_sorted, slot_pos, w, shared_out)
         y_tk = y_sorted.index_select(0, slot_pos.long()).view(T, K, -1).float()
         out = (y_tk * w.unsqueeze(-1).float()).sum(1)
-        if self.shared is not None:
-            out = out + self.shared(x).float()
+        if shared_out is not None:
+            out = out + shared_out.float()
         return out.to(x.dtype)
 
 
@@ -164,6 +191,8 @@ class PackedMoE(torch.nn.Module):
     def _ffn(self, handles, xs: torch.Tensor, offsets: torch.Tensor | None) -> torch.Tensor:
         from . import _lib
         P = xs.shape[0]
+        if P == 0:
+            return xs.new_empty((0, handles["down"].N))
         F_ = handles["gate"].N
         g = torch.empty((P, 2 * F_), dtype=xs.dtype, device=xs.device)
         handles["gate"].gemm(xs, g[:, :F_], offsets)
@@ -186,15 +215,44 @@ class PackedMoE(torch.nn.Module):
         T, E = logits.shape
         ids = torch.empty((T, k), dtype=torch.int32, device=logits.device)
         w = torch.empty((T, k), dtype=torch.float32, device=logits.device)
+        if T == 0:
+            return ids, w
         lg = logits.contiguous()
         _lib.call("oc_b200_moe_route", lg.data_ptr(), _lib.DT[lg.dtype], T, E, k, int(self.renorm), ids.data_ptr(),
                   w.data_ptr(), _lib.stream_of(lg.device))
         return ids, w
 
+    def combine(self, y_sorted: torch.Tensor, slot_pos: torch.Tensor, w: torch.Tensor,
+                shared: torch.Tensor | None = None) -> torch.Tensor:
+        """``out[t] = sum_j w[t,j] * y_sorted[slot_pos[t*k+j]] (+ shared[t])`` in one kernel
+        (fp32 sum, one rounding), the combine hook of ``ExpertParallelMoE``."""
+        from . import _lib
+        T, k = w.shape
+        H = y_sorted.shape[1]
+        dev = y_sorted.device
+        y = y_sorted.contiguous()
+        sp = slot_pos.to(device=dev, dtype=torch.int32).contiguous()
+        ww = w.to(device=dev, dtype=torch.float32).contiguous()
+        if y.shape[0] != T * k or sp.numel() != T * k:
+            raise ValueError(f"combine: {y.shape[0]} rows and {sp.numel()} slots for {T} tokens x top-{k}")
+        if shared is not None:
+            if shared.shape != (T, H) or shared.dtype != y.dtype:
+                raise ValueError(f"shared output {tuple(shared.shape)} {shared.dtype}, expected {(T, H)} {y.dtype}")
+            shared = shared.contiguous()
+        out = torch.empty((T, H), dtype=y.dtype, device=dev)
+        if T == 0:
+            return out
+        _lib.call("oc_b200_moe_combine", y.data_ptr(), y.stride(0), sp.data_ptr(), ww.data_ptr(), T, k, H,
+                  None if shared is None else shared.data_ptr(), 0 if shared is None else shared.stride(0),
+                  out.data_ptr(), out.stride(0), _lib.DT[y.dtype], _lib.stream_of(dev))
+        return out
+
     def forward(self, x: torch.Tensor, logits: torch.Tensor) -> torch.Tensor:
         from . import _lib
         T, H = x.shape
         dev = x.device
+        if T == 0:
+            return x.new_empty((0, H))
         st = _lib.stream_of(dev)
         x = x.contiguous()
         ids, w = self.route(logits, self.k)

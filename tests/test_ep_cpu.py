@@ -92,6 +92,28 @@ def test_ep_matches_single_rank(tmp_path, world):
     torch.testing.assert_close(y_ep, y_ref, rtol=1e-5, atol=1e-5)
 
 
+def test_combine_and_shared_hooks_single_process():
+    """The combine hook receives (y_sorted, slot_pos, w, shared_out) and its result is returned;
+    without it the shared expert's output is added to the weighted sum."""
+    from onecomp_runtime.moe import ExpertParallelMoE
+    x, logits = _inputs()
+    ffn = _ffn_factory(_experts(), 0)
+    shared = lambda xx: 0.5 * xx  # noqa: E731
+    plain = ExpertParallelMoE(E, K_TOP, ffn)(x, logits)
+    with_shared = ExpertParallelMoE(E, K_TOP, ffn, shared=shared)(x, logits)
+    torch.testing.assert_close(with_shared, plain + 0.5 * x, rtol=1e-6, atol=1e-6)
+    seen = {}
+
+    def combine(y_sorted, slot_pos, w, shared_out):
+        seen.update(rows=y_sorted.shape[0], slots=slot_pos.numel(), w=tuple(w.shape))
+        y_tk = y_sorted.index_select(0, slot_pos.long()).view(T, K_TOP, -1)
+        return (y_tk * w.unsqueeze(-1)).sum(1) + shared_out
+
+    hooked = ExpertParallelMoE(E, K_TOP, ffn, shared=shared, combine=combine)(x, logits)
+    assert seen == {"rows": T * K_TOP, "slots": T * K_TOP, "w": (T, K_TOP)}
+    torch.testing.assert_close(hooked, with_shared, rtol=1e-6, atol=1e-6)
+
+
 def test_routing_convention_and_permutation():
     from onecomp_runtime.moe import permute_reference, route_reference
     logits = torch.tensor([[0.0, 2.0, 1.0, 2.0], [3.0, 0.0, 0.0, 0.0]])

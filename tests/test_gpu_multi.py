@@ -75,7 +75,7 @@ def test_tp_two_gpus(tmp_path):
     assert float(torch.load(out)[0]) < 2e-2
 
 
-def _ep_worker(rank, world, port, out_path):
+def _ep_worker(rank, world, port, out_path, with_shared):
     dev = _init(rank, world, port)
     from onecomp_runtime.moe import ExpertParallelMoE, PackedMoE
     from onecomp_runtime.testing import dsv4_packed
@@ -83,18 +83,25 @@ def _ep_worker(rank, world, port, out_path):
     experts = [{"gate": dsv4_packed(F, H, 2, 64, seed=3 * e, device=dev),
                 "up": dsv4_packed(F, H, 2, 64, seed=3 * e + 1, device=dev),
                 "down": dsv4_packed(H, F, 2, 64, seed=3 * e + 2, device=dev)} for e in range(E)]
+    shared = None
+    if with_shared:
+        shared = {"gate": dsv4_packed(F, H, 4, 128, seed=900, device=dev),
+                  "up": dsv4_packed(F, H, 4, 128, seed=901, device=dev),
+                  "down": dsv4_packed(H, F, 4, 128, seed=902, device=dev)}
     g = torch.Generator(device=dev).manual_seed(9)
     x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
     logits = torch.randn(T, E, generator=g, device=dev)
     el = E // world
-    local = PackedMoE(experts[rank * el:(rank + 1) * el], None, k=k, device=dev)
-    ep = ExpertParallelMoE(E, k, local.expert_ffn, route=local.route)
+    local = PackedMoE(experts[rank * el:(rank + 1) * el], shared, k=k, device=dev)
+    sh_fn = (lambda xx: local._ffn(local._shared, xx.contiguous(), None)) if with_shared else None
+    ep = ExpertParallelMoE(E, k, local.expert_ffn, route=local.route, shared=sh_fn,
+                           combine=local.combine if with_shared else None)
     sh = T // world
     y = ep(x[rank * sh:(rank + 1) * sh], logits[rank * sh:(rank + 1) * sh])
     ys = [torch.empty_like(y) for _ in range(world)]
     torch.distributed.all_gather(ys, y)
     if rank == 0:
-        ref = PackedMoE(experts, None, k=k, device=dev)(x, logits)
+        ref = PackedMoE(experts, shared, k=k, device=dev)(x, logits)
         y = torch.cat(ys)
         err = float((y.float() - ref.float()).abs().max() / ref.float().abs().max())
         torch.save(torch.tensor([err]), out_path)
@@ -102,8 +109,11 @@ def _ep_worker(rank, world, port, out_path):
     torch.distributed.destroy_process_group()
 
 
-def test_ep_two_gpus(tmp_path):
+@pytest.mark.parametrize("with_shared", [False, True])
+def test_ep_two_gpus(tmp_path, with_shared):
+    """Without a shared expert: the torch combine; with one: the fused combine kernel and the
+    shared expert on the side stream."""
     _need_gpus(2)
     out = tmp_path / "err.pt"
-    mp.spawn(_ep_worker, args=(2, _free_port(), str(out)), nprocs=2, join=True)
+    mp.spawn(_ep_worker, args=(2, _free_port(), str(out), with_shared), nprocs=2, join=True)
     assert float(torch.load(out)[0]) < 1e-2

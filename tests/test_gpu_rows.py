@@ -146,6 +146,26 @@ def test_moe_expert_parallel_single_rank(cuda_device):
     assert float((y_ep.float() - ref).abs().max() / ref.abs().max()) < 1e-2
 
 
+@pytest.mark.parametrize("T", [16, 0])
+def test_moe_expert_parallel_combine_and_shared(cuda_device, T):
+    """World size 1 with the fused combine hook and the shared expert on the side stream:
+    the same kernels as PackedMoE.forward, so the same result."""
+    from onecomp_runtime.moe import ExpertParallelMoE, PackedMoE
+    experts, shared = _moe_setup(E=8)
+    moe = PackedMoE(experts, shared, k=2, device=cuda_device)
+    ep = ExpertParallelMoE(8, 2, moe.expert_ffn, route=moe.route,
+                           shared=lambda xx: moe._ffn(moe._shared, xx.contiguous(), None), combine=moe.combine)
+    g = torch.Generator(device=cuda_device).manual_seed(T + 3)
+    x = torch.randn(T, 256, generator=g, device=cuda_device).to(torch.bfloat16)
+    logits = torch.randn(T, 8, generator=g, device=cuda_device)
+    for _ in range(2):  # the second call reuses the cached side stream
+        y_ep = ep(x, logits)
+        assert y_ep.shape == (T, 256) and y_ep.dtype == torch.bfloat16
+        if T:
+            ref = moe(x, logits).float()
+            assert float((y_ep.float() - ref).abs().max() / ref.abs().max()) < 1e-2
+
+
 def test_no_device_errors_recorded(cuda_device):
     from onecomp_runtime import _lib
     assert _lib.read_device_error(cuda_device) == 0
