@@ -73,6 +73,7 @@ struct RowsCfg {
 template <bool BF16, int MODE>
 struct RowsConst {
   uint32_t zm;   // (z, z) in the pair type (RNE of z)
+  uint32_t zn;   // (-z, -z)
   uint32_t shi;  // RNE(s)
   uint32_t slo;  // exact mode: s - s_hi
 };
@@ -85,9 +86,19 @@ __device__ __forceinline__ RowsConst<BF16, MODE> rows_const(float s, float z) {
   const uint16_t hi = P::from_f32(s);
   const uint16_t lo = P::from_f32(s - P::to_f32(hi));
   c.zm = pack2(zz, zz);
+  c.zn = c.zm ^ 0x80008000u;
   c.shi = pack2(hi, hi);
   c.slo = pack2(lo, lo);
   return c;
+}
+
+// RNE(q - z) pair -> dequantized pair
+template <bool BF16, int MODE, bool HAS_LO>
+__device__ __forceinline__ uint32_t rows_scale(uint32_t d, const RowsConst<BF16, MODE>& c) {
+  using P = Pair<BF16>;
+  if (MODE == kRowsRtn) return P::mul(d, c.shi);
+  if (HAS_LO) return P::fma(d, c.shi, P::mul(d, c.slo));
+  return P::mul(d, c.shi);
 }
 
 // magic-biased code pair (M+c_a, M+c_b) -> dequantized pair
@@ -96,10 +107,31 @@ __device__ __forceinline__ uint32_t rows_dq(uint32_t mq, const RowsConst<BF16, M
   using P = Pair<BF16>;
   const uint32_t q = P::sub(mq, P::kMagic);   // exact integer codes
   const uint32_t d = P::sub(q, c.zm);         // RNE(q - z)
-  if (MODE == kRowsRtn) return P::mul(d, c.shi);
-  if (HAS_LO) return P::fma(d, c.shi, P::mul(d, c.slo));
-  return P::mul(d, c.shi);
+  return rows_scale<BF16, MODE, HAS_LO>(d, c);
 }
+
+// Code pair whose halves sit at mantissa bit offsets (o_lo, o_hi) over the magic:
+// (M + c_a 2^o_lo, M + c_b 2^o_hi). After the exact magic subtraction, one fma with the
+// factors (2^-o_lo, 2^-o_hi) and -z gives RNE(c - z) directly: the scaled code is exact
+// and the fma rounds once, the same value as sub(c, z).
+template <bool BF16, int MODE, bool HAS_LO>
+__device__ __forceinline__ uint32_t rows_dq_at(uint32_t mq, uint32_t unscale, const RowsConst<BF16, MODE>& c) {
+  using P = Pair<BF16>;
+  const uint32_t q = P::sub(mq, P::kMagic);
+  const uint32_t d = P::fma(q, unscale, c.zn);
+  return rows_scale<BF16, MODE, HAS_LO>(d, c);
+}
+
+// (1, 1/4) and (1/16, 1/64) as pairs (low half first)
+template <bool BF16> struct Int2Unscale;
+template <> struct Int2Unscale<true> {
+  static constexpr uint32_t k01 = 0x3E803F80u;   // bf16 (1.0, 0.25)
+  static constexpr uint32_t k23 = 0x3C803D80u;   // bf16 (0.0625, 0.015625)
+};
+template <> struct Int2Unscale<false> {
+  static constexpr uint32_t k01 = 0x34003C00u;   // f16 (1.0, 0.25)
+  static constexpr uint32_t k23 = 0x24002C00u;   // f16 (0.0625, 0.015625)
+};
 
 template <bool BF16, int WBITS, int MODE, bool HAS_LO, int BT, int ACC_STAGES, int X_STAGES, int W_STAGES,
           int A_STAGES>
@@ -330,14 +362,25 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
             r32[4 * w + 2] = prmt(p0, p1, 0x7632u);
             r32[4 * w + 3] = prmt(p2, p3, 0x7632u);
           } else {
-            uint32_t pp[8];  // pp[i] = (code i, code i+8)
+            // byte b holds codes 4b..4b+3 at bits 0,2,4,6. prmt copies it into both halves;
+            // the mask then keeps code 4b in the low half and code 4b+1 (bits 2-3) in the high
+            // half, already the (even k, odd k) order of the A operand. Codes 4b+2, 4b+3 come
+            // from the copy of (q >> 4) in bf16 (7 mantissa bits: bits 6-7 would reach the
+            // exponent) and from the same copy, masked higher, in f16 (10 mantissa bits).
+            const uint32_t qs = qq >> 4;
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
-              pp[i] = rows_dq<BF16, MODE, HAS_LO>(lop3_and_or(qq >> (2 * i), kMask, Pp::kMagic), cst[w]);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              r32[8 * w + j] = prmt(pp[2 * j], pp[2 * j + 1], 0x5410u);       // codes 2j, 2j+1
-              r32[8 * w + 4 + j] = prmt(pp[2 * j], pp[2 * j + 1], 0x7632u);   // codes 2j+8, 2j+9
+            for (int b = 0; b < 4; ++b) {
+              const uint32_t dup = prmt(qq, 0u, 0x0101u * b);
+              r32[8 * w + 2 * b] = rows_dq_at<BF16, MODE, HAS_LO>(lop3_and_or(dup, 0x000C0003u, Pp::kMagic),
+                                                                   Int2Unscale<BF16>::k01, cst[w]);
+              if (BF16) {
+                const uint32_t dup2 = prmt(qs, 0u, 0x0101u * b);
+                r32[8 * w + 2 * b + 1] = rows_dq_at<BF16, MODE, HAS_LO>(
+                    lop3_and_or(dup2, 0x000C0003u, Pp::kMagic), Int2Unscale<BF16>::k01, cst[w]);
+              } else {
+                r32[8 * w + 2 * b + 1] = rows_dq_at<BF16, MODE, HAS_LO>(
+                    lop3_and_or(dup, 0x00C00030u, Pp::kMagic), Int2Unscale<BF16>::k23, cst[w]);
+              }
             }
           }
         }

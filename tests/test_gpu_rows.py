@@ -72,6 +72,23 @@ def test_dsv4_linear_fused(cuda_device, wbits, gs, zeros, M):
     assert max_abs_rel(y, ref) < 1e-2
 
 
+@pytest.mark.parametrize("wbits,gs", [(2, 64), (4, 128), (2, 0)])
+@pytest.mark.parametrize("adt", ["bf16", "f16"])
+def test_dsv4_weights_bit_exact_through_gemm(cuda_device, wbits, gs, adt):
+    """One-hot activation rows make y = W^T exactly (one nonzero product per output, fp32 sum,
+    one exact rounding), so the weights the kernel decodes into the MMA operand are compared bit
+    for bit with the oracle. Half-integer zeros: the exact mode's domain. bf16 activations take
+    the split-scale path (fp16 scales), f16 activations the single-multiply path."""
+    from onecomp_runtime.layers import Dsv4PackedLinear
+    K, N = 512, 192
+    p = _dsv4_layer(N, K, wbits, gs, seed=wbits + gs, zeros="half")
+    layer = Dsv4PackedLinear(p, buffer_device=cuda_device)
+    assert layer._rows_handle() is not None
+    y = layer(torch.eye(K, device=cuda_device, dtype=TDT[adt]))
+    got = y.t().contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+    np.testing.assert_array_equal(got, _dsv4_weight(p, adt))
+
+
 def test_dsv4_host_buffers_match_fused(cuda_device):
     from onecomp_runtime.layers import Dsv4PackedLinear
     p = _dsv4_layer(128, 256, 2, 64, seed=5)
