@@ -63,7 +63,17 @@ def _inputs():
     return torch.randn(T, H, generator=g), torch.randn(T, E, generator=g)
 
 
-def _worker(rank, world, port, out_path):
+def _shared(xx):
+    return 0.5 * xx
+
+
+def _combine(y_sorted, slot_pos, w, shared_out):
+    y_tk = y_sorted.index_select(0, slot_pos.long()).view(w.shape[0], w.shape[1], -1)
+    out = (y_tk * w.unsqueeze(-1)).sum(1)
+    return out if shared_out is None else out + shared_out
+
+
+def _worker(rank, world, port, out_path, hooks=False):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
@@ -71,7 +81,8 @@ def _worker(rank, world, port, out_path):
     x, logits = _inputs()
     shard = T // world
     xs, ls = x[rank * shard:(rank + 1) * shard], logits[rank * shard:(rank + 1) * shard]
-    moe = ExpertParallelMoE(E, K_TOP, _ffn_factory(_experts(), rank * (E // world)))
+    extra = {"shared": _shared, "combine": _combine} if hooks else {}
+    moe = ExpertParallelMoE(E, K_TOP, _ffn_factory(_experts(), rank * (E // world)), **extra)
     y = moe(xs, ls)
     ys = [torch.empty_like(y) for _ in range(world)]
     dist.all_gather(ys, y)
@@ -81,14 +92,17 @@ def _worker(rank, world, port, out_path):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 4])
-def test_ep_matches_single_rank(tmp_path, world):
+@pytest.mark.parametrize("world,hooks", [(2, False), (4, False), (2, True)])
+def test_ep_matches_single_rank(tmp_path, world, hooks):
+    """hooks: a shared expert and a combine callable, as PackedMoE passes them on the GPU."""
     from onecomp_runtime.moe import ExpertParallelMoE
     out = tmp_path / "y.pt"
-    mp.spawn(_worker, args=(world, _free_port(), str(out)), nprocs=world, join=True)
+    mp.spawn(_worker, args=(world, _free_port(), str(out), hooks), nprocs=world, join=True)
     y_ep = torch.load(out)
     x, logits = _inputs()
     y_ref = ExpertParallelMoE(E, K_TOP, _ffn_factory(_experts(), 0))(x, logits)
+    if hooks:
+        y_ref = y_ref + 0.5 * x
     torch.testing.assert_close(y_ep, y_ref, rtol=1e-5, atol=1e-5)
 
 
@@ -98,7 +112,7 @@ def test_combine_and_shared_hooks_single_process():
     from onecomp_runtime.moe import ExpertParallelMoE
     x, logits = _inputs()
     ffn = _ffn_factory(_experts(), 0)
-    shared = lambda xx: 0.5 * xx  # noqa: E731
+    shared = _shared
     plain = ExpertParallelMoE(E, K_TOP, ffn)(x, logits)
     with_shared = ExpertParallelMoE(E, K_TOP, ffn, shared=shared)(x, logits)
     torch.testing.assert_close(with_shared, plain + 0.5 * x, rtol=1e-6, atol=1e-6)
