@@ -376,7 +376,7 @@ def bench_moe(args):
     else:
         loc = PackedMoE(experts, shared, k=k, device=dev)
         ep = ExpertParallelMoE(E, k, loc.expert_ffn, route=loc.route,
-                               shared=lambda xx: loc._ffn(loc._shared, xx.contiguous(), None), combine=loc.combine)
+                               shared=loc.shared_ffn, combine=loc.combine)
         fn = lambda: ep(x, logits)  # noqa: E731
     with torch.no_grad():
         ms = _timed(fn, args.steps, args.warmup, dev, world)

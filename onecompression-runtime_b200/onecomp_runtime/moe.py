@@ -210,6 +210,13 @@ class PackedMoE(torch.nn.Module):
             return xs.new_empty((0, self._h["down"].N))
         return self._ffn(self._h, xs.contiguous(), offsets.to(device=xs.device, dtype=torch.int32))
 
+    def shared_ffn(self, x: torch.Tensor) -> torch.Tensor:
+        """The shared expert's SwiGLU FFN over ``x [T, H]`` (the ``shared`` hook of
+        ``ExpertParallelMoE``)."""
+        if self._shared is None:
+            raise ValueError("this PackedMoE has no shared expert")
+        return self._ffn(self._shared, x.contiguous(), None)
+
     def route(self, logits: torch.Tensor, k: int):
         from . import _lib
         T, E = logits.shape

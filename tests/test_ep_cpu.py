@@ -138,3 +138,24 @@ def test_routing_convention_and_permutation():
     assert off.tolist() == [0, 1, 3, 3, 4]
     assert st.tolist() == [1, 0, 1, 0]                 # expert 0: t1; expert 1: t0, t1; expert 3: t0
     assert sp.tolist() == [1, 3, 0, 2]
+
+
+def test_packed_moe_shared_ffn_hook():
+    """PackedMoE.shared_ffn feeds the shared expert's handles a contiguous [T, H] input (no expert
+    offsets) and refuses a module built without a shared expert; host logic only, on a stub."""
+    from onecomp_runtime.moe import PackedMoE
+
+    class Stub:
+        _shared = {"gate": object()}
+
+        def _ffn(self, handles, xs, offsets):
+            return handles, xs, offsets
+
+    stub = Stub()
+    x = torch.randn(4, 3).t()
+    handles, xs, offsets = PackedMoE.shared_ffn(stub, x)
+    assert handles is stub._shared and xs.is_contiguous() and offsets is None
+    torch.testing.assert_close(xs, x)
+    stub._shared = None
+    with pytest.raises(ValueError, match="no shared expert"):
+        PackedMoE.shared_ffn(stub, x)

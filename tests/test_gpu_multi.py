@@ -93,7 +93,7 @@ def _ep_worker(rank, world, port, out_path, with_shared):
     logits = torch.randn(T, E, generator=g, device=dev)
     el = E // world
     local = PackedMoE(experts[rank * el:(rank + 1) * el], shared, k=k, device=dev)
-    sh_fn = (lambda xx: local._ffn(local._shared, xx.contiguous(), None)) if with_shared else None
+    sh_fn = local.shared_ffn if with_shared else None
     ep = ExpertParallelMoE(E, k, local.expert_ffn, route=local.route, shared=sh_fn,
                            combine=local.combine if with_shared else None)
     sh = T // world

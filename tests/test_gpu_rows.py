@@ -171,7 +171,7 @@ def test_moe_expert_parallel_combine_and_shared(cuda_device, T):
     experts, shared = _moe_setup(E=8)
     moe = PackedMoE(experts, shared, k=2, device=cuda_device)
     ep = ExpertParallelMoE(8, 2, moe.expert_ffn, route=moe.route,
-                           shared=lambda xx: moe._ffn(moe._shared, xx.contiguous(), None), combine=moe.combine)
+                           shared=moe.shared_ffn, combine=moe.combine)
     g = torch.Generator(device=cuda_device).manual_seed(T + 3)
     x = torch.randn(T, 256, generator=g, device=cuda_device).to(torch.bfloat16)
     logits = torch.randn(T, 8, generator=g, device=cuda_device)
