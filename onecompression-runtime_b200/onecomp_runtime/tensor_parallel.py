@@ -62,7 +62,11 @@ def shard_gptq_rows(t: dict, rank: int, world: int, groupsize: int) -> dict:
         "qzeros": t["qzeros"][rank * g:(rank + 1) * g].contiguous(),
     }
     if t.get("g_idx") is not None:
-        out["g_idx"] = (t["g_idx"][rank * k:(rank + 1) * k] - rank * g).contiguous()
+        gi = (t["g_idx"][rank * k:(rank + 1) * k] - rank * g).contiguous()
+        if gi.numel() and (int(gi.min()) < 0 or int(gi.max()) >= g):
+            raise ValueError(f"g_idx of rank {rank}'s rows reaches groups outside its own {g}: an act-order "
+                             "layer does not split along K")
+        out["g_idx"] = gi
     if t.get("bias") is not None and rank == 0:
         out["bias"] = t["bias"]
     return out
