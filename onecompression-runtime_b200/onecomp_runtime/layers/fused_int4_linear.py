@@ -28,7 +28,6 @@ import torch
 
 from .. import _lib
 from ..quant_utils import unpack_int_weights
-from . import _gptq_base
 from ._gptq_base import B200GPTQLinear, _PADDED_GROUPS_STATS, _PROFILE_PADDED_GROUPS
 
 

@@ -5,7 +5,6 @@ import numpy as np
 import torch
 
 from oracle import eager, gptq
-from oracle.fp import to_f32
 
 TDT = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}
 NAME = {torch.bfloat16: "bf16", torch.float16: "f16", torch.float32: "f32"}

@@ -7,7 +7,6 @@ max-abs-relative error <= 2e-2 (north star), and the tests also bound it to
 """
 from __future__ import annotations
 
-import numpy as np
 import pytest
 import torch
 

@@ -28,7 +28,7 @@ def test_gptq_eager_linear_within_tolerance(case):
         bias = d.get("bias_f16")
         # the eager nn.Linear keeps its bias in the compute dtype (backend.py:263)
         if bias is not None:
-            from oracle.fp import quantize, to_f32, round_to
+            from oracle.fp import round_to, to_f32
             bias = round_to(to_f32(bias, "f16"), od)
         y32, _ = eager.linear_ref(d[f"x_{od}"], od, w, od, bias, od if bias is not None else None)
         from oracle.fp import to_f32

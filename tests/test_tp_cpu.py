@@ -19,7 +19,6 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 from oracle import gptq
-from oracle.fp import to_f32
 
 
 def _free_port() -> int:
