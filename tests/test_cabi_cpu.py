@@ -106,3 +106,33 @@ def test_gemv_noalloc_validation(lib):
     from onecomp_runtime import _lib
     assert lib.oc_b200_gptq_gemv_noalloc(None, None, 1, 1, 64, None, 0, None, 64, None) != 0
     assert "NULL" in _lib.last_error()
+
+
+def test_moe_entry_points_validation(lib):
+    """Routing / gather / SwiGLU / combine reject bad arguments before any launch, and an
+    empty batch (with valid pointers) returns at once without device work."""
+    from onecomp_runtime import _lib
+    p = ctypes.c_void_p(0x10000)
+    # route: logits [T, E] -> ids, weights [T, k]
+    assert lib.oc_b200_moe_route(None, 1, 4, 8, 2, 1, p, p, None) != 0
+    assert "NULL" in _lib.last_error()
+    for T, E, k in ((-1, 8, 2), (4, 0, 1), (4, 2048, 2), (4, 8, 0), (4, 8, 17), (4, 4, 5)):
+        assert lib.oc_b200_moe_route(p, 1, T, E, k, 1, p, p, None) != 0, (T, E, k)
+    assert lib.oc_b200_moe_route(p, 7, 4, 8, 2, 1, p, p, None) != 0
+    assert "dtype" in _lib.last_error()
+    assert lib.oc_b200_moe_route(p, 1, 0, 8, 2, 1, p, p, None) == 0
+    # permute: bad sizes
+    assert lib.oc_b200_moe_permute(None, 4, 2, 8, p, p, p, p, None) != 0
+    assert lib.oc_b200_moe_permute(p, 4, 2, 4096, p, p, p, p, None) != 0
+    assert lib.oc_b200_moe_permute(p, -1, 2, 8, p, p, p, p, None) != 0
+    # gather: 16-bit rows of H % 8 == 0, 16-byte aligned
+    assert lib.oc_b200_gather_rows(p, 64, p, 4, 60, p, 64, None) != 0
+    assert lib.oc_b200_gather_rows(ctypes.c_void_p(0x10002), 64, p, 4, 64, p, 64, None) != 0
+    assert lib.oc_b200_gather_rows(p, 64, p, 0, 64, p, 64, None) == 0
+    # silu * mul and combine: 16-bit only
+    assert lib.oc_b200_silu_mul(p, p, 64, 4, 32, p, 32, 2, None) != 0
+    assert lib.oc_b200_silu_mul(p, p, 64, 0, 32, p, 32, 1, None) == 0
+    assert lib.oc_b200_moe_combine(p, 64, p, p, 4, 0, 64, None, 0, p, 64, 1, None) != 0
+    assert lib.oc_b200_moe_combine(p, 64, p, p, 4, 2, 64, None, 0, p, 64, 2, None) != 0
+    assert lib.oc_b200_moe_combine(None, 64, p, p, 4, 2, 64, None, 0, p, 64, 1, None) != 0
+    assert lib.oc_b200_moe_combine(p, 64, p, p, 0, 2, 64, None, 0, p, 64, 1, None) == 0
