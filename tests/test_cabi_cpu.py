@@ -136,3 +136,30 @@ def test_moe_entry_points_validation(lib):
     assert lib.oc_b200_moe_combine(p, 64, p, p, 4, 2, 64, None, 0, p, 64, 2, None) != 0
     assert lib.oc_b200_moe_combine(None, 64, p, p, 4, 2, 64, None, 0, p, 64, 1, None) != 0
     assert lib.oc_b200_moe_combine(p, 64, p, p, 0, 2, 64, None, 0, p, 64, 1, None) == 0
+
+
+def test_rows_layer_validation(lib):
+    """The row-packed layer rejects unsupported layouts before it touches the device (the
+    pointer arrays are not read on these paths)."""
+    from onecomp_runtime import _lib
+    p = ctypes.c_void_p(0x10000)
+    out = ctypes.c_void_p()
+
+    def create(E=2, wbits=2, ld=128, mode=0, K=512, N=256, gs=64, sdt=0, zdt=0, table=p, packed=p):
+        return lib.oc_b200_rows_layer_create(E, packed, ld, wbits, p, sdt, p, zdt, 1, 256, gs, K, N, mode, table,
+                                             None, ctypes.byref(out))
+
+    assert lib.oc_b200_rows_layer_create(2, p, 128, 2, p, 0, p, 0, 1, 256, 64, 512, 256, 0, p, None, None) != 0
+    cases = {
+        "E=": dict(E=0), "E=2000": dict(E=2000), "NULL": dict(packed=None), "wbits": dict(wbits=3),
+        "mode=": dict(mode=2), "RTN layers are 4-bit": dict(mode=1), "K=": dict(K=12),
+        "row stride": dict(ld=64), "groupsize": dict(gs=24), "dtype": dict(sdt=7),
+        "256-byte aligned": dict(table=ctypes.c_void_p(0x10010)),
+    }
+    for msg, kw in cases.items():
+        assert create(**kw) != 0, kw
+        assert msg.split("=")[0] in _lib.last_error(), (kw, _lib.last_error())
+        assert not out.value
+    assert lib.oc_b200_rows_gemm(None, p, 1, 4, 512, None, None, 0, p, 256, None) != 0
+    assert lib.oc_b200_rows_table_bytes(0) == 0
+    assert lib.oc_b200_rows_table_bytes(3) > 0 and lib.oc_b200_rows_table_bytes(3) % 256 == 0
