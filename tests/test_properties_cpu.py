@@ -127,3 +127,35 @@ def test_row_shards_reject_act_order():
     with pytest.raises(ValueError, match="act-order"):
         shard_gptq_rows(t, 0, 2, 32)
     shard_gptq_rows(t, 0, 1, 32)  # one rank keeps the whole layer
+
+
+@settings(max_examples=60, deadline=None)
+@given(G=st.integers(1, 12), gs=st.sampled_from([8, 16, 26, 32, 64, 128]), kind=st.sampled_from(["natural", "perm", "ragged"]),
+       seed=st.integers(0, 10_000))
+def test_plan_k_layout_properties(G, gs, kind, seed):
+    """The kernels' K layout: every input row k appears once, each group occupies whole 8-row
+    words starting on a word boundary, padding rows are -1, and the per-word group table (or the
+    uniform groupsize) names the group of every real row."""
+    from onecomp_runtime.layers._gptq_base import plan_k_layout
+    g = torch.Generator().manual_seed(seed)
+    if kind == "ragged":  # irregular group sizes, some groups empty
+        gi = torch.sort(torch.randint(0, G, (G * gs,), generator=g)).values
+    else:
+        gi = torch.arange(G * gs) // gs
+        if kind == "perm":
+            gi = gi[torch.randperm(G * gs, generator=g)]
+    K = gi.numel()
+    kp, kperm, word_group, gs_eff = plan_k_layout(K, gs, G, None if kind == "natural" else gi)
+    assert kp % 8 == 0 and kp >= K
+    if kperm is None:
+        assert torch.equal(gi, torch.arange(K) // gs) and gs % 8 == 0 and (kp, word_group, gs_eff) == (K, None, gs)
+        return
+    perm = kperm.tolist()
+    real = [k for k in perm if k >= 0]
+    assert sorted(real) == list(range(K)) and len(perm) == kp
+    groups = word_group.tolist() if word_group is not None else [w * 8 // gs_eff for w in range(kp // 8)]
+    assert len(groups) == kp // 8
+    for p, k in enumerate(perm):
+        if k >= 0:
+            assert int(gi[k]) == groups[p // 8]
+    assert groups == sorted(groups)  # groups are contiguous runs of words
