@@ -41,7 +41,12 @@ enum {
   OC_OPT_GEMV_CTAS = 3,    /* GEMV CTAs per SM that split-K sizing fills in one wave (default 2) */
   OC_OPT_GEMV_IMPL = 4,    /* decode kernel for uniform-group layers: 0 tcgen05, 1 TMA + mma.sync (default),
                               2 cp.async + mma.sync */
-  OC_OPT_TC_PAIR = 5       /* tcgen05 GEMM on CTA pairs (cta_group::2): 0 auto, 1 single CTAs (default), 2 pairs */
+  OC_OPT_TC_PAIR = 5,      /* tcgen05 GEMM on CTA pairs (cta_group::2): 0 auto, 1 single CTAs (default), 2 pairs */
+  OC_OPT_WAIT_US = 6,      /* failure tests: bound of the TMA decode GEMV's pipeline waits in microseconds
+                              (0, the default: 2 s); drains of copies in flight keep the 2 s bound */
+  OC_OPT_TEST_STALL = 7    /* failure tests: s > 0 makes the first CTA of each TMA decode GEMV leave stage
+                              s - 1 unissued, so a wait runs out, the kernel records OC_ERR_DEVICE's code,
+                              skips that tile's output and leaves its tickets re-armed; 0 (default) off */
 };
 
 /* ---- library / device ------------------------------------------------------ */
@@ -51,6 +56,8 @@ const char* oc_b200_last_error(void);
  * capability gate of backend.resolve_backend (backend.py:103-144). */
 int oc_b200_device_check(int device);
 int oc_b200_set_option(int key, int value);
+/* Current value of an OC_OPT_* option (process-wide). */
+int oc_b200_get_option(int key, int* value);
 /* Copies the kernels' device error word into *code (0 = none) and clears it.
  * Synchronises `stream`. */
 int oc_b200_read_device_error(int* code, oc_stream_t stream);

@@ -222,21 +222,26 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
 }
 
 // Bounded wait: returns false (and records `code`) if the phase does not complete
-// within OC_WAIT_NS, or as soon as another role of this CTA has aborted.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          unsigned code) {
+// within `limit_ns`, or as soon as another role of this CTA has aborted.
+__device__ __forceinline__ bool mbar_wait_ns(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                             unsigned code, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 15u) == 0u) {
       if (*abort_flag) return false;
-      if (global_timer_ns() - t0 > OC_WAIT_NS) break;
+      if (global_timer_ns() - t0 > limit_ns) break;
     }
   }
   record_error(code);
   *abort_flag = 1;
   return false;
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          unsigned code) {
+  return mbar_wait_ns(bar, parity, abort_flag, code, OC_WAIT_NS);
 }
 
 // Bounded wait used while unwinding after an abort (no abort-flag check).

@@ -232,10 +232,9 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
           x_armed[sx] = px;
         }
       }
-      if (!ok) {
-        for (int i = 0; i < X_STAGES; ++i)
-          if (x_armed[i] >= 0) mbar_drain(&full_x[i], x_armed[i]);
-      }
+      // every load issued lands before the CTA can exit (consumed ones return at once)
+      for (int i = 0; i < X_STAGES; ++i)
+        if (x_armed[i] >= 0) mbar_drain(&full_x[i], x_armed[i]);
     }
   } else if (warp == 2) {
     // packed weight tiles, decoupled from the activation stream
@@ -256,10 +255,9 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
           w_armed[sw] = pw;
         }
       }
-      if (!ok) {
-        for (int i = 0; i < W_STAGES; ++i)
-          if (w_armed[i] >= 0) mbar_drain(&full_w[i], w_armed[i]);
-      }
+      // every load issued lands before the CTA can exit (consumed ones return at once)
+      for (int i = 0; i < W_STAGES; ++i)
+        if (w_armed[i] >= 0) mbar_drain(&full_w[i], w_armed[i]);
     }
   } else if (warp == 1) {
     if (lane == 0) {

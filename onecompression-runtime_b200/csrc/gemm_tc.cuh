@@ -229,8 +229,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // released every stage we filled: then each of our copies has landed.
         for (int i = 0; i < X_STAGES; ++i)
           if (x_armed[i] >= 0) mbar_drain(&empty_x[i], x_armed[i]);
-      } else if (!ok) {
-        // drain our own loads in flight before the CTA (and its smem) goes away
+      } else {
+        // every load issued lands before the CTA (and its smem) can go away, whatever happened to
+        // the other roles; loads already consumed have completed their phase and return at once
         for (int i = 0; i < X_STAGES; ++i)
           if (x_armed[i] >= 0) mbar_drain(&full_x[i], x_armed[i]);
       }
@@ -260,10 +261,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           w_armed[sw] = pw;
         }
       }
-      if (!ok) {
-        for (int i = 0; i < W_STAGES; ++i)
-          if (w_armed[i] >= 0) mbar_drain(&full_w[i], w_armed[i]);
-      }
+      // every load issued lands before the CTA can exit (consumed ones return at once)
+      for (int i = 0; i < W_STAGES; ++i)
+        if (w_armed[i] >= 0) mbar_drain(&full_w[i], w_armed[i]);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer

@@ -155,11 +155,18 @@ __device__ __forceinline__ void gemv_bar(int bar_threads) {
     named_bar_sync(2, bar_threads);
 }
 
+// Ticket word of a column tile: arrivals in the low 16 bits, arrivals of CTAs that failed (a
+// bounded wait gave up) from bit 16. Failing CTAs still take their ticket, so the last CTA always
+// re-arms it and the tickets are zero after every launch, failed or not; the output of a tile
+// with a failed split is left unwritten (the error word tells the host).
+constexpr unsigned kTicketFail = 1u << 16;
+
 template <bool BF16, int MT>
 __device__ __forceinline__ void gemv_finish_n(const GemvParams& p, float (&acc)[MT][2][4], int wk, int col, int t,
-                                              int tile, int split, int* is_last, int bar_threads) {
+                                              int tile, int split, int* is_last, int bar_threads,
+                                              bool failed = false) {
   if (p.splits > 1) {
-    if (wk == 0 && col < p.N) {
+    if (!failed && wk == 0 && col < p.N) {
 #pragma unroll
       for (int a = 0; a < MT; ++a)
 #pragma unroll
@@ -174,11 +181,13 @@ __device__ __forceinline__ void gemv_finish_n(const GemvParams& p, float (&acc)[
     __threadfence();
     gemv_bar(bar_threads);
     if (threadIdx.x == 0) {
-      const unsigned prev = atomicAdd(p.tickets + tile, 1u);
-      *is_last = (prev == (unsigned)(p.splits - 1));
+      const unsigned prev = atomicAdd(p.tickets + tile, failed ? 1u + kTicketFail : 1u);
+      const bool last = (prev & (kTicketFail - 1u)) == (unsigned)(p.splits - 1);
+      *is_last = !last ? 0 : ((prev >= kTicketFail || failed) ? 2 : 1);
+      if (last) p.tickets[tile] = 0u;  // re-arm for the next launch (stream order)
     }
     gemv_bar(bar_threads);
-    if (!*is_last) return;
+    if (*is_last != 1) return;
     __threadfence();
     if (wk == 0 && col < p.N) {
 #pragma unroll
@@ -196,7 +205,8 @@ __device__ __forceinline__ void gemv_finish_n(const GemvParams& p, float (&acc)[
           }
         }
     }
-    if (threadIdx.x == 0) p.tickets[tile] = 0u;  // re-arm for the next launch (stream order)
+  } else if (failed) {
+    return;
   }
   if (wk != 0 || col >= p.N) return;
   float bv[4] = {0.f, 0.f, 0.f, 0.f};

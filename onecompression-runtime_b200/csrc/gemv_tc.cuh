@@ -137,17 +137,16 @@ __global__ void __launch_bounds__(kVtThreads, 1)
       griddep_wait();  // x is written by the previous kernel
       int armed[kVtXS];
       for (int i = 0; i < kVtXS; ++i) armed[i] = -1;
-      bool ok = true;
       for (int i = 0; i < nkb; ++i) {
         const int s = i % kVtXS, ph = (i / kVtXS) & 1;
-        if (!mbar_wait(&empty_x[s], ph ^ 1, abort_flag, kDevErrTmaEmpty)) { ok = false; break; }
+        if (!mbar_wait(&empty_x[s], ph ^ 1, abort_flag, kDevErrTmaEmpty)) break;
         mbar_arrive_expect_tx(&full_x[s], kVtXBytes);
         tma_load_2d(smem + kVtXOff + s * kVtXBytes, &tmap_x, &full_x[s], (kb0 + i) * kVtBK, 0);
         armed[s] = ph;
       }
-      if (!ok)
-        for (int s = 0; s < kVtXS; ++s)
-          if (armed[s] >= 0) mbar_drain(&full_x[s], armed[s]);
+      // every copy issued lands before the CTA can exit (consumed ones return at once)
+      for (int s = 0; s < kVtXS; ++s)
+        if (armed[s] >= 0) mbar_drain(&full_x[s], armed[s]);
     }
   } else if (warp == 2) {
     // ------------------------------------------------------------------ weight / scale producer
@@ -179,12 +178,11 @@ __global__ void __launch_bounds__(kVtThreads, 1)
         tma_load_2d(smem + kVtWOff + s * kVtWBytes, &tmap_w, &full_w[s], col0, kb * 8);
         warmed[s] = ph;
       }
-      if (!ok) {
-        for (int s = 0; s < kVtWS; ++s)
-          if (warmed[s] >= 0) mbar_drain(&full_w[s], warmed[s]);
-        for (int s = 0; s < kVtSZ; ++s)
-          if (zarmed[s] >= 0) mbar_drain(&full_sz[s], zarmed[s]);
-      }
+      // every copy issued lands before the CTA can exit (consumed ones return at once)
+      for (int s = 0; s < kVtWS; ++s)
+        if (warmed[s] >= 0) mbar_drain(&full_w[s], warmed[s]);
+      for (int s = 0; s < kVtSZ; ++s)
+        if (zarmed[s] >= 0) mbar_drain(&full_sz[s], zarmed[s]);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
@@ -311,20 +309,24 @@ __global__ void __launch_bounds__(kVtThreads, 1)
       for (int t = 0; t < kVtN; ++t) acc[t] = fmaf(sc, __uint_as_float(dv[t]), fmaf(-cz, __uint_as_float(sv[t]), acc[t]));
     }
     const bool any_fail = named_bar_or(1, 128, !ok);
-    if (!any_fail) {
-      griddep_wait();  // the previous kernel is done with the workspace and the output
-      const bool nvalid = n < p.N;
+    griddep_wait();  // the previous kernel is done with the workspace and the output
+    const bool nvalid = n < p.N;
+    {
+      // a failed CTA (its error is recorded) still takes its split-K ticket and writes nothing;
+      // the last CTA re-arms the ticket and skips the output if any split failed
       if (p.splits > 1) {
-        if (nvalid)
+        if (!any_fail && nvalid)
           for (int t = 0; t < p.M; ++t) p.ws[((long long)split * p.M + t) * p.N + n] = acc[t];
         __threadfence();
         named_bar_sync(1, 128);
         if (et == 0) {
-          const unsigned prev = atomicAdd(p.tickets + tile, 1u);
-          is_last = (prev == (unsigned)(p.splits - 1));
+          const unsigned prev = atomicAdd(p.tickets + tile, any_fail ? 1u + kTicketFail : 1u);
+          const bool last = (prev & (kTicketFail - 1u)) == (unsigned)(p.splits - 1);
+          is_last = !last ? 0 : ((prev >= kTicketFail || any_fail) ? 2 : 1);
+          if (last) p.tickets[tile] = 0u;  // re-arm for the next launch (stream order)
         }
         named_bar_sync(1, 128);
-        if (is_last) {
+        if (is_last == 1) {
           __threadfence();
           if (nvalid)
             for (int t = 0; t < p.M; ++t) {
@@ -332,10 +334,9 @@ __global__ void __launch_bounds__(kVtThreads, 1)
               for (int sp = 0; sp < p.splits; ++sp) sum += __ldcg(p.ws + ((long long)sp * p.M + t) * p.N + n);
               acc[t] = sum;
             }
-          if (et == 0) p.tickets[tile] = 0u;  // re-arm for the next launch (stream order)
         }
       }
-      if ((p.splits == 1 || is_last) && nvalid) {
+      if (((p.splits == 1 && !any_fail) || (p.splits > 1 && is_last == 1)) && nvalid) {
         const int odt = BF16 ? kBF16 : kF16;
         const float bv = p.bias ? load_as_f32(p.bias, p.bias_dtype, n) : 0.f;
 #pragma unroll

@@ -65,6 +65,9 @@ struct GtParams {
   GemvParams g;
   int rows_sz;        // scale/zero rows per stage: stage k / gs when gs divides it, else 1
   int kb_per_split;   // stages per split
+  unsigned long long wait_ns;  // bound of the pipeline waits (drains keep OC_WAIT_NS)
+  int stall_stage;    // failure test only: > 0 leaves stage stall_stage - 1 of CTA (0, 0) unissued,
+                      // so its consumers' wait runs out; 0 in normal use
 };
 
 template <bool BF16, int MT, int WB = 4>
@@ -132,24 +135,26 @@ __global__ void __launch_bounds__(kGtThreads, 2)
         const int s = i % Cfg::kDepth;
         tma_load_2d(smem + Cfg::kXOff + s * Cfg::kXBytes, &tmap_x, &full[s], (kb0 + i) * KS, 0);
       };
+      const int stall = (blockIdx.x == 0 && blockIdx.y == 0) ? gp.stall_stage - 1 : -1;
       // weights of the first stages before the previous kernel has finished
       const int pre = nst < Cfg::kDepth ? nst : Cfg::kDepth;
-      for (int i = 0; i < pre; ++i) load_wsz(i);
+      for (int i = 0; i < pre; ++i)
+        if (i != stall) load_wsz(i);
       griddep_wait();
-      for (int i = 0; i < pre; ++i) load_x(i);
-      bool ok = true;
+      for (int i = 0; i < pre; ++i)
+        if (i != stall) load_x(i);
       for (int i = pre; i < nst; ++i) {
         const int s = i % Cfg::kDepth;
-        if (!mbar_wait(&empty[s], ((i / Cfg::kDepth) & 1) ^ 1, abort_flag, kDevErrWEmpty)) {
-          ok = false;
-          break;
-        }
+        if (!mbar_wait_ns(&empty[s], ((i / Cfg::kDepth) & 1) ^ 1, abort_flag, kDevErrWEmpty, gp.wait_ns)) break;
+        if (i == stall) continue;
         load_wsz(i);
         load_x(i);
       }
-      if (!ok)
-        for (int s = 0; s < Cfg::kDepth; ++s)
-          if (armed[s] >= 0) mbar_drain(&full[s], armed[s]);
+      // Wait (bounded) for every copy this lane issued to land, whatever happened to the
+      // consumers: the CTA must not exit with a bulk copy in flight. Copies already consumed
+      // have completed their phase, so those waits return at once.
+      for (int s = 0; s < Cfg::kDepth; ++s)
+        if (armed[s] >= 0) mbar_drain(&full[s], armed[s]);
     }
     return;  // the producer warp takes no part in the reduction below (no further __syncthreads)
   }
@@ -245,7 +250,7 @@ __global__ void __launch_bounds__(kGtThreads, 2)
   int cur_grp = -1;  // group of the warp's last stage when a group spans whole stages
   for (int i = kh; i < nst; i += 2) {
     const int s = i % Cfg::kDepth;
-    if (!mbar_wait(&full[s], (i / Cfg::kDepth) & 1, abort_flag, kDevErrWFull)) {
+    if (!mbar_wait_ns(&full[s], (i / Cfg::kDepth) & 1, abort_flag, kDevErrWFull, gp.wait_ns)) {
       ok = false;
       break;
     }
@@ -355,9 +360,9 @@ __global__ void __launch_bounds__(kGtThreads, 2)
 #pragma unroll
         for (int c = 0; c < 4; ++c) acc[a][b][c] += red[wn][lane][a * 8 + b * 4 + c];
   }
-  if (any_fail) return;  // error recorded; leave the tickets and the output alone
-  griddep_wait();         // the previous kernel is done with the workspace and the output
-  gemv_finish_n<BF16, MT>(p, acc, kh, col, t, tile, split, &is_last, kGtConsumerWarps * 32);
+  griddep_wait();  // the previous kernel is done with the workspace and the output
+  // a failed CTA (its error is recorded) still takes its split-K ticket and writes nothing
+  gemv_finish_n<BF16, MT>(p, acc, kh, col, t, tile, split, &is_last, kGtConsumerWarps * 32, any_fail);
 }
 
 }  // namespace oc

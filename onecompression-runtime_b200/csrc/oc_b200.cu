@@ -47,6 +47,9 @@ bool dtf(int dt) { return dt == OC_DT_F16 || dt == OC_DT_BF16 || dt == OC_DT_F32
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
 std::atomic<int> g_opt_path{0}, g_opt_tile{0}, g_opt_gemv_ctas{2}, g_opt_gemv_impl{1}, g_opt_tc_pair{1};
+// failure tests only: bound of the decode GEMV's pipeline waits (0: OC_WAIT_NS) and the stage its
+// first CTA leaves unissued (0: none)
+std::atomic<int> g_opt_wait_us{0}, g_opt_test_stall{0};
 
 constexpr int kMaxDevices = 64;
 int g_sm_count[kMaxDevices];
@@ -191,6 +194,28 @@ int oc_b200_set_option(int key, int value) {
       if (value < 0 || value > 2) return fail(OC_ERR_INVALID, "OC_OPT_GEMV_IMPL: %d", value);
       g_opt_gemv_impl = value;
       return OC_OK;
+    case OC_OPT_WAIT_US:
+      if (value < 0) return fail(OC_ERR_INVALID, "OC_OPT_WAIT_US: %d", value);
+      g_opt_wait_us = value;
+      return OC_OK;
+    case OC_OPT_TEST_STALL:
+      if (value < 0) return fail(OC_ERR_INVALID, "OC_OPT_TEST_STALL: %d", value);
+      g_opt_test_stall = value;
+      return OC_OK;
+  }
+  return fail(OC_ERR_INVALID, "unknown option %d", key);
+}
+
+int oc_b200_get_option(int key, int* value) {
+  if (!value) return fail(OC_ERR_INVALID, "get_option: value is NULL");
+  switch (key) {
+    case OC_OPT_GEMM_PATH: *value = g_opt_path.load(); return OC_OK;
+    case OC_OPT_TC_TILE: *value = g_opt_tile.load(); return OC_OK;
+    case OC_OPT_GEMV_CTAS: *value = g_opt_gemv_ctas.load(); return OC_OK;
+    case OC_OPT_GEMV_IMPL: *value = g_opt_gemv_impl.load(); return OC_OK;
+    case OC_OPT_TC_PAIR: *value = g_opt_tc_pair.load(); return OC_OK;
+    case OC_OPT_WAIT_US: *value = g_opt_wait_us.load(); return OC_OK;
+    case OC_OPT_TEST_STALL: *value = g_opt_test_stall.load(); return OC_OK;
   }
   return fail(OC_ERR_INVALID, "unknown option %d", key);
 }
@@ -701,6 +726,9 @@ int launch_gemv_tma(const oc_b200_layer* L, const oc::GemvParams& p, const GemvP
   const int ks = L->wbits == 8 ? oc::gt_stage_k<8>() : oc::kGtBK;  // k per stage
   g.rows_sz = L->gt_rows;
   g.kb_per_split = gp.kstep / (oc::kGtBK / 32);
+  const int wait_us = g_opt_wait_us.load();
+  g.wait_ns = wait_us > 0 ? 1000ull * (unsigned long long)wait_us : (unsigned long long)OC_WAIT_NS;
+  g.stall_stage = g_opt_test_stall.load();
   const int mt = p.M <= 8 ? 1 : 2;
   CUtensorMap tx;
   if (int rc = make_tmap_2d(&tx, BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.x,

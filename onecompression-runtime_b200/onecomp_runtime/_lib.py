@@ -23,6 +23,8 @@ OPT_TC_TILE = 2
 OPT_GEMV_CTAS = 3
 OPT_GEMV_IMPL = 4
 OPT_TC_PAIR = 5
+OPT_WAIT_US = 6
+OPT_TEST_STALL = 7
 ACT_NONE = 0
 ACT_GELU_TANH = 1
 
@@ -40,6 +42,7 @@ _SIGNATURES = {
     "oc_b200_last_error": ([], ctypes.c_char_p),
     "oc_b200_device_check": ([_i], _i),
     "oc_b200_set_option": ([_i, _i], _i),
+    "oc_b200_get_option": ([_i, ctypes.POINTER(_i)], _i),
     "oc_b200_read_device_error": ([ctypes.POINTER(_i), _p], _i),
     "oc_b200_gptq_unpack": ([_p, _i, _i, _i, _p, _p], _i),
     "oc_b200_gptq_unpack_zeros": ([_p, _i, _i, _i, _p, _p], _i),
@@ -129,6 +132,12 @@ def require_b200(device: torch.device) -> None:
 
 def set_option(key: int, value: int) -> None:
     call("oc_b200_set_option", key, value)
+
+
+def get_option(key: int) -> int:
+    v = _i(0)
+    call("oc_b200_get_option", key, ctypes.byref(v))
+    return v.value
 
 
 def read_device_error(device: torch.device) -> int:

@@ -9,9 +9,13 @@ per byte (code j at bits ``j*wbits``); ``scales``/``qzeros`` are groupwise in
 ``[out, G]`` or ``[G, out]`` (fractional zeros allowed); the weight is
 ``(q - z) * s`` in fp32 rounded once -- reproduced bit for bit by
 ``oc_b200_dsv4_dequant``. When the buffers live on the GPU, ``forward`` runs the
-fused row-packed tcgen05 GEMM (``oc_b200_rows_gemm``); buffers kept on the host
-(offloaded experts) are copied to the activation's device per call, dequantized
-and multiplied with ``F.linear``, as the reference does.
+fused row-packed tcgen05 GEMM (``oc_b200_rows_gemm``). Buffers kept on the host
+(offloaded experts, the DSV4 adapter's default) are copied per call, still
+packed, into a device staging slot shared by every module of the same shape on
+that stream, and the same fused GEMM runs on the slot: the reference copies the
+packed bytes and dequantizes to a dense weight for ``F.linear``
+(dsv4_packed_linear.py:95-98); here only the packed bytes cross and no dense
+weight is materialized.
 """
 from __future__ import annotations
 
@@ -40,6 +44,14 @@ def dequant_dsv4_packed(p: dict, dtype: torch.dtype = torch.bfloat16, device=Non
     gs = int(p["groupsize"])
     packed = p["qweight_packed"]
     dev = torch.device(device) if device is not None else packed.device
+    home = dev
+    if dev.type != "cuda":
+        # host tensors and no target device: dequantize on the current CUDA device and return
+        # the result on the host, as the reference does for CPU buffers (no CPU fallback)
+        if not torch.cuda.is_available():
+            raise RuntimeError("onecomp_runtime (B200) dequantizes on CUDA sm_100 devices only; got "
+                               f"{dev} tensors and no CUDA device. There is no CPU fallback.")
+        dev = torch.device("cuda", torch.cuda.current_device())
     _lib.require_b200(dev)
     if dtype not in (torch.float16, torch.bfloat16):
         raise TypeError(f"unsupported dtype {dtype}")
@@ -60,7 +72,28 @@ def dequant_dsv4_packed(p: dict, dtype: torch.dtype = torch.bfloat16, device=Non
     _lib.call("oc_b200_dsv4_dequant", packed.data_ptr(), ncol, wbits, scales.data_ptr(), _lib.DT[scales.dtype],
               qzeros.data_ptr(), _lib.DT[qzeros.dtype], stride_n, stride_g, gs, in_f, out_f, out.data_ptr(),
               _lib.DT[dtype], _lib.stream_of(dev))
-    return out
+    return out if home == dev else out.to(home)
+
+
+# Staging slots for host-resident (offloaded) layers: one set of device buffers and one kernel
+# handle per (device, stream, shapes, dtypes). Every call copies its packed bytes into the slot and
+# runs the GEMM on it in the same stream, so modules of one shape share the slot in stream order.
+_STAGING: dict[tuple, tuple] = {}
+
+
+def _staging_slot(q: torch.Tensor, s: torch.Tensor, z: torch.Tensor, dev: torch.device, wbits: int, gs: int,
+                  K: int, N: int, sn: int, sg: int):
+    key = (dev, _lib.stream_of(dev), tuple(q.shape), q.dtype, tuple(s.shape), s.dtype, tuple(z.shape), z.dtype,
+           wbits, gs, K, N, sn, sg)
+    slot = _STAGING.get(key)
+    if slot is None:
+        qd = torch.empty(q.shape, dtype=q.dtype, device=dev)
+        sd = torch.empty(s.shape, dtype=s.dtype, device=dev)
+        zd = torch.empty(z.shape, dtype=z.dtype, device=dev)
+        h = RowsHandle([qd], [sd], [zd], wbits, gs, K, N, MODE_EXACT, sn, sg)
+        slot = (qd, sd, zd, h)
+        _STAGING[key] = slot
+    return slot
 
 
 class Dsv4PackedLinear(nn.Module):
@@ -106,14 +139,36 @@ class Dsv4PackedLinear(nn.Module):
         self.__dict__["_handle_key"] = key
         return h
 
+    def _fusable(self) -> bool:
+        gs = self.groupsize if self.groupsize > 0 else self.in_features
+        return self.wbits in (2, 4) and rows_fusable(int(self.qweight_packed.shape[1]), self.in_features,
+                                                     self.out_features, gs, self.wbits)
+
+    def _staged_handle(self, dev: torch.device):
+        """Copy the host-resident packed buffers into the shared device slot; its handle."""
+        gs = self.groupsize if self.groupsize > 0 else self.in_features
+        s, z = float_param(self.scales), float_param(self.qzeros)
+        sn, sg = _stride_of(s, self.out_features, self.in_features, self.groupsize)
+        qd, sd, zd, h = _staging_slot(self.qweight_packed, s, z, dev, self.wbits, gs, self.in_features,
+                                      self.out_features, sn, sg)
+        qd.copy_(self.qweight_packed, non_blocking=True)
+        sd.copy_(s, non_blocking=True)
+        zd.copy_(z, non_blocking=True)
+        return h
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        if x.is_cuda and self.qweight_packed.device == x.device and x.dtype in (torch.float16, torch.bfloat16):
-            h = self._rows_handle()
+        if x.is_cuda and x.dtype in (torch.float16, torch.bfloat16) and self._fusable():
+            if self.qweight_packed.device == x.device:
+                h = self._rows_handle()
+            elif self.qweight_packed.device.type == "cpu":
+                h = self._staged_handle(x.device)
+            else:
+                h = None
             if h is not None:
                 a = prep_activation(x, self.in_features)
                 out = torch.empty((a.shape[0], self.out_features), dtype=x.dtype, device=x.device)
                 if a.shape[0]:
-                    bias = self.bias.to(x.dtype) if self.bias is not None else None
+                    bias = self.bias.to(device=x.device, dtype=x.dtype) if self.bias is not None else None
                     h.gemm(a, out, bias=bias)
                 return out.reshape(*x.shape[:-1], self.out_features)
         w = dequant_dsv4_packed(self._packed_dict(), dtype=x.dtype, device=x.device)

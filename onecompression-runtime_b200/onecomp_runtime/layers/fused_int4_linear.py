@@ -23,6 +23,7 @@ AutoGPTQ-v1 zero restore (the reference kernel always applies it, :221);
 from __future__ import annotations
 
 import time
+from collections import OrderedDict
 
 import torch
 
@@ -162,12 +163,32 @@ def fused_int4_gemm(a: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor
     assert N % 8 == 0, f"N must be a multiple of 8 (qzeros packing), got N={N}"
     assert K % 32 == 0, f"K must be a multiple of 32 (groupsize), got K={K}"
     compute = torch.float16 if a.dtype == torch.float32 else a.dtype
-    if scales.dtype != compute:
-        scales = scales.to(compute)   # the reference casts scales to a's dtype (:421-422)
-    if bias is not None:
-        bias = bias.to(compute)       # ... and the bias too (:445-447)
-    layer = FusedInt4Linear(K, N, qweight, scales, qzeros, bias=bias, groupsize=32)
-    try:
-        return layer(a)
-    finally:
-        layer._release_handle()
+    return _functional_layer(qweight, scales, qzeros, bias, compute)(a)
+
+
+# Layers built by fused_int4_gemm, reused across calls on the same weight tensors: the handle
+# (K layout, TMA descriptors) is host work done once instead of per call. An entry holds its
+# weight tensors (so their memory cannot be reused while it exists) and matches on their data
+# pointers, shapes, dtypes and torch's in-place version counters, so an edited weight rebuilds
+# it. At most _FUNCTIONAL_MAX entries are kept (least recently used dropped first).
+_FUNCTIONAL: "OrderedDict[tuple, FusedInt4Linear]" = OrderedDict()
+_FUNCTIONAL_MAX = 64
+
+
+def _functional_layer(qweight, scales, qzeros, bias, compute) -> FusedInt4Linear:
+    srcs = (qweight, scales, qzeros) + ((bias,) if bias is not None else ())
+    key = (tuple((t.data_ptr(), tuple(t.shape), t.stride(), t.dtype, t.device, t._version) for t in srcs), compute)
+    layer = _FUNCTIONAL.get(key)
+    if layer is not None:
+        _FUNCTIONAL.move_to_end(key)
+        return layer
+    K, N = qweight.shape[0] * 8, scales.shape[1]
+    s = scales if scales.dtype == compute else scales.to(compute)   # the reference casts scales (:421-422)
+    b = None if bias is None else (bias if bias.dtype == compute else bias.to(compute))  # ... and bias (:445-447)
+    layer = FusedInt4Linear(K, N, qweight, s, qzeros, bias=b, groupsize=32)
+    layer._functional_srcs = srcs   # pins the caller's tensors for the key's lifetime
+    _FUNCTIONAL[key] = layer
+    while len(_FUNCTIONAL) > _FUNCTIONAL_MAX:
+        _, old = _FUNCTIONAL.popitem(last=False)
+        old._release_handle()
+    return layer

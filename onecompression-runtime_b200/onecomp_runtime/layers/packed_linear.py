@@ -10,9 +10,14 @@ Same API as the reference ``layers/packed_linear.py``:
 
 On the GPU, ``PackedRTNLinear.forward`` runs the fused row-packed tcgen05 GEMM
 (``oc_b200_rows_gemm``, RTN mode: the kernel multiplies exactly the weights
-``dequant_extra_u8_to_weight`` produces) whenever the byte stride of a packed
-row is a multiple of 16 and the group size a multiple of 8; other shapes
-dequantize with the bit-exact ``oc_b200_rtn_dequant`` kernel and call ``F.linear``.
+``dequant_extra_u8_to_weight`` produces) for fp16/bf16 inputs. Packed rows whose
+byte stride is not a multiple of 16, or an ``in_features`` that is not a
+multiple of 8 (one group per row), are copied once into a zero-padded device
+layout (K rounded up to 8, rows to 16 bytes; the activations are zero-padded to
+match per call). Only groups that are not a multiple of 8 columns (a group
+boundary inside a 32-bit code word) and fp32 inputs dequantize with the
+bit-exact ``oc_b200_rtn_dequant`` kernel and call ``F.linear`` in fp32, as the
+reference does.
 """
 from __future__ import annotations
 
@@ -46,26 +51,44 @@ class PackedRTNLinear(nn.Module):
                                           self.out_features, dtype)
 
     def _rows_handle(self):
+        """The fused-GEMM handle, or None for groups the kernel cannot take. Sets ``_k_run``, the
+        K the kernel runs (``in_features`` rounded up to 8 when the layout was padded)."""
         key = (self.qweight_u8.data_ptr(), self.scales.data_ptr(), self.zeros.data_ptr(), self.scales.dtype,
                self.zeros.dtype)
         h = self.__dict__.get("_handle")
         if h is not None and self.__dict__.get("_handle_key") == key:
             return h
+        K, N = self.in_features, self.out_features
         G = int(self.scales.shape[1])
-        gs = self.in_features if G == 1 else self.in_features // G
-        if not rows_fusable(int(self.qweight_u8.shape[1]), self.in_features, self.out_features, gs, 4):
-            return None
-        h = RowsHandle([self.qweight_u8], [float_param(self.scales)], [float_param(self.zeros)], 4, gs,
-                       self.in_features, self.out_features, MODE_RTN, G, 1)
+        gs = K if G == 1 else K // G
+        q = self.qweight_u8
+        ld = int(q.shape[1])
+        k_run = K
+        if not rows_fusable(ld, K, N, gs, 4):
+            k_run = (K + 7) // 8 * 8
+            gs_run = k_run if G == 1 else gs
+            ld_run = max((k_run + 1) // 2, ld)
+            ld_run = (ld_run + 15) // 16 * 16
+            if ld * 2 < K or not rows_fusable(ld_run, k_run, N, gs_run, 4):
+                return None
+            # zero-padded copy (codes past in_features meet zero activations)
+            qp = torch.zeros((N, ld_run), dtype=torch.uint8, device=q.device)
+            qp[:, :ld].copy_(q)
+            q, gs = qp, gs_run
+        h = RowsHandle([q], [float_param(self.scales)], [float_param(self.zeros)], 4, gs, k_run, N, MODE_RTN, G, 1)
         self.__dict__["_handle"] = h
         self.__dict__["_handle_key"] = key
+        self.__dict__["_k_run"] = k_run
         return h
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if x.is_cuda and x.dtype in (torch.float16, torch.bfloat16):
             h = self._rows_handle()
             if h is not None:
+                k_run = self.__dict__["_k_run"]
                 a = prep_activation(x, self.in_features)
+                if k_run != self.in_features:
+                    a = F.pad(a, (0, k_run - self.in_features))
                 out = torch.empty((a.shape[0], self.out_features), dtype=x.dtype, device=x.device)
                 if a.shape[0]:
                     bias = self.bias.to(x.dtype) if self.bias is not None else None

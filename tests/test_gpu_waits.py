@@ -1,0 +1,90 @@
+"""A bounded wait that runs out: the kernel reports it and the next calls are correct.
+
+The decode GEMV's failure-test options make the first CTA leave one pipeline stage unissued
+(its full barrier is armed by nobody), with a 20 ms bound on the pipeline waits. The consumer
+warps' wait runs out, the kernel records its error code and returns; every bulk copy that was
+issued is waited for before the CTA exits, the failed CTA still takes its split-K ticket, and
+the tile with the failed split is left unwritten. No trap, no fault: the context stays usable,
+and the same workspace (or the no-alloc scratch) gives exact results on the following calls.
+"""
+from __future__ import annotations
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+WFULL = 0x107  # kDevErrWFull: a consumer's wait for a weight stage gave up
+
+
+def _layer(device):
+    from onecomp_runtime.layers import PackedGPTQLinear
+    from onecomp_runtime.testing import gptq_layer
+    K, N = 5120, 1024   # config-2 style: gptq_v2, act-order gs128, several splits per column tile
+    t = gptq_layer(K, N, 128, seed=71, v1=False, actorder=True, bias=True, device=device)
+    return PackedGPTQLinear(K, N, t["qweight"], t["scales"], t["qzeros"], t["g_idx"], t["bias"], 128, 4, False)
+
+
+def _stalled(run, device):
+    """Run `run()` with the stall options set, restoring the previous option values."""
+    from onecomp_runtime import _lib
+    keys = (_lib.OPT_WAIT_US, _lib.OPT_TEST_STALL, _lib.OPT_GEMV_IMPL, _lib.OPT_GEMM_PATH)
+    saved = {k: _lib.get_option(k) for k in keys}
+    try:
+        _lib.set_option(_lib.OPT_GEMV_IMPL, 1)    # the TMA decode GEMV
+        _lib.set_option(_lib.OPT_GEMM_PATH, 0)
+        _lib.set_option(_lib.OPT_WAIT_US, 20000)  # 20 ms
+        _lib.set_option(_lib.OPT_TEST_STALL, 1)   # stage 0 of CTA (0, 0) is never issued
+        run()
+        torch.cuda.synchronize(device)
+    finally:
+        for k, v in saved.items():
+            _lib.set_option(k, v)
+    return _lib.read_device_error(device)
+
+
+def test_wait_runs_out_then_workspace_calls_are_exact(cuda_device):
+    from onecomp_runtime import _lib
+    from onecomp_runtime.testing import activations
+    layer = _layer(cuda_device)
+    x = activations(1, layer.in_features, seed=5).to(cuda_device)
+    ref = layer(x)
+    torch.cuda.synchronize(cuda_device)
+    assert _lib.read_device_error(cuda_device) == 0
+    out = torch.full_like(ref, float("nan"))
+    code = _stalled(lambda: layer._gemm_2d(x, out), cuda_device)
+    assert code == WFULL, hex(code)
+    assert torch.isnan(out[:, :128].float()).all()          # the failed tile is not written
+    torch.testing.assert_close(out[:, 128:], ref[:, 128:], rtol=0, atol=0)
+    for _ in range(2):                                     # same workspace, tickets re-armed
+        torch.testing.assert_close(layer(x), ref, rtol=0, atol=0)
+    torch.cuda.synchronize(cuda_device)
+    assert _lib.read_device_error(cuda_device) == 0
+
+
+def test_wait_runs_out_then_noalloc_calls_are_exact(cuda_device):
+    from onecomp_runtime import _lib
+    from onecomp_runtime.testing import activations
+    layer = _layer(cuda_device)
+    x = activations(1, layer.in_features, seed=6).to(cuda_device)
+    ref = layer(x)
+    h = layer._get_handle()
+    bias = layer.bias
+
+    def noalloc(out):
+        return _lib.lib().oc_b200_gptq_gemv_noalloc(
+            h, x.data_ptr(), _lib.DT[x.dtype], 1, x.stride(0), bias.data_ptr(), _lib.DT[bias.dtype],
+            out.data_ptr(), out.stride(0), _lib.stream_of(cuda_device))
+
+    _lib.check(noalloc(torch.empty_like(ref)), "oc_b200_gptq_gemv_noalloc")  # scratch set up
+    torch.cuda.synchronize(cuda_device)
+    out = torch.full_like(ref, float("nan"))
+    code = _stalled(lambda: _lib.check(noalloc(out), "oc_b200_gptq_gemv_noalloc"), cuda_device)
+    assert code == WFULL, hex(code)
+    assert torch.isnan(out[:, :128].float()).all()
+    for _ in range(2):                                     # the shared scratch's tickets are zero again
+        y = torch.full_like(ref, float("nan"))
+        _lib.check(noalloc(y), "oc_b200_gptq_gemv_noalloc")
+        torch.testing.assert_close(y, ref, rtol=0, atol=0)
+    torch.cuda.synchronize(cuda_device)
+    assert _lib.read_device_error(cuda_device) == 0

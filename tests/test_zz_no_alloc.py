@@ -77,6 +77,7 @@ def test_noalloc_rejects_oversize(cuda_device):
     out = torch.empty((32, N), dtype=torch.bfloat16, device=cuda_device)
     assert _noalloc(layer, x, out) != 0
     assert "M=32" in _lib.last_error()
+    saved = {k: _lib.get_option(k) for k in (_lib.OPT_GEMV_IMPL, _lib.OPT_GEMV_CTAS)}
     try:
         # the cp.async GEMV with many splits: 16 rows x 16384 x splits fp32 partials
         _lib.set_option(_lib.OPT_GEMV_IMPL, 2)
@@ -84,7 +85,7 @@ def test_noalloc_rejects_oversize(cuda_device):
         assert _noalloc(layer, x[:16], out[:16]) != 0
         assert "bytes of scratch" in _lib.last_error()
     finally:
-        _lib.set_option(_lib.OPT_GEMV_CTAS, 2)   # the library defaults
-        _lib.set_option(_lib.OPT_GEMV_IMPL, 1)
+        for k, v in saved.items():   # whatever was set before this test
+            _lib.set_option(k, v)
     _lib.check(_noalloc(layer, x[:16], out[:16]), "oc_b200_gptq_gemv_noalloc")
     torch.testing.assert_close(out[:16], layer(x[:16]), rtol=0, atol=0)
