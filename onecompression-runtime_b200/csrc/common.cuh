@@ -176,6 +176,29 @@ __device__ __forceinline__ DqConst<BF16> make_dq_const(float s, int z) {
   return c;
 }
 
+// Is the split s = s_hi + s_lo of make_dq_const exact and its products exact, so that
+// fma(d, s_hi, d * s_lo) rounds d * s once for every d with at most 5 significant bits?
+//   * s_hi must be finite and s_hi + s_lo == s (an fp32 sum that is exact whenever the split is);
+//   * s_lo = 0, or (bf16 pairs) s_lo has at most 3 significant bits (d * s_lo then fits the 8-bit
+//     pair mantissa) and is far above bf16's underflow. fp16 pairs need s_lo = 0: a nonzero s_lo
+//     times d may fall below fp16's subnormal range.
+// Always true for positive fp16 scales with bf16 pairs and for positive scales of the pair's
+// own dtype.
+template <bool BF16>
+__device__ __forceinline__ bool split_exact(float s, uint16_t hi, uint16_t lo) {
+  using P = Pair<BF16>;
+  const float hf = P::to_f32(hi), lf = P::to_f32(lo);
+  if (!(s > 0.f) || !isfinite(hf) || hf + lf != s) return false;  // (signed zeros of s <= 0 differ)
+  if (lf == 0.f) return true;
+  if (!BF16) return false;
+  return (__float_as_uint(lf) & 0x1FFFFFu) == 0u && fabsf(lf) >= 0x1p-110f;
+}
+
+template <bool BF16>
+__device__ __forceinline__ bool dq_const_exact(float s, const DqConst<BF16>& c) {
+  return split_exact<BF16>(s, (uint16_t)(c.shi & 0xFFFFu), (uint16_t)(c.slo & 0xFFFFu));
+}
+
 template <bool BF16, bool HAS_LO>
 __device__ __forceinline__ uint32_t dq_pair(uint32_t magic_q, const DqConst<BF16>& c) {
   using P = Pair<BF16>;

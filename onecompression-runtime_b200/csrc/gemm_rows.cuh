@@ -14,10 +14,13 @@
 // tile never straddles two experts (the MMA may read rows of the next segment; those
 // outputs are not stored).
 //
-// Dequant numerics (MODE):
-//   kRowsExact   (DSV4): w = RNE((q - z) * s) computed in pair arithmetic as
-//                 d = q - z, w = fma(d, s_hi, d * s_lo) -- exact whenever q - z is exact in
-//                 the pair type (always for half-integer zeros such as 1.5).
+// Dequant numerics (MODE), bit-exact with the reference in every case:
+//   kRowsExact   (DSV4, dsv4_packed_linear.py:52-56): w = RNE((q - z) * s) with the product in fp32.
+//                 int2: a per-(row, group) table of the four weights, computed in fp32 and
+//                 rounded once, indexed by the codes with byte permutes (any z and s).
+//                 int4: pair arithmetic d = q - z, w = fma(d, s_hi, d * s_lo) when it is exact
+//                 (half-integer zeros such as 1.5 or 7.5, 16-bit scales in range; checked per
+//                 group, warp-uniformly), else the fp32 formula per weight.
 //   kRowsRtn     (RTN, quant_utils.py:91-103): z_o = RNE(z), s_o = RNE(s),
 //                 d = RNE(q - z_o), w = RNE(d * s_o) -- the reference's two roundings.
 #pragma once
@@ -92,6 +95,19 @@ __device__ __forceinline__ RowsConst<BF16, MODE> rows_const(float s, float z) {
   return c;
 }
 
+// Exact mode: does the pair arithmetic give RNE_out(fp32((q - z) * s)) for every 4-bit code q?
+// It does when z is a half-integer in [-1, 16] (then q - z has at most 5 significant bits, is
+// exact in the pair type, and (q - z) * s is exact in fp32 for a 16-bit s) and the scale split is
+// exact (split_exact). Other zeros and fp32 scales take the fp32 formula.
+template <bool BF16, int MODE>
+__device__ __forceinline__ bool rows_pair_exact(float s, float z, const RowsConst<BF16, MODE>& c) {
+  using P = Pair<BF16>;
+  const float z2 = 2.f * z;
+  if (!(z2 == rintf(z2) && z >= -1.f && z <= 16.f)) return false;
+  if (P::to_f32((uint16_t)(c.zm & 0xFFFFu)) != z) return false;
+  return split_exact<BF16>(s, (uint16_t)(c.shi & 0xFFFFu), (uint16_t)(c.slo & 0xFFFFu));
+}
+
 // RNE(q - z) pair -> dequantized pair
 template <bool BF16, int MODE, bool HAS_LO>
 __device__ __forceinline__ uint32_t rows_scale(uint32_t d, const RowsConst<BF16, MODE>& c) {
@@ -109,29 +125,6 @@ __device__ __forceinline__ uint32_t rows_dq(uint32_t mq, const RowsConst<BF16, M
   const uint32_t d = P::sub(q, c.zm);         // RNE(q - z)
   return rows_scale<BF16, MODE, HAS_LO>(d, c);
 }
-
-// Code pair whose halves sit at mantissa bit offsets (o_lo, o_hi) over the magic:
-// (M + c_a 2^o_lo, M + c_b 2^o_hi). After the exact magic subtraction, one fma with the
-// factors (2^-o_lo, 2^-o_hi) and -z gives RNE(c - z) directly: the scaled code is exact
-// and the fma rounds once, the same value as sub(c, z).
-template <bool BF16, int MODE, bool HAS_LO>
-__device__ __forceinline__ uint32_t rows_dq_at(uint32_t mq, uint32_t unscale, const RowsConst<BF16, MODE>& c) {
-  using P = Pair<BF16>;
-  const uint32_t q = P::sub(mq, P::kMagic);
-  const uint32_t d = P::fma(q, unscale, c.zn);
-  return rows_scale<BF16, MODE, HAS_LO>(d, c);
-}
-
-// (1, 1/4) and (1/16, 1/64) as pairs (low half first)
-template <bool BF16> struct Int2Unscale;
-template <> struct Int2Unscale<true> {
-  static constexpr uint32_t k01 = 0x3E803F80u;   // bf16 (1.0, 0.25)
-  static constexpr uint32_t k23 = 0x3C803D80u;   // bf16 (0.0625, 0.015625)
-};
-template <> struct Int2Unscale<false> {
-  static constexpr uint32_t k01 = 0x34003C00u;   // f16 (1.0, 0.25)
-  static constexpr uint32_t k23 = 0x24002C00u;   // f16 (0.0625, 0.015625)
-};
 
 template <bool BF16, int WBITS, int MODE, bool HAS_LO, int BT, int ACC_STAGES, int X_STAGES, int W_STAGES,
           int A_STAGES>
@@ -315,69 +308,122 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
         if ((it % kRowsDqGroups) != wg) continue;
         const int sw = it % W_STAGES, pw = (it / W_STAGES) & 1;
         const int sa = it % A_STAGES, pa = (it / A_STAGES) & 1;
-        // group constants of the block's words: one division per k-block, then the group
-        // advances where a word starts on a group boundary (gs is a multiple of kSpan)
-        RowsConst<BF16, MODE> cst[kWords];
+        // group of each word of the block: one division per k-block, then the group advances
+        // where a word starts on a group boundary (gs is a multiple of kSpan)
         const int kbase = kb * 64;
-        int grp = kbase / p.gs;
-        int next_k = (grp + 1) * p.gs;
-#pragma unroll
-        for (int w = 0; w < kWords; ++w) {
-          const int k0 = kbase + w * kSpan;
-          const bool fresh = (w == 0) || (k0 >= next_k && k0 < p.K);
-          if (w > 0 && fresh) {
-            ++grp;
-            next_k += p.gs;
-          }
-          if (fresh) {
-            const long long si = s_row + (long long)(k0 < p.K ? grp : 0) * p.s_stride_g;
-            cst[w] = rows_const<BF16, MODE>(load_as_f32(sb, p.s_dtype, si), load_as_f32(zb, p.z_dtype, si));
-          } else {
-            cst[w] = cst[w > 0 ? w - 1 : 0];
-          }
-        }
-        if (!mbar_wait(&full_w[sw], pw, abort_flag, kDevErrWFull)) { ok = false; break; }
-        uint32_t q[kWords];
-        const uint32_t* wt = reinterpret_cast<const uint32_t*>(w_smem + sw * Cfg::kWStageBytes + row * Cfg::kKbBytes);
-#pragma unroll
-        for (int w = 0; w < kWords; w += 4) {
-          const uint4 v = *reinterpret_cast<const uint4*>(wt + w);
-          q[w] = v.x; q[w + 1] = v.y; q[w + 2] = v.z; q[w + 3] = v.w;
-        }
-        mbar_arrive(&empty_w[sw]);
-
         uint32_t r32[32];
+        if constexpr (MODE == kRowsExact && WBITS == 2) {
+          // Table decode, bit-exact for any scale and zero: per (row, group) the four weights
+          // RNE((c - z) * s), c = 0..3, are computed in fp32 as the reference does and rounded
+          // once; their low bytes form tlo and their high bytes thi, so a code c selects byte c
+          // of each, and one prmt per table turns four codes into their four values' bytes.
+          uint32_t tlo[kWords], thi[kWords];
+          int grp = kbase / p.gs;
+          int next_k = (grp + 1) * p.gs;
 #pragma unroll
-        for (int w = 0; w < kWords; ++w) {
-          const uint32_t qq = q[w];
-          if (WBITS == 4) {
-            const uint32_t p0 = rows_dq<BF16, MODE, HAS_LO>(lop3_and_or(qq, kMask, Pp::kMagic), cst[w]);
-            const uint32_t p1 = rows_dq<BF16, MODE, HAS_LO>(lop3_and_or(qq >> 4, kMask, Pp::kMagic), cst[w]);
-            const uint32_t p2 = rows_dq<BF16, MODE, HAS_LO>(lop3_and_or(qq >> 8, kMask, Pp::kMagic), cst[w]);
-            const uint32_t p3 = rows_dq<BF16, MODE, HAS_LO>(lop3_and_or(qq >> 12, kMask, Pp::kMagic), cst[w]);
-            r32[4 * w + 0] = prmt(p0, p1, 0x5410u);
-            r32[4 * w + 1] = prmt(p2, p3, 0x5410u);
-            r32[4 * w + 2] = prmt(p0, p1, 0x7632u);
-            r32[4 * w + 3] = prmt(p2, p3, 0x7632u);
-          } else {
-            // byte b holds codes 4b..4b+3 at bits 0,2,4,6. prmt copies it into both halves;
-            // the mask then keeps code 4b in the low half and code 4b+1 (bits 2-3) in the high
-            // half, already the (even k, odd k) order of the A operand. Codes 4b+2, 4b+3 come
-            // from the copy of (q >> 4) in bf16 (7 mantissa bits: bits 6-7 would reach the
-            // exponent) and from the same copy, masked higher, in f16 (10 mantissa bits).
-            const uint32_t qs = qq >> 4;
+          for (int w = 0; w < kWords; ++w) {
+            const int k0 = kbase + w * kSpan;
+            const bool fresh = (w == 0) || (k0 >= next_k && k0 < p.K);
+            if (w > 0 && fresh) {
+              ++grp;
+              next_k += p.gs;
+            }
+            if (fresh) {
+              const long long si = s_row + (long long)(k0 < p.K ? grp : 0) * p.s_stride_g;
+              const float sv = load_as_f32(sb, p.s_dtype, si), zv = load_as_f32(zb, p.z_dtype, si);
+              const uint32_t p01 = pack2_rn<BF16>(__fmul_rn(__fsub_rn(0.f, zv), sv), __fmul_rn(__fsub_rn(1.f, zv), sv));
+              const uint32_t p23 =
+                  pack2_rn<BF16>(__fmul_rn(__fsub_rn(2.f, zv), sv), __fmul_rn(__fsub_rn(3.f, zv), sv));
+              tlo[w] = prmt(p01, p23, 0x6420u);
+              thi[w] = prmt(p01, p23, 0x7531u);
+            } else {
+              tlo[w] = tlo[w > 0 ? w - 1 : 0];
+              thi[w] = thi[w > 0 ? w - 1 : 0];
+            }
+          }
+          if (!mbar_wait(&full_w[sw], pw, abort_flag, kDevErrWFull)) { ok = false; break; }
+          uint32_t q[kWords];
+          const uint32_t* wt =
+              reinterpret_cast<const uint32_t*>(w_smem + sw * Cfg::kWStageBytes + row * Cfg::kKbBytes);
+#pragma unroll
+          for (int w = 0; w < kWords; w += 4) {
+            const uint4 v = *reinterpret_cast<const uint4*>(wt + w);
+            q[w] = v.x; q[w + 1] = v.y; q[w + 2] = v.z; q[w + 3] = v.w;
+          }
+          mbar_arrive(&empty_w[sw]);
+#pragma unroll
+          for (int w = 0; w < kWords; ++w) {
+            // nibble i of u holds code 2i, nibble i of v code 2i + 1; x gathers codes
+            // (4b, 4b+2, 4b+1, 4b+3) as four byte selectors
+            const uint32_t u = q[w] & 0x33333333u, v = (q[w] >> 2) & 0x33333333u;
 #pragma unroll
             for (int b = 0; b < 4; ++b) {
-              const uint32_t dup = prmt(qq, 0u, 0x0101u * b);
-              r32[8 * w + 2 * b] = rows_dq_at<BF16, MODE, HAS_LO>(lop3_and_or(dup, 0x000C0003u, Pp::kMagic),
-                                                                   Int2Unscale<BF16>::k01, cst[w]);
-              if (BF16) {
-                const uint32_t dup2 = prmt(qs, 0u, 0x0101u * b);
-                r32[8 * w + 2 * b + 1] = rows_dq_at<BF16, MODE, HAS_LO>(
-                    lop3_and_or(dup2, 0x000C0003u, Pp::kMagic), Int2Unscale<BF16>::k01, cst[w]);
-              } else {
-                r32[8 * w + 2 * b + 1] = rows_dq_at<BF16, MODE, HAS_LO>(
-                    lop3_and_or(dup, 0x00C00030u, Pp::kMagic), Int2Unscale<BF16>::k23, cst[w]);
+              const uint32_t x = prmt(u, v, 0x40u + 0x11u * (uint32_t)b);
+              const uint32_t lo = prmt(tlo[w], tlo[w], x), hi = prmt(thi[w], thi[w], x);
+              r32[8 * w + 2 * b] = prmt(lo, hi, 0x6240u);      // codes 4b, 4b+1
+              r32[8 * w + 2 * b + 1] = prmt(lo, hi, 0x7351u);  // codes 4b+2, 4b+3
+            }
+          }
+        } else {
+          RowsConst<BF16, MODE> cst[kWords];
+          bool exact = true;  // exact mode: the pair arithmetic reproduces the fp32 formula
+          int grp = kbase / p.gs;
+          int next_k = (grp + 1) * p.gs;
+#pragma unroll
+          for (int w = 0; w < kWords; ++w) {
+            const int k0 = kbase + w * kSpan;
+            const bool fresh = (w == 0) || (k0 >= next_k && k0 < p.K);
+            if (w > 0 && fresh) {
+              ++grp;
+              next_k += p.gs;
+            }
+            if (fresh) {
+              const long long si = s_row + (long long)(k0 < p.K ? grp : 0) * p.s_stride_g;
+              const float sv = load_as_f32(sb, p.s_dtype, si), zv = load_as_f32(zb, p.z_dtype, si);
+              cst[w] = rows_const<BF16, MODE>(sv, zv);
+              if (MODE == kRowsExact) exact = exact && rows_pair_exact<BF16, MODE>(sv, zv, cst[w]);
+            } else {
+              cst[w] = cst[w > 0 ? w - 1 : 0];
+            }
+          }
+          if (!mbar_wait(&full_w[sw], pw, abort_flag, kDevErrWFull)) { ok = false; break; }
+          uint32_t q[kWords];
+          const uint32_t* wt =
+              reinterpret_cast<const uint32_t*>(w_smem + sw * Cfg::kWStageBytes + row * Cfg::kKbBytes);
+#pragma unroll
+          for (int w = 0; w < kWords; w += 4) {
+            const uint4 v = *reinterpret_cast<const uint4*>(wt + w);
+            q[w] = v.x; q[w + 1] = v.y; q[w + 2] = v.z; q[w + 3] = v.w;
+          }
+          mbar_arrive(&empty_w[sw]);
+          if (MODE == kRowsRtn || __all_sync(0xffffffffu, exact)) {
+#pragma unroll
+            for (int w = 0; w < kWords; ++w) {
+              const uint32_t qq = q[w];
+              const uint32_t p0 = rows_dq<BF16, MODE, HAS_LO>(lop3_and_or(qq, kMask, Pp::kMagic), cst[w]);
+              const uint32_t p1 = rows_dq<BF16, MODE, HAS_LO>(lop3_and_or(qq >> 4, kMask, Pp::kMagic), cst[w]);
+              const uint32_t p2 = rows_dq<BF16, MODE, HAS_LO>(lop3_and_or(qq >> 8, kMask, Pp::kMagic), cst[w]);
+              const uint32_t p3 = rows_dq<BF16, MODE, HAS_LO>(lop3_and_or(qq >> 12, kMask, Pp::kMagic), cst[w]);
+              r32[4 * w + 0] = prmt(p0, p1, 0x5410u);
+              r32[4 * w + 1] = prmt(p2, p3, 0x5410u);
+              r32[4 * w + 2] = prmt(p0, p1, 0x7632u);
+              r32[4 * w + 3] = prmt(p2, p3, 0x7632u);
+            }
+          } else {
+            // zeros or scales the pair arithmetic cannot reproduce exactly (a zero that is not a
+            // half-integer, an fp32 scale, a scale outside the pair type's range): the reference's
+            // formula in fp32, RNE((q - z) * s), for every weight of the warp's block
+#pragma unroll
+            for (int w = 0; w < kWords; ++w) {
+              const int k0 = kbase + w * kSpan;
+              const long long si = s_row + (long long)(k0 < p.K ? k0 / p.gs : 0) * p.s_stride_g;
+              const float sv = load_as_f32(sb, p.s_dtype, si), zv = load_as_f32(zb, p.z_dtype, si);
+              const uint32_t qq = q[w];
+#pragma unroll
+              for (int j = 0; j < 8; j += 2) {
+                const float qa = (float)((qq >> (4 * j)) & 0xFu), qb = (float)((qq >> (4 * j + 4)) & 0xFu);
+                r32[4 * w + j / 2] =
+                    pack2_rn<BF16>(__fmul_rn(__fsub_rn(qa, zv), sv), __fmul_rn(__fsub_rn(qb, zv), sv));
               }
             }
           }

@@ -372,8 +372,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             r32[2 * w + 1] = pack2_rn<BF16>(v[2], v[3]);  // k 4w+2, 4w+3
           }
         } else {
-          // per-word group constants
+          // per-word group constants. fp16 activations with bf16 scales (HAS_LO && !BF16) keep
+          // each word's scale and zero too: a bf16 scale outside fp16's range makes the split
+          // inexact, and then the warp's block takes the fp32 formula instead (below).
+          constexpr bool kCheck = HAS_LO && !BF16;
           DqConst<BF16> cst[8];
+          float sfw[kCheck ? 8 : 1];
+          int zfw[kCheck ? 8 : 1];
+          bool exact = true;
           if (!p.sz_tma) {
             int last = -1;
             float sv = 0.f;
@@ -388,9 +394,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 uint32_t z = (zw >> zsh) & 0xFu;
                 if (p.v1) z = (z + 1u) & 0xFu;
                 cst[w] = make_dq_const<BF16>(sv, (int)z);
+                if constexpr (kCheck) {
+                  exact = exact && dq_const_exact<BF16>(sv, cst[w]);
+                  sfw[w] = sv;
+                  zfw[w] = (int)z;
+                }
                 last = grp;
               } else {
                 cst[w] = cst[w > 0 ? w - 1 : 0];
+                if constexpr (kCheck) {
+                  sfw[w] = sfw[w > 0 ? w - 1 : 0];
+                  zfw[w] = zfw[w > 0 ? w - 1 : 0];
+                }
               }
             }
           }
@@ -412,26 +427,48 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 uint32_t z = (zt[r * 16 + (row >> 3)] >> zsh) & 0xFu;
                 if (p.v1) z = (z + 1u) & 0xFu;
                 const DqConst<BF16> c = make_dq_const<BF16>(sv, (int)z);
+                if constexpr (kCheck) exact = exact && dq_const_exact<BF16>(sv, c);
                 // words 4r..4r+3 (nr == 2) or all 8 words (nr == 1)
   #pragma unroll
                 for (int w = 0; w < 8; ++w)
-                  if ((nr == 1) || (w >> 2) == r) cst[w] = c;
+                  if ((nr == 1) || (w >> 2) == r) {
+                    cst[w] = c;
+                    if constexpr (kCheck) {
+                      sfw[w] = sv;
+                      zfw[w] = (int)z;
+                    }
+                  }
               }
             }
           }
           mbar_arrive(&empty_w[sw]);
 
+          if (!kCheck || __all_sync(0xffffffffu, exact)) {
   #pragma unroll
-          for (int w = 0; w < 8; ++w) {
-            const uint32_t qq = q[w];
-            const uint32_t p0 = dq_pair<BF16, HAS_LO>(lop3_and_or(qq, 0x000F000Fu, Pp::kMagic), cst[w]);        // k0,k4
-            const uint32_t p1 = dq_pair<BF16, HAS_LO>(lop3_and_or(qq >> 4, 0x000F000Fu, Pp::kMagic), cst[w]);   // k1,k5
-            const uint32_t p2 = dq_pair<BF16, HAS_LO>(lop3_and_or(qq >> 8, 0x000F000Fu, Pp::kMagic), cst[w]);   // k2,k6
-            const uint32_t p3 = dq_pair<BF16, HAS_LO>(lop3_and_or(qq >> 12, 0x000F000Fu, Pp::kMagic), cst[w]);  // k3,k7
-            r32[4 * w + 0] = prmt(p0, p1, 0x5410u);  // k0,k1
-            r32[4 * w + 1] = prmt(p2, p3, 0x5410u);  // k2,k3
-            r32[4 * w + 2] = prmt(p0, p1, 0x7632u);  // k4,k5
-            r32[4 * w + 3] = prmt(p2, p3, 0x7632u);  // k6,k7
+            for (int w = 0; w < 8; ++w) {
+              const uint32_t qq = q[w];
+              const uint32_t p0 = dq_pair<BF16, HAS_LO>(lop3_and_or(qq, 0x000F000Fu, Pp::kMagic), cst[w]);        // k0,k4
+              const uint32_t p1 = dq_pair<BF16, HAS_LO>(lop3_and_or(qq >> 4, 0x000F000Fu, Pp::kMagic), cst[w]);   // k1,k5
+              const uint32_t p2 = dq_pair<BF16, HAS_LO>(lop3_and_or(qq >> 8, 0x000F000Fu, Pp::kMagic), cst[w]);   // k2,k6
+              const uint32_t p3 = dq_pair<BF16, HAS_LO>(lop3_and_or(qq >> 12, 0x000F000Fu, Pp::kMagic), cst[w]);  // k3,k7
+              r32[4 * w + 0] = prmt(p0, p1, 0x5410u);  // k0,k1
+              r32[4 * w + 1] = prmt(p2, p3, 0x5410u);  // k2,k3
+              r32[4 * w + 2] = prmt(p0, p1, 0x7632u);  // k4,k5
+              r32[4 * w + 3] = prmt(p2, p3, 0x7632u);  // k6,k7
+            }
+          } else if constexpr (kCheck) {
+            // the formula of quant_utils.py:66-69 in fp32: (q - z) is an exact integer, its product
+            // with a bf16 scale is exact in fp32, and one conversion rounds it to fp16
+  #pragma unroll
+            for (int w = 0; w < 8; ++w) {
+              const uint32_t qq = q[w];
+  #pragma unroll
+              for (int j = 0; j < 8; j += 2) {
+                const float da = (float)((int)((qq >> (4 * j)) & 0xFu) - zfw[w]);
+                const float db = (float)((int)((qq >> (4 * j + 4)) & 0xFu) - zfw[w]);
+                r32[4 * w + j / 2] = pack2_rn<BF16>(__fmul_rn(da, sfw[w]), __fmul_rn(db, sfw[w]));
+              }
+            }
           }
         }
         if (!mbar_wait(&empty_a[sa], pa ^ 1, abort_flag, kDevErrAEmpty)) { ok = false; break; }

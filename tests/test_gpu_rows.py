@@ -37,23 +37,33 @@ def test_rtn_linear_golden(cuda_device, case):
         assert eager.max_abs_rel(y.float().cpu().numpy(), to_f32(d[f"y_{od}"], od)) < GEMM_TOL
 
 
-def _dsv4_layer(out_f, in_f, wbits, gs, seed, zeros="half"):
+def _dsv4_layer(out_f, in_f, wbits, gs, seed, zeros="half", sdt=np.float16):
     rng = np.random.default_rng(seed)
     codes = rng.integers(0, 1 << wbits, size=(out_f, in_f))
     packed = dsv4.pack_codes(codes, wbits)
     G = (in_f + gs - 1) // gs if gs > 0 else 1
-    s = rng.uniform(0.005, 0.05, size=(out_f, G)).astype(np.float16)
+    s = rng.uniform(0.005, 0.05, size=(out_f, G)).astype(sdt)
     if zeros == "half":
         z = np.full((out_f, G), 1.5 if wbits == 2 else 7.5, np.float16)
+    elif zeros == "mixed":  # half-integer zeros except in a few rows: per-warp choice of decode path
+        z = np.full((out_f, G), 1.5 if wbits == 2 else 7.5, np.float16)
+        z[::37] = rng.uniform(0, (1 << wbits) - 1, size=z[::37].shape).astype(np.float16)
     else:
         z = rng.uniform(0, (1 << wbits) - 1, size=(out_f, G)).astype(np.float16)
     return {"qweight_packed": torch.from_numpy(packed), "scales": torch.from_numpy(s),
             "qzeros": torch.from_numpy(z), "wbits": wbits, "groupsize": gs, "in_features": in_f}
 
 
+def _bits_and_name(t: torch.Tensor):
+    if t.dtype == torch.float32:
+        return t.numpy(), "f32"
+    return t.numpy().view(np.uint16), "f16"
+
+
 def _dsv4_weight(p, od):
-    return dsv4.dequant_dsv4(p["qweight_packed"].numpy(), p["scales"].numpy().view(np.uint16), "f16",
-                             p["qzeros"].numpy().view(np.uint16), "f16", p["wbits"], p["groupsize"],
+    s, sn = _bits_and_name(p["scales"])
+    z, zn = _bits_and_name(p["qzeros"])
+    return dsv4.dequant_dsv4(p["qweight_packed"].numpy(), s, sn, z, zn, p["wbits"], p["groupsize"],
                              p["in_features"], od)
 
 
@@ -72,16 +82,21 @@ def test_dsv4_linear_fused(cuda_device, wbits, gs, zeros, M):
     assert max_abs_rel(y, ref) < 1e-2
 
 
-@pytest.mark.parametrize("wbits,gs", [(2, 64), (4, 128), (2, 0)])
+@pytest.mark.parametrize("wbits,gs,zeros,sdt", [
+    (2, 64, "half", np.float16), (4, 128, "half", np.float16), (2, 0, "half", np.float16),
+    (2, 64, "rand", np.float16), (4, 64, "rand", np.float16), (2, 0, "rand", np.float16),
+    (4, 128, "mixed", np.float16), (4, 64, "half", np.float32), (2, 128, "rand", np.float32)],
+    ids=lambda v: v.__name__ if isinstance(v, type) else str(v))
 @pytest.mark.parametrize("adt", ["bf16", "f16"])
-def test_dsv4_weights_bit_exact_through_gemm(cuda_device, wbits, gs, adt):
+def test_dsv4_weights_bit_exact_through_gemm(cuda_device, wbits, gs, zeros, sdt, adt):
     """One-hot activation rows make y = W^T exactly (one nonzero product per output, fp32 sum,
     one exact rounding), so the weights the kernel decodes into the MMA operand are compared bit
-    for bit with the oracle. Half-integer zeros: the exact mode's domain. bf16 activations take
-    the split-scale path (fp16 scales), f16 activations the single-multiply path."""
+    for bit with the oracle, for any zero point and scale dtype: int2 layers decode through the
+    fp32 value table; int4 layers through the pair arithmetic where it is exact (half-integer
+    zeros, 16-bit scales) and the fp32 formula elsewhere, chosen per warp."""
     from onecomp_runtime.layers import Dsv4PackedLinear
     K, N = 512, 192
-    p = _dsv4_layer(N, K, wbits, gs, seed=wbits + gs, zeros="half")
+    p = _dsv4_layer(N, K, wbits, gs, seed=wbits + gs, zeros=zeros, sdt=sdt)
     layer = Dsv4PackedLinear(p, buffer_device=cuda_device)
     assert layer._rows_handle() is not None
     y = layer(torch.eye(K, device=cuda_device, dtype=TDT[adt]))
@@ -89,14 +104,47 @@ def test_dsv4_weights_bit_exact_through_gemm(cuda_device, wbits, gs, adt):
     np.testing.assert_array_equal(got, _dsv4_weight(p, adt))
 
 
-def test_dsv4_host_buffers_match_fused(cuda_device):
+@pytest.mark.parametrize("wbits,gs", [(2, 64), (4, 128)])
+def test_dsv4_host_buffers_match_fused(cuda_device, wbits, gs):
+    """Host-resident (offloaded) layers copy their packed bytes into the shared staging slot and
+    run the same fused kernel: identical output to device-resident buffers, also when two layers
+    of one shape take turns on the slot; and within tolerance of the oracle."""
     from onecomp_runtime.layers import Dsv4PackedLinear
-    p = _dsv4_layer(128, 256, 2, 64, seed=5)
+    p = _dsv4_layer(128, 256, wbits, gs, seed=5)
+    p2 = _dsv4_layer(128, 256, wbits, gs, seed=6)
     x = torch.randn(7, 256, device=cuda_device).to(torch.bfloat16)
-    y_host = Dsv4PackedLinear(p, buffer_device="cpu")(x)       # per-call copy + dequant + F.linear
-    y_dev = Dsv4PackedLinear(p, buffer_device=cuda_device)(x)  # fused row-packed kernel
-    ref = y_host.float()
-    assert float((y_dev.float() - ref).abs().max() / ref.abs().max()) < 1e-2
+    host, host2 = Dsv4PackedLinear(p, buffer_device="cpu"), Dsv4PackedLinear(p2, buffer_device="cpu")
+    y_host, y_host2, y_host_again = host(x), host2(x), host(x)
+    y_dev = Dsv4PackedLinear(p, buffer_device=cuda_device)(x)
+    y_dev2 = Dsv4PackedLinear(p2, buffer_device=cuda_device)(x)
+    assert torch.equal(y_host, y_dev) and torch.equal(y_host_again, y_dev) and torch.equal(y_host2, y_dev2)
+    xb = x.cpu().view(torch.int16).numpy().view(np.uint16)
+    ref, _ = eager.linear_ref(xb, "bf16", _dsv4_weight(p, "bf16"), "bf16")
+    assert max_abs_rel(y_host, ref) < 1e-2
+
+
+def test_rtn_padded_layouts(cuda_device):
+    """RTN layers whose packed row stride is not a multiple of 16 bytes, or whose in_features is
+    not a multiple of 8 (one group per row), run the fused kernel on a zero-padded copy."""
+    from onecomp_runtime.layers import PackedRTNLinear
+    from oracle import rtn
+    rng = np.random.default_rng(9)
+    for K, G in ((208, 2), (100, 1), (75, 1)):
+        N = 96
+        codes = rng.integers(0, 16, size=(N, K))
+        q = np.zeros((N, (K + 1) // 2), np.uint8)
+        q[:, :] = (codes[:, 0::2] | (np.pad(codes[:, 1::2], ((0, 0), (0, K % 2))) << 4)).astype(np.uint8)
+        s = rng.uniform(0.01, 0.1, size=(N, G)).astype(np.float16)
+        z = rng.integers(0, 16, size=(N, G)).astype(np.float16)
+        layer = PackedRTNLinear(K, N, torch.from_numpy(q).to(cuda_device), torch.from_numpy(s).to(cuda_device),
+                                torch.from_numpy(z).to(cuda_device))
+        assert layer._rows_handle() is not None
+        x = torch.randn(33, K, device=cuda_device).to(torch.bfloat16)
+        y = layer(x)
+        w = rtn.dequant_rtn(q, s.view(np.uint16), "f16", z.view(np.uint16), "f16", K, N, "bf16")
+        xb = x.cpu().view(torch.int16).numpy().view(np.uint16)
+        ref, _ = eager.linear_ref(xb, "bf16", w, "bf16")
+        assert max_abs_rel(y, ref) < 1e-2, (K, G)
 
 
 def _moe_setup(E=8, H=256, F=128, seed=0):
