@@ -1,28 +1,34 @@
 """Benchmark of the int4 linear hot path on B200 (one JSON line on rank 0).
 
-Default workload: a FLUX-style DiT block stack --
-8 blocks of qkv 3072->9216, proj 3072->3072, fc1 3072->9216, fc2 9216->3072,
-AutoGPTQ v1 int4, groupsize 32, bf16 activations N(0,1), M = 4608 tokens
-(4096 image + 512 text). Random-init packed weights (seeded), synthetic
-activations. Glue between linears (q slice of qkv as the attention stand-in,
-residual adds, RMS norm, tanh-GELU) runs in torch and is timed with the step.
+Default workload (the DiT stack the metric quotes at 1/2/4/8 GPUs): a
+video-DiT-shaped stack of 12 blocks, hidden 4096 (qkv 4096->12288, out 4096->4096,
+fc1 4096->16384, fc2 16384->4096), AutoGPTQ v1 int4 gs32, M = 32768 bf16 tokens N(0,1),
+seeded random packed weights (no checkpoints offline). Tensor parallel over the N ranks of
+the job: qkv and fc1 column-parallel, out and fc2 row-parallel with an NCCL all-reduce
+(sum) per row-parallel linear, issued in M-chunks that overlap the next chunk's GEMM.
+Per block: qkv; its q slice stands in for attention; out (+ residual in rank 0's
+epilogue); RMS norm; fc1 (tanh-GELU in the epilogue); fc2 (+ residual); RMS norm.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-                    [--workload cfg1|cfg0|cfg2]
+                    [--workload cfg4|cfg1|cfg2|cfg3] [--no-nested]
 
-* ``value``: whole-job tokens/s (N ranks each run their own 4608-token batch:
-  weak scaling, no data-path collective), device-timed with CUDA events,
-  max over ranks. Inputs and weights are resident in HBM; the stack's weights
-  (437 MB packed) exceed the 126 MB L2, so every step streams them from HBM.
-* ``e2e``: the same step through the public module API with the input copied
-  from pinned host memory and the output read back every step.
-* ``roofline``: the tcgen05 GEMM launches, timed individually with CUDA events
-  inside the timed steps: achieved = 2*M*K*N summed / their summed duration,
-  against the measured sustained bf16 peak (MEASURED_PEAKS.json).
-* ``cpu_baseline`` (rank 0, N=1): the reference CPU eager path (dequantize once,
-  torch CPU bf16 ``F.linear``) restated in ``oracle/``, on a bounded sample
-  (one block, extrapolated to the stack).
-* ``--impl reference``: the same CPU eager path as the reference arm.
+* ``value``: tokens/s of the whole job (the same 32768 tokens whatever N: strong scaling),
+  device-timed with CUDA events around K steps, max over ranks. Weights and inputs are
+  resident in HBM and larger than the 126 MB L2, so nothing needs flushing.
+* ``e2e``: the same steps through the public module API with each step's input copied from
+  pinned host memory and its output read back (on every rank), double-buffered on side streams.
+* ``roofline``: the tcgen05 GEMM launches of the timed steps, each bracketed by CUDA events on
+  the stream that launches it: achieved = sum(2 M K N) / sum(durations), against the measured
+  bf16 peak (burst when the SM clock held its maximum during the timed region, sustained
+  when it was power capped).
+* ``comm`` (N > 1): one step's all-reduces timed alone (no GEMM in between) and their share.
+* ``cpu_baseline`` (rank 0, N = 1): the reference's CPU eager path restated in ``oracle/``
+  (weights dequantized once, torch CPU bf16 ``F.linear``) on a bounded sample: one block at
+  ``--cpu-sample-m`` tokens, the same K and W steps as the reference arm, extrapolated x12.
+* ``workloads``: the other configurations, each with its own roofline: ``cfg1`` (FLUX-style
+  8-block stack, 4608 tokens per GPU, replicas), ``cfg2`` (decode layer set, M = 1/4/16, HBM
+  fraction) and ``cfg3`` (packed MoE layer, expert parallel over the N ranks).
+* ``--impl reference``: the CPU eager path above as the reference arm (rank 0 only).
 """
 from __future__ import annotations
 
@@ -45,14 +51,15 @@ for _p in (str(ROOT), str(PKG)):
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
-METRIC = "DiT-stack tokens/s (int4 GPTQ linear stack)"
+METRIC = "DiT-stack tokens/s (video-DiT int4 GPTQ stack, 12 blocks, hidden 4096, 32768 tokens, tensor parallel)"
+METRIC_CFG1 = "DiT-stack tokens/s (FLUX-style int4 GPTQ stack, 8 blocks, hidden 3072, 4608 tokens per GPU)"
 
-
-
-# DRAM traffic measured by ncu (dram__bytes_read.sum + dram__bytes_write.sum) for the dominant
-# kernel of each workload; the commands and per-launch figures are in profiles/.
-TC_TRAFFIC_BYTES_PER_LAUNCH = 103_200_000    # cfg1: mean of qkv, proj, fc1, fc2 launches
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the dominant kernel of
+# each workload, from one ncu capture (profiles/ holds the command and the per-launch figures).
+TC_TRAFFIC_CFG1 = 103_200_000     # cfg1: mean of the qkv, proj, fc1, fc2 launches at M = 4608
+TC_TRAFFIC_CFG4 = None            # cfg4: set from its capture
 GEMV_TRAFFIC_BYTES_PER_LAUNCH = 21_852_160   # cfg2: q/k/v layer, M = 1 (algorithmic 21.8 MB)
+
 
 def load_peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
@@ -61,6 +68,16 @@ def load_peaks() -> dict:
         return {"hbm_gbs": d.get("hbm_gbs"), "bf16": d.get("bf16_tflops"),
                 "bf16_sustained": d.get("bf16_tflops_sustained"), "source": "measured"}
     return {"hbm_gbs": 6650.0, "bf16": 1590.0, "bf16_sustained": 1400.0, "source": "fallback"}
+
+
+def tensor_peak(peaks: dict, clk: dict | None) -> tuple[float, str]:
+    """The bf16 denominator that matches the clocks seen: the burst figure when the SM clock stayed
+    at its maximum (a short region), the sustained (power-capped) one otherwise."""
+    burst = clk is not None and clk.get("sm_mhz") and clk.get("sm_max_mhz") and \
+        clk["sm_mhz"] >= 0.95 * clk["sm_max_mhz"] and "sw_power_cap" not in clk.get("reasons", [])
+    if burst:
+        return peaks["bf16"], f"{peaks['source']} bf16_tflops (burst: SM clock at its maximum)"
+    return peaks["bf16_sustained"], f"{peaks['source']} bf16_tflops_sustained (power-capped clocks)"
 
 
 # ----------------------------------------------------------------------------- clocks
@@ -145,65 +162,183 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows), "source": "nvidia-smi 100 ms"}
 
 
-# ----------------------------------------------------------------------------- model
+# ----------------------------------------------------------------------------- plumbing
 def rms_norm(h: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
     """RMS norm without weight, fp32 statistics (torch's fused rms_norm)."""
     return torch.nn.functional.rms_norm(h, (h.shape[-1],), eps=eps)
 
 
-class DiTStack:
-    """8 FLUX-style blocks of FusedInt4Linear layers (random packed weights)."""
+class Job:
+    """Rank, world and device of this process; NCCL process group when N > 1."""
 
-    def __init__(self, device, blocks: int, layers, gs: int, seed: int = 1000):
-        from onecomp_runtime.layers import FusedInt4Linear
-        from onecomp_runtime.testing import gptq_layer
-        self.blocks = []
-        for b in range(blocks):
-            blk = {}
-            for li, (name, K, N) in enumerate(layers):
-                t = gptq_layer(K, N, gs, seed=seed * (b + 1) + li, device=device)
-                blk[name] = FusedInt4Linear(K, N, t["qweight"], t["scales"], t["qzeros"], t["bias"], gs)
-            self.blocks.append(blk)
-        self.hidden = layers[0][1]
-        self.gemm_events: list | None = None
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.dev = None
 
-    def _lin(self, layer, x, residual=None, activation=None):
-        if self.gemm_events is None:
-            return layer.forward_fused(x, residual=residual, activation=activation)
-        s = torch.cuda.Event(enable_timing=True)
-        e = torch.cuda.Event(enable_timing=True)
-        s.record()
-        y = layer.forward_fused(x, residual=residual, activation=activation)
-        e.record()
-        self.gemm_events.append((s, e, 2 * x.shape[0] * layer.in_features * layer.out_features))
-        return y
+    def init_gpu(self):
+        import datetime
+        torch.cuda.set_device(self.local)
+        self.dev = torch.device("cuda", self.local)
+        if self.world > 1 and not torch.distributed.is_initialized():
+            torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=self.dev)
+        from onecomp_runtime import _lib
+        _lib.require_b200(self.dev)
+        return self
 
-    def forward(self, h: torch.Tensor) -> torch.Tensor:
-        """Per block: q = qkv(h)[:, :H]; h = rms(h + proj(q)); h = rms(h + fc2(gelu(fc1(h)))).
+    def barrier(self):
+        if self.world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(self.dev)
 
-        The residual adds and the tanh-GELU run in the GEMM epilogues (forward_fused)."""
-        H = self.hidden
-        for blk in self.blocks:
-            qkv = self._lin(blk["qkv"], h)
-            q = qkv[:, :H]                       # attention stand-in: the q slice
-            h = rms_norm(self._lin(blk["proj"], q, residual=h))
-            f = self._lin(blk["fc1"], h, activation="gelu_tanh")
-            h = rms_norm(self._lin(blk["fc2"], f, residual=h))
-        return h
+    def max_over_ranks(self, *vals: float) -> list[float]:
+        t = torch.tensor(list(vals), dtype=torch.float64, device=self.dev)
+        if self.world > 1:
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return [float(v) for v in t]
 
-    def gemm_count_per_step(self) -> int:
-        return 4 * len(self.blocks)
+    def close(self):
+        if self.world > 1 and torch.distributed.is_initialized():
+            torch.distributed.destroy_process_group()
 
 
-# ----------------------------------------------------------------------------- CPU eager
-def cpu_eager_block(layers, gs: int, M: int, seed: int = 1000):
-    """The reference CPU eager path (oracle restatement) for one block.
+class LaunchTimer:
+    """CUDA events around every launch of the instrumented kernels (on the launching stream), with
+    their algorithmic flops: the roofline's achieved rate and the count of our launches."""
 
-    Weights are dequantized once by the oracle (as ``backend.build_eager``
-    does at load time, not timed); each call runs the block's four
-    ``F.linear`` in bf16 on the host cores plus the glue. Returns
-    ``(run, threads)``.
-    """
+    def __init__(self):
+        self.on = False
+        self.rec: list = []
+        self.launches = 0
+
+    def wrap_gptq(self, layer):
+        orig = layer._gemm_2d
+
+        def timed(a_2d, out, residual=None, act=0):
+            if not self.on:
+                return orig(a_2d, out, residual, act)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            orig(a_2d, out, residual, act)
+            e.record()
+            self.rec.append((s, e, 2.0 * a_2d.shape[0] * layer.in_features * layer.out_features))
+            self.launches += 1 + (1 if layer._relayout else 0)
+        layer._gemm_2d = timed
+
+    def wrap_rows(self, handle):
+        orig = handle.gemm
+
+        def timed(a, out, offsets=None, bias=None):
+            if not self.on:
+                return orig(a, out, offsets, bias)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            orig(a, out, offsets, bias)
+            e.record()
+            self.rec.append((s, e, 2.0 * a.shape[0] * handle.K * handle.N))
+            self.launches += 1
+        handle.gemm = timed
+
+    def start(self):
+        self.rec, self.launches, self.on = [], 0, True
+
+    def stop(self) -> tuple[float, float]:
+        """(summed launch milliseconds, summed flops); events must have completed."""
+        self.on = False
+        return sum(s.elapsed_time(e) for s, e, _ in self.rec), sum(f for _, _, f in self.rec)
+
+
+def timed_steps(job: Job, fn, steps: int, warmup: int, clocks: bool = True, before=None):
+    """(max-over-ranks ms per step, clock record) for `steps` calls of fn after `warmup` calls;
+    `before()` runs between the warm-up and the timed calls."""
+    for _ in range(warmup):
+        fn()
+    job.barrier()
+    if before is not None:
+        before()
+    clk = ClockSampler(job.local) if clocks else None
+    if clk:
+        clk.start()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record()
+    for _ in range(steps):
+        fn()
+    s1.record()
+    job.barrier()
+    rec = clk.stop() if clk else None
+    ms, = job.max_over_ranks(s0.elapsed_time(s1) / steps)
+    return ms, rec
+
+
+def e2e_steps(job: Job, forward, x_shape, steps: int, dtype=torch.bfloat16):
+    """Steps through the public API with host buffers: each step's input is copied from pinned host
+    memory and its output read back; copies of step i+1 / i-1 overlap step i (double-buffered).
+    Returns (max-over-ranks total ms, h2d bytes per step, d2h bytes per step)."""
+    dev = job.dev
+    g = torch.Generator().manual_seed(99 + job.rank)
+    x_host = [torch.randn(x_shape, generator=g).to(dtype).pin_memory() for _ in range(2)]
+    y_host = [None, None]
+    x_dev = [torch.empty(x_shape, dtype=dtype, device=dev) for _ in range(2)]
+    main = torch.cuda.current_stream(dev)
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    in_ready = [torch.cuda.Event() for _ in range(2)]
+    in_free = [torch.cuda.Event() for _ in range(2)]
+    out_ready = [torch.cuda.Event() for _ in range(2)]
+    out_bytes = [0]
+
+    def run(n):
+        for i in range(n):
+            b = i & 1
+            with torch.cuda.stream(s_in):
+                if i >= 2:
+                    s_in.wait_event(in_free[b])
+                x_dev[b].copy_(x_host[b], non_blocking=True)
+                in_ready[b].record(s_in)
+            main.wait_event(in_ready[b])
+            y = forward(x_dev[b])
+            in_free[b].record(main)
+            out_ready[b].record(main)
+            if y_host[b] is None or y_host[b].shape != y.shape:
+                y_host[b] = torch.empty(y.shape, dtype=y.dtype, pin_memory=True)
+            out_bytes[0] = y.numel() * y.element_size()
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(out_ready[b])
+                y_host[b].copy_(y, non_blocking=True)
+                y.record_stream(s_out)
+        main.wait_stream(s_in)
+        main.wait_stream(s_out)
+
+    run(2)
+    job.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(main)
+    run(steps)
+    e1.record(main)
+    job.barrier()
+    ms, = job.max_over_ranks(e0.elapsed_time(e1))
+    if not torch.isfinite(y_host[(steps - 1) & 1].float()).all():
+        raise RuntimeError("non-finite end-to-end output")
+    return ms, x_host[0].numel() * x_host[0].element_size(), out_bytes[0]
+
+
+def roofline_tensor(ms: float, flops: float, peaks: dict, clk, traffic, kernel: str, step_ms_total: float,
+                    steps: int) -> dict:
+    achieved = flops / (ms / 1e3) / 1e12 if ms > 0 else 0.0
+    peak, src = tensor_peak(peaks, clk)
+    return {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+            "frac": round(achieved / peak, 4), "traffic": traffic, "traffic_unit": "bytes per launch",
+            "kernel": kernel, "peak_source": src,
+            "gemm_share_of_step": round(ms / step_ms_total, 4) if step_ms_total else None,
+            "gemm_ms_per_step": round(ms / steps, 3)}
+
+
+# ----------------------------------------------------------------------------- CPU eager baseline
+def cpu_eager_block(layers, gs: int, M: int, seed: int):
+    """The reference CPU eager path for one DiT block (``backend.build_eager``: dequantize once,
+    then ``nn.Linear`` in bf16 on the host cores), restated in ``oracle/``: weights from
+    ``oracle.gptq.dequant_gptq_torch`` (load time, not timed), each call the block's four
+    ``F.linear`` in bf16 plus the glue. Returns ``(run, threads)``."""
     from oracle import gptq
     from oracle.eager import EagerCPU
     from onecomp_runtime.testing import gptq_layer
@@ -211,24 +346,24 @@ def cpu_eager_block(layers, gs: int, M: int, seed: int = 1000):
     mods = {}
     for li, (name, K, N) in enumerate(layers):
         t = gptq_layer(K, N, gs, seed=seed + li)
-        s_bits = t["scales"].view(torch.int16).numpy().view(np.uint16)
-        w = gptq.dequant_gptq(t["qweight"].numpy(), s_bits, "f16", t["qzeros"].numpy(), t["g_idx"].numpy(), K, N,
-                              "bf16")
+        w = gptq.dequant_gptq_torch(t["qweight"], t["scales"], t["qzeros"], t["g_idx"], K, N, torch.bfloat16)
         b_bits = t["bias"].view(torch.int16).numpy().view(np.uint16)
-        mods[name] = EagerCPU(w, "bf16", b_bits, "f16")
+        mods[name] = EagerCPU(w.view(torch.int16).numpy().view(np.uint16), "bf16", b_bits, "f16")
+        del w, t
     H = layers[0][1]
     x = torch.randn(M, H, dtype=torch.float32).to(torch.bfloat16)
 
     def run():
-        qkv = mods["qkv"](x)
-        h = rms_norm(x + mods["proj"](qkv[:, :H].contiguous()))
-        f = torch.nn.functional.gelu(mods["fc1"](h), approximate="tanh")
-        return rms_norm(h + mods["fc2"](f))
+        qkv = mods[layers[0][0]](x)
+        h = rms_norm(x + mods[layers[1][0]](qkv[:, :H].contiguous()))
+        f = torch.nn.functional.gelu(mods[layers[2][0]](h), approximate="tanh")
+        return rms_norm(h + mods[layers[3][0]](f))
 
     return run, torch.get_num_threads()
 
 
 def time_cpu(run, warmup: int, steps: int) -> float:
+    """Seconds per call."""
     for _ in range(warmup):
         run()
     t0 = time.perf_counter()
@@ -237,28 +372,199 @@ def time_cpu(run, warmup: int, steps: int) -> float:
     return (time.perf_counter() - t0) / steps
 
 
-# ----------------------------------------------------------------------------- decode (cfg2)
-def bench_decode(args):
-    """gptq_v2 gs128 act-order layer set (fp16 scales, bf16 activations),
-    M in {1, 4, 16}, CUDA-graph replayed. ``--wbits 8``: the same shapes as 8-bit gs128 layers
-    without act-order and with bf16 scales (the model dtype), as the Qwen3.6 adapter builds them.
+def cpu_baseline_cfg4(args) -> dict:
+    from onecomp_runtime.testing import CFG4, CFG4_LAYERS
+    m, blocks = args.cpu_sample_m, CFG4["blocks"]
+    run, cores = cpu_eager_block(CFG4_LAYERS, CFG4["gs"], m, seed=4000)
+    per_block = time_cpu(run, args.warmup, args.steps)
+    return {"value": round(m / (per_block * blocks), 1), "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"one cfg4 block (4 linears + glue) at M={m} tokens per step, {args.steps} steps after "
+                      f"{args.warmup} warm-up, torch CPU bf16 F.linear on weights dequantized once by the oracle's "
+                      f"formula; tokens/s = M / (block time x {blocks} blocks)",
+            "ms_per_sample": round(per_block * 1e3, 3)}
 
-    Reported value: packed bytes streamed per second (qweight + scales + qzeros
-    + g_idx of the 5 layers, + activations) at the largest M; every M in ``per_m``.
-    """
+
+# ----------------------------------------------------------------------------- cfg4: TP video-DiT stack
+class TPStack:
+    """12 video-DiT blocks of B200 int4 linears sharded over the job's ranks."""
+
+    def __init__(self, job: Job, blocks: int, timer: LaunchTimer):
+        from onecomp_runtime.layers import FusedInt4Linear
+        from onecomp_runtime.tensor_parallel import build_tp_block
+        from onecomp_runtime.testing import CFG4, CFG4_LAYERS, gptq_layer
+        self.gs, self.H = CFG4["gs"], CFG4["hidden"]
+        self.hq = self.H // job.world
+        self.blocks = []
+        for b in range(blocks):
+            tens = {name: gptq_layer(K, N, self.gs, seed=4000 + 10 * b + i, device=job.dev)
+                    for i, (name, K, N) in enumerate(CFG4_LAYERS)}
+            blk = build_tp_block(tens, CFG4_LAYERS, job.rank, job.world, self.gs,
+                                 lambda t, K, N: FusedInt4Linear(K, N, t["qweight"], t["scales"], t["qzeros"],
+                                                                 t.get("bias"), self.gs))
+            for mod in blk.values():
+                timer.wrap_gptq(mod.local)
+            self.blocks.append(blk)
+            del tens
+
+    def forward(self, h: torch.Tensor) -> torch.Tensor:
+        for blk in self.blocks:
+            qkv = blk["qkv"](h)
+            h = rms_norm(blk["out"](qkv[:, :self.hq], residual=h))
+            f = blk["fc1"](h, activation="gelu_tanh")
+            h = rms_norm(blk["fc2"](f, residual=h))
+        return h
+
+
+def allreduce_alone(job: Job, M: int, H: int, per_step: int, chunks: int) -> float:
+    """Milliseconds of one step's row-parallel all-reduces issued back to back (no GEMMs)."""
+    buf = torch.zeros((M, H), dtype=torch.bfloat16, device=job.dev)
+    step = (M + chunks - 1) // chunks
+
+    def once():
+        for _ in range(per_step):
+            for c0 in range(0, M, step):
+                torch.distributed.all_reduce(buf[c0:c0 + step])
+
+    once()
+    ms, _ = timed_steps(job, once, 3, 1, clocks=False)
+    return ms
+
+
+def bench_cfg4(args, job: Job, peaks: dict, with_cpu: bool) -> dict:
+    from onecomp_runtime.testing import CFG4, CFG4_LAYERS
+    M, H, blocks = CFG4["M"], CFG4["hidden"], (args.blocks or CFG4["blocks"])
+    timer = LaunchTimer()
+    stack = TPStack(job, blocks, timer)
+    x = torch.randn((M, H), generator=torch.Generator(device=job.dev).manual_seed(5), device=job.dev).to(torch.bfloat16)
+    with torch.no_grad():
+        y = stack.forward(x)
+        torch.cuda.synchronize(job.dev)
+        if not torch.isfinite(y).all():
+            raise RuntimeError("non-finite stack output")
+        ms, clk = timed_steps(job, lambda: stack.forward(x), args.steps, args.warmup, before=timer.start)
+        gemm_ms, gemm_flops = timer.stop()
+        launches = timer.launches
+        ms_e2e, h2d, d2h = e2e_steps(job, stack.forward, (M, H), args.steps)
+    flops_step = blocks * sum(2.0 * M * K * N for _, K, N in CFG4_LAYERS)
+    line = {"metric": METRIC, "value": round(M / (ms / 1e3), 1), "unit": "tokens/s", "n_gpus": job.world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded random packed weights, N(0,1) activations)",
+            "config": {"workload": "cfg4: video-DiT int4 stack, 12 blocks x (qkv 4096->12288, out 4096->4096, "
+                                   "fc1 4096->16384, fc2 16384->4096), GPTQ v1 gs32, M=32768 tokens",
+                       "tokens": M, "blocks": blocks, "global_batch_tokens": M,
+                       "parallelism": f"tp{job.world} (column qkv/fc1, row out/fc2 + NCCL all-reduce)"
+                       if job.world > 1 else "tp1 (one GPU, no collective)",
+                       "l2_flush": "none needed: weights (1.4 GB packed) and activations exceed the 126 MB L2"},
+            "e2e": {"value": round(M * args.steps / (ms_e2e / 1e3), 1), "unit": "tokens/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "note": "every rank copies the step's input in and its output back"},
+            "gpu_launches": launches,
+            "roofline": roofline_tensor(gemm_ms, gemm_flops, peaks, clk, TC_TRAFFIC_CFG4,
+                                        "gptq_gemm_tc_kernel (tcgen05, A = dequantized weights in TMEM)",
+                                        ms * args.steps, args.steps),
+            "tflops_step": round(flops_step / (ms / 1e3) / 1e12, 1),
+            "clocks": clk}
+    del stack
+    torch.cuda.empty_cache()
+    if job.world > 1:
+        ar_ms = allreduce_alone(job, M, H, 2 * blocks, 4)
+        nbytes = 2 * blocks * M * H * 2
+        line["comm"] = {"allreduce_ms_per_step_alone": round(ar_ms, 3), "allreduce_bytes_per_step": nbytes,
+                        "busbw_GBs": round(nbytes * 2 * (job.world - 1) / job.world / (ar_ms / 1e3) / 1e9, 1),
+                        "alone_over_step": round(ar_ms / ms, 4),
+                        "note": "the step overlaps each chunk's reduction with the next chunk's GEMM"}
+    if with_cpu:
+        line["cpu_baseline"] = cpu_baseline_cfg4(args)
+    return line
+
+
+# ----------------------------------------------------------------------------- cfg1: FLUX-style stack
+class DiTStack:
+    """8 FLUX-style blocks of FusedInt4Linear layers (random packed weights), one per GPU."""
+
+    def __init__(self, job: Job, blocks: int, timer: LaunchTimer):
+        from onecomp_runtime.layers import FusedInt4Linear
+        from onecomp_runtime.testing import CFG1, CFG1_LAYERS, gptq_layer
+        gs = CFG1["gs"]
+        self.blocks = []
+        for b in range(blocks):
+            blk = {}
+            for li, (name, K, N) in enumerate(CFG1_LAYERS):
+                t = gptq_layer(K, N, gs, seed=(1000 + 17 * job.rank) * (b + 1) + li, device=job.dev)
+                blk[name] = FusedInt4Linear(K, N, t["qweight"], t["scales"], t["qzeros"], t["bias"], gs)
+                timer.wrap_gptq(blk[name])
+            self.blocks.append(blk)
+        self.hidden = CFG1["hidden"]
+
+    def forward(self, h: torch.Tensor) -> torch.Tensor:
+        """q = qkv(h)[:, :H]; h = rms(h + proj(q)); h = rms(h + fc2(gelu(fc1(h)))), adds/GELU in epilogues."""
+        H = self.hidden
+        for blk in self.blocks:
+            qkv = blk["qkv"](h)
+            h = rms_norm(blk["proj"].forward_fused(qkv[:, :H], residual=h))
+            f = blk["fc1"].forward_fused(h, activation="gelu_tanh")
+            h = rms_norm(blk["fc2"].forward_fused(f, residual=h))
+        return h
+
+
+def bench_cfg1(args, job: Job, peaks: dict, full_line: bool) -> dict:
+    from onecomp_runtime.testing import CFG1
+    M, blocks = CFG1["M"], (args.blocks or CFG1["blocks"])
+    if args.tc_tile:
+        from onecomp_runtime import _lib
+        _lib.set_option(_lib.OPT_TC_TILE, args.tc_tile)
+    timer = LaunchTimer()
+    stack = DiTStack(job, blocks, timer)
+    x = torch.randn(M, CFG1["hidden"], generator=torch.Generator(device=job.dev).manual_seed(1234 + job.rank),
+                    device=job.dev).to(torch.bfloat16)
+    steps = args.steps if full_line else max(args.steps, 10)
+    with torch.no_grad():
+        ms, clk = timed_steps(job, lambda: stack.forward(x), steps, args.warmup, before=timer.start)
+        gemm_ms, gemm_flops = timer.stop()
+        launches = timer.launches
+        e2e = None
+        if full_line:
+            ms_e2e, h2d, d2h = e2e_steps(job, stack.forward, (M, CFG1["hidden"]), steps)
+            e2e = {"value": round(job.world * M * steps / (ms_e2e / 1e3), 1), "unit": "tokens/s",
+                   "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+    out = {"metric": METRIC_CFG1, "value": round(job.world * M / (ms / 1e3), 1), "unit": "tokens/s",
+           "n_gpus": job.world, "steps": steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+           "data": "synthetic (seeded random packed weights, N(0,1) activations)",
+           "config": {"workload": "cfg1: FLUX-style DiT int4 stack, 8 blocks x (qkv 3072->9216, proj 3072->3072, "
+                                  "fc1 3072->9216, fc2 9216->3072), GPTQ v1 gs32, M=4608 tokens per GPU",
+                      "global_batch_tokens": M * job.world, "tokens_per_gpu": M, "blocks": blocks,
+                      "parallelism": f"replicas x{job.world} (weak scaling, no collective)",
+                      "l2_flush": "none needed: weights 437 MB packed per stack > 126 MB L2"},
+           "gpu_launches": launches,
+           "roofline": roofline_tensor(gemm_ms, gemm_flops, peaks, clk, TC_TRAFFIC_CFG1 if not args.blocks else None,
+                                       "gptq_gemm_tc_kernel (tcgen05, 384-token tiles = 2 x 192)", ms * steps, steps),
+           "clocks": clk}
+    if e2e:
+        out["e2e"] = e2e
+    del stack
+    torch.cuda.empty_cache()
+    return out
+
+
+# ----------------------------------------------------------------------------- cfg2: decode layer set
+def bench_cfg2(args, job: Job, peaks: dict) -> dict:
+    """gptq_v2 gs128 act-order layer set (fp16 scales, bf16 activations), M in {1, 4, 16},
+    replayed as one CUDA graph of the five layers; every rank runs its own copy (replicas). ``--wbits 8``:
+    the same shapes as 8-bit gs128 layers without act-order, bf16 scales (the Qwen3.6 adapter's 8-bit layers).
+    Reported: packed bytes streamed per second (qweight + scales + qzeros + g_idx, + activations)."""
     from onecomp_runtime import _lib
     from onecomp_runtime.layers import PackedGPTQLinear
     from onecomp_runtime.testing import CFG2_LAYERS, gptq_layer
-    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
-    torch.cuda.set_device(dev)
-    _lib.require_b200(dev)
     if args.gemv_ctas:
         _lib.set_option(_lib.OPT_GEMV_CTAS, args.gemv_ctas)
+    dev = job.dev
     layers, nbytes = [], 0
     w8 = args.wbits == 8
     for i, (name, K, N) in enumerate(CFG2_LAYERS):
         G = (K + 127) // 128
-        if w8:  # the 8-bit layers of a {4,8}-bit GPTQ checkpoint: v1 zeros, gs128, no act-order
+        if w8:
             t = gptq_layer(K, N, 128, seed=2000 + i, v1=True, scales_range=(0.001, 0.01),
                            scales_dtype=torch.bfloat16, bias=False, device=dev, wbits=8)
             layers.append(PackedGPTQLinear(K, N, t["qweight"], t["scales"], t["qzeros"], t["g_idx"], None, 128, 8,
@@ -266,95 +572,58 @@ def bench_decode(args):
             nbytes += K * N + 2 * G * N + G * N
         else:
             t = gptq_layer(K, N, 128, seed=2000 + i, v1=False, actorder=True, scales_range=(0.001, 0.01),
-                           scales_dtype=torch.float16, bias=False, device=dev)  # config 2: fp16 scales
+                           scales_dtype=torch.float16, bias=False, device=dev)
             layers.append(PackedGPTQLinear(K, N, t["qweight"], t["scales"], t["qzeros"], t["g_idx"], None, 128, 4,
                                            False))
             nbytes += K * N // 2 + 2 * G * N + G * N // 2 + 4 * K
-    peaks = load_peaks()
     per_m = {}
+    clk = None
     for M in (1, 4, 16):
         xs = [torch.randn(M, K, device=dev).to(torch.bfloat16) for _, K, _ in CFG2_LAYERS]
         act = sum(2 * M * K + 2 * M * N for _, K, N in CFG2_LAYERS)
         for _ in range(3):
-            [l(x) for l, x in zip(layers, xs)]
-        torch.cuda.synchronize()
+            [lay(x) for lay, x in zip(layers, xs)]
+        torch.cuda.synchronize(dev)
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
-            outs = [l(x) for l, x in zip(layers, xs)]
-        for _ in range(args.warmup):
-            g.replay()
-        # time each replay (the set is ~30 us; 200 replays stream 35 GB of weights > L2)
-        reps = max(args.steps, 1) * 20
-        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        torch.cuda.synchronize()
-        s0.record()
-        for _ in range(reps):
-            g.replay()
-        s1.record()
-        torch.cuda.synchronize()
-        us = s0.elapsed_time(s1) * 1e3 / reps
-        per_m[M] = {"us_per_set": round(us, 2), "GB_s": round((nbytes + act) / (us * 1e-6) / 1e9, 1),
-                    "frac_hbm": round((nbytes + act) / (us * 1e-6) / 1e9 / peaks["hbm_gbs"], 4)}
+            outs = [lay(x) for lay, x in zip(layers, xs)]
+        reps = max(args.steps, 1) * 20   # the set is ~30-150 us; 200+ replays stream 35 GB > L2
+        ms, c = timed_steps(job, g.replay, reps, args.warmup, clocks=(M == 16))
+        clk = c or clk
+        us = ms * 1e3
+        gbs = (nbytes + act) / (us * 1e-6) / 1e9
+        per_m[str(M)] = {"us_per_set": round(us, 2), "GB_s": round(gbs, 1), "frac_hbm": round(gbs / peaks["hbm_gbs"], 4)}
         del g, outs
-    top = per_m[16]
+    top = per_m["1"]
     kind = "gptq v1 gs128 8-bit" if w8 else "gptq_v2 gs128 act-order"
-    line = {"metric": f"decode GB/s ({kind} layer set, M=16)", "value": top["GB_s"], "unit": "GB/s",
-            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "cfg2: q/k/v 5120->8192, o 6144->5120, gate/up 5120->17408, down 17408->5120"
-                                   + (", 8-bit codes" if w8 else ""),
-                       "packed_bytes_per_set": nbytes, "graph": "CUDA graph of the 5 layers, replayed"},
-            "per_m": per_m,
-            "roofline": {"bound": "hbm", "achieved": top["GB_s"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                         "frac": top["frac_hbm"], "traffic": None if w8 else GEMV_TRAFFIC_BYTES_PER_LAUNCH,
-                         "traffic_unit": "bytes per launch (q/k/v layer)",
-                         "peak_source": f"{peaks['source']} hbm_gbs"}}
-    print(json.dumps(line), flush=True)
+    out = {"metric": f"decode GB/s ({kind} layer set, M=1)", "value": top["GB_s"], "unit": "GB/s",
+           "n_gpus": job.world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+           "config": {"workload": "cfg2: q/k/v 5120->8192, o 6144->5120, gate/up 5120->17408, down 17408->5120"
+                                  + (", 8-bit codes" if w8 else ", fp16 scales"),
+                      "packed_bytes_per_set": nbytes, "graph": "CUDA graph of the 5 layers, replayed",
+                      "parallelism": f"replicas x{job.world} (per-GPU figures, max time over ranks)",
+                      "l2_flush": "none needed: each replay streams 177 MB of weights > 126 MB L2"},
+           "per_m": per_m,
+           "roofline": {"bound": "hbm", "achieved": top["GB_s"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                        "frac": top["frac_hbm"], "traffic": None if w8 else GEMV_TRAFFIC_BYTES_PER_LAUNCH,
+                        "traffic_unit": "bytes per launch (q/k/v layer)",
+                        "kernel": "gptq_gemv_tma_kernel (split-K decode GEMV)",
+                        "peak_source": f"{peaks['source']} hbm_gbs"},
+           "clocks": clk}
+    del layers
+    torch.cuda.empty_cache()
+    return out
 
 
-# ----------------------------------------------------------------------------- MoE (cfg3)
-def _dist_init(dev):
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    if world > 1 and not torch.distributed.is_initialized():
-        import datetime
-        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    return world, int(os.environ.get("RANK", "0"))
-
-
-def _timed(fn, steps, warmup, dev, world):
-    for _ in range(warmup):
-        fn()
-    torch.cuda.synchronize(dev)
-    if world > 1:
-        torch.distributed.barrier()
-    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s0.record()
-    for _ in range(steps):
-        fn()
-    s1.record()
-    torch.cuda.synchronize(dev)
-    if world > 1:
-        torch.distributed.barrier()
-    ms = torch.tensor([s0.elapsed_time(s1) / steps], device=dev)
-    if world > 1:
-        torch.distributed.all_reduce(ms, op=torch.distributed.ReduceOp.MAX)
-    return float(ms[0])
-
-
-def bench_moe(args):
-    """256 int2 experts (top-8) + int4 shared expert, T=2048 tokens per rank.
-
-    N ranks: experts split contiguously, each rank routes its own 2048 tokens and exchanges
-    rows with NCCL all_to_all (weak scaling). value = tokens/s over all ranks.
-    """
-    from onecomp_runtime import _lib
+# ----------------------------------------------------------------------------- cfg3: packed MoE
+def bench_cfg3(args, job: Job, peaks: dict) -> dict:
+    """256 int2 experts (top-8) + int4 shared expert, T=2048 tokens per rank. N ranks:
+    experts split contiguously, each rank routes its own tokens and exchanges rows with NCCL all_to_all
+    (weak scaling). value = tokens/s over all ranks."""
     from onecomp_runtime.moe import ExpertParallelMoE, PackedMoE
     from onecomp_runtime.testing import CFG3, dsv4_packed
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
-    world, rank = _dist_init(dev)
-    _lib.require_b200(dev)
+    dev, world, rank = job.dev, job.world, job.rank
     E, k, H, F, T = CFG3["E"], CFG3["k"], CFG3["H"], CFG3["F"], CFG3["T"]
     E = args.moe_experts or E  # profiling only: a smaller case with the same rows per expert
     T = args.moe_tokens or T
@@ -370,283 +639,122 @@ def bench_moe(args):
     g = torch.Generator(device=dev).manual_seed(77 + rank)
     x = torch.randn((T, H), generator=g, device=dev).to(torch.bfloat16)
     logits = torch.randn((T, E), generator=g, device=dev)
+    timer = LaunchTimer()
+    moe = PackedMoE(experts, shared, k=k, device=dev)
+    for h in list(moe._h.values()) + list((moe._shared or {}).values()):
+        timer.wrap_rows(h)
     if world == 1:
-        moe = PackedMoE(experts, shared, k=k, device=dev)
         fn = lambda: moe(x, logits)  # noqa: E731
     else:
-        loc = PackedMoE(experts, shared, k=k, device=dev)
-        ep = ExpertParallelMoE(E, k, loc.expert_ffn, route=loc.route,
-                               shared=loc.shared_ffn, combine=loc.combine)
+        ep = ExpertParallelMoE(E, k, moe.expert_ffn, route=moe.route, shared=moe.shared_ffn, combine=moe.combine)
         fn = lambda: ep(x, logits)  # noqa: E731
     with torch.no_grad():
-        ms = _timed(fn, args.steps, args.warmup, dev, world)
+        ms, clk = timed_steps(job, fn, args.steps, args.warmup, before=timer.start)
+        gemm_ms, gemm_flops = timer.stop()
     flops = 2 * T * k * 3 * H * F + 2 * T * 3 * H * F
-    line = {"metric": "packed-MoE layer tokens/s (256 int2 experts top-8 + int4 shared)",
-            "value": round(world * T / (ms / 1e3), 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "cfg3", "tokens_per_gpu": T, "experts_per_gpu": el,
-                       "parallelism": f"expert parallel x{world} (NCCL all_to_all)" if world > 1 else "1 GPU"},
-            "tflops_per_gpu": round(flops / (ms / 1e3) / 1e12, 1)}
-    if world > 1:
-        torch.distributed.destroy_process_group()
-    if rank == 0:
-        print(json.dumps(line), flush=True)
+    # packed bytes a rank must read once per layer: its experts' int2 codes + fp16 scales and zeros, the
+    # shared expert's int4 codes + scales/zeros, activations in and out
+    G_e = (H + gs - 1) // gs
+    exp_bytes = el * (2 * F * H * wb // 8 + H * F * wb // 8 + 2 * (2 * F * G_e + 2 * H * ((F + gs - 1) // gs)) * 2)
+    sh_bytes = 3 * F * H * sw // 8 + 2 * 2 * (2 * F * ((H + sgs - 1) // sgs) + H * ((F + sgs - 1) // sgs))
+    act_bytes = 2 * T * H * 2
+    nbytes = exp_bytes + sh_bytes + act_bytes
+    gbs = nbytes / (ms / 1e3) / 1e9
+    rt = roofline_tensor(gemm_ms, gemm_flops, peaks, clk, None,
+                         "rows_gemm_tc_kernel (tcgen05, grouped over experts, int2 table decode)", ms * args.steps,
+                         args.steps)
+    rt["layer_tflops"] = round(flops / (ms / 1e3) / 1e12, 1)
+    rt["layer_frac_tensor"] = round(rt["layer_tflops"] / rt["peak"], 4)
+    rt["hbm"] = {"achieved_GBs": round(gbs, 1), "peak": peaks["hbm_gbs"], "frac": round(gbs / peaks["hbm_gbs"], 4),
+                 "bytes_per_layer": nbytes}
+    out = {"metric": "packed-MoE layer tokens/s (256 int2 experts top-8 + int4 shared)",
+           "value": round(world * T / (ms / 1e3), 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+           "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+           "config": {"workload": "cfg3", "tokens_per_gpu": T, "experts_per_gpu": el,
+                      "parallelism": f"expert parallel x{world} (NCCL all_to_all)" if world > 1 else "1 GPU",
+                      "l2_flush": "none needed: 2 GB of packed experts per layer > 126 MB L2"},
+           "roofline": rt, "clocks": clk}
+    del moe, experts, shared
+    torch.cuda.empty_cache()
+    return out
 
 
-# ----------------------------------------------------------------------------- TP stack (cfg4)
-def bench_tp(args):
-    """12 video-DiT blocks (hidden 4096), M=32768 tokens, column/row tensor parallel.
-
-    Strong scaling: the same 32768 tokens on every N; row-parallel outputs are summed with a
-    chunked NCCL all-reduce that overlaps the next chunk's GEMM.
-    """
-    from onecomp_runtime import _lib
-    from onecomp_runtime.layers import FusedInt4Linear
-    from onecomp_runtime.tensor_parallel import build_tp_block
-    from onecomp_runtime.testing import CFG4, CFG4_LAYERS, gptq_layer
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
-    world, rank = _dist_init(dev)
-    _lib.require_b200(dev)
-    blocks = args.blocks or CFG4["blocks"]
-    M, gs, H = CFG4["M"], CFG4["gs"], CFG4["hidden"]
-
-    def make(t, K, N):
-        return FusedInt4Linear(K, N, t["qweight"], t["scales"], t["qzeros"], t.get("bias"), gs)
-
-    stack = []
-    for b in range(blocks):
-        tens = {name: gptq_layer(K, N, gs, seed=4000 + 10 * b + i, device=dev)
-                for i, (name, K, N) in enumerate(CFG4_LAYERS)}
-        stack.append(build_tp_block(tens, CFG4_LAYERS, rank, world, gs, make))
-        del tens
-    g = torch.Generator(device=dev).manual_seed(5)
-    x = torch.randn((M, H), generator=g, device=dev).to(torch.bfloat16)
-    hq = H // world
-
-    def step():
-        h = x
-        for blk in stack:
-            qkv = blk["qkv"](h)
-            h = rms_norm(h + blk["out"](qkv[:, :hq]))
-            f = torch.nn.functional.gelu(blk["fc1"](h), approximate="tanh")
-            h = rms_norm(h + blk["fc2"](f))
-        return h
-
-    with torch.no_grad():
-        ms = _timed(step, args.steps, args.warmup, dev, world)
-    flops = blocks * sum(2 * M * K * N for _, K, N in CFG4_LAYERS)
-    line = {"metric": "TP video-DiT stack tokens/s (12 blocks, hidden 4096, int4 GPTQ gs32)",
-            "value": round(M / (ms / 1e3), 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "cfg4", "tokens": M, "blocks": blocks,
-                       "parallelism": f"tensor parallel x{world} (column/row, NCCL all-reduce)"},
-            "tflops_total": round(flops / (ms / 1e3) / 1e12, 1)}
-    if world > 1:
-        torch.distributed.destroy_process_group()
-    if rank == 0:
-        print(json.dumps(line), flush=True)
+# ----------------------------------------------------------------------------- reference arm
+def reference_arm(args, job: Job):
+    """The reference's CPU eager path (oracle port) on the host cores, rank 0 only."""
+    if job.rank != 0:
+        return
+    if args.workload == "cfg1":
+        from onecomp_runtime.testing import CFG1, CFG1_LAYERS
+        m, blocks, layers, gs, tokens, seed = args.cpu_sample_m, CFG1["blocks"], CFG1_LAYERS, CFG1["gs"], CFG1["M"], 1000
+        metric, cfg = METRIC_CFG1, {"workload": "cfg1", "tokens_per_gpu": tokens, "blocks": blocks}
+    else:
+        from onecomp_runtime.testing import CFG4, CFG4_LAYERS
+        m, blocks, layers, gs, tokens, seed = args.cpu_sample_m, CFG4["blocks"], CFG4_LAYERS, CFG4["gs"], CFG4["M"], 4000
+        metric, cfg = METRIC, {"workload": "cfg4: video-DiT int4 stack, 12 blocks, hidden 4096, GPTQ v1 gs32, "
+                                           "M=32768 tokens", "tokens": tokens, "blocks": blocks}
+    run, cores = cpu_eager_block(layers, gs, m, seed)
+    per_block = time_cpu(run, args.warmup, args.steps)
+    tps = m / (per_block * blocks)
+    sample = (f"one block (4 linears + glue) at M={m} tokens per step, torch CPU bf16 F.linear on weights "
+              f"dequantized once by the oracle's formula; value = M / (block time x {blocks} blocks); "
+              f"ms_per_step is the measured block time")
+    line = {"metric": metric, "impl": "reference", "value": round(tps, 1), "unit": "tokens/s",
+            "n_gpus": job.world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(per_block * 1e3, 3), "higher_is_better": True,
+            "scaling": "strong" if args.workload != "cfg1" else "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic", "config": cfg,
+            "cpu_baseline": {"value": round(tps, 1), "unit": "tokens/s", "cores": cores, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(tps, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
 
 
 # ----------------------------------------------------------------------------- main
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--workload", default="cfg1", choices=["cfg1", "cfg2", "cfg3", "cfg4"],
-                    help="cfg1: DiT stack (default, headline); cfg2: decode GEMV layer set; "
-                         "cfg3: packed MoE layer (expert parallel); cfg4: tensor-parallel video-DiT stack")
+    ap.add_argument("--workload", default="cfg4", choices=["cfg1", "cfg2", "cfg3", "cfg4"],
+                    help="cfg4: tensor-parallel video-DiT stack (default, headline); cfg1: FLUX-style stack; "
+                         "cfg2: decode GEMV layer set; cfg3: packed MoE layer (expert parallel)")
+    ap.add_argument("--no-nested", action="store_true", help="cfg4 line only (skip the cfg1/cfg2/cfg3 blocks)")
     ap.add_argument("--tc-tile", type=int, default=0, help="tokens per tcgen05 tile (0 = library default)")
     ap.add_argument("--gemv-ctas", type=int, default=0, help="GEMV split-K target CTAs per SM (0 = default)")
     ap.add_argument("--wbits", type=int, default=4, choices=[4, 8], help="cfg2 only: code width of the layer set")
     ap.add_argument("--blocks", type=int, default=0, help="override the number of DiT blocks (profiling only)")
     ap.add_argument("--moe-experts", type=int, default=0, help="cfg3: override the expert count (profiling only)")
     ap.add_argument("--moe-tokens", type=int, default=0, help="cfg3: override tokens per GPU (profiling only)")
-    ap.add_argument("--cpu-sample-m", type=int, default=1152,
-                    help="tokens of the bounded CPU-baseline sample (one block)")
+    ap.add_argument("--cpu-sample-m", type=int, default=512, help="tokens of the bounded CPU sample (one block)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-
-    if args.workload == "cfg2":
-        return bench_decode(args)
-    if args.workload == "cfg3":
-        return bench_moe(args)
-    if args.workload == "cfg4":
-        return bench_tp(args)
-    from onecomp_runtime.testing import CFG1, CFG1_LAYERS
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    M, blocks, gs = CFG1["M"], (args.blocks or CFG1["blocks"]), CFG1["gs"]
-    config = {"workload": "cfg1: FLUX-style DiT int4 stack, 8 blocks x (qkv 3072->9216, proj 3072->3072, "
-                          "fc1 3072->9216, fc2 9216->3072), GPTQ v1 gs32, M=4608 tokens per GPU",
-              "global_batch_tokens": M * world, "tokens_per_gpu": M, "blocks": blocks,
-              "l2_flush": "none needed: inputs larger than L2",
-              "parallelism": f"replicas x{world} (weak scaling, no collective)",
-              "l2": "weights 437 MB packed per stack > 126 MB L2 (streamed every step)"}
-
+    job = Job()
     if args.impl == "reference":
-        if rank != 0:
-            return
-        sample_m = args.cpu_sample_m
-        run, cores = cpu_eager_block(CFG1_LAYERS, gs, sample_m)
-        per_block = time_cpu(run, args.warmup, args.steps)
-        tps = sample_m / (per_block * blocks)
-        sample = (f"one block (4 linears + glue) at M={sample_m} tokens per step, torch CPU bf16 F.linear on "
-                  "weights dequantized once by the oracle, extrapolated x8 blocks")
-        line = {"metric": METRIC, "impl": "reference", "value": round(tps, 1), "unit": "tokens/s",
-                "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-                "ms_per_step": round(1e3 * M / tps, 3), "higher_is_better": True, "scaling": "weak",
-                "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": config,
-                "cpu_baseline": {"value": round(tps, 1), "unit": "tokens/s", "cores": cores, "kind": "port",
-                                 "sample": sample},
-                "e2e": {"value": round(tps, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0,
-                        "d2h_bytes_per_step": 0}}
-        print(json.dumps(line), flush=True)
-        return
-
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        import datetime
-        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                             device_id=dev)
-    from onecomp_runtime import _lib
-    _lib.require_b200(dev)
-    if args.tc_tile:
-        _lib.set_option(_lib.OPT_TC_TILE, args.tc_tile)
-        config["tc_tile"] = args.tc_tile
-    torch.manual_seed(1234 + rank)
-    stack = DiTStack(dev, blocks, CFG1_LAYERS, gs, seed=1000 + 17 * rank)
-    x = torch.randn(M, CFG1["hidden"], device=dev).to(torch.bfloat16)
-
-    def barrier():
-        if world > 1:
-            torch.distributed.barrier()
-        torch.cuda.synchronize(dev)
-
-    with torch.no_grad():
-        for _ in range(args.warmup):
-            y = stack.forward(x)
-        torch.cuda.synchronize(dev)
-        if not torch.isfinite(y).all():
-            raise RuntimeError("non-finite stack output")
-
-        # ---- device-timed steps (inputs resident in HBM)
-        clocks = ClockSampler(local)
-        barrier()
-        clocks.start()
-        stack.gemm_events = []
-        t_start = torch.cuda.Event(enable_timing=True)
-        t_end = torch.cuda.Event(enable_timing=True)
-        t_start.record()
-        for _ in range(args.steps):
-            y = stack.forward(x)
-        t_end.record()
-        barrier()
-        clk = clocks.stop()
-        ms_total = t_start.elapsed_time(t_end)
-        gemm = [(s.elapsed_time(e), fl) for s, e, fl in stack.gemm_events]
-        stack.gemm_events = None
-
-        # ---- end-to-end through the module API with host buffers: every step copies its input
-        # from pinned host memory and reads its result back; the copies of step i+1 / i-1 run on
-        # their own streams while step i computes (double-buffered device and host tensors)
-        shape = (M, CFG1["hidden"])
-        x_host = [torch.empty(shape, dtype=torch.bfloat16, pin_memory=True) for _ in range(2)]
-        y_host = [torch.empty(shape, dtype=torch.bfloat16, pin_memory=True) for _ in range(2)]
-        for b in range(2):
-            x_host[b].copy_(x.cpu())
-        x_dev = [torch.empty(shape, dtype=torch.bfloat16, device=dev) for _ in range(2)]
-        main = torch.cuda.current_stream(dev)
-        s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-        in_ready = [torch.cuda.Event() for _ in range(2)]
-        in_free = [torch.cuda.Event() for _ in range(2)]
-        out_ready = [torch.cuda.Event() for _ in range(2)]
-
-        def e2e_steps(n):
-            for i in range(n):
-                b = i & 1
-                with torch.cuda.stream(s_in):
-                    if i >= 2:
-                        s_in.wait_event(in_free[b])
-                    x_dev[b].copy_(x_host[b], non_blocking=True)
-                    in_ready[b].record(s_in)
-                main.wait_event(in_ready[b])
-                y = stack.forward(x_dev[b])
-                in_free[b].record(main)
-                out_ready[b].record(main)
-                with torch.cuda.stream(s_out):
-                    s_out.wait_event(out_ready[b])
-                    y_host[b].copy_(y, non_blocking=True)
-                    y.record_stream(s_out)
-            main.wait_stream(s_in)
-            main.wait_stream(s_out)
-
-        e2e_steps(2)
-        barrier()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record(main)
-        e2e_steps(args.steps)
-        e1.record(main)
-        barrier()
-        ms_e2e = e0.elapsed_time(e1)
-        if not torch.equal(y_host[(args.steps - 1) & 1], y.cpu()):
-            raise RuntimeError("end-to-end output differs from the device-timed output")
-
-    t = torch.tensor([ms_total, ms_e2e], device=dev)
-    if world > 1:
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    ms_total, ms_e2e = float(t[0]), float(t[1])
-    ms_step = ms_total / args.steps
-    value = world * M * args.steps / (ms_total / 1e3)
-    e2e_value = world * M * args.steps / (ms_e2e / 1e3)
-
+        return reference_arm(args, job)
+    job.init_gpu()
     peaks = load_peaks()
-    gemm_ms = sum(g[0] for g in gemm)
-    gemm_flops = sum(g[1] for g in gemm)
-    achieved = gemm_flops / (gemm_ms / 1e3) / 1e12
-    peak = peaks["bf16_sustained"]
-    roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
-                "frac": round(achieved / peak, 4),
-                # DRAM read + write bytes per launch, mean over one block's four GEMM launches, from
-                # one ncu capture of this workload (profiles/gptq_gemm_tc_cfg1.txt)
-                "traffic": TC_TRAFFIC_BYTES_PER_LAUNCH if args.blocks == 0 else None,
-                "traffic_unit": "bytes per launch",
-                "kernel": "gptq_gemm_tc_kernel (tcgen05, 384-token tiles = 2 x 192 chosen by the library at M=4608)",
-                "peak_source": f"{peaks['source']} bf16_tflops_sustained",
-                "gemm_share_of_step": round(gemm_ms / ms_total, 4),
-                "gemm_ms_per_step": round(gemm_ms / args.steps, 3)}
-
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        run, cores = cpu_eager_block(CFG1_LAYERS, gs, args.cpu_sample_m)
-        per_block = time_cpu(run, 1, 3)
-        cpu = {"value": round(args.cpu_sample_m / (per_block * blocks), 1), "unit": "tokens/s", "cores": cores,
-               "kind": "port",
-               "sample": f"one block (4 linears + glue) at M={args.cpu_sample_m} tokens, torch CPU bf16 "
-                         "F.linear on oracle-dequantized weights, extrapolated x8 blocks"}
-
-    if world > 1:
-        torch.distributed.destroy_process_group()
-    if rank != 0:
-        return
-    line = {"metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (seeded random packed weights, N(0,1) activations)", "config": config,
-            "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": M * CFG1["hidden"] * 2,
-                    "d2h_bytes_per_step": M * CFG1["hidden"] * 2},
-            "gpu_launches": stack.gemm_count_per_step() * args.steps,
-            "roofline": roofline, "cpu_baseline": cpu, "clocks": clk}
-    print(json.dumps(line), flush=True)
+    with_cpu = job.rank == 0 and job.world == 1 and not args.no_cpu_baseline
+    try:
+        if args.workload == "cfg4":
+            line = bench_cfg4(args, job, peaks, with_cpu)
+            if not args.no_nested:
+                line["workloads"] = {"cfg1": bench_cfg1(args, job, peaks, full_line=False),
+                                     "cfg2": bench_cfg2(args, job, peaks),
+                                     "cfg3": bench_cfg3(args, job, peaks)}
+        elif args.workload == "cfg1":
+            line = bench_cfg1(args, job, peaks, full_line=True)
+        elif args.workload == "cfg2":
+            line = bench_cfg2(args, job, peaks)
+        else:
+            line = bench_cfg3(args, job, peaks)
+    finally:
+        job.close()
+    if job.rank == 0:
+        print(json.dumps(line), flush=True)
 
 
 if __name__ == "__main__":

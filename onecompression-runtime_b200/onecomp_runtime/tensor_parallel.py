@@ -8,10 +8,16 @@ star asks for on the video-DiT stack:
 * row-parallel (``shard_gptq_rows``): split K. qweight rows (K/world must be a
   multiple of the groupsize and of 8), scales/qzeros rows; the bias is added by
   rank 0 only so the all-reduce sums it once;
-* ``RowParallelInt4Linear.forward`` runs the local GEMM in M-chunks and issues
-  an asynchronous all-reduce (sum, bf16) per chunk, so the reduction of chunk i
+* ``RowParallelInt4Linear.forward`` runs the local GEMM in M-chunks, each
+  chunk's GEMM writing straight into its rows of the output, and issues an
+  asynchronous all-reduce (sum, bf16) per chunk, so the reduction of chunk i
   overlaps the GEMM of chunk i+1; the current stream waits on every chunk's
-  reduction before returning.
+  reduction before returning. A residual (the DiT block's skip connection) is
+  added in rank 0's GEMM epilogue before the reduction, so the sum carries it
+  once and no separate elementwise pass runs;
+* ``ColumnParallelInt4Linear.forward(x, activation=...)`` applies an elementwise
+  activation (tanh-GELU) in the GEMM epilogue: the shard's outputs are whole
+  features, so the activation needs no communication.
 
 Sharding helpers are plain tensor slicing and run on any device; the linears
 themselves are the B200 modules (``FusedInt4Linear`` / ``FusedInt4LinearAnyGroup``).
@@ -79,8 +85,10 @@ class ColumnParallelInt4Linear(torch.nn.Module):
         super().__init__()
         self.local = local
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
-        return self.local(x)
+    def forward(self, x: torch.Tensor, activation: str | None = None) -> torch.Tensor:
+        if activation is None:
+            return self.local(x)
+        return self.local.forward_fused(x, activation=activation)
 
 
 class RowParallelInt4Linear(torch.nn.Module):
@@ -95,17 +103,29 @@ class RowParallelInt4Linear(torch.nn.Module):
         self.group = group
         self.chunks = max(1, int(chunks))
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
+        """``all_reduce(x_shard @ W_shard.T) + bias + residual``; ``residual`` [M, N] (optional)."""
         M = x.shape[0]
         world = dist.get_world_size(self.group) if dist.is_initialized() else 1
         if world == 1:
-            return self.local(x)
+            if residual is None:
+                return self.local(x)
+            return self.local.forward_fused(x, residual=residual)
+        rank = dist.get_rank(self.group)
+        fused = hasattr(self.local, "_gemm_2d") and x.dtype in (torch.float16, torch.bfloat16)
         out = torch.empty((M, self.local.out_features), dtype=x.dtype, device=x.device)
         step = (M + self.chunks - 1) // self.chunks
         works = []
         for c0 in range(0, M, step):
             c1 = min(M, c0 + step)
-            out[c0:c1] = self.local(x[c0:c1])
+            res = residual[c0:c1] if (residual is not None and rank == 0) else None
+            if fused:
+                xc = x[c0:c1]
+                if xc.stride(1) != 1 or xc.data_ptr() % 16 or xc.stride(0) % 8:
+                    xc = xc.contiguous()
+                self.local._gemm_2d(xc, out[c0:c1], res)   # written in place, residual in the epilogue
+            else:
+                out[c0:c1] = self.local(x[c0:c1]) if res is None else self.local(x[c0:c1]) + res
             works.append(dist.all_reduce(out[c0:c1], op=dist.ReduceOp.SUM, group=self.group, async_op=True))
         for w in works:
             w.wait()

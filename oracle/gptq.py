@@ -9,6 +9,8 @@ Restates ``onecomp_runtime/quant_utils.py`` (reference):
   product ``s * (q - z)`` rounded ONCE to the output dtype
 * ``pack_rows``         -- ``_pack_int4_weights`` (layers/fused_int4_linear.py:76-91),
   generalised to any ``wbits`` dividing 32
+* ``dequant_gptq_torch``-- the same formula on torch CPU tensors (multi-threaded), for
+  preparing the CPU baseline's large weights; checked equal to ``dequant_gptq`` by the tests
 """
 from __future__ import annotations
 
@@ -89,3 +91,23 @@ def pack_int_weights(w_int: np.ndarray, wbits: int = 4) -> np.ndarray:
 def pack_zeros(zeros: np.ndarray, wbits: int = 4) -> np.ndarray:
     """int [G, N] -> qzeros int32 [G, N/pf] packed along N."""
     return np.ascontiguousarray(pack_rows(np.ascontiguousarray(np.asarray(zeros).T), wbits).T)
+
+
+def dequant_gptq_torch(qweight, scales, qzeros, g_idx, in_features, out_features, out_dtype, v1=True, wbits=4):
+    """``dequant_gptq`` on torch CPU tensors: int32 qweight [K/pf, N], scales [G, N] (any float
+    dtype), int32 qzeros [G, N/pf], g_idx [K] -> [N, K] in ``out_dtype`` (a torch dtype).
+    Same fp32 product s * (q - z) and one round-to-nearest-even conversion (quant_utils.py:50-69)."""
+    import torch
+
+    pf = 32 // wbits
+    mask = (1 << wbits) - 1
+    shifts = torch.arange(0, 32, wbits, dtype=torch.int64)
+    qw = qweight.to(torch.int64) & 0xFFFFFFFF
+    q = ((qw.unsqueeze(1) >> shifts.view(1, pf, 1)) & mask).reshape(-1, qw.shape[1])[:in_features]  # [K, N]
+    qz = qzeros.to(torch.int64) & 0xFFFFFFFF
+    z = ((qz.unsqueeze(2) >> shifts.view(1, 1, pf)) & mask).reshape(qz.shape[0], -1)[:, :out_features]  # [G, N]
+    if v1:
+        z = (z + 1) & mask
+    g = g_idx.to(torch.int64)
+    prod = scales.to(torch.float32)[g] * (q.to(torch.float32) - z.to(torch.float32)[g])
+    return prod.t().contiguous().to(out_dtype)

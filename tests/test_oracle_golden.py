@@ -143,3 +143,23 @@ def test_conv_nibble_pack_roundtrip():
     packed = pack_int4_nibbles(codes)
     assert packed.shape == (5, 19) and packed.dtype == torch.uint8
     assert torch.equal(unpack_int4_nibbles(packed, 37).to(torch.int64), codes)
+
+
+@pytest.mark.parametrize("case", GPTQ_CASES)
+def test_gptq_torch_restatement_matches(case):
+    """The torch restatement used to prepare the CPU baseline's weights equals the numpy oracle."""
+    import torch
+    d = load_golden(case)
+    m = d["meta"]
+    s = d["scales"]
+    if m["scales_dtype"] == "f32":
+        st = torch.from_numpy(s.astype(np.float32))
+    else:
+        st = torch.from_numpy(s.view(np.int16).copy()).view(
+            torch.bfloat16 if m["scales_dtype"] == "bf16" else torch.float16)
+    out = gptq.dequant_gptq_torch(torch.from_numpy(d["qweight"]), st, torch.from_numpy(d["qzeros"]),
+                                  torch.from_numpy(d["g_idx"]), m["K"], m["N"], torch.bfloat16, v1=m["v1"],
+                                  wbits=m["wbits"])
+    ref = gptq.dequant_gptq(d["qweight"], d["scales"], m["scales_dtype"], d["qzeros"], d["g_idx"], m["K"], m["N"],
+                            "bf16", v1=m["v1"], wbits=m["wbits"])
+    np.testing.assert_array_equal(out.view(torch.int16).numpy().view(np.uint16), ref)

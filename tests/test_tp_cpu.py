@@ -43,6 +43,12 @@ class OracleLinear(torch.nn.Module):
         y = x.float() @ self.w.t()
         return y + self.b if self.b is not None else y
 
+    def forward_fused(self, x, residual=None, activation=None):
+        y = self.forward(x)
+        if activation == "gelu_tanh":
+            y = torch.nn.functional.gelu(y, approximate="tanh")
+        return y + residual if residual is not None else y
+
 
 LAYERS = (("qkv", 256, 768), ("out", 256, 256), ("fc1", 256, 512), ("fc2", 512, 256))
 GS = 32
@@ -60,6 +66,14 @@ def _block_forward(blk, x, hidden, local_q):
     return h + blk["fc2"](f)
 
 
+def _block_forward_fused(blk, x, local_q):
+    """The same block with the residual adds and the GELU folded into the linears' epilogues."""
+    qkv = blk["qkv"](x)
+    h = blk["out"](qkv[:, :local_q], residual=x)
+    f = blk["fc1"](h, activation="gelu_tanh")
+    return blk["fc2"](f, residual=h)
+
+
 def _worker(rank, world, port, out_path):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -69,8 +83,9 @@ def _worker(rank, world, port, out_path):
     blk = build_tp_block(tens, LAYERS, rank, world, GS, lambda t, K, N: OracleLinear(t, K, N, GS), chunks=3)
     x = torch.randn(10, 256, generator=torch.Generator().manual_seed(0))
     y = _block_forward(blk, x, 256, 256 // world)
+    y_fused = _block_forward_fused(blk, x, 256 // world)
     if rank == 0:
-        torch.save(y, out_path)
+        torch.save((y, y_fused), out_path)
     dist.barrier()
     dist.destroy_process_group()
 
@@ -79,12 +94,14 @@ def test_tp_block_matches_single_rank(tmp_path):
     world = 2
     out = tmp_path / "y.pt"
     mp.spawn(_worker, args=(world, _free_port(), str(out)), nprocs=world, join=True)
-    y_tp = torch.load(out)
+    y_tp, y_tp_fused = torch.load(out)
     tens = _tensors()
     full = {name: OracleLinear(tens[name], K, N, GS) for name, K, N in LAYERS}
     x = torch.randn(10, 256, generator=torch.Generator().manual_seed(0))
     y_ref = _block_forward(full, x, 256, 256)
     torch.testing.assert_close(y_tp, y_ref, rtol=1e-4, atol=1e-4)
+    # residual added once (rank 0's epilogue) before the reduction, GELU in the column shard
+    torch.testing.assert_close(y_tp_fused, y_ref, rtol=1e-4, atol=1e-4)
 
 
 def test_column_and_row_shards_cover_the_layer():
