@@ -188,6 +188,10 @@ size_t oc_b200_rows_table_bytes(int E);
  *                  code j of a byte at bits j*wbits (RTN: low nibble = even k)
  *   scales[e], zeros[e]  host arrays of device pointers; element (n, g) at n*stride_n + g*stride_g
  *   groupsize      k per scale group (>= K: one group per row)
+ *   Scales / zeros stored group-major (stride_n == 1, stride_g >= N, rows 16-byte aligned) are staged
+ *   by TMA with each 64-k weight block when a block's group rows fit 512 bytes per tensor (16-bit
+ *   with groups of >= 32 k, fp32 with groups of >= 64 k, or one group per row); other layouts are
+ *   read with cached global loads. Results are identical either way.
  *   mode           0: (q - z) * s in fp32, one rounding (DSV4, dsv4_packed_linear.py:52-56)
  *                  1: RTN, two roundings in the activation dtype (quant_utils.py:91-103)
  *   table          caller-allocated device memory of oc_b200_rows_table_bytes(E) bytes; the call

@@ -41,9 +41,14 @@ struct RowsParams {
   const CUtensorMap* wmaps;   // [E] TMA maps over the packed weights (device memory)
   const void* const* sptr;    // [E] scales
   const void* const* zptr;    // [E] zeros
+  const CUtensorMap* smaps;   // [E] TMA maps over scales / zeros stored [G, N] (sz_tma only)
+  const CUtensorMap* zmaps;
   int s_dtype, z_dtype;
   long long s_stride_n, s_stride_g;
   int gs;                     // k per scale group (a multiple of the k held by one 32-bit word)
+  int sz_tma;                 // scales/zeros ride in each weight stage by TMA
+  int sz_rows;                // group rows per stage (64 / gs for small groups, else 1)
+  int s_es, z_es;             // element bytes of scales / zeros
   const void* bias;
   int bias_dtype;
   uint16_t* out;
@@ -61,7 +66,10 @@ constexpr int kRowsThreads = 32 * (kRowsEpiWarp0 + 4);
 template <int WBITS, int BT, int ACC_STAGES, int X_STAGES, int W_STAGES, int A_STAGES>
 struct RowsCfg {
   static constexpr int kKbBytes = 64 * WBITS / 8;               // packed bytes of one row per 64-k block
-  static constexpr int kWStageBytes = 128 * kKbBytes;            // 2 KB (int2) / 4 KB (int4)
+  static constexpr int kWBytes = 128 * kKbBytes;                 // 2 KB (int2) / 4 KB (int4)
+  static constexpr int kSOff = kWBytes;                          // scale rows of the block (<= 512 B)
+  static constexpr int kZOff = kWBytes + 512;                    // zero rows of the block (<= 512 B)
+  static constexpr int kWStageBytes = kWBytes + 1024;
   static constexpr int kAccCols = ACC_STAGES * BT;
   static constexpr int kACols = A_STAGES * 32;
   static_assert(kAccCols + kACols <= 512, "TMEM budget");
@@ -151,6 +159,7 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
 
   const int warp = warp_id(), lane = lane_id();
   const int KB = (p.K + 63) / 64;
+  const uint32_t sz_tx = p.sz_tma ? (uint32_t)(p.sz_rows * 128 * (p.s_es + p.z_es)) : 0u;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < X_STAGES; ++i) { mbar_init(&full_x[i], 1); mbar_init(&empty_x[i], 1); }
@@ -243,8 +252,15 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
         for (int kb = 0; kb < KB; ++kb, ++it) {
           const int sw = it % W_STAGES, pw = (it / W_STAGES) & 1;
           if (!mbar_wait(&empty_w[sw], pw ^ 1, abort_flag, kDevErrWEmpty)) { ok = false; break; }
-          mbar_arrive_expect_tx(&full_w[sw], Cfg::kWStageBytes);
-          tma_load_2d(w_smem + sw * Cfg::kWStageBytes, wm, &full_w[sw], kb * Cfg::kKbBytes, nb * 128);
+          uint8_t* ws = w_smem + sw * Cfg::kWStageBytes;
+          mbar_arrive_expect_tx(&full_w[sw], Cfg::kWBytes + sz_tx);
+          tma_load_2d(ws, wm, &full_w[sw], kb * Cfg::kKbBytes, nb * 128);
+          if (p.sz_tma) {
+            // the group rows of this 64-k block, [rows][128 features] each
+            const int g0 = p.sz_rows > 1 ? kb * p.sz_rows : (kb * 64) / p.gs;
+            tma_load_2d(ws + Cfg::kSOff, p.smaps + e, &full_w[sw], nb * 128, g0);
+            tma_load_2d(ws + Cfg::kZOff, p.zmaps + e, &full_w[sw], nb * 128, g0);
+          }
           w_armed[sw] = pw;
         }
       }
@@ -254,10 +270,16 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc_f16(BF16, 128, BT);
       int it = 0, tcount = 0;
       bool ok = true, issued = false;
       for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x, ++tcount) {
+        // the MMA's N covers the tile's valid token rows (rounded up to 16): an expert segment
+        // shorter than BT costs only its own rows of tensor-core time
+        int e, m0, mend, nb;
+        tile_info(tile, e, m0, mend, nb);
+        const int valid = min(BT, mend - m0);
+        const int n_mma = valid <= 0 ? 16 : min(BT, (valid + 15) & ~15);
+        const uint32_t idesc = make_idesc_f16(BF16, 128, n_mma);
         const int sc = tcount % ACC_STAGES, pc = (tcount / ACC_STAGES) & 1;
         if (!mbar_wait(&empty_acc[sc], pc ^ 1, abort_flag, kDevErrAccEmpty)) { ok = false; break; }
         tc_fence_after();
@@ -311,45 +333,64 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
         // group of each word of the block: one division per k-block, then the group advances
         // where a word starts on a group boundary (gs is a multiple of kSpan)
         const int kbase = kb * 64;
+        const uint8_t* st = w_smem + sw * Cfg::kWStageBytes;
+        // scale and zero of word w (group grp): from the stage (staged by TMA, [rows][128]) or global
+        auto fetch = [&](int w, int grp, float& sv, float& zv) {
+          if (p.sz_tma) {
+            const int slot = p.sz_rows > 1 ? (w * kSpan) / p.gs : 0;
+            sv = load_as_f32(st + Cfg::kSOff, p.s_dtype, slot * 128 + row);
+            zv = load_as_f32(st + Cfg::kZOff, p.z_dtype, slot * 128 + row);
+          } else {
+            const long long si = s_row + (long long)grp * p.s_stride_g;
+            sv = load_as_f32(sb, p.s_dtype, si);
+            zv = load_as_f32(zb, p.z_dtype, si);
+          }
+        };
         uint32_t r32[32];
+        uint32_t q[kWords];
+        auto load_q = [&]() {
+          const uint32_t* wt = reinterpret_cast<const uint32_t*>(st + row * Cfg::kKbBytes);
+#pragma unroll
+          for (int w = 0; w < kWords; w += 4) {
+            const uint4 v = *reinterpret_cast<const uint4*>(wt + w);
+            q[w] = v.x; q[w + 1] = v.y; q[w + 2] = v.z; q[w + 3] = v.w;
+          }
+        };
         if constexpr (MODE == kRowsExact && WBITS == 2) {
           // Table decode, bit-exact for any scale and zero: per (row, group) the four weights
           // RNE((c - z) * s), c = 0..3, are computed in fp32 as the reference does and rounded
           // once; their low bytes form tlo and their high bytes thi, so a code c selects byte c
           // of each, and one prmt per table turns four codes into their four values' bytes.
           uint32_t tlo[kWords], thi[kWords];
-          int grp = kbase / p.gs;
-          int next_k = (grp + 1) * p.gs;
+          auto build = [&]() {
+            int grp = kbase / p.gs;
+            int next_k = (grp + 1) * p.gs;
 #pragma unroll
-          for (int w = 0; w < kWords; ++w) {
-            const int k0 = kbase + w * kSpan;
-            const bool fresh = (w == 0) || (k0 >= next_k && k0 < p.K);
-            if (w > 0 && fresh) {
-              ++grp;
-              next_k += p.gs;
+            for (int w = 0; w < kWords; ++w) {
+              const int k0 = kbase + w * kSpan;
+              const bool fresh = (w == 0) || (k0 >= next_k && k0 < p.K);
+              if (w > 0 && fresh) {
+                ++grp;
+                next_k += p.gs;
+              }
+              if (fresh) {
+                float sv, zv;
+                fetch(w, k0 < p.K ? grp : 0, sv, zv);
+                const uint32_t p01 = pack2_rn<BF16>(__fmul_rn(__fsub_rn(0.f, zv), sv), __fmul_rn(__fsub_rn(1.f, zv), sv));
+                const uint32_t p23 =
+                    pack2_rn<BF16>(__fmul_rn(__fsub_rn(2.f, zv), sv), __fmul_rn(__fsub_rn(3.f, zv), sv));
+                tlo[w] = prmt(p01, p23, 0x6420u);
+                thi[w] = prmt(p01, p23, 0x7531u);
+              } else {
+                tlo[w] = tlo[w > 0 ? w - 1 : 0];
+                thi[w] = thi[w > 0 ? w - 1 : 0];
+              }
             }
-            if (fresh) {
-              const long long si = s_row + (long long)(k0 < p.K ? grp : 0) * p.s_stride_g;
-              const float sv = load_as_f32(sb, p.s_dtype, si), zv = load_as_f32(zb, p.z_dtype, si);
-              const uint32_t p01 = pack2_rn<BF16>(__fmul_rn(__fsub_rn(0.f, zv), sv), __fmul_rn(__fsub_rn(1.f, zv), sv));
-              const uint32_t p23 =
-                  pack2_rn<BF16>(__fmul_rn(__fsub_rn(2.f, zv), sv), __fmul_rn(__fsub_rn(3.f, zv), sv));
-              tlo[w] = prmt(p01, p23, 0x6420u);
-              thi[w] = prmt(p01, p23, 0x7531u);
-            } else {
-              tlo[w] = tlo[w > 0 ? w - 1 : 0];
-              thi[w] = thi[w > 0 ? w - 1 : 0];
-            }
-          }
+          };
+          if (!p.sz_tma) build();  // global loads in flight while the weight stage lands
           if (!mbar_wait(&full_w[sw], pw, abort_flag, kDevErrWFull)) { ok = false; break; }
-          uint32_t q[kWords];
-          const uint32_t* wt =
-              reinterpret_cast<const uint32_t*>(w_smem + sw * Cfg::kWStageBytes + row * Cfg::kKbBytes);
-#pragma unroll
-          for (int w = 0; w < kWords; w += 4) {
-            const uint4 v = *reinterpret_cast<const uint4*>(wt + w);
-            q[w] = v.x; q[w + 1] = v.y; q[w + 2] = v.z; q[w + 3] = v.w;
-          }
+          if (p.sz_tma) build();
+          load_q();
           mbar_arrive(&empty_w[sw]);
 #pragma unroll
           for (int w = 0; w < kWords; ++w) {
@@ -367,36 +408,33 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
         } else {
           RowsConst<BF16, MODE> cst[kWords];
           bool exact = true;  // exact mode: the pair arithmetic reproduces the fp32 formula
-          int grp = kbase / p.gs;
-          int next_k = (grp + 1) * p.gs;
+          auto build = [&]() {
+            int grp = kbase / p.gs;
+            int next_k = (grp + 1) * p.gs;
 #pragma unroll
-          for (int w = 0; w < kWords; ++w) {
-            const int k0 = kbase + w * kSpan;
-            const bool fresh = (w == 0) || (k0 >= next_k && k0 < p.K);
-            if (w > 0 && fresh) {
-              ++grp;
-              next_k += p.gs;
+            for (int w = 0; w < kWords; ++w) {
+              const int k0 = kbase + w * kSpan;
+              const bool fresh = (w == 0) || (k0 >= next_k && k0 < p.K);
+              if (w > 0 && fresh) {
+                ++grp;
+                next_k += p.gs;
+              }
+              if (fresh) {
+                float sv, zv;
+                fetch(w, k0 < p.K ? grp : 0, sv, zv);
+                cst[w] = rows_const<BF16, MODE>(sv, zv);
+                if (MODE == kRowsExact) exact = exact && rows_pair_exact<BF16, MODE>(sv, zv, cst[w]);
+              } else {
+                cst[w] = cst[w > 0 ? w - 1 : 0];
+              }
             }
-            if (fresh) {
-              const long long si = s_row + (long long)(k0 < p.K ? grp : 0) * p.s_stride_g;
-              const float sv = load_as_f32(sb, p.s_dtype, si), zv = load_as_f32(zb, p.z_dtype, si);
-              cst[w] = rows_const<BF16, MODE>(sv, zv);
-              if (MODE == kRowsExact) exact = exact && rows_pair_exact<BF16, MODE>(sv, zv, cst[w]);
-            } else {
-              cst[w] = cst[w > 0 ? w - 1 : 0];
-            }
-          }
+          };
+          if (!p.sz_tma) build();
           if (!mbar_wait(&full_w[sw], pw, abort_flag, kDevErrWFull)) { ok = false; break; }
-          uint32_t q[kWords];
-          const uint32_t* wt =
-              reinterpret_cast<const uint32_t*>(w_smem + sw * Cfg::kWStageBytes + row * Cfg::kKbBytes);
-#pragma unroll
-          for (int w = 0; w < kWords; w += 4) {
-            const uint4 v = *reinterpret_cast<const uint4*>(wt + w);
-            q[w] = v.x; q[w + 1] = v.y; q[w + 2] = v.z; q[w + 3] = v.w;
-          }
-          mbar_arrive(&empty_w[sw]);
+          if (p.sz_tma) build();
+          load_q();
           if (MODE == kRowsRtn || __all_sync(0xffffffffu, exact)) {
+            mbar_arrive(&empty_w[sw]);
 #pragma unroll
             for (int w = 0; w < kWords; ++w) {
               const uint32_t qq = q[w];
@@ -412,12 +450,13 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
           } else {
             // zeros or scales the pair arithmetic cannot reproduce exactly (a zero that is not a
             // half-integer, an fp32 scale, a scale outside the pair type's range): the reference's
-            // formula in fp32, RNE((q - z) * s), for every weight of the warp's block
+            // formula in fp32, RNE((q - z) * s), for every weight of the warp's block (the stage is
+            // released after this decode: the staged scales are read here again)
 #pragma unroll
             for (int w = 0; w < kWords; ++w) {
               const int k0 = kbase + w * kSpan;
-              const long long si = s_row + (long long)(k0 < p.K ? k0 / p.gs : 0) * p.s_stride_g;
-              const float sv = load_as_f32(sb, p.s_dtype, si), zv = load_as_f32(zb, p.z_dtype, si);
+              float sv, zv;
+              fetch(w, k0 < p.K ? k0 / p.gs : 0, sv, zv);
               const uint32_t qq = q[w];
 #pragma unroll
               for (int j = 0; j < 8; j += 2) {
@@ -426,6 +465,7 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
                     pack2_rn<BF16>(__fmul_rn(__fsub_rn(qa, zv), sv), __fmul_rn(__fsub_rn(qb, zv), sv));
               }
             }
+            mbar_arrive(&empty_w[sw]);
           }
         }
         if (!mbar_wait(&empty_a[sa], pa ^ 1, abort_flag, kDevErrAEmpty)) { ok = false; break; }
@@ -454,8 +494,9 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
       tc_fence_after();
       __syncwarp();
       const uint32_t tbase = tmem_base + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(sc * BT);
+      const int nch = min(BT / 32, (mend - m0 + 31) / 32);  // chunks holding valid rows
 #pragma unroll 1
-      for (int c = 0; c < BT / 32; ++c) {
+      for (int c = 0; c < nch; ++c) {
         uint32_t v[32];
         tmem_ld_32x32b_x32(tbase + (uint32_t)(c * 32), v);
         tc_wait_ld();

@@ -1043,7 +1043,9 @@ extern "C" int oc_b200_moe_combine(const void* y, int64_t ldy, const int32_t* sl
 
 // ---------------------------------------------------------------- row-packed (RTN / DSV4) layers
 namespace {
-size_t rows_table_bytes(int E) { return align_up((size_t)E * sizeof(CUtensorMap), 256) + align_up((size_t)E * 16, 256); }
+// [E weight maps][E scale maps][E zero maps] then [E scale pointers][E zero pointers]
+size_t rows_maps_bytes(int E) { return align_up((size_t)3 * E * sizeof(CUtensorMap), 256); }
+size_t rows_table_bytes(int E) { return rows_maps_bytes(E) + align_up((size_t)E * 16, 256); }
 }
 
 extern "C" size_t oc_b200_rows_table_bytes(int E) { return E > 0 ? rows_table_bytes(E) : 0; }
@@ -1072,11 +1074,23 @@ extern "C" int oc_b200_rows_layer_create(int E, const uint8_t* const* packed, in
   int dev = 0;
   if (int rc = current_device(&dev)) return rc;
   if (int rc = oc_b200_device_check(dev)) return rc;
-  const size_t maps_bytes = align_up((size_t)E * sizeof(CUtensorMap), 256);
+  const size_t maps_bytes = rows_maps_bytes(E);
   uint8_t* host = new uint8_t[rows_table_bytes(E)]();
   CUtensorMap* maps = reinterpret_cast<CUtensorMap*>(host);
+  CUtensorMap* smaps = maps + E;
+  CUtensorMap* zmaps = maps + 2 * E;
   const void** sp = reinterpret_cast<const void**>(host + maps_bytes);
   const void** zp = sp + E;
+  // Scales / zeros stored [G, N] (stride_n == 1) ride in each weight stage by TMA: the rows of the
+  // groups one 64-k block covers, 128 features each, when they fit the stage's 512 bytes per tensor.
+  const int span_k = 32 / wbits;
+  const int gs_eff = groupsize >= K ? (K + span_k - 1) / span_k * span_k : groupsize;
+  const int G = (K + gs_eff - 1) / gs_eff;
+  const int sz_rows = (gs_eff < 64 && 64 % gs_eff == 0) ? 64 / gs_eff : 1;
+  const int s_es = scales_dtype == OC_DT_F32 ? 4 : 2, z_es = zeros_dtype == OC_DT_F32 ? 4 : 2;
+  bool sz_tma = stride_n == 1 && stride_g >= N && (G == 1 || gs_eff % 64 == 0 || 64 % gs_eff == 0) &&
+                sz_rows * 128 * s_es <= 512 && sz_rows * 128 * z_es <= 512 && (stride_g * s_es) % 16 == 0 &&
+                (stride_g * z_es) % 16 == 0;
   for (int e = 0; e < E; ++e) {
     if (!packed[e] || !scales[e] || !zeros[e]) {
       delete[] host;
@@ -1089,6 +1103,19 @@ extern "C" int oc_b200_rows_layer_create(int E, const uint8_t* const* packed, in
     }
     sp[e] = scales[e];
     zp[e] = zeros[e];
+    if (sz_tma && (!aligned(scales[e], 16) || !aligned(zeros[e], 16))) sz_tma = false;
+  }
+  if (sz_tma) {
+    const auto sdt = s_es == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16;
+    const auto zdt = z_es == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16;
+    for (int e = 0; e < E && sz_tma; ++e) {
+      if (make_tmap_2d(&smaps[e], sdt, s_es, scales[e], (uint64_t)N, (uint64_t)G, (uint64_t)stride_g * s_es, 128,
+                       (uint32_t)sz_rows, CU_TENSOR_MAP_SWIZZLE_NONE) != OC_OK ||
+          make_tmap_2d(&zmaps[e], zdt, z_es, zeros[e], (uint64_t)N, (uint64_t)G, (uint64_t)stride_g * z_es, 128,
+                       (uint32_t)sz_rows, CU_TENSOR_MAP_SWIZZLE_NONE) != OC_OK)
+        sz_tma = false;
+    }
+    g_last_error.clear();
   }
   int rc = cuda_check(cudaMemcpyAsync(table, host, rows_table_bytes(E), cudaMemcpyHostToDevice, stream), "table copy");
   if (!rc) rc = cuda_check(cudaStreamSynchronize(stream), "table copy sync");
@@ -1112,6 +1139,8 @@ extern "C" int oc_b200_rows_layer_create(int E, const uint8_t* const* packed, in
   L->d_wmaps = reinterpret_cast<const CUtensorMap*>(table);
   L->d_sptr = reinterpret_cast<const void* const*>(reinterpret_cast<uint8_t*>(table) + maps_bytes);
   L->d_zptr = L->d_sptr + E;
+  L->sz_tma = sz_tma ? 1 : 0;
+  L->sz_rows = sz_rows;
   *out = L;
   return OC_OK;
 }
@@ -1190,8 +1219,14 @@ extern "C" int oc_b200_rows_gemm(const oc_b200_layer* L, const void* a, int a_dt
   p.E = L->E;
   p.offsets = offsets;
   p.wmaps = L->d_wmaps;
+  p.smaps = L->d_wmaps + L->E;
+  p.zmaps = L->d_wmaps + 2 * L->E;
   p.sptr = L->d_sptr;
   p.zptr = L->d_zptr;
+  p.sz_tma = L->sz_tma;
+  p.sz_rows = L->sz_rows;
+  p.s_es = L->s_dtype_r == OC_DT_F32 ? 4 : 2;
+  p.z_es = L->z_dtype_r == OC_DT_F32 ? 4 : 2;
   p.s_dtype = L->s_dtype_r;
   p.z_dtype = L->z_dtype_r;
   p.s_stride_n = L->stride_n;

@@ -1,26 +1,34 @@
-"""Generic int4 loader for OneCompression GPTQ-packed diffusion checkpoints (B200 build).
+"""Loader for OneCompression GPTQ-packed diffusion checkpoints on B200.
 
-Same contract as the reference ``onecomp_runtime/diffusion.py:57-239``: a single
-``safetensors`` file with metadata ``config_json``, ``quant_layers_json``
-(entries ``name, wbits, groupsize, actorder, in_features, out_features``) and
-``checkpoint_format`` (``gptq`` / ``gptq_v2``). The model is built on the meta
-device by ``build_meta_model``, every quantized Linear is swapped for the module
-``backend.build_quant_layer`` returns, the remaining tensors are materialised on
-the device, key checks run, and the unique layer signatures are warmed up.
-``backend`` accepts ``"b200"`` (the default ``"auto"`` resolves to it).
+Contract of the reference ``onecomp_runtime/diffusion.py:57-239`` (kept so adapters and
+callers work unchanged): one ``safetensors`` file whose metadata holds ``config_json`` (the
+model config; keys starting with ``_`` are dropped), ``quant_layers_json`` (one entry per
+quantized ``nn.Linear``: ``name, wbits, groupsize, actorder, in_features, out_features``) and
+optionally ``checkpoint_format`` (``gptq`` / ``gptq_v2``, copied into every entry). The model is
+built on the meta device by ``build_meta_model(config)``, each selected quantized Linear is
+replaced by the module ``backend.build_quant_layer`` returns, every other tensor is
+materialised on the device in the compute dtype, and the load fails on a missing parent module,
+on missing or unexpected state-dict keys and on parameters left on the meta device. The summary
+line counts the built layers per kind, and ``warmup`` runs once per distinct
+``(in_features, out_features, has_bias)`` signature.
 
-``io="simple"`` (the default) reads tensor by tensor as the reference does. ``io="stream"``
-reads the checkpoint with ``_io.DeviceStreamer``: tensor bytes go from the file into pinned
-staging buffers and on to the device in large asynchronous copies, overlapped with the reads,
-before the layers are built from the device tensors. Measured on B200 with a 527 MB checkpoint
-in the page cache, it moves 16 GB/s against 6.3 GB/s once its pinned staging is allocated, but
-the first load of a process pays that allocation (142-266 ms against 92-144 ms), so it pays off
-for processes that load several checkpoints.
+This implementation is organised in three steps:
+
+1. ``Manifest.read`` parses and validates the header;
+2. ``plan_load`` resolves every selected layer to its parent module and the checkpoint keys it
+   owns, and lists the dense tensors to materialise;
+3. a reader delivers the tensors -- ``io="simple"`` (default) one ``get_tensor`` per key,
+   ``io="stream"`` through ``_io.DeviceStreamer`` (file -> pinned staging -> device in large
+   asynchronous copies, overlapped with the reads). Measured on B200 with a 527 MB checkpoint in
+   the page cache: 16 GB/s against 6.3 GB/s once the pinned staging exists, but the first load of
+   a process pays its allocation (142-266 ms against 92-144 ms), so it suits processes that load
+   several checkpoints.
 """
 from __future__ import annotations
 
 import json
 import time
+from dataclasses import dataclass, field
 from pathlib import Path
 from typing import Any, Callable
 
@@ -30,6 +38,137 @@ from safetensors import safe_open
 from ._io import DeviceStreamer
 from .backend import build_quant_layer, resolve_backend, resolve_dtype
 from .layers._gptq_base import B200GPTQLinear
+
+# checkpoint tensors a quantized layer may own, as "<layer name>.<role>"
+LAYER_ROLES = ("qweight", "scales", "qzeros", "g_idx", "bias")
+# the kinds build_quant_layer can report, in the order of the summary line
+LAYER_KINDS = ("gemlite", "a8w4", "a8w4_ffn_up", "mxfp4_ffn", "mxfp4_ffn_up", "nvfp4_ffn", "fused", "packed",
+               "eager")
+
+
+@dataclass(frozen=True)
+class Manifest:
+    """The checkpoint header: model config, quantized-layer entries, packing format, tensor keys."""
+
+    config: dict
+    layers: list
+    fmt: str
+    keys: frozenset
+
+    @classmethod
+    def read(cls, handle, path: Path) -> "Manifest":
+        meta = handle.metadata() or {}
+        raw_cfg, raw_layers = meta.get("config_json"), meta.get("quant_layers_json")
+        if raw_cfg is None or raw_layers is None:
+            raise ValueError(f"{path}: no 'config_json' / 'quant_layers_json' metadata (this is not a packed "
+                             "OneCompression diffusion checkpoint)")
+        config = {k: v for k, v in json.loads(raw_cfg).items() if not k.startswith("_")}
+        fmt = meta.get("checkpoint_format", "gptq")
+        layers = [dict(e, checkpoint_format=fmt) for e in json.loads(raw_layers)]
+        return cls(config, layers, fmt, frozenset(handle.keys()))
+
+    def owned_keys(self, name: str) -> dict:
+        """role -> checkpoint key for the tensors layer `name` has in this file."""
+        return {r: f"{name}.{r}" for r in LAYER_ROLES if f"{name}.{r}" in self.keys}
+
+
+@dataclass
+class LayerSlot:
+    entry: dict
+    parent: torch.nn.Module
+    child: str
+    keys: dict
+
+
+@dataclass
+class LoadPlan:
+    slots: list = field(default_factory=list)
+    dense_keys: list = field(default_factory=list)
+    claimed: frozenset = frozenset()   # keys owned by quantized layers (selected or not) + their weights
+
+    def tensor_keys(self) -> list:
+        return [k for s in self.slots for k in s.keys.values()] + self.dense_keys
+
+
+def plan_load(manifest: Manifest, model: torch.nn.Module, layer_filter, tensor_filter) -> LoadPlan:
+    """Resolve the selected quantized layers to (parent module, attribute, owned keys) and list
+    the dense tensors to materialise. Every quantized layer's keys are claimed, selected or not,
+    so they never count as dense tensors."""
+    modules = dict(model.named_modules())
+    claimed = set()
+    for e in manifest.layers:
+        claimed.add(f"{e['name']}.weight")
+        claimed.update(manifest.owned_keys(e["name"]).values())
+    plan = LoadPlan(claimed=frozenset(claimed))
+    for e in manifest.layers:
+        name = e["name"]
+        if layer_filter is not None and not layer_filter(name):
+            continue
+        parent_name, _, child = name.rpartition(".")
+        parent = modules.get(parent_name) if parent_name else model
+        if parent is None:
+            raise KeyError(f"parent module {parent_name!r} of quantized layer {name!r} is not in the model")
+        plan.slots.append(LayerSlot(e, parent, child, manifest.owned_keys(name)))
+    plan.dense_keys = sorted(k for k in manifest.keys
+                             if k not in plan.claimed and (tensor_filter is None or tensor_filter(k)))
+    return plan
+
+
+class _SimpleReader:
+    """One ``get_tensor`` per key (host tensors; the layers move them)."""
+
+    def __init__(self, handle):
+        self.handle = handle
+
+    def prefetch(self, keys):
+        pass
+
+    def take(self, key):
+        return self.handle.get_tensor(key)
+
+
+class _StreamReader:
+    """Every planned tensor on the device up front, in a few large asynchronous copies."""
+
+    def __init__(self, path: Path, dev: torch.device):
+        self.streamer = DeviceStreamer(str(path), dev)
+        self.got: dict = {}
+
+    def prefetch(self, keys):
+        self.got = self.streamer.load(list(keys))
+
+    def take(self, key):
+        return self.got.pop(key)
+
+
+def _check_loaded(model: torch.nn.Module, missing, unexpected, plan: LoadPlan) -> None:
+    """Missing keys other than the replaced layers' own, unexpected keys, and meta parameters fail."""
+    replaced = tuple(f"{s.entry['name']}." for s in plan.slots)
+    really_missing = [k for k in missing if k not in plan.claimed and not k.startswith(replaced)]
+    if really_missing:
+        raise RuntimeError(f"missing keys: {really_missing[:8]} ...")
+    if unexpected:
+        raise RuntimeError(f"unexpected keys: {unexpected[:8]} ...")
+
+
+def _check_materialised(model: torch.nn.Module) -> None:
+    on_meta = [n for n, prm in model.named_parameters() if prm.is_meta]
+    if on_meta:
+        raise RuntimeError(f"parameter left on meta device: {on_meta[:8]} ...")
+
+
+def _warm_up(model: torch.nn.Module, m_values, dev: torch.device, label: str) -> None:
+    """Warm one layer per distinct (in_features, out_features, has_bias) signature."""
+    t0 = time.perf_counter()
+    reps: dict = {}
+    for m in model.modules():
+        if isinstance(m, B200GPTQLinear):
+            reps.setdefault((m.in_features, m.out_features, m.bias is not None), m)
+    for layer in reps.values():
+        layer.warmup(m_values=m_values)
+    if reps:
+        torch.cuda.synchronize(dev)
+        print(f"[{label}] warmup {(time.perf_counter() - t0) * 1000:.0f} ms ({len(reps)} unique signatures)")
 
 
 def load_int4_model(
@@ -49,118 +188,43 @@ def load_int4_model(
     label: str = "onecomp_runtime",
     io: str = "simple",
 ) -> torch.nn.Module:
-    """Rebuild a packed-int4 diffusion transformer for inference on B200."""
-    backend = resolve_backend(backend, use_fused)
-    resolved = resolve_dtype(dtype)
-    dev = torch.device(device)
-    path = Path(checkpoint_path)
+    """Rebuild a packed-int4 diffusion transformer for inference on B200 (``backend="b200"``; the
+    default ``"auto"`` resolves to it). Arguments as the reference's; ``io`` picks the reader."""
     if io not in ("stream", "simple"):
         raise ValueError(f"io must be 'stream' or 'simple', got {io!r}")
+    backend = resolve_backend(backend, use_fused)
+    compute = resolve_dtype(dtype)
+    dev = torch.device(device)
+    path = Path(checkpoint_path)
+    counts = dict.fromkeys(LAYER_KINDS, 0)
 
-    with safe_open(str(path), framework="pt", device="cpu") as f:
-        streamer = DeviceStreamer(str(path), dev) if io == "stream" else None
-        md = f.metadata() or {}
-        cfg_json = md.get("config_json")
-        quant_layers_json = md.get("quant_layers_json")
-        if cfg_json is None or quant_layers_json is None:
-            raise ValueError(
-                f"{path} is missing 'config_json' / 'quant_layers_json' "
-                "metadata; not a packed OneCompression diffusion checkpoint")
-        cfg = {k: v for k, v in json.loads(cfg_json).items() if not k.startswith("_")}
-        quant_layers = json.loads(quant_layers_json)
-        ckpt_fmt = md.get("checkpoint_format", "gptq")
-        tensor_keys = set(f.keys())
-
+    with safe_open(str(path), framework="pt", device="cpu") as handle:
+        manifest = Manifest.read(handle, path)
         with torch.device("meta"):
-            model = build_meta_model(cfg)
+            model = build_meta_model(manifest.config)
         if prepare_meta_model is not None:
             prepare_meta_model(model)
-
-        modules = dict(model.named_modules())
-        counts = {"gemlite": 0, "a8w4": 0, "a8w4_ffn_up": 0, "mxfp4_ffn": 0, "mxfp4_ffn_up": 0,
-                  "nvfp4_ffn": 0, "fused": 0, "packed": 0, "eager": 0}
-        quant_keys: set[str] = set()
-        quant_names: list[str] = []
-        for entry in quant_layers:
-            name = entry["name"]
-            quant_keys.add(f"{name}.weight")
-            for suffix in ("qweight", "scales", "qzeros", "g_idx", "bias"):
-                key = f"{name}.{suffix}"
-                if key in tensor_keys:
-                    quant_keys.add(key)
-        selected = []
-        for entry in quant_layers:
-            entry["checkpoint_format"] = ckpt_fmt
-            name = entry["name"]
-            if quant_layer_filter is not None and not quant_layer_filter(name):
-                continue
-            parent_name, _, child = name.rpartition(".")
-            parent = modules.get(parent_name) if parent_name else model
-            if parent is None:
-                raise KeyError(f"quant layer parent not found: {parent_name!r}")
-            selected.append((entry, parent, child))
-        non_quant_keys = [k for k in sorted(tensor_keys) if k not in quant_keys
-                          and (tensor_filter is None or tensor_filter(k))]
-
-        if streamer is not None:  # every needed tensor to the device in a few large copies
-            wanted = [f"{e['name']}.{s}" for e, _, _ in selected
-                      for s in ("qweight", "scales", "qzeros", "g_idx", "bias") if f"{e['name']}.{s}" in tensor_keys]
-            dev_tensors = streamer.load(wanted + non_quant_keys)
-            get = dev_tensors.pop
-        else:
-            get = f.get_tensor
-        for entry, parent, child in selected:
-            name = entry["name"]
-            quant_names.append(name)
-            st: dict[str, Any] = {}
-            for s in ("qweight", "scales", "qzeros", "g_idx", "bias"):
-                k = f"{name}.{s}"
-                if k in tensor_keys:
-                    st[s] = get(k)
-            layer, kind = build_quant_layer(entry, st, backend, resolved, dev)
+        plan = plan_load(manifest, model, quant_layer_filter, tensor_filter)
+        reader = _StreamReader(path, dev) if io == "stream" else _SimpleReader(handle)
+        reader.prefetch(plan.tensor_keys())
+        for slot in plan.slots:
+            tensors: dict[str, Any] = {role: reader.take(key) for role, key in slot.keys.items()}
+            layer, kind = build_quant_layer(slot.entry, tensors, backend, compute, dev)
             counts[kind] += 1
-            setattr(parent, child, layer)
-            del st
+            setattr(slot.parent, slot.child, layer)
+        dense = {}
+        for key in plan.dense_keys:
+            t = reader.take(key)
+            dense[key] = t.to(device=dev, dtype=compute if t.dtype.is_floating_point else t.dtype)
 
-        non_quant = {}
-        for k in non_quant_keys:
-            tensor = get(k)
-            non_quant[k] = tensor.to(device=dev, dtype=resolved if tensor.dtype.is_floating_point else tensor.dtype)
-            del tensor
-    missing, unexpected = model.load_state_dict(non_quant, strict=False, assign=True)
-    quant_prefixes = tuple(f"{n}." for n in quant_names)
-    real_missing = [m for m in missing if m not in quant_keys and not m.startswith(quant_prefixes)]
-    if real_missing:
-        raise RuntimeError(f"missing keys: {real_missing[:8]} ...")
-    if unexpected:
-        raise RuntimeError(f"unexpected keys: {unexpected[:8]} ...")
-
+    missing, unexpected = model.load_state_dict(dense, strict=False, assign=True)
+    _check_loaded(model, missing, unexpected, plan)
     if post_load is not None:
         post_load(model)
-
-    leftover = [n for n, p in model.named_parameters() if p.is_meta]
-    if leftover:
-        raise RuntimeError(f"parameter left on meta device: {leftover[:8]} ...")
-
+    _check_materialised(model)
     model.eval()
-    print(f"[{label}] loaded {len(quant_names)} int4 layers "
-          f"(gemlite={counts['gemlite']}, a8w4={counts['a8w4']}, "
-          f"a8w4_ffn_up={counts['a8w4_ffn_up']}, "
-          f"mxfp4_ffn={counts['mxfp4_ffn']}, "
-          f"mxfp4_ffn_up={counts['mxfp4_ffn_up']}, "
-          f"nvfp4_ffn={counts['nvfp4_ffn']}, fused={counts['fused']}, "
-          f"packed={counts['packed']}, eager={counts['eager']}) on {dev}")
-
+    per_kind = ", ".join(f"{k}={counts[k]}" for k in LAYER_KINDS)
+    print(f"[{label}] loaded {len(plan.slots)} int4 layers ({per_kind}) on {dev}")
     if warmup and dev.type == "cuda":
-        t0 = time.perf_counter()
-        seen: dict[tuple, Any] = {}
-        for m in model.modules():
-            if isinstance(m, B200GPTQLinear):
-                seen.setdefault((m.in_features, m.out_features, m.bias is not None), m)
-        if seen:
-            for layer in seen.values():
-                layer.warmup(m_values=warmup_m_values)
-            torch.cuda.synchronize(dev)
-            print(f"[{label}] warmup {(time.perf_counter()-t0)*1000:.0f} ms "
-                  f"({len(seen)} unique signatures)")
+        _warm_up(model, warmup_m_values, dev, label)
     return model

@@ -66,6 +66,20 @@ class RowsHandle:
         self.close()
 
 
+def group_major(t: torch.Tensor, N: int, K: int, gs: int) -> torch.Tensor:
+    """Scales or zeros as a contiguous [G, N] float tensor (the layout the kernel stages by TMA with
+    each weight block): given [N, G] (``scales.shape == (out, groups)``, transposed as
+    dsv4_packed_linear.py:50-51 does) or [G, N]; one group per row (``gs <= 0`` or ``gs >= K``) gives
+    [1, N]."""
+    t = float_param(t)
+    G = 1 if (gs <= 0 or gs >= K) else (K + gs - 1) // gs
+    if G == 1:
+        return t.reshape(1, N).contiguous()
+    if tuple(t.shape) == (N, G):
+        return t.t().contiguous()
+    return t.reshape(G, N).contiguous()
+
+
 def float_param(t: torch.Tensor) -> torch.Tensor:
     """Scales/zeros as a float dtype the kernels read (int zero points become fp32, exactly)."""
     if t.dtype in (torch.float16, torch.bfloat16, torch.float32):

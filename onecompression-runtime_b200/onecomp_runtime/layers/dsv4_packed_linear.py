@@ -24,7 +24,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .. import _lib
-from ._rows_base import MODE_EXACT, RowsHandle, float_param, prep_activation, rows_fusable
+from ._rows_base import MODE_EXACT, RowsHandle, float_param, group_major, prep_activation, rows_fusable
 
 
 def _stride_of(scales: torch.Tensor, out_f: int, in_f: int, gs: int):
@@ -132,9 +132,11 @@ class Dsv4PackedLinear(nn.Module):
         if self.wbits not in (2, 4) or not rows_fusable(int(q.shape[1]), self.in_features, self.out_features, gs,
                                                         self.wbits):
             return None
-        sn, sg = _stride_of(self.scales, self.out_features, self.in_features, self.groupsize)
-        h = RowsHandle([q], [float_param(self.scales)], [float_param(self.qzeros)], self.wbits, gs,
-                       self.in_features, self.out_features, MODE_EXACT, sn, sg)
+        # group-major copies of scales / zeros (the kernel stages each block's rows by TMA)
+        N, K = self.out_features, self.in_features
+        s = group_major(self.scales, N, K, self.groupsize)
+        z = group_major(self.qzeros, N, K, self.groupsize)
+        h = RowsHandle([q], [s], [z], self.wbits, gs, K, N, MODE_EXACT, 1, N)
         self.__dict__["_handle"] = h
         self.__dict__["_handle_key"] = key
         return h

@@ -27,7 +27,7 @@ import torch.nn.functional as F
 
 from .. import _lib
 from ..quant_utils import dequant_extra_u8_to_weight
-from ._rows_base import MODE_RTN, RowsHandle, float_param, prep_activation, rows_fusable
+from ._rows_base import MODE_RTN, RowsHandle, group_major, prep_activation, rows_fusable
 
 
 class PackedRTNLinear(nn.Module):
@@ -75,7 +75,10 @@ class PackedRTNLinear(nn.Module):
             qp = torch.zeros((N, ld_run), dtype=torch.uint8, device=q.device)
             qp[:, :ld].copy_(q)
             q, gs = qp, gs_run
-        h = RowsHandle([q], [float_param(self.scales)], [float_param(self.zeros)], 4, gs, k_run, N, MODE_RTN, G, 1)
+        # group-major copies of scales / zeros (the kernel stages each block's rows by TMA)
+        s = group_major(self.scales, N, K, K if G == 1 else gs)
+        z = group_major(self.zeros, N, K, K if G == 1 else gs)
+        h = RowsHandle([q], [s], [z], 4, gs, k_run, N, MODE_RTN, 1, N)
         self.__dict__["_handle"] = h
         self.__dict__["_handle_key"] = key
         self.__dict__["_k_run"] = k_run

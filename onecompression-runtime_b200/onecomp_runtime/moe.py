@@ -164,8 +164,7 @@ class PackedMoE(torch.nn.Module):
                  device="cuda"):
         super().__init__()
         from . import _lib
-        from .layers._rows_base import MODE_EXACT, RowsHandle, float_param
-        from .layers.dsv4_packed_linear import _stride_of
+        from .layers._rows_base import MODE_EXACT, RowsHandle, group_major
         dev = torch.device(device)
         _lib.require_b200(dev)
         self.E = len(experts)
@@ -178,10 +177,10 @@ class PackedMoE(torch.nn.Module):
             wbits, gs, K = int(p0["wbits"]), int(p0["groupsize"]), int(p0["in_features"])
             N = int(p0["qweight_packed"].shape[0])
             q = [m["qweight_packed"].to(dev).contiguous() for m in mats]
-            s = [float_param(m["scales"].to(dev)) for m in mats]
-            z = [float_param(m["qzeros"].to(dev)) for m in mats]
-            sn, sg = _stride_of(s[0], N, K, gs)
-            return RowsHandle(q, s, z, wbits, gs if gs > 0 else K, K, N, MODE_EXACT, sn, sg)
+            # scales / zeros group-major ([G, N]): the kernel stages each block's rows by TMA
+            s = [group_major(m["scales"].to(dev), N, K, gs) for m in mats]
+            z = [group_major(m["qzeros"].to(dev), N, K, gs) for m in mats]
+            return RowsHandle(q, s, z, wbits, gs if gs > 0 else K, K, N, MODE_EXACT, 1, N)
 
         self._h = {name: build([ex[name] for ex in experts]) for name in ("gate", "up", "down")}
         self._shared = {name: build([shared[name]]) for name in ("gate", "up", "down")} if shared else None
