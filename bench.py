@@ -646,7 +646,8 @@ def bench_cfg3(args, job: Job, peaks: dict) -> dict:
     if world == 1:
         fn = lambda: moe(x, logits)  # noqa: E731
     else:
-        ep = ExpertParallelMoE(E, k, moe.expert_ffn, route=moe.route, shared=moe.shared_ffn, combine=moe.combine)
+        ep = ExpertParallelMoE(E, k, moe.expert_ffn, route=moe.route, shared=moe.shared_ffn, combine=moe.combine,
+                               permute=moe.permute, gather=moe.gather)
         fn = lambda: ep(x, logits)  # noqa: E731
     with torch.no_grad():
         ms, clk = timed_steps(job, fn, args.steps, args.warmup, before=timer.start)

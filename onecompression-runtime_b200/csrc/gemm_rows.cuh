@@ -79,6 +79,7 @@ struct RowsCfg {
   static constexpr int kSmemBytes = X_STAGES * kXStageBytes + W_STAGES * kWStageBytes + 1024 +
                                     (2 * (X_STAGES + W_STAGES + A_STAGES + ACC_STAGES) + 2) * 8 + 64 +
                                     (kRowsMaxE + 1) * 4;
+  static_assert(kSmemBytes <= 232448, "shared memory per CTA");
 };
 
 template <bool BF16, int MODE>

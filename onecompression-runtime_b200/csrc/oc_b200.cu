@@ -1169,8 +1169,15 @@ int launch_rows_t(const CUtensorMap& tx, const oc::RowsParams& p, int dev, cudaS
 
 template <bool BF16, int WB, int MODE, bool HL>
 int launch_rows_bt(int bt, const CUtensorMap& tx, const oc::RowsParams& p, int dev, cudaStream_t stream) {
-  if (bt == 128) return launch_rows_t<BF16, WB, MODE, HL, 128, 2, 10, 8, 8>(tx, p, dev, stream);
-  return launch_rows_t<BF16, WB, MODE, HL, 192, 2, 7, 8, 4>(tx, p, dev, stream);
+  // The weight ring is deep (16-32 stages of 3-5 KB) because packed weights stream from HBM with
+  // ~2 us of latency; activation tiles come from L2 and need fewer stages.
+  if (bt == 128) {
+    if constexpr (WB == 2)
+      return launch_rows_t<BF16, WB, MODE, HL, 128, 2, 6, 32, 8>(tx, p, dev, stream);
+    else
+      return launch_rows_t<BF16, WB, MODE, HL, 128, 2, 4, 24, 8>(tx, p, dev, stream);
+  }
+  return launch_rows_t<BF16, WB, MODE, HL, 192, 2, 5, 16, 4>(tx, p, dev, stream);
 }
 
 template <bool BF16>

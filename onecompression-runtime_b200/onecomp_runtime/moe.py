@@ -15,9 +15,11 @@ HBM and one call does:
 
 Expert parallelism (``ExpertParallelMoE``): experts are split contiguously
 across ranks, tokens are sharded; per layer the routed rows are exchanged with
-``all_to_all_single`` (split sizes exchanged first), processed by the local
-experts and sent back. Every step is a pluggable callable so the host-side
-logic is tested on CPU with gloo.
+``all_to_all_single`` (split sizes exchanged first, one host sync for them),
+processed by the local experts and sent back. Every step is a pluggable callable
+(routing, permutation, row gather, expert FFN, shared expert, combine) so the
+host-side logic is tested on CPU with gloo; ``PackedMoE`` supplies device
+kernels for each.
 """
 from __future__ import annotations
 
@@ -73,7 +75,8 @@ class ExpertParallelMoE(torch.nn.Module):
     """
 
     def __init__(self, num_experts: int, k: int, expert_ffn: Callable, route: Callable = route_reference,
-                 shared: Callable | None = None, group=None, combine: Callable | None = None):
+                 shared: Callable | None = None, group=None, combine: Callable | None = None,
+                 permute: Callable | None = None, gather: Callable | None = None):
         super().__init__()
         self.E = int(num_experts)
         self.k = int(k)
@@ -82,6 +85,9 @@ class ExpertParallelMoE(torch.nn.Module):
         self.shared = shared
         self.group = group
         self.combine = combine
+        # permute(ids [T, k], E) -> (offsets, sorted_token, slot_pos); gather(x, idx) -> x[idx]
+        self.permute = permute or permute_reference
+        self.gather = gather or (lambda x, idx: x.index_select(0, idx.long()))
         self._side: dict[int, torch.cuda.Stream] = {}
 
     def _launch_shared(self, x: torch.Tensor):
@@ -109,32 +115,31 @@ class ExpertParallelMoE(torch.nn.Module):
         T, H = x.shape
         shared_out, side = self._launch_shared(x)
         ids, w = self.route(logits, K)
-        offsets, sorted_token, slot_pos = permute_reference(ids, E)
-        x_send = x.index_select(0, sorted_token.long())
-        ids_send = ids.reshape(-1).index_select(0, torch.argsort(slot_pos.long()))  # expert of each sorted row
+        offsets, sorted_token, slot_pos = self.permute(ids, E)
+        x_send = self.gather(x, sorted_token)
         counts = (offsets[1:] - offsets[:-1]).to(torch.int64)                        # per expert, this rank
         if world == 1:
             y_sorted = self.expert_ffn(x_send, offsets)
         else:
+            # expert id of each sorted row: the segment its position falls in
+            pos = torch.arange(T * K, device=x.device, dtype=offsets.dtype)
+            ids_send = torch.searchsorted(offsets[1:].contiguous(), pos, right=True).to(torch.int32)
             send_split = counts.view(world, el).sum(1)
             recv_counts = torch.empty_like(counts)
             dist.all_to_all_single(recv_counts, counts, group=self.group)    # [src][local expert]
             recv_counts = recv_counts.view(world, el)
             recv_split = recv_counts.sum(1)
-            ss, rs = send_split.tolist(), recv_split.tolist()
+            splits = torch.cat([send_split, recv_split]).tolist()             # the one host sync
+            ss, rs = splits[:world], splits[world:]
             x_recv = x.new_empty((sum(rs), H))
             dist.all_to_all_single(x_recv, x_send.contiguous(), rs, ss, group=self.group)
             e_recv = ids_send.new_empty((sum(rs),))
             dist.all_to_all_single(e_recv, ids_send.contiguous(), rs, ss, group=self.group)
             # rows arrive grouped by source rank; order them by local expert (stable)
-            local_e = (e_recv.long() - rank * el)
-            order = torch.argsort(local_e, stable=True)
-            loc_counts = torch.bincount(local_e, minlength=el)
-            loc_off = torch.zeros(el + 1, dtype=torch.int32, device=x.device)
-            loc_off[1:] = torch.cumsum(loc_counts, 0).to(torch.int32)
-            y_loc = self.expert_ffn(x_recv.index_select(0, order), loc_off)
-            y_recv = torch.empty_like(y_loc)
-            y_recv[order] = y_loc
+            local_e = (e_recv - rank * el).view(-1, 1)
+            loc_off, order, back = self.permute(local_e, el)
+            y_loc = self.expert_ffn(self.gather(x_recv, order), loc_off)
+            y_recv = self.gather(y_loc, back)                                   # back to arrival order
             y_sorted = x.new_empty((T * K, y_recv.shape[1]))
             dist.all_to_all_single(y_sorted, y_recv, ss, rs, group=self.group)
         if side is not None:
@@ -215,6 +220,33 @@ class PackedMoE(torch.nn.Module):
         if self._shared is None:
             raise ValueError("this PackedMoE has no shared expert")
         return self._ffn(self._shared, x.contiguous(), None)
+
+    def permute(self, ids: torch.Tensor, E: int):
+        """Stable expert-major order of ``ids [T, k]`` on the device (``oc_b200_moe_permute``): the
+        ``permute`` hook of ``ExpertParallelMoE`` -> (offsets [E+1], sorted_token, slot_pos)."""
+        from . import _lib
+        T, k = ids.shape
+        dev = ids.device
+        ids = ids.to(torch.int32).contiguous()
+        counts = torch.empty(E, dtype=torch.int32, device=dev)
+        offsets = torch.empty(E + 1, dtype=torch.int32, device=dev)
+        sorted_token = torch.empty(T * k, dtype=torch.int32, device=dev)
+        slot_pos = torch.empty(T * k, dtype=torch.int32, device=dev)
+        _lib.call("oc_b200_moe_permute", ids.data_ptr(), T, k, E, counts.data_ptr(), offsets.data_ptr(),
+                  sorted_token.data_ptr(), slot_pos.data_ptr(), _lib.stream_of(dev))
+        return offsets, sorted_token, slot_pos
+
+    def gather(self, x: torch.Tensor, idx: torch.Tensor) -> torch.Tensor:
+        """``x[idx]`` for 16-bit rows on the device (``oc_b200_gather_rows``): the ``gather`` hook."""
+        from . import _lib
+        x = x.contiguous()
+        P, H = idx.numel(), x.shape[1]
+        out = torch.empty((P, H), dtype=x.dtype, device=x.device)
+        if P:
+            ii = idx.to(torch.int32).contiguous()
+            _lib.call("oc_b200_gather_rows", x.data_ptr(), x.stride(0), ii.data_ptr(), P, H, out.data_ptr(),
+                      out.stride(0), _lib.stream_of(x.device))
+        return out
 
     def route(self, logits: torch.Tensor, k: int):
         from . import _lib

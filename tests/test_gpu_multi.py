@@ -58,11 +58,17 @@ def _tp_worker(rank, world, port, out_path):
         h = x + blk["out"](qkv[:, :q])
         return h + blk["fc2"](torch.nn.functional.gelu(blk["fc1"](h), approximate="tanh"))
 
-    y = fwd(build_tp_block(tens, LAYERS, rank, world, 32, make, chunks=2), 512 // world)
+    def fwd_fused(blk, q):  # residual adds and GELU in the GEMM epilogues, as the benchmark stack runs
+        qkv = blk["qkv"](x)
+        h = blk["out"](qkv[:, :q], residual=x)
+        return blk["fc2"](blk["fc1"](h, activation="gelu_tanh"), residual=h)
+
+    blk = build_tp_block(tens, LAYERS, rank, world, 32, make, chunks=2)
+    y, yf = fwd(blk, 512 // world), fwd_fused(blk, 512 // world)
     if rank == 0:
         full = {n: make(tens[n], K, N) for n, K, N in LAYERS}
-        ref = fwd(full, 512)
-        err = float((y.float() - ref.float()).abs().max() / ref.float().abs().max())
+        ref = fwd(full, 512).float()
+        err = max(float((v.float() - ref).abs().max() / ref.abs().max()) for v in (y, yf))
         torch.save(torch.tensor([err]), out_path)
     torch.distributed.barrier()
     torch.distributed.destroy_process_group()
@@ -94,8 +100,9 @@ def _ep_worker(rank, world, port, out_path, with_shared):
     el = E // world
     local = PackedMoE(experts[rank * el:(rank + 1) * el], shared, k=k, device=dev)
     sh_fn = local.shared_ffn if with_shared else None
-    ep = ExpertParallelMoE(E, k, local.expert_ffn, route=local.route, shared=sh_fn,
-                           combine=local.combine if with_shared else None)
+    # with the shared expert: every device hook (permute, gather, combine); without: the torch ones
+    hooks = dict(combine=local.combine, permute=local.permute, gather=local.gather) if with_shared else {}
+    ep = ExpertParallelMoE(E, k, local.expert_ffn, route=local.route, shared=sh_fn, **hooks)
     sh = T // world
     y = ep(x[rank * sh:(rank + 1) * sh], logits[rank * sh:(rank + 1) * sh])
     ys = [torch.empty_like(y) for _ in range(world)]
