@@ -388,9 +388,10 @@ def cpu_baseline_cfg4(args) -> dict:
 class TPStack:
     """12 video-DiT blocks of B200 int4 linears sharded over the job's ranks."""
 
-    def __init__(self, job: Job, blocks: int, timer: LaunchTimer):
+    def __init__(self, job: Job, blocks: int, timer: LaunchTimer, chunks: int = 1):
         from onecomp_runtime.layers import FusedInt4Linear
         from onecomp_runtime.tensor_parallel import build_tp_block
+        self.chunks = max(1, chunks)
         from onecomp_runtime.testing import CFG4, CFG4_LAYERS, gptq_layer
         self.gs, self.H = CFG4["gs"], CFG4["hidden"]
         self.hq = self.H // job.world
@@ -407,12 +408,34 @@ class TPStack:
             del tens
 
     def forward(self, h: torch.Tensor) -> torch.Tensor:
-        for blk in self.blocks:
-            qkv = blk["qkv"](h)
-            h = rms_norm(blk["out"](qkv[:, :self.hq], residual=h))
-            f = blk["fc1"](h, activation="gelu_tanh")
-            h = rms_norm(blk["fc2"](f, residual=h))
-        return h
+        """The stack, pipelined over ``self.chunks`` row chunks. Per block: qkv of every chunk first
+        (attention needs all tokens), then per chunk the out-projection with its all-reduce started;
+        per chunk, once its reduction is done, norm, fc1 and fc2 with the second all-reduce started;
+        per chunk, once that is done, norm and the next block's qkv. Each reduction crosses NVLink
+        while the following chunks' GEMMs run."""
+        M = h.shape[0]
+        step = (M + self.chunks - 1) // self.chunks
+        hs = [h[c0:c0 + step] for c0 in range(0, M, step)]
+        qkv = [self.blocks[0]["qkv"](hc) for hc in hs]
+        for b, blk in enumerate(self.blocks):
+            pend = [blk["out"].forward_async(q[:, :self.hq], residual=hc) for q, hc in zip(qkv, hs)]
+            pend2 = []
+            for o, w in pend:
+                if w is not None:
+                    w.wait()
+                hn = rms_norm(o)
+                f = blk["fc1"](hn, activation="gelu_tanh")
+                pend2.append(blk["fc2"].forward_async(f, residual=hn))
+            nxt = self.blocks[b + 1] if b + 1 < len(self.blocks) else None
+            hs, qkv = [], []
+            for o, w in pend2:
+                if w is not None:
+                    w.wait()
+                hc = rms_norm(o)
+                hs.append(hc)
+                if nxt is not None:
+                    qkv.append(nxt["qkv"](hc))
+        return hs[0] if len(hs) == 1 else torch.cat(hs)
 
 
 def allreduce_alone(job: Job, M: int, H: int, per_step: int, chunks: int) -> float:
@@ -434,7 +457,11 @@ def bench_cfg4(args, job: Job, peaks: dict, with_cpu: bool) -> dict:
     from onecomp_runtime.testing import CFG4, CFG4_LAYERS
     M, H, blocks = CFG4["M"], CFG4["hidden"], (args.blocks or CFG4["blocks"])
     timer = LaunchTimer()
-    stack = TPStack(job, blocks, timer)
+    if job.world > 1 and args.tc_max_ctas:
+        from onecomp_runtime import _lib
+        _lib.set_option(_lib.OPT_TC_MAX_CTAS, args.tc_max_ctas)
+    chunks = args.tp_chunks if args.tp_chunks > 0 else (4 if job.world > 1 else 1)
+    stack = TPStack(job, blocks, timer, chunks)
     x = torch.randn((M, H), generator=torch.Generator(device=job.dev).manual_seed(5), device=job.dev).to(torch.bfloat16)
     with torch.no_grad():
         y = stack.forward(x)
@@ -455,6 +482,8 @@ def bench_cfg4(args, job: Job, peaks: dict, with_cpu: bool) -> dict:
                        "tokens": M, "blocks": blocks, "global_batch_tokens": M,
                        "parallelism": f"tp{job.world} (column qkv/fc1, row out/fc2 + NCCL all-reduce)"
                        if job.world > 1 else "tp1 (one GPU, no collective)",
+                       "pipeline_chunks": stack.chunks,
+                       "gemm_ctas": args.tc_max_ctas if (job.world > 1 and args.tc_max_ctas) else "one per SM",
                        "l2_flush": "none needed: weights (1.4 GB packed) and activations exceed the 126 MB L2"},
             "e2e": {"value": round(M * args.steps / (ms_e2e / 1e3), 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
@@ -731,6 +760,10 @@ def main():
     ap.add_argument("--moe-tokens", type=int, default=0, help="cfg3: override tokens per GPU (profiling only)")
     ap.add_argument("--cpu-sample-m", type=int, default=512, help="tokens of the bounded CPU sample (one block)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tp-chunks", type=int, default=0,
+                    help="cfg4: row chunks of the pipelined stack (0 = 4 with N > 1, 1 on one GPU)")
+    ap.add_argument("--tc-max-ctas", type=int, default=0,
+                    help="cfg4 with N > 1: CTAs of the persistent GEMMs (0 = one per SM), SMs left to NCCL")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     job = Job()

@@ -39,14 +39,18 @@ enum {
   OC_OPT_GEMM_PATH = 1,    /* 0 auto (M<=16 -> split-K GEMV, else tcgen05), 1 force GEMV, 2 force tcgen05 */
   OC_OPT_TC_TILE = 2,      /* tokens per tcgen05 tile: 0 auto, 128, 192, 256, 384, 448 */
   OC_OPT_GEMV_CTAS = 3,    /* GEMV CTAs per SM that split-K sizing fills in one wave (default 2) */
-  OC_OPT_GEMV_IMPL = 4,    /* decode kernel for uniform-group layers: 0 tcgen05, 1 TMA + mma.sync (default),
-                              2 cp.async + mma.sync */
+  OC_OPT_GEMV_IMPL = 4,    /* decode kernel for uniform-group layers: 0 tcgen05, 1 TMA + mma.sync split-K
+                              (default), 2 cp.async + mma.sync, 3 stream-K TMA + mma.sync with the act-order
+                              gather inside (M <= 8 and at least 256 columns; otherwise 1) */
   OC_OPT_TC_PAIR = 5,      /* tcgen05 GEMM on CTA pairs (cta_group::2): 0 auto, 1 single CTAs (default), 2 pairs */
   OC_OPT_WAIT_US = 6,      /* failure tests: bound of the TMA decode GEMV's pipeline waits in microseconds
                               (0, the default: 2 s); drains of copies in flight keep the 2 s bound */
-  OC_OPT_TEST_STALL = 7    /* failure tests: s > 0 makes the first CTA of each TMA decode GEMV leave stage
+  OC_OPT_TEST_STALL = 7,   /* failure tests: s > 0 makes the first CTA of each TMA decode GEMV leave stage
                               s - 1 unissued, so a wait runs out, the kernel records OC_ERR_DEVICE's code,
                               skips that tile's output and leaves its tickets re-armed; 0 (default) off */
+  OC_OPT_TC_MAX_CTAS = 8   /* persistent tcgen05 GEMMs (GPTQ and row-packed): at most this many CTAs,
+                              0 (default) one per SM; a tensor-parallel job leaves SMs to the NCCL
+                              all-reduce that overlaps the next chunk's GEMM */
 };
 
 /* ---- library / device ------------------------------------------------------ */
@@ -140,7 +144,7 @@ int oc_b200_gptq_layer_create_ex(const int32_t* qweight, const int32_t* qzeros, 
                                  int N, int G, int groupsize, int wbits, int v1, oc_b200_layer** out);
 int oc_b200_layer_destroy(oc_b200_layer* layer);
 /* Bytes of workspace oc_b200_gptq_gemm needs for M rows. The first
- * 1024 bytes hold split-K tickets that must be zero before the first call on a
+ * 8192 bytes hold split-K tickets that must be zero before the first call on a
  * workspace (every call leaves them zero again). */
 size_t oc_b200_gptq_gemm_workspace(const oc_b200_layer* layer, int64_t M);
 /* C[M, N] = A[M, in_features] @ dequant(W)^T + bias, fp32 accumulation, bias

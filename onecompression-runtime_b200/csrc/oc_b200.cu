@@ -19,6 +19,7 @@
 #include "gemv.cuh"
 #include "gemv_tma.cuh"
 #include "gemv_tc.cuh"
+#include "gemv_sk.cuh"
 #include "moe.cuh"
 
 namespace {
@@ -50,8 +51,17 @@ std::atomic<int> g_opt_path{0}, g_opt_tile{0}, g_opt_gemv_ctas{2}, g_opt_gemv_im
 // failure tests only: bound of the decode GEMV's pipeline waits (0: OC_WAIT_NS) and the stage its
 // first CTA leaves unissued (0: none)
 std::atomic<int> g_opt_wait_us{0}, g_opt_test_stall{0};
+// persistent tcgen05 GEMMs: at most this many CTAs (0: one per SM), leaving SMs to a collective
+// that runs beside them
+std::atomic<int> g_opt_tc_max_ctas{0};
 
 constexpr int kMaxDevices = 64;
+// Tickets at the head of every GEMV workspace, zero between launches (each launch re-arms the ones it
+// takes): one per 128-column tile for the split-K kernels (at most 256 tiles), one per (256-column
+// tile, consumer warp) for the stream-K kernel (at most 256 tiles x 8 warps).
+constexpr size_t kTicketBytes = 8192;
+constexpr int kSplitTilesMax = 256;
+constexpr int kSkTilesMax = (int)(kTicketBytes / 4) / oc::kSkWarps;
 int g_sm_count[kMaxDevices];
 std::mutex g_mu;
 
@@ -65,6 +75,13 @@ int sm_count(int dev) {
     g_sm_count[dev] = v > 0 ? v : 148;
   }
   return g_sm_count[dev];
+}
+
+// CTAs of a persistent tcgen05 GEMM: one per SM, or fewer under OC_OPT_TC_MAX_CTAS.
+int tc_ctas(int dev) {
+  const int sms = sm_count(dev);
+  const int cap = g_opt_tc_max_ctas.load();
+  return (cap > 0 && cap < sms) ? cap : sms;
 }
 
 // Launch with programmatic stream serialization (PDL): the kernel may start while the previous
@@ -146,6 +163,9 @@ struct oc_b200_layer {
   int gt_ok, gt_rows;      // decode GEMV fed by TMA (uniform groups of 32, 64 or 128*n rows)
   CUtensorMap tmap_gw, tmap_gs, tmap_gz;
   CUtensorMap tmap_s1, tmap_z1;  // one scale / zero row per box (tcgen05 decode GEMV)
+  int sk_ok;               // stream-K decode GEMV: gt_ok layouts with N >= 256
+  CUtensorMap tmap_ks, tmap_kz;  // 256-column scale / zero boxes of the stream-K GEMV
+  CUtensorMap tmap_kp;     // [16 word rows x 256 columns] boxes of qweight: the stream-K GEMV's L2 prefetch
   // row-packed layers
   int E, wbits, mode, s_dtype_r, z_dtype_r;
   long long stride_n, stride_g;
@@ -191,12 +211,16 @@ int oc_b200_set_option(int key, int value) {
       g_opt_tc_pair = value;
       return OC_OK;
     case OC_OPT_GEMV_IMPL:
-      if (value < 0 || value > 2) return fail(OC_ERR_INVALID, "OC_OPT_GEMV_IMPL: %d", value);
+      if (value < 0 || value > 3) return fail(OC_ERR_INVALID, "OC_OPT_GEMV_IMPL: %d", value);
       g_opt_gemv_impl = value;
       return OC_OK;
     case OC_OPT_WAIT_US:
       if (value < 0) return fail(OC_ERR_INVALID, "OC_OPT_WAIT_US: %d", value);
       g_opt_wait_us = value;
+      return OC_OK;
+    case OC_OPT_TC_MAX_CTAS:
+      if (value < 0) return fail(OC_ERR_INVALID, "OC_OPT_TC_MAX_CTAS: %d", value);
+      g_opt_tc_max_ctas = value;
       return OC_OK;
     case OC_OPT_TEST_STALL:
       if (value < 0) return fail(OC_ERR_INVALID, "OC_OPT_TEST_STALL: %d", value);
@@ -216,6 +240,7 @@ int oc_b200_get_option(int key, int* value) {
     case OC_OPT_TC_PAIR: *value = g_opt_tc_pair.load(); return OC_OK;
     case OC_OPT_WAIT_US: *value = g_opt_wait_us.load(); return OC_OK;
     case OC_OPT_TEST_STALL: *value = g_opt_test_stall.load(); return OC_OK;
+    case OC_OPT_TC_MAX_CTAS: *value = g_opt_tc_max_ctas.load(); return OC_OK;
   }
   return fail(OC_ERR_INVALID, "unknown option %d", key);
 }
@@ -533,6 +558,16 @@ int oc_b200_gptq_layer_create_ex(const int32_t* qweight, const int32_t* qzeros, 
       L->gt_rows = rows;
     }
   }
+  // Stream-K decode GEMV: the same layouts, tiles of 256 columns.
+  L->sk_ok = 0;
+  if (L->gt_ok && N >= oc::kSkCols && N <= oc::kSkCols * kSkTilesMax && aligned(k_perm, 16) &&
+      make_tmap_2d(&L->tmap_kp, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, qweight, (uint64_t)N, (uint64_t)(k_packed / 8),
+                   (uint64_t)N * 4, oc::kSkCols, 16, CU_TENSOR_MAP_SWIZZLE_NONE) == OC_OK &&
+      make_tmap_2d(&L->tmap_ks, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, scales, (uint64_t)N, (uint64_t)G, (uint64_t)N * 2,
+                   oc::kSkCols, L->gt_rows, CU_TENSOR_MAP_SWIZZLE_NONE) == OC_OK &&
+      make_tmap_2d(&L->tmap_kz, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, qzeros, (uint64_t)(N / 8), (uint64_t)G,
+                   (uint64_t)(N / 8) * 4, oc::kSkCols / 8, L->gt_rows, CU_TENSOR_MAP_SWIZZLE_NONE) == OC_OK)
+    L->sk_ok = 1;
   *out = L;
   return OC_OK;
 }
@@ -546,7 +581,6 @@ int oc_b200_layer_destroy(oc_b200_layer* layer) {
 
 namespace {
 
-constexpr size_t kTicketBytes = 1024;  // 256 tickets: enough for N <= 32768 (128 columns each)
 
 struct GemvPlan {
   int splits, kstep;
@@ -561,32 +595,60 @@ struct GemvPlan {
 int gemv_impl(const oc_b200_layer* L) {
   if (L->wbits == 8) return 1;  // 8-bit layers have only the TMA GEMV
   if (!L->gt_ok) return 2;
-  return g_opt_gemv_impl.load();
+  const int v = g_opt_gemv_impl.load();
+  if (v == 3 && !L->sk_ok) return 1;
+  return v;
+}
+
+// The split-K kernel that runs where the stream-K GEMV does not (the no-allocation entry point,
+// which sizes its fixed scratch for the split-K kernels): the TMA GEMV in its place.
+int legacy_impl(const oc_b200_layer* L) {
+  const int v = gemv_impl(L);
+  return v == 3 ? 1 : v;
+}
+
+// The stream-K GEMV runs decode sizes up to 8 tokens (one token tile); larger M takes the
+// split-K kernel, whose activations come by TMA from the gathered copy.
+bool use_sk(const oc_b200_layer* L, int64_t M) { return gemv_impl(L) == 3 && M <= 8; }
+
+// Stream-K plan: units of 256 columns x 128 k, an equal run per CTA, two CTAs per SM.
+struct SkPlan {
+  int tiles, KB, units, upc, grid;
+};
+SkPlan sk_plan(const oc_b200_layer* L, int dev) {
+  SkPlan q;
+  q.tiles = (L->N + oc::kSkCols - 1) / oc::kSkCols;
+  q.KB = (L->Kp + oc::kSkBK - 1) / oc::kSkBK;
+  q.units = q.tiles * q.KB;
+  const int ctas = 2 * sm_count(dev);  // two CTAs (16 consumer warps) per SM
+  q.upc = (q.units + ctas - 1) / ctas;
+  q.grid = (q.units + q.upc - 1) / q.upc;
+  return q;
 }
 
 GemvPlan gemv_plan(const oc_b200_layer* L, int dev) {
   const int n_tiles = (L->N + oc::kGemvCols - 1) / oc::kGemvCols;
   const int steps = (L->Kp + 31) / 32;
   const int target = sm_count(dev) * g_opt_gemv_ctas.load();
-  if (gemv_impl(L) == 0) {  // tcgen05 GEMV: one CTA per SM, splits in 64-k blocks, at least 4 each
+  if (legacy_impl(L) == 0) {  // tcgen05 GEMV: one CTA per SM, splits in 64-k blocks, at least 4 each
     const int KB = (L->Kp + oc::kVtBK - 1) / oc::kVtBK;
     int splits = sm_count(dev) / n_tiles;
     const int max_splits = KB / 4 > 0 ? KB / 4 : 1;
     if (splits > max_splits) splits = max_splits;
     if (splits < 1) splits = 1;
-    if (n_tiles > (int)(kTicketBytes / 4)) splits = 1;
+    if (n_tiles > kSplitTilesMax) splits = 1;
     const int kbs = (KB + splits - 1) / splits;
     splits = (KB + kbs - 1) / kbs;
     return {splits, kbs * (oc::kVtBK / 32)};
   }
-  if (gemv_impl(L) == 1) {  // TMA GEMV: splits in whole stages (128 k, 64 k for 8-bit), at least two per CTA
+  if (legacy_impl(L) == 1) {  // TMA GEMV: splits in whole stages (128 k, 64 k for 8-bit), at least two per CTA
     const int ks = L->wbits == 8 ? oc::gt_stage_k<8>() : oc::kGtBK;
     const int KB = (L->Kp + ks - 1) / ks;
     int splits = target / n_tiles;
     const int max_splits = KB / 2 > 0 ? KB / 2 : 1;
     if (splits > max_splits) splits = max_splits;
     if (splits < 1) splits = 1;
-    if (n_tiles > (int)(kTicketBytes / 4)) splits = 1;
+    if (n_tiles > kSplitTilesMax) splits = 1;
     const int kbs = (KB + splits - 1) / splits;
     splits = (KB + kbs - 1) / kbs;
     return {splits, kbs * (oc::kGtBK / 32)};
@@ -595,7 +657,7 @@ GemvPlan gemv_plan(const oc_b200_layer* L, int dev) {
   const int max_splits = steps / 8 > 0 ? steps / 8 : 1;
   if (splits > max_splits) splits = max_splits;
   if (splits < 1) splits = 1;
-  if (n_tiles > (int)(kTicketBytes / 4)) splits = 1;
+  if (n_tiles > kSplitTilesMax) splits = 1;
   int kstep = (steps + splits - 1) / splits;
   splits = (steps + kstep - 1) / kstep;
   return {splits, kstep};
@@ -645,6 +707,11 @@ bool layer_gemv(const oc_b200_layer* L, int64_t M) { return use_gemv(M); }
 extern "C" size_t oc_b200_gptq_gemm_workspace(const oc_b200_layer* L, int64_t M) {
   if (!L || M <= 0) return kTicketBytes;
   size_t bytes = kTicketBytes;
+  if (layer_gemv(L, M) && use_sk(L, M)) {  // gathers its own activations
+    const SkPlan q = sk_plan(L, L->device);
+    if (q.grid > 1) bytes += align_up((size_t)(q.tiles + q.grid) * M * oc::kSkCols * 4, 256);
+    return bytes;
+  }
   if (L->kperm) bytes += align_up((size_t)M * L->Kp * 2, 256);  // gathered activations
   if (layer_gemv(L, M)) {
     const GemvPlan gp = gemv_plan(L, L->device);
@@ -746,6 +813,62 @@ int launch_gemv_tma(const oc_b200_layer* L, const oc::GemvParams& p, const GemvP
   return launch_gt_k<oc::gptq_gemv_tma_kernel<BF16, 2>>(oc::GtCfg<2>::kSmemBytes, grid, stream, L, tx, g);
 }
 
+// The stream-K decode GEMV (layers with sk_ok): activations in the caller's K order.
+template <auto Kern>
+int launch_sk_k(dim3 grid, cudaStream_t stream, const oc_b200_layer* L, const oc::SkParams& q) {
+  static bool attr_set[kMaxDevices] = {};
+  int dev = 0;
+  if (int rc = current_device(&dev)) return rc;
+  if (dev >= 0 && dev < kMaxDevices && !attr_set[dev]) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (int rc = cuda_check(cudaFuncSetAttribute(Kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 oc::kSkSmemBytes),
+                            "cudaFuncSetAttribute(gemv sk smem)"))
+      return rc;
+    attr_set[dev] = true;
+  }
+  return launch_pdl(Kern, grid, dim3(oc::kSkThreads), (size_t)oc::kSkSmemBytes, stream, "gptq_gemv_sk", L->tmap_gw,
+                    L->tmap_ks, L->tmap_kz, L->tmap_kp, q);
+}
+
+template <bool BF16>
+int launch_gemv_sk(const oc_b200_layer* L, const void* a, int64_t lda, int64_t M, const void* bias, int bias_dtype,
+                   const void* residual, int64_t ldr, int act, void* c, int64_t ldc, float* ws, unsigned* tickets,
+                   int dev, cudaStream_t stream) {
+  const SkPlan pl = sk_plan(L, dev);
+  oc::SkParams q{};
+  q.x = reinterpret_cast<const uint16_t*>(a);
+  q.ldx = lda;
+  q.M = (int)M;
+  q.kperm = L->kperm;
+  q.K_in = L->K_in;
+  q.Kp = L->Kp;
+  q.N = L->N;
+  q.gs = L->gs;
+  q.v1 = L->v1;
+  q.s_dtype = L->s_dtype;
+  q.rows_sz = L->gt_rows;
+  q.KB = pl.KB;
+  q.units = pl.units;
+  q.upc = pl.upc;
+  q.bias = bias;
+  q.bias_dtype = bias_dtype;
+  q.residual = reinterpret_cast<const uint16_t*>(residual);
+  q.ldr = ldr;
+  q.act = act;
+  q.out = reinterpret_cast<uint16_t*>(c);
+  q.ldc = ldc;
+  q.ws = ws;
+  q.tickets = tickets;
+  const int wait_us = g_opt_wait_us.load();
+  q.wait_ns = wait_us > 0 ? 1000ull * (unsigned long long)wait_us : (unsigned long long)OC_WAIT_NS;
+  q.stall_stage = g_opt_test_stall.load();
+  // M <= 8: one token tile; MMA steps per scale group: 1, 2 or 4 (groups of 32, 64, >= 128 rows)
+  if (L->gs == 32) return launch_sk_k<oc::gptq_gemv_sk_kernel<BF16, 1, 1>>(dim3(pl.grid), stream, L, q);
+  if (L->gs == 64) return launch_sk_k<oc::gptq_gemv_sk_kernel<BF16, 1, 2>>(dim3(pl.grid), stream, L, q);
+  return launch_sk_k<oc::gptq_gemv_sk_kernel<BF16, 1, 4>>(dim3(pl.grid), stream, L, q);
+}
+
 template <bool BF16, bool HAS_LO>
 int launch_gemv(const oc::GemvParams& p, int n_tiles, int splits, cudaStream_t stream) {
   dim3 grid(n_tiles, splits);
@@ -780,12 +903,12 @@ int launch_tc_t(const TcMaps& tm, const oc_b200_layer* L, const oc::TcParams& p,
     attr_set[dev] = true;
   }
   if (CG == 1) {
-    int grid = p.num_tiles < sm_count(dev) ? p.num_tiles : sm_count(dev);
+    int grid = p.num_tiles < tc_ctas(dev) ? p.num_tiles : tc_ctas(dev);
     kern<<<grid, oc::kTcThreads, Cfg::kSmemBytes, stream>>>(tm.x, L->tmap_w, L->tmap_s, L->tmap_z, tm.c, tm.r, p);
     return launch_check("gptq_gemm_tc");
   }
   // CTA pairs: clusters of two, one pair tile (256 features) at a time
-  const int pairs = sm_count(dev) / 2;
+  const int pairs = tc_ctas(dev) / 2 > 0 ? tc_ctas(dev) / 2 : 1;
   const int grid = 2 * (p.num_tiles < pairs ? p.num_tiles : pairs);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
@@ -857,6 +980,15 @@ extern "C" int oc_b200_gptq_gemm_ex(const oc_b200_layer* L, const void* a, int a
   unsigned* tickets = reinterpret_cast<unsigned*>(ws);
   size_t off = kTicketBytes;
 
+  if (layer_gemv(L, M) && use_sk(L, M)) {
+    float* part = reinterpret_cast<float*>(ws + off);
+    return a_dtype == OC_DT_BF16
+               ? launch_gemv_sk<true>(L, a, lda, M, bias, bias_dtype, residual, ldr, act, c, ldc, part, tickets, dev,
+                                      stream)
+               : launch_gemv_sk<false>(L, a, lda, M, bias, bias_dtype, residual, ldr, act, c, ldc, part, tickets, dev,
+                                       stream);
+  }
+
   // activations in kernel K order
   const uint16_t* xk = reinterpret_cast<const uint16_t*>(a);
   int64_t ldx = lda;
@@ -898,9 +1030,9 @@ extern "C" int oc_b200_gptq_gemm_ex(const oc_b200_layer* L, const void* a, int a
     p.splits = gp.splits;
     p.kstep_per_split = gp.kstep;
     const int n_tiles = (L->N + oc::kGemvCols - 1) / oc::kGemvCols;
-    if (gemv_impl(L) == 0)
+    if (legacy_impl(L) == 0)
       return bf16 ? launch_gemv_tcv<true>(L, p, gp, n_tiles, stream) : launch_gemv_tcv<false>(L, p, gp, n_tiles, stream);
-    if (gemv_impl(L) == 1)
+    if (legacy_impl(L) == 1)
       return bf16 ? launch_gemv_tma<true>(L, p, gp, n_tiles, stream) : launch_gemv_tma<false>(L, p, gp, n_tiles, stream);
     if (bf16) return has_lo ? launch_gemv<true, true>(p, n_tiles, gp.splits, stream)
                             : launch_gemv<true, false>(p, n_tiles, gp.splits, stream);
@@ -1162,7 +1294,7 @@ int launch_rows_t(const CUtensorMap& tx, const oc::RowsParams& p, int dev, cudaS
   // upper bound on tiles: every expert segment adds at most one partial m-tile
   const long long m_tiles = ((long long)p.M + BT - 1) / BT + (p.offsets ? p.E : 0);
   const long long tiles = m_tiles * p.n_tiles_n;
-  const int grid = tiles < sm_count(dev) ? (int)tiles : sm_count(dev);
+  const int grid = tiles < tc_ctas(dev) ? (int)tiles : tc_ctas(dev);
   kern<<<grid, oc::kRowsThreads, Cfg::kSmemBytes, stream>>>(tx, p);
   return launch_check("rows_gemm_tc");
 }
@@ -1352,9 +1484,9 @@ extern "C" int oc_b200_gptq_gemv_noalloc(const oc_b200_layer* L, const void* a, 
   const int n_tiles = (L->N + oc::kGemvCols - 1) / oc::kGemvCols;
   const bool bf16 = a_dtype == OC_DT_BF16;
   const bool has_lo = L->s_dtype != a_dtype;
-  if (gemv_impl(L) == 0)
+  if (legacy_impl(L) == 0)
     return bf16 ? launch_gemv_tcv<true>(L, p, gp, n_tiles, stream) : launch_gemv_tcv<false>(L, p, gp, n_tiles, stream);
-  if (gemv_impl(L) == 1)
+  if (legacy_impl(L) == 1)
     return bf16 ? launch_gemv_tma<true>(L, p, gp, n_tiles, stream) : launch_gemv_tma<false>(L, p, gp, n_tiles, stream);
   if (bf16) return has_lo ? launch_gemv<true, true>(p, n_tiles, gp.splits, stream)
                           : launch_gemv<true, false>(p, n_tiles, gp.splits, stream);

@@ -25,6 +25,7 @@ OPT_GEMV_IMPL = 4
 OPT_TC_PAIR = 5
 OPT_WAIT_US = 6
 OPT_TEST_STALL = 7
+OPT_TC_MAX_CTAS = 8
 ACT_NONE = 0
 ACT_GELU_TANH = 1
 
@@ -154,7 +155,7 @@ def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
     """A zero-initialised byte buffer per (device, current stream), grown on demand.
 
     Kernels on one stream run in order, so layers share it; the split-K tickets
-    in its first KiB are left at zero by every call.
+    in its first 8 KiB are left at zero by every call.
     """
     idx = device.index if device.index is not None else torch.cuda.current_device()
     key = (idx, stream_of(device))

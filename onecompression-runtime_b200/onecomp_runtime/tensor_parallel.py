@@ -12,9 +12,12 @@ star asks for on the video-DiT stack:
   chunk's GEMM writing straight into its rows of the output, and issues an
   asynchronous all-reduce (sum, bf16) per chunk, so the reduction of chunk i
   overlaps the GEMM of chunk i+1; the current stream waits on every chunk's
-  reduction before returning. A residual (the DiT block's skip connection) is
-  added in rank 0's GEMM epilogue before the reduction, so the sum carries it
-  once and no separate elementwise pass runs;
+  reduction before returning. ``forward_async`` does one chunk without the wait,
+  for callers that pipeline whole blocks chunk by chunk (the reduction of one
+  chunk then overlaps the following layers' GEMMs of the other chunks). A
+  residual (the DiT block's skip connection) is added in rank 0's GEMM epilogue
+  before the reduction, so the sum carries it once and no separate elementwise
+  pass runs;
 * ``ColumnParallelInt4Linear.forward(x, activation=...)`` applies an elementwise
   activation (tanh-GELU) in the GEMM epilogue: the shard's outputs are whole
   features, so the activation needs no communication.
@@ -103,6 +106,34 @@ class RowParallelInt4Linear(torch.nn.Module):
         self.group = group
         self.chunks = max(1, int(chunks))
 
+    def _local_into(self, x: torch.Tensor, out: torch.Tensor, residual: torch.Tensor | None) -> None:
+        """out = x @ W_shard.T (+ bias on rank 0) (+ residual), written in place."""
+        if hasattr(self.local, "_gemm_2d") and x.dtype in (torch.float16, torch.bfloat16):
+            if x.stride(1) != 1 or x.data_ptr() % 16 or x.stride(0) % 8:
+                x = x.contiguous()
+            self.local._gemm_2d(x, out, residual)   # residual in the GEMM epilogue
+        else:
+            out.copy_(self.local(x) if residual is None else self.local(x) + residual)
+
+    def forward_async(self, x: torch.Tensor, residual: torch.Tensor | None = None,
+                      out: torch.Tensor | None = None):
+        """Start ``all_reduce(x_shard @ W_shard.T) + bias + residual`` for one chunk of rows.
+
+        Runs the local GEMM on the current stream into ``out`` (allocated when None) and issues its
+        all-reduce without waiting, so the caller can queue the next chunk's (or the next layer's)
+        GEMMs while the reduction crosses NVLink. Returns ``(out, work)``: ``work.wait()`` (None for
+        one rank) orders the current stream after the reduction; ``out`` must not be read before.
+        The residual is added by rank 0 only, so the sum carries it once.
+        """
+        if out is None:
+            out = torch.empty((x.shape[0], self.local.out_features), dtype=x.dtype, device=x.device)
+        world = dist.get_world_size(self.group) if dist.is_initialized() else 1
+        rank = dist.get_rank(self.group) if world > 1 else 0
+        self._local_into(x, out, residual if rank == 0 else None)
+        if world == 1:
+            return out, None
+        return out, dist.all_reduce(out, op=dist.ReduceOp.SUM, group=self.group, async_op=True)
+
     def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
         """``all_reduce(x_shard @ W_shard.T) + bias + residual``; ``residual`` [M, N] (optional)."""
         M = x.shape[0]
@@ -111,22 +142,13 @@ class RowParallelInt4Linear(torch.nn.Module):
             if residual is None:
                 return self.local(x)
             return self.local.forward_fused(x, residual=residual)
-        rank = dist.get_rank(self.group)
-        fused = hasattr(self.local, "_gemm_2d") and x.dtype in (torch.float16, torch.bfloat16)
         out = torch.empty((M, self.local.out_features), dtype=x.dtype, device=x.device)
         step = (M + self.chunks - 1) // self.chunks
         works = []
         for c0 in range(0, M, step):
             c1 = min(M, c0 + step)
-            res = residual[c0:c1] if (residual is not None and rank == 0) else None
-            if fused:
-                xc = x[c0:c1]
-                if xc.stride(1) != 1 or xc.data_ptr() % 16 or xc.stride(0) % 8:
-                    xc = xc.contiguous()
-                self.local._gemm_2d(xc, out[c0:c1], res)   # written in place, residual in the epilogue
-            else:
-                out[c0:c1] = self.local(x[c0:c1]) if res is None else self.local(x[c0:c1]) + res
-            works.append(dist.all_reduce(out[c0:c1], op=dist.ReduceOp.SUM, group=self.group, async_op=True))
+            res = residual[c0:c1] if residual is not None else None
+            works.append(self.forward_async(x[c0:c1], res, out[c0:c1])[1])
         for w in works:
             w.wait()
         return out

@@ -58,7 +58,7 @@ def test_null_arguments_rejected_before_any_launch(lib):
     rc = lib.oc_b200_gptq_layer_create(None, None, None, 0, None, None, 64, 64, 64, 2, 32, 1, ctypes.byref(out))
     assert rc == 1
     assert lib.oc_b200_gptq_gemm(None, None, 1, 1, 64, None, 0, None, 64, None, 0, None) == 1
-    assert lib.oc_b200_gptq_gemm_workspace(None, 4) == 1024
+    assert lib.oc_b200_gptq_gemm_workspace(None, 4) == 8192   # the ticket area alone
 
 
 def test_layer_create_ex_validation(lib):

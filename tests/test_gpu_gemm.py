@@ -318,14 +318,20 @@ GEMV_IMPL_SHAPES = [
     (16, 2176, 512, 128, False, True, torch.float16),
     (2, 6144, 256, 512, True, False, torch.float16),     # a group spans 4 stages
     (5, 4160, 384, 64, True, False, torch.bfloat16),     # K not a multiple of the 128-k stage
+    (4, 5120, 17408, 128, False, True, torch.float16),   # config-2 gate shape: several activation pieces
+    (13, 8192, 2048, 64, True, False, torch.bfloat16),   # two token tiles, two groups per stage
+    (1, 256, 256, 128, False, True, torch.float16),      # fewer units than SMs
+    (16, 17408, 512, 128, True, False, torch.float16),   # a run spans many K stages of one tile
 ]
 
 
-@pytest.mark.parametrize("impl", [0, 1, 2])
+@pytest.mark.parametrize("impl", [0, 1, 2, 3])
 @pytest.mark.parametrize("shape", GEMV_IMPL_SHAPES, ids=lambda s: f"M{s[0]}K{s[1]}N{s[2]}g{s[3]}")
 def test_gemv_impls(cuda_device, impl, shape):
-    """The three decode kernels for uniform-group layers (tcgen05, TMA + mma.sync, cp.async +
-    mma.sync) against the fp64 GEMM of the exact weight, with a residual + GELU epilogue."""
+    """The four decode kernels for uniform-group layers (tcgen05, TMA + mma.sync split-K, cp.async
+    + mma.sync, stream-K with the act-order gather inside; layers narrower than 256 columns run
+    the split-K TMA kernel under 3) against the fp64 GEMM of the exact weight, with a residual +
+    GELU epilogue."""
     from onecomp_runtime import _lib
     from onecomp_runtime.testing import gptq_layer, activations
     M, K, N, gs, v1, act, sdt = shape
@@ -334,12 +340,13 @@ def test_gemv_impls(cuda_device, impl, shape):
     layer = _module(t, K, N, gs, v1, "packed" if act else ("fused" if gs == 32 else "any"), cuda_device)
     x = activations(M, K, seed=M).to(cuda_device)
     r = activations(M, N, seed=M + 3).to(cuda_device)
+    saved = _lib.get_option(_lib.OPT_GEMV_IMPL)
     _lib.set_option(_lib.OPT_GEMV_IMPL, impl)
     try:
         y = layer(x)
         yf = layer.forward_fused(x, residual=r, activation="gelu_tanh")
     finally:
-        _lib.set_option(_lib.OPT_GEMV_IMPL, 1)
+        _lib.set_option(_lib.OPT_GEMV_IMPL, saved)
     ref = _gpu_reference(t, K, N, x, v1, t["bias"])
     err = float((y.double() - ref).abs().max() / ref.abs().max())
     assert err < 1e-2, err

@@ -25,41 +25,49 @@ def _layer(device):
     return PackedGPTQLinear(K, N, t["qweight"], t["scales"], t["qzeros"], t["g_idx"], t["bias"], 128, 4, False)
 
 
-def _stalled(run, device):
-    """Run `run()` with the stall options set, restoring the previous option values."""
+def _with_impl(impl, run, device, stall: bool):
+    """Run `run()` on decode kernel `impl` (1: split-K TMA GEMV, 3: stream-K GEMV), with the stall
+    options set when `stall`, restoring the previous option values. Returns the device error word."""
     from onecomp_runtime import _lib
     keys = (_lib.OPT_WAIT_US, _lib.OPT_TEST_STALL, _lib.OPT_GEMV_IMPL, _lib.OPT_GEMM_PATH)
     saved = {k: _lib.get_option(k) for k in keys}
     try:
-        _lib.set_option(_lib.OPT_GEMV_IMPL, 1)    # the TMA decode GEMV
+        _lib.set_option(_lib.OPT_GEMV_IMPL, impl)
         _lib.set_option(_lib.OPT_GEMM_PATH, 0)
-        _lib.set_option(_lib.OPT_WAIT_US, 20000)  # 20 ms
-        _lib.set_option(_lib.OPT_TEST_STALL, 1)   # stage 0 of CTA (0, 0) is never issued
-        run()
+        if stall:
+            _lib.set_option(_lib.OPT_WAIT_US, 20000)  # 20 ms
+            _lib.set_option(_lib.OPT_TEST_STALL, 1)   # the first stage of the first CTA is never issued
+        out = run()
         torch.cuda.synchronize(device)
     finally:
         for k, v in saved.items():
             _lib.set_option(k, v)
-    return _lib.read_device_error(device)
+    return out, _lib.read_device_error(device)
 
 
-def test_wait_runs_out_then_workspace_calls_are_exact(cuda_device):
+def _stalled(run, device):
+    return _with_impl(1, run, device, stall=True)[1]
+
+
+# Columns the first CTA's failure leaves unwritten: split-K (impl 1) one 128-column tile; stream-K
+# (impl 3) the 256-column tile its run starts in (5120 x 1024 at gs128: 160 units, 2 per CTA).
+@pytest.mark.parametrize("impl,cols", [(1, 128), (3, 256)])
+def test_wait_runs_out_then_workspace_calls_are_exact(cuda_device, impl, cols):
     from onecomp_runtime import _lib
     from onecomp_runtime.testing import activations
     layer = _layer(cuda_device)
     x = activations(1, layer.in_features, seed=5).to(cuda_device)
-    ref = layer(x)
-    torch.cuda.synchronize(cuda_device)
-    assert _lib.read_device_error(cuda_device) == 0
+    ref, code = _with_impl(impl, lambda: layer(x), cuda_device, stall=False)
+    assert code == 0
     out = torch.full_like(ref, float("nan"))
-    code = _stalled(lambda: layer._gemm_2d(x, out), cuda_device)
+    _, code = _with_impl(impl, lambda: layer._gemm_2d(x, out), cuda_device, stall=True)
     assert code == WFULL, hex(code)
-    assert torch.isnan(out[:, :128].float()).all()          # the failed tile is not written
-    torch.testing.assert_close(out[:, 128:], ref[:, 128:], rtol=0, atol=0)
+    assert torch.isnan(out[:, :cols].float()).all()          # the failed tile is not written
+    torch.testing.assert_close(out[:, cols:], ref[:, cols:], rtol=0, atol=0)
     for _ in range(2):                                     # same workspace, tickets re-armed
-        torch.testing.assert_close(layer(x), ref, rtol=0, atol=0)
-    torch.cuda.synchronize(cuda_device)
-    assert _lib.read_device_error(cuda_device) == 0
+        y, code = _with_impl(impl, lambda: layer(x), cuda_device, stall=False)
+        assert code == 0
+        torch.testing.assert_close(y, ref, rtol=0, atol=0)
 
 
 def test_wait_runs_out_then_noalloc_calls_are_exact(cuda_device):
@@ -67,7 +75,7 @@ def test_wait_runs_out_then_noalloc_calls_are_exact(cuda_device):
     from onecomp_runtime.testing import activations
     layer = _layer(cuda_device)
     x = activations(1, layer.in_features, seed=6).to(cuda_device)
-    ref = layer(x)
+    ref, _ = _with_impl(1, lambda: layer(x), cuda_device, stall=False)   # the kernel the no-alloc entry runs
     h = layer._get_handle()
     bias = layer.bias
 

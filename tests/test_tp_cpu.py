@@ -74,6 +74,27 @@ def _block_forward_fused(blk, x, local_q):
     return blk["fc2"](f, residual=h)
 
 
+def _block_forward_pipelined(blk, x, local_q, chunks):
+    """The fused block pipelined over row chunks with forward_async: every chunk's out-projection
+    reduction is started before any is waited for, then fc1 / fc2 per chunk."""
+    step = (x.shape[0] + chunks - 1) // chunks
+    xs = [x[c0:c0 + step] for c0 in range(0, x.shape[0], step)]
+    qkv = [blk["qkv"](xc) for xc in xs]
+    pend = [blk["out"].forward_async(q[:, :local_q], residual=xc) for q, xc in zip(qkv, xs)]
+    pend2 = []
+    for o, w in pend:
+        if w is not None:
+            w.wait()
+        f = blk["fc1"](o, activation="gelu_tanh")
+        pend2.append(blk["fc2"].forward_async(f, residual=o))
+    ys = []
+    for o, w in pend2:
+        if w is not None:
+            w.wait()
+        ys.append(o)
+    return torch.cat(ys)
+
+
 def _worker(rank, world, port, out_path):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -84,8 +105,9 @@ def _worker(rank, world, port, out_path):
     x = torch.randn(10, 256, generator=torch.Generator().manual_seed(0))
     y = _block_forward(blk, x, 256, 256 // world)
     y_fused = _block_forward_fused(blk, x, 256 // world)
+    y_pipe = _block_forward_pipelined(blk, x, 256 // world, chunks=3)
     if rank == 0:
-        torch.save((y, y_fused), out_path)
+        torch.save((y, y_fused, y_pipe), out_path)
     dist.barrier()
     dist.destroy_process_group()
 
@@ -94,7 +116,7 @@ def test_tp_block_matches_single_rank(tmp_path):
     world = 2
     out = tmp_path / "y.pt"
     mp.spawn(_worker, args=(world, _free_port(), str(out)), nprocs=world, join=True)
-    y_tp, y_tp_fused = torch.load(out)
+    y_tp, y_tp_fused, y_tp_pipe = torch.load(out)
     tens = _tensors()
     full = {name: OracleLinear(tens[name], K, N, GS) for name, K, N in LAYERS}
     x = torch.randn(10, 256, generator=torch.Generator().manual_seed(0))
@@ -102,6 +124,8 @@ def test_tp_block_matches_single_rank(tmp_path):
     torch.testing.assert_close(y_tp, y_ref, rtol=1e-4, atol=1e-4)
     # residual added once (rank 0's epilogue) before the reduction, GELU in the column shard
     torch.testing.assert_close(y_tp_fused, y_ref, rtol=1e-4, atol=1e-4)
+    # chunk pipeline: reductions started per chunk and waited for later give the same block
+    torch.testing.assert_close(y_tp_pipe, y_ref, rtol=1e-4, atol=1e-4)
 
 
 def test_column_and_row_shards_cover_the_layer():

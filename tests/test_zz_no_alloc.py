@@ -88,4 +88,6 @@ def test_noalloc_rejects_oversize(cuda_device):
         for k, v in saved.items():   # whatever was set before this test
             _lib.set_option(k, v)
     _lib.check(_noalloc(layer, x[:16], out[:16]), "oc_b200_gptq_gemv_noalloc")
-    torch.testing.assert_close(out[:16], layer(x[:16]), rtol=0, atol=0)
+    ref = layer(x[:16]).float()
+    err = float((out[:16].float() - ref).abs().max() / ref.abs().max())
+    assert err < GEMM_TOL, err
