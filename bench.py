@@ -388,10 +388,20 @@ def cpu_baseline_cfg4(args) -> dict:
 class TPStack:
     """12 video-DiT blocks of B200 int4 linears sharded over the job's ranks."""
 
-    def __init__(self, job: Job, blocks: int, timer: LaunchTimer, chunks: int = 1):
+    def __init__(self, job: Job, blocks: int, timer: LaunchTimer, chunks: int = 1, reduce: str = "nccl",
+                 M: int = 0):
         from onecomp_runtime.layers import FusedInt4Linear
-        from onecomp_runtime.tensor_parallel import build_tp_block
+        from onecomp_runtime.tensor_parallel import NvlsReducer, build_tp_block
         self.chunks = max(1, chunks)
+        self.reducers = None
+        self.reduce = "none" if job.world == 1 else "nccl"
+        if job.world > 1 and reduce == "nvls":
+            try:   # two symmetric buffers: out-projection and fc2 partial outputs
+                from onecomp_runtime.testing import CFG4
+                self.reducers = (NvlsReducer(M, CFG4["hidden"]), NvlsReducer(M, CFG4["hidden"]))
+                self.reduce = "nvls"
+            except RuntimeError as e:
+                print(f"[bench] NVLS all-reduce unavailable ({e}); using NCCL", file=sys.stderr)
         from onecomp_runtime.testing import CFG4, CFG4_LAYERS, gptq_layer
         self.gs, self.H = CFG4["gs"], CFG4["hidden"]
         self.hq = self.H // job.world
@@ -415,17 +425,22 @@ class TPStack:
         while the following chunks' GEMMs run."""
         M = h.shape[0]
         step = (M + self.chunks - 1) // self.chunks
-        hs = [h[c0:c0 + step] for c0 in range(0, M, step)]
+        spans = [(c0, min(M, c0 + step)) for c0 in range(0, M, step)]
+        hs = [h[c0:c1] for c0, c1 in spans]
+        r1, r2 = self.reducers if self.reducers else (None, None)
         qkv = [self.blocks[0]["qkv"](hc) for hc in hs]
         for b, blk in enumerate(self.blocks):
-            pend = [blk["out"].forward_async(q[:, :self.hq], residual=hc) for q, hc in zip(qkv, hs)]
+            pend = [blk["out"].forward_async(q[:, :self.hq], residual=hc, out=r1.view(c0, c1) if r1 else None,
+                                             reducer=r1)
+                    for q, hc, (c0, c1) in zip(qkv, hs, spans)]
             pend2 = []
-            for o, w in pend:
+            for (o, w), (c0, c1) in zip(pend, spans):
                 if w is not None:
                     w.wait()
                 hn = rms_norm(o)
                 f = blk["fc1"](hn, activation="gelu_tanh")
-                pend2.append(blk["fc2"].forward_async(f, residual=hn))
+                pend2.append(blk["fc2"].forward_async(f, residual=hn, out=r2.view(c0, c1) if r2 else None,
+                                                      reducer=r2))
             nxt = self.blocks[b + 1] if b + 1 < len(self.blocks) else None
             hs, qkv = [], []
             for o, w in pend2:
@@ -438,15 +453,19 @@ class TPStack:
         return hs[0] if len(hs) == 1 else torch.cat(hs)
 
 
-def allreduce_alone(job: Job, M: int, H: int, per_step: int, chunks: int) -> float:
-    """Milliseconds of one step's row-parallel all-reduces issued back to back (no GEMMs)."""
-    buf = torch.zeros((M, H), dtype=torch.bfloat16, device=job.dev)
+def allreduce_alone(job: Job, M: int, H: int, per_step: int, chunks: int, reducer=None) -> float:
+    """Milliseconds of one step's row-parallel all-reduces issued back to back (no GEMMs): NCCL, or
+    the NVLS kernel on the reducer's symmetric buffer."""
+    buf = reducer.buffer if reducer is not None else torch.zeros((M, H), dtype=torch.bfloat16, device=job.dev)
     step = (M + chunks - 1) // chunks
 
     def once():
         for _ in range(per_step):
             for c0 in range(0, M, step):
-                torch.distributed.all_reduce(buf[c0:c0 + step])
+                if reducer is not None:
+                    reducer.all_reduce_async(buf[c0:c0 + step]).wait()
+                else:
+                    torch.distributed.all_reduce(buf[c0:c0 + step])
 
     once()
     ms, _ = timed_steps(job, once, 3, 1, clocks=False)
@@ -461,7 +480,8 @@ def bench_cfg4(args, job: Job, peaks: dict, with_cpu: bool) -> dict:
         from onecomp_runtime import _lib
         _lib.set_option(_lib.OPT_TC_MAX_CTAS, args.tc_max_ctas)
     chunks = args.tp_chunks if args.tp_chunks > 0 else (4 if job.world > 1 else 1)
-    stack = TPStack(job, blocks, timer, chunks)
+    reduce = args.tp_reduce if args.tp_reduce != "auto" else ("nvls" if job.world >= 4 else "nccl")
+    stack = TPStack(job, blocks, timer, chunks, reduce, M)
     x = torch.randn((M, H), generator=torch.Generator(device=job.dev).manual_seed(5), device=job.dev).to(torch.bfloat16)
     with torch.no_grad():
         y = stack.forward(x)
@@ -483,6 +503,8 @@ def bench_cfg4(args, job: Job, peaks: dict, with_cpu: bool) -> dict:
                        "parallelism": f"tp{job.world} (column qkv/fc1, row out/fc2 + NCCL all-reduce)"
                        if job.world > 1 else "tp1 (one GPU, no collective)",
                        "pipeline_chunks": stack.chunks,
+                       "allreduce": {"nvls": "own NVLS kernel (multimem.ld_reduce / multimem.st)",
+                                     "nccl": "NCCL", "none": "none"}[stack.reduce],
                        "gemm_ctas": args.tc_max_ctas if (job.world > 1 and args.tc_max_ctas) else "one per SM",
                        "l2_flush": "none needed: weights (1.4 GB packed) and activations exceed the 126 MB L2"},
             "e2e": {"value": round(M * args.steps / (ms_e2e / 1e3), 1), "unit": "tokens/s",
@@ -494,15 +516,16 @@ def bench_cfg4(args, job: Job, peaks: dict, with_cpu: bool) -> dict:
                                         ms * args.steps, args.steps),
             "tflops_step": round(flops_step / (ms / 1e3) / 1e12, 1),
             "clocks": clk}
-    del stack
-    torch.cuda.empty_cache()
     if job.world > 1:
-        ar_ms = allreduce_alone(job, M, H, 2 * blocks, 4)
+        ar_ms = allreduce_alone(job, M, H, 2 * blocks, stack.chunks, stack.reducers[0] if stack.reducers else None)
         nbytes = 2 * blocks * M * H * 2
         line["comm"] = {"allreduce_ms_per_step_alone": round(ar_ms, 3), "allreduce_bytes_per_step": nbytes,
+                        "allreduce": line["config"]["allreduce"],
                         "busbw_GBs": round(nbytes * 2 * (job.world - 1) / job.world / (ar_ms / 1e3) / 1e9, 1),
                         "alone_over_step": round(ar_ms / ms, 4),
                         "note": "the step overlaps each chunk's reduction with the next chunk's GEMM"}
+    del stack
+    torch.cuda.empty_cache()
     if with_cpu:
         line["cpu_baseline"] = cpu_baseline_cfg4(args)
     return line
@@ -762,6 +785,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--tp-chunks", type=int, default=0,
                     help="cfg4: row chunks of the pipelined stack (0 = 4 with N > 1, 1 on one GPU)")
+    ap.add_argument("--tp-reduce", default="auto", choices=["auto", "nvls", "nccl"],
+                    help="cfg4 with N > 1: all-reduce of the row-parallel outputs (own NVLS kernel or NCCL; "
+                         "auto = NVLS from 4 ranks, where it measured faster, NCCL on 2)")
     ap.add_argument("--tc-max-ctas", type=int, default=0,
                     help="cfg4 with N > 1: CTAs of the persistent GEMMs (0 = one per SM), SMs left to NCCL")
     args = ap.parse_args()

@@ -234,6 +234,21 @@ int oc_b200_silu_mul(const void* g, const void* u, int64_t ld_in, int P, int F, 
 int oc_b200_moe_combine(const void* y, int64_t ldy, const int32_t* slot_pos, const float* w, int T, int k, int H,
                         const void* shared, int64_t lds, void* out, int64_t ldo, int dtype, oc_stream_t stream);
 
+/* ---- tensor-parallel reduction ---------------------------------------------
+ * Sum over the `world` ranks of a job of n_elems bf16 values (n_elems % 8 == 0) held in one NVLink
+ * multicast object, in place: afterwards every rank's copy holds the sum as the NVLink switch adds
+ * bf16 (within one bf16 ulp of the exact sum; not always the nearest value). mc_ptr is the multicast address of the first element (16-byte aligned).
+ * flags_dev points to a device array of `world` pointers, one per rank, to that rank's flag array
+ * of at least 2 * blocks * world zero-initialised uint32 words visible to every rank (symmetric
+ * memory); `epoch` must grow by at least one with every call on the same flag arrays, and every
+ * rank makes the same calls in the same order with the same `blocks` (1..64). Stream-ordered; a
+ * rank that does not arrive within the wait bound (OC_OPT_WAIT_US, default 2 s) makes the kernel
+ * record a device error (oc_b200_read_device_error) and return without writing.
+ * No reference counterpart (the reference has no distributed code); it replaces the NCCL
+ * all-reduce after each row-parallel linear of the tensor-parallel DiT stack. */
+int oc_b200_nvls_allreduce_bf16(void* mc_ptr, int64_t n_elems, void* const* flags_dev, int rank, int world,
+                                uint32_t epoch, int blocks, oc_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

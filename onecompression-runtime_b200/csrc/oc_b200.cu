@@ -20,6 +20,7 @@
 #include "gemv_tma.cuh"
 #include "gemv_tc.cuh"
 #include "gemv_sk.cuh"
+#include "allreduce.cuh"
 #include "moe.cuh"
 
 namespace {
@@ -258,6 +259,31 @@ int oc_b200_read_device_error(int* code, oc_stream_t stream) {
   if (rc) return rc;
   *code = (int)v;
   return OC_OK;
+}
+
+// ---------------------------------------------------------------- NVLS all-reduce
+int oc_b200_nvls_allreduce_bf16(void* mc_ptr, int64_t n_elems, void* const* flags_dev, int rank, int world,
+                                uint32_t epoch, int blocks, oc_stream_t stream_) {
+  if (!mc_ptr || !flags_dev) return fail(OC_ERR_INVALID, "nvls_allreduce: NULL pointer");
+  if (n_elems < 0 || n_elems % 8 != 0 || !aligned(mc_ptr, 16))
+    return fail(OC_ERR_INVALID, "nvls_allreduce: %lld elements at %p (needs 16-byte vectors)", (long long)n_elems,
+                mc_ptr);
+  if (world < 1 || world > oc::kArMaxWorld || rank < 0 || rank >= world)
+    return fail(OC_ERR_INVALID, "nvls_allreduce: rank %d of %d (at most %d ranks)", rank, world, oc::kArMaxWorld);
+  if (blocks < 1 || blocks > oc::kArMaxBlocks)
+    return fail(OC_ERR_INVALID, "nvls_allreduce: blocks=%d (1..%d)", blocks, oc::kArMaxBlocks);
+  if (n_elems == 0) return OC_OK;
+  oc::ArParams p{};
+  p.mc = reinterpret_cast<uint4*>(mc_ptr);
+  p.n16 = n_elems / 8;
+  p.flags = reinterpret_cast<uint32_t* const*>(flags_dev);
+  p.rank = rank;
+  p.world = world;
+  p.epoch = epoch;
+  const int wait_us = g_opt_wait_us.load();
+  p.wait_ns = wait_us > 0 ? 1000ull * (unsigned long long)wait_us : (unsigned long long)OC_WAIT_NS;
+  oc::nvls_allreduce_bf16_kernel<<<blocks, oc::kArThreads, 0, reinterpret_cast<cudaStream_t>(stream_)>>>(p);
+  return launch_check("nvls_allreduce_bf16");
 }
 
 // ---------------------------------------------------------------- unpack / pack / dequant

@@ -94,6 +94,72 @@ class ColumnParallelInt4Linear(torch.nn.Module):
         return self.local.forward_fused(x, activation=activation)
 
 
+class _Pending:
+    """An all-reduce started on a side stream: ``wait()`` orders the current stream after it."""
+
+    def __init__(self, done: torch.cuda.Event):
+        self.done = done
+
+    def wait(self) -> None:
+        torch.cuda.current_stream().wait_event(self.done)
+
+
+class NvlsReducer:
+    """In-place sum over the group's ranks of row ranges of one symmetric bf16 buffer, through
+    NVLink SHARP: the library's own kernel (``oc_b200_nvls_allreduce_bf16``) reads each rank's
+    slice with ``multimem.ld_reduce`` and writes the sum to every rank with ``multimem.st``.
+
+    ``buffer`` ([rows, cols] bf16) is allocated as symmetric memory (one NVLink multicast object
+    across the group); the row-parallel GEMMs write their partial outputs straight into row ranges
+    of it (``view``), and ``all_reduce_async`` reduces such a range on a side stream, ordered after
+    the current stream's work, returning a handle whose ``wait()`` orders the current stream after
+    the reduction. Every rank must make the same calls in the same order. Raises at construction
+    when the devices offer no multicast (then use NCCL: ``RowParallelInt4Linear`` without a reducer).
+    """
+
+    def __init__(self, rows: int, cols: int, group=None, blocks: int = 32):
+        import torch.distributed._symmetric_memory as symm
+        from . import _lib
+        self._lib = _lib
+        self.group = group if group is not None else dist.group.WORLD
+        self.world = dist.get_world_size(self.group)
+        self.rank = dist.get_rank(self.group)
+        self.blocks = int(blocks)
+        dev = torch.device("cuda", torch.cuda.current_device())
+        if not symm._SymmetricMemory.has_multicast_support(symm.DeviceType.CUDA, dev.index):
+            raise RuntimeError("NvlsReducer: these GPUs offer no NVLink multicast (NVLS)")
+        self.buffer = symm.empty((rows, cols), dtype=torch.bfloat16, device=dev)
+        self._h = symm.rendezvous(self.buffer, self.group)
+        self._mc = int(self._h.multicast_ptr)
+        if self._mc == 0:
+            raise RuntimeError("NvlsReducer: the symmetric buffer has no multicast mapping")
+        self.flags = symm.empty((2 * self.blocks * self.world,), dtype=torch.int32, device=dev)
+        self.flags.zero_()
+        self._fh = symm.rendezvous(self.flags, self.group)
+        self._flag_ptrs = int(self._fh.buffer_ptrs_dev)
+        self.epoch = 0
+        self.stream = torch.cuda.Stream(dev)
+        torch.cuda.synchronize(dev)
+        dist.barrier(group=self.group)  # every rank's flags are zero before any reduction starts
+
+    def view(self, r0: int, r1: int) -> torch.Tensor:
+        return self.buffer[r0:r1]
+
+    def all_reduce_async(self, t: torch.Tensor) -> _Pending:
+        """Sum ``t`` (a row range of ``buffer``) over the ranks, in place, on the side stream."""
+        off = t.data_ptr() - self.buffer.data_ptr()
+        if not (t.is_contiguous() and 0 <= off and off + t.numel() * 2 <= self.buffer.numel() * 2):
+            raise ValueError("NvlsReducer: the tensor must be a contiguous row range of the buffer")
+        self.epoch += 1
+        cur = torch.cuda.current_stream()
+        self.stream.wait_stream(cur)
+        self._lib.call("oc_b200_nvls_allreduce_bf16", self._mc + off, t.numel(), self._flag_ptrs, self.rank,
+                       self.world, self.epoch & 0xFFFFFFFF, self.blocks, self.stream.cuda_stream)
+        done = torch.cuda.Event()
+        done.record(self.stream)
+        return _Pending(done)
+
+
 class RowParallelInt4Linear(torch.nn.Module):
     """Local row shard followed by an all-reduce (sum) of the partial outputs.
 
@@ -116,14 +182,16 @@ class RowParallelInt4Linear(torch.nn.Module):
             out.copy_(self.local(x) if residual is None else self.local(x) + residual)
 
     def forward_async(self, x: torch.Tensor, residual: torch.Tensor | None = None,
-                      out: torch.Tensor | None = None):
+                      out: torch.Tensor | None = None, reducer: "NvlsReducer | None" = None):
         """Start ``all_reduce(x_shard @ W_shard.T) + bias + residual`` for one chunk of rows.
 
         Runs the local GEMM on the current stream into ``out`` (allocated when None) and issues its
         all-reduce without waiting, so the caller can queue the next chunk's (or the next layer's)
         GEMMs while the reduction crosses NVLink. Returns ``(out, work)``: ``work.wait()`` (None for
         one rank) orders the current stream after the reduction; ``out`` must not be read before.
-        The residual is added by rank 0 only, so the sum carries it once.
+        The residual is added by rank 0 only, so the sum carries it once. With a ``reducer``,
+        ``out`` is a row range of its symmetric buffer and the sum runs on NVLink SHARP
+        (``NvlsReducer``) instead of NCCL.
         """
         if out is None:
             out = torch.empty((x.shape[0], self.local.out_features), dtype=x.dtype, device=x.device)
@@ -132,6 +200,8 @@ class RowParallelInt4Linear(torch.nn.Module):
         self._local_into(x, out, residual if rank == 0 else None)
         if world == 1:
             return out, None
+        if reducer is not None:   # out is a row range of the reducer's symmetric buffer
+            return out, reducer.all_reduce_async(out)
         return out, dist.all_reduce(out, op=dist.ReduceOp.SUM, group=self.group, async_op=True)
 
     def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:

@@ -81,6 +81,72 @@ def test_tp_two_gpus(tmp_path):
     assert float(torch.load(out)[0]) < 2e-2
 
 
+def _nvls_worker(rank, world, port, out_path):
+    """NvlsReducer (the library's multimem all-reduce kernel): two row ranges of its buffer summed
+    over the ranks, each element within one bf16 ulp of the exact sum; then a tensor-parallel
+    block whose row-parallel outputs go through it, against the same block on one GPU."""
+    dev = _init(rank, world, port)
+    from onecomp_runtime.layers import FusedInt4Linear
+    from onecomp_runtime.tensor_parallel import NvlsReducer, build_tp_block
+    from onecomp_runtime.testing import gptq_layer
+    try:
+        red = NvlsReducer(300, 512, blocks=8)
+    except RuntimeError:
+        torch.save(torch.tensor([-1.0, -1.0]), out_path) if rank == 0 else None
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+        return
+    vals = [torch.randn(300, 512, generator=torch.Generator(device=dev).manual_seed(40 + r), device=dev)
+            .to(torch.bfloat16) for r in range(world)]
+    red.buffer.copy_(vals[rank])
+    pend = [red.all_reduce_async(red.view(0, 128)), red.all_reduce_async(red.view(128, 300))]
+    for w in pend:
+        w.wait()
+    exact = sum(v.float() for v in vals)
+    # the switch's bf16 addition: within one bf16 ulp (2^-7 relative at most) of the exact sum
+    mismatch = float(((red.buffer.float() - exact).abs() > exact.abs() * 2.0 ** -7 + 1e-30).sum())
+
+    def make(t, K, N):
+        return FusedInt4Linear(K, N, t["qweight"], t["scales"], t["qzeros"], t.get("bias"), 32)
+
+    tens = {n: gptq_layer(K, N, 32, seed=70 + i, device=dev) for i, (n, K, N) in enumerate(LAYERS)}
+    x = torch.randn(300, 512, generator=torch.Generator(device=dev).manual_seed(1), device=dev).to(torch.bfloat16)
+    blk = build_tp_block(tens, LAYERS, rank, world, 32, make, chunks=2)
+    r1, r2 = red, NvlsReducer(300, 512, blocks=8)
+    spans = [(0, 160), (160, 300)]
+    outs = [blk["out"].forward_async(blk["qkv"](x[a:b])[:, :512 // world], residual=x[a:b], out=r1.view(a, b),
+                                     reducer=r1) for a, b in spans]
+    ys = []
+    for (o, w), (a, b) in zip(outs, spans):
+        w.wait()
+        f = blk["fc1"](o, activation="gelu_tanh")
+        y, w2 = blk["fc2"].forward_async(f, residual=o, out=r2.view(a, b), reducer=r2)
+        w2.wait()
+        ys.append(y.clone())
+    y = torch.cat(ys)
+    torch.cuda.synchronize(dev)
+    if rank == 0:
+        full = {n: make(tens[n], K, N) for n, K, N in LAYERS}
+        qkv = full["qkv"](x)
+        h = x + full["out"](qkv[:, :512])
+        ref = (h + full["fc2"](torch.nn.functional.gelu(full["fc1"](h), approximate="tanh"))).float()
+        err = float((y.float() - ref).abs().max() / ref.abs().max())
+        torch.save(torch.tensor([mismatch, err]), out_path)
+    torch.distributed.barrier()
+    torch.distributed.destroy_process_group()
+
+
+def test_nvls_allreduce_two_gpus(tmp_path):
+    _need_gpus(2)
+    out = tmp_path / "nvls.pt"
+    mp.spawn(_nvls_worker, args=(2, _free_port(), str(out)), nprocs=2, join=True)
+    mismatch, err = (float(v) for v in torch.load(out))
+    if mismatch < 0:
+        pytest.skip("no NVLink multicast on these GPUs")
+    assert mismatch == 0
+    assert err < 2e-2, err
+
+
 def _ep_worker(rank, world, port, out_path, with_shared):
     dev = _init(rank, world, port)
     from onecomp_runtime.moe import ExpertParallelMoE, PackedMoE
