@@ -4,8 +4,11 @@ Default workload (the DiT stack the metric quotes at 1/2/4/8 
 video-DiT-shaped stack of 12 blocks, hidden 4096 (qkv 4096->12288, out 4096->4096,
 fc1 4096->16384, fc2 16384->4096), AutoGPTQ v1 int4 gs32, M = 32768 bf16 tokens N(0,1),
 seeded random packed weights (no checkpoints offline). Tensor parallel over the N ranks of
-the job: qkv and fc1 column-parallel, out and fc2 row-parallel with an NCCL all-reduce
-(sum) per row-parallel linear, issued in M-chunks that overlap the next chunk's GEMM.
+the job: qkv and fc1 column-parallel, out and fc2 row-parallel with an all-reduce (sum) per
+row-parallel linear: from 4 ranks the library's NVLS kernel (multimem.ld_reduce / multimem.st
+over symmetric memory, on 8 SMs the GEMMs leave free), NCCL on 2. The stack is pipelined over
+2 row chunks: each chunk's reduction runs on a side stream while the following GEMMs of the
+other chunk run.
 Per block: qkv; its q slice stands in for attention; out (+ residual in rank 0's
 epilogue); RMS norm; fc1 (tanh-GELU in the epilogue); fc2 (+ residual); RMS norm.
 
@@ -389,7 +392,7 @@ class TPStack:
     """12 video-DiT blocks of B200 int4 linears sharded over the job's ranks."""
 
     def __init__(self, job: Job, blocks: int, timer: LaunchTimer, chunks: int = 1, reduce: str = "nccl",
-                 M: int = 0):
+                 M: int = 0, nvls_blocks: int = 32):
         from onecomp_runtime.layers import FusedInt4Linear
         from onecomp_runtime.tensor_parallel import NvlsReducer, build_tp_block
         self.chunks = max(1, chunks)
@@ -398,7 +401,8 @@ class TPStack:
         if job.world > 1 and reduce == "nvls":
             try:   # two symmetric buffers: out-projection and fc2 partial outputs
                 from onecomp_runtime.testing import CFG4
-                self.reducers = (NvlsReducer(M, CFG4["hidden"]), NvlsReducer(M, CFG4["hidden"]))
+                self.reducers = (NvlsReducer(M, CFG4["hidden"], blocks=nvls_blocks),
+                                 NvlsReducer(M, CFG4["hidden"], blocks=nvls_blocks))
                 self.reduce = "nvls"
             except RuntimeError as e:
                 print(f"[bench] NVLS all-reduce unavailable ({e}); using NCCL", file=sys.stderr)
@@ -476,12 +480,18 @@ def bench_cfg4(args, job: Job, peaks: dict, with_cpu: bool) -> dict:
     from onecomp_runtime.testing import CFG4, CFG4_LAYERS
     M, H, blocks = CFG4["M"], CFG4["hidden"], (args.blocks or CFG4["blocks"])
     timer = LaunchTimer()
-    if job.world > 1 and args.tc_max_ctas:
-        from onecomp_runtime import _lib
-        _lib.set_option(_lib.OPT_TC_MAX_CTAS, args.tc_max_ctas)
-    chunks = args.tp_chunks if args.tp_chunks > 0 else (4 if job.world > 1 else 1)
+    chunks = args.tp_chunks if args.tp_chunks > 0 else (2 if job.world > 1 else 1)
     reduce = args.tp_reduce if args.tp_reduce != "auto" else ("nvls" if job.world >= 4 else "nccl")
-    stack = TPStack(job, blocks, timer, chunks, reduce, M)
+    if job.world > 1:
+        # The GEMM CTA holds a whole SM's register file, so a reduction gets only SMs the persistent
+        # GEMM leaves free: with NVLS, leave exactly the reduction's blocks (measured best at N = 8).
+        sms = torch.cuda.get_device_properties(job.dev).multi_processor_count
+        cap = args.tc_max_ctas if args.tc_max_ctas >= 0 else (sms - args.nvls_blocks if reduce == "nvls" else 0)
+        args.tc_max_ctas = cap
+        if cap:
+            from onecomp_runtime import _lib
+            _lib.set_option(_lib.OPT_TC_MAX_CTAS, cap)
+    stack = TPStack(job, blocks, timer, chunks, reduce, M, args.nvls_blocks)
     x = torch.randn((M, H), generator=torch.Generator(device=job.dev).manual_seed(5), device=job.dev).to(torch.bfloat16)
     with torch.no_grad():
         y = stack.forward(x)
@@ -503,9 +513,10 @@ def bench_cfg4(args, job: Job, peaks: dict, with_cpu: bool) -> dict:
                        "parallelism": f"tp{job.world} (column qkv/fc1, row out/fc2 + NCCL all-reduce)"
                        if job.world > 1 else "tp1 (one GPU, no collective)",
                        "pipeline_chunks": stack.chunks,
+                       "nvls_blocks": args.nvls_blocks if stack.reduce == "nvls" else None,
                        "allreduce": {"nvls": "own NVLS kernel (multimem.ld_reduce / multimem.st)",
                                      "nccl": "NCCL", "none": "none"}[stack.reduce],
-                       "gemm_ctas": args.tc_max_ctas if (job.world > 1 and args.tc_max_ctas) else "one per SM",
+                       "gemm_ctas": args.tc_max_ctas if (job.world > 1 and args.tc_max_ctas > 0) else "one per SM",
                        "l2_flush": "none needed: weights (1.4 GB packed) and activations exceed the 126 MB L2"},
             "e2e": {"value": round(M * args.steps / (ms_e2e / 1e3), 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
@@ -611,6 +622,8 @@ def bench_cfg2(args, job: Job, peaks: dict) -> dict:
     from onecomp_runtime.testing import CFG2_LAYERS, gptq_layer
     if args.gemv_ctas:
         _lib.set_option(_lib.OPT_GEMV_CTAS, args.gemv_ctas)
+    if args.gemv_impl >= 0:
+        _lib.set_option(_lib.OPT_GEMV_IMPL, args.gemv_impl)
     dev = job.dev
     layers, nbytes = [], 0
     w8 = args.wbits == 8
@@ -778,18 +791,22 @@ def main():
     ap.add_argument("--tc-tile", type=int, default=0, help="tokens per tcgen05 tile (0 = library default)")
     ap.add_argument("--gemv-ctas", type=int, default=0, help="GEMV split-K target CTAs per SM (0 = default)")
     ap.add_argument("--wbits", type=int, default=4, choices=[4, 8], help="cfg2 only: code width of the layer set")
+    ap.add_argument("--gemv-impl", type=int, default=-1, choices=[-1, 0, 1, 2, 3],
+                    help="cfg2: decode kernel (OC_OPT_GEMV_IMPL; -1 = library default, the split-K TMA GEMV)")
     ap.add_argument("--blocks", type=int, default=0, help="override the number of DiT blocks (profiling only)")
     ap.add_argument("--moe-experts", type=int, default=0, help="cfg3: override the expert count (profiling only)")
     ap.add_argument("--moe-tokens", type=int, default=0, help="cfg3: override tokens per GPU (profiling only)")
     ap.add_argument("--cpu-sample-m", type=int, default=512, help="tokens of the bounded CPU sample (one block)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--tp-chunks", type=int, default=0,
-                    help="cfg4: row chunks of the pipelined stack (0 = 4 with N > 1, 1 on one GPU)")
+                    help="cfg4: row chunks of the pipelined stack (0 = 2 with N > 1, 1 on one GPU)")
     ap.add_argument("--tp-reduce", default="auto", choices=["auto", "nvls", "nccl"],
                     help="cfg4 with N > 1: all-reduce of the row-parallel outputs (own NVLS kernel or NCCL; "
                          "auto = NVLS from 4 ranks, where it measured faster, NCCL on 2)")
-    ap.add_argument("--tc-max-ctas", type=int, default=0,
-                    help="cfg4 with N > 1: CTAs of the persistent GEMMs (0 = one per SM), SMs left to NCCL")
+    ap.add_argument("--nvls-blocks", type=int, default=8, help="cfg4 NVLS all-reduce: CTAs per reduction (1..64)")
+    ap.add_argument("--tc-max-ctas", type=int, default=-1,
+                    help="cfg4 with N > 1: CTAs of the persistent GEMMs (0 = one per SM; -1 = SMs minus the NVLS "
+                         "reduction's blocks when it runs, else one per SM)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     job = Job()

@@ -234,6 +234,14 @@ int oc_b200_silu_mul(const void* g, const void* u, int64_t ld_in, int P, int F, 
 int oc_b200_moe_combine(const void* y, int64_t ldy, const int32_t* slot_pos, const float* w, int T, int k, int H,
                         const void* shared, int64_t lds, void* out, int64_t ldo, int dtype, oc_stream_t stream);
 
+/* ---- Conv1d as a GEMM ------------------------------------------------------
+ * a[(b T + t) lda + c ksize + k] = x[b, c, t stride + k dilation - pad] (0 outside the input),
+ * 16-bit values, x element (b, c, l) at b sxb + c sxc + l; columns C ksize .. cols_out - 1 are 0.
+ * With the RTN nibble table of a Conv1d weight [out, C ksize] it turns PackedInt4Conv1d.forward
+ * (reference packed_conv.py:123-170: dequant + F.conv1d) into oc_b200_rows_gemm. */
+int oc_b200_im2col_1d(const void* x, int64_t sxb, int64_t sxc, int B, int C, int L, int ksize, int stride,
+                      int dilation, int pad, int T, int cols_out, void* a, int64_t lda, oc_stream_t stream);
+
 /* ---- tensor-parallel reduction ---------------------------------------------
  * Sum over the `world` ranks of a job of n_elems bf16 values (n_elems % 8 == 0) held in one NVLink
  * multicast object, in place: afterwards every rank's copy holds the sum as the NVLink switch adds

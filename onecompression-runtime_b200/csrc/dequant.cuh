@@ -169,6 +169,31 @@ __global__ void permute_cols_kernel(const uint16_t* __restrict__ x, long long ld
   }
 }
 
+// --- im2col of a 1-D convolution input: the A operand of Conv1d run as a GEMM ----------
+// a[(b T + t) lda + c ksize + k] = x[b, c, t stride + k dil - pad] (0 outside [0, L)), for
+// columns < C ksize; columns up to cols_out are written as 0 (the GEMM's zero-padded K). x element
+// (b, c, l) sits at b sxb + c sxc + l (16-bit values). Writes are coalesced along the columns.
+__global__ void im2col1d_kernel(const uint16_t* __restrict__ x, long long sxb, long long sxc, int C, int L,
+                                int ksize, int stride, int dil, int pad, int T, int cols_out, long long rows,
+                                uint16_t* __restrict__ a, long long lda) {
+  const int ck_total = C * ksize;
+  const long long total = rows * cols_out;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int col = (int)(i % cols_out);
+    const long long bt = i / cols_out;
+    uint16_t v = 0;
+    if (col < ck_total) {
+      const int t = (int)(bt % T);
+      const long long b = bt / T;
+      const int c = col / ksize, k = col - c * ksize;
+      const int l = t * stride + k * dil - pad;
+      if (l >= 0 && l < L) v = x[b * sxb + (long long)c * sxc + l];
+    }
+    a[bt * lda + col] = v;
+  }
+}
+
 // --- RTN uint8-nibble dequant (a11) ----------------------------------------------------
 // One element of torch's (q.to(dt) - z.to(dt)) * s.to(dt): for 16-bit dt a rounding after
 // each cast and op; for fp32 the casts are exact and each op rounds once.

@@ -261,6 +261,26 @@ int oc_b200_read_device_error(int* code, oc_stream_t stream) {
   return OC_OK;
 }
 
+// ---------------------------------------------------------------- Conv1d as a GEMM
+int oc_b200_im2col_1d(const void* x, int64_t sxb, int64_t sxc, int B, int C, int L, int ksize, int stride,
+                      int dilation, int pad, int T, int cols_out, void* a, int64_t lda, oc_stream_t stream) {
+  if (!x || !a) return fail(OC_ERR_INVALID, "im2col_1d: NULL pointer");
+  if (B < 0 || C <= 0 || L < 0 || ksize <= 0 || stride <= 0 || dilation <= 0 || pad < 0 || T < 0)
+    return fail(OC_ERR_INVALID, "im2col_1d: B=%d C=%d L=%d k=%d stride=%d dilation=%d pad=%d T=%d", B, C, L, ksize,
+                stride, dilation, pad, T);
+  if (cols_out < C * ksize || lda < cols_out)
+    return fail(OC_ERR_INVALID, "im2col_1d: cols_out=%d lda=%lld for %d columns", cols_out, (long long)lda,
+                C * ksize);
+  const long long rows = (long long)B * T;
+  if (rows == 0) return OC_OK;
+  int dev = 0;
+  if (int rc = current_device(&dev)) return rc;
+  oc::im2col1d_kernel<<<grid_1d(rows * cols_out, 256, dev), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const uint16_t*>(x), (long long)sxb, (long long)sxc, C, L, ksize, stride, dilation, pad, T,
+      cols_out, rows, reinterpret_cast<uint16_t*>(a), (long long)lda);
+  return launch_check("im2col_1d");
+}
+
 // ---------------------------------------------------------------- NVLS all-reduce
 int oc_b200_nvls_allreduce_bf16(void* mc_ptr, int64_t n_elems, void* const* flags_dev, int rank, int world,
                                 uint32_t epoch, int blocks, oc_stream_t stream_) {

@@ -70,6 +70,7 @@ _SIGNATURES = {
     "oc_b200_gather_rows": ([_p, _i64, _p, _i, _i, _p, _i64, _p], _i),
     "oc_b200_silu_mul": ([_p, _p, _i64, _i, _i, _p, _i64, _i, _p], _i),
     "oc_b200_moe_combine": ([_p, _i64, _p, _p, _i, _i, _i, _p, _i64, _p, _i64, _i, _p], _i),
+    "oc_b200_im2col_1d": ([_p, _i64, _i64, _i, _i, _i, _i, _i, _i, _i, _i, _i, _p, _i64, _p], _i),
     "oc_b200_nvls_allreduce_bf16": ([_p, _i64, _p, _i, _i, ctypes.c_uint32, _i, _p], _i),
 }
 

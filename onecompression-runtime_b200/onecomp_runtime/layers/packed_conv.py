@@ -8,12 +8,17 @@ Same public surface as the reference ``layers/packed_conv.py`` (DACVAE conv code
 pad / unpad rules for ``NormConv1d`` / ``NormConvTranspose1d`` replacements.
 
 The layer weight is a 2-D RTN table [rows, cols] (rows = output channels for Conv1d, input
-channels for ConvTranspose1d; cols = the flattened (channels / groups) x kernel_size). At
-forward time it is dequantized on the device by ``oc_b200_rtn_dequant`` -- bit-exact with
-the reference's ``(w_int - zeros) * scales`` in the activation dtype
-(packed_conv.py:48-60, the same arithmetic as quant_utils.dequant_extra_u8_to_weight) --
-and handed to ``F.conv1d`` / ``F.conv_transpose1d``. Only the layer being run holds a
-16-bit copy of its weight.
+channels for ConvTranspose1d; cols = the flattened (channels / groups) x kernel_size).
+
+* Conv1d (groups == 1, fp16/bf16 on the GPU): the table is exactly a ``PackedRTNLinear``
+  weight [out, C k], so the convolution runs as ``oc_b200_im2col_1d`` (the input unfolded to
+  [B T, C k]) followed by the row-packed tcgen05 GEMM in RTN mode, which multiplies the weights
+  the reference's dequant produces (two roundings in the activation dtype); no cuDNN.
+* Grouped Conv1d, ConvTranspose1d (whose contraction runs over the table's rows, across its
+  scale groups) and fp32 inputs: the weight is dequantized on the device by
+  ``oc_b200_rtn_dequant`` -- bit-exact with the reference's ``(w_int - zeros) * scales`` in the
+  activation dtype (packed_conv.py:48-60) -- and handed to ``F.conv1d`` /
+  ``F.conv_transpose1d``, as the reference does. Only the layer being run holds a 16-bit copy.
 """
 from __future__ import annotations
 
@@ -147,10 +152,52 @@ class PackedInt4Conv1d(_PackedConvBase):
         w = _dequant_weight(self.qweight, self.scales, self.zeros, self.cols, dtype)
         return w.reshape(self.out_channels, self.in_channels // self.groups, self.kernel_size)
 
+    def _gemm_linear(self):
+        """The same nibble table seen as an RTN linear [out, (in / groups) k] (shared buffers, not a
+        submodule, so ``state_dict`` is unchanged), or None when the row-packed GEMM cannot take it."""
+        from .packed_linear import PackedRTNLinear
+        lin = self.__dict__.get("_lin")
+        if lin is None or lin.qweight_u8 is not self.qweight or lin.scales is not self.scales:
+            lin = PackedRTNLinear(self.cols, self.out_channels, self.qweight, self.scales, self.zeros, None)
+            self.__dict__["_lin"] = lin
+        return lin if lin._rows_handle() is not None else None
+
+    def _forward_gemm(self, x: torch.Tensor, lin) -> torch.Tensor:
+        """Conv1d as im2col (``oc_b200_im2col_1d``) + the row-packed tcgen05 GEMM in RTN mode, which
+        multiplies exactly the weights ``_materialize`` produces; output [B, out, T] like F.conv1d."""
+        from .. import _lib
+        unbatched = x.dim() == 2
+        xb = x.unsqueeze(0) if unbatched else x
+        if xb.stride(-1) != 1:
+            xb = xb.contiguous()
+        B, C, L = xb.shape
+        span = self.dilation * (self.kernel_size - 1) + 1
+        T = (L + 2 * self.padding - span) // self.stride + 1
+        if T <= 0:
+            raise RuntimeError(f"PackedInt4Conv1d: input length {L} is shorter than the kernel span {span}")
+        k_run = lin.__dict__["_k_run"]
+        a = torch.empty((B * T, k_run), dtype=x.dtype, device=x.device)
+        _lib.call("oc_b200_im2col_1d", xb.data_ptr(), xb.stride(0), xb.stride(1), B, C, L, self.kernel_size,
+                  self.stride, self.dilation, self.padding, T, k_run, a.data_ptr(), a.stride(0),
+                  _lib.stream_of(x.device))
+        y = torch.empty((B * T, self.out_channels), dtype=x.dtype, device=x.device)
+        if B * T:
+            lin._rows_handle().gemm(a, y, bias=self._bias(x.dtype))
+        y = y.view(B, T, self.out_channels).permute(0, 2, 1).contiguous()
+        return y[0] if unbatched else y
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         x = _conv1d_pad(x, self.kernel_size, self.stride, self.dilation, self.pad_mode, self.causal)
+        if x.is_cuda and x.dtype in (torch.float16, torch.bfloat16) and self.groups == 1:
+            lin = self._gemm_linear()
+            if lin is not None:
+                return self._forward_gemm(x, lin)
         return F.conv1d(x, self._materialize(x.dtype), self._bias(x.dtype), self.stride, self.padding,
                         self.dilation, self.groups)
+
+    def _apply(self, fn, recurse=True):
+        self.__dict__["_lin"] = None
+        return super()._apply(fn, recurse=recurse)
 
 
 class PackedInt4ConvTranspose1d(_PackedConvBase):

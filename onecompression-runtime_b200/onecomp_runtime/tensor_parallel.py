@@ -117,7 +117,7 @@ class NvlsReducer:
     when the devices offer no multicast (then use NCCL: ``RowParallelInt4Linear`` without a reducer).
     """
 
-    def __init__(self, rows: int, cols: int, group=None, blocks: int = 32):
+    def __init__(self, rows: int, cols: int, group=None, blocks: int = 8):
         import torch.distributed._symmetric_memory as symm
         from . import _lib
         self._lib = _lib

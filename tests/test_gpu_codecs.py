@@ -109,3 +109,38 @@ def test_replace_conv_with_packed(cuda_device):
         w2, model[2].bias.float(), stride=2, padding=1)
     err = float((y.float() - ref).abs().max() / ref.abs().max())
     assert err < 1e-2, err
+
+
+CONV_GEMM_CASES = [
+    # cin, cout, k, stride, dilation, padding, batch (None: unbatched), length, groupsize, dtype
+    (64, 128, 7, 1, 1, 3, 2, 300, 32, torch.bfloat16),
+    (96, 64, 3, 2, 1, 0, 3, 257, 32, torch.float16),
+    (32, 96, 3, 1, 9, 9, 1, 200, 8, torch.bfloat16),     # dilated residual-unit shape
+    (13, 40, 5, 1, 1, 2, None, 128, -1, torch.bfloat16),  # C k = 65: K padded to 72, per-row groups
+]
+
+
+@pytest.mark.parametrize("case", CONV_GEMM_CASES, ids=lambda c: f"c{c[0]}o{c[1]}k{c[2]}s{c[3]}d{c[4]}")
+def test_conv1d_runs_as_im2col_gemm(cuda_device, case):
+    """Ungrouped PackedInt4Conv1d on the GPU: im2col + the row-packed RTN GEMM (no cuDNN), against
+    the fp64 convolution of the bit-exact dequantized weight."""
+    from onecomp_runtime import _lib
+    from onecomp_runtime.layers import PackedInt4Conv1d
+    from onecomp_runtime.layers.packed_conv import quantize_conv_weight
+    cin, cout, k, stride, dil, pad, batch, L, gs, dt = case
+    g = torch.Generator().manual_seed(cin * 7 + k)
+    w = torch.randn(cout, cin, k, generator=g) * 0.1
+    q, s, z, cols = quantize_conv_weight(w.reshape(cout, -1), groupsize=gs)
+    bias = torch.randn(cout, generator=g) * 0.1
+    mod = PackedInt4Conv1d(cin, cout, k, stride=stride, padding=pad, dilation=dil, qweight=q, scales=s, zeros=z,
+                           cols=cols, bias=bias, pad_mode="none").to(cuda_device)
+    shape = (cin, L) if batch is None else (batch, cin, L)
+    x = torch.randn(*shape, generator=g).to(cuda_device, dt)
+    y = mod(x)
+    assert mod.__dict__.get("_lin") is not None and mod.__dict__["_lin"]._rows_handle() is not None
+    wq = mod._materialize(dt).double()
+    ref = torch.nn.functional.conv1d(x.double(), wq, bias.to(dt).double().to(cuda_device), stride, pad, dil)
+    assert y.dtype == dt and tuple(y.shape) == tuple(ref.shape)
+    err = float((y.double() - ref).abs().max() / ref.abs().max())
+    assert err < 1e-2, err
+    assert _lib.read_device_error(cuda_device) == 0
