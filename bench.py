@@ -60,7 +60,7 @@ METRIC_CFG1 = "DiT-stack tokens/s (FLUX-style int4 GPTQ stack, 8 blocks, hidden 
 # DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the dominant kernel of
 # each workload, from one ncu capture (profiles/ holds the command and the per-launch figures).
 TC_TRAFFIC_CFG1 = 103_200_000     # cfg1: mean of the qkv, proj, fc1, fc2 launches at M = 4608
-TC_TRAFFIC_CFG4 = None            # cfg4: set from its capture
+TC_TRAFFIC_CFG4 = 1_637_000_000   # cfg4: mean of the qkv, out, fc1, fc2 launches at M = 32768
 GEMV_TRAFFIC_BYTES_PER_LAUNCH = 21_852_160   # cfg2: q/k/v layer, M = 1 (algorithmic 21.8 MB)
 
 
