@@ -96,3 +96,35 @@ def test_wait_runs_out_then_noalloc_calls_are_exact(cuda_device):
         torch.testing.assert_close(y, ref, rtol=0, atol=0)
     torch.cuda.synchronize(cuda_device)
     assert _lib.read_device_error(cuda_device) == 0
+
+
+PEER = 0x110  # kDevErrPeer: a cross-rank barrier of the NVLS all-reduce gave up
+
+
+def test_nvls_allreduce_peer_that_never_arrives(cuda_device):
+    """The NVLS all-reduce's entry barrier waits for a rank that does not exist: a two-rank call on
+    one GPU whose second flag array is a local buffer nobody writes. With a 20 ms bound the kernel
+    records the peer-wait code and returns before any multicast access (the buffer is never
+    touched, so no multicast object is needed), and the context stays usable."""
+    from onecomp_runtime import _lib
+    blocks, world = 2, 2
+    flags = [torch.zeros(2 * blocks * world, dtype=torch.int32, device=cuda_device) for _ in range(world)]
+    ptrs = torch.tensor([f.data_ptr() for f in flags], dtype=torch.int64, device=cuda_device)
+    buf = torch.full((64, 8), 3.0, dtype=torch.bfloat16, device=cuda_device)
+    saved = _lib.get_option(_lib.OPT_WAIT_US)
+    try:
+        _lib.set_option(_lib.OPT_WAIT_US, 20000)
+        _lib.call("oc_b200_nvls_allreduce_bf16", buf.data_ptr(), buf.numel(), ptrs.data_ptr(), 0, world, 1, blocks,
+                  _lib.stream_of(cuda_device))
+        torch.cuda.synchronize(cuda_device)
+    finally:
+        _lib.set_option(_lib.OPT_WAIT_US, saved)
+    assert _lib.read_device_error(cuda_device) == PEER
+    assert torch.equal(buf, torch.full_like(buf, 3.0))
+    # this rank's own arrival was recorded in the other rank's array, and nothing else
+    assert int(flags[1][0 * blocks * world + 0 * world + 0]) == 1
+    assert int(flags[0].sum()) == 1 * blocks  # its own slot of each block, from itself
+    y = buf.float() * 2                         # the context is still usable
+    torch.cuda.synchronize(cuda_device)
+    assert float(y[0, 0]) == 6.0
+    assert _lib.read_device_error(cuda_device) == 0
