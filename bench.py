@@ -791,7 +791,7 @@ def main():
     ap.add_argument("--tc-tile", type=int, default=0, help="tokens per tcgen05 tile (0 = library default)")
     ap.add_argument("--gemv-ctas", type=int, default=0, help="GEMV split-K target CTAs per SM (0 = default)")
     ap.add_argument("--wbits", type=int, default=4, choices=[4, 8], help="cfg2 only: code width of the layer set")
-    ap.add_argument("--gemv-impl", type=int, default=-1, choices=[-1, 0, 1, 2, 3],
+    ap.add_argument("--gemv-impl", type=int, default=-1, choices=[-1, 0, 1, 2, 3, 4],
                     help="cfg2: decode kernel (OC_OPT_GEMV_IMPL; -1 = library default, the split-K TMA GEMV)")
     ap.add_argument("--blocks", type=int, default=0, help="override the number of DiT blocks (profiling only)")
     ap.add_argument("--moe-experts", type=int, default=0, help="cfg3: override the expert count (profiling only)")

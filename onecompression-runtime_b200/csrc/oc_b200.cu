@@ -20,6 +20,7 @@
 #include "gemv_tma.cuh"
 #include "gemv_tc.cuh"
 #include "gemv_sk.cuh"
+#include "gemv_i8.cuh"
 #include "allreduce.cuh"
 #include "moe.cuh"
 
@@ -212,7 +213,7 @@ int oc_b200_set_option(int key, int value) {
       g_opt_tc_pair = value;
       return OC_OK;
     case OC_OPT_GEMV_IMPL:
-      if (value < 0 || value > 3) return fail(OC_ERR_INVALID, "OC_OPT_GEMV_IMPL: %d", value);
+      if (value < 0 || value > 4) return fail(OC_ERR_INVALID, "OC_OPT_GEMV_IMPL: %d", value);
       g_opt_gemv_impl = value;
       return OC_OK;
     case OC_OPT_WAIT_US:
@@ -650,7 +651,17 @@ int gemv_impl(const oc_b200_layer* L) {
 // which sizes its fixed scratch for the split-K kernels): the TMA GEMV in its place.
 int legacy_impl(const oc_b200_layer* L) {
   const int v = gemv_impl(L);
-  return v == 3 ? 1 : v;
+  return (v == 3 || v == 4) ? 1 : v;
+}
+
+// The integer decode GEMV (gemv_i8.cuh) for 4-bit uniform-group layers; it splits K in the TMA
+// GEMV's 128-k stages, so it shares that plan.
+bool use_i8(const oc_b200_layer* L, int64_t M) { return gemv_impl(L) == 4 && M <= 16; }
+
+// Prepared activations of the integer GEMV: [M][stages][320 B].
+size_t x8_bytes(const oc_b200_layer* L, int64_t M) {
+  const int KB = (L->Kp + oc::kX8StageK - 1) / oc::kX8StageK;
+  return ((size_t)M * KB * oc::kX8RowBytes + 255) / 256 * 256;
 }
 
 // The stream-K GEMV runs decode sizes up to 8 tokens (one token tile); larger M takes the
@@ -758,6 +769,12 @@ extern "C" size_t oc_b200_gptq_gemm_workspace(const oc_b200_layer* L, int64_t M)
     if (q.grid > 1) bytes += align_up((size_t)(q.tiles + q.grid) * M * oc::kSkCols * 4, 256);
     return bytes;
   }
+  if (layer_gemv(L, M) && use_i8(L, M)) {  // prepared activations (the act-order gather included)
+    bytes += x8_bytes(L, M);
+    const GemvPlan gp = gemv_plan(L, L->device);
+    if (gp.splits > 1) bytes += align_up((size_t)gp.splits * M * L->N * 4, 256);
+    return bytes;
+  }
   if (L->kperm) bytes += align_up((size_t)M * L->Kp * 2, 256);  // gathered activations
   if (layer_gemv(L, M)) {
     const GemvPlan gp = gemv_plan(L, L->device);
@@ -857,6 +874,62 @@ int launch_gemv_tma(const oc_b200_layer* L, const oc::GemvParams& p, const GemvP
   if (mt == 1)
     return launch_gt_k<oc::gptq_gemv_tma_kernel<BF16, 1>>(oc::GtCfg<1>::kSmemBytes, grid, stream, L, tx, g);
   return launch_gt_k<oc::gptq_gemv_tma_kernel<BF16, 2>>(oc::GtCfg<2>::kSmemBytes, grid, stream, L, tx, g);
+}
+
+// The integer decode GEMV: x8_prepare_kernel (gather + fixed-point digits into `xd`), then the
+// GEMV over them; both launched with programmatic stream serialization.
+template <auto Kern>
+int launch_g8_k(int smem, dim3 grid, cudaStream_t stream, const oc_b200_layer* L, const CUtensorMap& tx,
+                const oc::GtParams& g) {
+  static bool attr_set[kMaxDevices] = {};
+  int dev = 0;
+  if (int rc = current_device(&dev)) return rc;
+  if (dev >= 0 && dev < kMaxDevices && !attr_set[dev]) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (int rc = cuda_check(cudaFuncSetAttribute(Kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+                            "cudaFuncSetAttribute(gemv i8 smem)"))
+      return rc;
+    attr_set[dev] = true;
+  }
+  return launch_pdl(Kern, grid, dim3(oc::kGtThreads), (size_t)smem, stream, "gptq_gemv_i8", L->tmap_gw, L->tmap_gs,
+                    L->tmap_gz, tx, g);
+}
+
+template <bool BF16, int MT, bool ODD>
+int launch_g8_sps(const oc_b200_layer* L, dim3 grid, cudaStream_t stream, const CUtensorMap& tx,
+                  const oc::GtParams& g) {
+  constexpr int smem = oc::G8Cfg<MT>::kSmemBytes;
+  if (L->gt_rows == 4) return launch_g8_k<oc::gptq_gemv_i8_kernel<BF16, MT, 4, ODD>>(smem, grid, stream, L, tx, g);
+  if (L->gt_rows == 2) return launch_g8_k<oc::gptq_gemv_i8_kernel<BF16, MT, 2, ODD>>(smem, grid, stream, L, tx, g);
+  return launch_g8_k<oc::gptq_gemv_i8_kernel<BF16, MT, 1, ODD>>(smem, grid, stream, L, tx, g);
+}
+
+template <bool BF16>
+int launch_gemv_i8(const oc_b200_layer* L, const void* a, int64_t lda, const oc::GemvParams& p, const GemvPlan& gp,
+                   int n_tiles, uint8_t* xd, cudaStream_t stream) {
+  const int KB = (L->Kp + oc::kX8StageK - 1) / oc::kX8StageK;
+  const long long threads = (long long)p.M * KB * 16;
+  if (int rc = launch_pdl(oc::x8_prepare_kernel<BF16>, dim3((unsigned)((threads + 255) / 256)), dim3(256), 0, stream,
+                          "x8_prepare", reinterpret_cast<const uint16_t*>(a), (long long)lda, p.M, L->K_in,
+                          L->kperm, L->Kp, KB, xd))
+    return rc;
+  oc::GtParams g{};
+  g.g = p;
+  g.rows_sz = L->gt_rows;
+  g.kb_per_split = gp.kstep / (oc::kGtBK / 32);
+  const int wait_us = g_opt_wait_us.load();
+  g.wait_ns = wait_us > 0 ? 1000ull * (unsigned long long)wait_us : (unsigned long long)OC_WAIT_NS;
+  g.stall_stage = g_opt_test_stall.load();
+  const int mt = p.M <= 8 ? 1 : 2;
+  CUtensorMap tx;
+  if (int rc = make_tmap_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, xd, (uint64_t)KB * oc::kX8RowWords, (uint64_t)p.M,
+                            (uint64_t)KB * oc::kX8RowBytes, (uint32_t)oc::kX8RowWords, (uint32_t)(8 * mt),
+                            CU_TENSOR_MAP_SWIZZLE_NONE))
+    return rc;
+  const dim3 grid(n_tiles, gp.splits);
+  if (mt == 2) return launch_g8_sps<BF16, 2, true>(L, grid, stream, tx, g);
+  if (p.M > 1) return launch_g8_sps<BF16, 1, true>(L, grid, stream, tx, g);
+  return launch_g8_sps<BF16, 1, false>(L, grid, stream, tx, g);
 }
 
 // The stream-K decode GEMV (layers with sk_ok): activations in the caller's K order.
@@ -1033,6 +1106,40 @@ extern "C" int oc_b200_gptq_gemm_ex(const oc_b200_layer* L, const void* a, int a
                                       stream)
                : launch_gemv_sk<false>(L, a, lda, M, bias, bias_dtype, residual, ldr, act, c, ldc, part, tickets, dev,
                                        stream);
+  }
+
+  if (layer_gemv(L, M) && use_i8(L, M)) {  // prepares (and gathers) its own activations
+    const GemvPlan gp = gemv_plan(L, dev);
+    uint8_t* xd = ws + off;
+    off += x8_bytes(L, M);
+    oc::GemvParams p{};
+    p.x = nullptr;
+    p.ldx = 0;
+    p.M = (int)M;
+    p.qw = L->qw;
+    p.qz = L->qz;
+    p.s = L->s;
+    p.s_dtype = L->s_dtype;
+    p.wgrp = L->wgrp;
+    p.Kp = L->Kp;
+    p.N = L->N;
+    p.G = L->G;
+    p.gs = L->gs;
+    p.v1 = L->v1;
+    p.bias = bias;
+    p.bias_dtype = bias_dtype;
+    p.residual = reinterpret_cast<const uint16_t*>(residual);
+    p.ldr = ldr;
+    p.act = act;
+    p.out = reinterpret_cast<uint16_t*>(c);
+    p.ldc = ldc;
+    p.ws = gp.splits > 1 ? reinterpret_cast<float*>(ws + off) : nullptr;
+    p.tickets = tickets;
+    p.splits = gp.splits;
+    p.kstep_per_split = gp.kstep;
+    const int n_tiles = (L->N + oc::kGemvCols - 1) / oc::kGemvCols;
+    return a_dtype == OC_DT_BF16 ? launch_gemv_i8<true>(L, a, lda, p, gp, n_tiles, xd, stream)
+                                 : launch_gemv_i8<false>(L, a, lda, p, gp, n_tiles, xd, stream);
   }
 
   // activations in kernel K order

@@ -325,13 +325,13 @@ GEMV_IMPL_SHAPES = [
 ]
 
 
-@pytest.mark.parametrize("impl", [0, 1, 2, 3])
+@pytest.mark.parametrize("impl", [0, 1, 2, 3, 4])
 @pytest.mark.parametrize("shape", GEMV_IMPL_SHAPES, ids=lambda s: f"M{s[0]}K{s[1]}N{s[2]}g{s[3]}")
 def test_gemv_impls(cuda_device, impl, shape):
-    """The four decode kernels for uniform-group layers (tcgen05, TMA + mma.sync split-K, cp.async
-    + mma.sync, stream-K with the act-order gather inside; layers narrower than 256 columns run
-    the split-K TMA kernel under 3) against the fp64 GEMM of the exact weight, with a residual +
-    GELU epilogue."""
+    """The five decode kernels for uniform-group layers (tcgen05, TMA + mma.sync split-K, cp.async
+    + mma.sync, stream-K with the act-order gather inside -- layers narrower than 256 columns run
+    the split-K TMA kernel under 3 --, and the integer-MMA kernel on prepared activation digits)
+    against the fp64 GEMM of the exact weight, with a residual + GELU epilogue."""
     from onecomp_runtime import _lib
     from onecomp_runtime.testing import gptq_layer, activations
     M, K, N, gs, v1, act, sdt = shape
@@ -403,5 +403,58 @@ def test_tc_pairs_full_size(cuda_device, pair_option):
     w = quant_utils.dequant_gptq_to_fp(t["qweight"], t["scales"], t["qzeros"], t["g_idx"], K, N, torch.bfloat16)
     ref = x.float() @ w.float().t() + t["bias"].float()
     err = float((y.float() - ref).abs().max() / ref.abs().max())
+    assert err < 1e-2, err
+    assert _lib.read_device_error(cuda_device) == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("M", [1, 6, 16])
+def test_gemv_i8_activation_range(cuda_device, dtype, M):
+    """The integer decode GEMV represents activations as 16-bit fixed point per 128-k stage. Per
+    token (each against its own largest reference output): an outlier 1000x the others, 256 input
+    columns scaled to about 1e-30 (bf16) / 1e-6 (fp16), then those columns alone (stages holding
+    only tiny values), an all-zero token and a NaN token, which must give NaN in every column as
+    the reference's F.linear does. Two calls in a row give identical bits."""
+    from onecomp_runtime import _lib
+    from onecomp_runtime.testing import gptq_layer, activations
+    K, N = 5120, 1024
+    t = {k: v.to(cuda_device) for k, v in gptq_layer(K, N, 128, seed=91, v1=False, actorder=True,
+                                                     scales_dtype=torch.float16, bias=False).items()}
+    layer = _module(t, K, N, 128, False, "packed", cuda_device)
+    x = activations(M, K, seed=17).to(cuda_device).to(dtype)
+    x[0, 300] = 1000.0
+    tiny = 1e-30 if dtype == torch.bfloat16 else 1e-6
+    x[0, 1024:1280] *= tiny
+    if M > 2:
+        x[1].zero_()
+        x[2, 77] = float("nan")
+    saved = _lib.get_option(_lib.OPT_GEMV_IMPL)
+    _lib.set_option(_lib.OPT_GEMV_IMPL, 4)
+    try:
+        ys = [layer(x) for _ in range(2)]
+    finally:
+        _lib.set_option(_lib.OPT_GEMV_IMPL, saved)
+    torch.testing.assert_close(ys[0], ys[1], rtol=0, atol=0, equal_nan=True)
+    y = ys[0].double()
+    ref = _gpu_reference(t, K, N, x, False)
+    for m in range(M):
+        if M > 2 and m == 2:
+            assert torch.isnan(y[m]).all()
+            continue
+        if M > 2 and m == 1:
+            assert (y[m] == 0).all()
+            continue
+        err = float((y[m] - ref[m]).abs().max() / ref[m].abs().max())
+        assert err < 1e-2, (m, err)
+    # the tiny stage alone, in its own scale: zero every other column of token 0
+    xt = torch.zeros_like(x[:1])
+    xt[0, 1024:1280] = x[0, 1024:1280]
+    _lib.set_option(_lib.OPT_GEMV_IMPL, 4)
+    try:
+        yt = layer(xt).double()
+    finally:
+        _lib.set_option(_lib.OPT_GEMV_IMPL, saved)
+    reft = _gpu_reference(t, K, N, xt, False)
+    err = float((yt - reft).abs().max() / reft.abs().max())
     assert err < 1e-2, err
     assert _lib.read_device_error(cuda_device) == 0

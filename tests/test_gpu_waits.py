@@ -26,7 +26,8 @@ def _layer(device):
 
 
 def _with_impl(impl, run, device, stall: bool):
-    """Run `run()` on decode kernel `impl` (1: split-K TMA GEMV, 3: stream-K GEMV), with the stall
+    """Run `run()` on decode kernel `impl` (1: split-K TMA GEMV, 3: stream-K GEMV, 4: integer-MMA
+    split-K GEMV), with the stall
     options set when `stall`, restoring the previous option values. Returns the device error word."""
     from onecomp_runtime import _lib
     keys = (_lib.OPT_WAIT_US, _lib.OPT_TEST_STALL, _lib.OPT_GEMV_IMPL, _lib.OPT_GEMM_PATH)
@@ -51,7 +52,7 @@ def _stalled(run, device):
 
 # Columns the first CTA's failure leaves unwritten: split-K (impl 1) one 128-column tile; stream-K
 # (impl 3) the 256-column tile its run starts in (5120 x 1024 at gs128: 160 units, 2 per CTA).
-@pytest.mark.parametrize("impl,cols", [(1, 128), (3, 256)])
+@pytest.mark.parametrize("impl,cols", [(1, 128), (3, 256), (4, 128)])
 def test_wait_runs_out_then_workspace_calls_are_exact(cuda_device, impl, cols):
     from onecomp_runtime import _lib
     from onecomp_runtime.testing import activations
