@@ -673,7 +673,8 @@ def bench_cfg2(args, job: Job, peaks: dict) -> dict:
            "roofline": {"bound": "hbm", "achieved": top["GB_s"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
                         "frac": top["frac_hbm"], "traffic": None if w8 else GEMV_TRAFFIC_BYTES_PER_LAUNCH,
                         "traffic_unit": "bytes per launch (q/k/v layer)",
-                        "kernel": "gptq_gemv_tma_kernel (split-K decode GEMV)",
+                        "kernel": ("gptq_gemv_tma_kernel (split-K decode GEMV)" if w8 else
+                                   "gptq_gemv_i8_kernel (integer-MMA split-K decode GEMV; M = 16: gptq_gemv_tma_kernel)"),
                         "peak_source": f"{peaks['source']} hbm_gbs"},
            "clocks": clk}
     del layers
@@ -792,7 +793,7 @@ def main():
     ap.add_argument("--gemv-ctas", type=int, default=0, help="GEMV split-K target CTAs per SM (0 = default)")
     ap.add_argument("--wbits", type=int, default=4, choices=[4, 8], help="cfg2 only: code width of the layer set")
     ap.add_argument("--gemv-impl", type=int, default=-1, choices=[-1, 0, 1, 2, 3, 4],
-                    help="cfg2: decode kernel (OC_OPT_GEMV_IMPL; -1 = library default, the split-K TMA GEMV)")
+                    help="cfg2: decode kernel (OC_OPT_GEMV_IMPL; -1 = library default, the integer-MMA GEMV)")
     ap.add_argument("--blocks", type=int, default=0, help="override the number of DiT blocks (profiling only)")
     ap.add_argument("--moe-experts", type=int, default=0, help="cfg3: override the expert count (profiling only)")
     ap.add_argument("--moe-tokens", type=int, default=0, help="cfg3: override tokens per GPU (profiling only)")

@@ -39,11 +39,12 @@ enum {
   OC_OPT_GEMM_PATH = 1,    /* 0 auto (M<=16 -> split-K GEMV, else tcgen05), 1 force GEMV, 2 force tcgen05 */
   OC_OPT_TC_TILE = 2,      /* tokens per tcgen05 tile: 0 auto, 128, 192, 256, 384, 448 */
   OC_OPT_GEMV_CTAS = 3,    /* GEMV CTAs per SM that split-K sizing fills in one wave (default 2) */
-  OC_OPT_GEMV_IMPL = 4,    /* decode kernel for uniform-group layers: 0 tcgen05, 1 TMA + mma.sync split-K
-                              (default), 2 cp.async + mma.sync, 3 stream-K TMA + mma.sync with the act-order
-                              gather inside (M <= 8 and at least 256 columns; otherwise 1), 4 integer
-                              tensor cores: activations prepared as exact 16-bit fixed point per 128-k stage
-                              (two 8-bit digits) with the act-order gather, u8 codes x digits MMAs (4-bit) */
+  OC_OPT_GEMV_IMPL = 4,    /* decode kernel for uniform-group layers: 0 tcgen05, 1 TMA + mma.sync split-K,
+                              2 cp.async + mma.sync, 3 stream-K TMA + mma.sync with the act-order gather inside
+                              (M <= 8 and at least 256 columns; otherwise 1), 4 (default) integer tensor
+                              cores: activations prepared as 16-bit fixed point per 128-k stage (two 8-bit
+                              digits) with the act-order gather, u8 codes x digits MMAs (4-bit codes, M <= 8;
+                              otherwise 1) */
   OC_OPT_TC_PAIR = 5,      /* tcgen05 GEMM on CTA pairs (cta_group::2): 0 auto, 1 single CTAs (default), 2 pairs */
   OC_OPT_WAIT_US = 6,      /* failure tests: bound of the TMA decode GEMV's pipeline waits in microseconds
                               (0, the default: 2 s); drains of copies in flight keep the 2 s bound */

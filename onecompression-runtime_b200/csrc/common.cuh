@@ -41,6 +41,7 @@ enum : unsigned {
   kDevErrResFull = 0x10a,
   kDevErrIndex = 0x301,   // embedding id outside the table
   kDevErrSplitK = 0x201,
+  kDevErrCluster = 0x202,  // a cluster split-K reduction gave up waiting for a CTA of its cluster
 };
 
 __device__ __forceinline__ void record_error(unsigned code) { atomicCAS(&g_oc_dev_error, 0u, code); }
@@ -389,6 +390,41 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
 }
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Bounded wait on a local mbarrier whose arrivals come from other CTAs of the cluster (acquire at
+// cluster scope, so their shared-memory writes before the arrival are visible). Records `code`
+// and returns false when the phase does not complete within `limit_ns`.
+__device__ __forceinline__ bool mbar_wait_cluster_ns(uint64_t* bar, uint32_t parity, unsigned code,
+                                                     uint64_t limit_ns) {
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t it = 0;; ++it) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if ((it & 15u) == 15u && global_timer_ns() - t0 > limit_ns) break;
+  }
+  record_error(code);
+  return false;
+}
+// Loads from another CTA's shared memory (a shared::cluster address from mapa_shared).
+__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ int ld_dsmem_s32(uint32_t addr) {
+  int v;
+  asm volatile("ld.shared::cluster.s32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+  return v;
 }
 __device__ __forceinline__ void tmem_alloc_cg2(uint32_t* dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),

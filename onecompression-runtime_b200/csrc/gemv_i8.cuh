@@ -30,8 +30,18 @@
 // Pipeline, split-K, failure handling and programmatic dependent launch follow gemv_tma.cuh: one TMA
 // producer warp fills an mbarrier ring with the 128-k stage of a 128-column tile (four 32-column
 // weight slabs with the 128-byte swizzle, the stage's scale and zero rows, the prepared activation
-// rows of 8 MT tokens); 8 consumer warps (4 column warps x 2 stage halves) read shared memory only;
-// the last CTA of a column tile reduces the split-K partials in split order.
+// rows of 8 MT tokens); 8 consumer warps (4 column warps x 2 stage halves) read shared memory only.
+//
+// Split-K reduction. With two splits per column tile (the wide layers) the splits are one
+// thread-block cluster (launched with cluster dims (1, 2, 1)): each CTA leaves its partial sums in
+// its own shared memory and arrives on an mbarrier of the leader (split 0); the leader reads the
+// partials over distributed shared memory in split order (deterministic), applies the epilogue and
+// writes the tile, then releases the other CTA, which waits so that its shared memory outlives the
+// leader's reads. That replaces the global-memory reduction (partials to a workspace, a fence, an
+// atomic ticket and a re-read by the last CTA), a chain of dependent L2 round trips at the end of
+// the layer. Larger clusters measured slower (their CTAs must be co-scheduled on one GPC, which
+// delays launches while the previous layer's CTAs still hold SMs), so layers split more ways keep
+// the global reduction. Every wait is bounded.
 #pragma once
 
 #include "common.cuh"
@@ -166,19 +176,29 @@ __global__ void __launch_bounds__(256) x8_prepare_kernel(const uint16_t* __restr
 }
 
 // ---- the GEMV ----------------------------------------------------------------------------------
-template <int MT>
+// Shared-memory stage of XR activation rows and SPS scale / zero rows; the ring is as deep as
+// about 98 KB allows (two CTAs per SM), so a 2-row box (M <= 2) buys three more weight stages in
+// flight than an 8-row one.
+// Every slot is a multiple of 128 bytes: a tiled TMA copy needs a 128-byte aligned shared-memory
+// destination (1024 bytes for the 128-byte swizzle of the weight slabs).
+template <int MT, int SPS, int XR>
 struct G8Cfg {
-  static constexpr int kDepth = MT == 1 ? 8 : 6;
   static constexpr int kWBytes = 4 * 16 * 128;           // four [16 rows][32 words] slabs, 128B-swizzled
-  static constexpr int kSBytes = 4 * kGemvCols * 2;      // up to 4 scale rows (groups of 32)
-  static constexpr int kZBytes = 4 * (kGemvCols / 8) * 4;
-  static constexpr int kXBytes = 8 * MT * kX8RowBytes;   // [8 MT tokens][320 B]
+  static constexpr int kSBytes = SPS * kGemvCols * 2;    // one scale row per segment
+  static constexpr int kZBytes = (SPS * (kGemvCols / 8) * 4 + 127) / 128 * 128;  // zero rows, padded
+  static constexpr int kXBytes = XR * kX8RowBytes;       // [XR tokens][320 B]
+  static constexpr int kStage = kWBytes + kSBytes + kZBytes + kXBytes;
+  static constexpr int kBudget = (MT == 1 ? 98 : 94) * 1024;
+  static constexpr int kDepth = kBudget / kStage > 12 ? 12 : kBudget / kStage;
   static constexpr int kWOff = 0;
   static constexpr int kSOff = kDepth * kWBytes;
   static constexpr int kZOff = kSOff + kDepth * kSBytes;
   static constexpr int kXOff = kZOff + kDepth * kZBytes;
   static constexpr int kBarOff = kXOff + kDepth * kXBytes;
   static constexpr int kSmemBytes = kBarOff + 2 * kDepth * 8 + 16 + 1024 /*align*/;
+  static_assert(kWBytes % 1024 == 0 && kSBytes % 128 == 0 && kZBytes % 128 == 0 && kXBytes % 128 == 0,
+                "TMA destinations: 1024-byte swizzled weight slabs, 128-byte aligned other slots");
+  static_assert(kSOff % 128 == 0 && kZOff % 128 == 0 && kXOff % 128 == 0, "128-byte aligned slot arrays");
 };
 
 // D (+)= A * B, u8 A; B u8 (S8B false) or s8; ZERO: the accumulator starts at 0
@@ -210,24 +230,31 @@ __device__ __forceinline__ void mma_i8(int (&d)[4], const uint32_t (&a)[4], uint
 }
 
 // SPS: segments per stage (4: groups of 32 rows, 2: groups of 64, 1: groups of 128 * n, flushed
-// once per stage). ODD: tokens 2t + 1 exist (M > 1); with M == 1 the fix-up skips them.
-template <bool BF16, int MT, int SPS, bool ODD>
+// once per stage). ODD: tokens 2t + 1 exist (M > 1); with M == 1 the fix-up skips them. XR: rows of
+// the activation box (2 for M <= 2, else 8 MT; rows past M are zero-filled by the copy).
+// gp.cluster: the splits of a tile reduce in their cluster (launched with cluster dims
+// (1, splits, 1)); otherwise through the workspace, as the other decode GEMVs.
+template <bool BF16, int MT, int SPS, bool ODD, int XR>
 __global__ void __launch_bounds__(kGtThreads, 2)
     gptq_gemv_i8_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_s,
                         const __grid_constant__ CUtensorMap tmap_z, const __grid_constant__ CUtensorMap tmap_x,
                         const GtParams gp) {
-  using Cfg = G8Cfg<MT>;
+  using Cfg = G8Cfg<MT, SPS, XR>;
+  constexpr int kCons = kGtConsumerWarps;
   const GemvParams& p = gp.g;
   extern __shared__ __align__(1024) uint8_t g8_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(g8_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::kBarOff);
   uint64_t* empty = full + Cfg::kDepth;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + Cfg::kDepth);
-  __shared__ float red[kGemvWarpsN][32][MT * 8];
+  __shared__ __align__(16) float red[kGemvWarpsN][32][MT * 8];
+  __shared__ __align__(8) uint64_t cl_bar[2];  // [0] the leader's: partials ready; [1] the others': released
+  __shared__ int cta_failed;
   __shared__ int is_last;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tile = blockIdx.x, split = blockIdx.y;
+  const int tile = blockIdx.x, split = blockIdx.y;  // split == rank in the (1, splits, 1) cluster
+  const int nsplit = gridDim.y;
   const int KB = (p.Kp + kX8StageK - 1) / kX8StageK;
   const int kb0 = split * gp.kb_per_split;
   const int kb1 = min(KB, kb0 + gp.kb_per_split);
@@ -237,22 +264,28 @@ __global__ void __launch_bounds__(kGtThreads, 2)
   if (threadIdx.x == 0) {
     for (int i = 0; i < Cfg::kDepth; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], kGtConsumerWarps / 2);  // the 4 column warps of one stage half
+      mbar_init(&empty[i], 4);  // the 4 column warps that consume a stage
     }
+    mbar_init(&cl_bar[0], nsplit);
+    mbar_init(&cl_bar[1], 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
   __syncthreads();
+  // every CTA of the cluster has initialised its barriers once this phase completes; the consumers
+  // wait for it before their first access to another CTA's shared memory
+  if (gp.cluster) asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
   griddep_launch_dependents();
 
-  if (warp == kGtConsumerWarps) {
+  if (warp == kCons) {
     // ------------------------------------------------------------------ producer
     if (lane == 0) {
       tma_prefetch_desc(&tmap_w);
       tma_prefetch_desc(&tmap_s);
       tma_prefetch_desc(&tmap_z);
       tma_prefetch_desc(&tmap_x);
-      const uint32_t bytes = Cfg::kWBytes + gp.rows_sz * (kGemvCols * 2 + kGemvCols / 2) + 8 * MT * kX8RowBytes;
+      // bytes the copies of one stage deliver (the zero slot's padding is not copied)
+      const uint32_t bytes = Cfg::kWBytes + SPS * (kGemvCols * 2 + kGemvCols / 2) + Cfg::kXBytes;
       int armed[Cfg::kDepth];
       for (int i = 0; i < Cfg::kDepth; ++i) armed[i] = -1;
       auto load_wsz = [&](int i) {
@@ -335,7 +368,8 @@ __global__ void __launch_bounds__(kGtThreads, 2)
     for (int a = 0; a < MT; ++a) {
 #pragma unroll
       for (int h = 0; h < (ODD ? 2 : 1); ++h) {
-        const uint8_t* rec = xst + (8 * a + 2 * t + h) * kX8RowBytes + kX8RecOff;
+        const int tok = 8 * a + 2 * t + h;
+        const uint8_t* rec = xst + (tok < XR ? tok : 0) * kX8RowBytes + kX8RecOff;
         int sx;
         if constexpr (kQuartersPerSeg == 4) {
           const int4 q = *reinterpret_cast<const int4*>(rec);
@@ -346,7 +380,11 @@ __global__ void __launch_bounds__(kGtThreads, 2)
         } else {
           sx = *reinterpret_cast<const int*>(rec + 4 * q0);
         }
-        const float sc = *reinterpret_cast<const float*>(rec + 16);
+        float sc = *reinterpret_cast<const float*>(rec + 16);
+        if (tok >= XR) {  // a token row outside the box (never stored)
+          sx = 0;
+          sc = 0.f;
+        }
 #pragma unroll
         for (int b = 0; b < 2; ++b)
 #pragma unroll
@@ -391,8 +429,8 @@ __global__ void __launch_bounds__(kGtThreads, 2)
 #pragma unroll
       for (int a = 0; a < MT; ++a) {
         const int tok = g + 8 * a;
-        const uint4 xd = tok < p.M ? *reinterpret_cast<const uint4*>(xst + tok * kX8RowBytes + 16 * r)
-                                   : make_uint4(0u, 0u, 0u, 0u);
+        const uint4 xd = (tok < p.M && tok < XR) ? *reinterpret_cast<const uint4*>(xst + tok * kX8RowBytes + 16 * r)
+                                                 : make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
         for (int b = 0; b < 2; ++b) {
           const uint32_t af[4] = {ev[2 * b], ev[2 * b + 1], od[2 * b], od[2 * b + 1]};
@@ -411,7 +449,7 @@ __global__ void __launch_bounds__(kGtThreads, 2)
     if (lane == 0) mbar_arrive(&empty[s]);
   }
 
-  // reduce the two stage halves of the CTA (named barrier over the 256 consumer threads)
+  // reduce the two stage halves of the CTA (named barrier over the consumer warps)
   if (kh == 1) {
 #pragma unroll
     for (int a = 0; a < MT; ++a)
@@ -420,18 +458,69 @@ __global__ void __launch_bounds__(kGtThreads, 2)
 #pragma unroll
         for (int c = 0; c < 4; ++c) red[wn][lane][a * 8 + b * 4 + c] = acc[a][b][c];
   }
-  const bool any_fail = named_bar_or(1, kGtConsumerWarps * 32, !ok);
+  const bool any_fail = named_bar_or(1, kCons * 32, !ok);
   if (kh == 0) {
 #pragma unroll
     for (int a = 0; a < MT; ++a)
 #pragma unroll
       for (int b = 0; b < 2; ++b)
 #pragma unroll
-        for (int c = 0; c < 4; ++c) acc[a][b][c] += red[wn][lane][a * 8 + b * 4 + c];
+        for (int c = 0; c < 4; ++c) {
+          acc[a][b][c] += red[wn][lane][a * 8 + b * 4 + c];
+          red[wn][lane][a * 8 + b * 4 + c] = acc[a][b][c];  // this CTA's partial, read by the leader
+        }
   }
-  griddep_wait();  // the previous kernel is done with the workspace and the output
-  // a failed CTA (its error is recorded) still takes its split-K ticket and writes nothing
-  gemv_finish_n<BF16, MT>(p, acc, kh, col, t, tile, split, &is_last, kGtConsumerWarps * 32, any_fail);
+  if (!gp.cluster) {
+    griddep_wait();  // the previous kernel is done with the workspace and the output
+    // a failed CTA (its error is recorded) still takes its split-K ticket and writes nothing
+    gemv_finish_n<BF16, MT>(p, acc, kh, col, t, tile, split, &is_last, kCons * 32, any_fail);
+    return;
+  }
+  if (threadIdx.x == 0) cta_failed = any_fail ? 1 : 0;
+  named_bar_sync(2, kCons * 32);
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+  if (threadIdx.x == 0) {
+    asm volatile("fence.acq_rel.cluster;" ::: "memory");
+    mbar_arrive_cluster(mapa_shared(&cl_bar[0], 0));
+  }
+  if (split != 0) {
+    // keep this CTA's shared memory alive until the leader has read it
+    if (threadIdx.x == 0) mbar_wait_cluster_ns(&cl_bar[1], 0, kDevErrCluster, OC_WAIT_NS);
+    return;
+  }
+  if (kh == 1) return;
+  // ---- leader: the tile's partials in split order
+  const int nthr = 128;  // the 4 kh == 0 warps
+  bool fail = !mbar_wait_cluster_ns(&cl_bar[0], 0, kDevErrCluster, OC_WAIT_NS);
+  float sum[MT * 8];
+#pragma unroll
+  for (int i = 0; i < MT * 8; ++i) sum[i] = 0.f;
+  for (int sp = 0; sp < nsplit && !fail; ++sp) {
+    fail |= ld_dsmem_s32(mapa_shared(&cta_failed, sp)) != 0;
+    const uint32_t base = mapa_shared(&red[wn][lane][0], sp);
+#pragma unroll
+    for (int i = 0; i < MT * 2; ++i) {
+      const float4 v = ld_dsmem_f4(base + 16 * i);
+      sum[4 * i] += v.x;
+      sum[4 * i + 1] += v.y;
+      sum[4 * i + 2] += v.z;
+      sum[4 * i + 3] += v.w;
+    }
+  }
+  // the sums consumed every value read, so the other CTAs can go once all leader threads are here
+  fail = named_bar_or(3, nthr, fail);
+  if (threadIdx.x == 0)
+    for (int sp = 1; sp < nsplit; ++sp) mbar_arrive_cluster(mapa_shared(&cl_bar[1], sp));
+#pragma unroll
+  for (int a = 0; a < MT; ++a)
+#pragma unroll
+    for (int b = 0; b < 2; ++b)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) acc[a][b][c] = sum[a * 8 + b * 4 + c];
+  griddep_wait();  // the previous kernel is done with the output
+  GemvParams q = p;
+  q.splits = 1;  // the sum over splits is complete: epilogue and store only
+  gemv_finish_n<BF16, MT>(q, acc, 0, col, t, tile, 0, &is_last, nthr, fail);
 }
 
 }  // namespace oc

@@ -68,6 +68,7 @@ struct GtParams {
   unsigned long long wait_ns;  // bound of the pipeline waits (drains keep OC_WAIT_NS)
   int stall_stage;    // failure test only: > 0 leaves stage stall_stage - 1 of CTA (0, 0) unissued,
                       // so its consumers' wait runs out; 0 in normal use
+  int cluster;        // integer GEMV: the K splits of a tile are one cluster and reduce in it
 };
 
 template <bool BF16, int MT, int WB = 4>

@@ -49,7 +49,7 @@ bool dt16(int dt) { return dt == OC_DT_F16 || dt == OC_DT_BF16; }
 bool dtf(int dt) { return dt == OC_DT_F16 || dt == OC_DT_BF16 || dt == OC_DT_F32; }
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
-std::atomic<int> g_opt_path{0}, g_opt_tile{0}, g_opt_gemv_ctas{2}, g_opt_gemv_impl{1}, g_opt_tc_pair{1};
+std::atomic<int> g_opt_path{0}, g_opt_tile{0}, g_opt_gemv_ctas{2}, g_opt_gemv_impl{4}, g_opt_tc_pair{1};
 // failure tests only: bound of the decode GEMV's pipeline waits (0: OC_WAIT_NS) and the stage its
 // first CTA leaves unissued (0: none)
 std::atomic<int> g_opt_wait_us{0}, g_opt_test_stall{0};
@@ -632,13 +632,14 @@ namespace {
 struct GemvPlan {
   int splits, kstep;
 };
+constexpr int kI8ClusterMax = 2;
 
 // Split-K plan: as many K splits as fit one wave of CTAs (sm_count x OC_OPT_GEMV_CTAS, two
 // 100 KB cp.async-ring CTAs per SM by default) over the layer's 128-column tiles, each K-warp
 // keeping at least 4 steps of 32 k.
-// Which decode kernel runs for a layer: 0 tcgen05 GEMV, 1 TMA + mma.sync GEMV (both for
-// uniform groups of 32, 64 or 128*n rows; 1 is the default, measured faster), 2 cp.async +
-// mma.sync GEMV (any layout).
+// Which decode kernel runs for a layer: 0 tcgen05 GEMV, 1 TMA + mma.sync GEMV, 3 stream-K GEMV,
+// 4 integer-MMA GEMV (the default; up to 8 tokens, 1 above) -- all for uniform groups of 32, 64 or
+// 128*n rows --, 2 cp.async + mma.sync GEMV (any layout).
 int gemv_impl(const oc_b200_layer* L) {
   if (L->wbits == 8) return 1;  // 8-bit layers have only the TMA GEMV
   if (!L->gt_ok) return 2;
@@ -654,9 +655,10 @@ int legacy_impl(const oc_b200_layer* L) {
   return (v == 3 || v == 4) ? 1 : v;
 }
 
-// The integer decode GEMV (gemv_i8.cuh) for 4-bit uniform-group layers; it splits K in the TMA
-// GEMV's 128-k stages, so it shares that plan.
-bool use_i8(const oc_b200_layer* L, int64_t M) { return gemv_impl(L) == 4 && M <= 16; }
+// The integer decode GEMV (gemv_i8.cuh) for 4-bit uniform-group layers up to 8 tokens (one token
+// tile; with two the 16-bit TMA GEMV measured faster); it splits K in the TMA GEMV's 128-k stages,
+// so it shares that plan.
+bool use_i8(const oc_b200_layer* L, int64_t M) { return gemv_impl(L) == 4 && M <= 8; }
 
 // Prepared activations of the integer GEMV: [M][stages][320 B].
 size_t x8_bytes(const oc_b200_layer* L, int64_t M) {
@@ -720,6 +722,10 @@ GemvPlan gemv_plan(const oc_b200_layer* L, int dev) {
   return {splits, kstep};
 }
 
+// The integer GEMV splits K like the TMA GEMV (128-k stages); up to kI8ClusterMax splits of a tile
+// reduce inside their thread-block cluster, more through the workspace.
+bool i8_cluster(int splits) { return splits > 1 && splits <= kI8ClusterMax; }
+
 // Tokens per tcgen05 tile when the caller leaves it to the library: the preset with the
 // least (waves of persistent CTAs) x (measured time of one tile at K = 3072 on B200, us).
 // 384 and 448 are two sub-tiles of 192 / 224 tokens sharing each dequantized weight stage.
@@ -772,7 +778,7 @@ extern "C" size_t oc_b200_gptq_gemm_workspace(const oc_b200_layer* L, int64_t M)
   if (layer_gemv(L, M) && use_i8(L, M)) {  // prepared activations (the act-order gather included)
     bytes += x8_bytes(L, M);
     const GemvPlan gp = gemv_plan(L, L->device);
-    if (gp.splits > 1) bytes += align_up((size_t)gp.splits * M * L->N * 4, 256);
+    if (gp.splits > 1 && !i8_cluster(gp.splits)) bytes += align_up((size_t)gp.splits * M * L->N * 4, 256);
     return bytes;
   }
   if (L->kperm) bytes += align_up((size_t)M * L->Kp * 2, 256);  // gathered activations
@@ -891,17 +897,37 @@ int launch_g8_k(int smem, dim3 grid, cudaStream_t stream, const oc_b200_layer* L
       return rc;
     attr_set[dev] = true;
   }
-  return launch_pdl(Kern, grid, dim3(oc::kGtThreads), (size_t)smem, stream, "gptq_gemv_i8", L->tmap_gw, L->tmap_gs,
-                    L->tmap_gz, tx, g);
+  // with g.cluster: one cluster per column tile, its K splits
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(oc::kGtThreads);
+  cfg.dynamicSmemBytes = (size_t)smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 1;
+  attr[1].val.clusterDim.y = grid.y;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = g.cluster ? 2 : 1;
+  if (int rc = cuda_check(cudaLaunchKernelEx(&cfg, Kern, L->tmap_gw, L->tmap_gs, L->tmap_gz, tx, g), "gptq_gemv_i8"))
+    return rc;
+  return launch_check("gptq_gemv_i8");
 }
 
-template <bool BF16, int MT, bool ODD>
+template <bool BF16, int MT, bool ODD, int XR>
 int launch_g8_sps(const oc_b200_layer* L, dim3 grid, cudaStream_t stream, const CUtensorMap& tx,
                   const oc::GtParams& g) {
-  constexpr int smem = oc::G8Cfg<MT>::kSmemBytes;
-  if (L->gt_rows == 4) return launch_g8_k<oc::gptq_gemv_i8_kernel<BF16, MT, 4, ODD>>(smem, grid, stream, L, tx, g);
-  if (L->gt_rows == 2) return launch_g8_k<oc::gptq_gemv_i8_kernel<BF16, MT, 2, ODD>>(smem, grid, stream, L, tx, g);
-  return launch_g8_k<oc::gptq_gemv_i8_kernel<BF16, MT, 1, ODD>>(smem, grid, stream, L, tx, g);
+  if (L->gt_rows == 4)
+    return launch_g8_k<oc::gptq_gemv_i8_kernel<BF16, MT, 4, ODD, XR>>(oc::G8Cfg<MT, 4, XR>::kSmemBytes, grid, stream,
+                                                                      L, tx, g);
+  if (L->gt_rows == 2)
+    return launch_g8_k<oc::gptq_gemv_i8_kernel<BF16, MT, 2, ODD, XR>>(oc::G8Cfg<MT, 2, XR>::kSmemBytes, grid, stream,
+                                                                      L, tx, g);
+  return launch_g8_k<oc::gptq_gemv_i8_kernel<BF16, MT, 1, ODD, XR>>(oc::G8Cfg<MT, 1, XR>::kSmemBytes, grid, stream,
+                                                                    L, tx, g);
 }
 
 template <bool BF16>
@@ -920,16 +946,18 @@ int launch_gemv_i8(const oc_b200_layer* L, const void* a, int64_t lda, const oc:
   const int wait_us = g_opt_wait_us.load();
   g.wait_ns = wait_us > 0 ? 1000ull * (unsigned long long)wait_us : (unsigned long long)OC_WAIT_NS;
   g.stall_stage = g_opt_test_stall.load();
-  const int mt = p.M <= 8 ? 1 : 2;
+  g.cluster = i8_cluster(gp.splits) ? 1 : 0;
+  const int xr = p.M <= 2 ? 2 : (p.M <= 8 ? 8 : 16);  // activation rows per stage box
   CUtensorMap tx;
   if (int rc = make_tmap_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, xd, (uint64_t)KB * oc::kX8RowWords, (uint64_t)p.M,
-                            (uint64_t)KB * oc::kX8RowBytes, (uint32_t)oc::kX8RowWords, (uint32_t)(8 * mt),
+                            (uint64_t)KB * oc::kX8RowBytes, (uint32_t)oc::kX8RowWords, (uint32_t)xr,
                             CU_TENSOR_MAP_SWIZZLE_NONE))
     return rc;
   const dim3 grid(n_tiles, gp.splits);
-  if (mt == 2) return launch_g8_sps<BF16, 2, true>(L, grid, stream, tx, g);
-  if (p.M > 1) return launch_g8_sps<BF16, 1, true>(L, grid, stream, tx, g);
-  return launch_g8_sps<BF16, 1, false>(L, grid, stream, tx, g);
+  if (xr == 16) return launch_g8_sps<BF16, 2, true, 16>(L, grid, stream, tx, g);
+  if (xr == 8) return launch_g8_sps<BF16, 1, true, 8>(L, grid, stream, tx, g);
+  if (p.M == 2) return launch_g8_sps<BF16, 1, true, 2>(L, grid, stream, tx, g);
+  return launch_g8_sps<BF16, 1, false, 2>(L, grid, stream, tx, g);
 }
 
 // The stream-K decode GEMV (layers with sk_ok): activations in the caller's K order.
@@ -1133,7 +1161,7 @@ extern "C" int oc_b200_gptq_gemm_ex(const oc_b200_layer* L, const void* a, int a
     p.act = act;
     p.out = reinterpret_cast<uint16_t*>(c);
     p.ldc = ldc;
-    p.ws = gp.splits > 1 ? reinterpret_cast<float*>(ws + off) : nullptr;
+    p.ws = (gp.splits > 1 && !i8_cluster(gp.splits)) ? reinterpret_cast<float*>(ws + off) : nullptr;
     p.tickets = tickets;
     p.splits = gp.splits;
     p.kstep_per_split = gp.kstep;
