@@ -61,7 +61,7 @@ METRIC_CFG1 = "DiT-stack tokens/s (FLUX-style int4 GPTQ stack, 8 blocks, hidden 
 # each workload, from one ncu capture (profiles/ holds the command and the per-launch figures).
 TC_TRAFFIC_CFG1 = 103_200_000     # cfg1: mean of the qkv, proj, fc1, fc2 launches at M = 4608
 TC_TRAFFIC_CFG4 = 1_637_000_000   # cfg4: mean of the qkv, out, fc1, fc2 launches at M = 32768
-GEMV_TRAFFIC_BYTES_PER_LAUNCH = 21_852_160   # cfg2: q/k/v layer, M = 1 (algorithmic 21.8 MB)
+GEMV_TRAFFIC_BYTES_PER_LAUNCH = 21_847_808   # cfg2: q/k/v layer, M = 1, integer GEMV (algorithmic 21.85 MB)
 
 
 def load_peaks() -> dict:
