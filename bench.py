@@ -5,10 +5,11 @@ video-DiT-shaped stack of 12 blocks, hidden 4096 (qkv 4096->12288, out 4096->409
 fc1 4096->16384, fc2 16384->4096), AutoGPTQ v1 int4 gs32, M = 32768 bf16 tokens N(0,1),
 seeded random packed weights (no checkpoints offline). Tensor parallel over the N ranks of
 the job: qkv and fc1 column-parallel, out and fc2 row-parallel with an all-reduce (sum) per
-row-parallel linear: from 4 ranks the library's NVLS kernel (multimem.ld_reduce / multimem.st
-over symmetric memory, on 8 SMs the GEMMs leave free), NCCL on 2. The stack is pipelined over
-2 row chunks: each chunk's reduction runs on a side stream while the following GEMMs of the
-other chunk run.
+row-parallel linear: the library's NVLS kernel (multimem.ld_reduce / multimem.st over symmetric
+memory, on 8 SMs the GEMMs leave free), which also applies the block's RMS norm (each rank
+normalizes 1/N of the rows and multicasts them); ``--tp-reduce nccl`` runs NCCL and torch's norm
+instead. The stack is pipelined over 2 row chunks: each chunk's reduction runs on a side stream
+while the following GEMMs of the other chunk run.
 Per block: qkv; its q slice stands in for attention; out (+ residual in rank 0's
 epilogue); RMS norm; fc1 (tanh-GELU in the epilogue); fc2 (+ residual); RMS norm.
 
@@ -166,7 +167,10 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------- plumbing
-def rms_norm(h: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+RMS_EPS = 1e-6
+
+
+def rms_norm(h: torch.Tensor, eps: float = RMS_EPS) -> torch.Tensor:
     """RMS norm without weight, fp32 statistics (torch's fused rms_norm)."""
     return torch.nn.functional.rms_norm(h, (h.shape[-1],), eps=eps)
 
@@ -242,6 +246,18 @@ class LaunchTimer:
             self.rec.append((s, e, 2.0 * a.shape[0] * handle.K * handle.N))
             self.launches += 1
         handle.gemm = timed
+        orig_sw = handle.gemm_swiglu
+
+        def timed_sw(a, out, offsets=None):   # gate|up handle: K = 2 x hidden, so 2 M K N counts both
+            if not self.on:
+                return orig_sw(a, out, offsets)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            orig_sw(a, out, offsets)
+            e.record()
+            self.rec.append((s, e, 2.0 * a.shape[0] * handle.K * handle.N))
+            self.launches += 1
+        handle.gemm_swiglu = timed_sw
 
     def start(self):
         self.rec, self.launches, self.on = [], 0, True
@@ -392,10 +408,11 @@ class TPStack:
     """12 video-DiT blocks of B200 int4 linears sharded over the job's ranks."""
 
     def __init__(self, job: Job, blocks: int, timer: LaunchTimer, chunks: int = 1, reduce: str = "nccl",
-                 M: int = 0, nvls_blocks: int = 32):
+                 M: int = 0, nvls_blocks: int = 32, fused_norm: bool = True):
         from onecomp_runtime.layers import FusedInt4Linear
         from onecomp_runtime.tensor_parallel import NvlsReducer, build_tp_block
         self.chunks = max(1, chunks)
+        self.fused_norm = fused_norm
         self.reducers = None
         self.reduce = "none" if job.world == 1 else "nccl"
         if job.world > 1 and reduce == "nvls":
@@ -432,25 +449,28 @@ class TPStack:
         spans = [(c0, min(M, c0 + step)) for c0 in range(0, M, step)]
         hs = [h[c0:c1] for c0, c1 in spans]
         r1, r2 = self.reducers if self.reducers else (None, None)
+        # with the NVLS reducers each all-reduce also applies the block's RMS norm (every rank
+        # normalizes 1/N of the rows) instead of every rank normalizing every row afterwards
+        eps = RMS_EPS if (r1 is not None and self.fused_norm) else None
         qkv = [self.blocks[0]["qkv"](hc) for hc in hs]
         for b, blk in enumerate(self.blocks):
             pend = [blk["out"].forward_async(q[:, :self.hq], residual=hc, out=r1.view(c0, c1) if r1 else None,
-                                             reducer=r1)
+                                             reducer=r1, rms_norm_eps=eps)
                     for q, hc, (c0, c1) in zip(qkv, hs, spans)]
             pend2 = []
             for (o, w), (c0, c1) in zip(pend, spans):
                 if w is not None:
                     w.wait()
-                hn = rms_norm(o)
+                hn = o if eps is not None else rms_norm(o)   # the NVLS reduction normalized the rows
                 f = blk["fc1"](hn, activation="gelu_tanh")
                 pend2.append(blk["fc2"].forward_async(f, residual=hn, out=r2.view(c0, c1) if r2 else None,
-                                                      reducer=r2))
+                                                      reducer=r2, rms_norm_eps=eps))
             nxt = self.blocks[b + 1] if b + 1 < len(self.blocks) else None
             hs, qkv = [], []
             for o, w in pend2:
                 if w is not None:
                     w.wait()
-                hc = rms_norm(o)
+                hc = o if eps is not None else rms_norm(o)
                 hs.append(hc)
                 if nxt is not None:
                     qkv.append(nxt["qkv"](hc))
@@ -481,7 +501,7 @@ def bench_cfg4(args, job: Job, peaks: dict, with_cpu: bool) -> dict:
     M, H, blocks = CFG4["M"], CFG4["hidden"], (args.blocks or CFG4["blocks"])
     timer = LaunchTimer()
     chunks = args.tp_chunks if args.tp_chunks > 0 else (2 if job.world > 1 else 1)
-    reduce = args.tp_reduce if args.tp_reduce != "auto" else ("nvls" if job.world >= 4 else "nccl")
+    reduce = args.tp_reduce if args.tp_reduce != "auto" else "nvls"
     if job.world > 1:
         # The GEMM CTA holds a whole SM's register file, so a reduction gets only SMs the persistent
         # GEMM leaves free: with NVLS, leave exactly the reduction's blocks (measured best at N = 8).
@@ -491,7 +511,7 @@ def bench_cfg4(args, job: Job, peaks: dict, with_cpu: bool) -> dict:
         if cap:
             from onecomp_runtime import _lib
             _lib.set_option(_lib.OPT_TC_MAX_CTAS, cap)
-    stack = TPStack(job, blocks, timer, chunks, reduce, M, args.nvls_blocks)
+    stack = TPStack(job, blocks, timer, chunks, reduce, M, args.nvls_blocks, fused_norm=not args.no_fused_norm)
     x = torch.randn((M, H), generator=torch.Generator(device=job.dev).manual_seed(5), device=job.dev).to(torch.bfloat16)
     with torch.no_grad():
         y = stack.forward(x)
@@ -514,6 +534,8 @@ def bench_cfg4(args, job: Job, peaks: dict, with_cpu: bool) -> dict:
                        if job.world > 1 else "tp1 (one GPU, no collective)",
                        "pipeline_chunks": stack.chunks,
                        "nvls_blocks": args.nvls_blocks if stack.reduce == "nvls" else None,
+                       "rms_norm": ("in the NVLS all-reduce kernel (each rank normalizes 1/N of the rows)"
+                                    if stack.reduce == "nvls" and stack.fused_norm else "torch F.rms_norm"),
                        "allreduce": {"nvls": "own NVLS kernel (multimem.ld_reduce / multimem.st)",
                                      "nccl": "NCCL", "none": "none"}[stack.reduce],
                        "gemm_ctas": args.tc_max_ctas if (job.world > 1 and args.tc_max_ctas > 0) else "one per SM",
@@ -802,9 +824,11 @@ def main():
     ap.add_argument("--tp-chunks", type=int, default=0,
                     help="cfg4: row chunks of the pipelined stack (0 = 2 with N > 1, 1 on one GPU)")
     ap.add_argument("--tp-reduce", default="auto", choices=["auto", "nvls", "nccl"],
-                    help="cfg4 with N > 1: all-reduce of the row-parallel outputs (own NVLS kernel or NCCL; "
-                         "auto = NVLS from 4 ranks, where it measured faster, NCCL on 2)")
+                    help="cfg4 with N > 1: all-reduce of the row-parallel outputs (own NVLS kernel, with the RMS "
+                         "norm fused, or NCCL; auto = NVLS, which measured faster from 2 ranks)")
     ap.add_argument("--nvls-blocks", type=int, default=8, help="cfg4 NVLS all-reduce: CTAs per reduction (1..64)")
+    ap.add_argument("--no-fused-norm", action="store_true",
+                    help="cfg4 with NVLS: run the RMS norms after the all-reduces instead of inside them")
     ap.add_argument("--tc-max-ctas", type=int, default=-1,
                     help="cfg4 with N > 1: CTAs of the persistent GEMMs (0 = one per SM; -1 = SMs minus the NVLS "
                          "reduction's blocks when it runs, else one per SM)")

@@ -213,6 +213,16 @@ int oc_b200_rows_layer_create(int E, const uint8_t* const* packed, int64_t ld_by
 int oc_b200_rows_gemm(const oc_b200_layer* layer, const void* a, int a_dtype, int64_t M, int64_t lda,
                       const int32_t* offsets, const void* bias, int bias_dtype, void* c, int64_t ldc,
                       oc_stream_t stream);
+/* The gate and up projections of a SwiGLU expert FFN in one launch. `layer` describes [F, 2K]
+ * matrices whose row n is gate row n followed by up row n (packed codes concatenated along k;
+ * scale/zero groups: the K/groupsize gate groups, then the up groups), with K a multiple of 64
+ * and of the groupsize. A is [M, K] (dense or grouped as in oc_b200_rows_gemm, no bias) and
+ * C[M, F] = RNE(silu(g) * u), g and u each rounded to a_dtype first: the same bits as
+ * oc_b200_rows_gemm on the gate and up matrices followed by oc_b200_silu_mul.
+ * Replaces the first two expert matmuls and the activation of the reference's routed-expert
+ * path (dsv4_packed_linear.py:95-98 per expert, models/dsv4/loader.py:92-119). */
+int oc_b200_rows_gemm_swiglu(const oc_b200_layer* layer, const void* a, int a_dtype, int64_t M, int64_t lda,
+                             const int32_t* offsets, void* c, int64_t ldc, oc_stream_t stream);
 
 /* ---- packed-expert MoE -------------------------------- */
 /* The reference routes in an unvendored model file (models/dsv4/loader.py:50-53);
@@ -259,6 +269,20 @@ int oc_b200_im2col_1d(const void* x, int64_t sxb, int64_t sxc, int B, int C, int
  * all-reduce after each row-parallel linear of the tensor-parallel DiT stack. */
 int oc_b200_nvls_allreduce_bf16(void* mc_ptr, int64_t n_elems, void* const* flags_dev, int rank, int world,
                                 uint32_t epoch, int blocks, oc_stream_t stream);
+
+/* The same sum followed by an RMS norm of every row, in place: `rows` rows of `cols` bf16 values
+ * (cols a multiple of 8, at most 4096; rows stored contiguously from mc_ptr). Afterwards every
+ * rank's copy holds y = bf16(s * rsqrt(mean(s^2) + eps) * gain) per row, s the switch's bf16 sum
+ * of the ranks' rows (as oc_b200_nvls_allreduce_bf16 leaves it), the mean square taken in fp32;
+ * gain is an optional [cols] bf16 vector (16-byte aligned; NULL: no gain). The ranks split the
+ * rows, so each row is normalized once in the job instead of once per rank. Flags, epoch, blocks,
+ * ordering and the bounded waits are those of oc_b200_nvls_allreduce_bf16, whose flag arrays and
+ * epoch sequence it shares.
+ * No reference counterpart; it replaces the NCCL all-reduce and the norm that follows it in
+ * the tensor-parallel DiT block. */
+int oc_b200_nvls_allreduce_rmsnorm_bf16(void* mc_ptr, int rows, int cols, const void* gain, float eps,
+                                        void* const* flags_dev, int rank, int world, uint32_t epoch, int blocks,
+                                        oc_stream_t stream);
 
 #ifdef __cplusplus
 }

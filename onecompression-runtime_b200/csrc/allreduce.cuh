@@ -113,4 +113,82 @@ __global__ void __launch_bounds__(kArThreads) nvls_allreduce_bf16_kernel(const A
   ar_barrier(p, 1, &ok_smem);  // every rank's stores have landed before anyone reads or rewrites
 }
 
+// ---- all-reduce + RMS norm ---------------------------------------------------------------------
+// The DiT block normalizes each row-parallel output right after its all-reduce. Run separately,
+// every rank normalizes every row of the reduced buffer (the norm is replicated N times). Here the
+// ranks split the ROWS instead of the byte range: a warp reads one row of its rank's share through
+// the switch (multimem.ld_reduce: the bf16 sum over the ranks), computes its mean square in fp32,
+// scales it by rsqrt(mean + eps) (times an optional per-column gain) and multimem.st's the
+// normalized row to every rank's copy. Same barriers and flag slots as the plain kernel, so both
+// share one flag array and one epoch sequence.
+constexpr int kArNormThreads = 384;  // 12 warps; a 4096-wide row per warp fits the 168 registers this allows
+constexpr int kArNormMaxVpl = 16;  // 16-byte vectors per lane: rows up to 16 * 32 * 8 = 4096 columns
+
+struct ArNormParams {
+  ArParams ar;           // ar.mc = row 0 of the range; ar.n16 unused
+  int rows, cols;        // rows stored contiguously (stride cols), cols % 8 == 0
+  const uint4* gain;     // optional [cols] bf16 per-column gain, nullptr: none
+  float eps;
+};
+
+template <int VPL>
+__global__ void __launch_bounds__(kArNormThreads) nvls_allreduce_rmsnorm_bf16_kernel(const ArNormParams p) {
+  __shared__ int ok_smem;
+  if (!ar_barrier(p.ar, 0, &ok_smem)) return;  // every rank's copy is complete
+  const int per = (p.rows + p.ar.world - 1) / p.ar.world;
+  const int lo = p.ar.rank * per;
+  const int hi = min(p.rows, lo + per);
+  const int lane = threadIdx.x & 31;
+  const int wpb = blockDim.x >> 5;
+  const int nvec = p.cols >> 3;
+  for (int row = lo + blockIdx.x * wpb + (threadIdx.x >> 5); row < hi; row += gridDim.x * wpb) {
+    uint4* r = p.ar.mc + (long long)row * nvec;
+    uint32_t v[VPL][4];
+#pragma unroll
+    for (int u = 0; u < VPL; ++u) {
+      if (lane + 32 * u < nvec) {
+        asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(v[u][0]), "=r"(v[u][1]), "=r"(v[u][2]), "=r"(v[u][3])
+                     : "l"(r + lane + 32 * u)
+                     : "memory");
+      } else {
+        v[u][0] = v[u][1] = v[u][2] = v[u][3] = 0u;
+      }
+    }
+    // mean square of the reduced (bf16) row in fp32, as a norm applied after the all-reduce sees it
+    float ss = 0.f;
+#pragma unroll
+    for (int u = 0; u < VPL; ++u)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float a = __uint_as_float(v[u][j] << 16), b = __uint_as_float(v[u][j] & 0xFFFF0000u);
+        ss = fmaf(a, a, ss);
+        ss = fmaf(b, b, ss);
+      }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+    const float rs = rsqrtf(ss / (float)p.cols + p.eps);
+#pragma unroll
+    for (int u = 0; u < VPL; ++u) {
+      const int c = lane + 32 * u;
+      if (c >= nvec) continue;
+      uint32_t gw[4] = {0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u};  // bf16 pairs of 1.0
+      if (p.gain) {
+        const uint4 g = __ldg(p.gain + c);
+        gw[0] = g.x; gw[1] = g.y; gw[2] = g.z; gw[3] = g.w;
+      }
+      uint32_t y[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float a = __uint_as_float(v[u][j] << 16) * rs, b = __uint_as_float(v[u][j] & 0xFFFF0000u) * rs;
+        y[j] = pack2_rn<true>(a * __uint_as_float(gw[j] << 16), b * __uint_as_float(gw[j] & 0xFFFF0000u));
+      }
+      asm volatile("multimem.st.relaxed.sys.global.v4.bf16x2 [%0], {%1, %2, %3, %4};" ::"l"(r + c), "r"(y[0]),
+                   "r"(y[1]), "r"(y[2]), "r"(y[3])
+                   : "memory");
+    }
+  }
+  ar_barrier(p.ar, 1, &ok_smem);  // every rank's stores have landed before anyone reads or rewrites
+}
+
 }  // namespace oc

@@ -76,6 +76,12 @@ __device__ __forceinline__ float tanh_approx(float x) {
   asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// silu(g) = g / (1 + e^-g) with the fast exponential and division intrinsics (a few fp32 ulps
+// from the exact value, far below the 16-bit rounding that follows): the MoE expert activation,
+// shared by the silu-mul kernel and the fused gate|up GEMM epilogue so both give the same bits.
+// Large negative g: e^-g overflows to inf, the fast division gives (-)0, the limit of silu.
+__device__ __forceinline__ float silu_f32(float g) { return __fdividef(g, 1.f + __expf(-g)); }
+
 __device__ __forceinline__ float gelu_tanh(float v) {
   const float u = 0.7978845608028654f * fmaf(0.044715f * v, v * v, v);
   const float h = 0.5f * v;

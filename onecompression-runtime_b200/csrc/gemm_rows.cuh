@@ -13,6 +13,15 @@
 // Grouped mode: rows of X are sorted by expert, offsets[E+1] delimit the segments, and a
 // tile never straddles two experts (the MMA may read rows of the next segment; those
 // outputs are not stored).
+// SwiGLU mode (SWIGLU): the expert FFN's gate and up projections in one launch. Each matrix is
+// stored as [F, 2K] -- row n is gate row n followed by up row n (scales/zeros: the gate groups,
+// then the up groups) -- so weight staging and dequant see an ordinary K' = 2K matrix. The
+// activation k-block of step kb is kb mod K/64 (X is read twice per tile, the second time from
+// L2), the MMA accumulates the first K/64 steps into the tile's gate accumulator and the rest into
+// its up accumulator (same TMEM lanes, the next BT columns), and the epilogue writes
+// silu(g) * u with g and u first rounded to the output type and silu_f32 as the silu-mul kernel
+// computes it, so the bits equal separate gate / up GEMMs followed by that kernel: the [rows, 2F]
+// intermediate and its extra pass disappear.
 //
 // Dequant numerics (MODE), bit-exact with the reference in every case:
 //   kRowsExact   (DSV4, dsv4_packed_linear.py:52-56): w = RNE((q - z) * s) with the product in fp32.
@@ -43,6 +52,7 @@ struct RowsParams {
   const void* const* zptr;    // [E] zeros
   const CUtensorMap* smaps;   // [E] TMA maps over scales / zeros stored [G, N] (sz_tma only)
   const CUtensorMap* zmaps;
+  int kb_x;                   // SwiGLU mode: activation k-blocks (K / 2 / 64); else unused
   int s_dtype, z_dtype;
   long long s_stride_n, s_stride_g;
   int gs;                     // k per scale group (a multiple of the k held by one 32-bit word)
@@ -63,14 +73,15 @@ constexpr int kRowsDqGroups = 4;
 constexpr int kRowsEpiWarp0 = 4 + 4 * kRowsDqGroups;
 constexpr int kRowsThreads = 32 * (kRowsEpiWarp0 + 4);
 
-template <int WBITS, int BT, int ACC_STAGES, int X_STAGES, int W_STAGES, int A_STAGES>
+template <int WBITS, int BT, int ACC_STAGES, int X_STAGES, int W_STAGES, int A_STAGES, bool SWIGLU = false>
 struct RowsCfg {
   static constexpr int kKbBytes = 64 * WBITS / 8;               // packed bytes of one row per 64-k block
   static constexpr int kWBytes = 128 * kKbBytes;                 // 2 KB (int2) / 4 KB (int4)
   static constexpr int kSOff = kWBytes;                          // scale rows of the block (<= 512 B)
   static constexpr int kZOff = kWBytes + 512;                    // zero rows of the block (<= 512 B)
   static constexpr int kWStageBytes = kWBytes + 1024;
-  static constexpr int kAccCols = ACC_STAGES * BT;
+  static constexpr int kAccStride = SWIGLU ? 2 * BT : BT;        // TMEM columns of one accumulator stage
+  static constexpr int kAccCols = ACC_STAGES * kAccStride;
   static constexpr int kACols = A_STAGES * 32;
   static_assert(kAccCols + kACols <= 512, "TMEM budget");
   static_assert(W_STAGES % kRowsDqGroups == 0 && A_STAGES % kRowsDqGroups == 0,
@@ -136,10 +147,10 @@ __device__ __forceinline__ uint32_t rows_dq(uint32_t mq, const RowsConst<BF16, M
 }
 
 template <bool BF16, int WBITS, int MODE, bool HAS_LO, int BT, int ACC_STAGES, int X_STAGES, int W_STAGES,
-          int A_STAGES>
+          int A_STAGES, bool SWIGLU = false>
 __global__ void __launch_bounds__(kRowsThreads, 1)
     rows_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const RowsParams p) {
-  using Cfg = RowsCfg<WBITS, BT, ACC_STAGES, X_STAGES, W_STAGES, A_STAGES>;
+  using Cfg = RowsCfg<WBITS, BT, ACC_STAGES, X_STAGES, W_STAGES, A_STAGES, SWIGLU>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* x_smem = smem;
@@ -231,7 +242,8 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
           const int sx = it % X_STAGES, px = (it / X_STAGES) & 1;
           if (!mbar_wait(&empty_x[sx], px ^ 1, abort_flag, kDevErrTmaEmpty)) { ok = false; break; }
           mbar_arrive_expect_tx(&full_x[sx], Cfg::kXStageBytes);
-          tma_load_2d(x_smem + sx * Cfg::kXStageBytes, &tmap_x, &full_x[sx], kb * 64, m0);
+          const int kx = SWIGLU ? (kb < p.kb_x ? kb : kb - p.kb_x) : kb;  // gate half, then up half
+          tma_load_2d(x_smem + sx * Cfg::kXStageBytes, &tmap_x, &full_x[sx], kx * 64, m0);
           x_armed[sx] = px;
         }
       }
@@ -284,8 +296,12 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
         const int sc = tcount % ACC_STAGES, pc = (tcount / ACC_STAGES) & 1;
         if (!mbar_wait(&empty_acc[sc], pc ^ 1, abort_flag, kDevErrAccEmpty)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + (uint32_t)(sc * BT);
+        const uint32_t d_tmem0 = tmem_base + (uint32_t)(sc * Cfg::kAccStride);
         for (int kb = 0; kb < KB; ++kb, ++it) {
+          // SwiGLU: the up half accumulates into the next BT columns, starting afresh
+          const bool second = SWIGLU && kb >= p.kb_x;
+          const uint32_t d_tmem = d_tmem0 + (second ? (uint32_t)BT : 0u);
+          const int kacc = second ? kb - p.kb_x : kb;
           const int sx = it % X_STAGES, px = (it / X_STAGES) & 1;
           const int sa = it % A_STAGES, pa = (it / A_STAGES) & 1;
           if (!mbar_wait(&full_x[sx], px, abort_flag, kDevErrTmaFull)) { ok = false; break; }
@@ -295,7 +311,7 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
           const uint32_t a_tmem = tmem_base + (uint32_t)(Cfg::kAccCols + sa * 32);
 #pragma unroll
           for (int j = 0; j < 4; ++j)
-            tc_mma_ts(d_tmem, a_tmem + j * 8, smem_desc_kmajor_sw128(xaddr + j * 32), idesc, (kb | j) != 0 ? 1u : 0u);
+            tc_mma_ts(d_tmem, a_tmem + j * 8, smem_desc_kmajor_sw128(xaddr + j * 32), idesc, (kacc | j) != 0 ? 1u : 0u);
           issued = true;
           tc_commit(&empty_x[sx]);
           tc_commit(&empty_a[sa]);
@@ -494,14 +510,37 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
       if (!mbar_wait(&full_acc[sc], pc, abort_flag, kDevErrAccFull)) break;
       tc_fence_after();
       __syncwarp();
-      const uint32_t tbase = tmem_base + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(sc * BT);
+      const uint32_t tbase = tmem_base + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(sc * Cfg::kAccStride);
       const int nch = min(BT / 32, (mend - m0 + 31) / 32);  // chunks holding valid rows
 #pragma unroll 1
       for (int c = 0; c < nch; ++c) {
+        const int r0 = m0 + c * 32;
+        if constexpr (SWIGLU) {
+          // 16 rows at a time: the gate and up values of 32 rows at once would not fit the registers
+#pragma unroll 1
+          for (int hh = 0; hh < 2; ++hh) {
+            uint32_t gq[16], uq[16];
+            tmem_ld_32x32b_x16(tbase + (uint32_t)(c * 32 + 16 * hh), gq);
+            tmem_ld_32x32b_x16(tbase + (uint32_t)(BT + c * 32 + 16 * hh), uq);
+            tc_wait_ld();
+            if (nvalid) {
+              const int rh = r0 + 16 * hh;
+              uint16_t* dst = p.out + (long long)rh * p.ldc + n;
+#pragma unroll
+              for (int i = 0; i < 16; ++i)
+                if (rh + i < mend) {
+                  // the gate and up outputs as their own GEMMs would store them, then silu(g) * u
+                  const float gv = bits_to_f32(f32_to_bits(__uint_as_float(gq[i]) + bv, odt), odt);
+                  const float uv = bits_to_f32(f32_to_bits(__uint_as_float(uq[i]) + bv, odt), odt);
+                  dst[(long long)i * p.ldc] = f32_to_bits(silu_f32(gv) * uv, odt);
+                }
+            }
+          }
+          continue;
+        }
         uint32_t v[32];
         tmem_ld_32x32b_x32(tbase + (uint32_t)(c * 32), v);
         tc_wait_ld();
-        const int r0 = m0 + c * 32;
         if (nvalid) {
           uint16_t* dst = p.out + (long long)r0 * p.ldc + n;
 #pragma unroll

@@ -166,8 +166,7 @@ __global__ void silu_mul_kernel(const uint16_t* __restrict__ g, const uint16_t* 
     const int p = (int)(i / F), f = (int)(i % F);
     const float gv = bits_to_f32(g[(long long)p * ld_in + f], dt);
     const float uv = bits_to_f32(u[(long long)p * ld_in + f], dt);
-    const float s = gv / (1.f + expf(-gv));
-    h[(long long)p * ld_out + f] = f32_to_bits(s * uv, dt);
+    h[(long long)p * ld_out + f] = f32_to_bits(silu_f32(gv) * uv, dt);
   }
 }
 

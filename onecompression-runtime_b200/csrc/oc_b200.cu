@@ -307,6 +307,47 @@ int oc_b200_nvls_allreduce_bf16(void* mc_ptr, int64_t n_elems, void* const* flag
   return launch_check("nvls_allreduce_bf16");
 }
 
+int oc_b200_nvls_allreduce_rmsnorm_bf16(void* mc_ptr, int rows, int cols, const void* gain, float eps,
+                                        void* const* flags_dev, int rank, int world, uint32_t epoch, int blocks,
+                                        oc_stream_t stream_) {
+  if (!mc_ptr || !flags_dev) return fail(OC_ERR_INVALID, "nvls_allreduce_rmsnorm: NULL pointer");
+  constexpr int kMaxCols = oc::kArNormMaxVpl * 32 * 8;
+  if (rows < 0 || cols < 8 || cols % 8 != 0 || cols > kMaxCols || !aligned(mc_ptr, 16) ||
+      (gain && !aligned(gain, 16)))
+    return fail(OC_ERR_INVALID,
+                "nvls_allreduce_rmsnorm: %d x %d at %p, gain %p (cols a multiple of 8 up to %d, 16-byte aligned "
+                "rows and gain)", rows, cols, mc_ptr, gain, kMaxCols);
+  if (!(eps >= 0.f) || !(eps < 1e30f)) return fail(OC_ERR_INVALID, "nvls_allreduce_rmsnorm: eps=%g", (double)eps);
+  if (world < 1 || world > oc::kArMaxWorld || rank < 0 || rank >= world)
+    return fail(OC_ERR_INVALID, "nvls_allreduce_rmsnorm: rank %d of %d (at most %d ranks)", rank, world,
+                oc::kArMaxWorld);
+  if (blocks < 1 || blocks > oc::kArMaxBlocks)
+    return fail(OC_ERR_INVALID, "nvls_allreduce_rmsnorm: blocks=%d (1..%d)", blocks, oc::kArMaxBlocks);
+  if (rows == 0) return OC_OK;
+  oc::ArNormParams p{};
+  p.ar.mc = reinterpret_cast<uint4*>(mc_ptr);
+  p.ar.n16 = (long long)rows * (cols / 8);
+  p.ar.flags = reinterpret_cast<uint32_t* const*>(flags_dev);
+  p.ar.rank = rank;
+  p.ar.world = world;
+  p.ar.epoch = epoch;
+  const int wait_us = g_opt_wait_us.load();
+  p.ar.wait_ns = wait_us > 0 ? 1000ull * (unsigned long long)wait_us : (unsigned long long)OC_WAIT_NS;
+  p.rows = rows;
+  p.cols = cols;
+  p.gain = reinterpret_cast<const uint4*>(gain);
+  p.eps = eps;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream_);
+  const int vpl = (cols / 8 + 31) / 32;  // 16-byte vectors per lane
+  if (vpl <= 4)
+    oc::nvls_allreduce_rmsnorm_bf16_kernel<4><<<blocks, oc::kArNormThreads, 0, s>>>(p);
+  else if (vpl <= 8)
+    oc::nvls_allreduce_rmsnorm_bf16_kernel<8><<<blocks, oc::kArNormThreads, 0, s>>>(p);
+  else
+    oc::nvls_allreduce_rmsnorm_bf16_kernel<16><<<blocks, oc::kArNormThreads, 0, s>>>(p);
+  return launch_check("nvls_allreduce_rmsnorm_bf16");
+}
+
 // ---------------------------------------------------------------- unpack / pack / dequant
 int oc_b200_gptq_unpack(const int32_t* qweight, int K, int N, int wbits, int32_t* w_int, oc_stream_t stream) {
   if (!qweight || !w_int || K <= 0 || N <= 0) return fail(OC_ERR_INVALID, "gptq_unpack: bad arguments");
@@ -1460,10 +1501,10 @@ extern "C" int oc_b200_rows_layer_create(int E, const uint8_t* const* packed, in
 
 namespace {
 
-template <bool BF16, int WB, int MODE, bool HL, int BT, int ACC, int XS, int WS, int AS>
+template <bool BF16, int WB, int MODE, bool HL, int BT, int ACC, int XS, int WS, int AS, bool SWIGLU = false>
 int launch_rows_t(const CUtensorMap& tx, const oc::RowsParams& p, int dev, cudaStream_t stream) {
-  using Cfg = oc::RowsCfg<WB, BT, ACC, XS, WS, AS>;
-  auto kern = oc::rows_gemm_tc_kernel<BF16, WB, MODE, HL, BT, ACC, XS, WS, AS>;
+  using Cfg = oc::RowsCfg<WB, BT, ACC, XS, WS, AS, SWIGLU>;
+  auto kern = oc::rows_gemm_tc_kernel<BF16, WB, MODE, HL, BT, ACC, XS, WS, AS, SWIGLU>;
   static bool attr_set[kMaxDevices] = {};
   if (dev >= 0 && dev < kMaxDevices && !attr_set[dev]) {
     std::lock_guard<std::mutex> lk(g_mu);
@@ -1481,9 +1522,16 @@ int launch_rows_t(const CUtensorMap& tx, const oc::RowsParams& p, int dev, cudaS
 }
 
 template <bool BF16, int WB, int MODE, bool HL>
-int launch_rows_bt(int bt, const CUtensorMap& tx, const oc::RowsParams& p, int dev, cudaStream_t stream) {
+int launch_rows_bt(int bt, const CUtensorMap& tx, const oc::RowsParams& p, int dev, cudaStream_t stream,
+                   bool swiglu) {
   // The weight ring is deep (16-32 stages of 3-5 KB) because packed weights stream from HBM with
   // ~2 us of latency; activation tiles come from L2 and need fewer stages.
+  if (swiglu) {  // one accumulator stage of 2 x 128 columns (gate, up) beside the 8 A stages
+    if constexpr (WB == 2)
+      return launch_rows_t<BF16, WB, MODE, HL, 128, 1, 6, 32, 8, true>(tx, p, dev, stream);
+    else
+      return launch_rows_t<BF16, WB, MODE, HL, 128, 1, 4, 24, 8, true>(tx, p, dev, stream);
+  }
   if (bt == 128) {
     if constexpr (WB == 2)
       return launch_rows_t<BF16, WB, MODE, HL, 128, 2, 6, 32, 8>(tx, p, dev, stream);
@@ -1495,47 +1543,53 @@ int launch_rows_bt(int bt, const CUtensorMap& tx, const oc::RowsParams& p, int d
 
 template <bool BF16>
 int launch_rows(int bt, int wbits, int mode, bool has_lo, const CUtensorMap& tx, const oc::RowsParams& p, int dev,
-                cudaStream_t stream) {
-  if (mode == oc::kRowsRtn) return launch_rows_bt<BF16, 4, oc::kRowsRtn, false>(bt, tx, p, dev, stream);
+                cudaStream_t stream, bool swiglu) {
+  if (mode == oc::kRowsRtn) return launch_rows_bt<BF16, 4, oc::kRowsRtn, false>(bt, tx, p, dev, stream, swiglu);
   if (wbits == 4)
-    return has_lo ? launch_rows_bt<BF16, 4, oc::kRowsExact, true>(bt, tx, p, dev, stream)
-                  : launch_rows_bt<BF16, 4, oc::kRowsExact, false>(bt, tx, p, dev, stream);
-  return has_lo ? launch_rows_bt<BF16, 2, oc::kRowsExact, true>(bt, tx, p, dev, stream)
-                : launch_rows_bt<BF16, 2, oc::kRowsExact, false>(bt, tx, p, dev, stream);
+    return has_lo ? launch_rows_bt<BF16, 4, oc::kRowsExact, true>(bt, tx, p, dev, stream, swiglu)
+                  : launch_rows_bt<BF16, 4, oc::kRowsExact, false>(bt, tx, p, dev, stream, swiglu);
+  return has_lo ? launch_rows_bt<BF16, 2, oc::kRowsExact, true>(bt, tx, p, dev, stream, swiglu)
+                : launch_rows_bt<BF16, 2, oc::kRowsExact, false>(bt, tx, p, dev, stream, swiglu);
 }
 
-}  // namespace
-
-extern "C" int oc_b200_rows_gemm(const oc_b200_layer* L, const void* a, int a_dtype, int64_t M, int64_t lda,
-                                 const int32_t* offsets, const void* bias, int bias_dtype, void* c, int64_t ldc,
-                                 oc_stream_t stream_) {
-  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
-  if (!L || L->kind != 1) return fail(OC_ERR_INVALID, "rows_gemm: not a row-packed layer");
-  if (M < 0) return fail(OC_ERR_INVALID, "rows_gemm: M=%lld", (long long)M);
+// Shared body of oc_b200_rows_gemm and oc_b200_rows_gemm_swiglu (swiglu: the layer is the [F, 2K]
+// gate|up matrix; A has K = K_in / 2 columns and C gets silu(gate) * up, F columns).
+int rows_gemm_impl(const oc_b200_layer* L, const void* a, int a_dtype, int64_t M, int64_t lda, const int32_t* offsets,
+                   const void* bias, int bias_dtype, void* c, int64_t ldc, cudaStream_t stream, bool swiglu) {
+  const char* nm = swiglu ? "rows_gemm_swiglu" : "rows_gemm";
+  if (!L || L->kind != 1) return fail(OC_ERR_INVALID, "%s: not a row-packed layer", nm);
+  if (M < 0) return fail(OC_ERR_INVALID, "%s: M=%lld", nm, (long long)M);
+  const int k_act = swiglu ? L->K_in / 2 : L->K_in;
+  if (swiglu && (L->K_in % 128 != 0 || L->gs >= L->K_in || k_act % L->gs != 0))
+    return fail(OC_ERR_INVALID,
+                "%s: the layer must be a gate|up matrix of 2K columns with K a multiple of 64 and of the groupsize "
+                "(K_in=%d, groupsize=%d)", nm, L->K_in, L->gs);
   if (M == 0) return OC_OK;
-  if (!a || !c) return fail(OC_ERR_INVALID, "rows_gemm: NULL activation/output");
-  if (!dt16(a_dtype)) return fail(OC_ERR_INVALID, "rows_gemm: activations must be f16 or bf16");
-  if (L->E > 1 && !offsets) return fail(OC_ERR_INVALID, "rows_gemm: expert groups need offsets");
-  if (bias && (offsets || !dtf(bias_dtype))) return fail(OC_ERR_INVALID, "rows_gemm: bias (dense layers only)");
-  if (lda < L->K_in || lda % 8 != 0 || !aligned(a, 16))
-    return fail(OC_ERR_INVALID, "rows_gemm: A must be 16-byte aligned with lda %% 8 == 0");
-  if (ldc < L->N || !aligned(c, 2)) return fail(OC_ERR_INVALID, "rows_gemm: ldc");
-  if (M > 0x7fffffffLL) return fail(OC_ERR_INVALID, "rows_gemm: M too large");
+  if (!a || !c) return fail(OC_ERR_INVALID, "%s: NULL activation/output", nm);
+  if (!dt16(a_dtype)) return fail(OC_ERR_INVALID, "%s: activations must be f16 or bf16", nm);
+  if (L->E > 1 && !offsets) return fail(OC_ERR_INVALID, "%s: expert groups need offsets", nm);
+  if (bias && (offsets || swiglu || !dtf(bias_dtype))) return fail(OC_ERR_INVALID, "%s: bias (dense layers only)", nm);
+  if (lda < k_act || lda % 8 != 0 || !aligned(a, 16))
+    return fail(OC_ERR_INVALID, "%s: A must be 16-byte aligned with lda %% 8 == 0", nm);
+  if (ldc < L->N || !aligned(c, 2)) return fail(OC_ERR_INVALID, "%s: ldc", nm);
+  if (M > 0x7fffffffLL) return fail(OC_ERR_INVALID, "%s: M too large", nm);
   int dev = 0;
   if (int rc = current_device(&dev)) return rc;
-  if (dev != L->device) return fail(OC_ERR_INVALID, "rows_gemm: layer lives on device %d", L->device);
+  if (dev != L->device) return fail(OC_ERR_INVALID, "%s: layer lives on device %d", nm, L->device);
   const bool bf16 = a_dtype == OC_DT_BF16;
   int bt = g_opt_tile.load();
   if (bt != 128 && bt != 192) bt = offsets ? 128 : 192;
+  if (swiglu) bt = 128;
   CUtensorMap tx;
   if (int rc = make_tmap_2d(&tx, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a,
-                            (uint64_t)L->K_in, (uint64_t)M, (uint64_t)lda * 2, 64, (uint32_t)bt,
+                            (uint64_t)k_act, (uint64_t)M, (uint64_t)lda * 2, 64, (uint32_t)bt,
                             CU_TENSOR_MAP_SWIZZLE_128B))
     return rc;
   oc::RowsParams p{};
   p.M = (int)M;
   p.N = L->N;
   p.K = L->K_in;
+  p.kb_x = k_act / 64;
   p.E = L->E;
   p.offsets = offsets;
   p.wmaps = L->d_wmaps;
@@ -1558,8 +1612,23 @@ extern "C" int oc_b200_rows_gemm(const oc_b200_layer* L, const void* a, int a_dt
   p.ldc = ldc;
   p.n_tiles_n = (L->N + 127) / 128;
   const bool has_lo = L->s_dtype_r != a_dtype;
-  if (bf16) return launch_rows<true>(bt, L->wbits, L->mode, has_lo, tx, p, dev, stream);
-  return launch_rows<false>(bt, L->wbits, L->mode, has_lo, tx, p, dev, stream);
+  if (bf16) return launch_rows<true>(bt, L->wbits, L->mode, has_lo, tx, p, dev, stream, swiglu);
+  return launch_rows<false>(bt, L->wbits, L->mode, has_lo, tx, p, dev, stream, swiglu);
+}
+
+}  // namespace
+
+extern "C" int oc_b200_rows_gemm(const oc_b200_layer* L, const void* a, int a_dtype, int64_t M, int64_t lda,
+                                 const int32_t* offsets, const void* bias, int bias_dtype, void* c, int64_t ldc,
+                                 oc_stream_t stream) {
+  return rows_gemm_impl(L, a, a_dtype, M, lda, offsets, bias, bias_dtype, c, ldc,
+                        reinterpret_cast<cudaStream_t>(stream), false);
+}
+
+extern "C" int oc_b200_rows_gemm_swiglu(const oc_b200_layer* L, const void* a, int a_dtype, int64_t M, int64_t lda,
+                                        const int32_t* offsets, void* c, int64_t ldc, oc_stream_t stream) {
+  return rows_gemm_impl(L, a, a_dtype, M, lda, offsets, nullptr, 0, c, ldc, reinterpret_cast<cudaStream_t>(stream),
+                        true);
 }
 
 // ---------------------------------------------------------------- decode GEMV without a workspace

@@ -65,6 +65,7 @@ _SIGNATURES = {
     "oc_b200_rows_layer_create": ([_i, _p, _i64, _i, _p, _i, _p, _i, _i64, _i64, _i, _i, _i, _i, _p, _p,
                                    ctypes.POINTER(_p)], _i),
     "oc_b200_rows_gemm": ([_p, _p, _i, _i64, _i64, _p, _p, _i, _p, _i64, _p], _i),
+    "oc_b200_rows_gemm_swiglu": ([_p, _p, _i, _i64, _i64, _p, _p, _i64, _p], _i),
     "oc_b200_moe_route": ([_p, _i, _i, _i, _i, _i, _p, _p, _p], _i),
     "oc_b200_moe_permute": ([_p, _i, _i, _i, _p, _p, _p, _p, _p], _i),
     "oc_b200_gather_rows": ([_p, _i64, _p, _i, _i, _p, _i64, _p], _i),
@@ -72,6 +73,8 @@ _SIGNATURES = {
     "oc_b200_moe_combine": ([_p, _i64, _p, _p, _i, _i, _i, _p, _i64, _p, _i64, _i, _p], _i),
     "oc_b200_im2col_1d": ([_p, _i64, _i64, _i, _i, _i, _i, _i, _i, _i, _i, _i, _p, _i64, _p], _i),
     "oc_b200_nvls_allreduce_bf16": ([_p, _i64, _p, _i, _i, ctypes.c_uint32, _i, _p], _i),
+    "oc_b200_nvls_allreduce_rmsnorm_bf16": ([_p, _i, _i, _p, ctypes.c_float, _p, _i, _i, ctypes.c_uint32, _i, _p],
+                                            _i),
 }
 
 

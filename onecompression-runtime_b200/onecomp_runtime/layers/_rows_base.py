@@ -54,6 +54,13 @@ class RowsHandle:
                   None if bias is None else bias.data_ptr(), _lib.DT[bias.dtype] if bias is not None else 0,
                   out.data_ptr(), out.stride(0), _lib.stream_of(a.device))
 
+    def gemm_swiglu(self, a: torch.Tensor, out: torch.Tensor, offsets: torch.Tensor | None = None) -> None:
+        """``out = silu(a @ gate.T) * (a @ up.T)`` for a handle built on [N, 2K] gate|up matrices
+        (``oc_b200_rows_gemm_swiglu``); ``a`` has K = self.K / 2 columns."""
+        _lib.call("oc_b200_rows_gemm_swiglu", self.h, a.data_ptr(), _lib.DT[a.dtype], a.shape[0], a.stride(0),
+                  None if offsets is None else offsets.data_ptr(), out.data_ptr(), out.stride(0),
+                  _lib.stream_of(a.device))
+
     def close(self):
         if self.h is not None:
             try:

@@ -9,8 +9,9 @@ HBM and one call does:
 1. ``route``: softmax over expert logits (fp32), top-k, renormalised weights;
 2. ``permute``: stable per-expert ranking -> ``offsets[E+1]``, ``sorted_token``,
    ``slot_pos``; rows of x gathered into expert-contiguous order;
-3. ``expert_ffn``: grouped GEMMs over the expert segments -- gate and up, then
-   ``silu(gate) * up``, then down;
+3. ``expert_ffn``: grouped GEMMs over the expert segments -- gate, up and
+   ``silu(gate) * up`` in one launch (each expert's gate and up matrices stored as one
+   [F, 2K] gate|up matrix at load time), then down;
 4. ``combine``: ``y[t] = sum_j w[t,j] * out[slot_pos[t,j]] (+ shared(x)[t])``.
 
 Expert parallelism (``ExpertParallelMoE``): experts are split contiguously
@@ -177,33 +178,65 @@ class PackedMoE(torch.nn.Module):
         self.renorm = bool(renorm)
         self.device = dev
 
+        def shape(m: dict):
+            return (int(m["wbits"]), int(m["groupsize"]), int(m["in_features"]), int(m["qweight_packed"].shape[0]),
+                    int(m["qweight_packed"].shape[1]))
+
         def build(mats: list[dict]):
-            p0 = mats[0]
-            wbits, gs, K = int(p0["wbits"]), int(p0["groupsize"]), int(p0["in_features"])
-            N = int(p0["qweight_packed"].shape[0])
+            wbits, gs, K, N, _ = shape(mats[0])
             q = [m["qweight_packed"].to(dev).contiguous() for m in mats]
             # scales / zeros group-major ([G, N]): the kernel stages each block's rows by TMA
             s = [group_major(m["scales"].to(dev), N, K, gs) for m in mats]
             z = [group_major(m["qzeros"].to(dev), N, K, gs) for m in mats]
             return RowsHandle(q, s, z, wbits, gs if gs > 0 else K, K, N, MODE_EXACT, 1, N)
 
-        self._h = {name: build([ex[name] for ex in experts]) for name in ("gate", "up", "down")}
-        self._shared = {name: build([shared[name]]) for name in ("gate", "up", "down")} if shared else None
-        self.hidden = self._h["gate"].K
-        self.ffn = self._h["gate"].N
+        def gate_up(gates: list[dict], ups: list[dict]):
+            """One [F, 2K] gate|up matrix per expert (row n = gate row n, then up row n; groups: the
+            gate's, then the up's) for the fused SwiGLU launch, or None where the layout does not
+            allow it (then gate and up stay two matrices)."""
+            wbits, gs, K, N, ldb = shape(gates[0])
+            if any(shape(m) != shape(gates[0]) for m in gates + ups):
+                return None
+            if K % 64 or not (0 < gs < K) or K % gs or ldb * 8 != K * wbits or ldb % 16:
+                return None
+            q = [torch.cat([g["qweight_packed"].to(dev), u["qweight_packed"].to(dev)], dim=1).contiguous()
+                 for g, u in zip(gates, ups)]
+            s = [torch.cat([group_major(g["scales"].to(dev), N, K, gs), group_major(u["scales"].to(dev), N, K, gs)])
+                 for g, u in zip(gates, ups)]
+            z = [torch.cat([group_major(g["qzeros"].to(dev), N, K, gs), group_major(u["qzeros"].to(dev), N, K, gs)])
+                 for g, u in zip(gates, ups)]
+            if len({t.dtype for t in s}) != 1 or len({t.dtype for t in z}) != 1:
+                return None
+            return RowsHandle(q, s, z, wbits, gs, 2 * K, N, MODE_EXACT, 1, N)
+
+        def handles(ex: list[dict]) -> dict:
+            gu = gate_up([e["gate"] for e in ex], [e["up"] for e in ex])
+            h = {"gate_up": gu} if gu is not None else {n: build([e[n] for e in ex]) for n in ("gate", "up")}
+            h["down"] = build([e["down"] for e in ex])
+            return h
+
+        self._h = handles(experts)
+        self._shared = handles([shared]) if shared else None
+        g0 = experts[0]["gate"]
+        self.hidden = int(g0["in_features"])
+        self.ffn = int(g0["qweight_packed"].shape[0])
 
     def _ffn(self, handles, xs: torch.Tensor, offsets: torch.Tensor | None) -> torch.Tensor:
         from . import _lib
         P = xs.shape[0]
         if P == 0:
             return xs.new_empty((0, handles["down"].N))
-        F_ = handles["gate"].N
-        g = torch.empty((P, 2 * F_), dtype=xs.dtype, device=xs.device)
-        handles["gate"].gemm(xs, g[:, :F_], offsets)
-        handles["up"].gemm(xs, g[:, F_:], offsets)
-        h = torch.empty((P, F_), dtype=xs.dtype, device=xs.device)
-        _lib.call("oc_b200_silu_mul", g.data_ptr(), g[:, F_:].data_ptr(), g.stride(0), P, F_, h.data_ptr(),
-                  h.stride(0), _lib.DT[xs.dtype], _lib.stream_of(xs.device))
+        if "gate_up" in handles:   # gate, up and silu(gate) * up in one grouped launch
+            h = torch.empty((P, handles["gate_up"].N), dtype=xs.dtype, device=xs.device)
+            handles["gate_up"].gemm_swiglu(xs, h, offsets)
+        else:
+            F_ = handles["gate"].N
+            g = torch.empty((P, 2 * F_), dtype=xs.dtype, device=xs.device)
+            handles["gate"].gemm(xs, g[:, :F_], offsets)
+            handles["up"].gemm(xs, g[:, F_:], offsets)
+            h = torch.empty((P, F_), dtype=xs.dtype, device=xs.device)
+            _lib.call("oc_b200_silu_mul", g.data_ptr(), g[:, F_:].data_ptr(), g.stride(0), P, F_, h.data_ptr(),
+                      h.stride(0), _lib.DT[xs.dtype], _lib.stream_of(xs.device))
         y = torch.empty((P, handles["down"].N), dtype=xs.dtype, device=xs.device)
         handles["down"].gemm(h, y, offsets)
         return y

@@ -145,16 +145,39 @@ class NvlsReducer:
     def view(self, r0: int, r1: int) -> torch.Tensor:
         return self.buffer[r0:r1]
 
-    def all_reduce_async(self, t: torch.Tensor) -> _Pending:
-        """Sum ``t`` (a row range of ``buffer``) over the ranks, in place, on the side stream."""
+    def _offset(self, t: torch.Tensor) -> int:
         off = t.data_ptr() - self.buffer.data_ptr()
         if not (t.is_contiguous() and 0 <= off and off + t.numel() * 2 <= self.buffer.numel() * 2):
             raise ValueError("NvlsReducer: the tensor must be a contiguous row range of the buffer")
+        return off
+
+    def all_reduce_async(self, t: torch.Tensor, rms_norm_eps: float | None = None,
+                         gain: torch.Tensor | None = None) -> _Pending:
+        """Sum ``t`` (a row range of ``buffer``) over the ranks, in place, on the side stream.
+
+        With ``rms_norm_eps`` the same kernel pass also normalizes every row of the sum,
+        ``s * rsqrt(mean(s**2) + eps)`` (times ``gain``, a [cols] bf16 vector, when given), each
+        rank normalizing only its share of the rows (``oc_b200_nvls_allreduce_rmsnorm_bf16``).
+        """
+        off = self._offset(t)
+        if rms_norm_eps is not None and (off % (2 * self.buffer.shape[1]) or t.numel() % self.buffer.shape[1]):
+            raise ValueError("NvlsReducer: the normalized range must be whole rows of the buffer")
+        if rms_norm_eps is not None and gain is not None:
+            if gain.dtype != torch.bfloat16 or gain.numel() != self.buffer.shape[1] or not gain.is_contiguous():
+                raise ValueError("NvlsReducer: gain must be a contiguous bf16 vector of the buffer's width")
         self.epoch += 1
         cur = torch.cuda.current_stream()
         self.stream.wait_stream(cur)
-        self._lib.call("oc_b200_nvls_allreduce_bf16", self._mc + off, t.numel(), self._flag_ptrs, self.rank,
-                       self.world, self.epoch & 0xFFFFFFFF, self.blocks, self.stream.cuda_stream)
+        if rms_norm_eps is None:
+            self._lib.call("oc_b200_nvls_allreduce_bf16", self._mc + off, t.numel(), self._flag_ptrs, self.rank,
+                           self.world, self.epoch & 0xFFFFFFFF, self.blocks, self.stream.cuda_stream)
+        else:
+            cols = self.buffer.shape[1]
+            self._lib.call("oc_b200_nvls_allreduce_rmsnorm_bf16", self._mc + off, t.numel() // cols, cols,
+                           None if gain is None else gain.data_ptr(), float(rms_norm_eps), self._flag_ptrs,
+                           self.rank, self.world, self.epoch & 0xFFFFFFFF, self.blocks, self.stream.cuda_stream)
+            if gain is not None:
+                gain.record_stream(self.stream)
         done = torch.cuda.Event()
         done.record(self.stream)
         return _Pending(done)
@@ -182,7 +205,8 @@ class RowParallelInt4Linear(torch.nn.Module):
             out.copy_(self.local(x) if residual is None else self.local(x) + residual)
 
     def forward_async(self, x: torch.Tensor, residual: torch.Tensor | None = None,
-                      out: torch.Tensor | None = None, reducer: "NvlsReducer | None" = None):
+                      out: torch.Tensor | None = None, reducer: "NvlsReducer | None" = None,
+                      rms_norm_eps: float | None = None):
         """Start ``all_reduce(x_shard @ W_shard.T) + bias + residual`` for one chunk of rows.
 
         Runs the local GEMM on the current stream into ``out`` (allocated when None) and issues its
@@ -191,8 +215,11 @@ class RowParallelInt4Linear(torch.nn.Module):
         one rank) orders the current stream after the reduction; ``out`` must not be read before.
         The residual is added by rank 0 only, so the sum carries it once. With a ``reducer``,
         ``out`` is a row range of its symmetric buffer and the sum runs on NVLink SHARP
-        (``NvlsReducer``) instead of NCCL.
+        (``NvlsReducer``) instead of NCCL; ``rms_norm_eps`` (reducer only) makes that reduction also
+        RMS-normalize every row, so ``out`` then holds the normalized sum.
         """
+        if rms_norm_eps is not None and reducer is None:
+            raise ValueError("forward_async: rms_norm_eps needs an NvlsReducer (the norm runs in its kernel)")
         if out is None:
             out = torch.empty((x.shape[0], self.local.out_features), dtype=x.dtype, device=x.device)
         world = dist.get_world_size(self.group) if dist.is_initialized() else 1
@@ -201,7 +228,7 @@ class RowParallelInt4Linear(torch.nn.Module):
         if world == 1:
             return out, None
         if reducer is not None:   # out is a row range of the reducer's symmetric buffer
-            return out, reducer.all_reduce_async(out)
+            return out, reducer.all_reduce_async(out, rms_norm_eps=rms_norm_eps)
         return out, dist.all_reduce(out, op=dist.ReduceOp.SUM, group=self.group, async_op=True)
 
     def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:

@@ -163,3 +163,20 @@ def test_rows_layer_validation(lib):
     assert lib.oc_b200_rows_gemm(None, p, 1, 4, 512, None, None, 0, p, 256, None) != 0
     assert lib.oc_b200_rows_table_bytes(0) == 0
     assert lib.oc_b200_rows_table_bytes(3) > 0 and lib.oc_b200_rows_table_bytes(3) % 256 == 0
+
+
+def test_fused_entry_points_reject_bad_arguments_before_any_launch(lib):
+    """The fused SwiGLU grouped GEMM and the all-reduce + RMS norm check their arguments on the host."""
+    from onecomp_runtime import _lib
+    assert lib.oc_b200_rows_gemm_swiglu(None, None, 1, 4, 64, None, None, 64, None) == 1
+    assert "not a row-packed layer" in _lib.last_error()
+    buf = ctypes.create_string_buffer(64)
+    p = ctypes.cast(buf, ctypes.c_void_p)
+    args = (p, 4, 4096, None, 1e-6, p, 0, 2, 1, 8, None)
+    assert lib.oc_b200_nvls_allreduce_rmsnorm_bf16(None, *args[1:]) == 1          # no buffer
+    assert lib.oc_b200_nvls_allreduce_rmsnorm_bf16(p, 4, 4100, *args[3:]) == 1     # cols not a multiple of 8
+    assert lib.oc_b200_nvls_allreduce_rmsnorm_bf16(p, 4, 8192, *args[3:]) == 1     # wider than a warp's row
+    assert lib.oc_b200_nvls_allreduce_rmsnorm_bf16(p, 4, 4096, None, -1.0, *args[5:]) == 1   # eps
+    assert lib.oc_b200_nvls_allreduce_rmsnorm_bf16(*args[:6], 2, 2, *args[8:]) == 1   # rank outside the job
+    assert lib.oc_b200_nvls_allreduce_rmsnorm_bf16(*args[:9], 65, None) == 1          # blocks
+    assert lib.oc_b200_nvls_allreduce_rmsnorm_bf16(p, 0, 4096, *args[3:]) == 0        # no rows: nothing to do

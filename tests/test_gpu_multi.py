@@ -147,6 +147,87 @@ def test_nvls_allreduce_two_gpus(tmp_path):
     assert err < 2e-2, err
 
 
+def _nvls_norm_worker(rank, world, port, out_path):
+    """The NVLS all-reduce with the RMS norm in the same kernel: against torch's rms_norm of the
+    plain NVLS sum of the same rows (one bf16 ulp), with and without a gain, on a 4096-wide buffer
+    (the config-4 hidden size) and a 520-wide one (a partial last vector per lane); rows outside
+    the normalized range stay as they were; then a tensor-parallel block whose two reductions
+    normalize, against the block on one GPU."""
+    dev = _init(rank, world, port)
+    from onecomp_runtime import _lib
+    from onecomp_runtime.layers import FusedInt4Linear
+    from onecomp_runtime.tensor_parallel import NvlsReducer, build_tp_block
+    from onecomp_runtime.testing import gptq_layer
+    F = torch.nn.functional
+    try:
+        reds = [NvlsReducer(300, 4096, blocks=8), NvlsReducer(37, 520, blocks=4)]
+    except RuntimeError:
+        torch.save(torch.tensor([-1.0, -1.0, -1.0]), out_path) if rank == 0 else None
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+        return
+    bad = 0.0
+    for i, red in enumerate(reds):
+        R, C = red.buffer.shape
+        vals = [torch.randn(R, C, generator=torch.Generator(device=dev).manual_seed(60 + 7 * i + r), device=dev)
+                .mul(3.0).to(torch.bfloat16) for r in range(world)]
+        gain = torch.rand(C, generator=torch.Generator(device=dev).manual_seed(99 + i), device=dev).add(0.5) \
+            .to(torch.bfloat16)
+        red.buffer.copy_(vals[rank])
+        red.all_reduce_async(red.buffer).wait()
+        s = red.buffer.clone()                                   # the switch's bf16 sum
+        for g in (None, gain):
+            red.buffer.copy_(vals[rank])
+            r0 = 5 if R > 100 else 0
+            red.all_reduce_async(red.view(r0, R), rms_norm_eps=1e-6, gain=g).wait()
+            ref = F.rms_norm(s[r0:].float(), (C,), eps=1e-6)
+            if g is not None:
+                ref = ref * g.float()
+            y = red.buffer[r0:].float()
+            bad += float(((y - ref).abs() > ref.abs() * 2.0 ** -7 + 1e-30).sum())
+            bad += float((red.buffer[:r0] != vals[rank][:r0]).sum())   # rows outside the range untouched
+    torch.cuda.synchronize(dev)
+    bad += _lib.read_device_error(dev)
+
+    def make(t, K, N):
+        return FusedInt4Linear(K, N, t["qweight"], t["scales"], t["qzeros"], t.get("bias"), 32)
+
+    tens = {n: gptq_layer(K, N, 32, seed=70 + i, device=dev) for i, (n, K, N) in enumerate(LAYERS)}
+    x = torch.randn(300, 512, generator=torch.Generator(device=dev).manual_seed(1), device=dev).to(torch.bfloat16)
+    blk = build_tp_block(tens, LAYERS, rank, world, 32, make, chunks=2)
+    r1, r2 = NvlsReducer(300, 512, blocks=8), NvlsReducer(300, 512, blocks=8)
+    ys = []
+    for a, b in ((0, 160), (160, 300)):
+        o, w = blk["out"].forward_async(blk["qkv"](x[a:b])[:, :512 // world], residual=x[a:b], out=r1.view(a, b),
+                                        reducer=r1, rms_norm_eps=1e-6)
+        w.wait()
+        y, w2 = blk["fc2"].forward_async(blk["fc1"](o, activation="gelu_tanh"), residual=o, out=r2.view(a, b),
+                                         reducer=r2, rms_norm_eps=1e-6)
+        w2.wait()
+        ys.append(y.clone())
+    y = torch.cat(ys)
+    torch.cuda.synchronize(dev)
+    if rank == 0:
+        full = {n: make(tens[n], K, N) for n, K, N in LAYERS}
+        h = F.rms_norm((x + full["out"](full["qkv"](x)[:, :512])).float(), (512,), eps=1e-6).to(torch.bfloat16)
+        ref = F.rms_norm((h + full["fc2"](F.gelu(full["fc1"](h), approximate="tanh"))).float(), (512,), eps=1e-6)
+        err = float((y.float() - ref).abs().max() / ref.abs().max())
+        torch.save(torch.tensor([bad, err, 0.0]), out_path)
+    torch.distributed.barrier()
+    torch.distributed.destroy_process_group()
+
+
+def test_nvls_allreduce_rmsnorm_two_gpus(tmp_path):
+    _need_gpus(2)
+    out = tmp_path / "nvls_norm.pt"
+    mp.spawn(_nvls_norm_worker, args=(2, _free_port(), str(out)), nprocs=2, join=True)
+    bad, err, _ = (float(v) for v in torch.load(out))
+    if bad < 0:
+        pytest.skip("no NVLink multicast on these GPUs")
+    assert bad == 0
+    assert err < 2e-2, err
+
+
 def _ep_worker(rank, world, port, out_path, with_shared):
     dev = _init(rank, world, port)
     from onecomp_runtime.moe import ExpertParallelMoE, PackedMoE

@@ -231,6 +231,51 @@ def test_moe_expert_parallel_combine_and_shared(cuda_device, T):
             assert float((y_ep.float() - ref).abs().max() / ref.abs().max()) < 1e-2
 
 
+@pytest.mark.parametrize("grouped", [True, False])
+def test_swiglu_launch_matches_separate_gemms(cuda_device, grouped):
+    """The fused gate|up launch (oc_b200_rows_gemm_swiglu) gives the same bits as the gate and up
+    GEMMs run separately followed by the silu-mul kernel: grouped over 8 int2 gs64 experts with
+    ragged segments (an empty expert and one of 150 rows: two m-tiles), and dense on the int4 gs128
+    shared expert."""
+    from onecomp_runtime import _lib
+    from onecomp_runtime.layers._rows_base import MODE_EXACT, RowsHandle, group_major
+    from onecomp_runtime.moe import PackedMoE
+    experts, shared = _moe_setup(E=8, H=256, F=384)
+    moe = PackedMoE(experts, shared, k=2, device=cuda_device)
+    hs = moe._h if grouped else moe._shared
+    assert "gate_up" in hs
+    mats = experts if grouped else [shared]
+    counts = [20, 0, 150, 7, 33, 64, 1, 90] if grouped else [77]
+    P = sum(counts)
+    offsets = torch.tensor([0] + list(np.cumsum(counts)), dtype=torch.int32, device=cuda_device)
+    x = torch.randn(P, 256, generator=torch.Generator(device=cuda_device).manual_seed(5),
+                    device=cuda_device).to(torch.bfloat16)
+    m0 = mats[0]["gate"]
+    wbits, gs, K, F = int(m0["wbits"]), int(m0["groupsize"]), int(m0["in_features"]), 384
+
+    def handle(name):
+        dev = cuda_device
+        return RowsHandle([m[name]["qweight_packed"].to(dev).contiguous() for m in mats],
+                          [group_major(m[name]["scales"].to(dev), F, K, gs) for m in mats],
+                          [group_major(m[name]["qzeros"].to(dev), F, K, gs) for m in mats],
+                          wbits, gs, K, F, MODE_EXACT, 1, F)
+
+    off = offsets if grouped else None
+    g = torch.empty((P, 2 * F), dtype=torch.bfloat16, device=cuda_device)
+    handle("gate").gemm(x, g[:, :F], off)
+    handle("up").gemm(x, g[:, F:], off)
+    ref = torch.empty((P, F), dtype=torch.bfloat16, device=cuda_device)
+    st = _lib.stream_of(cuda_device)
+    _lib.call("oc_b200_silu_mul", g.data_ptr(), g[:, F:].data_ptr(), g.stride(0), P, F, ref.data_ptr(),
+              ref.stride(0), _lib.DT[torch.bfloat16], st)
+    h = torch.full((P, F), float("nan"), dtype=torch.bfloat16, device=cuda_device)
+    _lib.call("oc_b200_rows_gemm_swiglu", hs["gate_up"].h, x.data_ptr(), _lib.DT[torch.bfloat16], P, x.stride(0),
+              None if off is None else off.data_ptr(), h.data_ptr(), h.stride(0), st)
+    torch.cuda.synchronize(cuda_device)
+    assert torch.equal(h.view(torch.int16), ref.view(torch.int16))
+    assert _lib.read_device_error(cuda_device) == 0
+
+
 def test_no_device_errors_recorded(cuda_device):
     from onecomp_runtime import _lib
     assert _lib.read_device_error(cuda_device) == 0
