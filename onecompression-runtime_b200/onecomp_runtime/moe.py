@@ -164,10 +164,12 @@ class PackedMoE(torch.nn.Module):
     packed dicts (``qweight_packed``, ``scales``, ``qzeros``, ``wbits``,
     ``groupsize``, ``in_features``), the format ``Dsv4PackedLinear`` takes.
     All routed experts share one shape. ``forward(x [T, H], logits [T, E])``.
+    ``fuse_gate_up`` (default) stores each expert's gate and up matrices as one gate|up matrix and
+    runs gate, up and silu(gate) * up as one launch wherever the layout allows it.
     """
 
     def __init__(self, experts: list[dict], shared: dict | None = None, k: int = 8, renorm: bool = True,
-                 device="cuda"):
+                 device="cuda", fuse_gate_up: bool = True):
         super().__init__()
         from . import _lib
         from .layers._rows_base import MODE_EXACT, RowsHandle, group_major
@@ -210,7 +212,7 @@ class PackedMoE(torch.nn.Module):
             return RowsHandle(q, s, z, wbits, gs, 2 * K, N, MODE_EXACT, 1, N)
 
         def handles(ex: list[dict]) -> dict:
-            gu = gate_up([e["gate"] for e in ex], [e["up"] for e in ex])
+            gu = gate_up([e["gate"] for e in ex], [e["up"] for e in ex]) if fuse_gate_up else None
             h = {"gate_up": gu} if gu is not None else {n: build([e[n] for e in ex]) for n in ("gate", "up")}
             h["down"] = build([e["down"] for e in ex])
             return h
