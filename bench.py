@@ -646,6 +646,8 @@ def bench_cfg2(args, job: Job, peaks: dict) -> dict:
         _lib.set_option(_lib.OPT_GEMV_CTAS, args.gemv_ctas)
     if args.gemv_impl >= 0:
         _lib.set_option(_lib.OPT_GEMV_IMPL, args.gemv_impl)
+    if args.gemv_prep >= 0:
+        _lib.set_option(_lib.OPT_GEMV_PREP, args.gemv_prep)
     dev = job.dev
     layers, nbytes = [], 0
     w8 = args.wbits == 8
@@ -818,6 +820,9 @@ def main():
     ap.add_argument("--wbits", type=int, default=4, choices=[4, 8], help="cfg2 only: code width of the layer set")
     ap.add_argument("--gemv-impl", type=int, default=-1, choices=[-1, 0, 1, 2, 3, 4],
                     help="cfg2: decode kernel (OC_OPT_GEMV_IMPL; -1 = library default, the integer-MMA GEMV)")
+    ap.add_argument("--gemv-prep", type=int, default=-1, choices=[-1, 0, 1],
+                    help="cfg2: OC_OPT_GEMV_PREP (-1 = library default: the integer GEMV prepares its activations "
+                         "in each CTA at M <= 2)")
     ap.add_argument("--blocks", type=int, default=0, help="override the number of DiT blocks (profiling only)")
     ap.add_argument("--moe-experts", type=int, default=0, help="cfg3: override the expert count (profiling only)")
     ap.add_argument("--moe-tokens", type=int, default=0, help="cfg3: override tokens per GPU (profiling only)")

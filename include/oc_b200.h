@@ -51,9 +51,13 @@ enum {
   OC_OPT_TEST_STALL = 7,   /* failure tests: s > 0 makes the first CTA of each TMA decode GEMV leave stage
                               s - 1 unissued, so a wait runs out, the kernel records OC_ERR_DEVICE's code,
                               skips that tile's output and leaves its tickets re-armed; 0 (default) off */
-  OC_OPT_TC_MAX_CTAS = 8   /* persistent tcgen05 GEMMs (GPTQ and row-packed): at most this many CTAs,
+  OC_OPT_TC_MAX_CTAS = 8,  /* persistent tcgen05 GEMMs (GPTQ and row-packed): at most this many CTAs,
                               0 (default) one per SM; a tensor-parallel job leaves SMs to the NCCL
                               all-reduce that overlaps the next chunk's GEMM */
+  OC_OPT_GEMV_PREP = 9     /* integer decode GEMV, one token, no act-order permutation: 1 (default) each CTA
+                              prepares the activations of its K split itself (at most 20 stages of 128 k per
+                              split, else as 0), 0 a separate preparation launch into the workspace (always
+                              used for M > 1 and act-order layers); identical results */
 };
 
 /* ---- library / device ------------------------------------------------------ */

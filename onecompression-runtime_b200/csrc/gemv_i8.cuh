@@ -58,27 +58,16 @@ constexpr int kX8RecOff = 256;                 // record: int32 sum X per 32-k q
 // memory: the two token rows that one quarter-warp reads then use disjoint banks.
 
 // ---- activation preparation ------------------------------------------------------------------
-// One thread per (token, 8-k word of the kernel's K order); the 16 threads of a half-warp are one
-// stage. x element k of the kernel order is x[m, kperm[k]] (kperm null: x[m, k]); indices outside
-// [0, K) and words past Kp give 0.
+// One thread per (token, 8-k word of the kernel's K order); the 16 threads of a half-warp (all
+// active: half_mask) are one stage and write its 320-byte row `row`. x element k of the kernel
+// order is x[m, kperm[k]] (kperm null: x[m, k]); indices outside [0, K) and words past Kp give 0.
+// The permutation is part of the layer, so it is read before waiting for the kernel that wrote x.
 template <bool BF16>
-__global__ void __launch_bounds__(256) x8_prepare_kernel(const uint16_t* __restrict__ x, long long ldx, int M, int K,
-                                                         const int32_t* __restrict__ kperm, int Kp, int KB,
-                                                         uint8_t* __restrict__ out) {
-  griddep_launch_dependents();
-  const long long total = (long long)M * KB * 16;
-  const long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  // total is a multiple of 16, so a half-warp is either wholly inside or wholly past it
-  if (gid >= total) return;
-  const unsigned half_mask = 0xFFFFu << (threadIdx.x & 16);
-  const int m = (int)(gid / ((long long)KB * 16));
-  const int rem = (int)(gid - (long long)m * KB * 16);
-  const int kb = rem >> 4, w = rem & 15;
+__device__ __forceinline__ void x8_prepare_word(const uint16_t* __restrict__ x, long long ldx, int K,
+                                                const int32_t* __restrict__ kperm, int Kp, int m, int kb, int w,
+                                                unsigned half_mask, uint8_t* __restrict__ row) {
   const int k0 = kb * kX8StageK + 8 * w;  // first k (kernel order) of this word
   const bool in = k0 < Kp;                // Kp is a multiple of 8: a word is wholly in or out
-
-  // source columns: the permutation is part of the layer, so it is read before waiting for the
-  // kernel that produced x
   int src[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
@@ -169,10 +158,26 @@ __global__ void __launch_bounds__(256) x8_prepare_kernel(const uint16_t* __restr
     d1e |= hi_e << (8 * i);
     d1o |= hi_o << (8 * i);
   }
-  uint8_t* row = out + ((long long)m * KB + kb) * kX8RowBytes;
   *reinterpret_cast<uint4*>(row + 16 * w) = make_uint4(d0e, d0o, d1e, d1o);
   if ((w & 3) == 0) *reinterpret_cast<int*>(row + kX8RecOff + (w >> 2) * 4) = sx;
   if (w == 0) *reinterpret_cast<float*>(row + kX8RecOff + 16) = scale;
+}
+
+// The preparation as its own launch, into the workspace layout [M][stages][320 B].
+template <bool BF16>
+__global__ void __launch_bounds__(256) x8_prepare_kernel(const uint16_t* __restrict__ x, long long ldx, int M, int K,
+                                                         const int32_t* __restrict__ kperm, int Kp, int KB,
+                                                         uint8_t* __restrict__ out) {
+  griddep_launch_dependents();
+  const long long total = (long long)M * KB * 16;
+  const long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  // total is a multiple of 16, so a half-warp is either wholly inside or wholly past it
+  if (gid >= total) return;
+  const unsigned half_mask = 0xFFFFu << (threadIdx.x & 16);
+  const int m = (int)(gid / ((long long)KB * 16));
+  const int rem = (int)(gid - (long long)m * KB * 16);
+  const int kb = rem >> 4, w = rem & 15;
+  x8_prepare_word<BF16>(x, ldx, K, kperm, Kp, m, kb, w, half_mask, out + ((long long)m * KB + kb) * kX8RowBytes);
 }
 
 // ---- the GEMV ----------------------------------------------------------------------------------
@@ -181,21 +186,30 @@ __global__ void __launch_bounds__(256) x8_prepare_kernel(const uint16_t* __restr
 // flight than an 8-row one.
 // Every slot is a multiple of 128 bytes: a tiled TMA copy needs a 128-byte aligned shared-memory
 // destination (1024 bytes for the 128-byte swizzle of the weight slabs).
-template <int MT, int SPS, int XR>
+// PREP (the host uses it for one token without a K permutation; the kernel takes M <= 2): the CTA
+// prepares the activations of its whole K split itself, into a region of kPrepMaxStages x
+// [2 tokens][320 B] after the ring, instead of a separate launch writing them to the workspace and
+// a TMA copy per stage bringing them back (the ring then carries no activation slot; kSmemBytes
+// leaves out the prepared region, which the launch adds).
+constexpr int kPrepMaxStages = 20;
+template <int MT, int SPS, int XR, bool PREP = false>
 struct G8Cfg {
   static constexpr int kWBytes = 4 * 16 * 128;           // four [16 rows][32 words] slabs, 128B-swizzled
   static constexpr int kSBytes = SPS * kGemvCols * 2;    // one scale row per segment
   static constexpr int kZBytes = (SPS * (kGemvCols / 8) * 4 + 127) / 128 * 128;  // zero rows, padded
-  static constexpr int kXBytes = XR * kX8RowBytes;       // [XR tokens][320 B]
+  static constexpr int kXBytes = PREP ? 0 : XR * kX8RowBytes;  // [XR tokens][320 B]
   static constexpr int kStage = kWBytes + kSBytes + kZBytes + kXBytes;
-  static constexpr int kBudget = (MT == 1 ? 98 : 94) * 1024;
+  static constexpr int kBudget = (PREP ? 86 : (MT == 1 ? 98 : 94)) * 1024;
   static constexpr int kDepth = kBudget / kStage > 12 ? 12 : kBudget / kStage;
   static constexpr int kWOff = 0;
   static constexpr int kSOff = kDepth * kWBytes;
   static constexpr int kZOff = kSOff + kDepth * kSBytes;
   static constexpr int kXOff = kZOff + kDepth * kZBytes;
   static constexpr int kBarOff = kXOff + kDepth * kXBytes;
-  static constexpr int kSmemBytes = kBarOff + 2 * kDepth * 8 + 16 + 1024 /*align*/;
+  static constexpr int kPrepOff = (kBarOff + 2 * kDepth * 8 + 16 + 127) / 128 * 128;
+  static constexpr int kPrepRowBytes = 2 * kX8RowBytes;  // one stage: [2 tokens][320 B]
+  static constexpr int kSmemBytes = (PREP ? kPrepOff : kBarOff + 2 * kDepth * 8 + 16) + 1024 /*align*/;
+  static_assert(!PREP || (MT == 1 && XR == 2), "the CTA prepares activations for up to 2 tokens");
   static_assert(kWBytes % 1024 == 0 && kSBytes % 128 == 0 && kZBytes % 128 == 0 && kXBytes % 128 == 0,
                 "TMA destinations: 1024-byte swizzled weight slabs, 128-byte aligned other slots");
   static_assert(kSOff % 128 == 0 && kZOff % 128 == 0 && kXOff % 128 == 0, "128-byte aligned slot arrays");
@@ -234,12 +248,14 @@ __device__ __forceinline__ void mma_i8(int (&d)[4], const uint32_t (&a)[4], uint
 // the activation box (2 for M <= 2, else 8 MT; rows past M are zero-filled by the copy).
 // gp.cluster: the splits of a tile reduce in their cluster (launched with cluster dims
 // (1, splits, 1)); otherwise through the workspace, as the other decode GEMVs.
-template <bool BF16, int MT, int SPS, bool ODD, int XR>
+// PREP: the consumers prepare the split's activations from gp.x8 / gp.kperm (x8_prepare_word) before
+// their first stage; tmap_x is unused.
+template <bool BF16, int MT, int SPS, bool ODD, int XR, bool PREP = false>
 __global__ void __launch_bounds__(kGtThreads, 2)
     gptq_gemv_i8_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_s,
                         const __grid_constant__ CUtensorMap tmap_z, const __grid_constant__ CUtensorMap tmap_x,
                         const GtParams gp) {
-  using Cfg = G8Cfg<MT, SPS, XR>;
+  using Cfg = G8Cfg<MT, SPS, XR, PREP>;
   constexpr int kCons = kGtConsumerWarps;
   const GemvParams& p = gp.g;
   extern __shared__ __align__(1024) uint8_t g8_raw[];
@@ -283,7 +299,7 @@ __global__ void __launch_bounds__(kGtThreads, 2)
       tma_prefetch_desc(&tmap_w);
       tma_prefetch_desc(&tmap_s);
       tma_prefetch_desc(&tmap_z);
-      tma_prefetch_desc(&tmap_x);
+      if constexpr (!PREP) tma_prefetch_desc(&tmap_x);
       // bytes the copies of one stage deliver (the zero slot's padding is not copied)
       const uint32_t bytes = Cfg::kWBytes + SPS * (kGemvCols * 2 + kGemvCols / 2) + Cfg::kXBytes;
       int armed[Cfg::kDepth];
@@ -305,19 +321,22 @@ __global__ void __launch_bounds__(kGtThreads, 2)
         tma_load_2d(smem + Cfg::kXOff + s * Cfg::kXBytes, &tmap_x, &full[s], (kb0 + i) * kX8RowWords, 0);
       };
       const int stall = (blockIdx.x == 0 && blockIdx.y == 0) ? gp.stall_stage - 1 : -1;
-      // weights of the first stages before the previous kernel (the activation preparation) ends
+      // weights of the first stages before the previous kernel (the activation preparation) ends;
+      // with PREP the producer copies layer constants only and never waits for it
       const int pre = nst < Cfg::kDepth ? nst : Cfg::kDepth;
       for (int i = 0; i < pre; ++i)
         if (i != stall) load_wsz(i);
-      griddep_wait();
-      for (int i = 0; i < pre; ++i)
-        if (i != stall) load_x(i);
+      if constexpr (!PREP) {
+        griddep_wait();
+        for (int i = 0; i < pre; ++i)
+          if (i != stall) load_x(i);
+      }
       for (int i = pre; i < nst; ++i) {
         const int s = i % Cfg::kDepth;
         if (!mbar_wait_ns(&empty[s], ((i / Cfg::kDepth) & 1) ^ 1, abort_flag, kDevErrWEmpty, gp.wait_ns)) break;
         if (i == stall) continue;
         load_wsz(i);
-        load_x(i);
+        if constexpr (!PREP) load_x(i);
       }
       // the CTA must not exit with a bulk copy in flight: wait (bounded) for every armed stage
       for (int s = 0; s < Cfg::kDepth; ++s)
@@ -398,6 +417,24 @@ __global__ void __launch_bounds__(kGtThreads, 2)
     }
   };
 
+  if constexpr (PREP) {
+    // this split's activations, [stage][token][320 B], one half-warp per (token, stage); the weight
+    // stages keep landing meanwhile
+    const int items = p.M * nst * 16;   // a multiple of 16: half-warps are wholly in or out
+    const unsigned half_mask = 0xFFFFu << (threadIdx.x & 16);
+    for (int base = 0; base < items; base += kCons * 32) {
+      const int it = base + threadIdx.x;
+      if (it < items) {
+        const int m = it / (nst * 16);
+        const int rem = it - m * nst * 16;
+        const int j = rem >> 4;
+        x8_prepare_word<BF16>(p.x, p.ldx, gp.k_in, gp.kperm, p.Kp, m, kb0 + j, rem & 15, half_mask,
+                              smem + Cfg::kPrepOff + j * Cfg::kPrepRowBytes + m * kX8RowBytes);
+      }
+    }
+    named_bar_sync(4, kCons * 32);
+  }
+
   bool ok = true;
   for (int i = kh; i < nst; i += 2) {
     const int s = i % Cfg::kDepth;
@@ -408,7 +445,7 @@ __global__ void __launch_bounds__(kGtThreads, 2)
     const uint8_t* wst = smem + Cfg::kWOff + s * Cfg::kWBytes + wn * 2048;
     const uint8_t* sst = smem + Cfg::kSOff + s * Cfg::kSBytes;
     const uint8_t* zst = smem + Cfg::kZOff + s * Cfg::kZBytes;
-    const uint8_t* xst = smem + Cfg::kXOff + s * Cfg::kXBytes;
+    const uint8_t* xst = PREP ? smem + Cfg::kPrepOff + i * Cfg::kPrepRowBytes : smem + Cfg::kXOff + s * Cfg::kXBytes;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {  // 32-k step within the stage
       constexpr int kStepsPerSeg = 4 / SPS;

@@ -69,6 +69,8 @@ struct GtParams {
   int stall_stage;    // failure test only: > 0 leaves stage stall_stage - 1 of CTA (0, 0) unissued,
                       // so its consumers' wait runs out; 0 in normal use
   int cluster;        // integer GEMV: the K splits of a tile are one cluster and reduce in it
+  const int32_t* kperm;  // integer GEMV preparing its own activations (g.x in the caller's K
+  int k_in;              // order, g.ldx): the layer's K permutation (or null) and its K
 };
 
 template <bool BF16, int MT, int WB = 4>

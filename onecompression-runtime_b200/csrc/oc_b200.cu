@@ -56,6 +56,7 @@ std::atomic<int> g_opt_wait_us{0}, g_opt_test_stall{0};
 // persistent tcgen05 GEMMs: at most this many CTAs (0: one per SM), leaving SMs to a collective
 // that runs beside them
 std::atomic<int> g_opt_tc_max_ctas{0};
+std::atomic<int> g_opt_gemv_prep{1};
 
 constexpr int kMaxDevices = 64;
 // Tickets at the head of every GEMV workspace, zero between launches (each launch re-arms the ones it
@@ -224,6 +225,10 @@ int oc_b200_set_option(int key, int value) {
       if (value < 0) return fail(OC_ERR_INVALID, "OC_OPT_TC_MAX_CTAS: %d", value);
       g_opt_tc_max_ctas = value;
       return OC_OK;
+    case OC_OPT_GEMV_PREP:
+      if (value < 0 || value > 1) return fail(OC_ERR_INVALID, "OC_OPT_GEMV_PREP: %d", value);
+      g_opt_gemv_prep = value;
+      return OC_OK;
     case OC_OPT_TEST_STALL:
       if (value < 0) return fail(OC_ERR_INVALID, "OC_OPT_TEST_STALL: %d", value);
       g_opt_test_stall = value;
@@ -243,6 +248,7 @@ int oc_b200_get_option(int key, int* value) {
     case OC_OPT_WAIT_US: *value = g_opt_wait_us.load(); return OC_OK;
     case OC_OPT_TEST_STALL: *value = g_opt_test_stall.load(); return OC_OK;
     case OC_OPT_TC_MAX_CTAS: *value = g_opt_tc_max_ctas.load(); return OC_OK;
+    case OC_OPT_GEMV_PREP: *value = g_opt_gemv_prep.load(); return OC_OK;
   }
   return fail(OC_ERR_INVALID, "unknown option %d", key);
 }
@@ -767,6 +773,17 @@ GemvPlan gemv_plan(const oc_b200_layer* L, int dev) {
 // reduce inside their thread-block cluster, more through the workspace.
 bool i8_cluster(int splits) { return splits > 1 && splits <= kI8ClusterMax; }
 
+// The integer GEMV prepares its activations inside the GEMV (no preparation launch, no workspace
+// copy) for one token when the layer has no K permutation and a K split spans at most
+// kPrepMaxStages stages. Measured per layer on the config-2 shapes (B200, CUDA graph of copies
+// of one layer): M = 1 without act-order 0.3-1.4 us faster; with act-order every CTA would gather
+// its split's activation columns with scattered 2-byte loads (hundreds of CTAs, the same columns)
+// and the down layer ran 3 us slower (7 us at M = 2); at M = 2 without act-order mixed
+// (-1.4 to +1.0 us). Those cases keep the preparation launch.
+bool i8_prep(int64_t M, int kb_per_split, bool has_kperm) {
+  return g_opt_gemv_prep.load() != 0 && M == 1 && !has_kperm && kb_per_split <= oc::kPrepMaxStages;
+}
+
 // Tokens per tcgen05 tile when the caller leaves it to the library: the preset with the
 // least (waves of persistent CTAs) x (measured time of one tile at K = 3072 on B200, us).
 // 384 and 448 are two sub-tiles of 192 / 224 tokens sharing each dequantized weight stage.
@@ -927,13 +944,15 @@ int launch_gemv_tma(const oc_b200_layer* L, const oc::GemvParams& p, const GemvP
 // GEMV over them; both launched with programmatic stream serialization.
 template <auto Kern>
 int launch_g8_k(int smem, dim3 grid, cudaStream_t stream, const oc_b200_layer* L, const CUtensorMap& tx,
-                const oc::GtParams& g) {
+                const oc::GtParams& g, int smem_extra = 0) {
   static bool attr_set[kMaxDevices] = {};
   int dev = 0;
   if (int rc = current_device(&dev)) return rc;
   if (dev >= 0 && dev < kMaxDevices && !attr_set[dev]) {
     std::lock_guard<std::mutex> lk(g_mu);
-    if (int rc = cuda_check(cudaFuncSetAttribute(Kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+    // the largest size any launch of this kernel asks for (PREP adds the prepared stages)
+    const int most = smem + (smem_extra ? oc::kPrepMaxStages * 2 * oc::kX8RowBytes : 0);
+    if (int rc = cuda_check(cudaFuncSetAttribute(Kern, cudaFuncAttributeMaxDynamicSharedMemorySize, most),
                             "cudaFuncSetAttribute(gemv i8 smem)"))
       return rc;
     attr_set[dev] = true;
@@ -942,7 +961,7 @@ int launch_g8_k(int smem, dim3 grid, cudaStream_t stream, const oc_b200_layer* L
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(oc::kGtThreads);
-  cfg.dynamicSmemBytes = (size_t)smem;
+  cfg.dynamicSmemBytes = (size_t)(smem + smem_extra);
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -961,6 +980,20 @@ int launch_g8_k(int smem, dim3 grid, cudaStream_t stream, const oc_b200_layer* L
 template <bool BF16, int MT, bool ODD, int XR>
 int launch_g8_sps(const oc_b200_layer* L, dim3 grid, cudaStream_t stream, const CUtensorMap& tx,
                   const oc::GtParams& g) {
+  if (g.k_in > 0) {  // PREP: the CTAs prepare their activations (M <= 2)
+    if constexpr (MT == 1 && XR == 2) {
+      const int extra = g.kb_per_split * 2 * oc::kX8RowBytes;
+      if (L->gt_rows == 4)
+        return launch_g8_k<oc::gptq_gemv_i8_kernel<BF16, 1, 4, ODD, 2, true>>(oc::G8Cfg<1, 4, 2, true>::kSmemBytes,
+                                                                              grid, stream, L, tx, g, extra);
+      if (L->gt_rows == 2)
+        return launch_g8_k<oc::gptq_gemv_i8_kernel<BF16, 1, 2, ODD, 2, true>>(oc::G8Cfg<1, 2, 2, true>::kSmemBytes,
+                                                                              grid, stream, L, tx, g, extra);
+      return launch_g8_k<oc::gptq_gemv_i8_kernel<BF16, 1, 1, ODD, 2, true>>(oc::G8Cfg<1, 1, 2, true>::kSmemBytes,
+                                                                            grid, stream, L, tx, g, extra);
+    }
+    return fail(OC_ERR_UNSUPPORTED, "gemv_i8: activation preparation in the GEMV needs M <= 2");
+  }
   if (L->gt_rows == 4)
     return launch_g8_k<oc::gptq_gemv_i8_kernel<BF16, MT, 4, ODD, XR>>(oc::G8Cfg<MT, 4, XR>::kSmemBytes, grid, stream,
                                                                       L, tx, g);
@@ -975,15 +1008,22 @@ template <bool BF16>
 int launch_gemv_i8(const oc_b200_layer* L, const void* a, int64_t lda, const oc::GemvParams& p, const GemvPlan& gp,
                    int n_tiles, uint8_t* xd, cudaStream_t stream) {
   const int KB = (L->Kp + oc::kX8StageK - 1) / oc::kX8StageK;
-  const long long threads = (long long)p.M * KB * 16;
-  if (int rc = launch_pdl(oc::x8_prepare_kernel<BF16>, dim3((unsigned)((threads + 255) / 256)), dim3(256), 0, stream,
-                          "x8_prepare", reinterpret_cast<const uint16_t*>(a), (long long)lda, p.M, L->K_in,
-                          L->kperm, L->Kp, KB, xd))
-    return rc;
   oc::GtParams g{};
   g.g = p;
-  g.rows_sz = L->gt_rows;
   g.kb_per_split = gp.kstep / (oc::kGtBK / 32);
+  if (i8_prep(p.M, g.kb_per_split, L->kperm != nullptr)) {  // each CTA prepares its split's activations
+    g.g.x = reinterpret_cast<const uint16_t*>(a);
+    g.g.ldx = lda;
+    g.kperm = L->kperm;
+    g.k_in = L->K_in;
+  } else {
+    const long long threads = (long long)p.M * KB * 16;
+    if (int rc = launch_pdl(oc::x8_prepare_kernel<BF16>, dim3((unsigned)((threads + 255) / 256)), dim3(256), 0,
+                            stream, "x8_prepare", reinterpret_cast<const uint16_t*>(a), (long long)lda, p.M, L->K_in,
+                            L->kperm, L->Kp, KB, xd))
+      return rc;
+  }
+  g.rows_sz = L->gt_rows;
   const int wait_us = g_opt_wait_us.load();
   g.wait_ns = wait_us > 0 ? 1000ull * (unsigned long long)wait_us : (unsigned long long)OC_WAIT_NS;
   g.stall_stage = g_opt_test_stall.load();

@@ -26,6 +26,7 @@ OPT_TC_PAIR = 5
 OPT_WAIT_US = 6
 OPT_TEST_STALL = 7
 OPT_TC_MAX_CTAS = 8
+OPT_GEMV_PREP = 9
 ACT_NONE = 0
 ACT_GELU_TANH = 1
 

@@ -407,6 +407,63 @@ def test_tc_pairs_full_size(cuda_device, pair_option):
     assert _lib.read_device_error(cuda_device) == 0
 
 
+I8_PREP_SHAPES = [
+    # K, N, gs, v1, act-order, scales dtype. One token without act-order: K splits of up to 20 stages
+    # take the in-GEMV preparation; the others (a 43-stage split, act-order, M = 2) take the launch
+    # whatever the option, which the test checks gives the same bits too
+    (5120, 8192, 128, False, False, torch.float16),   # config-2 q/k/v shape: 4 splits, workspace reduction
+    (17408, 5120, 128, False, False, torch.float16),  # config-2 down shape: 7 splits
+    (5120, 17408, 128, False, False, torch.float16),  # config-2 gate shape: 2 splits reduced in a cluster
+    (3072, 1024, 32, True, False, torch.bfloat16),    # four groups per stage
+    (4160, 384, 64, True, False, torch.bfloat16),     # K not a multiple of the 128-k stage
+    (5504, 19200, 128, False, False, torch.float16),  # 150 column tiles, one split of 43 stages
+    (5120, 8192, 128, False, True, torch.float16),    # act-order
+]
+
+
+@pytest.mark.parametrize("shape", I8_PREP_SHAPES, ids=lambda s: f"K{s[0]}N{s[1]}g{s[2]}a{int(s[4])}")
+@pytest.mark.parametrize("M", [1, 2])
+def test_gemv_i8_prep_in_kernel_matches_launch(cuda_device, shape, M):
+    """The integer decode GEMV prepares the activations of its K split inside each CTA for one token
+    without act-order (OC_OPT_GEMV_PREP = 1, the default) instead of a separate preparation launch
+    into the workspace (0): the same bits, NaN tokens included; both against the fp64 GEMM of the
+    exact weight."""
+    from onecomp_runtime import _lib
+    from onecomp_runtime.testing import gptq_layer, activations
+    K, N, gs, v1, act, sdt = shape
+    t = {k: v.to(cuda_device) for k, v in gptq_layer(K, N, gs, seed=K + N, v1=v1, actorder=act,
+                                                     scales_dtype=sdt).items()}
+    layer = _module(t, K, N, gs, v1, "packed" if act else ("fused" if gs == 32 else "any"), cuda_device)
+    x = activations(M, K, seed=K + M).to(cuda_device)
+    r = activations(M, N, seed=M + 5).to(cuda_device)
+    saved = (_lib.get_option(_lib.OPT_GEMV_IMPL), _lib.get_option(_lib.OPT_GEMV_PREP))
+    outs = {}
+    try:
+        _lib.set_option(_lib.OPT_GEMV_IMPL, 4)
+        for prep in (1, 0):
+            _lib.set_option(_lib.OPT_GEMV_PREP, prep)
+            outs[prep] = (layer(x), layer.forward_fused(x, residual=r, activation="gelu_tanh"))
+        xn = x.clone()   # a NaN in the last token poisons that token's outputs only, on both paths
+        xn[M - 1, K // 3] = float("nan")
+        for prep in (1, 0):
+            _lib.set_option(_lib.OPT_GEMV_PREP, prep)
+            outs[prep] += (layer(xn),)
+    finally:
+        _lib.set_option(_lib.OPT_GEMV_IMPL, saved[0])
+        _lib.set_option(_lib.OPT_GEMV_PREP, saved[1])
+    for a, b in zip(outs[1], outs[0]):
+        torch.testing.assert_close(a, b, rtol=0, atol=0, equal_nan=True)
+    ref = _gpu_reference(t, K, N, x, v1, t["bias"])
+    err = float((outs[1][0].double() - ref).abs().max() / ref.abs().max())
+    assert err < 1e-2, err
+    yn = outs[1][2]
+    assert torch.isnan(yn[M - 1]).all()
+    if M == 2:
+        assert not torch.isnan(yn[0]).any()
+        torch.testing.assert_close(yn[0], outs[1][0][0], rtol=0, atol=0)
+    assert _lib.read_device_error(cuda_device) == 0
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("M", [1, 6, 16])
 def test_gemv_i8_activation_range(cuda_device, dtype, M):
