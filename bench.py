@@ -730,7 +730,7 @@ def bench_cfg3(args, job: Job, peaks: dict) -> dict:
     x = torch.randn((T, H), generator=g, device=dev).to(torch.bfloat16)
     logits = torch.randn((T, E), generator=g, device=dev)
     timer = LaunchTimer()
-    moe = PackedMoE(experts, shared, k=k, device=dev, fuse_gate_up=not args.moe_no_fuse)
+    moe = PackedMoE(experts, shared, k=k, device=dev, fuse_gate_up=False if args.moe_no_fuse else "shared")
     for h in list(moe._h.values()) + list((moe._shared or {}).values()):
         timer.wrap_rows(h)
     if world == 1:
@@ -764,8 +764,9 @@ def bench_cfg3(args, job: Job, peaks: dict) -> dict:
            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
            "config": {"workload": "cfg3", "tokens_per_gpu": T, "experts_per_gpu": el,
                       "parallelism": f"expert parallel x{world} (NCCL all_to_all)" if world > 1 else "1 GPU",
-                      "gate_up": "one SwiGLU launch (gate|up matrices)" if "gate_up" in moe._h else
-                                 "two GEMMs + silu-mul",
+                      "gate_up": {"routed": "one SwiGLU launch" if "gate_up" in moe._h else "two GEMMs + silu-mul",
+                                  "shared": "one SwiGLU launch" if "gate_up" in (moe._shared or {}) else
+                                            "two GEMMs + silu-mul"},
                       "l2_flush": "none needed: 2 GB of packed experts per layer > 126 MB L2"},
            "roofline": rt, "clocks": clk}
     del moe, experts, shared
@@ -827,7 +828,7 @@ def main():
     ap.add_argument("--moe-experts", type=int, default=0, help="cfg3: override the expert count (profiling only)")
     ap.add_argument("--moe-tokens", type=int, default=0, help="cfg3: override tokens per GPU (profiling only)")
     ap.add_argument("--moe-no-fuse", action="store_true",
-                    help="cfg3: gate and up as two grouped GEMMs + the silu-mul kernel (comparison only)")
+                    help="cfg3: the shared expert's gate and up as two GEMMs + the silu-mul kernel too (comparison)")
     ap.add_argument("--cpu-sample-m", type=int, default=512, help="tokens of the bounded CPU sample (one block)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--tp-chunks", type=int, default=0,

@@ -18,7 +18,8 @@
 // then the up groups) -- so weight staging and dequant see an ordinary K' = 2K matrix. The
 // activation k-block of step kb is kb mod K/64 (X is read twice per tile, the second time from
 // L2), the MMA accumulates the first K/64 steps into the tile's gate accumulator and the rest into
-// its up accumulator (same TMEM lanes, the next BT columns), and the epilogue writes
+// its up accumulator (two consecutive slots of the accumulator ring, each BT columns of the same
+// TMEM lanes), and the epilogue writes
 // silu(g) * u with g and u first rounded to the output type and silu_f32 as the silu-mul kernel
 // computes it, so the bits equal separate gate / up GEMMs followed by that kernel: the [rows, 2F]
 // intermediate and its extra pass disappear.
@@ -80,8 +81,7 @@ struct RowsCfg {
   static constexpr int kSOff = kWBytes;                          // scale rows of the block (<= 512 B)
   static constexpr int kZOff = kWBytes + 512;                    // zero rows of the block (<= 512 B)
   static constexpr int kWStageBytes = kWBytes + 1024;
-  static constexpr int kAccStride = SWIGLU ? 2 * BT : BT;        // TMEM columns of one accumulator stage
-  static constexpr int kAccCols = ACC_STAGES * kAccStride;
+  static constexpr int kAccCols = ACC_STAGES * BT;              // a ring of BT-column accumulator slots
   static constexpr int kACols = A_STAGES * 32;
   static_assert(kAccCols + kACols <= 512, "TMEM budget");
   static_assert(W_STAGES % kRowsDqGroups == 0 && A_STAGES % kRowsDqGroups == 0,
@@ -293,14 +293,26 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
         const int valid = min(BT, mend - m0);
         const int n_mma = valid <= 0 ? 16 : min(BT, (valid + 15) & ~15);
         const uint32_t idesc = make_idesc_f16(BF16, 128, n_mma);
-        const int sc = tcount % ACC_STAGES, pc = (tcount / ACC_STAGES) & 1;
-        if (!mbar_wait(&empty_acc[sc], pc ^ 1, abort_flag, kDevErrAccEmpty)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t d_tmem0 = tmem_base + (uint32_t)(sc * Cfg::kAccStride);
+        // accumulator slots: one per tile, two in SwiGLU mode (gate, then up), taken in turn from a
+        // ring of ACC_STAGES; a slot is free once the epilogue of its previous use has read it
+        int slot = tcount * (SWIGLU ? 2 : 1);
+        auto take = [&](int sl) {
+          if (!mbar_wait(&empty_acc[sl % ACC_STAGES], ((sl / ACC_STAGES) & 1) ^ 1, abort_flag, kDevErrAccEmpty))
+            return false;
+          tc_fence_after();
+          return true;
+        };
+        if (!take(slot)) { ok = false; break; }
+        uint32_t d_tmem = tmem_base + (uint32_t)((slot % ACC_STAGES) * BT);
         for (int kb = 0; kb < KB; ++kb, ++it) {
-          // SwiGLU: the up half accumulates into the next BT columns, starting afresh
+          // SwiGLU: the up half accumulates into the next slot, starting afresh
           const bool second = SWIGLU && kb >= p.kb_x;
-          const uint32_t d_tmem = d_tmem0 + (second ? (uint32_t)BT : 0u);
+          if (SWIGLU && kb == p.kb_x) {
+            tc_commit(&full_acc[slot % ACC_STAGES]);  // the gate accumulator is complete
+            ++slot;
+            if (!take(slot)) { ok = false; break; }
+            d_tmem = tmem_base + (uint32_t)((slot % ACC_STAGES) * BT);
+          }
           const int kacc = second ? kb - p.kb_x : kb;
           const int sx = it % X_STAGES, px = (it / X_STAGES) & 1;
           const int sa = it % A_STAGES, pa = (it / A_STAGES) & 1;
@@ -317,7 +329,7 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
           tc_commit(&empty_a[sa]);
         }
         if (!ok) break;
-        tc_commit(&full_acc[sc]);
+        tc_commit(&full_acc[slot % ACC_STAGES]);
       }
       if (!ok && issued) {
         tc_commit(drain);
@@ -501,16 +513,20 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
     const int odt = BF16 ? kBF16 : kF16;
     int tcount = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++tcount) {
-      const int sc = tcount % ACC_STAGES, pc = (tcount / ACC_STAGES) & 1;
+      const int s0 = tcount * (SWIGLU ? 2 : 1);                 // this tile's first accumulator slot
+      const int sc = s0 % ACC_STAGES, pc = (s0 / ACC_STAGES) & 1;
+      const int su = (s0 + 1) % ACC_STAGES, pu = ((s0 + 1) / ACC_STAGES) & 1;   // SwiGLU: the up slot
       int e, m0, mend, nb;
       tile_info(tile, e, m0, mend, nb);
       const int n = nb * 128 + row;
       const bool nvalid = n < p.N;
       const float bv = (p.bias && nvalid) ? load_as_f32(p.bias, p.bias_dtype, n) : 0.f;
       if (!mbar_wait(&full_acc[sc], pc, abort_flag, kDevErrAccFull)) break;
+      if (SWIGLU && !mbar_wait(&full_acc[su], pu, abort_flag, kDevErrAccFull)) break;
       tc_fence_after();
       __syncwarp();
-      const uint32_t tbase = tmem_base + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(sc * Cfg::kAccStride);
+      const uint32_t tbase = tmem_base + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(sc * BT);
+      const uint32_t ubase = tmem_base + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(su * BT);
       const int nch = min(BT / 32, (mend - m0 + 31) / 32);  // chunks holding valid rows
 #pragma unroll 1
       for (int c = 0; c < nch; ++c) {
@@ -521,7 +537,7 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
           for (int hh = 0; hh < 2; ++hh) {
             uint32_t gq[16], uq[16];
             tmem_ld_32x32b_x16(tbase + (uint32_t)(c * 32 + 16 * hh), gq);
-            tmem_ld_32x32b_x16(tbase + (uint32_t)(BT + c * 32 + 16 * hh), uq);
+            tmem_ld_32x32b_x16(ubase + (uint32_t)(c * 32 + 16 * hh), uq);
             tc_wait_ld();
             if (nvalid) {
               const int rh = r0 + 16 * hh;
@@ -550,6 +566,7 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
       }
       tc_fence_before();
       mbar_arrive(&empty_acc[sc]);
+      if (SWIGLU) mbar_arrive(&empty_acc[su]);
     }
   }
 

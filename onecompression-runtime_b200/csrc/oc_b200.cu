@@ -1566,11 +1566,18 @@ int launch_rows_bt(int bt, const CUtensorMap& tx, const oc::RowsParams& p, int d
                    bool swiglu) {
   // The weight ring is deep (16-32 stages of 3-5 KB) because packed weights stream from HBM with
   // ~2 us of latency; activation tiles come from L2 and need fewer stages.
-  if (swiglu) {  // one accumulator stage of 2 x 128 columns (gate, up) beside the 8 A stages
-    if constexpr (WB == 2)
-      return launch_rows_t<BF16, WB, MODE, HL, 128, 1, 6, 32, 8, true>(tx, p, dev, stream);
-    else
-      return launch_rows_t<BF16, WB, MODE, HL, 128, 1, 4, 24, 8, true>(tx, p, dev, stream);
+  if (swiglu) {
+    // a tile takes both slots of a two-slot accumulator ring (gate, up), so its epilogue holds the
+    // next tile's MMAs; measured variants that freed the gate slot first (three slots beside 4 A
+    // stages, or the gate outputs parked in shared memory at one activation or four weight stages
+    // fewer) ran config 3's routed experts slower (2.83-2.86 against 2.77 ms)
+    if (bt == 128) {
+      if constexpr (WB == 2)
+        return launch_rows_t<BF16, WB, MODE, HL, 128, 2, 6, 32, 8, true>(tx, p, dev, stream);
+      else
+        return launch_rows_t<BF16, WB, MODE, HL, 128, 2, 4, 24, 8, true>(tx, p, dev, stream);
+    }
+    return launch_rows_t<BF16, WB, MODE, HL, 192, 2, 5, 16, 4, true>(tx, p, dev, stream);
   }
   if (bt == 128) {
     if constexpr (WB == 2)
@@ -1619,7 +1626,6 @@ int rows_gemm_impl(const oc_b200_layer* L, const void* a, int a_dtype, int64_t M
   const bool bf16 = a_dtype == OC_DT_BF16;
   int bt = g_opt_tile.load();
   if (bt != 128 && bt != 192) bt = offsets ? 128 : 192;
-  if (swiglu) bt = 128;
   CUtensorMap tx;
   if (int rc = make_tmap_2d(&tx, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a,
                             (uint64_t)k_act, (uint64_t)M, (uint64_t)lda * 2, 64, (uint32_t)bt,

@@ -185,10 +185,11 @@ def test_moe_route_kernel_matches_convention(cuda_device):
     torch.testing.assert_close(w.cpu(), rw.cpu(), rtol=1e-5, atol=1e-6)
 
 
-def test_moe_forward(cuda_device):
+@pytest.mark.parametrize("fuse", [True, "shared", False])
+def test_moe_forward(cuda_device, fuse):
     from onecomp_runtime.moe import PackedMoE
     experts, shared = _moe_setup(E=8)
-    moe = PackedMoE(experts, shared, k=2, device=cuda_device)
+    moe = PackedMoE(experts, shared, k=2, device=cuda_device, fuse_gate_up=fuse)
     x = torch.randn(20, 256, device=cuda_device).to(torch.bfloat16)
     logits = torch.randn(20, 8, device=cuda_device)
     y = moe(x, logits)
@@ -241,7 +242,7 @@ def test_swiglu_launch_matches_separate_gemms(cuda_device, grouped):
     from onecomp_runtime.layers._rows_base import MODE_EXACT, RowsHandle, group_major
     from onecomp_runtime.moe import PackedMoE
     experts, shared = _moe_setup(E=8, H=256, F=384)
-    moe = PackedMoE(experts, shared, k=2, device=cuda_device)
+    moe = PackedMoE(experts, shared, k=2, device=cuda_device, fuse_gate_up=True)
     hs = moe._h if grouped else moe._shared
     assert "gate_up" in hs
     mats = experts if grouped else [shared]

@@ -179,3 +179,12 @@ def test_missing_rank_times_out_cleanly(tmp_path):
     for p in procs:
         p.join(timeout=60)
     assert flag.exists() and flag.read_text() != "none"
+
+
+def test_fused_norm_needs_the_nvls_reducer():
+    """The RMS norm rides in the NVLS reduction kernel: asking for it without a reducer is an
+    error on the host, before any GEMM runs (one process, no process group)."""
+    from onecomp_runtime.tensor_parallel import RowParallelInt4Linear
+    layer = RowParallelInt4Linear(torch.nn.Identity(), chunks=1)
+    with pytest.raises(ValueError, match="NvlsReducer"):
+        layer.forward_async(torch.zeros(4, 8), rms_norm_eps=1e-6)
