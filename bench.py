@@ -561,6 +561,10 @@ def bench_cfg4(args, job: Job, peaks: dict, with_cpu: bool) -> dict:
                         "note": "the step overlaps each chunk's reduction with the next chunk's GEMM"}
     del stack
     torch.cuda.empty_cache()
+    if job.world > 1 and args.tc_max_ctas:
+        # the cap only makes room for the stack's NVLS reductions: the nested workloads get every SM
+        from onecomp_runtime import _lib
+        _lib.set_option(_lib.OPT_TC_MAX_CTAS, 0)
     if with_cpu:
         line["cpu_baseline"] = cpu_baseline_cfg4(args)
     return line
