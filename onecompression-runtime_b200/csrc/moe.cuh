@@ -170,6 +170,30 @@ __global__ void silu_mul_kernel(const uint16_t* __restrict__ g, const uint16_t* 
   }
 }
 
+// The same, 8 columns per thread with 16-byte loads and stores (F a multiple of 8, rows 16-byte
+// aligned): identical arithmetic per element, a third of the time of the scalar form.
+template <bool BF16>
+__global__ void silu_mul_v8_kernel(const uint16_t* __restrict__ g, const uint16_t* __restrict__ u, long long ld_in,
+                                   int P, int F8, uint16_t* __restrict__ h, long long ld_out) {
+  const long long total = (long long)P * F8;
+  const int dt = BF16 ? kBF16 : kF16;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int p = (int)(i / F8), c = (int)(i % F8);
+    const uint4 gq = *reinterpret_cast<const uint4*>(g + (long long)p * ld_in + 8 * c);
+    const uint4 uq = *reinterpret_cast<const uint4*>(u + (long long)p * ld_in + 8 * c);
+    const uint32_t gw[4] = {gq.x, gq.y, gq.z, gq.w}, uw[4] = {uq.x, uq.y, uq.z, uq.w};
+    uint32_t hw[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float g0 = bits_to_f32((uint16_t)(gw[j] & 0xFFFFu), dt), g1 = bits_to_f32((uint16_t)(gw[j] >> 16), dt);
+      const float u0 = bits_to_f32((uint16_t)(uw[j] & 0xFFFFu), dt), u1 = bits_to_f32((uint16_t)(uw[j] >> 16), dt);
+      hw[j] = pack2(f32_to_bits(silu_f32(g0) * u0, dt), f32_to_bits(silu_f32(g1) * u1, dt));
+    }
+    *reinterpret_cast<uint4*>(h + (long long)p * ld_out + 8 * c) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+  }
+}
+
 // out[t, :] = sum_j w[t, j] * y[slot_pos[t*K + j], :] (+ shared[t, :]); fp32 sum, one rounding.
 template <bool BF16>
 __global__ void moe_combine_kernel(const uint16_t* __restrict__ y, long long ldy, const int32_t* __restrict__ slot_pos,
@@ -187,6 +211,49 @@ __global__ void moe_combine_kernel(const uint16_t* __restrict__ y, long long ldy
       acc += w[(long long)t * K + j] * bits_to_f32(y[(long long)p * ldy + c], dt);
     }
     out[(long long)t * ldo + c] = f32_to_bits(acc, dt);
+  }
+}
+
+// The same, 8 columns per thread with 16-byte loads and stores (H a multiple of 8, rows 16-byte
+// aligned); each column's sum is formed in the same order as in the scalar form.
+template <bool BF16>
+__global__ void moe_combine_v8_kernel(const uint16_t* __restrict__ y, long long ldy,
+                                      const int32_t* __restrict__ slot_pos, const float* __restrict__ w, int T, int K,
+                                      int H8, const uint16_t* __restrict__ shared, long long lds,
+                                      uint16_t* __restrict__ out, long long ldo) {
+  const int dt = BF16 ? kBF16 : kF16;
+  const long long total = (long long)T * H8;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int t = (int)(i / H8), c = (int)(i % H8);
+    float acc[8];
+    if (shared) {
+      const uint4 q = *reinterpret_cast<const uint4*>(shared + (long long)t * lds + 8 * c);
+      const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        acc[2 * e] = bits_to_f32((uint16_t)(qw[e] & 0xFFFFu), dt);
+        acc[2 * e + 1] = bits_to_f32((uint16_t)(qw[e] >> 16), dt);
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+    }
+    for (int j = 0; j < K; ++j) {
+      const int p = slot_pos[(long long)t * K + j];
+      const float wj = w[(long long)t * K + j];
+      const uint4 q = *reinterpret_cast<const uint4*>(y + (long long)p * ldy + 8 * c);
+      const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        acc[2 * e] += wj * bits_to_f32((uint16_t)(qw[e] & 0xFFFFu), dt);
+        acc[2 * e + 1] += wj * bits_to_f32((uint16_t)(qw[e] >> 16), dt);
+      }
+    }
+    uint32_t ow[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) ow[e] = pack2(f32_to_bits(acc[2 * e], dt), f32_to_bits(acc[2 * e + 1], dt));
+    *reinterpret_cast<uint4*>(out + (long long)t * ldo + 8 * c) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
   }
 }
 

@@ -1406,13 +1406,22 @@ extern "C" int oc_b200_silu_mul(const void* g, const void* u, int64_t ld_in, int
   if (P == 0) return OC_OK;
   int dev = 0;
   if (int rc = current_device(&dev)) return rc;
+  const auto* gg = reinterpret_cast<const uint16_t*>(g);
+  const auto* uu = reinterpret_cast<const uint16_t*>(u);
+  auto* hh = reinterpret_cast<uint16_t*>(h);
+  if (F % 8 == 0 && ld_in % 8 == 0 && ld_out % 8 == 0 && aligned(g, 16) && aligned(u, 16) && aligned(h, 16)) {
+    const int blocks = grid_1d((long long)P * (F / 8), 256, dev);
+    if (dtype == OC_DT_BF16)
+      oc::silu_mul_v8_kernel<true><<<blocks, 256, 0, stream>>>(gg, uu, ld_in, P, F / 8, hh, ld_out);
+    else
+      oc::silu_mul_v8_kernel<false><<<blocks, 256, 0, stream>>>(gg, uu, ld_in, P, F / 8, hh, ld_out);
+    return launch_check("silu_mul");
+  }
   const int blocks = grid_1d((long long)P * F, 256, dev);
   if (dtype == OC_DT_BF16)
-    oc::silu_mul_kernel<true><<<blocks, 256, 0, stream>>>(reinterpret_cast<const uint16_t*>(g),
-        reinterpret_cast<const uint16_t*>(u), ld_in, P, F, reinterpret_cast<uint16_t*>(h), ld_out);
+    oc::silu_mul_kernel<true><<<blocks, 256, 0, stream>>>(gg, uu, ld_in, P, F, hh, ld_out);
   else
-    oc::silu_mul_kernel<false><<<blocks, 256, 0, stream>>>(reinterpret_cast<const uint16_t*>(g),
-        reinterpret_cast<const uint16_t*>(u), ld_in, P, F, reinterpret_cast<uint16_t*>(h), ld_out);
+    oc::silu_mul_kernel<false><<<blocks, 256, 0, stream>>>(gg, uu, ld_in, P, F, hh, ld_out);
   return launch_check("silu_mul");
 }
 
@@ -1424,10 +1433,19 @@ extern "C" int oc_b200_moe_combine(const void* y, int64_t ldy, const int32_t* sl
   if (T == 0) return OC_OK;
   int dev = 0;
   if (int rc = current_device(&dev)) return rc;
-  const int blocks = grid_1d((long long)T * H, 256, dev);
   const auto* yy = reinterpret_cast<const uint16_t*>(y);
   const auto* sh = reinterpret_cast<const uint16_t*>(shared);
   auto* o = reinterpret_cast<uint16_t*>(out);
+  if (H % 8 == 0 && ldy % 8 == 0 && ldo % 8 == 0 && aligned(y, 16) && aligned(out, 16) &&
+      (!shared || (lds % 8 == 0 && aligned(shared, 16)))) {
+    const int blocks = grid_1d((long long)T * (H / 8), 256, dev);
+    if (dtype == OC_DT_BF16)
+      oc::moe_combine_v8_kernel<true><<<blocks, 256, 0, stream>>>(yy, ldy, slot_pos, w, T, k, H / 8, sh, lds, o, ldo);
+    else
+      oc::moe_combine_v8_kernel<false><<<blocks, 256, 0, stream>>>(yy, ldy, slot_pos, w, T, k, H / 8, sh, lds, o, ldo);
+    return launch_check("moe_combine");
+  }
+  const int blocks = grid_1d((long long)T * H, 256, dev);
   if (dtype == OC_DT_BF16)
     oc::moe_combine_kernel<true><<<blocks, 256, 0, stream>>>(yy, ldy, slot_pos, w, T, k, H, sh, lds, o, ldo);
   else

@@ -277,6 +277,48 @@ def test_swiglu_launch_matches_separate_gemms(cuda_device, grouped):
     assert _lib.read_device_error(cuda_device) == 0
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_silu_mul_and_combine_vector_paths_match_scalar(cuda_device, dtype):
+    """silu-mul and the weighted combine take 8 columns per thread when rows are 16-byte aligned
+    and a scalar path otherwise (odd row pitch): the same bits either way, and silu-mul against
+    torch's silu within a bf16/fp16 ulp."""
+    from onecomp_runtime import _lib
+    st = _lib.stream_of(cuda_device)
+    gen = torch.Generator(device=cuda_device).manual_seed(11)
+    P, F, T, k, H = 97, 264, 40, 3, 264
+    dt = _lib.DT[dtype]
+
+    def silu_mul(pitch):
+        gu = torch.randn(P, pitch, generator=gen, device=cuda_device).mul(4).to(dtype)
+        g, u = gu[:, :F], gu[:, F:2 * F]
+        outs = []
+        for ld_out in (F, F + 1):   # 16-byte rows (vector path) and an odd pitch (scalar path)
+            h = torch.zeros(P, ld_out, dtype=dtype, device=cuda_device)
+            _lib.call("oc_b200_silu_mul", g.data_ptr(), u.data_ptr(), gu.stride(0), P, F, h.data_ptr(), ld_out,
+                      dt, st)
+            outs.append(h[:, :F])
+        return g, u, outs
+
+    g, u, (hv, hs) = silu_mul(2 * F)
+    assert torch.equal(hv.view(torch.int16), hs.view(torch.int16))
+    ref = (torch.nn.functional.silu(g.float()) * u.float())
+    assert float(((hv.float() - ref).abs() / ref.abs().clamp_min(1e-3)).max()) < 2.0 ** -6
+    y = torch.randn(T * k, H, generator=gen, device=cuda_device).to(dtype)
+    slot = torch.randperm(T * k, generator=gen, device=cuda_device).to(torch.int32)
+    w = torch.rand(T, k, generator=gen, device=cuda_device)
+    sh = torch.randn(T, H, generator=gen, device=cuda_device).to(dtype)
+    y_odd = torch.zeros(T * k, H + 1, dtype=dtype, device=cuda_device)
+    y_odd[:, :H] = y
+    outs = []
+    for yy, ldy in ((y, H), (y_odd, H + 1)):
+        o = torch.zeros(T, H, dtype=dtype, device=cuda_device)
+        _lib.call("oc_b200_moe_combine", yy.data_ptr(), ldy, slot.data_ptr(), w.data_ptr(), T, k, H, sh.data_ptr(),
+                  H, o.data_ptr(), H, dt, st)
+        outs.append(o)
+    assert torch.equal(outs[0].view(torch.int16), outs[1].view(torch.int16))
+    assert _lib.read_device_error(cuda_device) == 0
+
+
 def test_no_device_errors_recorded(cuda_device):
     from onecomp_runtime import _lib
     assert _lib.read_device_error(cuda_device) == 0
