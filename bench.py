@@ -712,6 +712,49 @@ def bench_cfg2(args, job: Job, peaks: dict) -> dict:
     return out
 
 
+# ----------------------------------------------------------------------------- cfg0: one GPTQ linear
+def bench_cfg0(args, job: Job, peaks: dict) -> dict:
+    """BASELINE config 0 on the GPU: one AutoGPTQ v1 gs32 linear, K = N = 3072, M = 256 bf16 tokens
+    (the reference's CPU-runnable case). Its packed weights (5.5 MB) fit L2, so C copies with their
+    own weights (> 126 MB in all) run back to back in one CUDA graph; time per linear = graph / C."""
+    from onecomp_runtime.layers import FusedInt4Linear
+    from onecomp_runtime.testing import CFG0, gptq_layer
+    dev = job.dev
+    K, N, gs, M = CFG0["K"], CFG0["N"], CFG0["gs"], CFG0["M"]
+    per = K * N // 2 + 2 * (K // gs) * N + (K // gs) * N // 2
+    C = -(-160_000_000 // per)
+    layers = []
+    for c in range(C):
+        t = gptq_layer(K, N, gs, seed=c, device=dev)
+        layers.append(FusedInt4Linear(K, N, t["qweight"], t["scales"], t["qzeros"], t["bias"], gs))
+    x = torch.randn((M, K), generator=torch.Generator(device=dev).manual_seed(0), device=dev).to(torch.bfloat16)
+    with torch.no_grad():
+        for _ in range(3):
+            [lay(x) for lay in layers]
+        torch.cuda.synchronize(dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            outs = [lay(x) for lay in layers]
+        ms, clk = timed_steps(job, g.replay, max(args.steps, 1) * 5, args.warmup)
+    us = ms * 1e3 / C
+    tflops = 2.0 * M * K * N / (us * 1e-6) / 1e12
+    peak, src = tensor_peak(peaks, clk)
+    out = {"metric": "GPTQ int4 linear TFLOP/s (config 0: K=N=3072, gs32, M=256)", "value": round(tflops, 1),
+           "unit": "TFLOP/s", "n_gpus": job.world, "steps": args.steps, "warmup": args.warmup,
+           "us_per_linear": round(us, 2), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+           "dtype": "bf16", "data": "synthetic",
+           "config": {"workload": "cfg0", "copies_per_graph": C,
+                      "l2_flush": f"none needed: the graph streams {C} copies of 5.5 MB of packed weights"},
+           "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": peak, "unit": "TFLOP/s",
+                        "frac": round(tflops / peak, 4), "traffic": None,
+                        "kernel": "gptq_gemm_tc_kernel (24 column tiles of 128: 24 of 148 SMs at M = 256)",
+                        "peak_source": src},
+           "clocks": clk}
+    del g, outs, layers
+    torch.cuda.empty_cache()
+    return out
+
+
 # ----------------------------------------------------------------------------- cfg3: packed MoE
 def bench_cfg3(args, job: Job, peaks: dict) -> dict:
     """256 int2 experts (top-8) + int4 shared expert, T=2048 tokens per rank. N ranks:
@@ -860,7 +903,8 @@ def main():
         if args.workload == "cfg4":
             line = bench_cfg4(args, job, peaks, with_cpu)
             if not args.no_nested:
-                line["workloads"] = {"cfg1": bench_cfg1(args, job, peaks, full_line=False),
+                line["workloads"] = {"cfg0": bench_cfg0(args, job, peaks),
+                                     "cfg1": bench_cfg1(args, job, peaks, full_line=False),
                                      "cfg2": bench_cfg2(args, job, peaks),
                                      "cfg3": bench_cfg3(args, job, peaks)}
         elif args.workload == "cfg1":
