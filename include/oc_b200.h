@@ -120,6 +120,11 @@ int oc_b200_dsv4_dequant(const uint8_t* packed, int64_t ld_bytes, int wbits, con
  * source row k_perm[8w'+i] (or 0 when it is -1). */
 int oc_b200_gptq_repack_k(const int32_t* qweight, const int32_t* k_perm, int k_packed, int N, int32_t* qweight_out,
                           oc_stream_t stream);
+/* The same for wbits 4 (as above) or 8: an 8-bit qweight_out[w', n] packs, for i < 4, the code of
+ * source row k_perm[4w'+i] (k_packed a multiple of 4). The K re-layout of 8-bit act-order layers
+ * (PackedGPTQLinear(wbits=8) with g_idx, packed_gptq_linear.py:34-64). */
+int oc_b200_gptq_repack_k_ex(const int32_t* qweight, const int32_t* k_perm, int k_packed, int N, int wbits,
+                             int32_t* qweight_out, oc_stream_t stream);
 /* x_out[m, k'] = x[m, k_perm[k']] (0 when -1); 16-bit elements. */
 int oc_b200_permute_cols(const void* x, int64_t ldx, int64_t M, int K, const int32_t* k_perm, int k_packed,
                          void* x_out, oc_stream_t stream);
@@ -143,9 +148,11 @@ int oc_b200_gptq_layer_create(const int32_t* qweight, const int32_t* qzeros, con
  * (quant_utils.py:12-28 with wbits=8; PackedGPTQLinear(wbits=8), packed_gptq_linear.py:66-74)
  * have qweight int32 [in_features/4, N] and qzeros int32 [G, N/4]; oc_b200_gptq_gemm runs
  * them on the decode GEMV (M <= 16) or the tcgen05 GEMM (8-bit stages, exact dequant). They
- * need uniform groups (groupsize 32 or a multiple of 64, no k_perm / word_group), N a
- * multiple of 32 and >= 128, in_features >= 64, and 16-byte aligned tensors; other layouts
- * return OC_ERR_UNSUPPORTED. */
+ * need uniform groups in kernel K order (groupsize 32 or a multiple of 64, no word_group): either
+ * k_perm NULL, or an act-order layer whose groups each hold groupsize rows, with k_perm its
+ * group-sorted row order (in_features entries, k_packed == in_features) and qweight repacked in
+ * that order (oc_b200_gptq_repack_k_ex); N a multiple of 32 and >= 128, in_features >= 64, and
+ * 16-byte aligned tensors; other layouts return OC_ERR_UNSUPPORTED. */
 int oc_b200_gptq_layer_create_ex(const int32_t* qweight, const int32_t* qzeros, const void* scales, int scales_dtype,
                                  const int32_t* k_perm, const int32_t* word_group, int in_features, int k_packed,
                                  int N, int G, int groupsize, int wbits, int v1, oc_b200_layer** out);

@@ -153,6 +153,24 @@ __global__ void gptq_repack_k_kernel(const uint32_t* __restrict__ qw, const int3
   }
 }
 
+// 8-bit codes (4 per word): qweight_out[w', n] packs, for i < 4, the code of source row
+// kperm[4w'+i] (0 when it is -1).
+__global__ void gptq_repack_k8_kernel(const uint32_t* __restrict__ qw, const int32_t* __restrict__ kperm,
+                                      int Kp, int N, uint32_t* __restrict__ out) {
+  const long long total = (long long)(Kp / 4) * N;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int r = (int)(i / N), n = (int)(i % N);
+    uint32_t acc = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int src = kperm[r * 4 + j];
+      if (src >= 0) acc |= ((qw[(long long)(src >> 2) * N + n] >> (8 * (src & 3))) & 0xFFu) << (8 * j);
+    }
+    out[i] = acc;
+  }
+}
+
 // --- activation gather: x'[m, k'] = x[m, kperm[k']] (0 for -1) --------------------------
 __global__ void permute_cols_kernel(const uint16_t* __restrict__ x, long long ldx, int M, int K,
                                     const int32_t* __restrict__ kperm, int Kp, uint16_t* __restrict__ out) {

@@ -479,6 +479,20 @@ int oc_b200_gptq_repack_k(const int32_t* qweight, const int32_t* k_perm, int k_p
   return launch_check("repack_k");
 }
 
+int oc_b200_gptq_repack_k_ex(const int32_t* qweight, const int32_t* k_perm, int k_packed, int N, int wbits,
+                             int32_t* qweight_out, oc_stream_t stream) {
+  if (wbits == 4) return oc_b200_gptq_repack_k(qweight, k_perm, k_packed, N, qweight_out, stream);
+  if (wbits != 8) return fail(OC_ERR_UNSUPPORTED, "repack_k: wbits=%d (4 or 8)", wbits);
+  if (!qweight || !k_perm || !qweight_out) return fail(OC_ERR_INVALID, "repack_k: NULL pointer");
+  if (k_packed <= 0 || k_packed % 4 != 0 || N <= 0) return fail(OC_ERR_INVALID, "repack_k: k_packed=%d", k_packed);
+  int dev = 0;
+  if (int rc = current_device(&dev)) return rc;
+  oc::gptq_repack_k8_kernel<<<grid_1d((long long)(k_packed / 4) * N, 256, dev), 256, 0,
+                              reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const uint32_t*>(qweight), k_perm, k_packed, N, reinterpret_cast<uint32_t*>(qweight_out));
+  return launch_check("repack_k8");
+}
+
 int oc_b200_permute_cols(const void* x, int64_t ldx, int64_t M, int K, const int32_t* k_perm, int k_packed,
                          void* x_out, oc_stream_t stream) {
   if (!x || !k_perm || !x_out || M < 0 || K <= 0 || k_packed <= 0) return fail(OC_ERR_INVALID, "permute_cols");
@@ -491,9 +505,13 @@ int oc_b200_permute_cols(const void* x, int64_t ldx, int64_t M, int K, const int
 }
 
 // ---------------------------------------------------------------- GPTQ layer
-// 8-bit layers: the TMA decode GEMV only (uniform groups, no K permutation).
+// 8-bit layers: uniform groups in the kernel's K order. An act-order layer whose groups all hold
+// groupsize rows (a permutation of k // groupsize) is uniform once its rows are sorted by group:
+// k_perm (kernel row -> source row, in_features entries) gathers the activation columns and
+// qweight is the repacked copy (oc_b200_gptq_repack_k_ex).
 static int gptq_layer_create8(const int32_t* qweight, const int32_t* qzeros, const void* scales, int scales_dtype,
-                              int in_features, int N, int G, int groupsize, int v1, oc_b200_layer** out) {
+                              const int32_t* k_perm, int in_features, int N, int G, int groupsize, int v1,
+                              oc_b200_layer** out) {
   const int ks = oc::gt_stage_k<8>();
   if (in_features < ks || in_features % 8 != 0)
     return fail(OC_ERR_UNSUPPORTED, "layer_create: 8-bit in_features=%d (needs a multiple of 8, >= %d)", in_features,
@@ -519,6 +537,7 @@ static int gptq_layer_create8(const int32_t* qweight, const int32_t* qzeros, con
   L->s_dtype = scales_dtype;
   L->K_in = in_features;
   L->Kp = in_features;
+  L->kperm = k_perm;
   L->N = N;
   L->G = G;
   L->gs = groupsize;
@@ -570,9 +589,11 @@ int oc_b200_gptq_layer_create_ex(const int32_t* qweight, const int32_t* qzeros, 
   if (wbits != 4 && wbits != 8) return fail(OC_ERR_UNSUPPORTED, "layer_create: wbits=%d (4 or 8)", wbits);
   if (wbits == 8) {
     if (!dt16(scales_dtype)) return fail(OC_ERR_UNSUPPORTED, "layer_create: scales must be f16 or bf16");
-    if (k_perm || word_group || k_packed != in_features)
-      return fail(OC_ERR_UNSUPPORTED, "layer_create: 8-bit layers take no K permutation or word groups");
-    return gptq_layer_create8(qweight, qzeros, scales, scales_dtype, in_features, N, G, groupsize, v1, out);
+    if (word_group || k_packed != in_features)
+      return fail(OC_ERR_UNSUPPORTED,
+                  "layer_create: 8-bit layers take no word groups and no padded K permutation (k_packed=%d, "
+                  "in_features=%d)", k_packed, in_features);
+    return gptq_layer_create8(qweight, qzeros, scales, scales_dtype, k_perm, in_features, N, G, groupsize, v1, out);
   }
   if (!dt16(scales_dtype)) return fail(OC_ERR_UNSUPPORTED, "layer_create: scales must be f16 or bf16");
   if (in_features <= 0 || k_packed <= 0 || k_packed % 8 != 0)

@@ -54,6 +54,7 @@ _SIGNATURES = {
     "oc_b200_rtn_embedding": ([_p, _i64, _i64, _p, _i64, _p, _i, _p, _i, _i, _i, _p, _i, _p], _i),
     "oc_b200_dsv4_dequant": ([_p, _i64, _i, _p, _i, _p, _i, _i64, _i64, _i, _i, _i, _p, _i, _p], _i),
     "oc_b200_gptq_repack_k": ([_p, _p, _i, _i, _p, _p], _i),
+    "oc_b200_gptq_repack_k_ex": ([_p, _p, _i, _i, _i, _p, _p], _i),
     "oc_b200_permute_cols": ([_p, _i64, _i64, _i, _p, _i, _p, _p], _i),
     "oc_b200_gptq_layer_create": ([_p, _p, _p, _i, _p, _p, _i, _i, _i, _i, _i, _i, ctypes.POINTER(_p)], _i),
     "oc_b200_gptq_layer_create_ex": ([_p, _p, _p, _i, _p, _p, _i, _i, _i, _i, _i, _i, _i, ctypes.POINTER(_p)], _i),

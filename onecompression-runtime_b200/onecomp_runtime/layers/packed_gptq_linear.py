@@ -15,9 +15,12 @@ layers here run the fused sm_100a kernels directly on the packed buffers:
 8-bit layers with uniform groups (``g_idx == k // groupsize``, groupsize 32 or a multiple
 of 64) run the 8-bit decode GEMV for M <= 16 tokens and the tcgen05 GEMM up to
 ``_KERNEL8_MAX_M`` tokens (measured on B200 at 3072 -> 9216: 2.1x the dequant + ``F.linear``
-path at M = 64, 1.8x at 512, 0.9x at 4608). Larger M, act-order 8-bit layers and fp32 inputs
-dequantize with the B200 dequant kernel and call ``F.linear``, as the reference does for every
-call.
+path at M = 64, 1.8x at 512, 0.9x at 4608). Act-order 8-bit layers whose groups each hold
+``groupsize`` rows (g_idx a permutation of ``k // groupsize``, what GPTQ's act-order writes) run
+the same kernels after a K re-layout: rows sorted by group on the GPU
+(``oc_b200_gptq_repack_k_ex``) and the activation columns gathered in that order. Larger M,
+other group layouts and fp32 inputs dequantize with the B200 dequant kernel and call
+``F.linear``, as the reference does for every call.
 """
 from __future__ import annotations
 
@@ -65,12 +68,23 @@ class PackedGPTQLinear(B200GPTQLinear):
             self._handle = None
             self._handle_key = None
             K, N, gs = self.in_features, self.out_features, self.groupsize
-            trivial = torch.arange(K, device=self.g_idx.device, dtype=torch.long) // gs
-            self._kernel8_ok = (self.wbits == 8 and K >= 64 and K % 8 == 0 and N >= 128 and N % 32 == 0
-                           and (gs == 32 or (gs > 0 and gs % 64 == 0))
-                           and tuple(self.qweight.shape) == (K // 4, N)
-                           and int(self.scales.shape[0]) == (K + gs - 1) // gs
-                           and bool(torch.equal(self.g_idx, trivial)))
+            shapes_ok = (self.wbits == 8 and K >= 64 and K % 8 == 0 and N >= 128 and N % 32 == 0
+                         and (gs == 32 or (gs > 0 and gs % 64 == 0))
+                         and tuple(self.qweight.shape) == (K // 4, N)
+                         and int(self.scales.shape[0]) == (K + gs - 1) // gs
+                         and tuple(self.g_idx.shape) == (K,))
+            self._kperm8 = None   # group-sorted row order of an act-order layer (host int32)
+            self._h8_bufs = None  # the device copies the handle reads: (k_perm, repacked qweight)
+            uniform = False
+            if shapes_ok:
+                trivial = torch.arange(K, device=self.g_idx.device, dtype=torch.long) // gs
+                uniform = bool(torch.equal(self.g_idx, trivial))
+                if not uniform:
+                    order = torch.argsort(self.g_idx, stable=True)
+                    if bool(torch.equal(self.g_idx[order], trivial)):   # every group holds gs rows
+                        self._kperm8 = order.to(torch.int32).cpu()
+                        uniform = True
+            self._kernel8_ok = shapes_ok and uniform
 
     # ------------------------------------------------------------------ 8-bit kernels
     def _get_handle8(self):
@@ -79,13 +93,21 @@ class PackedGPTQLinear(B200GPTQLinear):
         if self._handle is not None and self._handle_key == key:
             return self._handle
         self._release_handle()
-        _lib.require_b200(self.qweight.device)
+        dev = self.qweight.device
+        _lib.require_b200(dev)
         h = ctypes.c_void_p()
-        with torch.cuda.device(self.qweight.device):
-            _lib.call("oc_b200_gptq_layer_create_ex", self.qweight.data_ptr(), self.qzeros.data_ptr(),
-                      self.scales.data_ptr(), _lib.DT[self.scales.dtype], None, None, self.in_features,
-                      self.in_features, self.out_features, int(self.scales.shape[0]), self.groupsize, 8,
-                      int(self.v1), ctypes.byref(h))
+        with torch.cuda.device(dev):
+            qw, kp = self.qweight, None
+            if self._kperm8 is not None:   # act-order: rows sorted by group, activations gathered
+                kp = self._kperm8.to(dev)
+                qw = torch.empty_like(self.qweight)
+                _lib.call("oc_b200_gptq_repack_k_ex", self.qweight.data_ptr(), kp.data_ptr(), self.in_features,
+                          self.out_features, 8, qw.data_ptr(), _lib.stream_of(dev))
+                self._h8_bufs = (kp, qw)
+            _lib.call("oc_b200_gptq_layer_create_ex", qw.data_ptr(), self.qzeros.data_ptr(),
+                      self.scales.data_ptr(), _lib.DT[self.scales.dtype], None if kp is None else kp.data_ptr(),
+                      None, self.in_features, self.in_features, self.out_features, int(self.scales.shape[0]),
+                      self.groupsize, 8, int(self.v1), ctypes.byref(h))
         self._handle = h
         self._handle_key = key
         return h

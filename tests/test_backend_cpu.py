@@ -133,13 +133,22 @@ def test_synthetic_packers_match_oracle():
     (1000, 256, 32, False, True),    # K not a multiple of the 64-k stage
     (512, 256, 48, False, False),    # groups of 48: neither 32 nor a multiple of 64
     (512, 64, 128, False, False),    # N below one 128-column tile
-    (512, 256, 128, True, False),    # act-order: dequant + F.linear
+    (512, 256, 128, True, True),     # act-order, every group 128 rows: kernels after a K re-layout
+    (512, 256, 128, "uneven", False),  # act-order with unequal groups: dequant + F.linear
 ])
 def test_packed_gptq_8bit_kernel_eligibility(K, N, gs, actorder, ok):
-    """Which 8-bit PackedGPTQLinear layers take the 8-bit kernels (decided at construction, no GPU)."""
+    """Which 8-bit PackedGPTQLinear layers take the 8-bit kernels (decided at construction, no GPU);
+    act-order layers get their group-sorted row order."""
     from onecomp_runtime.layers import PackedGPTQLinear
     from onecomp_runtime.testing import gptq_layer
-    t = gptq_layer(K, N, gs, seed=1, actorder=actorder, wbits=8, bias=False)
-    layer = PackedGPTQLinear(K, N, t["qweight"], t["scales"], t["qzeros"], t["g_idx"], None, gs, 8, True)
+    t = gptq_layer(K, N, gs, seed=1, actorder=bool(actorder), wbits=8, bias=False)
+    g_idx = t["g_idx"].clone()
+    if actorder == "uneven":
+        g_idx[int((g_idx == 0).nonzero()[0])] = 1
+    layer = PackedGPTQLinear(K, N, t["qweight"], t["scales"], t["qzeros"], g_idx, None, gs, 8, True)
     assert layer._kernel8_ok is ok
+    if actorder is True:
+        kp = layer._kperm8.long()
+        assert torch.equal(g_idx[kp], torch.arange(K) // gs)   # rows sorted by group
+        assert torch.equal(torch.sort(kp).values, torch.arange(K))
     assert layer.qweight.shape == (K // 4, N) and layer.qzeros.shape == (t["scales"].shape[0], N // 4)

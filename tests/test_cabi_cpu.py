@@ -71,8 +71,8 @@ def test_layer_create_ex_validation(lib):
                                             ctypes.byref(out)) != 0
     assert "wbits" in _lib.last_error()
     kp = ctypes.c_void_p(0x40000)
-    assert lib.oc_b200_gptq_layer_create_ex(qw, qz, sc, 0, kp, None, 256, 256, 128, 8, 32, 8, 1,
-                                            ctypes.byref(out)) != 0
+    assert lib.oc_b200_gptq_layer_create_ex(qw, qz, sc, 0, kp, None, 256, 264, 128, 8, 32, 8, 1,
+                                            ctypes.byref(out)) != 0   # padding rows in the K order
     assert "K permutation" in _lib.last_error()
     assert lib.oc_b200_gptq_layer_create_ex(qw, qz, sc, 0, None, None, 256, 256, 128, 6, 48, 8, 1,
                                             ctypes.byref(out)) != 0
@@ -172,6 +172,9 @@ def test_fused_entry_points_reject_bad_arguments_before_any_launch(lib):
     assert "not a row-packed layer" in _lib.last_error()
     buf = ctypes.create_string_buffer(64)
     p = ctypes.cast(buf, ctypes.c_void_p)
+    assert lib.oc_b200_gptq_repack_k_ex(p, p, 64, 128, 3, p, None) == 2          # wbits 4 or 8
+    assert lib.oc_b200_gptq_repack_k_ex(None, p, 64, 128, 8, p, None) == 1       # NULL weights
+    assert lib.oc_b200_gptq_repack_k_ex(p, p, 66, 128, 8, p, None) == 1          # k_packed % 4
     args = (p, 4, 4096, None, 1e-6, p, 0, 2, 1, 8, None)
     assert lib.oc_b200_nvls_allreduce_rmsnorm_bf16(None, *args[1:]) == 1          # no buffer
     assert lib.oc_b200_nvls_allreduce_rmsnorm_bf16(p, 4, 4100, *args[3:]) == 1     # cols not a multiple of 8

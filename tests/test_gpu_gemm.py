@@ -139,6 +139,39 @@ def test_gemv_8bit(cuda_device, shape):
     assert torch.equal(layer(x), y)
 
 
+@pytest.mark.parametrize("shape", [(1, 4096, 1024, 128), (9, 2048, 384, 64), (64, 2048, 512, 128),
+                                   (700, 1536, 256, 32)], ids=lambda s: f"M{s[0]}K{s[1]}N{s[2]}g{s[3]}")
+def test_gptq_8bit_act_order(cuda_device, shape):
+    """8-bit act-order layers (g_idx a permutation of k // groupsize) run the 8-bit decode GEMV or
+    tcgen05 GEMM on rows re-laid out by group (oc_b200_gptq_repack_k_ex) with the activation
+    columns gathered; against the oracle's exact weights. A g_idx whose groups do not all hold
+    groupsize rows keeps the dequant + F.linear path, also within tolerance."""
+    M, K, N, gs = shape
+    from onecomp_runtime import _lib
+    from onecomp_runtime.layers import PackedGPTQLinear
+    from onecomp_runtime.testing import activations, gptq_layer
+    t = gptq_layer(K, N, gs, seed=M + K, v1=False, actorder=True, scales_dtype=torch.float16, wbits=8)
+    tc = {k: v.to(cuda_device) for k, v in t.items()}
+    layer = PackedGPTQLinear(K, N, tc["qweight"], tc["scales"], tc["qzeros"], tc["g_idx"], tc.get("bias"), gs, 8,
+                             False)
+    x = activations(M, K, seed=M).to(cuda_device)
+    assert layer._kperm8 is not None and layer._use_kernel8(x, M)
+    y = layer(x)
+    w = oracle_weight(t, K, N, "bf16", v1=False, wbits=8)
+    assert max_abs_rel(y, reference_output(x, w, "bf16", layer.bias)) < 1e-2
+    assert torch.equal(layer(x), y)
+    # uneven groups: the first two groups swap one row each way, then one row moves from group 0
+    g2 = t["g_idx"].clone()
+    g2[int((g2 == 0).nonzero()[0])] = 1
+    t2 = dict(t, g_idx=g2)
+    layer2 = PackedGPTQLinear(K, N, tc["qweight"], tc["scales"], tc["qzeros"], g2.to(cuda_device), tc.get("bias"),
+                              gs, 8, False)
+    assert not layer2._kernel8_ok
+    w2 = oracle_weight(t2, K, N, "bf16", v1=False, wbits=8)
+    assert max_abs_rel(layer2(x), reference_output(x, w2, "bf16", layer2.bias)) < 1e-2
+    assert _lib.read_device_error(cuda_device) == 0
+
+
 def test_gemv_8bit_layer_errors(cuda_device):
     """8-bit handles refuse the layouts their kernels do not cover, with an error (no launch)."""
     import ctypes
@@ -147,9 +180,10 @@ def test_gemv_8bit_layer_errors(cuda_device):
     t = {k: v.to(cuda_device) for k, v in gptq_layer(256, 128, 32, wbits=8, scales_dtype=torch.float16).items()}
     lib = _lib.lib()
     h = ctypes.c_void_p()
-    kperm = torch.arange(256, dtype=torch.int32, device=cuda_device)
+    kperm = torch.arange(264, dtype=torch.int32, device=cuda_device)
     args = (t["qweight"].data_ptr(), t["qzeros"].data_ptr(), t["scales"].data_ptr(), _lib.DT[torch.float16])
-    assert lib.oc_b200_gptq_layer_create_ex(*args, kperm.data_ptr(), None, 256, 256, 128, 8, 32, 8, 1,
+    # a K permutation with padding rows (k_packed > in_features): no 8-bit kernel takes it
+    assert lib.oc_b200_gptq_layer_create_ex(*args, kperm.data_ptr(), None, 256, 264, 128, 8, 32, 8, 1,
                                             ctypes.byref(h)) != 0
     assert b"K permutation" in lib.oc_b200_last_error()
     assert lib.oc_b200_gptq_layer_create_ex(*args, None, None, 256, 256, 128, 8, 48, 8, 1, ctypes.byref(h)) != 0

@@ -102,11 +102,13 @@ def test_wait_runs_out_then_noalloc_calls_are_exact(cuda_device):
 PEER = 0x110  # kDevErrPeer: a cross-rank barrier of the NVLS all-reduce gave up
 
 
-def test_nvls_allreduce_peer_that_never_arrives(cuda_device):
-    """The NVLS all-reduce's entry barrier waits for a rank that does not exist: a two-rank call on
-    one GPU whose second flag array is a local buffer nobody writes. With a 20 ms bound the kernel
-    records the peer-wait code and returns before any multicast access (the buffer is never
-    touched, so no multicast object is needed), and the context stays usable."""
+@pytest.mark.parametrize("fused_norm", [False, True])
+def test_nvls_allreduce_peer_that_never_arrives(cuda_device, fused_norm):
+    """The NVLS all-reduce's entry barrier (plain, or with the RMS norm) waits for a rank that does
+    not exist: a two-rank call on one GPU whose second flag array is a local buffer nobody writes.
+    With a 20 ms bound the kernel records the peer-wait code and returns before any multicast
+    access (the buffer is never touched, so no multicast object is needed), and the context stays
+    usable."""
     from onecomp_runtime import _lib
     blocks, world = 2, 2
     flags = [torch.zeros(2 * blocks * world, dtype=torch.int32, device=cuda_device) for _ in range(world)]
@@ -115,8 +117,12 @@ def test_nvls_allreduce_peer_that_never_arrives(cuda_device):
     saved = _lib.get_option(_lib.OPT_WAIT_US)
     try:
         _lib.set_option(_lib.OPT_WAIT_US, 20000)
-        _lib.call("oc_b200_nvls_allreduce_bf16", buf.data_ptr(), buf.numel(), ptrs.data_ptr(), 0, world, 1, blocks,
-                  _lib.stream_of(cuda_device))
+        if fused_norm:
+            _lib.call("oc_b200_nvls_allreduce_rmsnorm_bf16", buf.data_ptr(), buf.shape[0], buf.shape[1], None, 1e-6,
+                      ptrs.data_ptr(), 0, world, 1, blocks, _lib.stream_of(cuda_device))
+        else:
+            _lib.call("oc_b200_nvls_allreduce_bf16", buf.data_ptr(), buf.numel(), ptrs.data_ptr(), 0, world, 1,
+                      blocks, _lib.stream_of(cuda_device))
         torch.cuda.synchronize(cuda_device)
     finally:
         _lib.set_option(_lib.OPT_WAIT_US, saved)
