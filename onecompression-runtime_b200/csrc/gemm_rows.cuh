@@ -82,6 +82,7 @@ struct RowsCfg {
   static constexpr int kZOff = kWBytes + 512;                    // zero rows of the block (<= 512 B)
   static constexpr int kWStageBytes = kWBytes + 1024;
   static constexpr int kAccCols = ACC_STAGES * BT;              // a ring of BT-column accumulator slots
+  static_assert(BT % 16 == 0 && (SWIGLU || BT % 32 == 0), "epilogue pieces: 16 tokens (SwiGLU), else 32");
   static constexpr int kACols = A_STAGES * 32;
   static_assert(kAccCols + kACols <= 512, "TMEM budget");
   static_assert(W_STAGES % kRowsDqGroups == 0 && A_STAGES % kRowsDqGroups == 0,
@@ -527,33 +528,38 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
       __syncwarp();
       const uint32_t tbase = tmem_base + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(sc * BT);
       const uint32_t ubase = tmem_base + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(su * BT);
+      if constexpr (SWIGLU) {
+        // 16 rows at a time (a tile of BT = 16 j tokens): the gate and up values of 32 rows at once
+        // would not fit the registers
+        const int n16 = min(BT / 16, (mend - m0 + 15) / 16);
+#pragma unroll 1
+        for (int c = 0; c < n16; ++c) {
+          uint32_t gq[16], uq[16];
+          tmem_ld_32x32b_x16(tbase + (uint32_t)(c * 16), gq);
+          tmem_ld_32x32b_x16(ubase + (uint32_t)(c * 16), uq);
+          tc_wait_ld();
+          if (nvalid) {
+            const int rh = m0 + 16 * c;
+            uint16_t* dst = p.out + (long long)rh * p.ldc + n;
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              if (rh + i < mend) {
+                // the gate and up outputs as their own GEMMs would store them, then silu(g) * u
+                const float gv = bits_to_f32(f32_to_bits(__uint_as_float(gq[i]) + bv, odt), odt);
+                const float uv = bits_to_f32(f32_to_bits(__uint_as_float(uq[i]) + bv, odt), odt);
+                dst[(long long)i * p.ldc] = f32_to_bits(silu_f32(gv) * uv, odt);
+              }
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&empty_acc[sc]);
+        mbar_arrive(&empty_acc[su]);
+        continue;
+      }
       const int nch = min(BT / 32, (mend - m0 + 31) / 32);  // chunks holding valid rows
 #pragma unroll 1
       for (int c = 0; c < nch; ++c) {
         const int r0 = m0 + c * 32;
-        if constexpr (SWIGLU) {
-          // 16 rows at a time: the gate and up values of 32 rows at once would not fit the registers
-#pragma unroll 1
-          for (int hh = 0; hh < 2; ++hh) {
-            uint32_t gq[16], uq[16];
-            tmem_ld_32x32b_x16(tbase + (uint32_t)(c * 32 + 16 * hh), gq);
-            tmem_ld_32x32b_x16(ubase + (uint32_t)(c * 32 + 16 * hh), uq);
-            tc_wait_ld();
-            if (nvalid) {
-              const int rh = r0 + 16 * hh;
-              uint16_t* dst = p.out + (long long)rh * p.ldc + n;
-#pragma unroll
-              for (int i = 0; i < 16; ++i)
-                if (rh + i < mend) {
-                  // the gate and up outputs as their own GEMMs would store them, then silu(g) * u
-                  const float gv = bits_to_f32(f32_to_bits(__uint_as_float(gq[i]) + bv, odt), odt);
-                  const float uv = bits_to_f32(f32_to_bits(__uint_as_float(uq[i]) + bv, odt), odt);
-                  dst[(long long)i * p.ldc] = f32_to_bits(silu_f32(gv) * uv, odt);
-                }
-            }
-          }
-          continue;
-        }
         uint32_t v[32];
         tmem_ld_32x32b_x32(tbase + (uint32_t)(c * 32), v);
         tc_wait_ld();
@@ -566,7 +572,6 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
       }
       tc_fence_before();
       mbar_arrive(&empty_acc[sc]);
-      if (SWIGLU) mbar_arrive(&empty_acc[su]);
     }
   }
 

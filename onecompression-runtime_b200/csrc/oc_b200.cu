@@ -1606,10 +1606,10 @@ int launch_rows_bt(int bt, const CUtensorMap& tx, const oc::RowsParams& p, int d
   // The weight ring is deep (16-32 stages of 3-5 KB) because packed weights stream from HBM with
   // ~2 us of latency; activation tiles come from L2 and need fewer stages.
   if (swiglu) {
-    // a tile takes both slots of a two-slot accumulator ring (gate, up), so its epilogue holds the
-    // next tile's MMAs; measured variants that freed the gate slot first (three slots beside 4 A
-    // stages, or the gate outputs parked in shared memory at one activation or four weight stages
-    // fewer) ran config 3's routed experts slower (2.83-2.86 against 2.77 ms)
+    // A tile takes both slots of a two-slot accumulator ring (gate, up). Measured alternatives at
+    // config 3's routed experts, all slower than this (2.77 ms): 80-token tiles with three slots
+    // beside 8 A stages (epilogue overlapped; 2.84 ms), three 128-token slots beside 4 A stages,
+    // or the gate outputs parked in shared memory (2.83-2.86 ms). Dense: 192-token tiles.
     if (bt == 128) {
       if constexpr (WB == 2)
         return launch_rows_t<BF16, WB, MODE, HL, 128, 2, 6, 32, 8, true>(tx, p, dev, stream);

@@ -167,9 +167,9 @@ class PackedMoE(torch.nn.Module):
     ``fuse_gate_up`` picks where gate, up and silu(gate) * up run as one launch on a gate|up
     matrix (``oc_b200_rows_gemm_swiglu``) instead of two GEMMs and the silu-mul kernel (same
     bits): ``"shared"`` (default) the dense shared expert only, ``True`` the routed experts too,
-    ``False`` neither. Measured at config 3 on B200: shared expert 0.45 against 0.47 ms fused;
-    routed experts 2.77 against 2.72 ms fused (a tile's epilogue then holds the next tile's
-    MMAs: the accumulator ring holds one tile's gate and up slots at a time).
+    ``False`` neither. Measured at config 3 on B200: shared expert 0.45 ms fused against 0.47;
+    routed experts 2.77 ms fused against 2.72 (2.84 against 2.65 once the silu-mul pass was
+    vectorized), also with the epilogue overlapped.
     """
 
     def __init__(self, experts: list[dict], shared: dict | None = None, k: int = 8, renorm: bool = True,
