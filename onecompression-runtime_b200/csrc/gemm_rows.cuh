@@ -19,10 +19,9 @@
 // activation k-block of step kb is kb mod K/64 (X is read twice per tile, the second time from
 // L2), the MMA accumulates the first K/64 steps into the tile's gate accumulator and the rest into
 // its up accumulator (two consecutive slots of the accumulator ring, each BT columns of the same
-// TMEM lanes), and the epilogue writes
-// silu(g) * u with g and u first rounded to the output type and silu_f32 as the silu-mul kernel
-// computes it, so the bits equal separate gate / up GEMMs followed by that kernel: the [rows, 2F]
-// intermediate and its extra pass disappear.
+// TMEM lanes), and the epilogue writes silu(g) * u with g and u first rounded to the output type
+// and silu_f32 as the silu-mul kernel computes it, so the bits equal separate gate / up GEMMs
+// followed by that kernel: the [rows, 2F] intermediate and its extra pass disappear.
 //
 // Dequant numerics (MODE), bit-exact with the reference in every case:
 //   kRowsExact   (DSV4, dsv4_packed_linear.py:52-56): w = RNE((q - z) * s) with the product in fp32.
@@ -529,8 +528,8 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
       const uint32_t tbase = tmem_base + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(sc * BT);
       const uint32_t ubase = tmem_base + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(su * BT);
       if constexpr (SWIGLU) {
-        // 16 rows at a time (a tile of BT = 16 j tokens): the gate and up values of 32 rows at once
-        // would not fit the registers
+        // 16 token rows at a time (BT is a multiple of 16): the gate and up values of 32 rows at
+        // once would not fit the registers
         const int n16 = min(BT / 16, (mend - m0 + 15) / 16);
 #pragma unroll 1
         for (int c = 0; c < n16; ++c) {
