@@ -8,8 +8,8 @@ the job: qkv and fc1 column-parallel, out and fc2 row-parallel with an all-reduc
 row-parallel linear: the library's NVLS kernel (multimem.ld_reduce / multimem.st over symmetric
 memory, on 8 SMs the GEMMs leave free), which also applies the block's RMS norm (each rank
 normalizes 1/N of the rows and multicasts them); ``--tp-reduce nccl`` runs NCCL and torch's norm
-instead. The stack is pipelined over 2 row chunks (3 on 8 GPUs): each chunk's reduction runs on a
-side stream while the following GEMMs of the other chunks run.
+instead. The stack is pipelined over 3 row chunks: each chunk's reduction runs on a side stream
+while the following GEMMs of the other chunks run.
 Per block: qkv; its q slice stands in for attention; out (+ residual in rank 0's
 epilogue); RMS norm; fc1 (tanh-GELU in the epilogue); fc2 (+ residual); RMS norm.
 
@@ -501,8 +501,8 @@ def bench_cfg4(args, job: Job, peaks: dict, with_cpu: bool) -> dict:
     M, H, blocks = CFG4["M"], CFG4["hidden"], (args.blocks or CFG4["blocks"])
     timer = LaunchTimer()
     # row chunks of the pipeline: more chunks overlap more of the reductions but shrink each GEMM;
-    # measured best: 2 on 2 GPUs, 3 on 8 (1.295M against 1.251M tokens/s with 2)
-    chunks = args.tp_chunks if args.tp_chunks > 0 else (1 if job.world == 1 else (2 if job.world < 8 else 3))
+    # measured: 3 on 8 GPUs 1.295M tokens/s against 1.251M with 2; on 2 GPUs 496.5k against 492.7k
+    chunks = args.tp_chunks if args.tp_chunks > 0 else (1 if job.world == 1 else 3)
     reduce = args.tp_reduce if args.tp_reduce != "auto" else "nvls"
     if job.world > 1:
         # The GEMM CTA holds a whole SM's register file, so a reduction gets only SMs the persistent
@@ -881,7 +881,7 @@ def main():
     ap.add_argument("--cpu-sample-m", type=int, default=512, help="tokens of the bounded CPU sample (one block)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--tp-chunks", type=int, default=0,
-                    help="cfg4: row chunks of the pipelined stack (0 = 1 on one GPU, 2 on 2-4 GPUs, 3 on 8)")
+                    help="cfg4: row chunks of the pipelined stack (0 = 1 on one GPU, 3 on several)")
     ap.add_argument("--tp-reduce", default="auto", choices=["auto", "nvls", "nccl"],
                     help="cfg4 with N > 1: all-reduce of the row-parallel outputs (own NVLS kernel, with the RMS "
                          "norm fused, or NCCL; auto = NVLS, which measured faster from 2 ranks)")
