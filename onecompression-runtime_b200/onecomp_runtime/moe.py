@@ -157,6 +157,30 @@ class ExpertParallelMoE(torch.nn.Module):
 
 
 # ----------------------------------------------------------------------------- B200 module
+def gate_up_matrix(gate: dict, up: dict, device=None):
+    """The [F, 2K] gate|up matrix of one expert for the fused SwiGLU launch
+    (``oc_b200_rows_gemm_swiglu``): row n is gate row n followed by up row n (packed bytes
+    concatenated along k), scales and zeros group-major ``[2G, F]`` (the gate's groups, then the
+    up's). ``gate`` / ``up`` are DSV4 packed dicts of one shape. Returns ``(qweight, scales,
+    zeros)``, or None where the layout does not allow it (K a multiple of 64 and of the
+    groupsize, more than one group, 16-byte packed rows): then gate and up stay two matrices."""
+    from .layers._rows_base import group_major
+
+    def shape(m):
+        return (int(m["wbits"]), int(m["groupsize"]), int(m["in_features"]), tuple(m["qweight_packed"].shape))
+
+    if shape(gate) != shape(up):
+        return None
+    wbits, gs, K, (N, ldb) = shape(gate)
+    if K % 64 or not (0 < gs < K) or K % gs or ldb * 8 != K * wbits or ldb % 16:
+        return None
+    dev = device if device is not None else gate["qweight_packed"].device
+    q = torch.cat([gate["qweight_packed"].to(dev), up["qweight_packed"].to(dev)], dim=1).contiguous()
+    s = torch.cat([group_major(gate["scales"].to(dev), N, K, gs), group_major(up["scales"].to(dev), N, K, gs)])
+    z = torch.cat([group_major(gate["qzeros"].to(dev), N, K, gs), group_major(up["qzeros"].to(dev), N, K, gs)])
+    return q, s, z
+
+
 class PackedMoE(torch.nn.Module):
     """Routed packed experts (+ optional shared expert) on the sm_100a kernels.
 
@@ -197,22 +221,16 @@ class PackedMoE(torch.nn.Module):
             return RowsHandle(q, s, z, wbits, gs if gs > 0 else K, K, N, MODE_EXACT, 1, N)
 
         def gate_up(gates: list[dict], ups: list[dict]):
-            """One [F, 2K] gate|up matrix per expert (row n = gate row n, then up row n; groups: the
-            gate's, then the up's) for the fused SwiGLU launch, or None where the layout does not
-            allow it (then gate and up stay two matrices)."""
-            wbits, gs, K, N, ldb = shape(gates[0])
+            """The experts' gate|up matrices as one handle for the fused SwiGLU launch, or None."""
             if any(shape(m) != shape(gates[0]) for m in gates + ups):
                 return None
-            if K % 64 or not (0 < gs < K) or K % gs or ldb * 8 != K * wbits or ldb % 16:
+            mats = [gate_up_matrix(g, u, dev) for g, u in zip(gates, ups)]
+            if any(m is None for m in mats):
                 return None
-            q = [torch.cat([g["qweight_packed"].to(dev), u["qweight_packed"].to(dev)], dim=1).contiguous()
-                 for g, u in zip(gates, ups)]
-            s = [torch.cat([group_major(g["scales"].to(dev), N, K, gs), group_major(u["scales"].to(dev), N, K, gs)])
-                 for g, u in zip(gates, ups)]
-            z = [torch.cat([group_major(g["qzeros"].to(dev), N, K, gs), group_major(u["qzeros"].to(dev), N, K, gs)])
-                 for g, u in zip(gates, ups)]
+            q, s, z = ([m[i] for m in mats] for i in range(3))
             if len({t.dtype for t in s}) != 1 or len({t.dtype for t in z}) != 1:
                 return None
+            wbits, gs, K, N, _ = shape(gates[0])
             return RowsHandle(q, s, z, wbits, gs, 2 * K, N, MODE_EXACT, 1, N)
 
         def handles(ex: list[dict], fuse: bool) -> dict:

@@ -159,3 +159,32 @@ def test_plan_k_layout_properties(G, gs, kind, seed):
         if k >= 0:
             assert int(gi[k]) == groups[p // 8]
     assert groups == sorted(groups)  # groups are contiguous runs of words
+
+
+@pytest.mark.parametrize("wbits,gs,K,N", [(2, 64, 256, 192), (4, 128, 512, 96), (4, 32, 256, 40)])
+def test_gate_up_matrix_dequantizes_to_gate_then_up(wbits, gs, K, N):
+    """The [F, 2K] gate|up matrix the fused SwiGLU launch reads dequantizes (oracle restatement of
+    the reference's dequant_dsv4_packed) to the gate weights followed by the up weights, row by row,
+    bit for bit; layouts it cannot express give None."""
+    from oracle import dsv4
+    from onecomp_runtime.moe import gate_up_matrix
+    from onecomp_runtime.testing import dsv4_packed
+    g = dsv4_packed(N, K, wbits, gs, seed=1, zero=None)
+    u = dsv4_packed(N, K, wbits, gs, seed=2, zero=None)
+    q, s, z = gate_up_matrix(g, u, "cpu")
+    G = K // gs
+    assert q.shape == (N, 2 * K * wbits // 8) and s.shape == (2 * G, N) and z.shape == (2 * G, N)
+
+    def bits(t):
+        return t.contiguous().view(torch.int16).numpy().view(np.uint16)
+
+    def deq(qq, ss, zz, k):
+        return dsv4.dequant_dsv4(qq.numpy(), bits(ss), "f16", bits(zz), "f16", wbits, gs, k, "bf16")
+
+    w_cat = deq(q, s, z, 2 * K)
+    w_ref = np.concatenate([deq(g["qweight_packed"], g["scales"], g["qzeros"], K),
+                            deq(u["qweight_packed"], u["scales"], u["qzeros"], K)], axis=1)
+    np.testing.assert_array_equal(w_cat, w_ref)
+    one_group = dsv4_packed(N, K, wbits, K, seed=3)
+    assert gate_up_matrix(one_group, one_group, "cpu") is None          # a single group per row
+    assert gate_up_matrix(g, dsv4_packed(N, 2 * K, wbits, gs, seed=4), "cpu") is None   # shapes differ
